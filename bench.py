@@ -1,0 +1,422 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 flash-Sinkhorn path (one JSON line on rank 0).
+
+A step is one forward + IFT backward of flash-Sinkhorn attention on BASELINE
+configuration 2: B=2, H=8, N=384, d=32, bf16 Q/K/V ~ N(0,1), eps=1, 20
+iterations, uniform marginals, upstream dO ~ N(0,1), CG tol 1e-6 / max 50 /
+zero start.  On N GPUs every rank runs its own (batch, head) shard of that size
+(weak scaling, no data-path collective); the reported value is whole-job
+calls/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle restatement in ``oracle/``, float32, all host threads) on the same
+workload and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "deepfold-linear_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "Sinkhorn attn fwd+IFT-bwd calls/sec & TFLOP/s vs bf16 peak, 1/2/4/8 B200"
+UNIT = "calls/s"
+CFG = dict(B=2, H=8, N=384, d=32, eps=1.0, K_iter=20, cg_rtol=1e-6, cg_max_iter=50)
+L2_FLUSH_BYTES = 256 << 20       # > 126 MB L2: written between timed steps
+
+
+def workload_name():
+    c = CFG
+    return (f"config2: flash-Sinkhorn fwd+IFT-bwd B={c['B']} H={c['H']} N={c['N']} d={c['d']} bf16 "
+            f"eps={c['eps']} K={c['K_iter']} uniform marginals, CG tol {c['cg_rtol']} max {c['cg_max_iter']}")
+
+
+def flops_per_call(n_cg_mean):
+    """Algorithmic flops (recompute included) of one fwd and one bwd call."""
+    c = CFG
+    per = c["N"] ** 2 * c["d"] * c["B"] * c["H"]
+    fwd = (4 * c["K_iter"] + 4) * per
+    bwd = (14 + 2 * n_cg_mean) * per
+    useful = 4 * per
+    return fwd, bwd, useful
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "resident_bwd_config2.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith("dram_bytes_per_launch:"):
+                try:
+                    return float(line.split(":", 1)[1].split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv") if os.path.isdir(
+            os.path.join(ROOT, "gpurun_out")) else f"/tmp/dfs_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def make_shard(dev, seed):
+    c = CFG
+    g = torch.Generator().manual_seed(seed)
+    B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+    host = dict(
+        Q=torch.randn(B, H, N, d, generator=g).to(torch.bfloat16),
+        K=torch.randn(B, H, N, d, generator=g).to(torch.bfloat16),
+        V=torch.randn(B, H, N, d, generator=g).to(torch.bfloat16),
+        dO=torch.randn(B, H, N, d, generator=g).to(torch.bfloat16),
+    )
+    host = {k: v.pin_memory() for k, v in host.items()}
+    eps = torch.full((H,), c["eps"], device=dev)
+    lm = torch.full((B, H, N), -math.log(N), device=dev)
+    return host, eps, lm
+
+
+def run_ours(args):
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    from deepfold import _native as nat
+    from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn
+
+    nat.lib()
+    c = CFG
+    host, eps, lm = make_shard(dev, 1000 + rank)
+    dQKV = {k: host[k].to(dev) for k in host}
+    cg = dict(rtol=c["cg_rtol"], atol=0.0, max_iter=c["cg_max_iter"])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step_resident():
+        Q = dQKV["Q"].requires_grad_(True)
+        K = dQKV["K"].requires_grad_(True)
+        V = dQKV["V"].requires_grad_(True)
+        O, _, _, _ = flash_sinkhorn(Q, K, V, None, None, None, eps, None, lm, lm, K_iter=c["K_iter"],
+                                    lam=float("inf"), cg_opts=cg)
+        dQ, dK, dV = torch.autograd.grad(O, (Q, K, V), grad_outputs=dQKV["dO"].float())
+        return dQ, dK, dV
+
+    # Device-time path: the two C-ABI launches back to back on pre-allocated
+    # buffers (the same kernels the autograd path runs), so host overhead never
+    # leaves the GPU idle inside the events.
+    B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+    f32 = dict(device=dev, dtype=torch.float32)
+    O = torch.empty(B, H, N, d, **f32)
+    lu, lv = torch.empty(B, H, N, **f32), torch.empty(B, H, N, **f32)
+    dO32 = dQKV["dO"].float()
+    grads = [torch.empty(B, H, N, d, **f32) for _ in range(3)]
+    iters = torch.empty(B * H, device=dev, dtype=torch.int32)
+    resid = torch.empty(B * H, **f32)
+    st_f, st_b = torch.zeros(1, device=dev, dtype=torch.int32), torch.zeros(1, device=dev, dtype=torch.int32)
+    prob = nat.make_problem(B, H, N, d, torch.bfloat16, c["K_iter"], float("inf"), 10.0)
+    fargs = nat.DfsFwdArgs(Q=dQKV["Q"].data_ptr(), K=dQKV["K"].data_ptr(), V=dQKV["V"].data_ptr(),
+                           eps=eps.data_ptr(), log_mu=lm.data_ptr(), log_nu=lm.data_ptr(), O=O.data_ptr(),
+                           log_u=lu.data_ptr(), log_v=lv.data_ptr(), status=st_f.data_ptr())
+    cgp = nat.DfsCgParams(rtol=c["cg_rtol"], atol=0.0, max_iter=c["cg_max_iter"], reserved=0)
+    bargs = nat.DfsBwdArgs(Q=dQKV["Q"].data_ptr(), K=dQKV["K"].data_ptr(), V=dQKV["V"].data_ptr(),
+                           eps=eps.data_ptr(), log_mu=lm.data_ptr(), log_nu=lm.data_ptr(), log_u=lu.data_ptr(),
+                           log_v=lv.data_ptr(), dO=dO32.data_ptr(), dQ=grads[0].data_ptr(),
+                           dK=grads[1].data_ptr(), dV=grads[2].data_ptr(), cg_iters=iters.data_ptr(),
+                           cg_residual=resid.data_ptr(), status=st_b.data_ptr())
+    L = nat.lib()
+    sp = stream.cuda_stream
+    fwd_ms, bwd_ms = [], []
+
+    def step_kernels():
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        nat.check(L.dfs_fwd(prob, fargs, None, 0, sp), "dfs_fwd")
+        e1.record(stream)
+        nat.check(L.dfs_bwd(prob, cgp, bargs, None, 0, sp), "dfs_bwd")
+        e2.record(stream)
+        return e0, e1, e2
+
+    for _ in range(args.warmup):
+        step_resident()
+        step_kernels()
+    torch.cuda.synchronize()
+
+    # ---- timed region: value (inputs resident in HBM, L2 flushed between steps)
+    sampler = ClockSampler(dev.index) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        evs.append(step_kernels())
+    torch.cuda.synchronize()
+    for e0, e1, e2 in evs:
+        fwd_ms.append(e0.elapsed_time(e1))
+        bwd_ms.append(e1.elapsed_time(e2))
+    step_ms = [f + b for f, b in zip(fwd_ms, bwd_ms)]
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    n_cg = float(iters.float().mean().item())
+    status = int(st_f.item()) | int(st_b.item())
+
+    # ---- e2e: public API, host buffers, H2D inputs + D2H gradients inside the timed region
+    out_host = {k: torch.empty(host["Q"].shape, dtype=torch.bfloat16).pin_memory() for k in ("dQ", "dK", "dV")}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = sum(v.numel() * v.element_size() for v in out_host.values())
+
+    def step_e2e():
+        dev_in = {k: host[k].to(dev, non_blocking=True) for k in host}
+        Q = dev_in["Q"].requires_grad_(True)
+        K = dev_in["K"].requires_grad_(True)
+        V = dev_in["V"].requires_grad_(True)
+        O, _, _, _ = flash_sinkhorn(Q, K, V, None, None, None, eps, None, lm, lm, K_iter=c["K_iter"],
+                                    lam=float("inf"), cg_opts=cg)
+        gq, gk, gv = torch.autograd.grad(O, (Q, K, V), grad_outputs=dev_in["dO"].float())
+        out_host["dQ"].copy_(gq, non_blocking=True)
+        out_host["dK"].copy_(gk, non_blocking=True)
+        out_host["dV"].copy_(gv, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        step_e2e()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ee0, ee1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ee0.record(stream)
+    for _ in range(args.steps):
+        step_e2e()
+    ee1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ee0.elapsed_time(ee1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    clocks = sampler.stop() if sampler else None
+
+    if rank == 0:
+        peak, _, peak_src = load_peaks()
+        f_fwd, f_bwd, useful = flops_per_call(n_cg)
+        mf, mb = statistics.mean(fwd_ms), statistics.mean(bwd_ms)
+        dom_name, dom_ms, dom_flops = ("resident_bwd_kernel", mb, f_bwd) if mb >= mf else \
+            ("resident_fwd_kernel", mf, f_fwd)
+        achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+        calls = world * args.steps
+        value = calls / (total_ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) Q/K/V/dO; BASELINE config 2 shapes)",
+            "config": {"workload": workload_name(), "global_batch": CFG["B"] * world,
+                       "heads": CFG["H"], "seq_len": CFG["N"], "head_dim": CFG["d"],
+                       "parallelism": f"(batch,head)-shard x{world}",
+                       "l2": "flushed between timed steps (256 MB write, outside the step events)"},
+            "tflops": {"algorithmic_per_call": round((f_fwd + f_bwd) / 1e12, 6),
+                       "achieved": round((f_fwd + f_bwd) * calls / (total_ms * 1e-3) / 1e12, 3),
+                       "useful_flops_per_call": useful, "cg_iters_mean": n_cg,
+                       "frac_of_bf16_peak": round((f_fwd + f_bwd) * calls / (total_ms * 1e-3) / 1e12 / peak, 5)},
+            "kernels_ms": {"resident_fwd_kernel": round(mf, 5), "resident_bwd_kernel": round(mb, 5)},
+            "roofline": {"bound": "tensor", "kernel": dom_name, "achieved": round(achieved, 3),
+                         "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 5), "traffic": profile_traffic()},
+            "e2e": {"value": round(world * args.steps / (e2e_ms * 1e-3), 3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 2 * args.steps,
+            "device_status": status,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def _oracle_call(orc, inp):
+    """One fwd + unrolled bwd of the oracle on the config-2 workload."""
+    c = CFG
+    Q, K, V, dO = inp
+    H, N = c["H"], c["N"]
+    lm = np.full((c["B"], H, N), -math.log(N), np.float32)
+    with orc.precision(np.float32):
+        orc.flash_sinkhorn_attn(Q, K, V, None, None, None, None, np.full(H, c["eps"], np.float32), None,
+                                lm, lm, K_iter=c["K_iter"], lam=float("inf"), with_grad=True, dO_flat=dO)
+
+
+def _oracle_inputs():
+    c = CFG
+    r = np.random.default_rng(7)
+    shp = (c["B"], c["H"], c["N"], c["d"])
+    Q, K, V = (r.standard_normal(shp).astype(np.float32) for _ in range(3))
+    dO = r.standard_normal((c["B"], c["N"], c["H"] * c["d"])).astype(np.float32)
+    return Q, K, V, dO
+
+
+def cpu_baseline(seconds=15.0):
+    """Oracle (reference algorithm restated in numpy, float32) timed on a bounded
+    sample: whole config-2 calls repeated until ~`seconds` have elapsed."""
+    from oracle import sinkhorn_oracle as orc
+    inp = _oracle_inputs()
+    _oracle_call(orc, inp)  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        _oracle_call(orc, inp)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": UNIT, "cores": len(os.sched_getaffinity(0)), "kind": "port",
+            "sample": f"{n} full config-2 calls (fwd + unrolled bwd, float32 numpy) in {dt:.1f} s",
+            "cpu": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle import sinkhorn_oracle as orc
+    inp = _oracle_inputs()
+    for _ in range(args.warmup):
+        _oracle_call(orc, inp)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _oracle_call(orc, inp)
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    cores = len(os.sched_getaffinity(0))
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1); BASELINE config 2 shapes)",
+            "config": {"workload": workload_name(), "global_batch": CFG["B"], "heads": CFG["H"],
+                       "seq_len": CFG["N"], "head_dim": CFG["d"], "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} full config-2 calls (fwd + unrolled bwd), oracle "
+                                       "restatement of the reference algorithm, float32 numpy",
+                             "cpu": _cpu_model()},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,117 @@
+// dfs_abi.cu -- the extern "C" entry points of libdfsink.so (include/dfsink.h):
+// argument validation, workspace sizing and kernel dispatch.  Nothing here
+// allocates device memory.
+#include <cmath>
+#include <cstring>
+
+#include "dfs_kernels.cuh"
+
+using namespace dfs;
+
+namespace {
+
+bool dims_ok(const dfs_problem* p) {
+  return p && p->B > 0 && p->H > 0 && p->N > 0 && p->d > 0 && p->K_iter >= 0 &&
+         (p->in_dtype == DFS_BF16 || p->in_dtype == DFS_F16 || p->in_dtype == DFS_F32) &&
+         (p->cost_mode == DFS_COST_QK || p->cost_mode == DFS_COST_DENSE) &&
+         !(p->lam <= 0.0f) && !std::isnan(p->lam) && (p->threshold <= 0.0f || p->check_every > 0);
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? DFS_OK : DFS_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+int dfs_abi_version(void) { return DFS_ABI_VERSION; }
+
+const char* dfs_status_string(int s) {
+  switch (s) {
+    case DFS_OK: return "ok";
+    case DFS_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case DFS_ERR_UNSUPPORTED: return "shape or dtype not supported by the resident kernels";
+    case DFS_ERR_WORKSPACE: return "workspace too small";
+    case DFS_ERR_CUDA: return "CUDA runtime error";
+    case DFS_ERR_DEVICE_TIMEOUT: return "device: bounded wait gave up";
+    case DFS_ERR_NUMERIC: return "device: non-finite potentials after re-stabilisation";
+    case DFS_WARN_CG_NOT_CONVERGED: return "device: CG reached max_iter";
+    default: return "several device status bits set";
+  }
+}
+
+int dfs_max_n(int d) { return d == 32 ? 384 : 0; }
+
+int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes) {
+  if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
+  if (fwd_bytes) *fwd_bytes = 0;
+  if (bwd_bytes) *bwd_bytes = resident_bwd_workspace(p->B, p->H, p->N, p->d);
+  return DFS_OK;
+}
+
+int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t workspace_bytes,
+            void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (!dims_ok(p) || !a) return DFS_ERR_INVALID_ARGUMENT;
+  if (!a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->cost_mode == DFS_COST_QK && (!a->Q || !a->K)) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->cost_mode == DFS_COST_DENSE && !a->C) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->O && !a->V) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->N > dfs_max_n(p->d)) return DFS_ERR_UNSUPPORTED;
+  if (a->O && (reinterpret_cast<uintptr_t>(a->O) & 15)) return DFS_ERR_INVALID_ARGUMENT;
+  FwdParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.Q = a->Q; q.K = a->K; q.V = a->V; q.C = a->C;
+  q.x_res = a->x_res; q.pos_weight = a->pos_weight; q.pos_bins = a->pos_bins;
+  q.eps = a->eps; q.w_dist = a->w_dist; q.log_mu = a->log_mu; q.log_nu = a->log_nu;
+  q.log_u_init = a->log_u_init; q.log_v_init = a->log_v_init; q.mask = a->mask;
+  q.O = a->O; q.x_centroid = a->x_centroid; q.log_u = a->log_u; q.log_v = a->log_v;
+  q.status = a->status;
+  q.T_out = a->T_norm;
+  q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
+  q.cost_mode = p->cost_mode; q.K_iter = p->K_iter; q.check_every = p->check_every > 0 ? p->check_every : 1;
+  q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
+  return cuda_status(launch_resident_fwd(q, static_cast<cudaStream_t>(stream)));
+}
+
+int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a, void* workspace,
+            size_t workspace_bytes, void* stream) {
+  if (!dims_ok(p) || !a || !cg) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->cost_mode != DFS_COST_QK) return DFS_ERR_UNSUPPORTED;
+  if (!a->Q || !a->K || !a->V || !a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v || !a->dO)
+    return DFS_ERR_INVALID_ARGUMENT;
+  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->dxc && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->N > dfs_max_n(p->d)) return DFS_ERR_UNSUPPORTED;
+  const size_t need = resident_bwd_workspace(p->B, p->H, p->N, p->d);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return DFS_ERR_WORKSPACE;
+  BwdParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.Q = a->Q; q.K = a->K; q.V = a->V;
+  q.x_res = a->x_res; q.pos_weight = a->pos_weight; q.pos_bins = a->pos_bins;
+  q.eps = a->eps; q.w_dist = a->w_dist; q.log_mu = a->log_mu; q.log_nu = a->log_nu; q.mask = a->mask;
+  q.log_u = a->log_u; q.log_v = a->log_v; q.dO = a->dO; q.dxc = a->dxc;
+  q.dQ = a->dQ; q.dK = a->dK; q.dV = a->dV; q.dlog_mu = a->dlog_mu; q.dlog_nu = a->dlog_nu;
+  q.dx_res = a->dx_res; q.dpos_weight = a->dpos_weight; q.dw_dist = a->dw_dist;
+  q.cg_iters = a->cg_iters; q.cg_residual = a->cg_residual; q.status = a->status;
+  q.ws = static_cast<float*>(workspace);
+  q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
+  q.cg_max_iter = cg->max_iter; q.cg_rtol = cg->rtol; q.cg_atol = cg->atol;
+  q.lam = p->lam; q.r_0 = p->r_0;
+  return cuda_status(launch_resident_bwd(q, static_cast<cudaStream_t>(stream)));
+}
+
+int dfs_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K, void* stream) {
+  if (!A || !B || !D || which < 0 || which > 2) return DFS_ERR_INVALID_ARGUMENT;
+  if (M != 64 || K <= 0 || K % 8 || N <= 0 || N > 384 || N % 32) return DFS_ERR_INVALID_ARGUMENT;
+  const size_t abytes = static_cast<size_t>(M) * K * 4, bbytes = static_cast<size_t>(N) * K * 4;
+  if (abytes > 98304 || bbytes > 98304) return DFS_ERR_UNSUPPORTED;
+  return cuda_status(launch_selftest_mma(which, A, B, D, M, N, K, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,184 @@
+// dfs_slab.cuh -- pieces shared by the resident forward and backward kernels.
+//
+// A CTA owns a 64-row slab of one N x N problem.  In registers the slab is laid
+// out as E[r][k] = element (8*warp + r, 32*k + lane): each warp holds 8 rows,
+// each lane the columns congruent to it mod 32.  Row reductions are lane
+// reductions (reduce8_rows), column reductions go through shared memory and,
+// across the cluster, through distributed shared memory.
+#pragma once
+
+#include "dfs_kernels.cuh"
+
+namespace dfs {
+
+// Drain an M=64 fp32 accumulator (TMEM columns [col_base, col_base+NP)) into the
+// 64 x NP 128B-swizzled staging buffer, multiplied by `scale`.  TMEM row m of an
+// M=64 MMA sits in lane (m % 16) + 32 (m / 16); warps w and w+4 share those
+// lanes and split the columns.  Caller synchronises before and after.
+template <int NP>
+DFS_DEV void drain_m64(float* Ts, uint32_t tbase, uint32_t col_base, float scale, int warp, int lane) {
+  const int q = warp & 3, hf = warp >> 2;
+#pragma unroll 1
+  for (int ch = 0; ch < NP / 64; ++ch) {
+    const int col0 = hf * (NP / 2) + 32 * ch;
+    float v[32];
+    tmem_ld32(tbase + (static_cast<uint32_t>(32 * q) << 16) + col_base + col0, v);
+    if (lane < 16) {
+      const int row = 16 * q + lane, r = row & 7;
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(Ts) +
+                                              ((((col0 >> 5) * 8 + (row >> 3)) << 10) + (r << 7)));
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4)
+        dst[c4 ^ r] = make_float4(v[4 * c4] * scale, v[4 * c4 + 1] * scale, v[4 * c4 + 2] * scale,
+                                  v[4 * c4 + 3] * scale);
+    }
+  }
+}
+
+template <int NS>
+DFS_DEV void stage_to_regs(float (&E)[8][NS], const float* Ts, int warp, int lane) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int k = 0; k < NS; ++k) E[r][k] = Ts[sw_off(8 * warp + r, 32 * k + lane, 64) >> 2];
+}
+
+template <int NS>
+DFS_DEV void regs_to_stage(const float (&E)[8][NS], float* Ts, int warp, int lane) {
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int k = 0; k < NS; ++k) Ts[sw_off(8 * warp + r, 32 * k + lane, 64) >> 2] = E[r][k];
+}
+
+// Position / geometry terms of the cost, folded into the slab as
+// S' -= (pos_weight[h, bins_ij] + w_h dist_ij / (r_0 + dist_ij)) * s_scale
+// (src/deepfold/model/kernels/sinkhorn_kernel.py:107-127).
+struct BiasArgs {
+  const float* pos_weight;   // (H, 68) or null
+  const int32_t* pos_bins;   // (B, N, N)
+  const float* xrow;         // smem, 3 x 64 row coordinates (x, y, z planes)
+  const float* xcol;         // smem, 3 x NP column coordinates
+  bool geo;                  // geometry term present
+  float w_h, r_0, s_scale;
+  int bb, hh, N, row0;
+  bool transposed;           // slab rows are cost columns (bins read as [col][row])
+};
+
+template <int NS>
+DFS_DEV void add_cost_bias(float (&E)[8][NS], const BiasArgs& a, int warp, int lane) {
+  constexpr int NP = 32 * NS;
+  if (a.pos_weight == nullptr && !a.geo) return;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int li = 8 * warp + r, gi = a.row0 + li;
+    const float xi0 = a.geo ? a.xrow[li] : 0.f, xi1 = a.geo ? a.xrow[64 + li] : 0.f,
+                xi2 = a.geo ? a.xrow[128 + li] : 0.f;
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      const int gj = 32 * k + lane;
+      float bias = 0.0f;
+      if (gi < a.N && gj < a.N) {
+        if (a.pos_weight) {
+          const size_t bi = a.transposed ? (static_cast<size_t>(a.bb) * a.N + gj) * a.N + gi
+                                         : (static_cast<size_t>(a.bb) * a.N + gi) * a.N + gj;
+          bias += a.pos_weight[a.hh * 68 + a.pos_bins[bi]];
+        }
+        if (a.geo) {
+          const float d0 = xi0 - a.xcol[gj], d1 = xi1 - a.xcol[NP + gj], d2 = xi2 - a.xcol[2 * NP + gj];
+          const float dist = sqrtf(d0 * d0 + d1 * d1 + d2 * d2 + 1e-8f);
+          bias += a.w_h * dist / (a.r_0 + dist);
+        }
+      }
+      E[r][k] -= bias * a.s_scale;
+    }
+  }
+}
+
+// Load rows [row_first, row_first+rows) of a (., DH) tensor into a 128B-swizzled
+// fp32 operand buffer with `rows` rows (rows beyond N are zero).
+template <int DH>
+DFS_DEV void load_operand(float* dst, const void* src, int dtype, size_t base_row, int row_first, int rows,
+                          int N, int tid, int nthreads) {
+  for (int e = tid; e < rows * DH; e += nthreads) {
+    const int i = e / DH, c = e % DH, gi = row_first + i;
+    const float v = gi < N ? load_f32(src, (base_row + gi) * DH + c, dtype) : 0.0f;
+    dst[sw_off(i, c, rows) >> 2] = v;
+  }
+}
+
+// Transposed load: element (row gi, c) of a (., DH) tensor goes to (row c,
+// column gi - row_first) of a 128B-swizzled buffer with DH rows and `cols`
+// columns, i.e. the K-major operand holding the tensor's transpose.
+template <int DH>
+DFS_DEV void load_operand_t(float* dst, const void* src, int dtype, size_t base_row, int row_first, int cols,
+                            int N, int tid, int nthreads) {
+  for (int e = tid; e < cols * DH; e += nthreads) {
+    const int i = e / DH, c = e % DH, gi = row_first + i;
+    const float v = gi < N ? load_f32(src, (base_row + gi) * DH + c, dtype) : 0.0f;
+    dst[sw_off(c, i, DH) >> 2] = v;
+  }
+}
+
+// Issue D (TMEM, M=64 rows x NN columns) = A (64 x KD, K-major) * B (NN x KD,
+// K-major)^T, both 128B-swizzled fp32 buffers read as tf32 (one elected thread).
+// rows_b is the row count B was stored with (its atom column stride).
+template <int NN, int KD>
+DFS_DEV void issue_abt(uint32_t d_tmem, const float* A, const float* Bm, int rows_b) {
+  constexpr int NH = NN > 256 ? 2 : 1;
+  constexpr int NCH = NN / NH;
+  const uint32_t aa = smem_u32(A), ba = smem_u32(Bm);
+#pragma unroll
+  for (int h2 = 0; h2 < NH; ++h2) {
+#pragma unroll 4
+    for (int kk = 0; kk < KD / 8; ++kk) {
+      const uint64_t ad = sw128_desc(aa + (kk >> 2) * 8192u + (kk & 3) * 32u, 16, 1024);
+      const uint64_t bd = sw128_desc(ba + (kk >> 2) * (static_cast<uint32_t>(rows_b) * 128u) +
+                                         (h2 * NCH / 8) * 1024u + (kk & 3) * 32u, 16, 1024);
+      mma_tf32(d_tmem + h2 * NCH, ad, bd, idesc_tf32(64, NCH, 0, 0), kk > 0 ? 1u : 0u);
+    }
+  }
+}
+
+// Issue S = Q K^T for the slab (one elected thread): A = Q slab (64 x DH,
+// K-major), B = K (NP x DH, K-major), D = TMEM columns [0, NP).
+template <int NP, int DH>
+DFS_DEV void issue_qk(uint32_t tbase, const float* Qs, const float* Ks) {
+  issue_abt<NP, DH>(tbase, Qs, Ks, NP);
+}
+
+// Drain an M=64 accumulator of DH columns (TMEM columns [col, col+DH)) to a
+// row-major global (rows, DH) tensor, rows row0.. (< N), scaled.
+template <int DH>
+DFS_DEV void drain_rows_to_global(uint32_t tbase, uint32_t col, float* out, size_t row_base, int row0, int N,
+                                  float scale, int warp, int lane) {
+  if (warp >= 4) return;
+#pragma unroll
+  for (int a = 0; a < DH / 32; ++a) {
+    float v[32];
+    tmem_ld32(tbase + (static_cast<uint32_t>(32 * warp) << 16) + col + 32 * a, v);
+    const int gi = row0 + 16 * warp + lane;
+    if (lane < 16 && gi < N) {
+      float4* dst = reinterpret_cast<float4*>(out + (row_base + gi) * DH + 32 * a);
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4)
+        dst[c4] = make_float4(v[4 * c4] * scale, v[4 * c4 + 1] * scale, v[4 * c4 + 2] * scale,
+                              v[4 * c4 + 3] * scale);
+    }
+  }
+}
+
+// fp32 variant for already-fp32 tensors (upstream gradients).
+template <int DH>
+DFS_DEV void load_operand_f32(float* dst, const float* src, size_t base_row, int row_first, int rows, int N,
+                              int tid, int nthreads) {
+  load_operand<DH>(dst, src, DFS_F32, base_row, row_first, rows, N, tid, nthreads);
+}
+
+template <int DH>
+DFS_DEV void load_operand_f32_t(float* dst, const float* src, size_t base_row, int row_first, int cols, int N,
+                                int tid, int nthreads) {
+  load_operand_t<DH>(dst, src, DFS_F32, base_row, row_first, cols, N, tid, nthreads);
+}
+
+}  // namespace dfs

@@ -1,0 +1,188 @@
+"""Binding to ``libdfsink.so``, the C-ABI CUDA library behind every op here.
+
+The library is built in-tree (``build_library``) with nvcc for sm_100a and
+loaded with ctypes; the structures below mirror ``include/dfsink.h`` field by
+field.  There is no fallback: if the library or a CUDA device is missing the
+ops raise ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+import threading
+
+import torch
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT_DIR = os.path.dirname(PKG_DIR)                      # .../deepfold-linear_b200
+CSRC_DIR = os.path.join(ROOT_DIR, "csrc")
+INCLUDE_DIR = os.path.join(os.path.dirname(ROOT_DIR), "include")
+LIB_DIR = os.path.join(PKG_DIR, "_lib")
+LIB_PATH = os.path.join(LIB_DIR, "libdfsink.so")
+SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_selftest.cu"]
+HEADERS = ["dfs_device.cuh", "dfs_kernels.cuh", "dfs_slab.cuh"]
+
+NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
+              "-Xcompiler", "-fPIC", "-shared"]
+
+# status codes (include/dfsink.h)
+DFS_OK = 0
+DFS_ERR_INVALID_ARGUMENT = 1
+DFS_ERR_UNSUPPORTED = 2
+DFS_ERR_WORKSPACE = 3
+DFS_ERR_CUDA = 4
+DFS_ERR_DEVICE_TIMEOUT = 8
+DFS_ERR_NUMERIC = 16
+DFS_WARN_CG_NOT_CONVERGED = 32
+
+DFS_BF16, DFS_F16, DFS_F32 = 0, 1, 2
+DFS_COST_QK, DFS_COST_DENSE = 0, 1
+
+_P = ctypes.c_void_p
+
+
+class DfsProblem(ctypes.Structure):
+    _fields_ = [("B", ctypes.c_int32), ("H", ctypes.c_int32), ("N", ctypes.c_int32),
+                ("d", ctypes.c_int32), ("in_dtype", ctypes.c_int32), ("cost_mode", ctypes.c_int32),
+                ("K_iter", ctypes.c_int32), ("check_every", ctypes.c_int32),
+                ("lam", ctypes.c_float), ("r_0", ctypes.c_float), ("threshold", ctypes.c_float),
+                ("reserved", ctypes.c_float)]
+
+
+class DfsFwdArgs(ctypes.Structure):
+    _fields_ = [(n, _P) for n in (
+        "Q", "K", "V", "C", "x_res", "pos_weight", "pos_bins", "eps", "w_dist", "log_mu", "log_nu",
+        "log_u_init", "log_v_init", "mask", "O", "x_centroid", "log_u", "log_v", "status", "T_norm")]
+
+
+class DfsCgParams(ctypes.Structure):
+    _fields_ = [("rtol", ctypes.c_float), ("atol", ctypes.c_float), ("max_iter", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
+class DfsBwdArgs(ctypes.Structure):
+    _fields_ = [(n, _P) for n in (
+        "Q", "K", "V", "x_res", "pos_weight", "pos_bins", "eps", "w_dist", "log_mu", "log_nu", "mask",
+        "log_u", "log_v", "dO", "dxc", "dQ", "dK", "dV", "dlog_mu", "dlog_nu", "dx_res",
+        "dpos_weight", "dw_dist", "cg_iters", "cg_residual", "status")]
+
+
+EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
+                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma")
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _stale() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    deps = [os.path.join(CSRC_DIR, f) for f in SOURCES + HEADERS] + [os.path.join(INCLUDE_DIR, "dfsink.h")]
+    return any(os.path.exists(f) and os.path.getmtime(f) > t for f in deps)
+
+
+def build_library(force: bool = False, verbose: bool = False) -> str:
+    """Compile ``libdfsink.so`` for sm_100a into the package (in-tree)."""
+    if not force and not _stale():
+        return LIB_PATH
+    os.makedirs(LIB_DIR, exist_ok=True)
+    nvcc = os.environ.get("NVCC", "nvcc")
+    tmp = LIB_PATH + ".tmp.%d" % os.getpid()
+    cmd = [nvcc] + NVCC_FLAGS + ["-I", INCLUDE_DIR] + [os.path.join(CSRC_DIR, f) for f in SOURCES] + ["-o", tmp]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"libdfsink.so not found at {LIB_PATH}; build it with "
+                    "`python -c 'import __graft_entry__ as g; g.build()'` (needs nvcc)")
+            L = ctypes.CDLL(LIB_PATH)
+            L.dfs_abi_version.restype = ctypes.c_int
+            L.dfs_status_string.restype = ctypes.c_char_p
+            L.dfs_status_string.argtypes = [ctypes.c_int]
+            L.dfs_max_n.restype = ctypes.c_int
+            L.dfs_max_n.argtypes = [ctypes.c_int]
+            L.dfs_workspace_size.restype = ctypes.c_int
+            L.dfs_workspace_size.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(ctypes.c_size_t),
+                                             ctypes.POINTER(ctypes.c_size_t)]
+            L.dfs_fwd.restype = ctypes.c_int
+            L.dfs_fwd.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs), _P,
+                                  ctypes.c_size_t, _P]
+            L.dfs_bwd.restype = ctypes.c_int
+            L.dfs_bwd.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsCgParams),
+                                  ctypes.POINTER(DfsBwdArgs), _P, ctypes.c_size_t, _P]
+            L.dfs_selftest_mma.restype = ctypes.c_int
+            L.dfs_selftest_mma.argtypes = [ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, _P]
+            _lib = L
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().dfs_status_string(int(code)).decode()
+
+
+def check(code: int, what: str) -> None:
+    if code != DFS_OK:
+        raise RuntimeError(f"{what} failed: {status_string(code)} (code {code})")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return DFS_BF16
+    if dt == torch.float16:
+        return DFS_F16
+    if dt == torch.float32:
+        return DFS_F32
+    raise TypeError(f"unsupported dtype {dt}; expected bfloat16, float16 or float32")
+
+
+def make_problem(B, H, N, d, dtype, K_iter, lam, r_0, cost_mode=DFS_COST_QK, threshold=None,
+                 check_every=2) -> DfsProblem:
+    return DfsProblem(B=B, H=H, N=N, d=d, in_dtype=dtype_code(dtype), cost_mode=cost_mode,
+                      K_iter=int(K_iter), check_every=int(check_every),
+                      lam=float(lam) if not math.isinf(lam) else float("inf"), r_0=float(r_0),
+                      threshold=float(threshold) if threshold is not None else 0.0, reserved=0.0)
+
+
+def max_n(d: int) -> int:
+    return int(lib().dfs_max_n(int(d)))
+
+
+def require_cuda(*tensors) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("deepfold B200 Sinkhorn ops run on CUDA tensors only (no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+    if dev is None:
+        raise RuntimeError("no CUDA tensor given")
+    return dev

@@ -1,0 +1,111 @@
+"""Dense-cost Sinkhorn surface: ``sinkhorn_solve`` and ``compute_transport_output``.
+
+Drop-in for ``deepfold.model.sinkhorn`` of the reference
+(src/deepfold/model/sinkhorn.py:17-198) on CUDA tensors.  The cost matrix C is
+read by the same resident kernel as the flash path (``DFS_COST_DENSE``), so the
+Sinkhorn loop never leaves the GPU:
+
+* ``sinkhorn_solve``: log-domain (un)balanced iterations with the optional
+  L-inf early stop.  The reference tests the stop condition once for the whole
+  batch (one host sync per check); here every (batch, head) problem tests its
+  own potentials on the device and stops independently, without a host sync.
+  Problems that converge early therefore stop earlier than in the reference, a
+  difference below ``threshold``.
+* ``compute_transport_output``: row-normalised plan T_norm (materialised, as the
+  reference returns it), gated output and optional centroid.
+
+The backward of these two entry points is not provided (the reference differentiates
+them with autograd through K dense iterations); use ``flash_sinkhorn`` for
+gradients.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from deepfold import _native as nat
+
+__all__ = ["sinkhorn_solve", "compute_transport_output"]
+
+
+def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshold, check_every,
+                mask, V=None, x_res=None, want_T=False):
+    dev = nat.require_cuda(C)
+    B, H, N, _ = C.shape
+    if N > nat.max_n(32):
+        raise ValueError(f"N={N} exceeds the resident kernels' range ({nat.max_n(32)})")
+    if C.requires_grad or (V is not None and V.requires_grad):
+        raise NotImplementedError("gradients through the dense-cost entry points are not provided; "
+                                  "use flash_sinkhorn")
+    f32 = lambda t: None if t is None else t.detach().contiguous().float()  # noqa: E731
+    # every tensor handed to the library is bound to a local name for the whole call
+    Cc, lmu, lnu, epsc = f32(C), f32(log_mu), f32(log_nu), f32(eps)
+    lui, lvi, mk, xr = f32(log_u_init), f32(log_v_init), f32(mask), f32(x_res)
+    d = 32
+    Vp = None
+    if V is not None:
+        d = V.shape[-1]
+        if d != 32:
+            raise ValueError("compute_transport_output supports head dim 32")
+        Vp = f32(V)
+    lu = torch.empty(B, H, N, device=dev, dtype=torch.float32)
+    lv = torch.empty(B, H, N, device=dev, dtype=torch.float32)
+    O = torch.empty(B, H, N, d, device=dev, dtype=torch.float32) if Vp is not None else None
+    xc = torch.empty(B, H, N, 3, device=dev, dtype=torch.float32) if xr is not None else None
+    T = torch.empty(B, H, N, N, device=dev, dtype=torch.float32) if want_T else None
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+    prob = nat.make_problem(B, H, N, d, torch.float32, K, lam, 10.0, cost_mode=nat.DFS_COST_DENSE,
+                            threshold=threshold, check_every=check_every)
+    args = nat.DfsFwdArgs(
+        Q=None, K=None, V=nat.ptr(Vp), C=nat.ptr(Cc), x_res=nat.ptr(xr), pos_weight=None,
+        pos_bins=None, eps=nat.ptr(epsc), w_dist=None, log_mu=nat.ptr(lmu), log_nu=nat.ptr(lnu),
+        log_u_init=nat.ptr(lui), log_v_init=nat.ptr(lvi), mask=nat.ptr(mk), O=nat.ptr(O),
+        x_centroid=nat.ptr(xc), log_u=nat.ptr(lu), log_v=nat.ptr(lv), status=nat.ptr(status),
+        T_norm=nat.ptr(T))
+    nat.check(nat.lib().dfs_fwd(prob, args, None, 0, nat.stream_ptr(dev)), "dfs_fwd")
+    return lu, lv, O, xc, T
+
+
+def sinkhorn_solve(C, log_mu, log_nu, eps, lam: float = 1.0, K: int = 7, log_u_init=None,
+                   log_v_init=None, threshold: float | None = None, check_every: int = 2, mask=None):
+    """Log-domain Sinkhorn on a dense cost (H,N,N) or (B,H,N,N); returns (log_u, log_v)."""
+    unb = C.dim() == 3
+    if unb:
+        C = C.unsqueeze(0)
+        log_mu, log_nu = log_mu.unsqueeze(0), log_nu.unsqueeze(0)
+        log_u_init = None if log_u_init is None else log_u_init.unsqueeze(0)
+        log_v_init = None if log_v_init is None else log_v_init.unsqueeze(0)
+        mask = None  # the reference ignores the mask for unbatched input
+    f32 = lambda t: None if t is None else t.float().contiguous()  # noqa: E731
+    lu, lv, _, _, _ = _dense_call(C, f32(log_mu), f32(log_nu), f32(eps), float(lam), int(K),
+                                  f32(log_u_init), f32(log_v_init), threshold, check_every, f32(mask))
+    if unb:
+        return lu.squeeze(0), lv.squeeze(0)
+    return lu, lv
+
+
+def compute_transport_output(V, G, log_u, log_v, C, eps, x_res=None, mask=None):
+    """Gated transport output, T_norm and centroid (sinkhorn.py:115-198).
+
+    Returns (o (B,N,H*d) or (N,H*d), T_norm, x_centroid or None).
+    """
+    unb = C.dim() == 3
+    if unb:
+        V, G, C = V.unsqueeze(0), G.unsqueeze(0), C.unsqueeze(0)
+        log_u, log_v = log_u.unsqueeze(0), log_v.unsqueeze(0)
+        x_res = None if x_res is None else x_res.unsqueeze(0)
+        mask = None
+    B, H, N, d = V.shape
+    zeros = torch.zeros(B, H, N, device=C.device, dtype=torch.float32)
+    lu = log_u.float().contiguous()
+    lv = log_v.float().contiguous()
+    _, _, O, xc, T = _dense_call(C, zeros, zeros, eps.float().contiguous(), float("inf"), 0, lu, lv,
+                                 None, 2, None if mask is None else mask.float().contiguous(),
+                                 V=V, x_res=x_res, want_T=True)
+    o = torch.sigmoid(G.float()) * O
+    o = o.permute(0, 2, 1, 3).reshape(B, N, H * d)
+    if mask is not None:
+        o = o * mask.float()[:, :, None]
+    if unb:
+        return o.squeeze(0), T.squeeze(0), None if xc is None else xc.squeeze(0)
+    return o, T, xc

@@ -1,0 +1,167 @@
+/*
+ * dfsink.h -- C ABI of the B200 flash-Sinkhorn library (libdfsink.so).
+ *
+ * One (batch, head) pair is one optimal-transport problem.  For each problem
+ * the library runs the log-domain (un)balanced Sinkhorn iteration of the
+ * reference (vv137/deepfold-linear) on the log-kernel S = -C/eps with
+ *     C_ij = -q_i.k_j/sqrt(d) + pos_weight[h, bins_ij] + w_h * dist_ij/(r_0+dist_ij),
+ * produces the row-normalised transport output O = T_norm V (and the optional
+ * centroid T_norm x), and differentiates it with the implicit-function theorem,
+ * solving the adjoint system by conjugate gradient on the device.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise; every tensor is
+ *     dense row-major (C-contiguous) with the shape given beside it.
+ *   - The caller owns all memory.  No entry point allocates device memory; the
+ *     scratch a call needs is passed in as `workspace` (size from
+ *     dfs_workspace_size).
+ *   - Calls are asynchronous on `stream` (a cudaStream_t passed as void*).  The
+ *     return value reports argument errors and launch errors only.  Errors found
+ *     on the device (a bounded wait that gave up, non-finite potentials) are
+ *     OR-ed into the int32 word `status` (device memory, may be NULL) and can be
+ *     read after the stream is synchronised.
+ *   - Entry points are thread-safe; concurrent calls on different streams need
+ *     separate `status` words and workspaces.
+ *   - Natural-log potentials (log_u, log_v) in and out, as in the reference.
+ */
+#ifndef DFSINK_H
+#define DFSINK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DFS_ABI_VERSION 1
+
+/* return / status codes */
+enum {
+  DFS_OK = 0,
+  DFS_ERR_INVALID_ARGUMENT = 1, /* null pointer where one is required, bad sizes   */
+  DFS_ERR_UNSUPPORTED = 2,      /* shape or dtype outside the kernels' range       */
+  DFS_ERR_WORKSPACE = 3,        /* workspace smaller than dfs_workspace_size       */
+  DFS_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed           */
+  DFS_ERR_DEVICE_TIMEOUT = 8,   /* device: a bounded wait gave up (bit in status)  */
+  DFS_ERR_NUMERIC = 16,         /* device: potentials not finite after re-scaling  */
+  DFS_WARN_CG_NOT_CONVERGED = 32/* device: some CG solve hit max_iter (soft)       */
+};
+
+/* element type of Q, K, V */
+enum { DFS_BF16 = 0, DFS_F16 = 1, DFS_F32 = 2 };
+
+/* where the cost comes from */
+enum {
+  DFS_COST_QK = 0,    /* C = -QK^T/sqrt(d) (+ position / geometry terms)          */
+  DFS_COST_DENSE = 1  /* C read from a dense (B,H,N,N) fp32 tensor                */
+};
+
+typedef struct {
+  int32_t B, H, N, d;     /* problems are (B, H); N points per side; head dim d  */
+  int32_t in_dtype;       /* DFS_BF16 / DFS_F16 / DFS_F32 for Q, K, V             */
+  int32_t cost_mode;      /* DFS_COST_QK / DFS_COST_DENSE                          */
+  int32_t K_iter;         /* Sinkhorn iterations (row update then column update)  */
+  int32_t check_every;    /* early-stop test period (used when threshold > 0)     */
+  float lam;              /* marginal penalty; kappa = lam/(lam+eps); +inf -> 1   */
+  float r_0;              /* geometry scale r_0                                    */
+  float threshold;        /* L-inf early-stop tolerance on the potentials; <= 0 off */
+  float reserved;
+} dfs_problem;
+
+typedef struct {
+  /* inputs */
+  const void* Q;            /* (B,H,N,d) in_dtype, DFS_COST_QK                       */
+  const void* K;            /* (B,H,N,d) in_dtype, DFS_COST_QK                       */
+  const void* V;            /* (B,H,N,d) in_dtype, or NULL when O is NULL            */
+  const float* C;           /* (B,H,N,N) dense cost, DFS_COST_DENSE                  */
+  const float* x_res;       /* (B,N,3) or NULL: no geometry term, no centroid        */
+  const float* pos_weight;  /* (H,68) or NULL: no position term                      */
+  const int32_t* pos_bins;  /* (B,N,N) int32 in [0,68), required with pos_weight     */
+  const float* eps;         /* (H,) entropic regularisation                          */
+  const float* w_dist;      /* (H,) geometry weight, or NULL                         */
+  const float* log_mu;      /* (B,H,N) log row marginals                             */
+  const float* log_nu;      /* (B,H,N) log column marginals                          */
+  const float* log_u_init;  /* (B,H,N) warm start or NULL                            */
+  const float* log_v_init;  /* (B,H,N) warm start or NULL                            */
+  const float* mask;        /* (B,N) 1 = real point, 0 = padding; or NULL            */
+  /* outputs */
+  float* O;                 /* (B,H,N,d) O = T_norm V (padded rows 0), or NULL       */
+  float* x_centroid;        /* (B,H,N,3) T_norm x, or NULL                           */
+  float* log_u;             /* (B,H,N) row potential, padded entries 0               */
+  float* log_v;             /* (B,H,N) column potential, padded entries 0            */
+  int32_t* status;          /* device int32, error bits OR-ed in; or NULL            */
+  float* T_norm;            /* (B,H,N,N) row-normalised plan, or NULL (materialises  */
+                            /* the plan: only for the dense compute_transport_output)*/
+} dfs_fwd_args;
+
+typedef struct {
+  float rtol;               /* CG stops when ||r|| <= max(atol, rtol*||r0||)        */
+  float atol;
+  int32_t max_iter;         /* CG iteration cap                                      */
+  int32_t reserved;
+} dfs_cg_params;
+
+typedef struct {
+  /* forward inputs (same tensors as the forward call) */
+  const void* Q; const void* K; const void* V;
+  const float* x_res; const float* pos_weight; const int32_t* pos_bins;
+  const float* eps; const float* w_dist;
+  const float* log_mu; const float* log_nu;
+  const float* mask;
+  /* forward outputs */
+  const float* log_u;       /* (B,H,N) from dfs_fwd                                  */
+  const float* log_v;       /* (B,H,N) from dfs_fwd                                  */
+  /* upstream gradients */
+  const float* dO;          /* (B,H,N,d) dL/dO (after the gate), fp32                */
+  const float* dxc;         /* (B,H,N,3) dL/dx_centroid, or NULL                     */
+  /* gradients (written, not accumulated); NULL = not wanted */
+  float* dQ; float* dK; float* dV;      /* (B,H,N,d) fp32                           */
+  float* dlog_mu; float* dlog_nu;       /* (B,H,N)                                  */
+  float* dx_res;            /* (B,N,3)                                               */
+  float* dpos_weight;       /* (H,68)                                                */
+  float* dw_dist;           /* (H,)                                                  */
+  /* per-problem CG report, (B*H) each, or NULL */
+  int32_t* cg_iters;
+  float* cg_residual;
+  int32_t* status;
+} dfs_bwd_args;
+
+/* Library ABI version (DFS_ABI_VERSION of the build). */
+int dfs_abi_version(void);
+
+/* Text for a status code or an OR of device status bits. */
+const char* dfs_status_string(int status);
+
+/* Largest N the resident (on-chip) kernels accept for head dim d; 0 if d is
+ * unsupported. */
+int dfs_max_n(int d);
+
+/* Bytes of device workspace dfs_fwd / dfs_bwd need for problem p. */
+int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes);
+
+/* Forward: Sinkhorn potentials and transport output.
+ * Replaces FlashSinkhornFunction.forward
+ *   (src/deepfold/model/kernels/sinkhorn_kernel.py:1923-2084) and, with
+ *   DFS_COST_DENSE and O == NULL, the loop of sinkhorn_solve
+ *   (src/deepfold/model/sinkhorn.py:17-112). */
+int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace,
+            size_t workspace_bytes, void* stream);
+
+/* Backward: implicit-function-theorem gradients via device-side conjugate
+ * gradient.  Replaces FlashSinkhornFunction.backward
+ *   (src/deepfold/model/kernels/sinkhorn_kernel.py:2086-2382), whose unrolled
+ *   K-step adjoint it equals at a converged fixed point. */
+int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a,
+            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Self-test of the tensor-core building blocks: runs the three tcgen05 MMA
+ * operand layouts the kernels use on caller-provided data (see csrc). */
+int dfs_selftest_mma(int which, const float* A, const float* B, float* D,
+                     int M, int N, int K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DFSINK_H */

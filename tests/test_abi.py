@@ -1,0 +1,68 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+declared in include/dfsink.h, and rejects bad arguments on the host before any
+CUDA call is made."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from deepfold import _native as nat
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "dfsink.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^[A-Za-z_][\w\s\*]*?\b(dfs_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    nat.build_library()
+    return nat.lib()
+
+
+def test_header_declares_the_expected_entry_points():
+    assert set(declared_functions()) == set(nat.EXPORTED_SYMBOLS)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_strings(lib):
+    assert lib.dfs_abi_version() == 1
+    assert nat.status_string(nat.DFS_OK) == "ok"
+    assert "workspace" in nat.status_string(nat.DFS_ERR_WORKSPACE)
+    assert nat.max_n(32) >= 384
+    assert nat.max_n(48) == 0
+
+
+def test_struct_sizes_match_header_layout():
+    # every pointer field is 8 bytes; the problem block is 8 int32 + 4 floats
+    assert ctypes.sizeof(nat.DfsProblem) == 48
+    assert ctypes.sizeof(nat.DfsFwdArgs) == 20 * 8
+    assert ctypes.sizeof(nat.DfsBwdArgs) == 26 * 8
+    assert ctypes.sizeof(nat.DfsCgParams) == 16
+
+
+def test_host_side_validation(lib):
+    p = nat.make_problem(2, 8, 384, 32, __import__("torch").bfloat16, 20, float("inf"), 10.0)
+    a = nat.DfsFwdArgs()
+    assert lib.dfs_fwd(p, a, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    big = nat.make_problem(1, 1, 4096, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
+    fake = nat.DfsFwdArgs(Q=16, K=16, V=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16)
+    assert lib.dfs_fwd(big, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
+    bad = nat.make_problem(1, 1, 64, 32, __import__("torch").bfloat16, 20, -1.0, 10.0)
+    assert lib.dfs_fwd(bad, fake, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    cg = nat.DfsCgParams(rtol=1e-6, atol=1e-6, max_iter=-1)
+    ok = nat.make_problem(1, 1, 64, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
+    assert lib.dfs_bwd(ok, cg, nat.DfsBwdArgs(), None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    fws, bws = ctypes.c_size_t(7), ctypes.c_size_t(7)
+    assert lib.dfs_workspace_size(ok, ctypes.byref(fws), ctypes.byref(bws)) == nat.DFS_OK
+    assert fws.value == 0
+    assert lib.dfs_selftest_mma(5, None, None, None, 64, 32, 32, None) == nat.DFS_ERR_INVALID_ARGUMENT

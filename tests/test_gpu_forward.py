@@ -1,0 +1,145 @@
+"""Forward parity of the CUDA flash-Sinkhorn path against the CPU oracle.
+
+Tolerances: output max-abs error <= 2e-3 with bf16
+inputs and fp32 potentials; row and column marginal residuals <= 1e-4.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import make_inputs, max_abs, oracle_run
+from oracle import sinkhorn_oracle as orc
+
+from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn, last_cg_report
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL = 2e-3
+MARG_TOL = 1e-4
+
+
+def run(inp, K_iter, lam, **kw):
+    O, xc, lu, lv = flash_sinkhorn(inp["Q"], inp["K"], inp["V"], kw.get("x_res"), kw.get("pos_weight"),
+                                   kw.get("pos_bins"), inp["eps"], kw.get("w_dist"), inp["log_mu"],
+                                   inp["log_nu"], K_iter=K_iter, lam=lam, r_0=kw.get("r_0", 10.0),
+                                   mask=inp["mask"])
+    torch.cuda.synchronize()
+    return O, xc, lu, lv
+
+
+def marginals(inp, lu, lv):
+    """Residuals of P = exp(f + S + g) built from the kernel's potentials."""
+    Q = inp["Q"].float().cpu().numpy()
+    K = inp["K"].float().cpu().numpy()
+    eps = inp["eps"].cpu().numpy()
+    mask = None if inp["mask"] is None else inp["mask"].cpu().numpy()
+    B, H, N, d = Q.shape
+    worst = 0.0
+    for b in range(B):
+        for h in range(H):
+            S = (Q[b, h].astype(np.float64) @ K[b, h].T.astype(np.float64)) / math.sqrt(d) / eps[h]
+            r, c = orc.marginal_residuals(S, lu[b, h].astype(np.float64), lv[b, h].astype(np.float64),
+                                          inp["log_mu"][b, h].cpu().numpy(), inp["log_nu"][b, h].cpu().numpy(),
+                                          None if mask is None else mask[b])
+            worst = max(worst, r, c)
+    return worst
+
+
+def test_config1_forward():
+    """Config 1: B=2 H=8 N=384 d=32 bf16, eps=1, 20 iterations, uniform marginals."""
+    inp = make_inputs(2, 8, 384, 32, seed=0)
+    O, _, lu, lv = run(inp, 20, float("inf"))
+    res, _ = oracle_run(inp, 20, float("inf"), with_grad=False)
+    assert max_abs(O.cpu().numpy(), res.O_avg) <= OUT_TOL
+    assert max_abs(lu.cpu().numpy(), res.log_u) <= 1e-3
+    assert max_abs(lv.cpu().numpy(), res.log_v) <= 1e-3
+    assert marginals(inp, lu.cpu().numpy(), lv.cpu().numpy()) <= MARG_TOL
+    st = last_cg_report()
+    del st
+
+
+def test_reference_lambda_matches_balanced():
+    """lam = 1e6 (what the reference needs for the balanced case) ~ lam = inf."""
+    inp = make_inputs(1, 4, 128, 32, seed=3)
+    O1, _, lu1, _ = run(inp, 20, 1e6)
+    O2, _, lu2, _ = run(inp, 20, float("inf"))
+    assert max_abs(O1.cpu().numpy(), O2.cpu().numpy()) < 1e-4
+
+
+@pytest.mark.parametrize("N,lengths,eps,K", [(320, [320, 150], 0.5, 50), (100, [100, 37], 1.0, 30),
+                                             (384, [384, 64], 0.5, 50)])
+def test_masked_varlen_nonuniform(N, lengths, eps, K):
+    inp = make_inputs(2, 4, N, 32, seed=5, eps=eps, uniform=False, lengths=lengths)
+    O, _, lu, lv = run(inp, K, float("inf"))
+    res, _ = oracle_run(inp, K, float("inf"), with_grad=False)
+    assert max_abs(O.cpu().numpy(), res.O_avg) <= OUT_TOL
+    assert marginals(inp, lu.cpu().numpy(), lv.cpu().numpy()) <= MARG_TOL
+    m = inp["mask"].cpu().numpy()
+    for b in range(2):
+        assert np.all(lu.cpu().numpy()[b][:, m[b] == 0] == 0)
+        assert np.all(lv.cpu().numpy()[b][:, m[b] == 0] == 0)
+        assert np.all(O.cpu().numpy()[b][:, m[b] == 0] == 0)
+
+
+@pytest.mark.parametrize("lam,K", [(1.0, 5), (1.0, 20), (0.3, 7)])
+def test_uot_full_features(lam, K):
+    """Position bins, geometry, centroid, per-head eps, kappa < 1 (reference defaults)."""
+    B, H, N, d = 2, 4, 96, 32
+    inp = make_inputs(B, H, N, d, seed=11, dtype=torch.float32, eps=[0.5, 1.0, 2.0, 4.0], uniform=False)
+    g = torch.Generator().manual_seed(12)
+    extra = dict(x_res=(torch.randn(B, N, 3, generator=g) * 3).cuda(),
+                 pos_weight=(torch.randn(H, 68, generator=g) * 0.3).cuda(),
+                 pos_bins=torch.randint(0, 68, (B, N, N), generator=g, dtype=torch.int32).cuda(),
+                 w_dist=(torch.rand(H, generator=g) * 0.5).cuda())
+    O, xc, lu, lv = run(inp, K, lam, **extra)
+    res, _ = oracle_run(inp, K, lam, with_grad=False, **extra)
+    # fp32 inputs go through tf32 tensor-core products
+    assert max_abs(O.cpu().numpy(), res.O_avg) <= 5e-3
+    assert max_abs(xc.cpu().numpy(), res.xc) <= 1e-2
+    assert max_abs(lu.cpu().numpy(), res.log_u) <= 5e-3
+    assert max_abs(lv.cpu().numpy(), res.log_v) <= 5e-3
+
+
+def test_small_eps_restabilises():
+    """eps = 0.05 spans exp(+-400): exercises the re-absorption path."""
+    inp = make_inputs(1, 2, 128, 32, seed=21, eps=0.05)
+    O, _, lu, lv = run(inp, 60, float("inf"))
+    res, _ = oracle_run(inp, 60, float("inf"), with_grad=False)
+    assert np.isfinite(O.cpu().numpy()).all()
+    assert max_abs(O.cpu().numpy(), res.O_avg) <= 1e-2
+    assert max_abs(lv.cpu().numpy(), res.log_v) / max(np.abs(res.log_v).max(), 1) <= 1e-3
+
+
+@pytest.mark.parametrize("N", [8, 64, 65, 200])
+def test_odd_sizes(N):
+    inp = make_inputs(1, 2, N, 32, seed=N)
+    O, _, lu, lv = run(inp, 15, 1.0)
+    res, _ = oracle_run(inp, 15, 1.0, with_grad=False)
+    assert max_abs(O.cpu().numpy(), res.O_avg) <= OUT_TOL
+    assert max_abs(lu.cpu().numpy(), res.log_u) <= 1e-3
+
+
+def test_zero_iterations_and_warm_start():
+    inp = make_inputs(1, 2, 64, 32, seed=2)
+    O0, _, lu0, lv0 = run(inp, 0, 1.0)
+    res, _ = oracle_run(inp, 0, 1.0, with_grad=False)
+    assert max_abs(O0.cpu().numpy(), res.O_avg) <= OUT_TOL
+    # warm start from converged potentials: one more iteration changes little
+    _, _, lu, lv = run(inp, 40, 1.0)
+    O1, _, lu1, lv1 = flash_sinkhorn(inp["Q"], inp["K"], inp["V"], None, None, None, inp["eps"], None,
+                                     inp["log_mu"], inp["log_nu"], K_iter=1, lam=1.0, log_u_init=lu,
+                                     log_v_init=lv)
+    assert max_abs(lv1.cpu().numpy(), lv.cpu().numpy()) < 1e-4
+
+
+def test_bf16_and_fp32_inputs_agree():
+    inp = make_inputs(1, 2, 128, 32, seed=4)
+    O1, _, _, _ = run(inp, 20, 1.0)
+    inp32 = dict(inp)
+    for k in ("Q", "K", "V"):
+        inp32[k] = inp[k].float()
+    O2, _, _, _ = run(inp32, 20, 1.0)
+    assert max_abs(O1.cpu().numpy(), O2.cpu().numpy()) < 1e-6
