@@ -43,13 +43,18 @@ struct BwdCfg {
   static constexpr uint32_t OFF_SA = OFF_T + 256u * NP;               // 64 x DH slab operand
   static constexpr uint32_t OFF_DA = OFF_SA + 256u * DH;              // 64 x DH dO slab
   static constexpr uint32_t OFF_KV = OFF_DA + 256u * DH;              // NP x DH operand / partials
-  static constexpr uint32_t XS = 2 * NP + 3 * 64 + 32;                // exchange stride (floats)
-  static constexpr uint32_t OFF_XCH = OFF_KV + 4u * NP * DH;          // 2 x XS
-  static constexpr uint32_t OFF_COL = OFF_XCH + 8u * XS;              // column / all-row vectors
+  // one-off exchange of phase 2 (single buffer) and the CG / all-gather
+  // exchanges (double buffered), see ClusterExchange
+  static constexpr int RSA = 2 * NP + 3 * 64 + 8;
+  static constexpr int RSB = NP + 8;
+  static constexpr uint32_t OFF_XA = OFF_KV + 4u * NP * DH;           // C x RSA
+  static constexpr uint32_t OFF_XB = OFF_XA + 4u * C * RSA;           // 2 x C x RSB
+  static constexpr uint32_t OFF_COL = OFF_XB + 8u * C * RSB;          // column / all-row vectors
   static constexpr uint32_t OFF_ROW = OFF_COL + 4u * 12 * NP;         // slab-row vectors
   static constexpr uint32_t OFF_MISC = OFF_ROW + 4u * 4 * 64;
   static constexpr uint32_t SMEM_NEED = OFF_MISC + 1024 + 1024;
   static constexpr uint32_t SMEM = SMEM_NEED > 122880u ? SMEM_NEED : 122880u;
+  static_assert(SMEM <= 232448u, "exceeds the 227 KB of shared memory a CTA can use");
   static_assert(8u * 2 * NP * 4 <= 4u * NP * DH, "column partials must fit the K/V region");
   static_assert(NP + DH <= 512, "TMEM columns");
 };
@@ -69,7 +74,8 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   float* SA = reinterpret_cast<float*>(base + Cfg::OFF_SA);
   float* DA = reinterpret_cast<float*>(base + Cfg::OFF_DA);
   float* KV = reinterpret_cast<float*>(base + Cfg::OFF_KV);
-  float* xch = reinterpret_cast<float*>(base + Cfg::OFF_XCH);
+  ClusterExchange<C, Cfg::RSA> exa{reinterpret_cast<float*>(base + Cfg::OFF_XA), 0, 0};
+  ClusterExchange<C, Cfg::RSB> exb{reinterpret_cast<float*>(base + Cfg::OFF_XB), 0, 0};
   float* colv = reinterpret_cast<float*>(base + Cfg::OFF_COL);
   float* rowv = reinterpret_cast<float*>(base + Cfg::OFF_ROW);
   float* misc = reinterpret_cast<float*>(base + Cfg::OFF_MISC);       // 192 scalars
@@ -78,6 +84,9 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int crank = static_cast<int>(cluster_rank());
+  exa.rank = exb.rank = crank;
+  constexpr int OWN = NP / 4;  // threads that own 4 consecutive columns for the exchanges
+  const int j4 = 4 * tid;
   const int prob = blockIdx.x / C;
   const int bb = prob / p.H, hh = prob % p.H;
   const int N = p.N;
@@ -91,7 +100,6 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   const float w_h = p.w_dist ? p.w_dist[hh] : 0.0f;
   int err = 0;
   uint32_t mma_phase = 0;
-  int xbuf = 0;
 
   auto mma_wait = [&]() {
     if (!mbar_wait(mbar, mma_phase & 1)) err |= DFS_ERR_DEVICE_TIMEOUT;
@@ -285,63 +293,59 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     }
   }
   __syncthreads();
-  {
-    float* xb = xch + xbuf * Cfg::XS;
-    for (int j = tid; j < NP; j += 256) {
-      float a = 0.0f, b = 0.0f;
+  if (tid < OWN) {
+    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        a += red[w * NP + j];
-        b += red[8 * NP + w * NP + j];
-      }
-      xb[j] = a;
-      xb[NP + j] = b;
+    for (int w = 0; w < 8; ++w) {
+      const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
+      const float4 y = *reinterpret_cast<const float4*>(red + 8 * NP + w * NP + j4);
+      a4 = make_float4(a4.x + x.x, a4.y + x.y, a4.z + x.z, a4.w + x.w);
+      b4 = make_float4(b4.x + y.x, b4.y + y.y, b4.z + y.z, b4.w + y.w);
     }
-    if ((lane & 3) == 0) {  // this slab's rows for the all-gathers
-      const int li = 8 * warp + rho;
-      xb[2 * NP + li] = fr;
-      xb[2 * NP + 64 + li] = inv_r;
-      xb[2 * NP + 128 + li] = D_r;
-    }
-    if (tid == 0) {
-      float a = 0.0f, b = 0.0f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        a += misc[w];
-        b += misc[8 + w];
-      }
-      xb[2 * NP + 192] = a;
-      xb[2 * NP + 193] = b;
-    }
+    exa.put4(j4, a4);
+    exa.put4(NP + j4, b4);
   }
-  cluster_sync();
+  if ((lane & 3) == 0) {  // this slab's rows for the all-gathers
+    const int li = 8 * warp + rho;
+    exa.put(2 * NP + li, fr);
+    exa.put(2 * NP + 64 + li, inv_r);
+    exa.put(2 * NP + 128 + li, D_r);
+  }
+  if (tid == 0) {
+    float a = 0.0f, b = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      a += misc[w];
+      b += misc[8 + w];
+    }
+    exa.put4(2 * NP + 192, make_float4(a, b, 0.0f, 0.0f));
+  }
+  exa.sync();
   float cc[MC], gv[MC];
   bool okc[MC];
   float sum_fbar = 0.0f, sum_r = 0.0f;
-  {
-    const uint32_t xa = smem_u32(xch + xbuf * Cfg::XS);
 #pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      const int j = tid + 256 * m;
-      cc[m] = gv[m] = 0.0f;
-      okc[m] = j < NP && colv[BC_OK * NP + j] != 0.0f;
-      if (j < NP) {
-        for (int c = 0; c < C; ++c) {
-          cc[m] += dsmem_ld(dsmem_addr(xa + 4u * j, c));
-          gv[m] += dsmem_ld(dsmem_addr(xa + 4u * (NP + j), c));
-        }
-        const uint32_t src = static_cast<uint32_t>(j >> 6), li = static_cast<uint32_t>(j & 63);
-        colv[BC_FA * NP + j] = dsmem_ld(dsmem_addr(xa + 4u * (2 * NP + li), src));
-        colv[BC_INV * NP + j] = dsmem_ld(dsmem_addr(xa + 4u * (2 * NP + 64 + li), src));
-        colv[BC_DD * NP + j] = dsmem_ld(dsmem_addr(xa + 4u * (2 * NP + 128 + li), src));
+  for (int m = 0; m < MC; ++m) {
+    const int j = tid + 256 * m;
+    cc[m] = gv[m] = 0.0f;
+    okc[m] = j < NP && colv[BC_OK * NP + j] != 0.0f;
+    if (j < NP) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        cc[m] += exa.from(c)[j];
+        gv[m] += exa.from(c)[NP + j];
       }
-    }
-    for (int c = 0; c < C; ++c) {
-      sum_fbar += dsmem_ld(dsmem_addr(xa + 4u * (2 * NP + 192), c));
-      sum_r += dsmem_ld(dsmem_addr(xa + 4u * (2 * NP + 193), c));
+      const float* src = exa.from(j >> 6);
+      colv[BC_FA * NP + j] = src[2 * NP + (j & 63)];
+      colv[BC_INV * NP + j] = src[2 * NP + 64 + (j & 63)];
+      colv[BC_DD * NP + j] = src[2 * NP + 128 + (j & 63)];
     }
   }
-  xbuf ^= 1;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    sum_fbar += exa.from(c)[2 * NP + 192];
+    sum_r += exa.from(c)[2 * NP + 193];
+  }
   __syncthreads();
 
   // ---------------------------------------------------------------- phase 3 (CG)
@@ -420,46 +424,49 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
       misc[48 + warp] = a2;
     }
     __syncthreads();
-    float* xbm = xch + xbuf * Cfg::XS;
-    for (int j = tid; j < NP; j += 256) {
-      float s = 0.0f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) s += red[w * NP + j];
-      xbm[j] = s;
-    }
-    if (tid == 0) {
-      float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+    if (tid < OWN) {
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
-        s0 += misc[32 + w];
-        s1 += misc[40 + w];
-        s2 += misc[48 + w];
+        const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
+        s4 = make_float4(s4.x + x.x, s4.y + x.y, s4.z + x.z, s4.w + x.w);
       }
-      xbm[NP] = s0;
-      xbm[NP + 1] = s1;
-      xbm[NP + 2] = s2;
+      exb.put4(j4, s4);
+      if (tid == 0) {
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          s0 += misc[32 + w];
+          s1 += misc[40 + w];
+          s2 += misc[48 + w];
+        }
+        exb.put4(NP, make_float4(s0, s1, s2, 0.0f));
+      }
     }
-    cluster_sync();
-    const uint32_t xa = smem_u32(xbm);
+    exb.sync();
     float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
 #pragma unroll
     for (int m = 0; m < MC; ++m) {
       const int j = tid + 256 * m;
       float t = 0.0f;
-      if (j < NP)
-        for (int c = 0; c < C; ++c) t += dsmem_ld(dsmem_addr(xa + 4u * j, c));
+      if (j < NP) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) t += exb.from(c)[j];
+      }
       w2[m] = okc[m] ? t + d2[m] * u2[m] : 0.0f;
       c0 += res2[m] * u2[m];
       c1 += w2[m] * u2[m];
       c2 += res2[m] * res2[m];
     }
     float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll
     for (int c = 0; c < C; ++c) {
-      g0 += dsmem_ld(dsmem_addr(xa + 4u * NP, c));
-      g1 += dsmem_ld(dsmem_addr(xa + 4u * (NP + 1), c));
-      g2 += dsmem_ld(dsmem_addr(xa + 4u * (NP + 2), c));
+      const float4 d = *reinterpret_cast<const float4*>(exb.from(c) + NP);
+      g0 += d.x;
+      g1 += d.y;
+      g2 += d.z;
     }
-    xbuf ^= 1;
+    exb.next();
     c0 = cta_sum(c0, 56);
     c1 = cta_sum(c1, 64);
     c2 = cta_sum(c2, 72);
@@ -530,21 +537,19 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     const float a = warp_sum(own ? rsum_r * x1 : 0.0f);
     if (lane == 0) misc[80 + warp] = a;
     __syncthreads();
-    float* xbm = xch + xbuf * Cfg::XS;
-    if ((lane & 3) == 0) xbm[8 * warp + rho] = x1;
+    if ((lane & 3) == 0) exb.put(8 * warp + rho, x1);
     if (tid == 0) {
-      float s = 0.0f;
+      float t = 0.0f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) s += misc[80 + w];
-      xbm[64] = s;
+      for (int w = 0; w < 8; ++w) t += misc[80 + w];
+      exb.put(64, t);
     }
-    cluster_sync();
-    const uint32_t xa = smem_u32(xbm);
-    for (int i = tid; i < NP; i += 256)
-      colv[BC_W1 * NP + i] = dsmem_ld(dsmem_addr(xa + 4u * (i & 63), static_cast<uint32_t>(i >> 6)));
+    exb.sync();
+    for (int i = tid; i < NP; i += 256) colv[BC_W1 * NP + i] = exb.from(i >> 6)[i & 63];
     float tot = 0.0f;
-    for (int c = 0; c < C; ++c) tot += dsmem_ld(dsmem_addr(xa + 4u * 64, c));
-    xbuf ^= 1;
+#pragma unroll
+    for (int c = 0; c < C; ++c) tot += exb.from(c)[64];
+    exb.next();
     if (kap >= 1.0f) tshift = sum_r > 0.0f ? -tot / sum_r : 0.0f;
   }
   if (p.dlog_mu && (lane & 3) == 0 && grow < N) p.dlog_mu[bh * N + grow] = rok ? rsum_r * (x1 + tshift) : 0.0f;

@@ -161,6 +161,43 @@ DFS_DEV uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
+DFS_DEV void dsmem_st(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+DFS_DEV void dsmem_st4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// Push-style all-to-all over distributed shared memory.  Every CTA of the
+// cluster owns a receive buffer recv[2][C][RS] (floats); a CTA publishes its
+// values into slot [buf][its rank] of every CTA with remote stores (which do
+// not stall the writer), one cluster barrier orders them, and readers then use
+// their own copy with ordinary shared-memory loads.  The two buffers alternate:
+// a CTA can only start the next exchange after every peer has arrived at the
+// barrier of this one, i.e. has finished reading the previous one.
+template <int C, int RS>
+struct ClusterExchange {
+  float* recv;
+  int buf;
+  int rank;
+  DFS_DEV uint32_t slot_addr(int off) const { return smem_u32(recv + (buf * C + rank) * RS + off); }
+  DFS_DEV void put(int off, float v) const {
+    const uint32_t a = slot_addr(off);
+#pragma unroll
+    for (int c = 0; c < C; ++c) dsmem_st(dsmem_addr(a, static_cast<uint32_t>(c)), v);
+  }
+  DFS_DEV void put4(int off, float4 v) const {
+    const uint32_t a = slot_addr(off);
+#pragma unroll
+    for (int c = 0; c < C; ++c) dsmem_st4(dsmem_addr(a, static_cast<uint32_t>(c)), v);
+  }
+  DFS_DEV const float* from(int src) const { return recv + (buf * C + src) * RS; }
+  DFS_DEV void sync() const { cluster_sync(); }
+  DFS_DEV void next() { buf ^= 1; }
+};
+
 DFS_DEV float dsmem_ld(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");

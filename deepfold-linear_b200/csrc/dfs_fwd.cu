@@ -32,15 +32,16 @@ struct FwdCfg {
   static constexpr uint32_t OFF_Q = OFF_T + 256u * NP;              // 64 x DH
   static constexpr uint32_t OFF_KV = OFF_Q + 256u * DH;             // NP x DH (K, then V)
   static constexpr uint32_t OFF_RED = OFF_KV + 4u * NP * DH;        // 8 x NP
-  static constexpr uint32_t XS = NP + 32;                           // exchange stride (floats)
-  static constexpr uint32_t OFF_XCH = OFF_RED + 32u * NP;           // 2 x XS
-  static constexpr uint32_t OFF_COL = OFF_XCH + 8u * XS;            // 10 x NP column vectors
+  static constexpr int RS = NP + 8;                                 // exchange slot (floats)
+  static constexpr uint32_t OFF_XCH = OFF_RED + 32u * NP;           // 2 x C x RS receive buffers
+  static constexpr uint32_t OFF_COL = OFF_XCH + 8u * C * RS;        // 10 x NP column vectors
   static constexpr uint32_t OFF_ROW = OFF_COL + 40u * NP;           // 4 x 64 row vectors
   static constexpr uint32_t OFF_MISC = OFF_ROW + 4u * 4 * 64;       // scalars, barrier
   // at least 120 KB so that only one CTA fits per SM and its 512 TMEM columns
   // never wait for another CTA of the same cluster
   static constexpr uint32_t SMEM_NEED = OFF_MISC + 512 + 1024;      // + alignment slack
   static constexpr uint32_t SMEM = SMEM_NEED > 122880u ? SMEM_NEED : 122880u;
+  static_assert(SMEM <= 232448u, "exceeds the 227 KB of shared memory a CTA can use");
 };
 
 // column-vector slots (each NP floats)
@@ -58,7 +59,7 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
   float* Qs = reinterpret_cast<float*>(base + Cfg::OFF_Q);
   float* KVs = reinterpret_cast<float*>(base + Cfg::OFF_KV);
   float* red = reinterpret_cast<float*>(base + Cfg::OFF_RED);
-  float* xch = reinterpret_cast<float*>(base + Cfg::OFF_XCH);
+  ClusterExchange<C, Cfg::RS> ex{reinterpret_cast<float*>(base + Cfg::OFF_XCH), 0, 0};
   float* colv = reinterpret_cast<float*>(base + Cfg::OFF_COL);
   float* rowv = reinterpret_cast<float*>(base + Cfg::OFF_ROW);
   float* misc = reinterpret_cast<float*>(base + Cfg::OFF_MISC);     // [0..63] scalars
@@ -67,6 +68,9 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int crank = static_cast<int>(cluster_rank());
+  ex.rank = crank;
+  constexpr int OWN = NP / 4;  // threads that own 4 consecutive columns for vector work
+  const int j4 = 4 * tid;
   const int prob = blockIdx.x / C;
   const int bb = prob / p.H, hh = prob % p.H;
   const int N = p.N;
@@ -139,7 +143,6 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
   float atr = 0.0f, fabs_r = 0.0f;
   float wk[NS];
   uint32_t cokm = 0;                               // bit k: column 32k+lane valid
-  int xbuf = 0;                                    // exchange double-buffer index
 
   // S' (log2 units, bias terms included, invalid entries kNeg) into E.
   BiasArgs bias;
@@ -217,25 +220,36 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
       red[warp * NP + 32 * k + lane] = cm;
     }
     __syncthreads();
-    float* xb = xch + xbuf * Cfg::XS;
-    for (int j = tid; j < NP; j += 256) {
-      float m = kNeg;
+    if (tid < OWN) {
+      float4 m = make_float4(kNeg, kNeg, kNeg, kNeg);
 #pragma unroll
-      for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w * NP + j]);
-      xb[j] = m;
+      for (int w = 0; w < 8; ++w) {
+        const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
+        m = make_float4(fmaxf(m.x, x.x), fmaxf(m.y, x.y), fmaxf(m.z, x.z), fmaxf(m.w, x.w));
+      }
+      ex.put4(j4, m);
     }
-    cluster_sync();
-    const uint32_t xb_addr = smem_u32(xb);
-    for (int j = tid; j < NP; j += 256) {
-      float m = kNeg;
-      for (int c = 0; c < C; ++c) m = fmaxf(m, dsmem_ld(dsmem_addr(xb_addr + 4u * j, c)));
-      const bool ok = colv[CV_OK * NP + j] != 0.0f;
-      const float beta = ok ? m : 0.0f;
-      colv[CV_GN * NP + j] = beta;              // beta (temporary)
-      colv[CV_BT * NP + j] = beta - colv[CV_G * NP + j];
-      colv[CV_GABS * NP + j] = colv[CV_G * NP + j];
+    ex.sync();
+    if (tid < OWN) {
+      float m[4] = {kNeg, kNeg, kNeg, kNeg};
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const float4 x = *reinterpret_cast<const float4*>(ex.from(c) + j4);
+        m[0] = fmaxf(m[0], x.x);
+        m[1] = fmaxf(m[1], x.y);
+        m[2] = fmaxf(m[2], x.z);
+        m[3] = fmaxf(m[3], x.w);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = j4 + q;
+        const float beta = colv[CV_OK * NP + j] != 0.0f ? m[q] : 0.0f;
+        colv[CV_GN * NP + j] = beta;  // beta (temporary)
+        colv[CV_BT * NP + j] = beta - colv[CV_G * NP + j];
+        colv[CV_GABS * NP + j] = colv[CV_G * NP + j];
+      }
     }
-    xbuf ^= 1;
+    ex.next();
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
@@ -254,13 +268,11 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
 
   // Row update: f = kappa (a - LSE_j(S + g)); returns the new f of row rho.
   auto row_pass = [&](float* rowmax_out, float* v_out) -> float {
-    float mw = kNeg;
-#pragma unroll
-    for (int k = 0; k < NS; ++k) mw = fmaxf(mw, ((cokm >> k) & 1u) ? wk[k] : kNeg);
-    mw = warp_max(mw);
+    // wk = beta + (g - g_abs) <= kDrift (beta <= 0 and the drift is bounded by
+    // re-absorption), so exp2(wk) needs no shift
     float v[NS];
 #pragma unroll
-    for (int k = 0; k < NS; ++k) v[k] = ((cokm >> k) & 1u) ? ex2(wk[k] - mw) : 0.0f;
+    for (int k = 0; k < NS; ++k) v[k] = ((cokm >> k) & 1u) ? ex2(wk[k]) : 0.0f;
     float acc[8], amx[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
@@ -281,14 +293,14 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
       for (int k = 0; k < NS; ++k) v_out[k] = v[k];
     }
     if (rowmax_out) return s;
-    const float L = atr + mw + lg2(s);
+    const float L = atr + lg2(s);
     return rok ? kap * (ar - L) : 0.0f;
   };
 
   // Column update from the new row potential fn; writes g_new into CV_GN.
   // Returns a cluster-uniform flag: 1 if the result must be recomputed after
   // re-absorption (underflow / drift), plus the L-inf changes for early stop.
-  auto col_pass = [&](float fn, float fprev, float& dfmax, float& dgmax) -> int {
+  auto col_pass = [&](float fn, float fprev, float& dfmax) -> int {
     const float t = rok ? fn + atr : kNeg;
     const float mu = warp_max(t);
     const float u_r = rok ? ex2(t - mu) : 0.0f;
@@ -310,69 +322,69 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
       misc[16 + warp] = dabs;
     }
     __syncthreads();
-    float mc = kNeg, dfl = 0.0f, dal = 0.0f;
+    if (tid < OWN) {  // CTA partial of 4 columns, shifted to the CTA max, to every CTA
+      float mc = kNeg;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      mc = fmaxf(mc, misc[w]);
-      dfl = fmaxf(dfl, misc[8 + w]);
-      dal = fmaxf(dal, misc[16 + w]);
-    }
-    float fac[8];
+      for (int w = 0; w < 8; ++w) mc = fmaxf(mc, misc[w]);
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < 8; ++w) fac[w] = ex2(misc[w] - mc);
-    float* xb = xch + xbuf * Cfg::XS;
-    for (int j = tid; j < NP; j += 256) {
-      float s = 0.0f;
+      for (int w = 0; w < 8; ++w) {
+        const float fw = ex2(misc[w] - mc);
+        const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
+        s4.x += x.x * fw;
+        s4.y += x.y * fw;
+        s4.z += x.z * fw;
+        s4.w += x.w * fw;
+      }
+      ex.put4(j4, s4);
+      if (tid == 0) {
+        float dfl = 0.0f, dal = 0.0f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) s += red[w * NP + j] * fac[w];
-      xb[j] = s;
+        for (int w = 0; w < 8; ++w) {
+          dfl = fmaxf(dfl, misc[8 + w]);
+          dal = fmaxf(dal, misc[16 + w]);
+        }
+        ex.put4(NP, make_float4(mc, dfl, dal, 0.0f));
+      }
     }
-    if (tid == 0) {
-      xb[NP] = mc;
-      xb[NP + 1] = dfl;
-      xb[NP + 2] = dal;
-    }
-    cluster_sync();
-    const uint32_t xb_addr = smem_u32(xb);
+    ex.sync();
     float mall = kNeg, dfg = 0.0f, dag = 0.0f;
     float mcs[C];
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      mcs[c] = dsmem_ld(dsmem_addr(xb_addr + 4u * NP, c));
-      mall = fmaxf(mall, mcs[c]);
-      dfg = fmaxf(dfg, dsmem_ld(dsmem_addr(xb_addr + 4u * (NP + 1), c)));
-      dag = fmaxf(dag, dsmem_ld(dsmem_addr(xb_addr + 4u * (NP + 2), c)));
+      const float4 sc = *reinterpret_cast<const float4*>(ex.from(c) + NP);
+      mcs[c] = sc.x;
+      mall = fmaxf(mall, sc.x);
+      dfg = fmaxf(dfg, sc.y);
+      dag = fmaxf(dag, sc.z);
     }
-    float wfac[C];
-#pragma unroll
-    for (int c = 0; c < C; ++c) wfac[c] = ex2(mcs[c] - mall);
     int bad = 0;
-    float dgl = 0.0f;
-    for (int j = tid; j < NP; j += 256) {
-      float tot = 0.0f;
+    if (tid < OWN) {
+      float tot[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < C; ++c) tot += dsmem_ld(dsmem_addr(xb_addr + 4u * j, c)) * wfac[c];
-      const bool ok = colv[CV_OK * NP + j] != 0.0f;
-      float gn = 0.0f;
-      if (ok) {
-        if (!(tot > 1e-30f) || !(tot < 3e38f)) bad = 1;
-        gn = kap * (colv[CV_BNU * NP + j] - (colv[CV_BT * NP + j] + mall + lg2(tot)));
-        dgl = fmaxf(dgl, fabsf(gn - colv[CV_G * NP + j]));
+      for (int c = 0; c < C; ++c) {
+        const float wf = ex2(mcs[c] - mall);
+        const float4 x = *reinterpret_cast<const float4*>(ex.from(c) + j4);
+        tot[0] += x.x * wf;
+        tot[1] += x.y * wf;
+        tot[2] += x.z * wf;
+        tot[3] += x.w * wf;
       }
-      colv[CV_GN * NP + j] = gn;
-    }
-    xbuf ^= 1;
-    // CTA-uniform: any bad column, drift since absorption (rows, from the exchange)
-    bad = __syncthreads_or(bad);
-    dgl = warp_max(dgl);
-    if (lane == 0) misc[24 + warp] = dgl;
-    __syncthreads();
-    float dg = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) dg = fmaxf(dg, misc[24 + w]);
-    __syncthreads();
+      for (int q = 0; q < 4; ++q) {
+        const int j = j4 + q;
+        float gn = 0.0f;
+        if (colv[CV_OK * NP + j] != 0.0f) {
+          if (!(tot[q] > 1e-30f) || !(tot[q] < 3e38f)) bad = 1;
+          gn = kap * (colv[CV_BNU * NP + j] - (colv[CV_BT * NP + j] + mall + lg2(tot[q])));
+        }
+        colv[CV_GN * NP + j] = gn;
+      }
+    }
+    ex.next();
+    // cluster-uniform: every CTA combined the same exchanged values
+    bad = __syncthreads_or(bad);
     dfmax = dfg;
-    dgmax = dg;
     return (bad || dag > kDrift) ? 1 : 0;
   };
 
@@ -389,39 +401,49 @@ __global__ void __launch_bounds__(256, 1) resident_fwd_kernel(const FwdParams p)
     if (gdrift > kDrift) absorb();
     const float fprev = fr;
     const float fn = row_pass(nullptr, nullptr);
-    float dfmax, dgmax;
-    int redo = col_pass(fn, fprev, dfmax, dgmax);
+    float dfmax;
+    int redo = col_pass(fn, fprev, dfmax);
     if (redo) {
       fr = fn;   // absorb around the new row potential, then repeat the column update
       absorb();
-      redo = col_pass(fn, fprev, dfmax, dgmax);
+      redo = col_pass(fn, fprev, dfmax);
       if (redo) {
         // drift alone is harmless right after absorption; only underflow is fatal
         bool anybad = false;
-        for (int j = tid; j < NP; j += 256) {
-          const float g = colv[CV_GN * NP + j];
-          if (!isfinite(g)) anybad = true;
-        }
+        for (int j = tid; j < NP; j += 256)
+          if (!isfinite(colv[CV_GN * NP + j])) anybad = true;
         if (__syncthreads_or(anybad)) err |= DFS_ERR_NUMERIC;
       }
     }
     fr = fn;
-    // commit g and track its drift from the last absorption (replicated, uniform)
-    float drift = 0.0f;
-    for (int j = tid; j < NP; j += 256) {
-      const float g = colv[CV_GN * NP + j];
-      colv[CV_G * NP + j] = g;
-      drift = fmaxf(drift, fabsf(g - colv[CV_GABS * NP + j]));
+    // commit g; track its change (early stop) and its drift since absorption
+    float drift = 0.0f, dgl = 0.0f;
+    if (tid < OWN) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = j4 + q;
+        const float g = colv[CV_GN * NP + j];
+        dgl = fmaxf(dgl, fabsf(g - colv[CV_G * NP + j]));
+        colv[CV_G * NP + j] = g;
+        drift = fmaxf(drift, fabsf(g - colv[CV_GABS * NP + j]));
+      }
     }
     drift = warp_max(drift);
-    if (lane == 0) misc[32 + warp] = drift;
+    dgl = warp_max(dgl);
+    if (lane == 0) {
+      misc[32 + warp] = drift;
+      misc[40 + warp] = dgl;
+    }
     __syncthreads();
     gdrift = 0.0f;
+    float dgmax = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) gdrift = fmaxf(gdrift, misc[32 + w]);
+    for (int w = 0; w < 8; ++w) {
+      gdrift = fmaxf(gdrift, misc[32 + w]);
+      dgmax = fmaxf(dgmax, misc[40 + w]);
+    }
 #pragma unroll
     for (int k = 0; k < NS; ++k) wk[k] = colv[CV_BT * NP + 32 * k + lane] + colv[CV_G * NP + 32 * k + lane];
-    __syncthreads();
     if (p.threshold > 0.0f && ((it + 1) % p.check_every) == 0) {
       // threshold is in natural-log units, potentials here in log2 units
       if (fmaxf(dfmax, dgmax) * kLn2 < p.threshold) break;
