@@ -19,6 +19,9 @@ bool dims_ok(const dfs_problem* p) {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? DFS_OK : DFS_ERR_CUDA; }
 
+// the kernels read Q, K, V and dO in 16-byte chunks
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 }  // namespace
 
 extern "C" {
@@ -60,7 +63,8 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if (p->N > dfs_max_n(p->d)) return DFS_ERR_UNSUPPORTED;
-  if (a->O && (reinterpret_cast<uintptr_t>(a->O) & 15)) return DFS_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V))
+    return DFS_ERR_INVALID_ARGUMENT;
   FwdParams q;
   std::memset(&q, 0, sizeof(q));
   q.Q = a->Q; q.K = a->K; q.V = a->V; q.C = a->C;
@@ -87,6 +91,9 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) || !aligned16(a->dQ) ||
+      !aligned16(a->dK) || !aligned16(a->dV))
+    return DFS_ERR_INVALID_ARGUMENT;
   if (p->N > dfs_max_n(p->d)) return DFS_ERR_UNSUPPORTED;
   const size_t need = resident_bwd_workspace(p->B, p->H, p->N, p->d);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return DFS_ERR_WORKSPACE;

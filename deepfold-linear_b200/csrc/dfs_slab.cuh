@@ -95,16 +95,95 @@ DFS_DEV void add_cost_bias(float (&E)[8][NS], const BiasArgs& a, int warp, int l
   }
 }
 
+// 16-byte chunk of elements of type T widened to fp32.
+template <typename T>
+struct Chunk16 {
+  static constexpr int kElems = 16 / static_cast<int>(sizeof(T));
+};
+DFS_DEV void widen(const uint4& raw, float (&v)[8], __nv_bfloat16*) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(h[q]);
+    v[2 * q] = f.x;
+    v[2 * q + 1] = f.y;
+  }
+}
+DFS_DEV void widen(const uint4& raw, float (&v)[8], __half*) {
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __half22float2(h[q]);
+    v[2 * q] = f.x;
+    v[2 * q + 1] = f.y;
+  }
+}
+DFS_DEV void widen(const uint4& raw, float (&v)[4], float*) {
+  v[0] = __uint_as_float(raw.x);
+  v[1] = __uint_as_float(raw.y);
+  v[2] = __uint_as_float(raw.z);
+  v[3] = __uint_as_float(raw.w);
+}
+
+// Rows [row_first, row_first+rows) of a row-major (., DH) tensor of T (rows at
+// or beyond N read as zero) into a 128B-swizzled fp32 operand buffer: with
+// TR = false element (i, c) lands at (i, c) of a buffer with `rows` rows, with
+// TR = true at (c, i) of a buffer with DH rows (the K-major operand holding the
+// transpose).  Each thread moves 16-byte chunks and issues a batch of loads
+// before consuming any, so the global-memory latency is paid once per batch.
+template <int DH, bool TR, typename T>
+DFS_DEV void load_tile(float* dst, const T* src, int row_first, int rows, int N, int tid) {
+  constexpr int EPC = Chunk16<T>::kElems;   // elements per chunk
+  constexpr int CPR = DH / EPC;             // chunks per row
+  constexpr int BATCH = 4;
+  const int total = rows * CPR;
+  for (int base = 0; base < total; base += 256 * BATCH) {
+    uint4 raw[BATCH];
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      const int c = base + tid + 256 * b;
+      const int gi = row_first + c / CPR;
+      raw[b] = make_uint4(0u, 0u, 0u, 0u);
+      if (c < total && gi < N)
+        raw[b] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(gi) * DH) + (c % CPR));
+    }
+#pragma unroll
+    for (int b = 0; b < BATCH; ++b) {
+      const int c = base + tid + 256 * b;
+      if (c >= total) break;
+      const int i = c / CPR, c0 = (c % CPR) * EPC;
+      float v[EPC];
+      widen(raw[b], v, static_cast<T*>(nullptr));
+      if (!TR) {
+#pragma unroll
+        for (int q = 0; q < EPC / 4; ++q)
+          *reinterpret_cast<float4*>(dst + (sw_off(i, c0 + 4 * q, rows) >> 2)) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPC; ++q) dst[sw_off(c0 + q, i, DH) >> 2] = v[q];
+      }
+    }
+  }
+}
+
+template <int DH, bool TR>
+DFS_DEV void load_tile_any(float* dst, const void* src, int dtype, size_t base_row, int row_first, int rows,
+                           int N, int tid) {
+  if (dtype == DFS_BF16)
+    load_tile<DH, TR>(dst, reinterpret_cast<const __nv_bfloat16*>(src) + base_row * DH, row_first, rows, N, tid);
+  else if (dtype == DFS_F16)
+    load_tile<DH, TR>(dst, reinterpret_cast<const __half*>(src) + base_row * DH, row_first, rows, N, tid);
+  else
+    load_tile<DH, TR>(dst, reinterpret_cast<const float*>(src) + base_row * DH, row_first, rows, N, tid);
+}
+
 // Load rows [row_first, row_first+rows) of a (., DH) tensor into a 128B-swizzled
 // fp32 operand buffer with `rows` rows (rows beyond N are zero).
 template <int DH>
 DFS_DEV void load_operand(float* dst, const void* src, int dtype, size_t base_row, int row_first, int rows,
-                          int N, int tid, int nthreads) {
-  for (int e = tid; e < rows * DH; e += nthreads) {
-    const int i = e / DH, c = e % DH, gi = row_first + i;
-    const float v = gi < N ? load_f32(src, (base_row + gi) * DH + c, dtype) : 0.0f;
-    dst[sw_off(i, c, rows) >> 2] = v;
-  }
+                          int N, int tid, int /*nthreads*/) {
+  load_tile_any<DH, false>(dst, src, dtype, base_row, row_first, rows, N, tid);
 }
 
 // Transposed load: element (row gi, c) of a (., DH) tensor goes to (row c,
@@ -112,12 +191,8 @@ DFS_DEV void load_operand(float* dst, const void* src, int dtype, size_t base_ro
 // columns, i.e. the K-major operand holding the tensor's transpose.
 template <int DH>
 DFS_DEV void load_operand_t(float* dst, const void* src, int dtype, size_t base_row, int row_first, int cols,
-                            int N, int tid, int nthreads) {
-  for (int e = tid; e < cols * DH; e += nthreads) {
-    const int i = e / DH, c = e % DH, gi = row_first + i;
-    const float v = gi < N ? load_f32(src, (base_row + gi) * DH + c, dtype) : 0.0f;
-    dst[sw_off(c, i, DH) >> 2] = v;
-  }
+                            int N, int tid, int /*nthreads*/) {
+  load_tile_any<DH, true>(dst, src, dtype, base_row, row_first, cols, N, tid);
 }
 
 // Issue D (TMEM, M=64 rows x NN columns) = A (64 x KD, K-major) * B (NN x KD,

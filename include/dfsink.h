@@ -11,7 +11,8 @@
  *
  * Conventions
  *   - Every pointer is a device pointer unless stated otherwise; every tensor is
- *     dense row-major (C-contiguous) with the shape given beside it.
+ *     dense row-major (C-contiguous) with the shape given beside it.  Q, K, V,
+ *     dO, O, dQ, dK and dV must be 16-byte aligned.
  *   - The caller owns all memory.  No entry point allocates device memory; the
  *     scratch a call needs is passed in as `workspace` (size from
  *     dfs_workspace_size).
