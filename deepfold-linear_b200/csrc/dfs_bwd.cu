@@ -55,7 +55,7 @@ struct BwdCfg {
   static constexpr uint32_t SMEM_NEED = OFF_MISC + 1024 + 1024;
   static constexpr uint32_t SMEM = SMEM_NEED > 122880u ? SMEM_NEED : 122880u;
   static_assert(SMEM <= 232448u, "exceeds the 227 KB of shared memory a CTA can use");
-  static_assert(8u * 2 * NP * 4 <= 4u * NP * DH, "column partials must fit the K/V region");
+  static_assert(kWarps * 2u * NP * 4 <= 4u * NP * DH, "column partials must fit the K/V region");
   static_assert(NP + DH <= 512, "TMEM columns");
 };
 
@@ -64,10 +64,10 @@ enum { BC_G = 0, BC_OK, BC_U2, BC_SOL2, BC_FA, BC_INV, BC_DD, BC_W1, BC_X0, BC_X
 enum { BR_X0 = 0, BR_X1, BR_X2 };
 
 template <int C, int DH>
-__global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdParams p) {
   using Cfg = BwdCfg<C, DH>;
   constexpr int NP = Cfg::NP, NS = Cfg::NS;
-  constexpr int MC = (NP + 255) / 256;  // columns per thread for vector work (j = tid + 256 m)
+  constexpr int MC = (NP + kThreads - 1) / kThreads;  // columns per thread for vector work (j = tid + kThreads m)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* Ts = reinterpret_cast<float*>(base + Cfg::OFF_T);
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   ClusterExchange<C, Cfg::RSB> exb{reinterpret_cast<float*>(base + Cfg::OFF_XB), 0, 0};
   float* colv = reinterpret_cast<float*>(base + Cfg::OFF_COL);
   float* rowv = reinterpret_cast<float*>(base + Cfg::OFF_ROW);
-  float* misc = reinterpret_cast<float*>(base + Cfg::OFF_MISC);       // 192 scalars
+  float* misc = reinterpret_cast<float*>(base + Cfg::OFF_MISC);       // 192 scalars (per-warp slots of 16)
   uint64_t* mbar = reinterpret_cast<uint64_t*>(base + Cfg::OFF_MISC + 768);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + Cfg::OFF_MISC + 784);
 
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     mbar_init(mbar, 1);
     fence_mbar_init();
   }
-  for (int j = tid; j < NP; j += 256) {
+  for (int j = tid; j < NP; j += kThreads) {
     const bool ok = j < N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + j] != 0.0f);
     colv[BC_OK * NP + j] = ok ? 1.0f : 0.0f;
     colv[BC_G * NP + j] = ok ? p.log_v[bh * N + j] * kLog2e : 0.0f;
@@ -129,15 +129,15 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     for (int c = 0; c < 3; ++c)
       colv[(BC_X0 + c) * NP + j] = (p.x_res && j < N) ? p.x_res[(static_cast<size_t>(bb) * N + j) * 3 + c] : 0.0f;
   }
-  for (int i = tid; i < 64; i += 256) {
+  for (int i = tid; i < 64; i += kThreads) {
     const int gi = row0 + i;
 #pragma unroll
     for (int c = 0; c < 3; ++c)
       rowv[(BR_X0 + c) * 64 + i] = (p.x_res && gi < N) ? p.x_res[(static_cast<size_t>(bb) * N + gi) * 3 + c] : 0.0f;
   }
-  load_operand<DH>(SA, p.Q, p.in_dtype, bh * N, row0, 64, N, tid, 256);
-  load_operand<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, 256);
-  load_operand_f32<DH>(DA, p.dO, bh * N, row0, 64, N, tid, 256);
+  load_operand<DH>(SA, p.Q, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);
+  load_operand<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
+  load_operand_f32<DH>(DA, p.dO, bh * N, row0, 64, N, tid, kThreads);
   operands_ready();
   const uint32_t tbase = *tslot;
 
@@ -156,13 +156,13 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   bias.row0 = row0;
   bias.transposed = false;
 
-  const int rho = (lane >> 2) & 7;
-  const int grow = row0 + 8 * warp + rho;
+  const int rho = (lane >> 3) & 3;
+  const int grow = row0 + kRpw * warp + rho;
   const bool rok = grow < N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + grow] != 0.0f);
   uint32_t rokm = 0, cokm = 0;
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int gi = row0 + 8 * warp + r;
+  for (int r = 0; r < kRpw; ++r) {
+    const int gi = row0 + kRpw * warp + r;
     const bool ok = gi < N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + gi] != 0.0f);
     rokm |= ok ? (1u << r) : 0u;
   }
@@ -179,18 +179,18 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, qk_scale, warp, lane);
   __syncthreads();
-  float P[8][NS];
+  float P[kRpw][NS];
   stage_to_regs<NS>(P, Ts, warp, lane);
   add_cost_bias<NS>(P, bias, warp, lane);
   {
-    float fall[8];
+    float fall[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) fall[r] = __shfl_sync(0xffffffffu, fr, 4 * r);
+    for (int r = 0; r < kRpw; ++r) fall[r] = __shfl_sync(0xffffffffu, fr, 8 * r);
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const float g = colv[BC_G * NP + 32 * k + lane];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
+      for (int r = 0; r < kRpw; ++r) {
         const bool ok = ((rokm >> r) & 1u) && ((cokm >> k) & 1u);
         P[r][k] = ok ? ex2(P[r][k] + fall[r] + g) : 0.0f;
       }
@@ -198,9 +198,9 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   }
   float rsum_r, inv_r;
   {
-    float a[8], m[8];
+    float a[kRpw], m[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < kRpw; ++r) {
       a[r] = 0.0f;
       m[r] = 0.0f;
 #pragma unroll
@@ -209,15 +209,15 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
         m[r] = fmaxf(m[r], P[r][k]);
       }
     }
-    rsum_r = reduce8_rows<false>(a, lane);
-    const float pm = reduce8_rows<true>(m, lane);
+    rsum_r = reduce4_rows<false>(a, lane);
+    const float pm = reduce4_rows<true>(m, lane);
     inv_r = (rok && rsum_r > 0.0f) ? 1.0f / (rsum_r + 1e-6f * pm) : 0.0f;
     if (!isfinite(rsum_r)) err |= DFS_ERR_NUMERIC;
   }
 
   // ---------------------------------------------------------------- phase 2
   __syncthreads();
-  load_operand<DH>(KV, p.V, p.in_dtype, bh * N, 0, NP, N, tid, 256);
+  load_operand<DH>(KV, p.V, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
   operands_ready();
   if (tid == 0) {
     issue_abt<NP, DH>(tbase, DA, KV, NP);  // dT = dO_s V^T
@@ -227,47 +227,47 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, 1.0f, warp, lane);
   __syncthreads();
-  float* red = KV;  // V is no longer needed: 2 x 8 x NP column partials (P and E)
+  float* red = KV;  // V is no longer needed: 2 x kWarps x NP column partials (P and E)
   float fbar_r, D_r;
   {
-    float inv[8];
+    float inv[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) inv[r] = __shfl_sync(0xffffffffu, inv_r, 4 * r);
-    float dxr[3][8];
+    for (int r = 0; r < kRpw; ++r) inv[r] = __shfl_sync(0xffffffffu, inv_r, 8 * r);
+    float dxr[3][kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int gi = row0 + 8 * warp + r;
+    for (int r = 0; r < kRpw; ++r) {
+      const int gi = row0 + kRpw * warp + r;
 #pragma unroll
       for (int c = 0; c < 3; ++c) dxr[c][r] = (p.dxc && gi < N) ? p.dxc[(bh * N + gi) * 3 + c] : 0.0f;
     }
-    float accD[8];
+    float accD[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < kRpw; ++r) {
       accD[r] = 0.0f;
 #pragma unroll
       for (int k = 0; k < NS; ++k) {
         const int j = 32 * k + lane;
-        float dt = Ts[sw_off(8 * warp + r, j, 64) >> 2];
+        float dt = Ts[sw_off(kRpw * warp + r, j, 64) >> 2];
         if (p.dxc)
           dt += dxr[0][r] * colv[BC_X0 * NP + j] + dxr[1][r] * colv[BC_X1 * NP + j] +
                 dxr[2][r] * colv[BC_X2 * NP + j];
         accD[r] += P[r][k] * inv[r] * dt;
       }
     }
-    D_r = reduce8_rows<false>(accD, lane);
-    float D[8];
+    D_r = reduce4_rows<false>(accD, lane);
+    float D[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) D[r] = __shfl_sync(0xffffffffu, D_r, 4 * r);
-    float re[8];
+    for (int r = 0; r < kRpw; ++r) D[r] = __shfl_sync(0xffffffffu, D_r, 8 * r);
+    float re[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) re[r] = 0.0f;
+    for (int r = 0; r < kRpw; ++r) re[r] = 0.0f;
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const int j = 32 * k + lane;
       float cp = 0.0f, ce = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const uint32_t o = sw_off(8 * warp + r, j, 64) >> 2;
+      for (int r = 0; r < kRpw; ++r) {
+        const uint32_t o = sw_off(kRpw * warp + r, j, 64) >> 2;
         float dt = Ts[o];
         if (p.dxc)
           dt += dxr[0][r] * colv[BC_X0 * NP + j] + dxr[1][r] * colv[BC_X1 * NP + j] +
@@ -279,34 +279,34 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
         re[r] += e;
       }
       red[warp * NP + j] = cp;
-      red[8 * NP + warp * NP + j] = ce;
+      red[kWarps * NP + warp * NP + j] = ce;
     }
-    fbar_r = reduce8_rows<false>(re, lane);
+    fbar_r = reduce4_rows<false>(re, lane);
   }
   {
-    const bool own = (lane & 3) == 0 && rok;
+    const bool own = (lane & 7) == 0 && rok;
     const float sf = warp_sum(own ? fbar_r : 0.0f);
     const float sr = warp_sum(own ? rsum_r : 0.0f);
     if (lane == 0) {
       misc[warp] = sf;
-      misc[8 + warp] = sr;
+      misc[16 + warp] = sr;
     }
   }
   __syncthreads();
   if (tid < OWN) {
     float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
-      const float4 y = *reinterpret_cast<const float4*>(red + 8 * NP + w * NP + j4);
+      const float4 y = *reinterpret_cast<const float4*>(red + kWarps * NP + w * NP + j4);
       a4 = make_float4(a4.x + x.x, a4.y + x.y, a4.z + x.z, a4.w + x.w);
       b4 = make_float4(b4.x + y.x, b4.y + y.y, b4.z + y.z, b4.w + y.w);
     }
     exa.put4(j4, a4);
     exa.put4(NP + j4, b4);
   }
-  if ((lane & 3) == 0) {  // this slab's rows for the all-gathers
-    const int li = 8 * warp + rho;
+  if ((lane & 7) == 0) {  // this slab's rows for the all-gathers
+    const int li = kRpw * warp + rho;
     exa.put(2 * NP + li, fr);
     exa.put(2 * NP + 64 + li, inv_r);
     exa.put(2 * NP + 128 + li, D_r);
@@ -314,9 +314,9 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   if (tid == 0) {
     float a = 0.0f, b = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       a += misc[w];
-      b += misc[8 + w];
+      b += misc[16 + w];
     }
     exa.put4(2 * NP + 192, make_float4(a, b, 0.0f, 0.0f));
   }
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   float sum_fbar = 0.0f, sum_r = 0.0f;
 #pragma unroll
   for (int m = 0; m < MC; ++m) {
-    const int j = tid + 256 * m;
+    const int j = tid + kThreads * m;
     cc[m] = gv[m] = 0.0f;
     okc[m] = j < NP && colv[BC_OK * NP + j] != 0.0f;
     if (j < NP) {
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     __syncthreads();
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += misc[slot + w];
+    for (int w = 0; w < kWarps; ++w) s += misc[slot + w];
     return s;
   };
   const float d1 = (rok && rsum_r > 0.0f) ? rsum_r / kap : 0.0f;
@@ -373,8 +373,8 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
       s2 += b2[m];
       nv += okc[m] ? 1.0f : 0.0f;
     }
-    s2 = cta_sum(s2, 16);
-    nv = cta_sum(nv, 24);
+    s2 = cta_sum(s2, 32);
+    nv = cta_sum(nv, 48);
     const float sh = nv > 0.0f ? (sum_fbar - s2) / (2.0f * nv) : 0.0f;
     if (rok) b1 -= sh;
 #pragma unroll
@@ -389,45 +389,45 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
                     float& wu, float& rr) {
 #pragma unroll
     for (int m = 0; m < MC; ++m)
-      if (tid + 256 * m < NP) colv[BC_U2 * NP + tid + 256 * m] = u2[m];
+      if (tid + kThreads * m < NP) colv[BC_U2 * NP + tid + kThreads * m] = u2[m];
     __syncthreads();
-    float acc[8];
+    float acc[kRpw];
     float u2k[NS];
 #pragma unroll
     for (int k = 0; k < NS; ++k) u2k[k] = colv[BC_U2 * NP + 32 * k + lane];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < kRpw; ++r) {
       float s = 0.0f;
 #pragma unroll
       for (int k = 0; k < NS; ++k) s += P[r][k] * u2k[k];
       acc[r] = s;
     }
-    const float pu = reduce8_rows<false>(acc, lane);
+    const float pu = reduce4_rows<false>(acc, lane);
     w1 = rok ? d1 * u1 + pu : 0.0f;
-    float u1a[8];
+    float u1a[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) u1a[r] = __shfl_sync(0xffffffffu, u1, 4 * r);
+    for (int r = 0; r < kRpw; ++r) u1a[r] = __shfl_sync(0xffffffffu, u1, 8 * r);
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       float s = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 8; ++r) s += P[r][k] * u1a[r];
+      for (int r = 0; r < kRpw; ++r) s += P[r][k] * u1a[r];
       red[warp * NP + 32 * k + lane] = s;
     }
-    const bool own = (lane & 3) == 0 && rok;
+    const bool own = (lane & 7) == 0 && rok;
     const float a0 = warp_sum(own ? res1 * u1 : 0.0f);
     const float a1 = warp_sum(own ? w1 * u1 : 0.0f);
     const float a2 = warp_sum(own ? res1 * res1 : 0.0f);
     if (lane == 0) {
-      misc[32 + warp] = a0;
-      misc[40 + warp] = a1;
-      misc[48 + warp] = a2;
+      misc[64 + warp] = a0;
+      misc[80 + warp] = a1;
+      misc[96 + warp] = a2;
     }
     __syncthreads();
     if (tid < OWN) {
       float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
+      for (int w = 0; w < kWarps; ++w) {
         const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
         s4 = make_float4(s4.x + x.x, s4.y + x.y, s4.z + x.z, s4.w + x.w);
       }
@@ -435,10 +435,10 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
       if (tid == 0) {
         float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          s0 += misc[32 + w];
-          s1 += misc[40 + w];
-          s2 += misc[48 + w];
+        for (int w = 0; w < kWarps; ++w) {
+          s0 += misc[64 + w];
+          s1 += misc[80 + w];
+          s2 += misc[96 + w];
         }
         exb.put4(NP, make_float4(s0, s1, s2, 0.0f));
       }
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
 #pragma unroll
     for (int m = 0; m < MC; ++m) {
-      const int j = tid + 256 * m;
+      const int j = tid + kThreads * m;
       float t = 0.0f;
       if (j < NP) {
 #pragma unroll
@@ -467,9 +467,9 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
       g2 += d.z;
     }
     exb.next();
-    c0 = cta_sum(c0, 56);
-    c1 = cta_sum(c1, 64);
-    c2 = cta_sum(c2, 72);
+    c0 = cta_sum(c0, 112);
+    c1 = cta_sum(c1, 128);
+    c2 = cta_sum(c2, 144);
     __syncthreads();
     ru = g0 + c0;
     wu = g1 + c1;
@@ -533,29 +533,29 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   // sum(dlog_mu) = sum(dlog_nu) = 0
   float tshift = 0.0f;
   {
-    const bool own = (lane & 3) == 0 && rok;
+    const bool own = (lane & 7) == 0 && rok;
     const float a = warp_sum(own ? rsum_r * x1 : 0.0f);
-    if (lane == 0) misc[80 + warp] = a;
+    if (lane == 0) misc[160 + warp] = a;
     __syncthreads();
-    if ((lane & 3) == 0) exb.put(8 * warp + rho, x1);
+    if ((lane & 7) == 0) exb.put(kRpw * warp + rho, x1);
     if (tid == 0) {
       float t = 0.0f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) t += misc[80 + w];
+      for (int w = 0; w < kWarps; ++w) t += misc[160 + w];
       exb.put(64, t);
     }
     exb.sync();
-    for (int i = tid; i < NP; i += 256) colv[BC_W1 * NP + i] = exb.from(i >> 6)[i & 63];
+    for (int i = tid; i < NP; i += kThreads) colv[BC_W1 * NP + i] = exb.from(i >> 6)[i & 63];
     float tot = 0.0f;
 #pragma unroll
     for (int c = 0; c < C; ++c) tot += exb.from(c)[64];
     exb.next();
     if (kap >= 1.0f) tshift = sum_r > 0.0f ? -tot / sum_r : 0.0f;
   }
-  if (p.dlog_mu && (lane & 3) == 0 && grow < N) p.dlog_mu[bh * N + grow] = rok ? rsum_r * (x1 + tshift) : 0.0f;
+  if (p.dlog_mu && (lane & 7) == 0 && grow < N) p.dlog_mu[bh * N + grow] = rok ? rsum_r * (x1 + tshift) : 0.0f;
 #pragma unroll
   for (int m = 0; m < MC; ++m) {
-    const int j = tid + 256 * m;
+    const int j = tid + kThreads * m;
     if (j < NP) colv[BC_SOL2 * NP + j] = x2[m];
     if (p.dlog_nu && j >= row0 && j < row0 + 64 && j < N)
       p.dlog_nu[bh * N + j] = okc[m] ? cc[m] * (x2[m] - tshift) : 0.0f;
@@ -564,21 +564,21 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
 
   // ---------------------------------------------------------------- phase 5 (dQ)
   {
-    float xa[8];
+    float xa[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) xa[r] = __shfl_sync(0xffffffffu, x1, 4 * r);
+    for (int r = 0; r < kRpw; ++r) xa[r] = __shfl_sync(0xffffffffu, x1, 8 * r);
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const int j = 32 * k + lane;
       const float xs = colv[BC_SOL2 * NP + j];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const uint32_t o = sw_off(8 * warp + r, j, 64) >> 2;
+      for (int r = 0; r < kRpw; ++r) {
+        const uint32_t o = sw_off(kRpw * warp + r, j, 64) >> 2;
         Ts[o] = Ts[o] - P[r][k] * (xa[r] + xs);
       }
     }
   }
-  load_operand_t<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, 256);  // K^T (DH x NP)
+  load_operand_t<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);  // K^T (DH x NP)
   operands_ready();
   if (tid == 0) {
     issue_abt<DH, NP>(tbase, Ts, KV, DH);  // dQ = dS K
@@ -590,8 +590,8 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   // ---------------------------------------------------------------- phase 6
   tc_fence_before();
   __syncthreads();
-  load_operand<DH>(SA, p.K, p.in_dtype, bh * N, row0, 64, N, tid, 256);  // K slab
-  load_operand<DH>(KV, p.Q, p.in_dtype, bh * N, 0, NP, N, tid, 256);     // Q (all rows)
+  load_operand<DH>(SA, p.K, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);  // K slab
+  load_operand<DH>(KV, p.Q, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);     // Q (all rows)
   operands_ready();
   if (tid == 0) {
     issue_qk<NP, DH>(tbase, SA, KV);  // S^T for the column slab
@@ -606,15 +606,15 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   add_cost_bias<NS>(P, bias, warp, lane);
   {
     // slab rows r are columns j of the cost, lanes run over rows i
-    float gj[8];
+    float gj[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) gj[r] = colv[BC_G * NP + row0 + 8 * warp + r];
+    for (int r = 0; r < kRpw; ++r) gj[r] = colv[BC_G * NP + row0 + kRpw * warp + r];
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const int i = 32 * k + lane;
       const float fi = colv[BC_FA * NP + i];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
+      for (int r = 0; r < kRpw; ++r) {
         const bool ok = ((rokm >> r) & 1u) && ((cokm >> k) & 1u);
         P[r][k] = ok ? ex2(P[r][k] + gj[r] + fi) : 0.0f;
       }
@@ -623,8 +623,8 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
 
   // ---------------------------------------------------------------- phase 7 (dV)
   __syncthreads();
-  load_operand<DH>(SA, p.V, p.in_dtype, bh * N, row0, 64, N, tid, 256);   // V slab
-  load_operand_f32<DH>(KV, p.dO, bh * N, 0, NP, N, tid, 256);              // dO (all rows)
+  load_operand<DH>(SA, p.V, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);   // V slab
+  load_operand_f32<DH>(KV, p.dO, bh * N, 0, NP, N, tid, kThreads);              // dO (all rows)
   operands_ready();
   if (tid == 0) {
     issue_abt<NP, DH>(tbase, SA, KV, NP);  // dT^T = V_s dO^T
@@ -635,11 +635,11 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
     const int i = 32 * k + lane;
     const float inv = colv[BC_INV * NP + i];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) Ts[sw_off(8 * warp + r, i, 64) >> 2] = P[r][k] * inv;
+    for (int r = 0; r < kRpw; ++r) Ts[sw_off(kRpw * warp + r, i, 64) >> 2] = P[r][k] * inv;
   }
   mma_wait();
   __syncthreads();
-  load_operand_f32_t<DH>(KV, p.dO, bh * N, 0, NP, N, tid, 256);            // dO^T (DH x NP)
+  load_operand_f32_t<DH>(KV, p.dO, bh * N, 0, NP, N, tid, kThreads);            // dO^T (DH x NP)
   operands_ready();
   if (tid == 0) {
     issue_abt<DH, NP>(tbase + NP, Ts, KV, DH);  // dV = T_norm^T dO
@@ -654,10 +654,10 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
   drain_m64<NP>(Ts, tbase, 0, 1.0f, warp, lane);  // dT^T
   __syncthreads();
   {
-    float xj[3][8], sol2j[8];
+    float xj[3][kRpw], sol2j[kRpw];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int j = row0 + 8 * warp + r;
+    for (int r = 0; r < kRpw; ++r) {
+      const int j = row0 + kRpw * warp + r;
       sol2j[r] = colv[BC_SOL2 * NP + j];
 #pragma unroll
       for (int c = 0; c < 3; ++c) xj[c][r] = colv[(BC_X0 + c) * NP + j];
@@ -673,15 +673,15 @@ __global__ void __launch_bounds__(256, 1) resident_bwd_kernel(const BwdParams p)
         dx2 = p.dxc[(bh * N + i) * 3 + 2];
       }
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const uint32_t o = sw_off(8 * warp + r, i, 64) >> 2;
+      for (int r = 0; r < kRpw; ++r) {
+        const uint32_t o = sw_off(kRpw * warp + r, i, 64) >> 2;
         float dt = Ts[o];
         if (p.dxc) dt += dx0 * xj[0][r] + dx1 * xj[1][r] + dx2 * xj[2][r];
         Ts[o] = P[r][k] * inv * (dt - Di) - P[r][k] * (w1i + sol2j[r]);
       }
     }
   }
-  load_operand_t<DH>(KV, p.Q, p.in_dtype, bh * N, 0, NP, N, tid, 256);  // Q^T (DH x NP)
+  load_operand_t<DH>(KV, p.Q, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);  // Q^T (DH x NP)
   operands_ready();
   if (tid == 0) {
     issue_abt<DH, NP>(tbase, Ts, KV, DH);  // dK = dS^T Q
@@ -706,7 +706,7 @@ static cudaError_t launch_bwd_cd(const BwdParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C * p.B * p.H);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -234,6 +234,41 @@ DFS_DEV float warp_sum(float v) {
   return v;
 }
 
+// Reduce 4 per-lane partials (one per row of the warp's 4-row block) across the
+// 32 lanes.  Lane l ends with the total of row (l >> 3) & 3.  6 shuffles.
+template <bool kMax>
+DFS_DEV float reduce4_rows(const float (&a)[4], int lane) {
+  const bool hi4 = lane & 16, hi3 = lane & 8;
+  float b[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = hi4 ? a[i] : a[i + 2];
+    const float keep = hi4 ? a[i + 2] : a[i];
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+    b[i] = kMax ? fmaxf(keep, recv) : keep + recv;
+  }
+  float d;
+  {
+    const float send = hi3 ? b[0] : b[1];
+    const float keep = hi3 ? b[1] : b[0];
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 8);
+    d = kMax ? fmaxf(keep, recv) : keep + recv;
+  }
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) {
+    const float e = __shfl_xor_sync(0xffffffffu, d, o);
+    d = kMax ? fmaxf(d, e) : d + e;
+  }
+  return d;
+}
+
+// Order-preserving map between floats and ints, for atomicMax on floats of any sign.
+DFS_DEV int float_to_ordered(float x) {
+  const int i = __float_as_int(x);
+  return i >= 0 ? i : (i ^ 0x7fffffff);
+}
+DFS_DEV float ordered_to_float(int i) { return __int_as_float(i >= 0 ? i : (i ^ 0x7fffffff)); }
+
 // Reduce 8 per-lane partials (one per row of the warp's 8-row block) across the
 // 32 lanes.  Lane l ends with the total of row (l >> 2) & 7.  9 shuffles.
 template <bool kMax>

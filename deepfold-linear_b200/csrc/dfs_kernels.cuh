@@ -6,6 +6,11 @@
 
 namespace dfs {
 
+// Resident kernels: 16 warps per CTA, each warp owning 4 rows of the 64-row slab.
+constexpr int kThreads = 512;
+constexpr int kWarps = 16;
+constexpr int kRpw = 4;
+
 // Potential drift (log2 units) since the last absorption beyond which the
 // stabilised kernel matrix is rebuilt: row/column sums then stay above 2^-60.
 constexpr float kDrift = 30.0f;

@@ -1,10 +1,10 @@
 // dfs_slab.cuh -- pieces shared by the resident forward and backward kernels.
 //
 // A CTA owns a 64-row slab of one N x N problem.  In registers the slab is laid
-// out as E[r][k] = element (8*warp + r, 32*k + lane): each warp holds 8 rows,
-// each lane the columns congruent to it mod 32.  Row reductions are lane
-// reductions (reduce8_rows), column reductions go through shared memory and,
-// across the cluster, through distributed shared memory.
+// out as E[r][k] = element (kRpw*warp + r, 32*k + lane): each of the kWarps warps
+// holds kRpw rows, each lane the columns congruent to it mod 32.  Row reductions
+// are lane reductions (reduce4_rows), column reductions go through shared memory
+// and, across the cluster, through distributed shared memory.
 #pragma once
 
 #include "dfs_kernels.cuh"
@@ -13,14 +13,15 @@ namespace dfs {
 
 // Drain an M=64 fp32 accumulator (TMEM columns [col_base, col_base+NP)) into the
 // 64 x NP 128B-swizzled staging buffer, multiplied by `scale`.  TMEM row m of an
-// M=64 MMA sits in lane (m % 16) + 32 (m / 16); warps w and w+4 share those
-// lanes and split the columns.  Caller synchronises before and after.
+// M=64 MMA sits in lane (m % 16) + 32 (m / 16); a warp may only read the lane
+// quarter warp % 4, so the kWarps/4 warps sharing a quarter split the 32-column
+// chunks.  Caller synchronises before and after.
 template <int NP>
 DFS_DEV void drain_m64(float* Ts, uint32_t tbase, uint32_t col_base, float scale, int warp, int lane) {
-  const int q = warp & 3, hf = warp >> 2;
+  const int q = warp & 3, grp = warp >> 2;
 #pragma unroll 1
-  for (int ch = 0; ch < NP / 64; ++ch) {
-    const int col0 = hf * (NP / 2) + 32 * ch;
+  for (int ch = grp; ch < NP / 32; ch += kWarps / 4) {
+    const int col0 = 32 * ch;
     float v[32];
     tmem_ld32(tbase + (static_cast<uint32_t>(32 * q) << 16) + col_base + col0, v);
     if (lane < 16) {
@@ -36,19 +37,19 @@ DFS_DEV void drain_m64(float* Ts, uint32_t tbase, uint32_t col_base, float scale
 }
 
 template <int NS>
-DFS_DEV void stage_to_regs(float (&E)[8][NS], const float* Ts, int warp, int lane) {
+DFS_DEV void stage_to_regs(float (&E)[kRpw][NS], const float* Ts, int warp, int lane) {
 #pragma unroll
-  for (int r = 0; r < 8; ++r)
+  for (int r = 0; r < kRpw; ++r)
 #pragma unroll
-    for (int k = 0; k < NS; ++k) E[r][k] = Ts[sw_off(8 * warp + r, 32 * k + lane, 64) >> 2];
+    for (int k = 0; k < NS; ++k) E[r][k] = Ts[sw_off(kRpw * warp + r, 32 * k + lane, 64) >> 2];
 }
 
 template <int NS>
-DFS_DEV void regs_to_stage(const float (&E)[8][NS], float* Ts, int warp, int lane) {
+DFS_DEV void regs_to_stage(const float (&E)[kRpw][NS], float* Ts, int warp, int lane) {
 #pragma unroll
-  for (int r = 0; r < 8; ++r)
+  for (int r = 0; r < kRpw; ++r)
 #pragma unroll
-    for (int k = 0; k < NS; ++k) Ts[sw_off(8 * warp + r, 32 * k + lane, 64) >> 2] = E[r][k];
+    for (int k = 0; k < NS; ++k) Ts[sw_off(kRpw * warp + r, 32 * k + lane, 64) >> 2] = E[r][k];
 }
 
 // Position / geometry terms of the cost, folded into the slab as
@@ -66,12 +67,12 @@ struct BiasArgs {
 };
 
 template <int NS>
-DFS_DEV void add_cost_bias(float (&E)[8][NS], const BiasArgs& a, int warp, int lane) {
+DFS_DEV void add_cost_bias(float (&E)[kRpw][NS], const BiasArgs& a, int warp, int lane) {
   constexpr int NP = 32 * NS;
   if (a.pos_weight == nullptr && !a.geo) return;
 #pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const int li = 8 * warp + r, gi = a.row0 + li;
+  for (int r = 0; r < kRpw; ++r) {
+    const int li = kRpw * warp + r, gi = a.row0 + li;
     const float xi0 = a.geo ? a.xrow[li] : 0.f, xi1 = a.geo ? a.xrow[64 + li] : 0.f,
                 xi2 = a.geo ? a.xrow[128 + li] : 0.f;
 #pragma unroll
@@ -135,13 +136,13 @@ template <int DH, bool TR, typename T>
 DFS_DEV void load_tile(float* dst, const T* src, int row_first, int rows, int N, int tid) {
   constexpr int EPC = Chunk16<T>::kElems;   // elements per chunk
   constexpr int CPR = DH / EPC;             // chunks per row
-  constexpr int BATCH = 4;
+  constexpr int BATCH = 2;
   const int total = rows * CPR;
-  for (int base = 0; base < total; base += 256 * BATCH) {
+  for (int base = 0; base < total; base += kThreads * BATCH) {
     uint4 raw[BATCH];
 #pragma unroll
     for (int b = 0; b < BATCH; ++b) {
-      const int c = base + tid + 256 * b;
+      const int c = base + tid + kThreads * b;
       const int gi = row_first + c / CPR;
       raw[b] = make_uint4(0u, 0u, 0u, 0u);
       if (c < total && gi < N)
@@ -149,7 +150,7 @@ DFS_DEV void load_tile(float* dst, const T* src, int row_first, int rows, int N,
     }
 #pragma unroll
     for (int b = 0; b < BATCH; ++b) {
-      const int c = base + tid + 256 * b;
+      const int c = base + tid + kThreads * b;
       if (c >= total) break;
       const int i = c / CPR, c0 = (c % CPR) * EPC;
       float v[EPC];
