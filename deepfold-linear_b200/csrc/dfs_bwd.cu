@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   bias.N = N;
   bias.row0 = row0;
   bias.transposed = false;
+  const bool bias_on = p.pos_weight != nullptr || bias.geo;
 
   const int rho = (lane >> 3) & 3;
   const int grow = row0 + kRpw * warp + rho;
@@ -179,9 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, qk_scale, warp, lane);
   __syncthreads();
+  if (bias_on) {
+    add_cost_bias_stage<NP>(Ts, bias, tid);
+    __syncthreads();
+  }
   float P[kRpw][NS];
   stage_to_regs<NS>(P, Ts, warp, lane);
-  add_cost_bias<NS>(P, bias, warp, lane);
   {
     float fall[kRpw];
 #pragma unroll
@@ -601,9 +605,12 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, qk_scale, warp, lane);
   __syncthreads();
+  if (bias_on) {
+    bias.transposed = true;
+    add_cost_bias_stage<NP>(Ts, bias, tid);
+    __syncthreads();
+  }
   stage_to_regs<NS>(P, Ts, warp, lane);
-  bias.transposed = true;
-  add_cost_bias<NS>(P, bias, warp, lane);
   {
     // slab rows r are columns j of the cost, lanes run over rows i
     float gj[kRpw];

@@ -183,18 +183,120 @@ struct ClusterExchange {
   int buf;
   int rank;
   DFS_DEV uint32_t slot_addr(int off) const { return smem_u32(recv + (buf * C + rank) * RS + off); }
+  // a cluster of one CTA exchanges through its own shared memory and a CTA barrier
   DFS_DEV void put(int off, float v) const {
-    const uint32_t a = slot_addr(off);
+    if constexpr (C == 1) {
+      recv[buf * RS + off] = v;
+    } else {
+      const uint32_t a = slot_addr(off);
 #pragma unroll
-    for (int c = 0; c < C; ++c) dsmem_st(dsmem_addr(a, static_cast<uint32_t>(c)), v);
+      for (int c = 0; c < C; ++c) dsmem_st(dsmem_addr(a, static_cast<uint32_t>(c)), v);
+    }
   }
   DFS_DEV void put4(int off, float4 v) const {
-    const uint32_t a = slot_addr(off);
+    if constexpr (C == 1) {
+      *reinterpret_cast<float4*>(recv + buf * RS + off) = v;
+    } else {
+      const uint32_t a = slot_addr(off);
 #pragma unroll
-    for (int c = 0; c < C; ++c) dsmem_st4(dsmem_addr(a, static_cast<uint32_t>(c)), v);
+      for (int c = 0; c < C; ++c) dsmem_st4(dsmem_addr(a, static_cast<uint32_t>(c)), v);
+    }
+  }
+  // four values to CTA `dst` only
+  DFS_DEV void put4_to(int dst, int off, float4 v) const {
+    if constexpr (C == 1)
+      *reinterpret_cast<float4*>(recv + buf * RS + off) = v;
+    else
+      dsmem_st4(dsmem_addr(slot_addr(off), static_cast<uint32_t>(dst)), v);
+  }
+  // one value to CTA `dst` only (callers spread the C destinations over lanes)
+  DFS_DEV void put_to(int dst, int off, float v) const {
+    if constexpr (C == 1)
+      recv[buf * RS + off] = v;
+    else
+      dsmem_st(dsmem_addr(slot_addr(off), static_cast<uint32_t>(dst)), v);
   }
   DFS_DEV const float* from(int src) const { return recv + (buf * C + src) * RS; }
-  DFS_DEV void sync() const { cluster_sync(); }
+  DFS_DEV void sync() const {
+    if constexpr (C == 1)
+      __syncthreads();
+    else
+      cluster_sync();
+  }
+  DFS_DEV void next() { buf ^= 1; }
+};
+
+DFS_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Bulk copy of `bytes` from this CTA's shared memory into the shared memory of a
+// CTA of the cluster; completion is counted in bytes on that CTA's mbarrier.
+DFS_DEV void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t dst_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "r"(src), "r"(bytes), "r"(dst_bar)
+               : "memory");
+}
+
+// Cluster all-to-all through bulk asynchronous copies.  Every CTA stages its
+// contribution in local shared memory; after a CTA barrier one thread copies
+// the stage into this CTA's receive slot in every CTA (one cp.async.bulk per
+// destination, completion counted in bytes on the destination's mbarrier) and
+// every thread waits on its own CTA's mbarrier.  Stages, receive buffers and
+// mbarriers are double-buffered by round parity.  Reuse is safe without further
+// synchronisation: a CTA rewrites stage / receive buffer b two rounds later,
+// and completing the round in between requires every peer's copy of that
+// round, which each peer issues only after it has received (so read) the
+// earlier round.  A cluster of one CTA exchanges through its stage and the
+// CTA barrier alone.
+template <int C, int RS>
+struct BulkExchange {
+  float* recv;        // [2][C][RS] floats
+  float* stg;         // [2][RS] floats
+  uint64_t* bar;      // [2] mbarriers, arrival count 1
+  int buf;
+  uint32_t phase;     // bit b: parity of bar[b]'s next completion
+  int rank;
+  bool dead;          // a wait timed out: later waits return at once
+
+  DFS_DEV void init() const {  // one thread; then fence_mbar_init and a cluster barrier
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+  }
+  DFS_DEV float* stage() const { return stg + buf * RS; }
+  DFS_DEV const float* from(int src) const {
+    if constexpr (C == 1)
+      return stg + buf * RS;
+    else
+      return recv + (buf * C + src) * RS;
+  }
+  // All threads, after writing this round's stage: exchange `bytes` (a multiple
+  // of 16) of it.  Returns false if the wait timed out.
+  DFS_DEV bool exchange(int tid, uint32_t bytes) {
+    if constexpr (C == 1) {
+      __syncthreads();
+      return true;
+    } else {
+      fence_async_smem();  // stage writes -> visible to the bulk-copy engine
+      __syncthreads();
+      const uint32_t b = smem_u32(&bar[buf]);
+      if (tid == 0) {
+        mbar_arrive_expect_tx(b, C * bytes);
+        const uint32_t dst = smem_u32(recv + (buf * C + rank) * RS), src = smem_u32(stage());
+#pragma unroll
+        for (int c = 0; c < C; ++c)
+          bulk_copy_to_cluster(dsmem_addr(dst, static_cast<uint32_t>(c)), src, bytes,
+                               dsmem_addr(b, static_cast<uint32_t>(c)));
+      }
+      const uint32_t par = (phase >> buf) & 1u;
+      phase ^= 1u << buf;
+      if (dead) return false;
+      if (!mbar_wait(&bar[buf], par)) {
+        dead = true;
+        return false;
+      }
+      return true;
+    }
+  }
   DFS_DEV void next() { buf ^= 1; }
 };
 

@@ -31,10 +31,13 @@ namespace dfs {
 enum { CV_G0 = 0, CV_G1, CV_BT, CV_GABS, CV_BNU, CV_OK, CV_V, CV_X0, CV_X1, CV_X2, CV_NUM };
 // slab-row vector slots (each 64 floats)
 enum { RV_X0 = 0, RV_X1, RV_X2, RV_NUM };
-// int slots used with shared-memory atomicMax: [0] CTA max of alpha (ordered
-// ints); [1 + 4 s + q] per-iteration maxima (non-negative float bits) of set s:
-// q = 0 |f - f_prev|, 1 |f - f_abs|, 2 |g - g_abs|, 3 |g - g_prev|
-enum { MI_ALPHA = 0, MI_SET = 1 };
+// int slots: [MI_ALPHA] CTA max of alpha (ordered ints, shared-memory atomicMax);
+// [MI_FL + s] flag word of iteration parity s (atomicOr of warp-reduced bits)
+enum { MI_ALPHA = 0, MI_FL = 1 };
+// flag bits: FL_FDRIFT / FL_FNC are this CTA's rows (|f - f_abs| > kDrift,
+// |f - f_prev| >= threshold), the _C variants the same over the whole cluster,
+// FL_GDRIFT / FL_GNC the columns (identical in every CTA)
+enum : unsigned { FL_FDRIFT = 1u, FL_FNC = 2u, FL_GDRIFT = 4u, FL_GNC = 8u, FL_FDRIFT_C = 16u, FL_FNC_C = 32u };
 
 template <int C, int DH>
 struct FwdCfg {
@@ -45,8 +48,10 @@ struct FwdCfg {
   static constexpr uint32_t OFF_KV = OFF_Q + 256u * DH;             // NP x DH (K, then V^T)
   static constexpr uint32_t OFF_RED = OFF_KV + 4u * NP * DH;        // kWarps x NP
   static constexpr int RS = NP + 8;                                 // exchange slot (floats)
-  static constexpr uint32_t OFF_XCH = OFF_RED + 4u * kWarps * NP;   // 2 x C x RS
-  static constexpr uint32_t OFF_COL = OFF_XCH + 8u * C * RS;
+  static constexpr uint32_t XBYTES = 4u * (NP + 4);                 // bytes exchanged per round
+  static constexpr uint32_t OFF_XCH = OFF_RED + 4u * kWarps * NP;   // 2 x C x RS receive slots
+  static constexpr uint32_t OFF_STG = OFF_XCH + 8u * C * RS;         // 2 x RS stages
+  static constexpr uint32_t OFF_COL = OFF_STG + 8u * RS;
   static constexpr uint32_t OFF_ROW = OFF_COL + 4u * CV_NUM * NP;
   static constexpr uint32_t OFF_MISC = OFF_ROW + 4u * RV_NUM * 64;  // 32 ints, barrier, TMEM slot
   // at least 120 KB so that only one CTA fits per SM and its 512 TMEM columns
@@ -72,7 +77,9 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
   int* mi = reinterpret_cast<int*>(base + Cfg::OFF_MISC);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(base + Cfg::OFF_MISC + 128);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + Cfg::OFF_MISC + 144);
-  ClusterExchange<C, Cfg::RS> ex{reinterpret_cast<float*>(base + Cfg::OFF_XCH), 0, 0};
+  BulkExchange<C, Cfg::RS> ex{reinterpret_cast<float*>(base + Cfg::OFF_XCH),
+                              reinterpret_cast<float*>(base + Cfg::OFF_STG),
+                              reinterpret_cast<uint64_t*>(base + Cfg::OFF_MISC + 160), 0, 0u, 0, false};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int crank = static_cast<int>(cluster_rank());
@@ -85,15 +92,13 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
   const size_t bh = static_cast<size_t>(bb) * p.H + hh;
   const float eps_h = p.eps[hh];
   const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
-  const float s_scale = kLog2e / eps_h;            // S' = S * log2(e),  S = -C / eps
-  const float qk_scale = s_scale * rsqrtf(static_cast<float>(DH));
-  const float w_h = p.w_dist ? p.w_dist[hh] : 0.0f;
   int err = 0;
 
   // ---------------------------------------------------------------- setup
   if (warp == 0) tmem_alloc(tslot, 512);
   if (tid == 0) {
     mbar_init(mbar, 1);
+    ex.init();
     fence_mbar_init();
   }
   if (tid < 32) mi[tid] = 0;
@@ -122,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if constexpr (C > 1) cluster_sync();  // every CTA's exchange mbarriers initialised
   const uint32_t tbase = *tslot;
   uint32_t mma_phase = 0;
 
@@ -156,41 +162,39 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     rokm |= ok ? (1u << r) : 0u;
   }
 
-  BiasArgs bias;
-  bias.pos_weight = p.pos_weight;
-  bias.pos_bins = p.pos_bins;
-  bias.xrow = rowv + RV_X0 * 64;
-  bias.xcol = colv + CV_X0 * NP;
-  bias.geo = p.x_res != nullptr && w_h != 0.0f;
-  bias.w_h = w_h;
-  bias.r_0 = p.r_0;
-  bias.s_scale = s_scale;
-  bias.bb = bb;
-  bias.hh = hh;
-  bias.N = N;
-  bias.row0 = row0;
-  bias.transposed = false;
-
-  // S' (log2 units, bias terms included) into E.
+  // S' = S log2(e) (S = -C / eps, bias terms included) into E.  Everything it
+  // needs besides E is recomputed from the parameters here, so that none of it
+  // occupies registers across the iterations.
   auto load_S = [&]() {
+    const int pq = blockIdx.x / C, hq = pq % p.H, bq = pq / p.H;
+    const int r0 = 64 * static_cast<int>(cluster_rank());
+    const float ssc = kLog2e / p.eps[hq];
+    const float wq = p.w_dist ? p.w_dist[hq] : 0.0f;
     __syncthreads();
-    if (p.cost_mode == DFS_COST_QK) {
-      drain_m64<NP>(Ts, tbase, 0, qk_scale, warp, lane);
+    if (p.cost_mode == DFS_COST_QK)
+      drain_m64<NP>(Ts, *tslot, 0, ssc * rsqrtf(static_cast<float>(DH)), warp, lane);
+    else
+      dense_cost_to_stage<NP>(Ts, p.C, static_cast<size_t>(bq) * p.H + hq, p.N, r0, ssc, tid);
+    if (p.pos_weight != nullptr || (p.x_res != nullptr && wq != 0.0f)) {
+      BiasArgs bias;
+      bias.pos_weight = p.pos_weight;
+      bias.pos_bins = p.pos_bins;
+      bias.xrow = rowv + RV_X0 * 64;
+      bias.xcol = colv + CV_X0 * NP;
+      bias.geo = p.x_res != nullptr && wq != 0.0f;
+      bias.w_h = wq;
+      bias.r_0 = p.r_0;
+      bias.s_scale = ssc;
+      bias.bb = bq;
+      bias.hh = hq;
+      bias.N = p.N;
+      bias.row0 = r0;
+      bias.transposed = false;
       __syncthreads();
-      stage_to_regs<NS>(E, Ts, warp, lane);
-      __syncthreads();
-    } else {
-#pragma unroll
-      for (int r = 0; r < kRpw; ++r) {
-        const int gi = row0 + kRpw * warp + r;
-#pragma unroll
-        for (int k = 0; k < NS; ++k) {
-          const int gj = 32 * k + lane;
-          E[r][k] = (gi < N && gj < N) ? -p.C[(bh * N + gi) * N + gj] * s_scale : 0.0f;
-        }
-      }
+      add_cost_bias_stage<NP>(Ts, bias, tid);
     }
-    add_cost_bias<NS>(E, bias, warp, lane);
+    __syncthreads();
+    stage_to_regs<NS>(E, Ts, warp, lane);
   };
 
   // Rebuild the stabilised kernel matrix from S' and the potentials (fr, G[gcur]).
@@ -235,10 +239,10 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
         const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
         m = make_float4(fmaxf(m.x, x.x), fmaxf(m.y, x.y), fmaxf(m.z, x.z), fmaxf(m.w, x.w));
       }
-      ex.put4(j4, m);
-      if (tid == 0) ex.put4(NP, make_float4(ordered_to_float(mi[MI_ALPHA]), 0.f, 0.f, 0.f));
+      *reinterpret_cast<float4*>(ex.stage() + j4) = m;
+      if (tid == 0) ex.stage()[NP] = ordered_to_float(mi[MI_ALPHA]);
     }
-    ex.sync();
+    if (!ex.exchange(tid, Cfg::XBYTES)) err |= DFS_ERR_DEVICE_TIMEOUT;
     float* beta_tmp = colv + (CV_G0 + CV_G1 - gcur) * NP;  // the next-g buffer is free here
     if (tid < OWN) {
       float m[4] = {kNeg, kNeg, kNeg, kNeg};
@@ -280,39 +284,39 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     __syncthreads();
   };
 
-  // Row update: f = kappa (a - LSE_j(S + g)) for row rho.  With `rowmax` it
-  // instead returns the row sum and max of E v (for the transport plan).
-  auto row_pass = [&](float (&v)[NS], float* rowmax) -> float {
-    // v = exp2(beta + g - g_abs) <= exp2(kDrift): beta <= 0 and the drift is
-    // bounded by re-absorption, so the sum needs no further shift
+  // Hot-loop code below is written without short-circuit logic or conditional
+  // calls (bitwise & on bools, selects after unconditional arithmetic): each
+  // divergent branch region costs far more than the arithmetic it guards.
+
+  // v = exp2(beta + g - g_abs) <= exp2(kDrift): beta <= 0 and the drift is
+  // bounded by re-absorption, so the row sums need no further shift.
+  auto load_v = [&](float (&v)[NS]) {
 #pragma unroll
     for (int k = 0; k < NS; ++k) v[k] = colv[CV_V * NP + 32 * k + lane];
-    float acc[kRpw], amx[kRpw];
+  };
+  // Row update: f = kappa (a - LSE_j(S + g)) for row rho.
+  auto row_pass = [&]() -> float {
+    float v[NS];
+    load_v(v);
+    float acc[kRpw];
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) {
-      float s = 0.0f, m = 0.0f;
+      float s = 0.0f;
 #pragma unroll
-      for (int k = 0; k < NS; ++k) {
-        const float t = E[r][k] * v[k];
-        s += t;
-        if (rowmax) m = fmaxf(m, t);
-      }
+      for (int k = 0; k < NS; ++k) s = fmaf(E[r][k], v[k], s);
       acc[r] = s;
-      amx[r] = m;
     }
     const float s = reduce4_rows<false>(acc, lane);
-    if (rowmax) {
-      *rowmax = reduce4_rows<true>(amx, lane);
-      return s;
-    }
-    return rok ? kap * (ar - (atr + lg2(s))) : 0.0f;
+    const float f = kap * (ar - (atr + lg2(s)));
+    return rok ? f : 0.0f;
   };
 
-  // Column update from the new row potential fn into G[next]; returns a
-  // cluster-uniform "must re-absorb and repeat" flag, and the cluster maxima of
-  // |f - f_prev| and |f - f_abs|.
-  auto col_pass = [&](float fn, float fprev, int set, float& dfg, float& fdg) -> int {
-    const float u_r = rok ? ex2(fn + atr - mall) : 0.0f;
+  // Column update from the new row potential fn into G[next] and v; returns a
+  // cluster-uniform "must re-absorb and repeat" flag.  Drift / convergence
+  // flags of the iteration go to mi[MI_FL + set].
+  auto col_pass = [&](float fn, float fprev, int set, bool chk) -> int {
+    const float ue = ex2(fn + atr - mall);
+    const float u_r = rok ? ue : 0.0f;
     float u[kRpw];
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) u[r] = __shfl_sync(0xffffffffu, u_r, 8 * r);
@@ -320,67 +324,72 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     for (int k = 0; k < NS; ++k) {
       float cs = 0.0f;
 #pragma unroll
-      for (int r = 0; r < kRpw; ++r) cs += E[r][k] * u[r];
+      for (int r = 0; r < kRpw; ++r) cs = fmaf(E[r][k], u[r], cs);
       red[warp * NP + 32 * k + lane] = cs;
     }
-    int* ms = mi + MI_SET + 4 * set;
-    if (row_owner && rok) {
-      atomicMax(&ms[0], __float_as_int(fabsf(fn - fprev)));
-      atomicMax(&ms[1], __float_as_int(fabsf(fn - fabs_r)));
+    {
+      const bool own = row_owner & rok;
+      const unsigned fb = static_cast<unsigned>(own & (fabsf(fn - fabs_r) > kDrift)) * FL_FDRIFT |
+                          static_cast<unsigned>(own & chk & (fabsf(fn - fprev) * kLn2 >= p.threshold)) * FL_FNC;
+      const unsigned wb = __reduce_or_sync(0xffffffffu, fb);
+      if (lane == 0 && wb) atomicOr(&mi[MI_FL + set], static_cast<int>(wb));
     }
     __syncthreads();
-    if (tid < 4) mi[MI_SET + 4 * (set ^ 1) + tid] = 0;  // the other set, for the next iteration
-    if (tid < OWN) {  // CTA partial of 4 columns to every CTA
-      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid == 0) mi[MI_FL + (set ^ 1)] = 0;  // the other parity, for the next iteration
+    // From here each thread tid < NP works on one column jc.  CTA partial: lane
+    // l of warp w takes quad q = 8w + (l & 7) (columns 4q..4q+3) and sums the
+    // 4 warp partials 4g..4g+3, g = l >> 3, so that each quarter-warp reads
+    // 128 contiguous bytes (no bank conflicts); a reduce-scatter over the 4
+    // lanes of the quad (xor 8, xor 16: 3 shuffles) leaves lane l with column
+    // jc = 4q + g, staged for the cluster exchange.
+    const bool colt = tid < NP;  // warp-uniform (NP is a multiple of 64)
+    const int jc = 32 * warp + 4 * (lane & 7) + (lane >> 3);
+    float c_ok = 0.0f, c_bnu = 0.0f, c_bt = 0.0f, c_gab = 0.0f, c_gc = 0.0f;
+    if (colt) {
+      const int qd = 8 * warp + (lane & 7), g4 = lane >> 3;
+      const float* rp = red + (4 * g4) * NP + 4 * qd;
+      float4 s4 = *reinterpret_cast<const float4*>(rp);
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
+      for (int w = 1; w < 4; ++w) {
+        const float4 x = *reinterpret_cast<const float4*>(rp + w * NP);
         s4 = make_float4(s4.x + x.x, s4.y + x.y, s4.z + x.z, s4.w + x.w);
       }
-      ex.put4(j4, s4);
-      if (tid == 0) ex.put4(NP, make_float4(__int_as_float(ms[0]), __int_as_float(ms[1]), 0.f, 0.f));
+      const bool hi = (g4 & 2) != 0, odd = (g4 & 1) != 0;
+      const float k0 = hi ? s4.z : s4.x, k1 = hi ? s4.w : s4.y;   // columns 2h, 2h+1 kept
+      const float o0 = hi ? s4.x : s4.z, o1 = hi ? s4.y : s4.w;   // the other half, sent
+      const float a0 = k0 + __shfl_xor_sync(0xffffffffu, o0, 16);
+      const float a1 = k1 + __shfl_xor_sync(0xffffffffu, o1, 16);
+      const float kk = odd ? a1 : a0, oo = odd ? a0 : a1;
+      const float ctot = kk + __shfl_xor_sync(0xffffffffu, oo, 8);
+      ex.stage()[jc] = ctot;
+      // this column's constants, loaded before the exchange
+      c_ok = colv[CV_OK * NP + jc];
+      c_bnu = colv[CV_BNU * NP + jc];
+      c_bt = colv[CV_BT * NP + jc];
+      c_gab = colv[CV_GABS * NP + jc];
+      c_gc = colv[gcur * NP + jc];
     }
-    ex.sync();
-    dfg = 0.0f;
-    fdg = 0.0f;
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const float4 sc = *reinterpret_cast<const float4*>(ex.from(c) + NP);
-      dfg = fmaxf(dfg, sc.x);
-      fdg = fmaxf(fdg, sc.y);
-    }
+    if (tid == 0) ex.stage()[NP] = __int_as_float(mi[MI_FL + set]);  // this CTA's row flags
+    if (!ex.exchange(tid, Cfg::XBYTES)) err |= DFS_ERR_DEVICE_TIMEOUT;
     int bad = 0;
-    if (tid < OWN) {
-      float tot[4] = {0.f, 0.f, 0.f, 0.f};
+    unsigned gb = 0;
+    if (warp == 0 && lane < C) gb = (__float_as_uint(ex.from(lane)[NP]) & (FL_FDRIFT | FL_FNC)) << 4;
+    if (colt) {
+      float t = ex.from(0)[jc];
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const float4 x = *reinterpret_cast<const float4*>(ex.from(c) + j4);
-        tot[0] += x.x;
-        tot[1] += x.y;
-        tot[2] += x.z;
-        tot[3] += x.w;
-      }
-      float gd = 0.0f, dg = 0.0f;
-      float* gnext = colv + (CV_G0 + CV_G1 - gcur) * NP;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = j4 + q;
-        float gn = 0.0f;
-        if (colv[CV_OK * NP + j] != 0.0f) {
-          if (!(tot[q] > 1e-30f) || !(tot[q] < 3e38f)) bad = 1;
-          gn = kap * (colv[CV_BNU * NP + j] - (colv[CV_BT * NP + j] + mall + lg2(tot[q])));
-          gd = fmaxf(gd, fabsf(gn - colv[CV_GABS * NP + j]));
-          dg = fmaxf(dg, fabsf(gn - colv[gcur * NP + j]));
-        }
-        gnext[j] = gn;
-        // the row update of the next iteration reads v (all reads of this
-        // iteration's v finished before the first barrier above)
-        colv[CV_V * NP + j] = colv[CV_OK * NP + j] != 0.0f ? ex2(colv[CV_BT * NP + j] + gn) : 0.0f;
-      }
-      if (!bad) {  // NaN bits would compare as huge ints: only finite values enter
-        atomicMax(&ms[2], __float_as_int(gd));
-        atomicMax(&ms[3], __float_as_int(dg));
-      }
+      for (int c = 1; c < C; ++c) t += ex.from(c)[jc];
+      const bool ok = c_ok != 0.0f;
+      bad = static_cast<int>(ok & !((t > 1e-30f) & (t < 3e38f)));
+      const float g = kap * (c_bnu - (c_bt + mall + lg2(t)));
+      const float e = ex2(c_bt + g);
+      colv[(CV_G0 + CV_G1 - gcur) * NP + jc] = ok ? g : 0.0f;
+      // the row update of the next iteration reads v (all reads of this
+      // iteration's v finished before the first barrier above)
+      colv[CV_V * NP + jc] = ok ? e : 0.0f;
+      gb |= static_cast<unsigned>(ok & (fabsf(g - c_gab) > kDrift)) * FL_GDRIFT |
+            static_cast<unsigned>(ok & chk & (fabsf(g - c_gc) * kLn2 >= p.threshold)) * FL_GNC;
+      const unsigned wb = __reduce_or_sync(0xffffffffu, gb);
+      if (lane == 0 && wb) atomicOr(&mi[MI_FL + set], static_cast<int>(wb));
     }
     ex.next();
     return __syncthreads_or(bad);  // every CTA combined the same values: cluster-uniform
@@ -390,43 +399,76 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
 #pragma unroll
   for (int k = 0; k < NS; ++k) cokm |= (colv[CV_OK * NP + 32 * k + lane] != 0.0f) ? (1u << k) : 0u;
 
-  absorb();
-
   // ---------------------------------------------------------------- iterations
-  bool need_absorb = false;
+  // absorb() has a single call site (the loop must fit the instruction cache):
+  // the first absorption, re-absorption on drift, the emergency absorption
+  // before a repeated column update and the one before the outputs all enter
+  // through the top of this loop.  All control flow is cluster-uniform.
+  const bool want_out = p.O != nullptr || p.x_centroid != nullptr || p.T_out != nullptr;
+  bool need_absorb = true, redo = false, finishing = p.K_iter <= 0;
+  float fn = 0.0f, fprev = 0.0f;
+  int it = 0;
+  const bool use_thr = p.threshold > 0.0f;
+  int chk_left = p.check_every;  // iterations until the next convergence check
 #pragma unroll 1
-  for (int it = 0; it < p.K_iter; ++it) {
-    const int set = it & 1;
-    if (need_absorb) absorb();
-    const float fprev = fr;
-    float v[NS];
-    const float fn = row_pass(v, nullptr);
-    float dfg, fdg;
-    if (col_pass(fn, fprev, set, dfg, fdg)) {
-      // a column sum left the fp32 range: absorb around the new row potential
-      // (and the previous, valid g) and repeat the column update
-      if (tid < 4) mi[MI_SET + 4 * set + tid] = 0;
-      fr = fn;
+  for (;;) {
+    if (__builtin_expect(need_absorb, 0)) {
       absorb();
-      if (col_pass(fn, fprev, set, dfg, fdg)) err |= DFS_ERR_NUMERIC;
+      need_absorb = false;
+      if (finishing) break;
     }
+    const int set = it & 1;
+    const bool chk = use_thr & (chk_left == 1);
+    if (!redo) {
+      fprev = fr;
+      fn = row_pass();
+    }
+    const int bad = col_pass(fn, fprev, set, chk);
+    if (__builtin_expect(bad != 0, 0)) {
+      if (!redo) {
+        // a column sum left the fp32 range: absorb around the new row
+        // potential (and the previous, valid g) and repeat the column update
+        if (tid == 0) mi[MI_FL + set] = 0;
+        fr = fn;
+        redo = need_absorb = true;
+        continue;
+      }
+      err |= DFS_ERR_NUMERIC;
+    }
+    redo = false;
+    const unsigned fl = static_cast<unsigned>(mi[MI_FL + set]);
     fr = fn;
     gcur = CV_G0 + CV_G1 - gcur;
-    const float gdrift = __int_as_float(mi[MI_SET + 4 * set + 2]);
-    const float dgmax = __int_as_float(mi[MI_SET + 4 * set + 3]);
-    need_absorb = gdrift > kDrift || fdg > kDrift;
-    if (p.threshold > 0.0f && ((it + 1) % p.check_every) == 0) {
-      // threshold is in natural-log units, potentials here in log2 units
-      if (fmaxf(dfg, dgmax) * kLn2 < p.threshold) break;
+    need_absorb = (fl & (FL_FDRIFT_C | FL_GDRIFT)) != 0;
+    ++it;
+    chk_left = chk ? p.check_every : chk_left - 1;
+    const bool stop = (chk & ((fl & (FL_FNC_C | FL_GNC)) == 0)) | (it >= p.K_iter);
+    if (__builtin_expect(stop, 0)) {
+      finishing = true;
+      need_absorb = need_absorb & want_out;
+      if (!need_absorb) break;
     }
   }
 
   // ---------------------------------------------------------------- outputs
-  if (p.O != nullptr || p.x_centroid != nullptr || p.T_out != nullptr) {
-    if (need_absorb) absorb();  // cluster-uniform: the drift maxima are identical in every CTA
+  if (want_out) {
     float v[NS];
-    float rmax;
-    const float s = row_pass(v, &rmax);
+    load_v(v);
+    float acc[kRpw], amx[kRpw];
+#pragma unroll
+    for (int r = 0; r < kRpw; ++r) {
+      float sr = 0.0f, m = 0.0f;
+#pragma unroll
+      for (int k = 0; k < NS; ++k) {
+        const float t = E[r][k] * v[k];
+        sr += t;
+        m = fmaxf(m, t);
+      }
+      acc[r] = sr;
+      amx[r] = m;
+    }
+    const float s = reduce4_rows<false>(acc, lane);
+    const float rmax = reduce4_rows<true>(amx, lane);
     const float inv_r = (rok && s > 0.0f) ? 1.0f / (s + 1e-6f * rmax) : 0.0f;
     float inv[kRpw];
 #pragma unroll

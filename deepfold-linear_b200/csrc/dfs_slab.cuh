@@ -66,33 +66,39 @@ struct BiasArgs {
   bool transposed;           // slab rows are cost columns (bins read as [col][row])
 };
 
-template <int NS>
-DFS_DEV void add_cost_bias(float (&E)[kRpw][NS], const BiasArgs& a, int warp, int lane) {
-  constexpr int NP = 32 * NS;
-  if (a.pos_weight == nullptr && !a.geo) return;
-#pragma unroll
-  for (int r = 0; r < kRpw; ++r) {
-    const int li = kRpw * warp + r, gi = a.row0 + li;
-    const float xi0 = a.geo ? a.xrow[li] : 0.f, xi1 = a.geo ? a.xrow[64 + li] : 0.f,
-                xi2 = a.geo ? a.xrow[128 + li] : 0.f;
-#pragma unroll
-    for (int k = 0; k < NS; ++k) {
-      const int gj = 32 * k + lane;
-      float bias = 0.0f;
-      if (gi < a.N && gj < a.N) {
-        if (a.pos_weight) {
-          const size_t bi = a.transposed ? (static_cast<size_t>(a.bb) * a.N + gj) * a.N + gi
-                                         : (static_cast<size_t>(a.bb) * a.N + gi) * a.N + gj;
-          bias += a.pos_weight[a.hh * 68 + a.pos_bins[bi]];
-        }
-        if (a.geo) {
-          const float d0 = xi0 - a.xcol[gj], d1 = xi1 - a.xcol[NP + gj], d2 = xi2 - a.xcol[2 * NP + gj];
-          const float dist = sqrtf(d0 * d0 + d1 * d1 + d2 * d2 + 1e-8f);
-          bias += a.w_h * dist / (a.r_0 + dist);
-        }
-      }
-      E[r][k] -= bias * a.s_scale;
+// Subtract the bias terms from the staged 64 x NP slab S' (128B-swizzled, see
+// sw_off).  A rolled loop over the tile: the code stays small, consecutive
+// threads touch consecutive columns (coalesced bin reads).
+template <int NP>
+DFS_DEV void add_cost_bias_stage(float* Ts, const BiasArgs& a, int tid) {
+#pragma unroll 1
+  for (int idx = tid; idx < 64 * NP; idx += kThreads) {
+    const int li = idx / NP, gj = idx - li * NP, gi = a.row0 + li;
+    if (gi >= a.N || gj >= a.N) continue;
+    float bias = 0.0f;
+    if (a.pos_weight) {
+      const size_t bi = a.transposed ? (static_cast<size_t>(a.bb) * a.N + gj) * a.N + gi
+                                     : (static_cast<size_t>(a.bb) * a.N + gi) * a.N + gj;
+      bias += a.pos_weight[a.hh * 68 + a.pos_bins[bi]];
     }
+    if (a.geo) {
+      const float d0 = a.xrow[li] - a.xcol[gj], d1 = a.xrow[64 + li] - a.xcol[NP + gj],
+                  d2 = a.xrow[128 + li] - a.xcol[2 * NP + gj];
+      const float dist = sqrtf(d0 * d0 + d1 * d1 + d2 * d2 + 1e-8f);
+      bias += a.w_h * dist / (a.r_0 + dist);
+    }
+    Ts[sw_off(li, gj, 64) >> 2] -= bias * a.s_scale;
+  }
+}
+
+// Dense cost rows [row0, row0+64) of a (., N, N) fp32 matrix into the staging
+// tile as S' = -C * s_scale (zero outside N x N).
+template <int NP>
+DFS_DEV void dense_cost_to_stage(float* Ts, const float* Cm, size_t bh, int N, int row0, float s_scale, int tid) {
+#pragma unroll 1
+  for (int idx = tid; idx < 64 * NP; idx += kThreads) {
+    const int li = idx / NP, gj = idx - li * NP, gi = row0 + li;
+    Ts[sw_off(li, gj, 64) >> 2] = (gi < N && gj < N) ? -__ldg(Cm + (bh * N + gi) * N + gj) * s_scale : 0.0f;
   }
 }
 
