@@ -21,19 +21,27 @@
 //
 // Phases (all MMAs tcgen05 kind::tf32, K-major operands, accumulators in TMEM):
 //   1  row slab:    S = Q_s K^T -> P, r, T_norm           (registers)
-//   2               dT = dO_s V^T -> E, D; one cluster exchange gives c = P^T 1,
-//                   g_v = E^T 1 and all-gathers f, 1/rowsum and D
-//   3  CG:          Jacobi-preconditioned, Chronopoulos-Gear form, one matvec and
-//                   one fused cluster reduction per iteration, no host sync
-//   4               w1 all-gathered; marginal gradients
+//   2               dT = dO_s V^T -> E (in shared memory), D; one cluster
+//                   exchange of the column sums c = P^T 1 and g_v = E^T 1
+//   3  CG:          on the Schur complement of the row block (preconditioner
+//                   D2), Chronopoulos-Gear form: per iteration one P / P^T
+//                   product pair, one cluster exchange, three CTA barriers
+//   4               all-gather w1, f, 1/rowsum, D; marginal gradients
 //   5               dS = E - P (w1 + w2);  dQ = dS K
-//   6  column slab: S^T = K_s Q^T -> P^T, T_norm^T           (registers)
-//   7               dV = T_norm^T dO,  dT^T = V_s dO^T
+//   6  column slab: S^T = K_s Q^T -> P^T                     (registers)
+//   7               dT^T = V_s dO^T,  dV = T_norm^T dO
 //   8               dS^T = T_norm^T (dT^T - D) - P^T (w1 + w2);  dK = dS^T Q
 // Every row or column is owned by exactly one CTA: no atomics, deterministic.
+// Element loops over the register slab are branch-free; optional terms (dxc,
+// bias) are separate rolled passes over the shared-memory tile.
 #include "dfs_slab.cuh"
 
 namespace dfs {
+
+// column-indexed vectors; FA/INV/DD/W1 hold all N rows after the all-gather
+enum { BC_G = 0, BC_OK, BC_U2, BC_SOL2, BC_FA, BC_INV, BC_DD, BC_W1, BC_CC, BC_X0, BC_X1, BC_X2, BC_NUM };
+// slab-row vectors: coordinates and per-row values kept out of registers
+enum { BR_X0 = 0, BR_X1, BR_X2, BR_INV, BR_D, BR_F, BR_NUM };
 
 template <int C, int DH>
 struct BwdCfg {
@@ -43,15 +51,13 @@ struct BwdCfg {
   static constexpr uint32_t OFF_SA = OFF_T + 256u * NP;               // 64 x DH slab operand
   static constexpr uint32_t OFF_DA = OFF_SA + 256u * DH;              // 64 x DH dO slab
   static constexpr uint32_t OFF_KV = OFF_DA + 256u * DH;              // NP x DH operand / partials
-  // one-off exchange of phase 2 (single buffer) and the CG / all-gather
-  // exchanges (double buffered), see ClusterExchange
-  static constexpr int RSA = 2 * NP + 3 * 64 + 8;
-  static constexpr int RSB = NP + 8;
-  static constexpr uint32_t OFF_XA = OFF_KV + 4u * NP * DH;           // C x RSA
-  static constexpr uint32_t OFF_XB = OFF_XA + 4u * C * RSA;           // 2 x C x RSB
-  static constexpr uint32_t OFF_COL = OFF_XB + 8u * C * RSB;          // column / all-row vectors
-  static constexpr uint32_t OFF_ROW = OFF_COL + 4u * 12 * NP;         // slab-row vectors
-  static constexpr uint32_t OFF_MISC = OFF_ROW + 4u * 4 * 64;
+  // exchange rounds: phase 2 (2 NP + 4 floats), CG (NP + 4), phase 4 (260)
+  static constexpr int RS = (2 * NP > 256 ? 2 * NP : 256) + 8;
+  static constexpr uint32_t OFF_XR = OFF_KV + 4u * NP * DH;           // 2 x C x RS receive slots
+  static constexpr uint32_t OFF_STG = OFF_XR + 8u * C * RS;           // 2 x RS stages
+  static constexpr uint32_t OFF_COL = OFF_STG + 8u * RS;              // column / all-row vectors
+  static constexpr uint32_t OFF_ROW = OFF_COL + 4u * BC_NUM * NP;     // slab-row vectors
+  static constexpr uint32_t OFF_MISC = OFF_ROW + 4u * BR_NUM * 64;    // 192 floats, barriers
   static constexpr uint32_t SMEM_NEED = OFF_MISC + 1024 + 1024;
   static constexpr uint32_t SMEM = SMEM_NEED > 122880u ? SMEM_NEED : 122880u;
   static_assert(SMEM <= 232448u, "exceeds the 227 KB of shared memory a CTA can use");
@@ -59,34 +65,28 @@ struct BwdCfg {
   static_assert(NP + DH <= 512, "TMEM columns");
 };
 
-// column-indexed vectors; FA/INV/DD/W1 hold all N rows after the all-gathers
-enum { BC_G = 0, BC_OK, BC_U2, BC_SOL2, BC_FA, BC_INV, BC_DD, BC_W1, BC_X0, BC_X1, BC_X2, BC_NUM };
-enum { BR_X0 = 0, BR_X1, BR_X2 };
-
 template <int C, int DH>
 __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdParams p) {
   using Cfg = BwdCfg<C, DH>;
   constexpr int NP = Cfg::NP, NS = Cfg::NS;
-  constexpr int MC = (NP + kThreads - 1) / kThreads;  // columns per thread for vector work (j = tid + kThreads m)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* Ts = reinterpret_cast<float*>(base + Cfg::OFF_T);
   float* SA = reinterpret_cast<float*>(base + Cfg::OFF_SA);
   float* DA = reinterpret_cast<float*>(base + Cfg::OFF_DA);
   float* KV = reinterpret_cast<float*>(base + Cfg::OFF_KV);
-  ClusterExchange<C, Cfg::RSA> exa{reinterpret_cast<float*>(base + Cfg::OFF_XA), 0, 0};
-  ClusterExchange<C, Cfg::RSB> exb{reinterpret_cast<float*>(base + Cfg::OFF_XB), 0, 0};
   float* colv = reinterpret_cast<float*>(base + Cfg::OFF_COL);
   float* rowv = reinterpret_cast<float*>(base + Cfg::OFF_ROW);
-  float* misc = reinterpret_cast<float*>(base + Cfg::OFF_MISC);       // 192 scalars (per-warp slots of 16)
+  float* misc = reinterpret_cast<float*>(base + Cfg::OFF_MISC);  // [0,64) and [64,128): per-warp sums
   uint64_t* mbar = reinterpret_cast<uint64_t*>(base + Cfg::OFF_MISC + 768);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(base + Cfg::OFF_MISC + 784);
+  BulkExchange<C, Cfg::RS> ex{reinterpret_cast<float*>(base + Cfg::OFF_XR),
+                              reinterpret_cast<float*>(base + Cfg::OFF_STG),
+                              reinterpret_cast<uint64_t*>(base + Cfg::OFF_MISC + 800), 0, 0u, 0, false};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int crank = static_cast<int>(cluster_rank());
-  exa.rank = exb.rank = crank;
-  constexpr int OWN = NP / 4;  // threads that own 4 consecutive columns for the exchanges
-  const int j4 = 4 * tid;
+  ex.rank = crank;
   const int prob = blockIdx.x / C;
   const int bb = prob / p.H, hh = prob % p.H;
   const int N = p.N;
@@ -114,52 +114,94 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     __syncthreads();
     tc_fence_after();
   };
+  // sum of the 16 per-warp partials slot[0..15] (broadcast float4 loads, fixed order)
+  auto sum16 = [](const float* slot) -> float {
+    const float4 a = *reinterpret_cast<const float4*>(slot), b = *reinterpret_cast<const float4*>(slot + 4),
+                 c = *reinterpret_cast<const float4*>(slot + 8), d = *reinterpret_cast<const float4*>(slot + 12);
+    return (((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w))) +
+           (((c.x + c.y) + (c.z + c.w)) + ((d.x + d.y) + (d.z + d.w)));
+  };
+  // CTA-wide sums of three per-thread values with one barrier; `slot` is one of
+  // the two 64-float regions of misc, laid out [value][warp].  Per warp: a
+  // 4-value transpose-reduce (6 shuffles) leaves lanes 0, 8, 16 with the warp
+  // totals; after the barrier each warp loads the 16 partials of each value
+  // (32-bit loads, one wavefront) and finishes with a 4-level xor butterfly,
+  // which gives every lane (and every CTA, for identical inputs) the same bits.
+  auto cta_sum3 = [&](float a, float b, float c, float* slot, float& A, float& B, float& Cs) {
+    const float v4[4] = {a, b, c, 0.0f};
+    const float v = reduce4_rows<false>(v4, lane);  // lane l: total of value (l >> 3) & 3
+    if ((lane & 7) == 0 && lane < 24) slot[(lane >> 3) * 16 + warp] = v;
+    __syncthreads();
+    const int l16 = lane & 15;
+    float x = slot[l16], y = slot[16 + l16], z = slot[32 + l16];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      x += __shfl_xor_sync(0xffffffffu, x, o);
+      y += __shfl_xor_sync(0xffffffffu, y, o);
+      z += __shfl_xor_sync(0xffffffffu, z, o);
+    }
+    A = x;
+    B = y;
+    Cs = z;
+  };
 
   // ---------------------------------------------------------------- setup
   if (warp == 0) tmem_alloc(tslot, 512);
   if (tid == 0) {
     mbar_init(mbar, 1);
+    ex.init();
     fence_mbar_init();
   }
-  for (int j = tid; j < NP; j += kThreads) {
-    const bool ok = j < N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + j] != 0.0f);
-    colv[BC_OK * NP + j] = ok ? 1.0f : 0.0f;
-    colv[BC_G * NP + j] = ok ? p.log_v[bh * N + j] * kLog2e : 0.0f;
+  const bool colt = tid < NP;  // column threads (whole warps)
+  const int jc = col_of_thread(warp, lane);
+  if (colt) {
+    const bool ok = jc < N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + jc] != 0.0f);
+    colv[BC_OK * NP + jc] = ok ? 1.0f : 0.0f;
+    colv[BC_G * NP + jc] = ok ? p.log_v[bh * N + jc] * kLog2e : 0.0f;
 #pragma unroll
     for (int c = 0; c < 3; ++c)
-      colv[(BC_X0 + c) * NP + j] = (p.x_res && j < N) ? p.x_res[(static_cast<size_t>(bb) * N + j) * 3 + c] : 0.0f;
+      colv[(BC_X0 + c) * NP + jc] =
+          (p.x_res && jc < N) ? p.x_res[(static_cast<size_t>(bb) * N + jc) * 3 + c] : 0.0f;
   }
-  for (int i = tid; i < 64; i += kThreads) {
-    const int gi = row0 + i;
+  if (tid < 64) {
+    const int gi = row0 + tid;
 #pragma unroll
     for (int c = 0; c < 3; ++c)
-      rowv[(BR_X0 + c) * 64 + i] = (p.x_res && gi < N) ? p.x_res[(static_cast<size_t>(bb) * N + gi) * 3 + c] : 0.0f;
+      rowv[(BR_X0 + c) * 64 + tid] =
+          (p.x_res && gi < N) ? p.x_res[(static_cast<size_t>(bb) * N + gi) * 3 + c] : 0.0f;
   }
   load_operand<DH>(SA, p.Q, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);
   load_operand<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
   load_operand_f32<DH>(DA, p.dO, bh * N, row0, 64, N, tid, kThreads);
   operands_ready();
+  if constexpr (C > 1) cluster_sync();  // every CTA's exchange mbarriers initialised
   const uint32_t tbase = *tslot;
 
-  BiasArgs bias;
-  bias.pos_weight = p.pos_weight;
-  bias.pos_bins = p.pos_bins;
-  bias.xrow = rowv + BR_X0 * 64;
-  bias.xcol = colv + BC_X0 * NP;
-  bias.geo = p.x_res != nullptr && w_h != 0.0f;
-  bias.w_h = w_h;
-  bias.r_0 = p.r_0;
-  bias.s_scale = s_scale;
-  bias.bb = bb;
-  bias.hh = hh;
-  bias.N = N;
-  bias.row0 = row0;
-  bias.transposed = false;
-  const bool bias_on = p.pos_weight != nullptr || bias.geo;
+  const bool bias_on = p.pos_weight != nullptr || (p.x_res != nullptr && w_h != 0.0f);
+  // subtract the position / geometry terms from the staged S' (built here so
+  // that none of it occupies registers in between)
+  auto add_bias = [&](bool transposed) {
+    BiasArgs bias;
+    bias.pos_weight = p.pos_weight;
+    bias.pos_bins = p.pos_bins;
+    bias.xrow = rowv + BR_X0 * 64;
+    bias.xcol = colv + BC_X0 * NP;
+    bias.geo = p.x_res != nullptr && w_h != 0.0f;
+    bias.w_h = w_h;
+    bias.r_0 = p.r_0;
+    bias.s_scale = s_scale;
+    bias.bb = bb;
+    bias.hh = hh;
+    bias.N = N;
+    bias.row0 = row0;
+    bias.transposed = transposed;
+    add_cost_bias_stage<NP>(Ts, bias, tid);
+  };
 
-  const int rho = (lane >> 3) & 3;
-  const int grow = row0 + kRpw * warp + rho;
+  const int rho = (lane >> 3) & 3;  // row whose totals this lane holds after reduce4_rows
+  const int li_own = kRpw * warp + rho, grow = row0 + li_own;
   const bool rok = grow < N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + grow] != 0.0f);
+  const bool own = ((lane & 7) == 0) & rok;  // one lane per valid row for row sums
   uint32_t rokm = 0, cokm = 0;
 #pragma unroll
   for (int r = 0; r < kRpw; ++r) {
@@ -170,6 +212,15 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
 #pragma unroll
   for (int k = 0; k < NS; ++k) cokm |= (colv[BC_OK * NP + 32 * k + lane] != 0.0f) ? (1u << k) : 0u;
   const float fr = rok ? p.log_u[bh * N + grow] * kLog2e : 0.0f;
+  if ((lane & 7) == 0) rowv[BR_F * 64 + li_own] = fr;
+  // sum of a per-row value over this warp's 4 rows (lanes 0, 8, 16, 24 hold
+  // one copy each); lane 0 ends with the warp total
+  auto rows_sum = [&](float v) -> float {
+    v = own ? v : 0.0f;
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    return v;
+  };
 
   // ---------------------------------------------------------------- phase 1
   if (tid == 0) {
@@ -177,50 +228,43 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     mma_commit(mbar);
   }
   mma_wait();
-  __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, qk_scale, warp, lane);
   __syncthreads();
   if (bias_on) {
-    add_cost_bias_stage<NP>(Ts, bias, tid);
+    add_bias(false);
     __syncthreads();
   }
   float P[kRpw][NS];
   stage_to_regs<NS>(P, Ts, warp, lane);
+  float rsum_r, inv_r;
   {
     float fall[kRpw];
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) fall[r] = __shfl_sync(0xffffffffu, fr, 8 * r);
+    float a[kRpw], m[kRpw];
+#pragma unroll
+    for (int r = 0; r < kRpw; ++r) a[r] = m[r] = 0.0f;
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const float g = colv[BC_G * NP + 32 * k + lane];
 #pragma unroll
       for (int r = 0; r < kRpw; ++r) {
-        const bool ok = ((rokm >> r) & 1u) && ((cokm >> k) & 1u);
-        P[r][k] = ok ? ex2(P[r][k] + fall[r] + g) : 0.0f;
-      }
-    }
-  }
-  float rsum_r, inv_r;
-  {
-    float a[kRpw], m[kRpw];
-#pragma unroll
-    for (int r = 0; r < kRpw; ++r) {
-      a[r] = 0.0f;
-      m[r] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < NS; ++k) {
+        const bool ok = ((rokm >> r) & (cokm >> k) & 1u) != 0u;
+        const float e = ex2(P[r][k] + fall[r] + g);
+        P[r][k] = ok ? e : 0.0f;
         a[r] += P[r][k];
         m[r] = fmaxf(m[r], P[r][k]);
       }
     }
     rsum_r = reduce4_rows<false>(a, lane);
     const float pm = reduce4_rows<true>(m, lane);
-    inv_r = (rok && rsum_r > 0.0f) ? 1.0f / (rsum_r + 1e-6f * pm) : 0.0f;
+    const float iv = 1.0f / (rsum_r + 1e-6f * pm);
+    inv_r = (rok & (rsum_r > 0.0f)) ? iv : 0.0f;
     if (!isfinite(rsum_r)) err |= DFS_ERR_NUMERIC;
   }
 
   // ---------------------------------------------------------------- phase 2
-  __syncthreads();
+  __syncthreads();  // Ts (S) fully read
   load_operand<DH>(KV, p.V, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
   operands_ready();
   if (tid == 0) {
@@ -228,37 +272,35 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     mma_commit(mbar);
   }
   mma_wait();
-  __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, 1.0f, warp, lane);
   __syncthreads();
+  if (p.dxc) {  // dT[i][j] += dxc_i . x_j
+#pragma unroll 1
+    for (int idx = tid; idx < 64 * NP; idx += kThreads) {
+      const int li = idx / NP, gj = idx - li * NP, gi = row0 + li;
+      if (gi < N) {
+        const float* dx = p.dxc + (bh * N + gi) * 3;
+        Ts[sw_off(li, gj, 64) >> 2] += dx[0] * colv[BC_X0 * NP + gj] + dx[1] * colv[BC_X1 * NP + gj] +
+                                       dx[2] * colv[BC_X2 * NP + gj];
+      }
+    }
+    __syncthreads();
+  }
   float* red = KV;  // V is no longer needed: 2 x kWarps x NP column partials (P and E)
   float fbar_r, D_r;
   {
     float inv[kRpw];
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) inv[r] = __shfl_sync(0xffffffffu, inv_r, 8 * r);
-    float dxr[3][kRpw];
-#pragma unroll
-    for (int r = 0; r < kRpw; ++r) {
-      const int gi = row0 + kRpw * warp + r;
-#pragma unroll
-      for (int c = 0; c < 3; ++c) dxr[c][r] = (p.dxc && gi < N) ? p.dxc[(bh * N + gi) * 3 + c] : 0.0f;
-    }
     float accD[kRpw];
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) {
-      accD[r] = 0.0f;
+      float s = 0.0f;
 #pragma unroll
-      for (int k = 0; k < NS; ++k) {
-        const int j = 32 * k + lane;
-        float dt = Ts[sw_off(kRpw * warp + r, j, 64) >> 2];
-        if (p.dxc)
-          dt += dxr[0][r] * colv[BC_X0 * NP + j] + dxr[1][r] * colv[BC_X1 * NP + j] +
-                dxr[2][r] * colv[BC_X2 * NP + j];
-        accD[r] += P[r][k] * inv[r] * dt;
-      }
+      for (int k = 0; k < NS; ++k) s = fmaf(P[r][k], Ts[sw_off(kRpw * warp + r, 32 * k + lane, 64) >> 2], s);
+      accD[r] = s;
     }
-    D_r = reduce4_rows<false>(accD, lane);
+    D_r = inv_r * reduce4_rows<false>(accD, lane);  // D = sum_j T_norm dT
     float D[kRpw];
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) D[r] = __shfl_sync(0xffffffffu, D_r, 8 * r);
@@ -272,11 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
 #pragma unroll
       for (int r = 0; r < kRpw; ++r) {
         const uint32_t o = sw_off(kRpw * warp + r, j, 64) >> 2;
-        float dt = Ts[o];
-        if (p.dxc)
-          dt += dxr[0][r] * colv[BC_X0 * NP + j] + dxr[1][r] * colv[BC_X1 * NP + j] +
-                dxr[2][r] * colv[BC_X2 * NP + j];
-        const float e = P[r][k] * inv[r] * (dt - D[r]);
+        const float e = P[r][k] * inv[r] * (Ts[o] - D[r]);
         Ts[o] = e;
         ce += e;
         cp += P[r][k];
@@ -286,284 +324,199 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       red[kWarps * NP + warp * NP + j] = ce;
     }
     fbar_r = reduce4_rows<false>(re, lane);
+    if ((lane & 7) == 0) {
+      rowv[BR_INV * 64 + li_own] = inv_r;
+      rowv[BR_D * 64 + li_own] = D_r;
+    }
   }
   {
-    const bool own = (lane & 7) == 0 && rok;
-    const float sf = warp_sum(own ? fbar_r : 0.0f);
-    const float sr = warp_sum(own ? rsum_r : 0.0f);
+    const float sf = rows_sum(fbar_r), sr = rows_sum(rsum_r);
     if (lane == 0) {
       misc[warp] = sf;
       misc[16 + warp] = sr;
     }
   }
   __syncthreads();
-  if (tid < OWN) {
-    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (colt) {
+    ex.stage()[jc] = colsum16<NP>(red, warp, lane);
+    ex.stage()[NP + jc] = colsum16<NP>(red + kWarps * NP, warp, lane);
+  }
+  if (tid == kThreads - 32) {  // last warp: no column work (NP <= 384 < 512)
+    ex.stage()[2 * NP] = sum16(misc);
+    ex.stage()[2 * NP + 1] = sum16(misc + 16);
+  }
+  if (!ex.exchange(tid, 4u * (2 * NP + 4))) err |= DFS_ERR_DEVICE_TIMEOUT;
+  float cc = 0.0f, gv = 0.0f, okc = 0.0f;
+  if (colt) {
+    cc = ex.from(0)[jc];
+    gv = ex.from(0)[NP + jc];
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
-      const float4 y = *reinterpret_cast<const float4*>(red + kWarps * NP + w * NP + j4);
-      a4 = make_float4(a4.x + x.x, a4.y + x.y, a4.z + x.z, a4.w + x.w);
-      b4 = make_float4(b4.x + y.x, b4.y + y.y, b4.z + y.z, b4.w + y.w);
+    for (int c = 1; c < C; ++c) {
+      cc += ex.from(c)[jc];
+      gv += ex.from(c)[NP + jc];
     }
-    exa.put4(j4, a4);
-    exa.put4(NP + j4, b4);
+    okc = colv[BC_OK * NP + jc];
+    colv[BC_CC * NP + jc] = cc;
   }
-  if ((lane & 7) == 0) {  // this slab's rows for the all-gathers
-    const int li = kRpw * warp + rho;
-    exa.put(2 * NP + li, fr);
-    exa.put(2 * NP + 64 + li, inv_r);
-    exa.put(2 * NP + 128 + li, D_r);
-  }
-  if (tid == 0) {
-    float a = 0.0f, b = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      a += misc[w];
-      b += misc[16 + w];
-    }
-    exa.put4(2 * NP + 192, make_float4(a, b, 0.0f, 0.0f));
-  }
-  exa.sync();
-  float cc[MC], gv[MC];
-  bool okc[MC];
   float sum_fbar = 0.0f, sum_r = 0.0f;
 #pragma unroll
-  for (int m = 0; m < MC; ++m) {
-    const int j = tid + kThreads * m;
-    cc[m] = gv[m] = 0.0f;
-    okc[m] = j < NP && colv[BC_OK * NP + j] != 0.0f;
-    if (j < NP) {
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        cc[m] += exa.from(c)[j];
-        gv[m] += exa.from(c)[NP + j];
-      }
-      const float* src = exa.from(j >> 6);
-      colv[BC_FA * NP + j] = src[2 * NP + (j & 63)];
-      colv[BC_INV * NP + j] = src[2 * NP + 64 + (j & 63)];
-      colv[BC_DD * NP + j] = src[2 * NP + 128 + (j & 63)];
-    }
-  }
-#pragma unroll
   for (int c = 0; c < C; ++c) {
-    sum_fbar += exa.from(c)[2 * NP + 192];
-    sum_r += exa.from(c)[2 * NP + 193];
+    sum_fbar += ex.from(c)[2 * NP];
+    sum_r += ex.from(c)[2 * NP + 1];
   }
-  __syncthreads();
+  ex.next();
 
   // ---------------------------------------------------------------- phase 3 (CG)
-  auto cta_sum = [&](float v, int slot) -> float {  // identical in every CTA
-    v = warp_sum(v);
-    if (lane == 0) misc[slot + warp] = v;
-    __syncthreads();
-    float s = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += misc[slot + w];
-    return s;
-  };
-  const float d1 = (rok && rsum_r > 0.0f) ? rsum_r / kap : 0.0f;
-  float d2[MC];
-#pragma unroll
-  for (int m = 0; m < MC; ++m) d2[m] = (okc[m] && cc[m] > 0.0f) ? cc[m] / kap : 0.0f;
+  // The Jacobi-preconditioned block system is 2-cyclic, so CG on it takes
+  // twice the iterations of CG on its Schur complement
+  //     S w2 = b2 - P^T D1^-1 b1,   S = D2 - P^T D1^-1 P,   preconditioner D2,
+  // followed by w1 = D1^-1 (b1 - P w2).  Rows are CTA-local, so one S
+  // product costs one cluster exchange (the column partials of P^T t).
+  const bool cok = okc != 0.0f;
+  const float d1 = (rok & (rsum_r > 0.0f)) ? rsum_r / kap : 0.0f;
+  const float d1i = d1 > 0.0f ? 1.0f / d1 : 0.0f;
+  const float d2 = (cok & (cc > 0.0f)) ? cc / kap : 0.0f;
+  const float d2i = d2 > 0.0f ? 1.0f / d2 : 0.0f;
   float b1 = rok ? fbar_r : 0.0f;
-  float b2[MC];
-#pragma unroll
-  for (int m = 0; m < MC; ++m) b2[m] = okc[m] ? gv[m] : 0.0f;
+  float b2 = cok ? gv : 0.0f;
   if (kap >= 1.0f) {  // project [b1; b2] onto the range of the singular system
-    float s2 = 0.0f, nv = 0.0f;
-#pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      s2 += b2[m];
-      nv += okc[m] ? 1.0f : 0.0f;
-    }
-    s2 = cta_sum(s2, 32);
-    nv = cta_sum(nv, 48);
+    float s2, nv, unused;
+    cta_sum3(b2, cok ? 1.0f : 0.0f, 0.0f, misc + 64, s2, nv, unused);
     const float sh = nv > 0.0f ? (sum_fbar - s2) / (2.0f * nv) : 0.0f;
-    if (rok) b1 -= sh;
-#pragma unroll
-    for (int m = 0; m < MC; ++m)
-      if (okc[m]) b2[m] += sh;
+    b1 = rok ? b1 - sh : 0.0f;
+    b2 = cok ? b2 + sh : 0.0f;
   }
 
-  float w1;
-  float w2[MC];
-  // w = A u for the block system; returns the global dots (res.u, w.u, res.res)
-  auto matvec = [&](float u1, const float (&u2)[MC], float res1, const float (&res2)[MC], float& ru,
-                    float& wu, float& rr) {
-#pragma unroll
-    for (int m = 0; m < MC; ++m)
-      if (tid + kThreads * m < NP) colv[BC_U2 * NP + tid + kThreads * m] = u2[m];
+  // P x for a column vector x (value of column thread jc); returns the row
+  // value (held by all 8 lanes of the row's group).  One barrier.
+  auto p_apply = [&](float xcol) -> float {
+    if (colt) colv[BC_U2 * NP + jc] = xcol;
     __syncthreads();
-    float acc[kRpw];
-    float u2k[NS];
-#pragma unroll
-    for (int k = 0; k < NS; ++k) u2k[k] = colv[BC_U2 * NP + 32 * k + lane];
-#pragma unroll
-    for (int r = 0; r < kRpw; ++r) {
-      float s = 0.0f;
-#pragma unroll
-      for (int k = 0; k < NS; ++k) s += P[r][k] * u2k[k];
-      acc[r] = s;
-    }
-    const float pu = reduce4_rows<false>(acc, lane);
-    w1 = rok ? d1 * u1 + pu : 0.0f;
-    float u1a[kRpw];
-#pragma unroll
-    for (int r = 0; r < kRpw; ++r) u1a[r] = __shfl_sync(0xffffffffu, u1, 8 * r);
+    float acc[kRpw] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
-      float s = 0.0f;
+      const float xk = colv[BC_U2 * NP + 32 * k + lane];
 #pragma unroll
-      for (int r = 0; r < kRpw; ++r) s += P[r][k] * u1a[r];
-      red[warp * NP + 32 * k + lane] = s;
+      for (int r = 0; r < kRpw; ++r) acc[r] = fmaf(P[r][k], xk, acc[r]);
     }
-    const bool own = (lane & 7) == 0 && rok;
-    const float a0 = warp_sum(own ? res1 * u1 : 0.0f);
-    const float a1 = warp_sum(own ? w1 * u1 : 0.0f);
-    const float a2 = warp_sum(own ? res1 * res1 : 0.0f);
-    if (lane == 0) {
-      misc[64 + warp] = a0;
-      misc[80 + warp] = a1;
-      misc[96 + warp] = a2;
+    return reduce4_rows<false>(acc, lane);
+  };
+  // P^T t for a row vector t (held by the row's lanes); returns the value of
+  // column jc (column threads).  One barrier and one cluster exchange.
+  auto pt_apply = [&](float trow) -> float {
+    float ta[kRpw];
+#pragma unroll
+    for (int r = 0; r < kRpw; ++r) ta[r] = __shfl_sync(0xffffffffu, trow, 8 * r);
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      float sk = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kRpw; ++r) sk = fmaf(P[r][k], ta[r], sk);
+      red[warp * NP + 32 * k + lane] = sk;
     }
     __syncthreads();
-    if (tid < OWN) {
-      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (colt) ex.stage()[jc] = colsum16<NP>(red, warp, lane);
+    if (!ex.exchange(tid, 4u * (NP + 4))) err |= DFS_ERR_DEVICE_TIMEOUT;
+    float t = 0.0f;
+    if (colt) {
+      t = ex.from(0)[jc];
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float4 x = *reinterpret_cast<const float4*>(red + w * NP + j4);
-        s4 = make_float4(s4.x + x.x, s4.y + x.y, s4.z + x.z, s4.w + x.w);
-      }
-      exb.put4(j4, s4);
-      if (tid == 0) {
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-          s0 += misc[64 + w];
-          s1 += misc[80 + w];
-          s2 += misc[96 + w];
-        }
-        exb.put4(NP, make_float4(s0, s1, s2, 0.0f));
-      }
+      for (int c = 1; c < C; ++c) t += ex.from(c)[jc];
     }
-    exb.sync();
-    float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
-#pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      const int j = tid + kThreads * m;
-      float t = 0.0f;
-      if (j < NP) {
-#pragma unroll
-        for (int c = 0; c < C; ++c) t += exb.from(c)[j];
-      }
-      w2[m] = okc[m] ? t + d2[m] * u2[m] : 0.0f;
-      c0 += res2[m] * u2[m];
-      c1 += w2[m] * u2[m];
-      c2 += res2[m] * res2[m];
-    }
-    float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const float4 d = *reinterpret_cast<const float4*>(exb.from(c) + NP);
-      g0 += d.x;
-      g1 += d.y;
-      g2 += d.z;
-    }
-    exb.next();
-    c0 = cta_sum(c0, 112);
-    c1 = cta_sum(c1, 128);
-    c2 = cta_sum(c2, 144);
-    __syncthreads();
-    ru = g0 + c0;
-    wu = g1 + c1;
-    rr = g2 + c2;
+    ex.next();
+    return t;
+  };
+  // S x = D2 x - P^T D1^-1 P x
+  auto schur = [&](float xcol) -> float {
+    const float q = p_apply(xcol);
+    const float s = pt_apply(rok ? q * d1i : 0.0f);
+    const float y = d2 * xcol - s;
+    return cok ? y : 0.0f;
   };
 
-  float x1 = 0.0f, res1 = b1, p1 = 0.0f, s1 = 0.0f;
-  float x2[MC], res2[MC], p2[MC], s2v[MC], u2[MC];
-#pragma unroll
-  for (int m = 0; m < MC; ++m) {
-    x2[m] = 0.0f;
-    res2[m] = b2[m];
-    p2[m] = s2v[m] = 0.0f;
-    u2[m] = d2[m] > 0.0f ? res2[m] / d2[m] : 0.0f;
-  }
-  float u1 = d1 > 0.0f ? res1 / d1 : 0.0f;
-  float ru, wu, rr;
-  matvec(u1, u2, res1, res2, ru, wu, rr);
+  // Chronopoulos-Gear CG (one fused CTA reduction of (r,u), (w,u), (r,r) per
+  // iteration); every CTA holds all columns, so these dots need no exchange
+  // and are bit-identical across the cluster (uniform control flow).
+  const float bs = pt_apply(rok ? b1 * d1i : 0.0f);
+  float res2 = cok ? b2 - bs : 0.0f;
+  float x2 = 0.0f, p2 = 0.0f, s2v = 0.0f, u2 = res2 * d2i;
+  float w2 = schur(u2), ru, wu, rr;
+  cta_sum3(res2 * u2, w2 * u2, res2 * res2, misc + 64, ru, wu, rr);
   const float nrm0 = sqrtf(fmaxf(rr, 0.0f));
   const float tol = fmaxf(p.cg_atol, p.cg_rtol * nrm0);
-  float resn = nrm0;
+  const float tol2 = tol * tol;
   int iters = 0;
   bool conv = !(nrm0 > tol) || !(wu > 0.0f);
   float gam = ru, alpha = (wu > 0.0f) ? ru / wu : 0.0f, beta = 0.0f;
 #pragma unroll 1
   for (int it = 0; it < p.cg_max_iter && !conv; ++it) {
-    p1 = u1 + beta * p1;
-    s1 = w1 + beta * s1;
-    x1 += alpha * p1;
-    res1 -= alpha * s1;
-#pragma unroll
-    for (int m = 0; m < MC; ++m) {
-      p2[m] = u2[m] + beta * p2[m];
-      s2v[m] = w2[m] + beta * s2v[m];
-      x2[m] += alpha * p2[m];
-      res2[m] -= alpha * s2v[m];
-      u2[m] = d2[m] > 0.0f ? res2[m] / d2[m] : 0.0f;
-    }
-    u1 = d1 > 0.0f ? res1 / d1 : 0.0f;
-    matvec(u1, u2, res1, res2, ru, wu, rr);
+    p2 = u2 + beta * p2;
+    s2v = w2 + beta * s2v;
+    x2 += alpha * p2;
+    res2 -= alpha * s2v;
+    u2 = res2 * d2i;
+    w2 = schur(u2);
+    cta_sum3(res2 * u2, w2 * u2, res2 * res2, misc + 64, ru, wu, rr);
     iters = it + 1;
-    resn = sqrtf(fmaxf(rr, 0.0f));
-    if (resn <= tol) {
+    if (rr <= tol2) {
       conv = true;
       break;
     }
-    beta = ru / gam;
-    const float den = wu - beta * ru / alpha;
-    if (!(den > 0.0f) || !isfinite(den)) break;
-    alpha = ru / den;
+    // CG scalars: fast divisions (a few ulp) are ample here
+    beta = __fdividef(ru, gam);
+    const float den = wu - beta * __fdividef(ru, alpha);
+    if (!(den > 0.0f) | !(den < 3.0e38f)) break;
+    alpha = __fdividef(ru, den);
     gam = ru;
   }
+  const float resn = sqrtf(fmaxf(rr, 0.0f));
   if (!conv) err |= DFS_WARN_CG_NOT_CONVERGED;
   if (crank == 0 && tid == 0) {
     if (p.cg_iters) p.cg_iters[bh] = iters;
     if (p.cg_residual) p.cg_residual[bh] = resn;
   }
+  // back-substitution for the row block
+  float x1;
+  {
+    const float q = p_apply(x2);
+    x1 = rok ? d1i * (b1 - q) : 0.0f;
+  }
 
   // ---------------------------------------------------------------- phase 4
-  // all-gather w1; for kappa = 1 remove the null-space component so that
-  // sum(dlog_mu) = sum(dlog_nu) = 0
+  // all-gather w1, f, 1/rowsum, D of every row; for kappa = 1 remove the
+  // null-space component so that sum(dlog_mu) = sum(dlog_nu) = 0
   float tshift = 0.0f;
   {
-    const bool own = (lane & 7) == 0 && rok;
-    const float a = warp_sum(own ? rsum_r * x1 : 0.0f);
-    if (lane == 0) misc[160 + warp] = a;
-    __syncthreads();
-    if ((lane & 7) == 0) exb.put(kRpw * warp + rho, x1);
-    if (tid == 0) {
-      float t = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) t += misc[160 + w];
-      exb.put(64, t);
+    float* st = ex.stage();
+    if ((lane & 7) == 0) {
+      st[li_own] = rok ? x1 : 0.0f;
+      st[64 + li_own] = rowv[BR_F * 64 + li_own];
+      st[128 + li_own] = rowv[BR_INV * 64 + li_own];
+      st[192 + li_own] = rowv[BR_D * 64 + li_own];
     }
-    exb.sync();
-    for (int i = tid; i < NP; i += kThreads) colv[BC_W1 * NP + i] = exb.from(i >> 6)[i & 63];
+    const float a = rows_sum(rsum_r * x1);
+    if (lane == 0) misc[warp] = a;
+    __syncthreads();
+    if (tid == 0) st[256] = sum16(misc);
+    if (!ex.exchange(tid, 4u * 260)) err |= DFS_ERR_DEVICE_TIMEOUT;
+    if (colt) {
+      const float* src = ex.from(jc >> 6);
+      const int o = jc & 63;
+      colv[BC_W1 * NP + jc] = src[o];
+      colv[BC_FA * NP + jc] = src[64 + o];
+      colv[BC_INV * NP + jc] = src[128 + o];
+      colv[BC_DD * NP + jc] = src[192 + o];
+      colv[BC_SOL2 * NP + jc] = x2;
+    }
     float tot = 0.0f;
 #pragma unroll
-    for (int c = 0; c < C; ++c) tot += exb.from(c)[64];
-    exb.next();
+    for (int c = 0; c < C; ++c) tot += ex.from(c)[256];
+    ex.next();
     if (kap >= 1.0f) tshift = sum_r > 0.0f ? -tot / sum_r : 0.0f;
   }
   if (p.dlog_mu && (lane & 7) == 0 && grow < N) p.dlog_mu[bh * N + grow] = rok ? rsum_r * (x1 + tshift) : 0.0f;
-#pragma unroll
-  for (int m = 0; m < MC; ++m) {
-    const int j = tid + kThreads * m;
-    if (j < NP) colv[BC_SOL2 * NP + j] = x2[m];
-    if (p.dlog_nu && j >= row0 && j < row0 + 64 && j < N)
-      p.dlog_nu[bh * N + j] = okc[m] ? cc[m] * (x2[m] - tshift) : 0.0f;
-  }
+  if (p.dlog_nu && colt && jc >= row0 && jc < row0 + 64 && jc < N)
+    p.dlog_nu[bh * N + jc] = cok ? colv[BC_CC * NP + jc] * (x2 - tshift) : 0.0f;
   __syncthreads();
 
   // ---------------------------------------------------------------- phase 5 (dQ)
@@ -578,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
 #pragma unroll
       for (int r = 0; r < kRpw; ++r) {
         const uint32_t o = sw_off(kRpw * warp + r, j, 64) >> 2;
-        Ts[o] = Ts[o] - P[r][k] * (xa[r] + xs);
+        Ts[o] = fmaf(-P[r][k], xa[r] + xs, Ts[o]);
       }
     }
   }
@@ -602,12 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     mma_commit(mbar);
   }
   mma_wait();
-  __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, qk_scale, warp, lane);
   __syncthreads();
   if (bias_on) {
-    bias.transposed = true;
-    add_cost_bias_stage<NP>(Ts, bias, tid);
+    add_bias(true);
     __syncthreads();
   }
   stage_to_regs<NS>(P, Ts, warp, lane);
@@ -618,18 +569,18 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     for (int r = 0; r < kRpw; ++r) gj[r] = colv[BC_G * NP + row0 + kRpw * warp + r];
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
-      const int i = 32 * k + lane;
-      const float fi = colv[BC_FA * NP + i];
+      const float fi = colv[BC_FA * NP + 32 * k + lane];
 #pragma unroll
       for (int r = 0; r < kRpw; ++r) {
-        const bool ok = ((rokm >> r) & 1u) && ((cokm >> k) & 1u);
-        P[r][k] = ok ? ex2(P[r][k] + gj[r] + fi) : 0.0f;
+        const bool ok = ((rokm >> r) & (cokm >> k) & 1u) != 0u;
+        const float e = ex2(P[r][k] + gj[r] + fi);
+        P[r][k] = ok ? e : 0.0f;
       }
     }
   }
 
   // ---------------------------------------------------------------- phase 7 (dV)
-  __syncthreads();
+  __syncthreads();  // Ts (S^T) fully read
   load_operand<DH>(SA, p.V, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);   // V slab
   load_operand_f32<DH>(KV, p.dO, bh * N, 0, NP, N, tid, kThreads);              // dO (all rows)
   operands_ready();
@@ -660,31 +611,30 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   __syncthreads();
   drain_m64<NP>(Ts, tbase, 0, 1.0f, warp, lane);  // dT^T
   __syncthreads();
-  {
-    float xj[3][kRpw], sol2j[kRpw];
-#pragma unroll
-    for (int r = 0; r < kRpw; ++r) {
-      const int j = row0 + kRpw * warp + r;
-      sol2j[r] = colv[BC_SOL2 * NP + j];
-#pragma unroll
-      for (int c = 0; c < 3; ++c) xj[c][r] = colv[(BC_X0 + c) * NP + j];
+  if (p.dxc) {  // dT^T[j][i] += dxc_i . x_j
+#pragma unroll 1
+    for (int idx = tid; idx < 64 * NP; idx += kThreads) {
+      const int lj = idx / NP, gi = idx - lj * NP;
+      if (gi < N) {
+        const float* dx = p.dxc + (bh * N + gi) * 3;
+        Ts[sw_off(lj, gi, 64) >> 2] += dx[0] * rowv[BR_X0 * 64 + lj] + dx[1] * rowv[BR_X1 * 64 + lj] +
+                                       dx[2] * rowv[BR_X2 * 64 + lj];
+      }
     }
+    __syncthreads();
+  }
+  {
+    float sol2j[kRpw];
+#pragma unroll
+    for (int r = 0; r < kRpw; ++r) sol2j[r] = colv[BC_SOL2 * NP + row0 + kRpw * warp + r];
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const int i = 32 * k + lane;
       const float inv = colv[BC_INV * NP + i], Di = colv[BC_DD * NP + i], w1i = colv[BC_W1 * NP + i];
-      float dx0 = 0.0f, dx1 = 0.0f, dx2 = 0.0f;
-      if (p.dxc && i < N) {
-        dx0 = p.dxc[(bh * N + i) * 3 + 0];
-        dx1 = p.dxc[(bh * N + i) * 3 + 1];
-        dx2 = p.dxc[(bh * N + i) * 3 + 2];
-      }
 #pragma unroll
       for (int r = 0; r < kRpw; ++r) {
         const uint32_t o = sw_off(kRpw * warp + r, i, 64) >> 2;
-        float dt = Ts[o];
-        if (p.dxc) dt += dx0 * xj[0][r] + dx1 * xj[1][r] + dx2 * xj[2][r];
-        Ts[o] = P[r][k] * inv * (dt - Di) - P[r][k] * (w1i + sol2j[r]);
+        Ts[o] = P[r][k] * fmaf(inv, Ts[o] - Di, -(w1i + sol2j[r]));
       }
     }
   }

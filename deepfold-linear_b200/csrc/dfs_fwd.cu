@@ -336,31 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     }
     __syncthreads();
     if (tid == 0) mi[MI_FL + (set ^ 1)] = 0;  // the other parity, for the next iteration
-    // From here each thread tid < NP works on one column jc.  CTA partial: lane
-    // l of warp w takes quad q = 8w + (l & 7) (columns 4q..4q+3) and sums the
-    // 4 warp partials 4g..4g+3, g = l >> 3, so that each quarter-warp reads
-    // 128 contiguous bytes (no bank conflicts); a reduce-scatter over the 4
-    // lanes of the quad (xor 8, xor 16: 3 shuffles) leaves lane l with column
-    // jc = 4q + g, staged for the cluster exchange.
+    // From here each thread tid < NP works on one column jc (colsum16).
     const bool colt = tid < NP;  // warp-uniform (NP is a multiple of 64)
-    const int jc = 32 * warp + 4 * (lane & 7) + (lane >> 3);
+    const int jc = col_of_thread(warp, lane);
     float c_ok = 0.0f, c_bnu = 0.0f, c_bt = 0.0f, c_gab = 0.0f, c_gc = 0.0f;
     if (colt) {
-      const int qd = 8 * warp + (lane & 7), g4 = lane >> 3;
-      const float* rp = red + (4 * g4) * NP + 4 * qd;
-      float4 s4 = *reinterpret_cast<const float4*>(rp);
-#pragma unroll
-      for (int w = 1; w < 4; ++w) {
-        const float4 x = *reinterpret_cast<const float4*>(rp + w * NP);
-        s4 = make_float4(s4.x + x.x, s4.y + x.y, s4.z + x.z, s4.w + x.w);
-      }
-      const bool hi = (g4 & 2) != 0, odd = (g4 & 1) != 0;
-      const float k0 = hi ? s4.z : s4.x, k1 = hi ? s4.w : s4.y;   // columns 2h, 2h+1 kept
-      const float o0 = hi ? s4.x : s4.z, o1 = hi ? s4.y : s4.w;   // the other half, sent
-      const float a0 = k0 + __shfl_xor_sync(0xffffffffu, o0, 16);
-      const float a1 = k1 + __shfl_xor_sync(0xffffffffu, o1, 16);
-      const float kk = odd ? a1 : a0, oo = odd ? a0 : a1;
-      const float ctot = kk + __shfl_xor_sync(0xffffffffu, oo, 8);
+      const float ctot = colsum16<NP>(red, warp, lane);
       ex.stage()[jc] = ctot;
       // this column's constants, loaded before the exchange
       c_ok = colv[CV_OK * NP + jc];

@@ -36,6 +36,37 @@ DFS_DEV void drain_m64(float* Ts, uint32_t tbase, uint32_t col_base, float scale
   }
 }
 
+// Column owned by thread tid = 32 warp + lane (tid < NP) in the CTA column
+// reductions below: a permutation of 0..NP-1 inside each warp.
+DFS_DEV int col_of_thread(int warp, int lane) { return 32 * warp + 4 * (lane & 7) + (lane >> 3); }
+
+// CTA total of the per-warp column partials red[w * NP + j] (w < kWarps) for
+// column col_of_thread(warp, lane); call from the threads tid < NP only
+// (whole warps).  Lane l of warp w takes quad q = 8w + (l & 7) (columns
+// 4q..4q+3) and sums the warp partials 4g..4g+3, g = l >> 3, so that each
+// quarter-warp reads 128 contiguous bytes (no bank conflicts); a reduce-scatter
+// over the 4 lanes of the quad (xor 16, xor 8: 3 shuffles) leaves lane l with
+// column 4q + g.  Summation order is fixed: every CTA gets identical bits.
+template <int NP>
+DFS_DEV float colsum16(const float* red, int warp, int lane) {
+  static_assert(kWarps == 16, "four warp partials per lane of a quad");
+  const int qd = 8 * warp + (lane & 7), g4 = lane >> 3;
+  const float* rp = red + (4 * g4) * NP + 4 * qd;
+  float4 s4 = *reinterpret_cast<const float4*>(rp);
+#pragma unroll
+  for (int w = 1; w < 4; ++w) {
+    const float4 x = *reinterpret_cast<const float4*>(rp + w * NP);
+    s4 = make_float4(s4.x + x.x, s4.y + x.y, s4.z + x.z, s4.w + x.w);
+  }
+  const bool hi = (g4 & 2) != 0, odd = (g4 & 1) != 0;
+  const float k0 = hi ? s4.z : s4.x, k1 = hi ? s4.w : s4.y;  // columns 2h, 2h+1 kept
+  const float o0 = hi ? s4.x : s4.z, o1 = hi ? s4.y : s4.w;  // the other half, sent
+  const float a0 = k0 + __shfl_xor_sync(0xffffffffu, o0, 16);
+  const float a1 = k1 + __shfl_xor_sync(0xffffffffu, o1, 16);
+  const float kk = odd ? a1 : a0, oo = odd ? a0 : a1;
+  return kk + __shfl_xor_sync(0xffffffffu, oo, 8);
+}
+
 template <int NS>
 DFS_DEV void stage_to_regs(float (&E)[kRpw][NS], const float* Ts, int warp, int lane) {
 #pragma unroll
