@@ -146,6 +146,13 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   };
 
   // ---------------------------------------------------------------- setup
+  if (tid == 0) {  // this CTA's slab of every operand into L2
+    const int es = p.in_dtype == DFS_F32 ? 4 : 2;
+    prefetch_slab_l2(p.Q, bh * N, row0, N, DH, es);
+    prefetch_slab_l2(p.K, bh * N, row0, N, DH, es);
+    prefetch_slab_l2(p.V, bh * N, row0, N, DH, es);
+    prefetch_slab_l2(p.dO, bh * N, row0, N, DH, 4);
+  }
   if (warp == 0) tmem_alloc(tslot, 512);
   if (tid == 0) {
     mbar_init(mbar, 1);
@@ -170,9 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       rowv[(BR_X0 + c) * 64 + tid] =
           (p.x_res && gi < N) ? p.x_res[(static_cast<size_t>(bb) * N + gi) * 3 + c] : 0.0f;
   }
-  load_operand<DH>(SA, p.Q, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);
-  load_operand<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
-  load_operand_f32<DH>(DA, p.dO, bh * N, row0, 64, N, tid, kThreads);
+  load_operand<DH, 64>(SA, p.Q, p.in_dtype, bh * N, row0, N, tid);
+  load_operand<DH, NP>(KV, p.K, p.in_dtype, bh * N, 0, N, tid);
+  load_operand_f32<DH, 64>(DA, p.dO, bh * N, row0, N, tid);
   operands_ready();
   if constexpr (C > 1) cluster_sync();  // every CTA's exchange mbarriers initialised
   const uint32_t tbase = *tslot;
@@ -265,10 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
 
   // ---------------------------------------------------------------- phase 2
   __syncthreads();  // Ts (S) fully read
-  load_operand<DH>(KV, p.V, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
+  load_operand<DH, NP>(KV, p.V, p.in_dtype, bh * N, 0, N, tid);
   operands_ready();
   if (tid == 0) {
-    issue_abt<NP, DH>(tbase, DA, KV, NP);  // dT = dO_s V^T
+    issue_abt<NP, DH>(tbase, DA, KV);  // dT = dO_s V^T
     mma_commit(mbar);
   }
   mma_wait();
@@ -535,20 +542,20 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       }
     }
   }
-  load_operand_t<DH>(KV, p.K, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);  // K^T (DH x NP)
+  load_operand_t<DH, NP>(KV, p.K, p.in_dtype, bh * N, 0, N, tid);  // K^T (DH x NP)
   operands_ready();
   if (tid == 0) {
-    issue_abt<DH, NP>(tbase, Ts, KV, DH);  // dQ = dS K
+    issue_abt_split<DH, NP, kGradAcc>(tbase, Ts, KV);  // dQ = dS K
     mma_commit(mbar);
   }
   mma_wait();
-  if (p.dQ) drain_rows_to_global<DH>(tbase, 0, p.dQ, bh * N, row0, N, grad_scale, warp, lane);
+  if (p.dQ) drain_rows_to_global<DH, kGradAcc>(tbase, 0, p.dQ, bh * N, row0, N, grad_scale, warp, lane);
 
   // ---------------------------------------------------------------- phase 6
   tc_fence_before();
   __syncthreads();
-  load_operand<DH>(SA, p.K, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);  // K slab
-  load_operand<DH>(KV, p.Q, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);     // Q (all rows)
+  load_operand<DH, 64>(SA, p.K, p.in_dtype, bh * N, row0, N, tid);  // K slab
+  load_operand<DH, NP>(KV, p.Q, p.in_dtype, bh * N, 0, N, tid);     // Q (all rows)
   operands_ready();
   if (tid == 0) {
     issue_qk<NP, DH>(tbase, SA, KV);  // S^T for the column slab
@@ -581,11 +588,11 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
 
   // ---------------------------------------------------------------- phase 7 (dV)
   __syncthreads();  // Ts (S^T) fully read
-  load_operand<DH>(SA, p.V, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);   // V slab
-  load_operand_f32<DH>(KV, p.dO, bh * N, 0, NP, N, tid, kThreads);              // dO (all rows)
+  load_operand<DH, 64>(SA, p.V, p.in_dtype, bh * N, row0, N, tid);   // V slab
+  load_operand_f32<DH, NP>(KV, p.dO, bh * N, 0, N, tid);              // dO (all rows)
   operands_ready();
   if (tid == 0) {
-    issue_abt<NP, DH>(tbase, SA, KV, NP);  // dT^T = V_s dO^T
+    issue_abt<NP, DH>(tbase, SA, KV);  // dT^T = V_s dO^T
     mma_commit(mbar);
   }
 #pragma unroll
@@ -597,14 +604,14 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   }
   mma_wait();
   __syncthreads();
-  load_operand_f32_t<DH>(KV, p.dO, bh * N, 0, NP, N, tid, kThreads);            // dO^T (DH x NP)
+  load_operand_f32_t<DH, NP>(KV, p.dO, bh * N, 0, N, tid);            // dO^T (DH x NP)
   operands_ready();
   if (tid == 0) {
-    issue_abt<DH, NP>(tbase + NP, Ts, KV, DH);  // dV = T_norm^T dO
+    issue_abt_split<DH, NP, kGradAcc>(tbase + NP, Ts, KV);  // dV = T_norm^T dO
     mma_commit(mbar);
   }
   mma_wait();
-  if (p.dV) drain_rows_to_global<DH>(tbase, NP, p.dV, bh * N, row0, N, 1.0f, warp, lane);
+  if (p.dV) drain_rows_to_global<DH, kGradAcc>(tbase, NP, p.dV, bh * N, row0, N, 1.0f, warp, lane);
 
   // ---------------------------------------------------------------- phase 8 (dK)
   tc_fence_before();
@@ -638,14 +645,14 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       }
     }
   }
-  load_operand_t<DH>(KV, p.Q, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);  // Q^T (DH x NP)
+  load_operand_t<DH, NP>(KV, p.Q, p.in_dtype, bh * N, 0, N, tid);  // Q^T (DH x NP)
   operands_ready();
   if (tid == 0) {
-    issue_abt<DH, NP>(tbase, Ts, KV, DH);  // dK = dS^T Q
+    issue_abt_split<DH, NP, kGradAcc>(tbase, Ts, KV);  // dK = dS^T Q
     mma_commit(mbar);
   }
   mma_wait();
-  if (p.dK) drain_rows_to_global<DH>(tbase, 0, p.dK, bh * N, row0, N, grad_scale, warp, lane);
+  if (p.dK) drain_rows_to_global<DH, kGradAcc>(tbase, 0, p.dK, bh * N, row0, N, grad_scale, warp, lane);
 
   // ---------------------------------------------------------------- teardown
   if (err && p.status) atomicOr(p.status, err);

@@ -95,6 +95,12 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
   int err = 0;
 
   // ---------------------------------------------------------------- setup
+  if (tid == 0 && p.cost_mode == DFS_COST_QK) {  // this CTA's slab of every operand into L2
+    const int es = p.in_dtype == DFS_F32 ? 4 : 2;
+    prefetch_slab_l2(p.Q, bh * N, row0, N, DH, es);
+    prefetch_slab_l2(p.K, bh * N, row0, N, DH, es);
+    if (p.V) prefetch_slab_l2(p.V, bh * N, row0, N, DH, es);
+  }
   if (warp == 0) tmem_alloc(tslot, 512);
   if (tid == 0) {
     mbar_init(mbar, 1);
@@ -120,8 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
       rowv[(RV_X0 + c) * 64 + tid] = gi < N ? p.x_res[(static_cast<size_t>(bb) * N + gi) * 3 + c] : 0.0f;
   }
   if (p.cost_mode == DFS_COST_QK) {
-    load_operand<DH>(Qs, p.Q, p.in_dtype, bh * N, row0, 64, N, tid, kThreads);
-    load_operand<DH>(KVs, p.K, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
+    load_operand<DH, 64>(Qs, p.Q, p.in_dtype, bh * N, row0, N, tid);
+    load_operand<DH, NP>(KVs, p.K, p.in_dtype, bh * N, 0, N, tid);
     fence_async_smem();
   }
   tc_fence_before();
@@ -142,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     __syncthreads();
   }
   // K is no longer needed (S stays in TMEM): V^T goes over it for the output MMA.
-  if (p.O != nullptr) load_operand_t<DH>(KVs, p.V, p.in_dtype, bh * N, 0, NP, N, tid, kThreads);
+  if (p.O != nullptr) load_operand_t<DH, NP>(KVs, p.V, p.in_dtype, bh * N, 0, N, tid);
 
   // ---------------------------------------------------------------- registers
   float E[kRpw][NS];
@@ -492,13 +498,13 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     }
     if (p.O != nullptr) {
       if (tid == 0) {
-        issue_abt<DH, NP>(tbase + NP, Ts, KVs, DH);  // O = T_norm (V^T)^T
+        issue_abt_split<DH, NP, kGradAcc>(tbase + NP, Ts, KVs);  // O = T_norm (V^T)^T
         mma_commit(mbar);
       }
       if (!mbar_wait(mbar, mma_phase & 1)) err |= DFS_ERR_DEVICE_TIMEOUT;
       ++mma_phase;
       tc_fence_after();
-      drain_rows_to_global<DH>(tbase, NP, p.O, bh * N, row0, N, 1.0f, warp, lane);
+      drain_rows_to_global<DH, kGradAcc>(tbase, NP, p.O, bh * N, row0, N, 1.0f, warp, lane);
     }
   }
   if (row_owner && grow < N) p.log_u[bh * N + grow] = rok ? fr * kLn2 : 0.0f;

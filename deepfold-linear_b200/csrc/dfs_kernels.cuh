@@ -10,6 +10,8 @@ namespace dfs {
 constexpr int kThreads = 512;
 constexpr int kWarps = 16;
 constexpr int kRpw = 4;
+// Independent TMEM accumulators for the narrow (d-column) MMAs with K = N.
+constexpr int kGradAcc = 1;
 
 // Potential drift (log2 units) since the last absorption beyond which the
 // stabilised kernel matrix is rebuilt: row/column sums then stay above 2^-60.

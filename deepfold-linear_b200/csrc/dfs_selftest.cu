@@ -37,11 +37,11 @@ __global__ void __launch_bounds__(128, 1)
   if (tid == 0) {
     // N and K are runtime values here: dispatch to the compile-time shapes the
     // kernels use
-    if (N == 32 && K == 384) issue_abt<32, 384>(tbase, As, Bs, N);
-    else if (N == 192 && K == 32) issue_abt<192, 32>(tbase, As, Bs, N);
-    else if (N == 256 && K == 64) issue_abt<256, 64>(tbase, As, Bs, N);
-    else if (N == 384 && K == 32) issue_abt<384, 32>(tbase, As, Bs, N);
-    else if (N == 64 && K == 128) issue_abt<64, 128>(tbase, As, Bs, N);
+    if (N == 32 && K == 384) issue_abt<32, 384>(tbase, As, Bs);
+    else if (N == 192 && K == 32) issue_abt<192, 32>(tbase, As, Bs);
+    else if (N == 256 && K == 64) issue_abt<256, 64>(tbase, As, Bs);
+    else if (N == 384 && K == 32) issue_abt<384, 32>(tbase, As, Bs);
+    else if (N == 64 && K == 128) issue_abt<64, 128>(tbase, As, Bs);
     else err = 2;
     mma_commit(&mbar);
   }

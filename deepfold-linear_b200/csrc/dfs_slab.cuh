@@ -163,93 +163,137 @@ DFS_DEV void widen(const uint4& raw, float (&v)[4], float*) {
   v[3] = __uint_as_float(raw.w);
 }
 
-// Rows [row_first, row_first+rows) of a row-major (., DH) tensor of T (rows at
+// Rows [row_first, row_first+ROWS) of a row-major (., DH) tensor of T (rows at
 // or beyond N read as zero) into a 128B-swizzled fp32 operand buffer: with
-// TR = false element (i, c) lands at (i, c) of a buffer with `rows` rows, with
+// TR = false element (i, c) lands at (i, c) of a buffer with ROWS rows, with
 // TR = true at (c, i) of a buffer with DH rows (the K-major operand holding the
-// transpose).  Each thread moves 16-byte chunks and issues a batch of loads
-// before consuming any, so the global-memory latency is paid once per batch.
-template <int DH, bool TR, typename T>
-DFS_DEV void load_tile(float* dst, const T* src, int row_first, int rows, int N, int tid) {
+// transpose).  Each thread moves 16-byte chunks and issues all of its loads
+// before consuming any, so the tile costs one global-memory round trip.
+template <int DH, int ROWS, bool TR, typename T>
+DFS_DEV void load_tile(float* dst, const T* src, int row_first, int N, int tid) {
   constexpr int EPC = Chunk16<T>::kElems;   // elements per chunk
   constexpr int CPR = DH / EPC;             // chunks per row
-  constexpr int BATCH = 2;
-  const int total = rows * CPR;
-  for (int base = 0; base < total; base += kThreads * BATCH) {
-    uint4 raw[BATCH];
+  constexpr int TOTAL = ROWS * CPR;
+  constexpr int BATCH = (TOTAL + kThreads - 1) / kThreads;
+  uint4 raw[BATCH];
+  // chunk c -> (row i, chunk-in-row ch): row-major order for the plain tile
+  // (coalesced reads, 16-byte stores); column-major order for the transposed
+  // one, so that the 32 lanes of a warp store 32 consecutive columns of one
+  // output row (conflict-free)
+  auto row_of = [](int c) { return TR ? c % ROWS : c / CPR; };
+  auto chunk_of = [](int c) { return TR ? c / ROWS : c % CPR; };
 #pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      const int c = base + tid + kThreads * b;
-      const int gi = row_first + c / CPR;
-      raw[b] = make_uint4(0u, 0u, 0u, 0u);
-      if (c < total && gi < N)
-        raw[b] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(gi) * DH) + (c % CPR));
-    }
+  for (int b = 0; b < BATCH; ++b) {
+    const int c = tid + kThreads * b;
+    const int gi = row_first + row_of(c);
+    raw[b] = make_uint4(0u, 0u, 0u, 0u);
+    if ((TOTAL % kThreads == 0 || c < TOTAL) && gi < N)
+      raw[b] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(gi) * DH) + chunk_of(c));
+  }
 #pragma unroll
-    for (int b = 0; b < BATCH; ++b) {
-      const int c = base + tid + kThreads * b;
-      if (c >= total) break;
-      const int i = c / CPR, c0 = (c % CPR) * EPC;
-      float v[EPC];
-      widen(raw[b], v, static_cast<T*>(nullptr));
-      if (!TR) {
+  for (int b = 0; b < BATCH; ++b) {
+    const int c = tid + kThreads * b;
+    if (TOTAL % kThreads != 0 && c >= TOTAL) break;
+    const int i = row_of(c), c0 = chunk_of(c) * EPC;
+    float v[EPC];
+    widen(raw[b], v, static_cast<T*>(nullptr));
+    if (!TR) {
 #pragma unroll
-        for (int q = 0; q < EPC / 4; ++q)
-          *reinterpret_cast<float4*>(dst + (sw_off(i, c0 + 4 * q, rows) >> 2)) =
-              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      } else {
+      for (int q = 0; q < EPC / 4; ++q)
+        *reinterpret_cast<float4*>(dst + (sw_off(i, c0 + 4 * q, ROWS) >> 2)) =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
 #pragma unroll
-        for (int q = 0; q < EPC; ++q) dst[sw_off(c0 + q, i, DH) >> 2] = v[q];
-      }
+      for (int q = 0; q < EPC; ++q) dst[sw_off(c0 + q, i, DH) >> 2] = v[q];
     }
   }
 }
 
-template <int DH, bool TR>
-DFS_DEV void load_tile_any(float* dst, const void* src, int dtype, size_t base_row, int row_first, int rows,
-                           int N, int tid) {
+template <int DH, int ROWS, bool TR>
+DFS_DEV void load_tile_any(float* dst, const void* src, int dtype, size_t base_row, int row_first, int N,
+                           int tid) {
   if (dtype == DFS_BF16)
-    load_tile<DH, TR>(dst, reinterpret_cast<const __nv_bfloat16*>(src) + base_row * DH, row_first, rows, N, tid);
+    load_tile<DH, ROWS, TR>(dst, reinterpret_cast<const __nv_bfloat16*>(src) + base_row * DH, row_first, N, tid);
   else if (dtype == DFS_F16)
-    load_tile<DH, TR>(dst, reinterpret_cast<const __half*>(src) + base_row * DH, row_first, rows, N, tid);
+    load_tile<DH, ROWS, TR>(dst, reinterpret_cast<const __half*>(src) + base_row * DH, row_first, N, tid);
   else
-    load_tile<DH, TR>(dst, reinterpret_cast<const float*>(src) + base_row * DH, row_first, rows, N, tid);
+    load_tile<DH, ROWS, TR>(dst, reinterpret_cast<const float*>(src) + base_row * DH, row_first, N, tid);
 }
 
-// Load rows [row_first, row_first+rows) of a (., DH) tensor into a 128B-swizzled
-// fp32 operand buffer with `rows` rows (rows beyond N are zero).
-template <int DH>
-DFS_DEV void load_operand(float* dst, const void* src, int dtype, size_t base_row, int row_first, int rows,
-                          int N, int tid, int /*nthreads*/) {
-  load_tile_any<DH, false>(dst, src, dtype, base_row, row_first, rows, N, tid);
+// Load rows [row_first, row_first+ROWS) of a (., DH) tensor into a
+// 128B-swizzled fp32 operand buffer with ROWS rows (rows beyond N are zero).
+template <int DH, int ROWS>
+DFS_DEV void load_operand(float* dst, const void* src, int dtype, size_t base_row, int row_first, int N, int tid) {
+  load_tile_any<DH, ROWS, false>(dst, src, dtype, base_row, row_first, N, tid);
 }
 
 // Transposed load: element (row gi, c) of a (., DH) tensor goes to (row c,
-// column gi - row_first) of a 128B-swizzled buffer with DH rows and `cols`
+// column gi - row_first) of a 128B-swizzled buffer with DH rows and ROWS
 // columns, i.e. the K-major operand holding the tensor's transpose.
-template <int DH>
-DFS_DEV void load_operand_t(float* dst, const void* src, int dtype, size_t base_row, int row_first, int cols,
-                            int N, int tid, int /*nthreads*/) {
-  load_tile_any<DH, true>(dst, src, dtype, base_row, row_first, cols, N, tid);
+template <int DH, int ROWS>
+DFS_DEV void load_operand_t(float* dst, const void* src, int dtype, size_t base_row, int row_first, int N,
+                            int tid) {
+  load_tile_any<DH, ROWS, true>(dst, src, dtype, base_row, row_first, N, tid);
+}
+
+// fp32 variants for already-fp32 tensors (upstream gradients).
+template <int DH, int ROWS>
+DFS_DEV void load_operand_f32(float* dst, const float* src, size_t base_row, int row_first, int N, int tid) {
+  load_tile<DH, ROWS, false>(dst, src + base_row * DH, row_first, N, tid);
+}
+template <int DH, int ROWS>
+DFS_DEV void load_operand_f32_t(float* dst, const float* src, size_t base_row, int row_first, int N, int tid) {
+  load_tile<DH, ROWS, true>(dst, src + base_row * DH, row_first, N, tid);
+}
+
+// Bulk prefetch into L2 of rows [row0, min(row0+64, N)) of a row-major
+// (., DH) tensor with `esize`-byte elements (one instruction per tensor; the
+// caller guarantees 16-byte alignment, which DH * esize a multiple of 16 keeps).
+DFS_DEV void prefetch_slab_l2(const void* base, size_t base_row, int row0, int N, int DH, int esize) {
+  const int rows = min(64, N - row0);
+  if (rows <= 0) return;
+  const char* p = reinterpret_cast<const char*>(base) + (base_row + row0) * static_cast<size_t>(DH) * esize;
+  const uint32_t bytes = static_cast<uint32_t>(rows) * DH * esize;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // Issue D (TMEM, M=64 rows x NN columns) = A (64 x KD, K-major) * B (NN x KD,
-// K-major)^T, both 128B-swizzled fp32 buffers read as tf32 (one elected thread).
-// rows_b is the row count B was stored with (its atom column stride).
+// K-major)^T, both 128B-swizzled fp32 buffers read as tf32, B stored with NN
+// rows (one elected thread).  The descriptors are built once; each K step
+// advances their start-address field (bits 0-13, 16-byte units, no carry for
+// shared-memory addresses) by a compile-time offset, so issuing costs a few
+// instructions per MMA.
 template <int NN, int KD>
-DFS_DEV void issue_abt(uint32_t d_tmem, const float* A, const float* Bm, int rows_b) {
+DFS_DEV void issue_abt(uint32_t d_tmem, const float* A, const float* Bm) {
   constexpr int NH = NN > 256 ? 2 : 1;
   constexpr int NCH = NN / NH;
-  const uint32_t aa = smem_u32(A), ba = smem_u32(Bm);
+  constexpr uint32_t idesc = idesc_tf32(64, NCH, 0, 0);
+  const uint64_t a0 = sw128_desc(smem_u32(A), 16, 1024), b0 = sw128_desc(smem_u32(Bm), 16, 1024);
 #pragma unroll
   for (int h2 = 0; h2 < NH; ++h2) {
-#pragma unroll 4
+#pragma unroll
     for (int kk = 0; kk < KD / 8; ++kk) {
-      const uint64_t ad = sw128_desc(aa + (kk >> 2) * 8192u + (kk & 3) * 32u, 16, 1024);
-      const uint64_t bd = sw128_desc(ba + (kk >> 2) * (static_cast<uint32_t>(rows_b) * 128u) +
-                                         (h2 * NCH / 8) * 1024u + (kk & 3) * 32u, 16, 1024);
-      mma_tf32(d_tmem + h2 * NCH, ad, bd, idesc_tf32(64, NCH, 0, 0), kk > 0 ? 1u : 0u);
+      const uint64_t ao = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+      const uint64_t bo = static_cast<uint64_t>(((kk >> 2) * NN * 128 + (h2 * NCH / 8) * 1024 + (kk & 3) * 32) >> 4);
+      mma_tf32(d_tmem + h2 * NCH, a0 + ao, b0 + bo, idesc, kk > 0 ? 1u : 0u);
     }
+  }
+}
+
+// As issue_abt for a narrow result (NN <= 256) with a long K: the K steps are
+// dealt round-robin to NACC independent accumulators at TMEM columns
+// d_tmem + a * NN (a < NACC), so consecutive MMAs do not wait on each other's
+// accumulation; the reader sums the NACC partials.
+template <int NN, int KD, int NACC>
+DFS_DEV void issue_abt_split(uint32_t d_tmem, const float* A, const float* Bm) {
+  static_assert(NN <= 256 && (KD / 8) % NACC == 0, "narrow result, K steps divisible by NACC");
+  constexpr uint32_t idesc = idesc_tf32(64, NN, 0, 0);
+  const uint64_t a0 = sw128_desc(smem_u32(A), 16, 1024), b0 = sw128_desc(smem_u32(Bm), 16, 1024);
+#pragma unroll
+  for (int kk = 0; kk < KD / 8; ++kk) {
+    const uint64_t ao = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+    const uint64_t bo = static_cast<uint64_t>(((kk >> 2) * NN * 128 + (kk & 3) * 32) >> 4);
+    mma_tf32(d_tmem + (kk % NACC) * NN, a0 + ao, b0 + bo, idesc, kk >= NACC ? 1u : 0u);
   }
 }
 
@@ -257,41 +301,38 @@ DFS_DEV void issue_abt(uint32_t d_tmem, const float* A, const float* Bm, int row
 // K-major), B = K (NP x DH, K-major), D = TMEM columns [0, NP).
 template <int NP, int DH>
 DFS_DEV void issue_qk(uint32_t tbase, const float* Qs, const float* Ks) {
-  issue_abt<NP, DH>(tbase, Qs, Ks, NP);
+  issue_abt<NP, DH>(tbase, Qs, Ks);
 }
 
-// Drain an M=64 accumulator of DH columns (TMEM columns [col, col+DH)) to a
-// row-major global (rows, DH) tensor, rows row0.. (< N), scaled.
-template <int DH>
+// Drain an M=64 result of DH columns held as NACC partial accumulators (TMEM
+// columns [col + a*DH, col + (a+1)*DH), see issue_abt_split) to a row-major
+// global (rows, DH) tensor, rows row0.. (< N), scaled.  Warps 0-3 (one per
+// TMEM lane quarter) read 16 columns at a time.
+template <int DH, int NACC>
 DFS_DEV void drain_rows_to_global(uint32_t tbase, uint32_t col, float* out, size_t row_base, int row0, int N,
                                   float scale, int warp, int lane) {
   if (warp >= 4) return;
+  const uint32_t lanes = static_cast<uint32_t>(32 * warp) << 16;
+  const int gi = row0 + 16 * warp + lane;
 #pragma unroll
-  for (int a = 0; a < DH / 32; ++a) {
-    float v[32];
-    tmem_ld32(tbase + (static_cast<uint32_t>(32 * warp) << 16) + col + 32 * a, v);
-    const int gi = row0 + 16 * warp + lane;
+  for (int g = 0; g < DH / 16; ++g) {
+    float v[16];
+    tmem_ld16(tbase + lanes + col + 16 * g, v);
+#pragma unroll
+    for (int a = 1; a < NACC; ++a) {
+      float t[16];
+      tmem_ld16(tbase + lanes + col + a * DH + 16 * g, t);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += t[i];
+    }
     if (lane < 16 && gi < N) {
-      float4* dst = reinterpret_cast<float4*>(out + (row_base + gi) * DH + 32 * a);
+      float4* dst = reinterpret_cast<float4*>(out + (row_base + gi) * DH + 16 * g);
 #pragma unroll
-      for (int c4 = 0; c4 < 8; ++c4)
+      for (int c4 = 0; c4 < 4; ++c4)
         dst[c4] = make_float4(v[4 * c4] * scale, v[4 * c4 + 1] * scale, v[4 * c4 + 2] * scale,
                               v[4 * c4 + 3] * scale);
     }
   }
-}
-
-// fp32 variant for already-fp32 tensors (upstream gradients).
-template <int DH>
-DFS_DEV void load_operand_f32(float* dst, const float* src, size_t base_row, int row_first, int rows, int N,
-                              int tid, int nthreads) {
-  load_operand<DH>(dst, src, DFS_F32, base_row, row_first, rows, N, tid, nthreads);
-}
-
-template <int DH>
-DFS_DEV void load_operand_f32_t(float* dst, const float* src, size_t base_row, int row_first, int cols, int N,
-                                int tid, int nthreads) {
-  load_operand_t<DH>(dst, src, DFS_F32, base_row, row_first, cols, N, tid, nthreads);
 }
 
 }  // namespace dfs

@@ -1,0 +1,243 @@
+// dfs_torch.cpp -- native autograd glue between PyTorch and libdfsink.
+//
+// FlashSinkhornFn is the autograd function behind deepfold's flash_sinkhorn
+// (reference: FlashSinkhornFunction, src/deepfold/model/kernels/
+// sinkhorn_kernel.py:1923-2382).  Its forward and backward validate shapes,
+// allocate outputs with the caching allocator and call dfs_fwd / dfs_bwd of the
+// C ABI on the current stream; nothing here computes.  Doing this in C++
+// rather than Python keeps the per-call host cost to a few allocations, so the
+// GPU, not the interpreter, bounds a training step.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include <string>
+#include <vector>
+
+#include "dfsink.h"
+
+namespace {
+
+using at::Tensor;
+using torch::autograd::AutogradContext;
+using torch::autograd::variable_list;
+
+void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == DFS_OK, what, " failed: ", dfs_status_string(rc), " (code ", rc, ")");
+}
+
+int dtype_code(at::ScalarType t) {
+  if (t == at::kBFloat16) return DFS_BF16;
+  if (t == at::kHalf) return DFS_F16;
+  return DFS_F32;
+}
+
+Tensor f32(const c10::optional<Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return Tensor();
+  return t->contiguous().to(at::kFloat);
+}
+
+template <typename T>
+T* ptr_or_null(const Tensor& t) {
+  return t.defined() ? static_cast<T*>(t.data_ptr()) : nullptr;
+}
+
+// Most recent backward's per-problem CG report (device tensors).
+std::vector<Tensor>& last_report() {
+  static std::vector<Tensor> r;
+  return r;
+}
+
+struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
+  // Arguments (positions in the gradient list backward returns): 0 Q, 1 K, 2 V,
+  // 3 x_res, 4 pos_weight, 5 pos_bins, 6 eps, 7 w_dist, 8 log_mu, 9 log_nu,
+  // 10 log_u_init, 11 log_v_init, 12 mask, 13 K_iter, 14 lam, 15 r_0, 16 cg_rtol,
+  // 17 cg_atol, 18 cg_max_iter.  needs_input_grad counts only the tensors that
+  // were passed (absent optionals are no autograd edge), so the forward records
+  // each argument's edge index.
+  static variable_list forward(AutogradContext* ctx, Tensor Q, Tensor K, Tensor V, c10::optional<Tensor> x_res,
+                               c10::optional<Tensor> pos_weight, c10::optional<Tensor> pos_bins, Tensor eps,
+                               c10::optional<Tensor> w_dist, Tensor log_mu, Tensor log_nu,
+                               c10::optional<Tensor> log_u_init, c10::optional<Tensor> log_v_init,
+                               c10::optional<Tensor> mask, int64_t K_iter, double lam, double r_0,
+                               double cg_rtol, double cg_atol, int64_t cg_max_iter) {
+    TORCH_CHECK(Q.is_cuda() && K.is_cuda() && V.is_cuda(),
+                "deepfold B200 Sinkhorn ops run on CUDA tensors only (no CPU path)");
+    TORCH_CHECK(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(),
+                "Q, K, V must share the shape (B, H, N, d)");
+    const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
+    TORCH_CHECK(N <= dfs_max_n(static_cast<int>(d)), "N=", N, ", d=", d,
+                " is outside the resident kernels' range (N <= ", dfs_max_n(static_cast<int>(d)), ")");
+    const auto st = Q.scalar_type();
+    const auto cdt = (st == at::kBFloat16 || st == at::kHalf || st == at::kFloat) ? st : at::kFloat;
+    const Tensor Qc = Q.contiguous().to(cdt), Kc = K.contiguous().to(cdt), Vc = V.contiguous().to(cdt);
+    const Tensor xr = f32(x_res), pw = f32(pos_weight);
+    Tensor pb;
+    if (pw.defined() && pos_bins.has_value() && pos_bins->defined()) pb = pos_bins->contiguous().to(at::kInt);
+    const Tensor epsc = eps.contiguous().to(at::kFloat), wd = f32(w_dist);
+    const Tensor lmu = log_mu.contiguous().to(at::kFloat), lnu = log_nu.contiguous().to(at::kFloat);
+    const Tensor lui = f32(log_u_init), lvi = f32(log_v_init), mk = f32(mask);
+    const auto fo = Q.options().dtype(at::kFloat);
+    Tensor O = at::empty({B, H, N, d}, fo);
+    Tensor xc = xr.defined() ? at::empty({B, H, N, 3}, fo) : Tensor();
+    Tensor lu = at::empty({B, H, N}, fo), lv = at::empty({B, H, N}, fo);
+    Tensor status = at::zeros({1}, Q.options().dtype(at::kInt));
+
+    dfs_problem prob{};
+    prob.B = static_cast<int32_t>(B);
+    prob.H = static_cast<int32_t>(H);
+    prob.N = static_cast<int32_t>(N);
+    prob.d = static_cast<int32_t>(d);
+    prob.in_dtype = dtype_code(cdt);
+    prob.cost_mode = DFS_COST_QK;
+    prob.K_iter = static_cast<int32_t>(K_iter);
+    prob.check_every = 2;
+    prob.lam = static_cast<float>(lam);
+    prob.r_0 = static_cast<float>(r_0);
+    dfs_fwd_args a{};
+    a.Q = Qc.data_ptr();
+    a.K = Kc.data_ptr();
+    a.V = Vc.data_ptr();
+    a.x_res = ptr_or_null<const float>(xr);
+    a.pos_weight = ptr_or_null<const float>(pw);
+    a.pos_bins = ptr_or_null<const int32_t>(pb);
+    a.eps = epsc.data_ptr<float>();
+    a.w_dist = ptr_or_null<const float>(wd);
+    a.log_mu = lmu.data_ptr<float>();
+    a.log_nu = lnu.data_ptr<float>();
+    a.log_u_init = ptr_or_null<const float>(lui);
+    a.log_v_init = ptr_or_null<const float>(lvi);
+    a.mask = ptr_or_null<const float>(mk);
+    a.O = O.data_ptr<float>();
+    a.x_centroid = ptr_or_null<float>(xc);
+    a.log_u = lu.data_ptr<float>();
+    a.log_v = lv.data_ptr<float>();
+    a.status = status.data_ptr<int32_t>();
+    const cudaStream_t stream = at::cuda::getCurrentCUDAStream(Q.device().index()).stream();
+    check_rc(dfs_fwd(&prob, &a, nullptr, 0, stream), "dfs_fwd");
+
+    ctx->save_for_backward({Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv});
+    ctx->saved_data["K_iter"] = K_iter;
+    ctx->saved_data["lam"] = lam;
+    ctx->saved_data["r_0"] = r_0;
+    ctx->saved_data["cg_rtol"] = cg_rtol;
+    ctx->saved_data["cg_atol"] = cg_atol;
+    ctx->saved_data["cg_max_iter"] = cg_max_iter;
+    ctx->saved_data["fwd_status"] = status;
+    ctx->saved_data["in_dtype"] = static_cast<int64_t>(Q.scalar_type());
+    int64_t edge = 3;  // Q, K, V are edges 0..2
+    auto next_edge = [&](bool present) -> int64_t { return present ? edge++ : -1; };
+    ctx->saved_data["e_x"] = next_edge(x_res.has_value());
+    ctx->saved_data["e_pw"] = next_edge(pos_weight.has_value());
+    next_edge(pos_bins.has_value());
+    next_edge(true);  // eps
+    ctx->saved_data["e_wd"] = next_edge(w_dist.has_value());
+    ctx->saved_data["e_mu"] = next_edge(true);
+    ctx->saved_data["e_nu"] = next_edge(true);
+    ctx->mark_non_differentiable({lu, lv});
+    // autograd outputs must be defined tensors: without x_res there is no centroid
+    if (xc.defined()) return {O, xc, lu, lv};
+    return {O, lu, lv};
+  }
+
+  static variable_list backward(AutogradContext* ctx, variable_list grads) {
+    const auto saved = ctx->get_saved_variables();
+    const Tensor &Qc = saved[0], &Kc = saved[1], &Vc = saved[2], &xr = saved[3], &pw = saved[4],
+                 &pb = saved[5], &epsc = saved[6], &wd = saved[7], &lmu = saved[8], &lnu = saved[9],
+                 &mk = saved[10], &lu = saved[11], &lv = saved[12];
+    auto needs = [&](const char* key) {
+      const int64_t e = ctx->saved_data[key].toInt();
+      return e >= 0 && ctx->needs_input_grad(static_cast<size_t>(e));
+    };
+    TORCH_CHECK(!((needs("e_x") && xr.defined()) || (needs("e_pw") && pw.defined()) ||
+                  (needs("e_wd") && wd.defined())),
+                "gradients for x_res / pos_weight / w_dist are not implemented by the B200 backward yet; "
+                "pass them without requires_grad");
+    const int64_t B = Qc.size(0), H = Qc.size(1), N = Qc.size(2), d = Qc.size(3);
+    const auto fo = Qc.options().dtype(at::kFloat);
+    const Tensor dOc = grads[0].defined() ? grads[0].contiguous().to(at::kFloat) : at::zeros({B, H, N, d}, fo);
+    const Tensor dxc = (xr.defined() && grads[1].defined()) ? grads[1].contiguous().to(at::kFloat) : Tensor();
+    Tensor dQ = ctx->needs_input_grad(0) ? at::empty({B, H, N, d}, fo) : Tensor();
+    Tensor dK = ctx->needs_input_grad(1) ? at::empty({B, H, N, d}, fo) : Tensor();
+    Tensor dV = ctx->needs_input_grad(2) ? at::empty({B, H, N, d}, fo) : Tensor();
+    Tensor dmu = needs("e_mu") ? at::empty({B, H, N}, fo) : Tensor();
+    Tensor dnu = needs("e_nu") ? at::empty({B, H, N}, fo) : Tensor();
+    Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
+    Tensor resid = at::empty({B * H}, fo);
+    Tensor status = at::zeros({1}, Qc.options().dtype(at::kInt));
+
+    dfs_problem prob{};
+    prob.B = static_cast<int32_t>(B);
+    prob.H = static_cast<int32_t>(H);
+    prob.N = static_cast<int32_t>(N);
+    prob.d = static_cast<int32_t>(d);
+    prob.in_dtype = dtype_code(Qc.scalar_type());
+    prob.cost_mode = DFS_COST_QK;
+    prob.K_iter = static_cast<int32_t>(ctx->saved_data["K_iter"].toInt());
+    prob.check_every = 2;
+    prob.lam = static_cast<float>(ctx->saved_data["lam"].toDouble());
+    prob.r_0 = static_cast<float>(ctx->saved_data["r_0"].toDouble());
+    dfs_cg_params cg{};
+    cg.rtol = static_cast<float>(ctx->saved_data["cg_rtol"].toDouble());
+    cg.atol = static_cast<float>(ctx->saved_data["cg_atol"].toDouble());
+    cg.max_iter = static_cast<int32_t>(ctx->saved_data["cg_max_iter"].toInt());
+    dfs_bwd_args a{};
+    a.Q = Qc.data_ptr();
+    a.K = Kc.data_ptr();
+    a.V = Vc.data_ptr();
+    a.x_res = ptr_or_null<const float>(xr);
+    a.pos_weight = ptr_or_null<const float>(pw);
+    a.pos_bins = ptr_or_null<const int32_t>(pb);
+    a.eps = epsc.data_ptr<float>();
+    a.w_dist = ptr_or_null<const float>(wd);
+    a.log_mu = lmu.data_ptr<float>();
+    a.log_nu = lnu.data_ptr<float>();
+    a.mask = ptr_or_null<const float>(mk);
+    a.log_u = lu.data_ptr<float>();
+    a.log_v = lv.data_ptr<float>();
+    a.dO = dOc.data_ptr<float>();
+    a.dxc = ptr_or_null<const float>(dxc);
+    a.dQ = ptr_or_null<float>(dQ);
+    a.dK = ptr_or_null<float>(dK);
+    a.dV = ptr_or_null<float>(dV);
+    a.dlog_mu = ptr_or_null<float>(dmu);
+    a.dlog_nu = ptr_or_null<float>(dnu);
+    a.cg_iters = iters.data_ptr<int32_t>();
+    a.cg_residual = resid.data_ptr<float>();
+    a.status = status.data_ptr<int32_t>();
+    const cudaStream_t stream = at::cuda::getCurrentCUDAStream(Qc.device().index()).stream();
+    check_rc(dfs_bwd(&prob, &cg, &a, nullptr, 0, stream), "dfs_bwd");
+    last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
+
+    // gradients in the dtype of the forward's inputs
+    const auto in_dt = static_cast<at::ScalarType>(ctx->saved_data["in_dtype"].toInt());
+    auto cast = [&](const Tensor& g) { return g.defined() ? g.to(in_dt) : g; };
+    variable_list out(19);
+    out[0] = cast(dQ);
+    out[1] = cast(dK);
+    out[2] = cast(dV);
+    out[8] = dmu;
+    out[9] = dnu;
+    return out;
+  }
+};
+
+std::vector<Tensor> flash_sinkhorn_autograd(Tensor Q, Tensor K, Tensor V, c10::optional<Tensor> x_res,
+                                            c10::optional<Tensor> pos_weight, c10::optional<Tensor> pos_bins,
+                                            Tensor eps, c10::optional<Tensor> w_dist, Tensor log_mu,
+                                            Tensor log_nu, c10::optional<Tensor> log_u_init,
+                                            c10::optional<Tensor> log_v_init, c10::optional<Tensor> mask,
+                                            int64_t K_iter, double lam, double r_0, double cg_rtol,
+                                            double cg_atol, int64_t cg_max_iter) {
+  return FlashSinkhornFn::apply(Q, K, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu, log_u_init,
+                                log_v_init, mask, K_iter, lam, r_0, cg_rtol, cg_atol, cg_max_iter);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "native autograd glue for libdfsink (flash Sinkhorn forward / IFT backward)";
+  m.def("flash_sinkhorn", &flash_sinkhorn_autograd,
+        "FlashSinkhornFn.apply: returns [O, x_centroid, log_u, log_v], or [O, log_u, log_v] without x_res");
+  m.def("last_report", []() { return last_report(); },
+        "[cg_iters, cg_residual, status, fwd_status] of the most recent backward");
+}

@@ -73,7 +73,7 @@ class DfsBwdArgs(ctypes.Structure):
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
                     "dfs_fwd", "dfs_bwd", "dfs_selftest_mma")
 
-_lock = threading.Lock()
+_lock = threading.RLock()  # ext() loads lib() while holding it
 _lib = None
 
 
@@ -98,6 +98,58 @@ def build_library(force: bool = False, verbose: bool = False) -> str:
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
+
+
+TORCH_EXT_NAME = "dfsink_torch"
+TORCH_EXT_PATH = os.path.join(LIB_DIR, TORCH_EXT_NAME + ".so")
+TORCH_EXT_SOURCE = os.path.join(CSRC_DIR, "dfs_torch.cpp")
+_ext = None
+
+
+def build_torch_ext(force: bool = False, verbose: bool = False) -> str:
+    """Compile the native autograd glue (``dfsink_torch.so``, linked to
+    ``libdfsink.so``) into the package with torch's extension builder."""
+    build_library(verbose=verbose)
+    deps = [TORCH_EXT_SOURCE, LIB_PATH, os.path.join(INCLUDE_DIR, "dfsink.h")]
+    if (not force and os.path.exists(TORCH_EXT_PATH)
+            and all(os.path.getmtime(f) <= os.path.getmtime(TORCH_EXT_PATH) for f in deps)):
+        return TORCH_EXT_PATH
+    from torch.utils import cpp_extension
+
+    bdir = os.path.join(LIB_DIR, "_build")
+    os.makedirs(bdir, exist_ok=True)
+    # the extension finds libdfsink.so beside itself ($ORIGIN, escaped for ninja ("$$") and
+    # for the shell that runs the link ("\\$"))
+    ldflags = [f"-L{LIB_DIR}", "-ldfsink", "-Wl,-rpath,\\$$ORIGIN:\\$$ORIGIN/.."]
+    cpp_extension.load(name=TORCH_EXT_NAME, sources=[TORCH_EXT_SOURCE], extra_include_paths=[INCLUDE_DIR],
+                       extra_cflags=["-O2"], extra_ldflags=ldflags, build_directory=bdir, with_cuda=True,
+                       verbose=verbose, is_python_module=True)
+    tmp = TORCH_EXT_PATH + ".tmp.%d" % os.getpid()
+    with open(os.path.join(bdir, TORCH_EXT_NAME + ".so"), "rb") as src, open(tmp, "wb") as dst:
+        dst.write(src.read())
+    os.replace(tmp, TORCH_EXT_PATH)
+    return TORCH_EXT_PATH
+
+
+def ext():
+    """The native autograd module (raises if it has not been built)."""
+    global _ext
+    if _ext is not None:
+        return _ext
+    with _lock:
+        if _ext is None:
+            if not os.path.exists(TORCH_EXT_PATH):
+                raise RuntimeError(
+                    f"{TORCH_EXT_NAME}.so not found at {TORCH_EXT_PATH}; build it with "
+                    "`python -c 'import __graft_entry__ as g; g.build()'`")
+            import importlib.util
+
+            lib()  # libdfsink first (the extension links to it)
+            spec = importlib.util.spec_from_file_location(TORCH_EXT_NAME, TORCH_EXT_PATH)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            _ext = mod
+    return _ext
 
 
 def lib() -> ctypes.CDLL:

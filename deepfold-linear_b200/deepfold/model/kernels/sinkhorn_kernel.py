@@ -27,112 +27,18 @@ import torch
 
 from deepfold import _native as nat
 
-__all__ = ["flash_sinkhorn", "FlashSinkhornFunction", "CG_DEFAULTS", "last_cg_report"]
+__all__ = ["flash_sinkhorn", "CG_DEFAULTS", "last_cg_report"]
 
 # CG stopping rule of the backward: ||r|| <= max(atol, rtol * ||r0||), as in
 # deepfold.utils.cg.conjugate_gradient.
 CG_DEFAULTS = dict(rtol=1e-6, atol=1e-10, max_iter=50)
 
-_last_report: dict = {}
-
 
 def last_cg_report() -> dict:
-    """Device tensors (cg_iters, cg_residual, status) of the most recent backward."""
-    return dict(_last_report)
-
-
-def _f32(t):
-    return None if t is None else t.contiguous().float()
-
-
-class FlashSinkhornFunction(torch.autograd.Function):
-    """Autograd wrapper around ``dfs_fwd`` / ``dfs_bwd``."""
-
-    @staticmethod
-    def forward(ctx, Q, K, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu,
-                K_iter, lam, r_0, log_u_init, log_v_init, mask, cg):
-        dev = nat.require_cuda(Q, K, V)
-        B, H, N, d = Q.shape
-        if K.shape != Q.shape or V.shape != Q.shape:
-            raise ValueError("Q, K, V must share the shape (B, H, N, d)")
-        if N > nat.max_n(d):
-            raise ValueError(f"N={N}, d={d} is outside the resident kernels' range "
-                             f"(N <= {nat.max_n(d)} for this d)")
-        cdt = Q.dtype if Q.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32
-        Qc, Kc, Vc = (t.contiguous().to(cdt) for t in (Q, K, V))
-        xr = _f32(x_res)
-        pw = _f32(pos_weight)
-        pb = None if pos_bins is None or pos_weight is None else pos_bins.contiguous().to(torch.int32)
-        epsc = _f32(eps)
-        wd = _f32(w_dist)
-        lmu, lnu = _f32(log_mu), _f32(log_nu)
-        lui, lvi = _f32(log_u_init), _f32(log_v_init)
-        mk = _f32(mask)
-        O = torch.empty(B, H, N, d, device=dev, dtype=torch.float32)
-        xc = torch.empty(B, H, N, 3, device=dev, dtype=torch.float32) if xr is not None else None
-        lu = torch.empty(B, H, N, device=dev, dtype=torch.float32)
-        lv = torch.empty(B, H, N, device=dev, dtype=torch.float32)
-        status = torch.zeros(1, device=dev, dtype=torch.int32)
-        prob = nat.make_problem(B, H, N, d, cdt, K_iter, lam, r_0)
-        args = nat.DfsFwdArgs(
-            Q=nat.ptr(Qc), K=nat.ptr(Kc), V=nat.ptr(Vc), C=None, x_res=nat.ptr(xr),
-            pos_weight=nat.ptr(pw), pos_bins=nat.ptr(pb), eps=nat.ptr(epsc), w_dist=nat.ptr(wd),
-            log_mu=nat.ptr(lmu), log_nu=nat.ptr(lnu), log_u_init=nat.ptr(lui),
-            log_v_init=nat.ptr(lvi), mask=nat.ptr(mk), O=nat.ptr(O), x_centroid=nat.ptr(xc),
-            log_u=nat.ptr(lu), log_v=nat.ptr(lv), status=nat.ptr(status))
-        nat.check(nat.lib().dfs_fwd(prob, args, None, 0, nat.stream_ptr(dev)), "dfs_fwd")
-        ctx.save_for_backward(Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv)
-        ctx.prob = (B, H, N, d, cdt, K_iter, lam, r_0)
-        ctx.cg = cg
-        ctx.status = status
-        ctx.mark_non_differentiable(lu, lv)
-        if xc is None:
-            return O, None, lu, lv
-        return O, xc, lu, lv
-
-    @staticmethod
-    def backward(ctx, dO, dxc, _dlu, _dlv):
-        Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv = ctx.saved_tensors
-        B, H, N, d, cdt, K_iter, lam, r_0 = ctx.prob
-        need = ctx.needs_input_grad
-        if (need[3] and xr is not None) or (need[4] and pw is not None) or (need[7] and wd is not None):
-            raise NotImplementedError(
-                "gradients for x_res / pos_weight / w_dist are not implemented by the B200 "
-                "backward yet; pass them without requires_grad")
-        dev = Qc.device
-        if dO is None:
-            dO = torch.zeros(B, H, N, d, device=dev, dtype=torch.float32)
-        dOc = dO.contiguous().float()
-        dxcc = None if (dxc is None or xr is None) else dxc.contiguous().float()
-        dQ = torch.empty(B, H, N, d, device=dev, dtype=torch.float32) if need[0] else None
-        dK = torch.empty(B, H, N, d, device=dev, dtype=torch.float32) if need[1] else None
-        dV = torch.empty(B, H, N, d, device=dev, dtype=torch.float32) if need[2] else None
-        dmu = torch.empty(B, H, N, device=dev, dtype=torch.float32) if need[8] else None
-        dnu = torch.empty(B, H, N, device=dev, dtype=torch.float32) if need[9] else None
-        iters = torch.empty(B * H, device=dev, dtype=torch.int32)
-        resid = torch.empty(B * H, device=dev, dtype=torch.float32)
-        status = torch.zeros(1, device=dev, dtype=torch.int32)
-        cg = ctx.cg
-        prob = nat.make_problem(B, H, N, d, cdt, K_iter, lam, r_0)
-        cgp = nat.DfsCgParams(rtol=float(cg["rtol"]), atol=float(cg["atol"]),
-                              max_iter=int(cg["max_iter"]), reserved=0)
-        args = nat.DfsBwdArgs(
-            Q=nat.ptr(Qc), K=nat.ptr(Kc), V=nat.ptr(Vc), x_res=nat.ptr(xr), pos_weight=nat.ptr(pw),
-            pos_bins=nat.ptr(pb), eps=nat.ptr(epsc), w_dist=nat.ptr(wd), log_mu=nat.ptr(lmu),
-            log_nu=nat.ptr(lnu), mask=nat.ptr(mk), log_u=nat.ptr(lu), log_v=nat.ptr(lv),
-            dO=nat.ptr(dOc), dxc=nat.ptr(dxcc), dQ=nat.ptr(dQ), dK=nat.ptr(dK), dV=nat.ptr(dV),
-            dlog_mu=nat.ptr(dmu), dlog_nu=nat.ptr(dnu), dx_res=None, dpos_weight=None,
-            dw_dist=None, cg_iters=nat.ptr(iters), cg_residual=nat.ptr(resid),
-            status=nat.ptr(status))
-        nat.check(nat.lib().dfs_bwd(prob, cgp, args, None, 0, nat.stream_ptr(dev)), "dfs_bwd")
-        _last_report.update(cg_iters=iters, cg_residual=resid, status=status,
-                            fwd_status=ctx.status)
-
-        def cast(g, like):
-            return None if g is None else g.to(like.dtype)
-
-        return (cast(dQ, Qc), cast(dK, Kc), cast(dV, Vc), None, None, None, None, None,
-                dmu, dnu, None, None, None, None, None, None, None)
+    """Device tensors (cg_iters, cg_residual, status, fwd_status) of the most
+    recent backward."""
+    rep = nat.ext().last_report()
+    return dict(zip(("cg_iters", "cg_residual", "status", "fwd_status"), rep))
 
 
 def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu,
@@ -168,9 +74,12 @@ def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_
         lam = float(lam)
     if not (lam > 0.0) or math.isnan(lam):
         raise ValueError("lam must be positive (inf for the balanced problem)")
-    out = FlashSinkhornFunction.apply(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist,
-                                      log_mu, log_nu, int(K_iter), float(lam), float(r_0),
-                                      log_u_init, log_v_init, mask, cg)
+    # native autograd function FlashSinkhornFn (csrc/dfs_torch.cpp): validates,
+    # allocates and calls dfs_fwd / dfs_bwd of libdfsink on the current stream
+    out = nat.ext().flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu,
+                                   log_nu, log_u_init, log_v_init, mask, int(K_iter), float(lam),
+                                   float(r_0), float(cg["rtol"]), float(cg["atol"]), int(cg["max_iter"]))
+    out = tuple(out) if len(out) == 4 else (out[0], None, out[1], out[2])
     if unbatched:
         return tuple(None if t is None else t.squeeze(0) for t in out)
     return out

@@ -66,3 +66,23 @@ def test_host_side_validation(lib):
     assert lib.dfs_workspace_size(ok, ctypes.byref(fws), ctypes.byref(bws)) == nat.DFS_OK
     assert fws.value == 0
     assert lib.dfs_selftest_mma(5, None, None, None, 64, 32, 32, None) == nat.DFS_ERR_INVALID_ARGUMENT
+
+
+def test_native_autograd_extension_loads():
+    # dfsink_torch.so (csrc/dfs_torch.cpp) links libdfsink and carries the
+    # autograd function behind flash_sinkhorn; importing it needs no GPU
+    nat.build_torch_ext()
+    ext = nat.ext()
+    assert callable(ext.flash_sinkhorn) and callable(ext.last_report)
+    assert ext.last_report() == []
+
+
+def test_native_autograd_rejects_cpu_tensors():
+    import torch
+
+    ext = nat.ext()
+    x = torch.zeros(1, 1, 64, 32)
+    lm = torch.zeros(1, 1, 64)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ext.flash_sinkhorn(x, x, x, None, None, None, torch.ones(1), None, lm, lm, None, None, None,
+                           5, float("inf"), 10.0, 1e-6, 0.0, 50)
