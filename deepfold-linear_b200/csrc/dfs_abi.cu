@@ -22,6 +22,13 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? DFS_OK : DFS_ERR_CUDA
 // the kernels read Q, K, V and dO in 16-byte chunks
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// cluster-resident kernels (S kept on chip): d = 32, N <= 384; streamed
+// kernels (S recomputed tile by tile): d = 32 or 64, N <= kStreamMaxN
+constexpr int kResidentMaxN = 384;
+constexpr int kStreamMaxN = 1 << 16;
+bool resident(const dfs_problem* p) { return p->d == 32 && p->N <= kResidentMaxN; }
+bool streamed(const dfs_problem* p) { return (p->d == 32 || p->d == 64) && p->N <= kStreamMaxN; }
+
 }  // namespace
 
 extern "C" {
@@ -32,7 +39,7 @@ const char* dfs_status_string(int s) {
   switch (s) {
     case DFS_OK: return "ok";
     case DFS_ERR_INVALID_ARGUMENT: return "invalid argument";
-    case DFS_ERR_UNSUPPORTED: return "shape or dtype not supported by the resident kernels";
+    case DFS_ERR_UNSUPPORTED: return "shape, dtype or option not supported by the kernels";
     case DFS_ERR_WORKSPACE: return "workspace too small";
     case DFS_ERR_CUDA: return "CUDA runtime error";
     case DFS_ERR_DEVICE_TIMEOUT: return "device: bounded wait gave up";
@@ -42,19 +49,18 @@ const char* dfs_status_string(int s) {
   }
 }
 
-int dfs_max_n(int d) { return d == 32 ? 384 : 0; }
+int dfs_max_n(int d) { return (d == 32 || d == 64) ? kStreamMaxN : 0; }
 
 int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes) {
   if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
-  if (fwd_bytes) *fwd_bytes = 0;
-  if (bwd_bytes) *bwd_bytes = resident_bwd_workspace(p->B, p->H, p->N, p->d);
+  const bool res = resident(p);
+  if (fwd_bytes) *fwd_bytes = res ? 0 : stream_fwd_workspace(p->B, p->H, p->N);
+  if (bwd_bytes) *bwd_bytes = res ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : 0;
   return DFS_OK;
 }
 
 int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t workspace_bytes,
             void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (!dims_ok(p) || !a) return DFS_ERR_INVALID_ARGUMENT;
   if (!a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v) return DFS_ERR_INVALID_ARGUMENT;
   if (p->cost_mode == DFS_COST_QK && (!a->Q || !a->K)) return DFS_ERR_INVALID_ARGUMENT;
@@ -62,9 +68,19 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   if (a->O && !a->V) return DFS_ERR_INVALID_ARGUMENT;
   if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
-  if (p->N > dfs_max_n(p->d)) return DFS_ERR_UNSUPPORTED;
+  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   if (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V))
     return DFS_ERR_INVALID_ARGUMENT;
+  if (!resident(p)) {
+    // streamed path: QK cost with masks, marginals, kappa and warm starts; the
+    // position / geometry terms, early stopping and the dense plan are resident-only
+    if (p->cost_mode != DFS_COST_QK || a->pos_weight || a->w_dist || p->threshold > 0.0f || a->T_norm ||
+        (a->x_centroid && !a->O))
+      return DFS_ERR_UNSUPPORTED;
+    if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N) ||
+        !aligned16(workspace))
+      return DFS_ERR_WORKSPACE;
+  }
   FwdParams q;
   std::memset(&q, 0, sizeof(q));
   q.Q = a->Q; q.K = a->K; q.V = a->V; q.C = a->C;
@@ -77,6 +93,8 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
   q.cost_mode = p->cost_mode; q.K_iter = p->K_iter; q.check_every = p->check_every > 0 ? p->check_every : 1;
   q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
+  if (!resident(p))
+    return cuda_status(launch_stream_fwd(q, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
   return cuda_status(launch_resident_fwd(q, static_cast<cudaStream_t>(stream)));
 }
 
@@ -94,7 +112,7 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   if (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) || !aligned16(a->dQ) ||
       !aligned16(a->dK) || !aligned16(a->dV))
     return DFS_ERR_INVALID_ARGUMENT;
-  if (p->N > dfs_max_n(p->d)) return DFS_ERR_UNSUPPORTED;
+  if (!resident(p)) return DFS_ERR_UNSUPPORTED;
   const size_t need = resident_bwd_workspace(p->B, p->H, p->N, p->d);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return DFS_ERR_WORKSPACE;
   BwdParams q;

@@ -82,6 +82,8 @@ struct BwdParams {
 
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
 size_t resident_fwd_smem(int N, int d);
+cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
+size_t stream_fwd_workspace(int B, int H, int N);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
 size_t resident_bwd_smem(int N, int d);
 size_t resident_bwd_workspace(int B, int H, int N, int d);

@@ -169,8 +169,9 @@ DFS_DEV void widen(const uint4& raw, float (&v)[4], float*) {
 // TR = true at (c, i) of a buffer with DH rows (the K-major operand holding the
 // transpose).  Each thread moves 16-byte chunks and issues all of its loads
 // before consuming any, so the tile costs one global-memory round trip.
-template <int DH, int ROWS, bool TR, typename T>
+template <int DH, int ROWS, bool TR, typename T, int NT = kThreads>
 DFS_DEV void load_tile(float* dst, const T* src, int row_first, int N, int tid) {
+  constexpr int kThreads = NT;              // threads taking part
   constexpr int EPC = Chunk16<T>::kElems;   // elements per chunk
   constexpr int CPR = DH / EPC;             // chunks per row
   constexpr int TOTAL = ROWS * CPR;
@@ -209,15 +210,18 @@ DFS_DEV void load_tile(float* dst, const T* src, int row_first, int N, int tid) 
   }
 }
 
-template <int DH, int ROWS, bool TR>
+template <int DH, int ROWS, bool TR, int NT = kThreads>
 DFS_DEV void load_tile_any(float* dst, const void* src, int dtype, size_t base_row, int row_first, int N,
                            int tid) {
   if (dtype == DFS_BF16)
-    load_tile<DH, ROWS, TR>(dst, reinterpret_cast<const __nv_bfloat16*>(src) + base_row * DH, row_first, N, tid);
+    load_tile<DH, ROWS, TR, __nv_bfloat16, NT>(dst, reinterpret_cast<const __nv_bfloat16*>(src) + base_row * DH,
+                                               row_first, N, tid);
   else if (dtype == DFS_F16)
-    load_tile<DH, ROWS, TR>(dst, reinterpret_cast<const __half*>(src) + base_row * DH, row_first, N, tid);
+    load_tile<DH, ROWS, TR, __half, NT>(dst, reinterpret_cast<const __half*>(src) + base_row * DH, row_first, N,
+                                        tid);
   else
-    load_tile<DH, ROWS, TR>(dst, reinterpret_cast<const float*>(src) + base_row * DH, row_first, N, tid);
+    load_tile<DH, ROWS, TR, float, NT>(dst, reinterpret_cast<const float*>(src) + base_row * DH, row_first, N,
+                                       tid);
 }
 
 // Load rows [row_first, row_first+ROWS) of a (., DH) tensor into a
@@ -277,6 +281,23 @@ DFS_DEV void issue_abt(uint32_t d_tmem, const float* A, const float* Bm) {
       const uint64_t bo = static_cast<uint64_t>(((kk >> 2) * NN * 128 + (h2 * NCH / 8) * 1024 + (kk & 3) * 32) >> 4);
       mma_tf32(d_tmem + h2 * NCH, a0 + ao, b0 + bo, idesc, kk > 0 ? 1u : 0u);
     }
+  }
+}
+
+// D (TMEM, MA rows x NN columns, MA = 64 or 128) (+)= A (MA x KD) * B (NN x KD)^T,
+// both K-major 128B-swizzled fp32 buffers (A stored with MA rows, B with NN
+// rows) read as tf32; `accumulate` = false starts the accumulator.  With
+// MA = 128, row m of the result is TMEM lane m.  One elected thread.
+template <int MA, int NN, int KD>
+DFS_DEV void issue_mma(uint32_t d_tmem, const float* A, const float* Bm, bool accumulate) {
+  static_assert((MA == 64 || MA == 128) && NN % 16 == 0 && NN <= 256 && KD % 8 == 0, "UMMA shape");
+  constexpr uint32_t idesc = idesc_tf32(MA, NN, 0, 0);
+  const uint64_t a0 = sw128_desc(smem_u32(A), 16, 1024), b0 = sw128_desc(smem_u32(Bm), 16, 1024);
+#pragma unroll
+  for (int kk = 0; kk < KD / 8; ++kk) {
+    const uint64_t ao = static_cast<uint64_t>(((kk >> 2) * MA * 128 + (kk & 3) * 32) >> 4);
+    const uint64_t bo = static_cast<uint64_t>(((kk >> 2) * NN * 128 + (kk & 3) * 32) >> 4);
+    mma_tf32(d_tmem, a0 + ao, b0 + bo, idesc, (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 

@@ -112,8 +112,11 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     a.log_u = lu.data_ptr<float>();
     a.log_v = lv.data_ptr<float>();
     a.status = status.data_ptr<int32_t>();
+    size_t fwd_ws = 0, bwd_ws = 0;  // the streamed path (large N, d = 64) needs scratch
+    check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
+    Tensor ws = fwd_ws ? at::empty({static_cast<int64_t>((fwd_ws + 3) / 4)}, fo) : Tensor();
     const cudaStream_t stream = at::cuda::getCurrentCUDAStream(Q.device().index()).stream();
-    check_rc(dfs_fwd(&prob, &a, nullptr, 0, stream), "dfs_fwd");
+    check_rc(dfs_fwd(&prob, &a, ws.defined() ? ws.data_ptr() : nullptr, fwd_ws, stream), "dfs_fwd");
 
     ctx->save_for_backward({Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv});
     ctx->saved_data["K_iter"] = K_iter;
@@ -204,8 +207,11 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     a.cg_iters = iters.data_ptr<int32_t>();
     a.cg_residual = resid.data_ptr<float>();
     a.status = status.data_ptr<int32_t>();
+    size_t fwd_ws = 0, bwd_ws = 0;
+    check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
+    Tensor ws = bwd_ws ? at::empty({static_cast<int64_t>((bwd_ws + 3) / 4)}, fo) : Tensor();
     const cudaStream_t stream = at::cuda::getCurrentCUDAStream(Qc.device().index()).stream();
-    check_rc(dfs_bwd(&prob, &cg, &a, nullptr, 0, stream), "dfs_bwd");
+    check_rc(dfs_bwd(&prob, &cg, &a, ws.defined() ? ws.data_ptr() : nullptr, bwd_ws, stream), "dfs_bwd");
     last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
 
     // gradients in the dtype of the forward's inputs

@@ -134,8 +134,10 @@ int dfs_abi_version(void);
 /* Text for a status code or an OR of device status bits. */
 const char* dfs_status_string(int status);
 
-/* Largest N the resident (on-chip) kernels accept for head dim d; 0 if d is
- * unsupported. */
+/* Largest N accepted for head dim d (0 if d is unsupported).  d = 32 and
+ * N <= 384 run on the cluster-resident kernels (the log-kernel stays on chip);
+ * larger N and d = 64 run on the streamed kernels, which recompute it tile by
+ * tile and need a workspace (dfs_workspace_size). */
 int dfs_max_n(int d);
 
 /* Bytes of device workspace dfs_fwd / dfs_bwd need for problem p. */

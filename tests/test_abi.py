@@ -54,9 +54,17 @@ def test_host_side_validation(lib):
     p = nat.make_problem(2, 8, 384, 32, __import__("torch").bfloat16, 20, float("inf"), 10.0)
     a = nat.DfsFwdArgs()
     assert lib.dfs_fwd(p, a, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
-    big = nat.make_problem(1, 1, 4096, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
     fake = nat.DfsFwdArgs(Q=16, K=16, V=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16)
-    assert lib.dfs_fwd(big, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
+    # beyond the resident range the streamed kernels need a workspace
+    big = nat.make_problem(1, 1, 4096, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
+    assert lib.dfs_fwd(big, fake, None, 0, None) == nat.DFS_ERR_WORKSPACE
+    fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    assert lib.dfs_workspace_size(big, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
+    assert fb.value == 4 * 4 * 4096
+    huge = nat.make_problem(1, 1, 1 << 17, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
+    assert lib.dfs_fwd(huge, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
+    odd_d = nat.make_problem(1, 1, 128, 48, __import__("torch").bfloat16, 20, 1.0, 10.0)
+    assert lib.dfs_fwd(odd_d, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
     bad = nat.make_problem(1, 1, 64, 32, __import__("torch").bfloat16, 20, -1.0, 10.0)
     assert lib.dfs_fwd(bad, fake, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
     cg = nat.DfsCgParams(rtol=1e-6, atol=1e-6, max_iter=-1)
