@@ -55,7 +55,8 @@ int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_byte
   if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
   const bool res = resident(p);
   if (fwd_bytes) *fwd_bytes = res ? 0 : stream_fwd_workspace(p->B, p->H, p->N);
-  if (bwd_bytes) *bwd_bytes = res ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : 0;
+  if (bwd_bytes)
+    *bwd_bytes = res ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : stream_bwd_workspace(p->B, p->H, p->N);
   return DFS_OK;
 }
 
@@ -112,8 +113,14 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   if (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) || !aligned16(a->dQ) ||
       !aligned16(a->dK) || !aligned16(a->dV))
     return DFS_ERR_INVALID_ARGUMENT;
-  if (!resident(p)) return DFS_ERR_UNSUPPORTED;
-  const size_t need = resident_bwd_workspace(p->B, p->H, p->N, p->d);
+  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
+  if (!resident(p)) {
+    // streamed path: no position / geometry terms and none of their gradients
+    if (a->pos_weight || a->w_dist || a->dx_res || a->dpos_weight || a->dw_dist) return DFS_ERR_UNSUPPORTED;
+    if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
+      return DFS_ERR_WORKSPACE;
+  }
+  const size_t need = resident(p) ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : 0;
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return DFS_ERR_WORKSPACE;
   BwdParams q;
   std::memset(&q, 0, sizeof(q));
@@ -128,6 +135,8 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
   q.cg_max_iter = cg->max_iter; q.cg_rtol = cg->rtol; q.cg_atol = cg->atol;
   q.lam = p->lam; q.r_0 = p->r_0;
+  if (!resident(p))
+    return cuda_status(launch_stream_bwd(q, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
   return cuda_status(launch_resident_bwd(q, static_cast<cudaStream_t>(stream)));
 }
 

@@ -85,6 +85,8 @@ size_t resident_fwd_smem(int N, int d);
 cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
 size_t stream_fwd_workspace(int B, int H, int N);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
+cudaError_t launch_stream_bwd(const BwdParams& p, float* ws, cudaStream_t st);
+size_t stream_bwd_workspace(int B, int H, int N);
 size_t resident_bwd_smem(int N, int d);
 size_t resident_bwd_workspace(int B, int H, int N, int d);
 cudaError_t launch_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K,

@@ -1,0 +1,755 @@
+// dfs_stream_bwd.cu -- streamed IFT backward for sm_100a (any N, d = 32 or 64).
+//
+// The same gradient as the cluster-resident backward (csrc/dfs_bwd.cu): with
+// the forward's fixed point (f, g), P = exp2(x), x = S' + f_i + g_j (log2 units),
+// T_norm = exp2(x - m_i) / (R_i + 1e-6), dT = dO V^T (+ dxc x^T),
+// D_i = sum_j T_norm dT, E = T_norm o (dT - D), the IFT system is solved on the
+// Schur complement of its row block by conjugate gradient, and
+// dS = E - P o (w1 (+) w2) gives dQ = dS K and dK = dS^T Q (scaled by
+// 1/(eps sqrt d)), dV = T_norm^T dO.  Nothing of size N x N is stored: every
+// pass below recomputes its tiles of S (and of dT) with tcgen05 MMAs.
+//
+// Tile passes (one CTA = 128 rows of one problem, one thread per row = TMEM
+// lane, column tiles of 64):
+//   SB_ROW     rows:    m, R, D                    (S, dT tiles)
+//   SB_COL     columns: c = P^T 1, g_v = E^T 1      (S^T, dT^T tiles; roles swapped)
+//   SB_MATVEC  y_i = scale_i sum_j P_ij v_j        (either orientation)
+//   SB_DQ      rows:    dQ += dS K                  (dS tile -> third MMA)
+//   SB_DKV     columns: dK += dS^T Q, dV += T_norm^T dO
+// Per-problem vector steps (setup of the CG system, one CG iteration, the
+// null-space shift and marginal gradients) run as one CTA per problem.
+#include <type_traits>
+
+#include "dfs_slab.cuh"
+
+namespace dfs {
+
+constexpr int kBThreads = 128;
+constexpr int kBTile = 64;
+
+enum StreamBwdMode { SB_ROW = 0, SB_COL = 1, SB_MATVEC = 2, SB_DQ = 3, SB_DKV = 4 };
+
+struct StreamBwdParams {
+  // operands, each (BH, N, d) row-major, of type dtype unless marked fp32
+  const void* Aop; int a_f32;     // rows of S = A B^T
+  const void* Bop; int b_f32;     // columns
+  const void* A2op; int a2_f32;   // rows of the second product (dT)
+  const void* B2op; int b2_f32;   // columns of the second product
+  const void* B3op; int b3_f32;   // SB_DQ / SB_DKV: first accumulation MMA, stored transposed
+  const void* B4op; int b4_f32;   // SB_DKV: second accumulation MMA, stored transposed
+  int dtype;
+  const float* eps;
+  const float* mask;              // (B, N) or null
+  const float* tv[8];             // per-column-position vectors (BH, N), see each mode
+  const float* xvec;              // (B, N, 3) per-position 3-vectors (x_res or dxc), or null
+  int xvec_per_head;              // xvec is (BH, N, 3) (dxc) rather than (B, N, 3) (x_res)
+  const float* rv[8];             // per-row vectors (BH, N)
+  const float* rxvec;             // (B or BH, N, 3) per-row 3-vectors, or null
+  int rxvec_per_head;
+  const int32_t* done;            // (BH) skip the problem when nonzero (converged CG), or null
+  float* out0;                    // (BH, N) results per row
+  float* out1;
+  float* out2;
+  float* acc0;                    // (BH, N, d) accumulated results
+  float* acc1;
+  float acc_scale0, acc_scale1;
+  int B, H, N;
+  int row_begin, row_end;
+};
+
+template <int MODE, int D>
+struct SBCfg {
+  static constexpr bool kDT = MODE == SB_ROW || MODE == SB_COL || MODE == SB_DQ || MODE == SB_DKV;
+  static constexpr bool kAcc = MODE == SB_DQ || MODE == SB_DKV;
+  static constexpr bool kTwo = MODE == SB_DKV;
+  static constexpr int TW = kBTile;
+  static constexpr uint32_t OFF_A = 0;                                        // 128 x D
+  static constexpr uint32_t OFF_A2 = OFF_A + 4u * 128 * D;                    // 128 x D
+  static constexpr uint32_t OFF_B = OFF_A2 + (kDT ? 4u * 128 * D : 0u);       // TW x D
+  static constexpr uint32_t OFF_B2 = OFF_B + 4u * TW * D;                     // TW x D
+  static constexpr uint32_t OFF_B3 = OFF_B2 + (kDT ? 4u * TW * D : 0u);       // D x TW
+  static constexpr uint32_t OFF_B4 = OFF_B3 + (kAcc ? 4u * D * TW : 0u);      // D x TW
+  static constexpr uint32_t OFF_DS = OFF_B4 + (kTwo ? 4u * D * TW : 0u);      // 128 x TW
+  static constexpr uint32_t OFF_TT = OFF_DS + (kAcc ? 4u * 128 * TW : 0u);    // 128 x TW
+  static constexpr uint32_t OFF_TV = OFF_TT + (kTwo ? 4u * 128 * TW : 0u);    // 11 x TW vectors
+  static constexpr uint32_t OFF_BAR = OFF_TV + 4u * 11 * TW;
+  static constexpr uint32_t NEED = OFF_BAR + 64 + 1024;
+  static constexpr uint32_t SMEM = NEED > 81920u ? NEED : 81920u;  // <= 2 CTAs / SM (TMEM 2 x 256)
+  static_assert(NEED <= 232448u, "shared memory");
+};
+
+template <int MODE, int D>
+__global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdParams p) {
+  using Cfg = SBCfg<MODE, D>;
+  constexpr int TW = Cfg::TW;
+  constexpr bool kDT = Cfg::kDT, kAcc = Cfg::kAcc, kTwo = Cfg::kTwo;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* As = reinterpret_cast<float*>(base + Cfg::OFF_A);
+  float* A2s = reinterpret_cast<float*>(base + Cfg::OFF_A2);
+  float* Bs = reinterpret_cast<float*>(base + Cfg::OFF_B);
+  float* B2s = reinterpret_cast<float*>(base + Cfg::OFF_B2);
+  float* B3s = reinterpret_cast<float*>(base + Cfg::OFF_B3);
+  float* B4s = reinterpret_cast<float*>(base + Cfg::OFF_B4);
+  float* dSs = reinterpret_cast<float*>(base + Cfg::OFF_DS);
+  float* TTs = reinterpret_cast<float*>(base + Cfg::OFF_TT);
+  float* tvs = reinterpret_cast<float*>(base + Cfg::OFF_TV);  // [11][TW]: tv0..7, x 3-vector
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(base + Cfg::OFF_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + Cfg::OFF_BAR + 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nrb = (p.row_end - p.row_begin + 127) / 128;
+  const int prob = blockIdx.x / nrb, rb = blockIdx.x % nrb;
+  if (p.done != nullptr && p.done[prob] != 0) return;  // uniform over the CTA
+  const int bb = prob / p.H, hh = prob % p.H;
+  const int N = p.N;
+  const size_t bh = static_cast<size_t>(prob);
+  const int r0 = p.row_begin + 128 * rb, row = r0 + tid;
+  const float eps_h = p.eps[hh];
+  const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
+  const bool rin = row < p.row_end && row < N;
+  const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
+  int err = 0;
+
+  if (warp == 0) tmem_alloc(tslot, 256);
+  if (tid == 0) {
+    mbar_init(&mbar[0], 1);
+    mbar_init(&mbar[1], 1);
+    fence_mbar_init();
+  }
+  auto ldt = [&](float* dst, const void* src, int is_f32, int row_first, auto rows_tag, auto tr_tag) {
+    constexpr int ROWS = decltype(rows_tag)::value;
+    constexpr bool TR = decltype(tr_tag)::value;
+    load_tile_any<D, ROWS, TR, kBThreads>(dst, src, is_f32 ? static_cast<int>(DFS_F32) : p.dtype, bh * N,
+                                          row_first, N, tid);
+  };
+  using R128 = std::integral_constant<int, 128>;
+  using RTW = std::integral_constant<int, TW>;
+  using NoT = std::false_type;
+  using Tr = std::true_type;
+  ldt(As, p.Aop, p.a_f32, r0, R128{}, NoT{});
+  if constexpr (kDT) ldt(A2s, p.A2op, p.a2_f32, r0, R128{}, NoT{});
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t tlane = static_cast<uint32_t>(32 * warp) << 16;
+  // TMEM columns: S [0, TW), dT [TW, 2 TW), accumulators [2 TW, 2 TW + D), [2 TW + D, 2 TW + 2 D)
+  const uint32_t t_s = tbase, t_dt = tbase + TW, t_a0 = tbase + 2 * TW, t_a1 = tbase + 2 * TW + D;
+
+  float rv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) rv[k] = (rin && p.rv[k] != nullptr) ? p.rv[k][bh * N + row] : 0.0f;
+  float rx[3] = {0.0f, 0.0f, 0.0f};
+  if (p.rxvec != nullptr && rin) {
+    const size_t o = (p.rxvec_per_head ? bh : static_cast<size_t>(bb)) * N + row;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) rx[c] = p.rxvec[o * 3 + c];
+  }
+  const bool has_x = p.xvec != nullptr && p.rxvec != nullptr;
+  float s0 = 0.0f, s1 = 0.0f, mrun = -1.0e30f;  // running results
+
+  const int ntiles = (N + TW - 1) / TW;
+  uint32_t ph0 = 0, ph1 = 0;
+  auto wait_bar = [&](int b) {
+    const uint32_t par = b == 0 ? ph0 : ph1;
+    if (!mbar_wait(&mbar[b], par)) err |= DFS_ERR_DEVICE_TIMEOUT;
+    if (b == 0) ph0 ^= 1u; else ph1 ^= 1u;
+    tc_fence_after();
+  };
+
+#pragma unroll 1
+  for (int t = 0; t < ntiles; ++t) {
+    const int c0 = t * TW;
+    if (kAcc && t > 0) wait_bar(1);  // accumulation MMAs of tile t-1 done: their operands are free
+    // ---- stage the tile
+    ldt(Bs, p.Bop, p.b_f32, c0, RTW{}, NoT{});
+    if constexpr (kDT) ldt(B2s, p.B2op, p.b2_f32, c0, RTW{}, NoT{});
+    if constexpr (kAcc) ldt(B3s, p.B3op, p.b3_f32, c0, RTW{}, Tr{});
+    if constexpr (kTwo) ldt(B4s, p.B4op, p.b4_f32, c0, RTW{}, Tr{});
+    if (tid < TW) {
+      const int j = c0 + tid;
+      const bool cin = j < N;
+      const bool cok = cin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + j] != 0.0f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float v = (cin && p.tv[k] != nullptr) ? p.tv[k][bh * N + j] : 0.0f;
+        // tv0 (and for SB_COL / SB_DKV tv1) are potentials: -inf on invalid columns zeroes P, T
+        const bool pot = k == 0 || (k == 1 && (MODE == SB_COL || MODE == SB_DKV));
+        if (pot && !cok) v = -INFINITY;
+        tvs[k * TW + tid] = v;
+      }
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        float v = 0.0f;
+        if (has_x && cin) {
+          const size_t o = (p.xvec_per_head ? bh : static_cast<size_t>(bb)) * N + j;
+          v = p.xvec[o * 3 + c];
+        }
+        tvs[(8 + c) * TW + tid] = v;
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      issue_mma<128, TW, D>(t_s, As, Bs, false);
+      if constexpr (kDT) issue_mma<128, TW, D>(t_dt, A2s, B2s, false);
+      mma_commit(&mbar[0]);
+    }
+    wait_bar(0);
+
+    // ---- epilogue: 2 chunks of 32 columns
+#pragma unroll 1
+    for (int ch = 0; ch < TW / 32; ++ch) {
+      float sv[32], dv[32];
+      tmem_ld32(t_s + tlane + 32 * ch, sv);
+      if constexpr (kDT) tmem_ld32(t_dt + tlane + 32 * ch, dv);
+      const float* tv0 = tvs + 32 * ch;
+      if constexpr (MODE == SB_ROW) {
+        // rv0 = f; tv0 = g; dT += dxc_i . x_j (rx = dxc_i, tv 8..10 = x_j)
+        float cm = -1.0e30f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          sv[k] = fmaf(sv[k], scale, tv0[k] + rv[0]);
+          cm = fmaxf(cm, sv[k]);
+        }
+        const float mn = fmaxf(mrun, cm), resc = ex2(mrun - mn);
+        float r = s0 * resc, pd = s1 * resc;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          float dt = dv[k];
+          if (has_x) dt += rx[0] * tv0[8 * TW + k] + rx[1] * tv0[9 * TW + k] + rx[2] * tv0[10 * TW + k];
+          const float e = ex2(sv[k] - mn);
+          r += e;
+          pd = fmaf(e, dt, pd);
+        }
+        mrun = mn;
+        s0 = r;
+        s1 = pd;
+      } else if constexpr (MODE == SB_COL) {
+        // thread = column j: rv0 = g_j, rx = x_j; tile i: tv0 = f, tv1 = f - m, tv2 = 1/(R+1e-6),
+        // tv3 = D, tv 8..10 = dxc_i
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float sc = sv[k] * scale + rv[0];
+          const float P = ex2(sc + tv0[k]);
+          const float T = ex2(sc + tv0[TW + k]) * tv0[2 * TW + k];
+          float dt = dv[k];
+          if (has_x) dt += rx[0] * tv0[8 * TW + k] + rx[1] * tv0[9 * TW + k] + rx[2] * tv0[10 * TW + k];
+          s0 += P;
+          s1 = fmaf(T, dt - tv0[3 * TW + k], s1);
+        }
+      } else if constexpr (MODE == SB_MATVEC) {
+        // rv0 = row potential; tv0 = column potential, tv1 = the vector
+#pragma unroll
+        for (int k = 0; k < 32; ++k) s0 = fmaf(ex2(fmaf(sv[k], scale, tv0[k] + rv[0])), tv0[TW + k], s0);
+      } else if constexpr (MODE == SB_DQ) {
+        // rv0 = f, rv1 = f - m, rv2 = 1/(R+1e-6), rv3 = D, rv4 = w1; tv0 = g, tv1 = w2, tv 8..10 = x_j;
+        // rx = dxc_i
+        float ds[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float sc = fmaf(sv[k], scale, tv0[k]);
+          const float P = ex2(sc + rv[0]);
+          const float T = ex2(sc + rv[1]) * rv[2];
+          float dt = dv[k];
+          if (has_x) dt += rx[0] * tv0[8 * TW + k] + rx[1] * tv0[9 * TW + k] + rx[2] * tv0[10 * TW + k];
+          ds[k] = rok ? T * (dt - rv[3]) - P * (rv[4] + tv0[TW + k]) : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4*>(dSs + (sw_off(tid, 32 * ch + 4 * q, 128) >> 2)) =
+              make_float4(ds[4 * q], ds[4 * q + 1], ds[4 * q + 2], ds[4 * q + 3]);
+      } else {  // SB_DKV
+        // thread = column j: rv0 = g_j, rv1 = w2_j, rx = x_j; tile i: tv0 = f, tv1 = f - m,
+        // tv2 = 1/(R+1e-6), tv3 = D, tv4 = w1, tv 8..10 = dxc_i
+        float ds[32], tt[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float sc = sv[k] * scale + rv[0];
+          const float P = ex2(sc + tv0[k]);
+          const float T = ex2(sc + tv0[TW + k]) * tv0[2 * TW + k];
+          float dt = dv[k];
+          if (has_x) dt += rx[0] * tv0[8 * TW + k] + rx[1] * tv0[9 * TW + k] + rx[2] * tv0[10 * TW + k];
+          ds[k] = rok ? T * (dt - tv0[3 * TW + k]) - P * (tv0[4 * TW + k] + rv[1]) : 0.0f;
+          tt[k] = rok ? T : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          *reinterpret_cast<float4*>(dSs + (sw_off(tid, 32 * ch + 4 * q, 128) >> 2)) =
+              make_float4(ds[4 * q], ds[4 * q + 1], ds[4 * q + 2], ds[4 * q + 3]);
+          *reinterpret_cast<float4*>(TTs + (sw_off(tid, 32 * ch + 4 * q, 128) >> 2)) =
+              make_float4(tt[4 * q], tt[4 * q + 1], tt[4 * q + 2], tt[4 * q + 3]);
+        }
+      }
+    }
+    // every thread is done with the tile's vectors and TMEM S / dT; dS and T tiles are written
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if constexpr (kAcc) {
+      if (tid == 0) {
+        issue_mma<128, D, TW>(t_a0, dSs, B3s, t > 0);
+        if constexpr (kTwo) issue_mma<128, D, TW>(t_a1, TTs, B4s, t > 0);
+        mma_commit(&mbar[1]);
+      }
+    }
+  }
+
+  // ---------------------------------------------------------------- results
+  if constexpr (kAcc) {
+    wait_bar(1);
+#pragma unroll
+    for (int a = 0; a < (kTwo ? 2 : 1); ++a) {
+      float* dst_base = a == 0 ? p.acc0 : p.acc1;
+      float sc = a == 0 ? p.acc_scale0 : p.acc_scale1;
+      if (sc < 0.0f) sc = 1.0f / (eps_h * sqrtf(static_cast<float>(D)));  // dS -> dQ, dK
+#pragma unroll
+      for (int g = 0; g < D / 16; ++g) {
+        float v[16];
+        tmem_ld16((a == 0 ? t_a0 : t_a1) + tlane + 16 * g, v);
+        if (rin && dst_base != nullptr) {
+          float4* dst = reinterpret_cast<float4*>(dst_base + (bh * N + row) * D + 16 * g);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = rok ? make_float4(v[4 * q] * sc, v[4 * q + 1] * sc, v[4 * q + 2] * sc, v[4 * q + 3] * sc)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+  } else if (rin) {
+    const size_t o = bh * N + row;
+    if constexpr (MODE == SB_ROW) {
+      p.out0[o] = rok ? mrun : 0.0f;                       // m
+      p.out1[o] = rok ? s0 : 0.0f;                         // R
+      p.out2[o] = rok ? s1 / (s0 + 1e-6f) : 0.0f;          // D
+    } else if constexpr (MODE == SB_COL) {
+      p.out0[o] = rok ? s0 : 0.0f;                         // c
+      p.out1[o] = rok ? s1 : 0.0f;                         // g_v
+    } else {
+      p.out0[o] = rok ? s0 * (p.rv[1] != nullptr ? rv[1] : 1.0f) : 0.0f;
+    }
+  }
+  (void)err;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
+template <int MODE, int D>
+static cudaError_t launch_sb_md(const StreamBwdParams& p, cudaStream_t st) {
+  using Cfg = SBCfg<MODE, D>;
+  auto kern = stream_bwd_kernel<MODE, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+  if (e != cudaSuccess) return e;
+  const int nrb = (p.row_end - p.row_begin + 127) / 128;
+  kern<<<p.B * p.H * nrb, kBThreads, Cfg::SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D>
+static cudaError_t launch_sb_d(int mode, const StreamBwdParams& p, cudaStream_t st) {
+  switch (mode) {
+    case SB_ROW: return launch_sb_md<SB_ROW, D>(p, st);
+    case SB_COL: return launch_sb_md<SB_COL, D>(p, st);
+    case SB_MATVEC: return launch_sb_md<SB_MATVEC, D>(p, st);
+    case SB_DQ: return launch_sb_md<SB_DQ, D>(p, st);
+    default: return launch_sb_md<SB_DKV, D>(p, st);
+  }
+}
+
+cudaError_t launch_stream_bwd_pass(int mode, int d, const StreamBwdParams& p, cudaStream_t st) {
+  if (p.row_end <= p.row_begin) return cudaSuccess;
+  if (d == 32) return launch_sb_d<32>(mode, p, st);
+  if (d == 64) return launch_sb_d<64>(mode, p, st);
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------- vector steps
+// Workspace slots (each (BH, N) fp32) and per-problem scalars.
+enum {
+  WS_F = 0, WS_G, WS_M, WS_R, WS_D, WS_FM, WS_INVR, WS_C, WS_GV, WS_D1I, WS_B1, WS_D2, WS_D2I,
+  WS_X2, WS_R2, WS_P2, WS_S2, WS_U2, WS_W2, WS_T, WS_S, WS_W1, WS_NUM
+};
+enum { SC_GAM = 0, SC_ALPHA, SC_BETA, SC_TOL2, SC_RR, SC_NUM = 8 };
+
+constexpr int kVThreads = 256;
+
+struct VecParams {
+  float* ws;
+  float* sc;        // (BH, SC_NUM)
+  int32_t* done;    // (BH)
+  int32_t* iters;   // (BH)
+  const float* eps;
+  const float* mask;
+  const float* log_u;
+  const float* log_v;
+  float* dlog_mu;
+  float* dlog_nu;
+  int32_t* cg_iters;
+  float* cg_residual;
+  int32_t* status;
+  float lam, rtol, atol;
+  int B, H, N, max_iter;
+};
+
+DFS_DEV bool pos_ok(const VecParams& p, int bb, int i) {
+  return i < p.N && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * p.N + i] != 0.0f);
+}
+
+// deterministic block sums of up to 3 values (fixed order)
+DFS_DEV void block_sum3(float& a, float& b, float& c, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  c = warp_sum(c);
+  __syncthreads();
+  if (lane == 0) {
+    red[warp] = a;
+    red[8 + warp] = b;
+    red[16 + warp] = c;
+  }
+  __syncthreads();
+  a = b = c = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kVThreads / 32; ++w) {
+    a += red[w];
+    b += red[8 + w];
+    c += red[16 + w];
+  }
+}
+
+// phase 0: potentials into log2 units (elementwise over BH N)
+__global__ void sb_prep_kernel(VecParams p) {
+  const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int pos = static_cast<int>(i % p.N), prob = static_cast<int>(i / p.N), bb = prob / p.H;
+  const bool ok = pos_ok(p, bb, pos);
+  p.ws[WS_F * n + i] = ok ? p.log_u[i] * kLog2e : 0.0f;
+  p.ws[WS_G * n + i] = ok ? p.log_v[i] * kLog2e : 0.0f;
+}
+
+// after SB_ROW: f - m, 1/(R + 1e-6), the row block d1 = r/kappa (r = R 2^m) and
+// b1 = dL/df = rowsum(E) = D (1 - R/(R + 1e-6))
+__global__ void sb_rowderive_kernel(VecParams p) {
+  const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int pos = static_cast<int>(i % p.N), prob = static_cast<int>(i / p.N), bb = prob / p.H, hh = prob % p.H;
+  const float eps_h = p.eps[hh];
+  const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
+  const bool ok = pos_ok(p, bb, pos);
+  const float m = p.ws[WS_M * n + i], R = p.ws[WS_R * n + i], D = p.ws[WS_D * n + i];
+  const float inv = 1.0f / (R + 1e-6f);
+  const float r = R * ex2(m);
+  p.ws[WS_FM * n + i] = ok ? p.ws[WS_F * n + i] - m : 0.0f;
+  p.ws[WS_INVR * n + i] = ok ? inv : 0.0f;
+  p.ws[WS_D1I * n + i] = (ok && r > 0.0f) ? kap / r : 0.0f;
+  p.ws[WS_B1 * n + i] = ok ? D * (1.0f - R * inv) : 0.0f;
+  p.ws[WS_T * n + i] = 0.0f;
+}
+
+// after SB_COL (one CTA per problem): d2 = c/kappa, the kappa = 1 projection of
+// the right-hand side onto the range of the singular system, and t = D1^-1 b1
+__global__ void __launch_bounds__(kVThreads) sb_setup_kernel(VecParams p) {
+  __shared__ float red[32];
+  const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
+  const int prob = blockIdx.x, bb = prob / p.H, hh = prob % p.H, N = p.N;
+  const size_t o = static_cast<size_t>(prob) * N;
+  const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + p.eps[hh]);
+  float* ws = p.ws;
+  float sb1 = 0.0f, sb2 = 0.0f, nv = 0.0f;
+  for (int i = threadIdx.x; i < N; i += kVThreads) {
+    const bool ok = pos_ok(p, bb, i);
+    const float c = ws[WS_C * n + o + i];
+    const float d2 = (ok && c > 0.0f) ? c / kap : 0.0f;
+    ws[WS_D2 * n + o + i] = d2;
+    ws[WS_D2I * n + o + i] = d2 > 0.0f ? 1.0f / d2 : 0.0f;
+    const float b2 = ok ? ws[WS_GV * n + o + i] : 0.0f;
+    ws[WS_GV * n + o + i] = b2;
+    sb1 += ws[WS_B1 * n + o + i];
+    sb2 += b2;
+    nv += ok ? 1.0f : 0.0f;
+  }
+  block_sum3(sb1, sb2, nv, red);
+  const float sh = (kap >= 1.0f && nv > 0.0f) ? (sb1 - sb2) / (2.0f * nv) : 0.0f;
+  for (int i = threadIdx.x; i < N; i += kVThreads) {
+    const bool ok = pos_ok(p, bb, i);
+    const float b1 = ok ? ws[WS_B1 * n + o + i] - sh : 0.0f;
+    ws[WS_B1 * n + o + i] = b1;
+    ws[WS_GV * n + o + i] = ok ? ws[WS_GV * n + o + i] + sh : 0.0f;
+    ws[WS_T * n + o + i] = ws[WS_D1I * n + o + i] * b1;
+  }
+  if (threadIdx.x == 0) {
+    p.done[prob] = 0;
+    p.iters[prob] = 0;
+  }
+}
+
+// after s = P^T D1^-1 b1: the reduced right-hand side r2 = b2 - s; x2 = 0; u2 = D2^-1 r2
+__global__ void sb_cginit_kernel(VecParams p) {
+  const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int pos = static_cast<int>(i % p.N), prob = static_cast<int>(i / p.N), bb = prob / p.H;
+  const bool ok = pos_ok(p, bb, pos);
+  const float r2 = ok ? p.ws[WS_GV * n + i] - p.ws[WS_S * n + i] : 0.0f;
+  p.ws[WS_R2 * n + i] = r2;
+  p.ws[WS_U2 * n + i] = r2 * p.ws[WS_D2I * n + i];
+  p.ws[WS_X2 * n + i] = 0.0f;
+  p.ws[WS_P2 * n + i] = 0.0f;
+  p.ws[WS_S2 * n + i] = 0.0f;
+}
+
+// One Chronopoulos-Gear step (one CTA per problem), after s = P^T D1^-1 P u2:
+// w2 = D2 u2 - s, the dots (r,u), (w,u), (r,r), the convergence test and the
+// scalars, then the vector updates for the next product (same recurrence as
+// the resident backward).
+__global__ void __launch_bounds__(kVThreads) sb_cgstep_kernel(VecParams p, int first) {
+  __shared__ float red[32];
+  const int prob = blockIdx.x;
+  if (p.done[prob]) return;
+  const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
+  const int bb = prob / p.H, N = p.N;
+  const size_t o = static_cast<size_t>(prob) * N;
+  float* ws = p.ws;
+  float* sc = p.sc + static_cast<size_t>(prob) * SC_NUM;
+  float ru = 0.0f, wu = 0.0f, rr = 0.0f;
+  for (int i = threadIdx.x; i < N; i += kVThreads) {
+    const bool ok = pos_ok(p, bb, i);
+    const float u = ws[WS_U2 * n + o + i];
+    const float w = ok ? ws[WS_D2 * n + o + i] * u - ws[WS_S * n + o + i] : 0.0f;
+    ws[WS_W2 * n + o + i] = w;
+    const float r = ws[WS_R2 * n + o + i];
+    ru += r * u;
+    wu += w * u;
+    rr += r * r;
+  }
+  block_sum3(ru, wu, rr, red);
+  float gam = sc[SC_GAM], alpha = sc[SC_ALPHA], beta = sc[SC_BETA];
+  int result = 0;  // 0: continue, 1: converged, 2: stopped unconverged (cap or breakdown)
+  if (first) {
+    const float nrm0 = sqrtf(fmaxf(rr, 0.0f));
+    const float tol = fmaxf(p.atol, p.rtol * nrm0);
+    if (threadIdx.x == 0) sc[SC_TOL2] = tol * tol;
+    if (!(nrm0 > tol)) result = 1;
+    else if (!(wu > 0.0f) || p.max_iter <= 0) result = 2;
+    gam = ru;
+    alpha = wu > 0.0f ? ru / wu : 0.0f;
+    beta = 0.0f;
+  } else {
+    const int it = p.iters[prob] + 1;
+    if (threadIdx.x == 0) p.iters[prob] = it;
+    if (rr <= sc[SC_TOL2]) {
+      result = 1;
+    } else {
+      beta = ru / gam;
+      const float den = wu - beta * ru / alpha;
+      if (!(den > 0.0f) || !(den < 3.0e38f) || it >= p.max_iter) {
+        result = 2;
+      } else {
+        alpha = ru / den;
+        gam = ru;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    sc[SC_GAM] = gam;
+    sc[SC_ALPHA] = alpha;
+    sc[SC_BETA] = beta;
+    sc[SC_RR] = rr;
+    if (result) p.done[prob] = result;
+  }
+  const bool stop = result != 0;
+  if (stop) return;
+  for (int i = threadIdx.x; i < N; i += kVThreads) {
+    const float pp = ws[WS_U2 * n + o + i] + beta * ws[WS_P2 * n + o + i];
+    const float ss = ws[WS_W2 * n + o + i] + beta * ws[WS_S2 * n + o + i];
+    ws[WS_P2 * n + o + i] = pp;
+    ws[WS_S2 * n + o + i] = ss;
+    ws[WS_X2 * n + o + i] += alpha * pp;
+    const float r = ws[WS_R2 * n + o + i] - alpha * ss;
+    ws[WS_R2 * n + o + i] = r;
+    ws[WS_U2 * n + o + i] = r * ws[WS_D2I * n + o + i];
+  }
+}
+
+// After q = P x2 (in WS_S): w1 = D1^-1 (b1 - q); for kappa = 1 the null-space
+// shift t = -sum(r w1)/sum(r); marginal gradients; CG report (one CTA per problem).
+__global__ void __launch_bounds__(kVThreads) sb_final_kernel(VecParams p) {
+  __shared__ float red[32];
+  const int prob = blockIdx.x, bb = prob / p.H, hh = prob % p.H, N = p.N;
+  const size_t n = static_cast<size_t>(p.B) * p.H * N;
+  const size_t o = static_cast<size_t>(prob) * N;
+  const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + p.eps[hh]);
+  float* ws = p.ws;
+  float srw = 0.0f, sr = 0.0f, unused = 0.0f;
+  for (int i = threadIdx.x; i < N; i += kVThreads) {
+    const bool ok = pos_ok(p, bb, i);
+    const float d1i = ws[WS_D1I * n + o + i];
+    const float w1 = ok ? d1i * (ws[WS_B1 * n + o + i] - ws[WS_S * n + o + i]) : 0.0f;
+    ws[WS_W1 * n + o + i] = w1;
+    const float r = d1i > 0.0f ? kap / d1i : 0.0f;
+    srw += r * w1;
+    sr += r;
+  }
+  block_sum3(srw, sr, unused, red);
+  const float tshift = (kap >= 1.0f && sr > 0.0f) ? -srw / sr : 0.0f;
+  for (int i = threadIdx.x; i < N; i += kVThreads) {
+    const bool ok = pos_ok(p, bb, i);
+    const float d1i = ws[WS_D1I * n + o + i];
+    const float r = d1i > 0.0f ? kap / d1i : 0.0f;
+    if (p.dlog_mu) p.dlog_mu[o + i] = ok ? r * (ws[WS_W1 * n + o + i] + tshift) : 0.0f;
+    if (p.dlog_nu) p.dlog_nu[o + i] = ok ? ws[WS_C * n + o + i] * (ws[WS_X2 * n + o + i] - tshift) : 0.0f;
+  }
+  if (threadIdx.x == 0) {
+    if (p.cg_iters) p.cg_iters[prob] = p.iters[prob];
+    if (p.cg_residual) p.cg_residual[prob] = sqrtf(fmaxf(p.sc[static_cast<size_t>(prob) * SC_NUM + SC_RR], 0.0f));
+    if (p.done[prob] != 1 && p.status) atomicOr(p.status, DFS_WARN_CG_NOT_CONVERGED);
+  }
+}
+
+size_t stream_bwd_workspace(int B, int H, int N) {
+  const size_t n = static_cast<size_t>(B) * H * N, bh = static_cast<size_t>(B) * H;
+  return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256;
+}
+
+cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) {
+  const int B = bp.B, H = bp.H, N = bp.N, d = bp.d;
+  const size_t n = static_cast<size_t>(B) * H * N, nbh = static_cast<size_t>(B) * H;
+  VecParams v{};
+  v.ws = wsp;
+  v.sc = wsp + WS_NUM * n;
+  v.done = reinterpret_cast<int32_t*>(v.sc + SC_NUM * nbh);
+  v.iters = v.done + nbh;
+  v.eps = bp.eps;
+  v.mask = bp.mask;
+  v.log_u = bp.log_u;
+  v.log_v = bp.log_v;
+  v.dlog_mu = bp.dlog_mu;
+  v.dlog_nu = bp.dlog_nu;
+  v.cg_iters = bp.cg_iters;
+  v.cg_residual = bp.cg_residual;
+  v.status = bp.status;
+  v.lam = bp.lam;
+  v.rtol = bp.cg_rtol;
+  v.atol = bp.cg_atol;
+  v.B = B;
+  v.H = H;
+  v.N = N;
+  v.max_iter = bp.cg_max_iter;
+  float* ws = wsp;
+  auto slot = [&](int k) { return ws + static_cast<size_t>(k) * n; };
+  const unsigned eblocks = static_cast<unsigned>((n + 255) / 256);
+  cudaError_t e;
+#define DFS_TRY(x)                  \
+  if ((e = (x)) != cudaSuccess) return e
+  sb_prep_kernel<<<eblocks, 256, 0, st>>>(v);
+  DFS_TRY(cudaGetLastError());
+
+  StreamBwdParams base{};
+  base.dtype = bp.in_dtype;
+  base.eps = bp.eps;
+  base.mask = bp.mask;
+  base.B = B;
+  base.H = H;
+  base.N = N;
+  base.row_begin = 0;
+  base.row_end = N;
+
+  // ---- row statistics: m, R, D
+  StreamBwdParams q = base;
+  q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V;
+  q.tv[0] = slot(WS_G);
+  q.rv[0] = slot(WS_F);
+  q.xvec = bp.dxc ? bp.x_res : nullptr; q.xvec_per_head = 0;
+  q.rxvec = bp.dxc; q.rxvec_per_head = 1;
+  q.out0 = slot(WS_M); q.out1 = slot(WS_R); q.out2 = slot(WS_D);
+  DFS_TRY(launch_stream_bwd_pass(SB_ROW, d, q, st));
+  sb_rowderive_kernel<<<eblocks, 256, 0, st>>>(v);
+  DFS_TRY(cudaGetLastError());
+
+  // ---- column sums: c, g_v
+  q = base;
+  q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
+  q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);
+  q.rv[0] = slot(WS_G);
+  q.xvec = bp.dxc; q.xvec_per_head = 1;
+  q.rxvec = bp.dxc ? bp.x_res : nullptr; q.rxvec_per_head = 0;
+  q.out0 = slot(WS_C); q.out1 = slot(WS_GV);
+  DFS_TRY(launch_stream_bwd_pass(SB_COL, d, q, st));
+  sb_setup_kernel<<<static_cast<unsigned>(nbh), kVThreads, 0, st>>>(v);
+  DFS_TRY(cudaGetLastError());
+
+  // matrix-free products with the plan: P x (rows, scaled by D1^-1) and P^T t
+  auto p_rows = [&](const float* xcol, float* out, const float* rowscale, const int32_t* done) {
+    StreamBwdParams m = base;
+    m.Aop = bp.Q; m.Bop = bp.K;
+    m.tv[0] = slot(WS_G); m.tv[1] = xcol;
+    m.rv[0] = slot(WS_F); m.rv[1] = rowscale;
+    m.done = done;
+    m.out0 = out;
+    return launch_stream_bwd_pass(SB_MATVEC, d, m, st);
+  };
+  auto pt_cols = [&](const float* trow, float* out, const int32_t* done) {
+    StreamBwdParams m = base;
+    m.Aop = bp.K; m.Bop = bp.Q;
+    m.tv[0] = slot(WS_F); m.tv[1] = trow;
+    m.rv[0] = slot(WS_G);
+    m.done = done;
+    m.out0 = out;
+    return launch_stream_bwd_pass(SB_MATVEC, d, m, st);
+  };
+
+  // ---- Schur-complement CG (D2 preconditioner), Chronopoulos-Gear form
+  DFS_TRY(pt_cols(slot(WS_T), slot(WS_S), nullptr));  // s = P^T D1^-1 b1
+  sb_cginit_kernel<<<eblocks, 256, 0, st>>>(v);
+  DFS_TRY(cudaGetLastError());
+  for (int it = 0; it <= bp.cg_max_iter; ++it) {
+    DFS_TRY(p_rows(slot(WS_U2), slot(WS_T), slot(WS_D1I), v.done));  // t = D1^-1 P u2
+    DFS_TRY(pt_cols(slot(WS_T), slot(WS_S), v.done));                // s = P^T t
+    sb_cgstep_kernel<<<static_cast<unsigned>(nbh), kVThreads, 0, st>>>(v, it == 0 ? 1 : 0);
+    DFS_TRY(cudaGetLastError());
+  }
+
+  // ---- back-substitution w1 = D1^-1 (b1 - P x2), marginal gradients
+  DFS_TRY(p_rows(slot(WS_X2), slot(WS_S), nullptr, nullptr));
+  sb_final_kernel<<<static_cast<unsigned>(nbh), kVThreads, 0, st>>>(v);
+  DFS_TRY(cudaGetLastError());
+
+  // ---- dQ = dS K, then dK = dS^T Q and dV = T_norm^T dO (dQ, dK scaled by 1/(eps_h sqrt d))
+  for (int pass = 0; pass < 2; ++pass) {
+    q = base;
+    if (pass == 0) {
+      q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V; q.B3op = bp.K;
+      q.tv[0] = slot(WS_G); q.tv[1] = slot(WS_X2);
+      q.rv[0] = slot(WS_F); q.rv[1] = slot(WS_FM); q.rv[2] = slot(WS_INVR); q.rv[3] = slot(WS_D);
+      q.rv[4] = slot(WS_W1);
+      q.xvec = bp.dxc ? bp.x_res : nullptr; q.xvec_per_head = 0;
+      q.rxvec = bp.dxc; q.rxvec_per_head = 1;
+      q.acc0 = bp.dQ;
+    } else {
+      q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
+      q.B3op = bp.Q; q.B4op = bp.dO; q.b4_f32 = 1;
+      q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);
+      q.tv[4] = slot(WS_W1);
+      q.rv[0] = slot(WS_G); q.rv[1] = slot(WS_X2);
+      q.xvec = bp.dxc; q.xvec_per_head = 1;
+      q.rxvec = bp.dxc ? bp.x_res : nullptr; q.rxvec_per_head = 0;
+      q.acc0 = bp.dK;
+      q.acc1 = bp.dV;
+    }
+    q.acc_scale0 = -1.0f;  // negative: 1/(eps_h sqrt d) of the problem's head
+    q.acc_scale1 = 1.0f;
+    DFS_TRY(launch_stream_bwd_pass(pass == 0 ? SB_DQ : SB_DKV, d, q, st));
+  }
+#undef DFS_TRY
+  return cudaSuccess;
+}
+
+}  // namespace dfs

@@ -64,3 +64,41 @@ def test_stream_single_iteration_and_warm_start():
     """K = 1 from a warm start: exactly one row and one column half-update."""
     inp = make_inputs(1, 1, 640, 64, seed=8, eps=1.0)
     check_forward(inp, 1, float("inf"))
+
+
+# ---------------------------------------------------------------- backward
+from test_gpu_backward import check, grads  # noqa: E402
+from helpers import rel_err  # noqa: E402
+
+
+def test_stream_backward_d64_balanced():
+    """Config 3 shapes, balanced: IFT/Schur-CG gradients vs the oracle's unrolled gradient."""
+    inp = make_inputs(1, 2, 1024, 64, seed=11, eps=0.5)
+    g = grads(inp, 60, float("inf"))
+    _, ref = oracle_run(inp, 60, float("inf"))
+    check(g, ref)
+
+
+def test_stream_backward_padded_unbalanced_marginals():
+    """Padded variable lengths, non-uniform marginals, kappa < 1, marginal gradients too."""
+    inp = make_inputs(2, 2, 640, 64, seed=12, eps=0.5, uniform=False, lengths=[640, 301])
+    g = grads(inp, 40, 1.0, want_marg=True)
+    _, ref = oracle_run(inp, 40, 1.0)
+    check(g, ref)
+    for k in ("dlog_mu", "dlog_nu"):
+        assert rel_err(g[k], ref[k]) <= 2e-2, k
+
+
+def test_stream_backward_d32_ragged():
+    inp = make_inputs(1, 2, 520, 32, seed=13, eps=1.0)
+    g = grads(inp, 30, float("inf"))
+    _, ref = oracle_run(inp, 30, float("inf"))
+    check(g, ref)
+
+
+def test_stream_backward_unconverged_matches_ift():
+    """Few iterations: the kernel returns the fixed-point (IFT) gradient at those potentials."""
+    inp = make_inputs(1, 1, 512, 64, seed=14, eps=1.0)
+    g = grads(inp, 3, 1.0)
+    _, ref = oracle_run(inp, 3, 1.0, grad_mode="ift")
+    check(g, ref)
