@@ -22,7 +22,8 @@ CSRC_DIR = os.path.join(ROOT_DIR, "csrc")
 INCLUDE_DIR = os.path.join(os.path.dirname(ROOT_DIR), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libdfsink.so")
-SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_stream.cu", "dfs_stream_bwd.cu", "dfs_selftest.cu"]
+SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_stream.cu", "dfs_stream_bwd.cu", "dfs_selftest.cu",
+           "dfs_noalloc.cu"]
 HEADERS = ["dfs_device.cuh", "dfs_kernels.cuh", "dfs_slab.cuh"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -71,7 +72,10 @@ class DfsBwdArgs(ctypes.Structure):
 
 
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
-                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma")
+                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static")
+
+# fixed device scratch behind dfs_fwd_static (DFS_STATIC_SCRATCH_BYTES in include/dfsink.h)
+DFS_STATIC_SCRATCH_BYTES = 16 << 20
 
 _lock = threading.RLock()  # ext() loads lib() while holding it
 _lib = None
@@ -178,6 +182,8 @@ def lib() -> ctypes.CDLL:
             L.dfs_bwd.restype = ctypes.c_int
             L.dfs_bwd.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsCgParams),
                                   ctypes.POINTER(DfsBwdArgs), _P, ctypes.c_size_t, _P]
+            L.dfs_fwd_static.restype = ctypes.c_int
+            L.dfs_fwd_static.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs), _P]
             L.dfs_selftest_mma.restype = ctypes.c_int
             L.dfs_selftest_mma.argtypes = [ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, _P]

@@ -158,6 +158,28 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace,
 int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a,
             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the library's fixed device scratch used by dfs_fwd_static: 16 MiB,
+ * i.e. streamed problems with B*H*N up to 1,048,576 (the forward needs
+ * 16 bytes of workspace per (batch, head, point)). */
+#define DFS_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* Forward for callers that cannot allocate device memory.  No counterpart in
+ * the reference.  Same arguments and results as dfs_fwd, but the workspace the
+ * streamed kernels need is a fixed DFS_STATIC_SCRATCH_BYTES array of device
+ * memory that the library itself holds (on every GPU that loads it, until the
+ * process exits), so the call allocates nothing.  It serves callers that only
+ * receive their buffers from another runtime or framework and have no
+ * allocator to ask for a workspace.
+ *   - Problems whose forward workspace exceeds DFS_STATIC_SCRATCH_BYTES are
+ *     rejected with DFS_ERR_WORKSPACE before anything runs.
+ *   - The device that owns `stream` must be current.  The first call on a
+ *     device looks up the scratch's device address once (cudaGetSymbolAddress),
+ *     so make that first call before any stream capture on the device.
+ *   - All calls on a device share the one scratch: calls whose work overlaps on
+ *     the GPU (different streams with no ordering between them) race and must
+ *     be serialised by the caller.  Nothing in it needs to start at zero. */
+int dfs_fwd_static(const dfs_problem* p, const dfs_fwd_args* a, void* stream);
+
 /* Self-test of the tensor-core building blocks: runs the three tcgen05 MMA
  * operand layouts the kernels use on caller-provided data (see csrc). */
 int dfs_selftest_mma(int which, const float* A, const float* B, float* D,
