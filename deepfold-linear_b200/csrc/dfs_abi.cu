@@ -29,6 +29,90 @@ constexpr int kStreamMaxN = 1 << 16;
 bool resident(const dfs_problem* p) { return p->d == 32 && p->N <= kResidentMaxN; }
 bool streamed(const dfs_problem* p) { return (p->d == 32 || p->d == 64) && p->N <= kStreamMaxN; }
 
+FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
+  FwdParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.Q = a->Q; q.K = a->K; q.V = a->V; q.C = a->C;
+  q.x_res = a->x_res; q.pos_weight = a->pos_weight; q.pos_bins = a->pos_bins;
+  q.eps = a->eps; q.w_dist = a->w_dist; q.log_mu = a->log_mu; q.log_nu = a->log_nu;
+  q.log_u_init = a->log_u_init; q.log_v_init = a->log_v_init; q.mask = a->mask;
+  q.O = a->O; q.x_centroid = a->x_centroid; q.log_u = a->log_u; q.log_v = a->log_v;
+  q.status = a->status;
+  q.T_out = a->T_norm;
+  q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
+  q.cost_mode = p->cost_mode; q.K_iter = p->K_iter; q.check_every = p->check_every > 0 ? p->check_every : 1;
+  q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
+  return q;
+}
+
+BwdParams bwd_params(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a, void* workspace) {
+  BwdParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.Q = a->Q; q.K = a->K; q.V = a->V;
+  q.x_res = a->x_res; q.pos_weight = a->pos_weight; q.pos_bins = a->pos_bins;
+  q.eps = a->eps; q.w_dist = a->w_dist; q.log_mu = a->log_mu; q.log_nu = a->log_nu; q.mask = a->mask;
+  q.log_u = a->log_u; q.log_v = a->log_v; q.dO = a->dO; q.dxc = a->dxc;
+  q.dQ = a->dQ; q.dK = a->dK; q.dV = a->dV; q.dlog_mu = a->dlog_mu; q.dlog_nu = a->dlog_nu;
+  q.dx_res = a->dx_res; q.dpos_weight = a->dpos_weight; q.dw_dist = a->dw_dist;
+  q.cg_iters = a->cg_iters; q.cg_residual = a->cg_residual; q.status = a->status;
+  q.ws = static_cast<float*>(workspace);
+  q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
+  q.cg_max_iter = cg->max_iter; q.cg_rtol = cg->rtol; q.cg_atol = cg->atol;
+  q.lam = p->lam; q.r_0 = p->r_0;
+  return q;
+}
+
+// argument checks shared by dfs_fwd and the forward phases
+int check_fwd_args(const dfs_problem* p, const dfs_fwd_args* a) {
+  if (!dims_ok(p) || !a) return DFS_ERR_INVALID_ARGUMENT;
+  if (!a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->cost_mode == DFS_COST_QK && (!a->Q || !a->K)) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->cost_mode == DFS_COST_DENSE && !a->C) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->O && !a->V) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
+  if (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V))
+    return DFS_ERR_INVALID_ARGUMENT;
+  return DFS_OK;
+}
+
+// streamed path: QK cost with masks, marginals, kappa and warm starts; the
+// position / geometry terms, early stopping and the dense plan are resident-only
+int check_stream_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t workspace_bytes) {
+  if (p->cost_mode != DFS_COST_QK || a->pos_weight || a->w_dist || p->threshold > 0.0f || a->T_norm ||
+      (a->x_centroid && !a->O))
+    return DFS_ERR_UNSUPPORTED;
+  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
+    return DFS_ERR_WORKSPACE;
+  return DFS_OK;
+}
+
+int check_bwd_args(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a) {
+  if (!dims_ok(p) || !a || !cg) return DFS_ERR_INVALID_ARGUMENT;
+  if (p->cost_mode != DFS_COST_QK) return DFS_ERR_UNSUPPORTED;
+  if (!a->Q || !a->K || !a->V || !a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v || !a->dO)
+    return DFS_ERR_INVALID_ARGUMENT;
+  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->dxc && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
+  if (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) || !aligned16(a->dQ) ||
+      !aligned16(a->dK) || !aligned16(a->dV))
+    return DFS_ERR_INVALID_ARGUMENT;
+  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
+  return DFS_OK;
+}
+
+// streamed path: no position / geometry terms and none of their gradients
+int check_stream_bwd(const dfs_problem* p, const dfs_bwd_args* a, void* workspace, size_t workspace_bytes) {
+  if (a->pos_weight || a->w_dist || a->dx_res || a->dpos_weight || a->dw_dist) return DFS_ERR_UNSUPPORTED;
+  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
+    return DFS_ERR_WORKSPACE;
+  return DFS_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -62,38 +146,10 @@ int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_byte
 
 int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t workspace_bytes,
             void* stream) {
-  if (!dims_ok(p) || !a) return DFS_ERR_INVALID_ARGUMENT;
-  if (!a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v) return DFS_ERR_INVALID_ARGUMENT;
-  if (p->cost_mode == DFS_COST_QK && (!a->Q || !a->K)) return DFS_ERR_INVALID_ARGUMENT;
-  if (p->cost_mode == DFS_COST_DENSE && !a->C) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->O && !a->V) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
-  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
-  if (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V))
-    return DFS_ERR_INVALID_ARGUMENT;
-  if (!resident(p)) {
-    // streamed path: QK cost with masks, marginals, kappa and warm starts; the
-    // position / geometry terms, early stopping and the dense plan are resident-only
-    if (p->cost_mode != DFS_COST_QK || a->pos_weight || a->w_dist || p->threshold > 0.0f || a->T_norm ||
-        (a->x_centroid && !a->O))
-      return DFS_ERR_UNSUPPORTED;
-    if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N) ||
-        !aligned16(workspace))
-      return DFS_ERR_WORKSPACE;
-  }
-  FwdParams q;
-  std::memset(&q, 0, sizeof(q));
-  q.Q = a->Q; q.K = a->K; q.V = a->V; q.C = a->C;
-  q.x_res = a->x_res; q.pos_weight = a->pos_weight; q.pos_bins = a->pos_bins;
-  q.eps = a->eps; q.w_dist = a->w_dist; q.log_mu = a->log_mu; q.log_nu = a->log_nu;
-  q.log_u_init = a->log_u_init; q.log_v_init = a->log_v_init; q.mask = a->mask;
-  q.O = a->O; q.x_centroid = a->x_centroid; q.log_u = a->log_u; q.log_v = a->log_v;
-  q.status = a->status;
-  q.T_out = a->T_norm;
-  q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
-  q.cost_mode = p->cost_mode; q.K_iter = p->K_iter; q.check_every = p->check_every > 0 ? p->check_every : 1;
-  q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
+  int rc = check_fwd_args(p, a);
+  if (rc != DFS_OK) return rc;
+  if (!resident(p) && (rc = check_stream_fwd(p, a, workspace, workspace_bytes)) != DFS_OK) return rc;
+  const FwdParams q = fwd_params(p, a);
   if (!resident(p))
     return cuda_status(launch_stream_fwd(q, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
   return cuda_status(launch_resident_fwd(q, static_cast<cudaStream_t>(stream)));
@@ -101,43 +157,37 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
 
 int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a, void* workspace,
             size_t workspace_bytes, void* stream) {
-  if (!dims_ok(p) || !a || !cg) return DFS_ERR_INVALID_ARGUMENT;
-  if (p->cost_mode != DFS_COST_QK) return DFS_ERR_UNSUPPORTED;
-  if (!a->Q || !a->K || !a->V || !a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v || !a->dO)
-    return DFS_ERR_INVALID_ARGUMENT;
-  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->dxc && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
-  if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
-  if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
-  if (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) || !aligned16(a->dQ) ||
-      !aligned16(a->dK) || !aligned16(a->dV))
-    return DFS_ERR_INVALID_ARGUMENT;
-  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
+  int rc = check_bwd_args(p, cg, a);
+  if (rc != DFS_OK) return rc;
   if (!resident(p)) {
-    // streamed path: no position / geometry terms and none of their gradients
-    if (a->pos_weight || a->w_dist || a->dx_res || a->dpos_weight || a->dw_dist) return DFS_ERR_UNSUPPORTED;
-    if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
-      return DFS_ERR_WORKSPACE;
+    if ((rc = check_stream_bwd(p, a, workspace, workspace_bytes)) != DFS_OK) return rc;
+    return cuda_status(launch_stream_bwd(bwd_params(p, cg, a, workspace), static_cast<float*>(workspace),
+                                         static_cast<cudaStream_t>(stream)));
   }
-  const size_t need = resident(p) ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : 0;
+  const size_t need = resident_bwd_workspace(p->B, p->H, p->N, p->d);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return DFS_ERR_WORKSPACE;
-  BwdParams q;
-  std::memset(&q, 0, sizeof(q));
-  q.Q = a->Q; q.K = a->K; q.V = a->V;
-  q.x_res = a->x_res; q.pos_weight = a->pos_weight; q.pos_bins = a->pos_bins;
-  q.eps = a->eps; q.w_dist = a->w_dist; q.log_mu = a->log_mu; q.log_nu = a->log_nu; q.mask = a->mask;
-  q.log_u = a->log_u; q.log_v = a->log_v; q.dO = a->dO; q.dxc = a->dxc;
-  q.dQ = a->dQ; q.dK = a->dK; q.dV = a->dV; q.dlog_mu = a->dlog_mu; q.dlog_nu = a->dlog_nu;
-  q.dx_res = a->dx_res; q.dpos_weight = a->dpos_weight; q.dw_dist = a->dw_dist;
-  q.cg_iters = a->cg_iters; q.cg_residual = a->cg_residual; q.status = a->status;
-  q.ws = static_cast<float*>(workspace);
-  q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
-  q.cg_max_iter = cg->max_iter; q.cg_rtol = cg->rtol; q.cg_atol = cg->atol;
-  q.lam = p->lam; q.r_0 = p->r_0;
-  if (!resident(p))
-    return cuda_status(launch_stream_bwd(q, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
-  return cuda_status(launch_resident_bwd(q, static_cast<cudaStream_t>(stream)));
+  return cuda_status(launch_resident_bwd(bwd_params(p, cg, a, workspace), static_cast<cudaStream_t>(stream)));
+}
+
+int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const dfs_fwd_args* fa,
+                  const dfs_bwd_args* ba, int row_begin, int row_end, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  if (!dims_ok(p) || !streamed(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  if (row_begin < 0 || row_end < row_begin || row_end > p->N) return DFS_ERR_INVALID_ARGUMENT;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (op >= DFS_OP_FWD_INIT && op <= DFS_OP_FWD_OUT) {
+    if ((rc = check_fwd_args(p, fa)) != DFS_OK) return rc;
+    if ((rc = check_stream_fwd(p, fa, workspace, workspace_bytes)) != DFS_OK) return rc;
+    return cuda_status(stream_fwd_op(op, fwd_params(p, fa), static_cast<float*>(workspace), row_begin, row_end, st));
+  }
+  if (op >= DFS_OP_BWD_PREP && op <= DFS_OP_BWD_DKV) {
+    if ((rc = check_bwd_args(p, cg, ba)) != DFS_OK) return rc;
+    if ((rc = check_stream_bwd(p, ba, workspace, workspace_bytes)) != DFS_OK) return rc;
+    return cuda_status(
+        stream_bwd_op(op, bwd_params(p, cg, ba, workspace), static_cast<float*>(workspace), row_begin, row_end, st));
+  }
+  return DFS_ERR_INVALID_ARGUMENT;
 }
 
 int dfs_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K, void* stream) {

@@ -83,6 +83,8 @@ struct BwdParams {
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
 size_t resident_fwd_smem(int N, int d);
 cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
+cudaError_t stream_fwd_op(int op, const FwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
+cudaError_t stream_bwd_op(int op, const BwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
 size_t stream_fwd_workspace(int B, int H, int N);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
 cudaError_t launch_stream_bwd(const BwdParams& p, float* ws, cudaStream_t st);

@@ -283,10 +283,14 @@ __global__ void __launch_bounds__(kSThreads) stream_kernel(const StreamParams p)
   if (warp == 0) tmem_dealloc(tbase, 256);
 }
 
-// initial potentials (log2 units) from an optional natural-log warm start
-__global__ void stream_init_kernel(float* out, const float* init, size_t n) {
+// initial potentials from an optional natural-log warm start: log2 units into
+// the workspace, natural units into the output (so K_iter = 0 returns them)
+__global__ void stream_init_kernel(float* out2, float* out_nat, const float* init, size_t n) {
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) out[i] = init ? init[i] * kLog2e : 0.0f;
+  if (i >= n) return;
+  const float v = init ? init[i] : 0.0f;
+  out2[i] = v * kLog2e;
+  out_nat[i] = v;
 }
 
 template <int MODE, int D>
@@ -319,19 +323,26 @@ size_t stream_fwd_workspace(int B, int H, int N) {
   return 4 * sizeof(float) * static_cast<size_t>(B) * H * N;  // f, g (log2), m, R
 }
 
-// Full streamed forward: K_iter x (row half-update, column half-update), then
-// the transport output.  Workspace: f, g (log2 units), m, R, each (BH, N) fp32.
-cudaError_t launch_stream_fwd(const FwdParams& fp, float* ws, cudaStream_t st) {
+// One phase of the streamed forward on rows [r0, r1) (the whole problem for a
+// single GPU; a row range per GPU when the rows are sharded, with the
+// potentials all-gathered between phases).  Workspace slots, (BH, N) fp32 each:
+// f, g (log2 units), m, R.
+//   FWD_INIT  f, g (and log_u, log_v) from the warm starts, all positions
+//   FWD_ROWS  f = kappa (a - LSE_j(S' + g)) for rows [r0, r1); also log_u there
+//   FWD_COLS  g = kappa (b - LSE_i(S' + f)) for columns [r0, r1); also log_v there
+//   FWD_OUT   row statistics, O and x_centroid for rows [r0, r1)
+cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1, cudaStream_t st) {
   const size_t n = static_cast<size_t>(fp.B) * fp.H * fp.N;
   float* fw = ws;
   float* gw = ws + n;
   float* mw = ws + 2 * n;
   float* Rw = ws + 3 * n;
-  const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
-  stream_init_kernel<<<blocks, 256, 0, st>>>(fw, fp.log_u_init, n);
-  stream_init_kernel<<<blocks, 256, 0, st>>>(gw, fp.log_v_init, n);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  if (op == DFS_OP_FWD_INIT) {
+    const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
+    stream_init_kernel<<<blocks, 256, 0, st>>>(fw, fp.log_u, fp.log_u_init, n);
+    stream_init_kernel<<<blocks, 256, 0, st>>>(gw, fp.log_v, fp.log_v_init, n);
+    return cudaGetLastError();
+  }
   StreamParams p{};
   p.dtype = fp.in_dtype;
   p.eps = fp.eps;
@@ -339,55 +350,57 @@ cudaError_t launch_stream_fwd(const FwdParams& fp, float* ws, cudaStream_t st) {
   p.B = fp.B;
   p.H = fp.H;
   p.N = fp.N;
-  p.row_begin = 0;
-  p.row_end = fp.N;
+  p.row_begin = r0;
+  p.row_end = r1;
   p.lam = fp.lam;
-  for (int it = 0; it < fp.K_iter; ++it) {
-    const bool last = it + 1 == fp.K_iter;
-    // rows: f = kappa (a - LSE_j(S' + g))
+  if (op == DFS_OP_FWD_ROWS) {
     p.Aop = fp.Q;
     p.Bop = fp.K;
     p.col_bias = gw;
     p.row_marg = fp.log_mu;
     p.row_out = fw;
-    p.row_out_nat = last ? fp.log_u : nullptr;
-    if ((e = launch_stream(SM_LSE, fp.d, p, st)) != cudaSuccess) return e;
-    // columns: g = kappa (b - LSE_i(S' + f)), the same kernel on S^T = K Q^T
+    p.row_out_nat = fp.log_u;
+    return launch_stream(SM_LSE, fp.d, p, st);
+  }
+  if (op == DFS_OP_FWD_COLS) {  // the same kernel on S^T = K Q^T
     p.Aop = fp.K;
     p.Bop = fp.Q;
     p.col_bias = fw;
     p.row_marg = fp.log_nu;
     p.row_out = gw;
-    p.row_out_nat = last ? fp.log_v : nullptr;
-    if ((e = launch_stream(SM_LSE, fp.d, p, st)) != cudaSuccess) return e;
+    p.row_out_nat = fp.log_v;
+    return launch_stream(SM_LSE, fp.d, p, st);
   }
-  if (fp.K_iter <= 0) {  // potentials are the warm start
-    if (fp.log_u_init)
-      cudaMemcpyAsync(fp.log_u, fp.log_u_init, n * sizeof(float), cudaMemcpyDeviceToDevice, st);
-    else
-      cudaMemsetAsync(fp.log_u, 0, n * sizeof(float), st);
-    if (fp.log_v_init)
-      cudaMemcpyAsync(fp.log_v, fp.log_v_init, n * sizeof(float), cudaMemcpyDeviceToDevice, st);
-    else
-      cudaMemsetAsync(fp.log_v, 0, n * sizeof(float), st);
-  }
-  if (fp.O != nullptr || fp.x_centroid != nullptr) {
+  if (op == DFS_OP_FWD_OUT) {
+    if (fp.O == nullptr) return cudaSuccess;
     p.Aop = fp.Q;
     p.Bop = fp.K;
     p.col_bias = gw;
     p.row_bias = fw;
     p.row_out = mw;
     p.row_R = Rw;
-    if ((e = launch_stream(SM_ROWSTATS, fp.d, p, st)) != cudaSuccess) return e;
+    cudaError_t e = launch_stream(SM_ROWSTATS, fp.d, p, st);
+    if (e != cudaSuccess) return e;
     p.Vop = fp.V;
     p.row_m = mw;
     p.O = fp.O;
     p.x_res = fp.x_res;
     p.x_centroid = fp.x_centroid;
-    if (fp.O == nullptr) return cudaErrorInvalidValue;  // the output pass always writes O
-    if ((e = launch_stream(SM_OUT, fp.d, p, st)) != cudaSuccess) return e;
+    return launch_stream(SM_OUT, fp.d, p, st);
   }
-  return cudaSuccess;
+  return cudaErrorInvalidValue;
+}
+
+// Full streamed forward on one GPU: K_iter x (row half-update, column
+// half-update), then the transport output.
+cudaError_t launch_stream_fwd(const FwdParams& fp, float* ws, cudaStream_t st) {
+  cudaError_t e = stream_fwd_op(DFS_OP_FWD_INIT, fp, ws, 0, fp.N, st);
+  for (int it = 0; e == cudaSuccess && it < fp.K_iter; ++it) {
+    e = stream_fwd_op(DFS_OP_FWD_ROWS, fp, ws, 0, fp.N, st);
+    if (e == cudaSuccess) e = stream_fwd_op(DFS_OP_FWD_COLS, fp, ws, 0, fp.N, st);
+  }
+  if (e == cudaSuccess) e = stream_fwd_op(DFS_OP_FWD_OUT, fp, ws, 0, fp.N, st);
+  return e;
 }
 
 }  // namespace dfs

@@ -619,7 +619,30 @@ size_t stream_bwd_workspace(int B, int H, int N) {
   return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256;
 }
 
-cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) {
+static_assert(WS_F == DFS_WS_BWD_F && WS_G == DFS_WS_BWD_G && WS_M == DFS_WS_BWD_M && WS_R == DFS_WS_BWD_R &&
+                  WS_D == DFS_WS_BWD_D && WS_C == DFS_WS_BWD_C && WS_GV == DFS_WS_BWD_GV && WS_T == DFS_WS_BWD_T &&
+                  WS_S == DFS_WS_BWD_S && WS_NUM == DFS_WS_BWD_NSLOTS && SC_NUM == DFS_WS_BWD_NSCALARS,
+              "workspace slots named in include/dfsink.h");
+
+// One phase of the streamed backward on rows (or, for the column phases,
+// columns) [r0, r1): the whole problem on a single GPU, a range per GPU when
+// rows are sharded.  Phases without a range work on every position, from the
+// all-gathered vectors.  The order, and the vectors each range phase produces
+// (which a sharded run all-gathers before the next phase):
+//   BWD_PREP                     f, g in log2 units
+//   BWD_ROWSTATS   rows          m, R, D
+//   BWD_ROWDERIVE                f - m, 1/(R+1e-6), D1^-1, b1
+//   BWD_COLSTATS   columns       c, g_v
+//   BWD_SETUP                    D2, kappa = 1 projection, t = D1^-1 b1
+//   BWD_PT_T       columns       s = P^T t
+//   BWD_CGINIT                   reduced right-hand side, u2
+//   then (max_iter + 1) x { BWD_P_U rows: t = D1^-1 P u2;  BWD_PT_T columns: s = P^T t;
+//                           BWD_CGSTEP_FIRST (first time) / BWD_CGSTEP }
+//   BWD_P_X        rows          s = P x2
+//   BWD_FINAL                    w1, null-space shift, dlog_mu, dlog_nu, CG report
+//   BWD_DQ         rows          dQ
+//   BWD_DKV        columns       dK, dV
+cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r1, cudaStream_t st) {
   const int B = bp.B, H = bp.H, N = bp.N, d = bp.d;
   const size_t n = static_cast<size_t>(B) * H * N, nbh = static_cast<size_t>(B) * H;
   VecParams v{};
@@ -646,86 +669,69 @@ cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) 
   float* ws = wsp;
   auto slot = [&](int k) { return ws + static_cast<size_t>(k) * n; };
   const unsigned eblocks = static_cast<unsigned>((n + 255) / 256);
-  cudaError_t e;
-#define DFS_TRY(x)                  \
-  if ((e = (x)) != cudaSuccess) return e
-  sb_prep_kernel<<<eblocks, 256, 0, st>>>(v);
-  DFS_TRY(cudaGetLastError());
+  const unsigned pblocks = static_cast<unsigned>(nbh);
 
-  StreamBwdParams base{};
-  base.dtype = bp.in_dtype;
-  base.eps = bp.eps;
-  base.mask = bp.mask;
-  base.B = B;
-  base.H = H;
-  base.N = N;
-  base.row_begin = 0;
-  base.row_end = N;
-
-  // ---- row statistics: m, R, D
-  StreamBwdParams q = base;
-  q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V;
-  q.tv[0] = slot(WS_G);
-  q.rv[0] = slot(WS_F);
-  q.xvec = bp.dxc ? bp.x_res : nullptr; q.xvec_per_head = 0;
-  q.rxvec = bp.dxc; q.rxvec_per_head = 1;
-  q.out0 = slot(WS_M); q.out1 = slot(WS_R); q.out2 = slot(WS_D);
-  DFS_TRY(launch_stream_bwd_pass(SB_ROW, d, q, st));
-  sb_rowderive_kernel<<<eblocks, 256, 0, st>>>(v);
-  DFS_TRY(cudaGetLastError());
-
-  // ---- column sums: c, g_v
-  q = base;
-  q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
-  q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);
-  q.rv[0] = slot(WS_G);
-  q.xvec = bp.dxc; q.xvec_per_head = 1;
-  q.rxvec = bp.dxc ? bp.x_res : nullptr; q.rxvec_per_head = 0;
-  q.out0 = slot(WS_C); q.out1 = slot(WS_GV);
-  DFS_TRY(launch_stream_bwd_pass(SB_COL, d, q, st));
-  sb_setup_kernel<<<static_cast<unsigned>(nbh), kVThreads, 0, st>>>(v);
-  DFS_TRY(cudaGetLastError());
-
-  // matrix-free products with the plan: P x (rows, scaled by D1^-1) and P^T t
-  auto p_rows = [&](const float* xcol, float* out, const float* rowscale, const int32_t* done) {
-    StreamBwdParams m = base;
-    m.Aop = bp.Q; m.Bop = bp.K;
-    m.tv[0] = slot(WS_G); m.tv[1] = xcol;
-    m.rv[0] = slot(WS_F); m.rv[1] = rowscale;
-    m.done = done;
-    m.out0 = out;
-    return launch_stream_bwd_pass(SB_MATVEC, d, m, st);
-  };
-  auto pt_cols = [&](const float* trow, float* out, const int32_t* done) {
-    StreamBwdParams m = base;
-    m.Aop = bp.K; m.Bop = bp.Q;
-    m.tv[0] = slot(WS_F); m.tv[1] = trow;
-    m.rv[0] = slot(WS_G);
-    m.done = done;
-    m.out0 = out;
-    return launch_stream_bwd_pass(SB_MATVEC, d, m, st);
-  };
-
-  // ---- Schur-complement CG (D2 preconditioner), Chronopoulos-Gear form
-  DFS_TRY(pt_cols(slot(WS_T), slot(WS_S), nullptr));  // s = P^T D1^-1 b1
-  sb_cginit_kernel<<<eblocks, 256, 0, st>>>(v);
-  DFS_TRY(cudaGetLastError());
-  for (int it = 0; it <= bp.cg_max_iter; ++it) {
-    DFS_TRY(p_rows(slot(WS_U2), slot(WS_T), slot(WS_D1I), v.done));  // t = D1^-1 P u2
-    DFS_TRY(pt_cols(slot(WS_T), slot(WS_S), v.done));                // s = P^T t
-    sb_cgstep_kernel<<<static_cast<unsigned>(nbh), kVThreads, 0, st>>>(v, it == 0 ? 1 : 0);
-    DFS_TRY(cudaGetLastError());
-  }
-
-  // ---- back-substitution w1 = D1^-1 (b1 - P x2), marginal gradients
-  DFS_TRY(p_rows(slot(WS_X2), slot(WS_S), nullptr, nullptr));
-  sb_final_kernel<<<static_cast<unsigned>(nbh), kVThreads, 0, st>>>(v);
-  DFS_TRY(cudaGetLastError());
-
-  // ---- dQ = dS K, then dK = dS^T Q and dV = T_norm^T dO (dQ, dK scaled by 1/(eps_h sqrt d))
-  for (int pass = 0; pass < 2; ++pass) {
-    q = base;
-    if (pass == 0) {
+  StreamBwdParams q{};
+  q.dtype = bp.in_dtype;
+  q.eps = bp.eps;
+  q.mask = bp.mask;
+  q.B = B;
+  q.H = H;
+  q.N = N;
+  q.row_begin = r0;
+  q.row_end = r1;
+  switch (op) {
+    case DFS_OP_BWD_PREP:
+      sb_prep_kernel<<<eblocks, 256, 0, st>>>(v);
+      return cudaGetLastError();
+    case DFS_OP_BWD_ROWSTATS:  // m, R, D
+      q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V;
+      q.tv[0] = slot(WS_G);
+      q.rv[0] = slot(WS_F);
+      q.xvec = bp.dxc ? bp.x_res : nullptr; q.xvec_per_head = 0;
+      q.rxvec = bp.dxc; q.rxvec_per_head = 1;
+      q.out0 = slot(WS_M); q.out1 = slot(WS_R); q.out2 = slot(WS_D);
+      return launch_stream_bwd_pass(SB_ROW, d, q, st);
+    case DFS_OP_BWD_ROWDERIVE:
+      sb_rowderive_kernel<<<eblocks, 256, 0, st>>>(v);
+      return cudaGetLastError();
+    case DFS_OP_BWD_COLSTATS:  // c, g_v
+      q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
+      q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);
+      q.rv[0] = slot(WS_G);
+      q.xvec = bp.dxc; q.xvec_per_head = 1;
+      q.rxvec = bp.dxc ? bp.x_res : nullptr; q.rxvec_per_head = 0;
+      q.out0 = slot(WS_C); q.out1 = slot(WS_GV);
+      return launch_stream_bwd_pass(SB_COL, d, q, st);
+    case DFS_OP_BWD_SETUP:
+      sb_setup_kernel<<<pblocks, kVThreads, 0, st>>>(v);
+      return cudaGetLastError();
+    case DFS_OP_BWD_CGINIT:
+      sb_cginit_kernel<<<eblocks, 256, 0, st>>>(v);
+      return cudaGetLastError();
+    case DFS_OP_BWD_P_U:   // t = D1^-1 P u2 (problems whose CG has stopped are skipped)
+    case DFS_OP_BWD_P_X:   // s = P x2
+      q.Aop = bp.Q; q.Bop = bp.K;
+      q.tv[0] = slot(WS_G); q.tv[1] = slot(op == DFS_OP_BWD_P_U ? WS_U2 : WS_X2);
+      q.rv[0] = slot(WS_F); q.rv[1] = op == DFS_OP_BWD_P_U ? slot(WS_D1I) : nullptr;
+      q.done = op == DFS_OP_BWD_P_U ? v.done : nullptr;
+      q.out0 = slot(op == DFS_OP_BWD_P_U ? WS_T : WS_S);
+      return launch_stream_bwd_pass(SB_MATVEC, d, q, st);
+    case DFS_OP_BWD_PT_T:  // s = P^T t (skips stopped problems once the CG has started)
+      q.Aop = bp.K; q.Bop = bp.Q;
+      q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_T);
+      q.rv[0] = slot(WS_G);
+      q.done = v.done;
+      q.out0 = slot(WS_S);
+      return launch_stream_bwd_pass(SB_MATVEC, d, q, st);
+    case DFS_OP_BWD_CGSTEP_FIRST:
+    case DFS_OP_BWD_CGSTEP:
+      sb_cgstep_kernel<<<pblocks, kVThreads, 0, st>>>(v, op == DFS_OP_BWD_CGSTEP_FIRST ? 1 : 0);
+      return cudaGetLastError();
+    case DFS_OP_BWD_FINAL:
+      sb_final_kernel<<<pblocks, kVThreads, 0, st>>>(v);
+      return cudaGetLastError();
+    case DFS_OP_BWD_DQ:    // dQ = dS K / (eps_h sqrt d)
       q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V; q.B3op = bp.K;
       q.tv[0] = slot(WS_G); q.tv[1] = slot(WS_X2);
       q.rv[0] = slot(WS_F); q.rv[1] = slot(WS_FM); q.rv[2] = slot(WS_INVR); q.rv[3] = slot(WS_D);
@@ -733,7 +739,9 @@ cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) 
       q.xvec = bp.dxc ? bp.x_res : nullptr; q.xvec_per_head = 0;
       q.rxvec = bp.dxc; q.rxvec_per_head = 1;
       q.acc0 = bp.dQ;
-    } else {
+      q.acc_scale0 = -1.0f;  // negative: 1/(eps_h sqrt d) of the problem's head
+      return launch_stream_bwd_pass(SB_DQ, d, q, st);
+    case DFS_OP_BWD_DKV:   // dK = dS^T Q / (eps_h sqrt d), dV = T_norm^T dO
       q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
       q.B3op = bp.Q; q.B4op = bp.dO; q.b4_f32 = 1;
       q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);
@@ -743,13 +751,38 @@ cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) 
       q.rxvec = bp.dxc ? bp.x_res : nullptr; q.rxvec_per_head = 0;
       q.acc0 = bp.dK;
       q.acc1 = bp.dV;
-    }
-    q.acc_scale0 = -1.0f;  // negative: 1/(eps_h sqrt d) of the problem's head
-    q.acc_scale1 = 1.0f;
-    DFS_TRY(launch_stream_bwd_pass(pass == 0 ? SB_DQ : SB_DKV, d, q, st));
+      q.acc_scale0 = -1.0f;
+      q.acc_scale1 = 1.0f;
+      return launch_stream_bwd_pass(SB_DKV, d, q, st);
+    default:
+      return cudaErrorInvalidValue;
   }
-#undef DFS_TRY
-  return cudaSuccess;
+}
+
+// The whole streamed backward on one GPU: every phase over all rows.
+cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) {
+  const int N = bp.N;
+  cudaError_t e = cudaSuccess;
+  auto run = [&](int op) {
+    if (e == cudaSuccess) e = stream_bwd_op(op, bp, wsp, 0, N, st);
+  };
+  run(DFS_OP_BWD_PREP);
+  run(DFS_OP_BWD_ROWSTATS);
+  run(DFS_OP_BWD_ROWDERIVE);
+  run(DFS_OP_BWD_COLSTATS);
+  run(DFS_OP_BWD_SETUP);
+  run(DFS_OP_BWD_PT_T);   // s = P^T D1^-1 b1 (no problem has stopped yet)
+  run(DFS_OP_BWD_CGINIT);
+  for (int it = 0; it <= bp.cg_max_iter; ++it) {
+    run(DFS_OP_BWD_P_U);
+    run(DFS_OP_BWD_PT_T);
+    run(it == 0 ? DFS_OP_BWD_CGSTEP_FIRST : DFS_OP_BWD_CGSTEP);
+  }
+  run(DFS_OP_BWD_P_X);
+  run(DFS_OP_BWD_FINAL);
+  run(DFS_OP_BWD_DQ);
+  run(DFS_OP_BWD_DKV);
+  return e;
 }
 
 }  // namespace dfs

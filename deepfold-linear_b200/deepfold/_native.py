@@ -72,7 +72,17 @@ class DfsBwdArgs(ctypes.Structure):
 
 
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
-                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static")
+                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op")
+
+# phases of the streamed path for row-sharded runs (include/dfsink.h)
+DFS_OP_FWD_INIT, DFS_OP_FWD_ROWS, DFS_OP_FWD_COLS, DFS_OP_FWD_OUT = 0, 1, 2, 3
+(DFS_OP_BWD_PREP, DFS_OP_BWD_ROWSTATS, DFS_OP_BWD_ROWDERIVE, DFS_OP_BWD_COLSTATS, DFS_OP_BWD_SETUP,
+ DFS_OP_BWD_PT_T, DFS_OP_BWD_CGINIT, DFS_OP_BWD_P_U, DFS_OP_BWD_CGSTEP_FIRST, DFS_OP_BWD_CGSTEP,
+ DFS_OP_BWD_P_X, DFS_OP_BWD_FINAL, DFS_OP_BWD_DQ, DFS_OP_BWD_DKV) = range(10, 24)
+DFS_WS_FWD_F, DFS_WS_FWD_G = 0, 1
+DFS_WS_BWD_M, DFS_WS_BWD_R, DFS_WS_BWD_D, DFS_WS_BWD_C, DFS_WS_BWD_GV, DFS_WS_BWD_T, DFS_WS_BWD_S = \
+    2, 3, 4, 7, 8, 19, 20
+DFS_WS_BWD_NSLOTS, DFS_WS_BWD_NSCALARS = 22, 8
 
 # fixed device scratch behind dfs_fwd_static (DFS_STATIC_SCRATCH_BYTES in include/dfsink.h)
 DFS_STATIC_SCRATCH_BYTES = 16 << 20
@@ -182,6 +192,10 @@ def lib() -> ctypes.CDLL:
             L.dfs_bwd.restype = ctypes.c_int
             L.dfs_bwd.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsCgParams),
                                   ctypes.POINTER(DfsBwdArgs), _P, ctypes.c_size_t, _P]
+            L.dfs_stream_op.restype = ctypes.c_int
+            L.dfs_stream_op.argtypes = [ctypes.c_int, ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsCgParams),
+                                        ctypes.POINTER(DfsFwdArgs), ctypes.POINTER(DfsBwdArgs), ctypes.c_int,
+                                        ctypes.c_int, _P, ctypes.c_size_t, _P]
             L.dfs_fwd_static.restype = ctypes.c_int
             L.dfs_fwd_static.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs), _P]
             L.dfs_selftest_mma.restype = ctypes.c_int
@@ -224,6 +238,13 @@ def make_problem(B, H, N, d, dtype, K_iter, lam, r_0, cost_mode=DFS_COST_QK, thr
                       K_iter=int(K_iter), check_every=int(check_every),
                       lam=float(lam) if not math.isinf(lam) else float("inf"), r_0=float(r_0),
                       threshold=float(threshold) if threshold is not None else 0.0, reserved=0.0)
+
+
+def workspace_bytes(prob: DfsProblem) -> tuple[int, int]:
+    """(forward, backward) workspace bytes of a problem (dfs_workspace_size)."""
+    fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    check(lib().dfs_workspace_size(prob, ctypes.byref(fb), ctypes.byref(bb)), "dfs_workspace_size")
+    return fb.value, bb.value
 
 
 def max_n(d: int) -> int:

@@ -1,0 +1,232 @@
+"""Row-sharded flash Sinkhorn: one long-sequence problem set over several GPUs.
+
+BASELINE config 4 (B=1, H=16, N=8192, d=64) splits the query rows of every
+(batch, head) problem evenly over the GPUs of a ``torch.distributed`` group
+(NCCL over NVLink).  Every GPU holds Q, K, V, dO and the marginals in full
+(N x d per head: a few MB) and owns one contiguous range of rows, which is also
+its range of columns for the column half-updates (the streamed kernels run a
+column update as a row update of S^T = K Q^T).  Each phase of the streamed
+path (``dfs_stream_op`` in include/dfsink.h) runs on the local range, and the
+vectors a phase produced are all-gathered before the next one:
+
+* forward: per Sinkhorn iteration the row potential f after the row half-update
+  and the column potential g after the column half-update (B*H*N fp32 each);
+* backward: the row statistics, the column sums, and per CG iteration the two
+  matrix-free plan products t = D1^-1 P u and s = P^T t; the CG scalars are then
+  computed redundantly, and identically, on every GPU, so all GPUs stop the
+  solve together without a further collective.
+
+Outputs (O, potentials, gradients) are all-gathered too, so every rank ends
+with the same full tensors a single GPU would produce.  Where the reference
+runs on one device only (src/deepfold/model/kernels/sinkhorn_kernel.py), this
+module has no counterpart there.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from deepfold import _native as nat
+
+__all__ = ["row_range", "RowGather", "row_sharded_flash_sinkhorn"]
+
+
+def row_range(N: int, world: int, rank: int) -> tuple[int, int, int]:
+    """Rows [r0, r1) of `rank` and the padded per-rank length ceil(N / world)."""
+    n_loc = -(-N // world)
+    r0 = min(N, rank * n_loc)
+    return r0, min(N, r0 + n_loc), n_loc
+
+
+class RowGather:
+    """All-gather of row slices: each rank holds valid rows [r0, r1) of a tensor
+    (P, N, *rest) laid out like the kernels' (B*H, N, ...) vectors; after the
+    call every rank holds all rows."""
+
+    def __init__(self, N: int, group=None):
+        self.group = group
+        on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if on else 1
+        self.rank = dist.get_rank(group) if on else 0
+        self.nccl = on and dist.get_backend(group) == "nccl"
+        self.N = N
+        self.r0, self.r1, self.n_loc = row_range(N, self.world, self.rank)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return x
+        P, rest = x.shape[0], x.shape[2:]
+        loc = x.new_zeros((P, self.n_loc) + tuple(rest))
+        loc[:, : self.r1 - self.r0] = x[:, self.r0:self.r1]
+        out = x.new_empty((self.world, P, self.n_loc) + tuple(rest))
+        if self.nccl:
+            dist.all_gather_into_tensor(out, loc, group=self.group)
+        else:  # gloo (CPU tests of this orchestration)
+            dist.all_gather(list(out.unbind(0)), loc, group=self.group)
+        full = out.transpose(0, 1).reshape((P, self.world * self.n_loc) + tuple(rest))
+        x.copy_(full[:, : self.N])
+        return x
+
+
+def _slot(ws: torch.Tensor, k: int, P: int, N: int) -> torch.Tensor:
+    return ws[k * P * N:(k + 1) * P * N].view(P, N)
+
+
+class _Sharded:
+    """One row-sharded problem set: argument blocks, workspaces and the phase loop."""
+
+    def __init__(self, Q, K, V, eps, log_mu, log_nu, K_iter, lam, mask, log_u_init, log_v_init, x_res,
+                 cg, group):
+        nat.require_cuda(Q, K, V)
+        self.B, self.H, self.N, self.d = Q.shape
+        self.P = self.B * self.H
+        self.group = group
+        self.gather = RowGather(self.N, group)
+        cdt = Q.dtype if Q.dtype in (torch.bfloat16, torch.float16, torch.float32) else torch.float32
+        f32 = lambda t: None if t is None else t.contiguous().float()  # noqa: E731
+        self.Q, self.K, self.V = (t.contiguous().to(cdt) for t in (Q, K, V))
+        self.eps, self.lmu, self.lnu = f32(eps), f32(log_mu), f32(log_nu)
+        self.mask, self.lui, self.lvi, self.xr = f32(mask), f32(log_u_init), f32(log_v_init), f32(x_res)
+        self.K_iter, self.lam, self.cg = int(K_iter), float(lam), cg
+        self.prob = nat.make_problem(self.B, self.H, self.N, self.d, cdt, K_iter, lam, 10.0)
+        self.fwd_bytes, self.bwd_bytes = nat.workspace_bytes(self.prob)
+        self.stream = nat.stream_ptr(Q.device)
+
+    def _op(self, op, r0, r1, fa=None, ba=None, ws=None, nbytes=0, cgp=None):
+        nat.check(nat.lib().dfs_stream_op(op, self.prob, cgp, fa, ba, r0, r1, ws.data_ptr(), nbytes,
+                                          self.stream), f"dfs_stream_op({op})")
+
+    def forward(self):
+        dev = self.Q.device
+        B, H, N, d, P = self.B, self.H, self.N, self.d, self.P
+        fo = dict(device=dev, dtype=torch.float32)
+        self.O = torch.empty(B, H, N, d, **fo)
+        self.xc = torch.empty(B, H, N, 3, **fo) if self.xr is not None else None
+        self.lu, self.lv = torch.empty(B, H, N, **fo), torch.empty(B, H, N, **fo)
+        self.fstatus = torch.zeros(1, device=dev, dtype=torch.int32)
+        ws = torch.empty(max(self.fwd_bytes // 4, 1), **fo)
+        fa = nat.DfsFwdArgs(Q=nat.ptr(self.Q), K=nat.ptr(self.K), V=nat.ptr(self.V), x_res=nat.ptr(self.xr),
+                            eps=nat.ptr(self.eps), log_mu=nat.ptr(self.lmu), log_nu=nat.ptr(self.lnu),
+                            log_u_init=nat.ptr(self.lui), log_v_init=nat.ptr(self.lvi), mask=nat.ptr(self.mask),
+                            O=nat.ptr(self.O), x_centroid=nat.ptr(self.xc), log_u=nat.ptr(self.lu),
+                            log_v=nat.ptr(self.lv), status=nat.ptr(self.fstatus))
+        g, r0, r1 = self.gather, self.gather.r0, self.gather.r1
+        run = lambda op, a, b: self._op(op, a, b, fa=fa, ws=ws, nbytes=self.fwd_bytes)  # noqa: E731
+        run(nat.DFS_OP_FWD_INIT, 0, N)
+        f, gg = _slot(ws, nat.DFS_WS_FWD_F, P, N), _slot(ws, nat.DFS_WS_FWD_G, P, N)
+        for _ in range(self.K_iter):
+            run(nat.DFS_OP_FWD_ROWS, r0, r1)
+            g(f)
+            run(nat.DFS_OP_FWD_COLS, r0, r1)
+            g(gg)
+        run(nat.DFS_OP_FWD_OUT, r0, r1)
+        if self.K_iter > 0:
+            g(self.lu.view(P, N))
+            g(self.lv.view(P, N))
+        g(self.O.view(P, N, d))
+        if self.xc is not None:
+            g(self.xc.view(P, N, 3))
+        return self.O, self.xc, self.lu, self.lv
+
+    def backward(self, dO, dxc, need_marg: bool):
+        dev = self.Q.device
+        B, H, N, d, P = self.B, self.H, self.N, self.d, self.P
+        fo = dict(device=dev, dtype=torch.float32)
+        dOc = dO.contiguous().float()
+        dxcc = None if (dxc is None or self.xr is None) else dxc.contiguous().float()
+        dQ, dK, dV = (torch.empty(B, H, N, d, **fo) for _ in range(3))
+        dmu = torch.empty(B, H, N, **fo) if need_marg else None
+        dnu = torch.empty(B, H, N, **fo) if need_marg else None
+        iters = torch.empty(P, device=dev, dtype=torch.int32)
+        resid = torch.empty(P, **fo)
+        status = torch.zeros(1, device=dev, dtype=torch.int32)
+        ws = torch.empty(max(self.bwd_bytes // 4, 1), **fo)
+        cgp = nat.DfsCgParams(rtol=float(self.cg["rtol"]), atol=float(self.cg["atol"]),
+                              max_iter=int(self.cg["max_iter"]), reserved=0)
+        ba = nat.DfsBwdArgs(Q=nat.ptr(self.Q), K=nat.ptr(self.K), V=nat.ptr(self.V), x_res=nat.ptr(self.xr),
+                            eps=nat.ptr(self.eps), log_mu=nat.ptr(self.lmu), log_nu=nat.ptr(self.lnu),
+                            mask=nat.ptr(self.mask), log_u=nat.ptr(self.lu), log_v=nat.ptr(self.lv),
+                            dO=nat.ptr(dOc), dxc=nat.ptr(dxcc), dQ=nat.ptr(dQ), dK=nat.ptr(dK), dV=nat.ptr(dV),
+                            dlog_mu=nat.ptr(dmu), dlog_nu=nat.ptr(dnu), cg_iters=nat.ptr(iters),
+                            cg_residual=nat.ptr(resid), status=nat.ptr(status))
+        g, r0, r1 = self.gather, self.gather.r0, self.gather.r1
+        run = lambda op, a=0, b=N: self._op(op, a, b, ba=ba, ws=ws, nbytes=self.bwd_bytes, cgp=cgp)  # noqa: E731
+        slot = lambda k: _slot(ws, k, P, N)  # noqa: E731
+        # the per-problem CG stop flags (int32) follow the vector slots and the scalars
+        o = nat.DFS_WS_BWD_NSLOTS * P * N + nat.DFS_WS_BWD_NSCALARS * P
+        done = ws[o:o + P].view(torch.int32)
+        run(nat.DFS_OP_BWD_PREP)
+        run(nat.DFS_OP_BWD_ROWSTATS, r0, r1)
+        for k in (nat.DFS_WS_BWD_M, nat.DFS_WS_BWD_R, nat.DFS_WS_BWD_D):
+            g(slot(k))
+        run(nat.DFS_OP_BWD_ROWDERIVE)
+        run(nat.DFS_OP_BWD_COLSTATS, r0, r1)
+        g(slot(nat.DFS_WS_BWD_C))
+        g(slot(nat.DFS_WS_BWD_GV))
+        run(nat.DFS_OP_BWD_SETUP)
+        run(nat.DFS_OP_BWD_PT_T, r0, r1)
+        g(slot(nat.DFS_WS_BWD_S))
+        run(nat.DFS_OP_BWD_CGINIT)
+        for it in range(int(self.cg["max_iter"]) + 1):
+            run(nat.DFS_OP_BWD_P_U, r0, r1)
+            g(slot(nat.DFS_WS_BWD_T))
+            run(nat.DFS_OP_BWD_PT_T, r0, r1)
+            g(slot(nat.DFS_WS_BWD_S))
+            run(nat.DFS_OP_BWD_CGSTEP_FIRST if it == 0 else nat.DFS_OP_BWD_CGSTEP)
+            # identical on every rank (same gathered vectors, same arithmetic): all ranks stop together
+            if bool((done != 0).all()):
+                break
+        run(nat.DFS_OP_BWD_P_X, r0, r1)
+        g(slot(nat.DFS_WS_BWD_S))
+        run(nat.DFS_OP_BWD_FINAL)
+        run(nat.DFS_OP_BWD_DQ, r0, r1)
+        run(nat.DFS_OP_BWD_DKV, r0, r1)
+        for t in (dQ, dK, dV):
+            g(t.view(P, N, d))
+        self.report = dict(cg_iters=iters, cg_residual=resid, status=status, fwd_status=self.fstatus)
+        return dQ, dK, dV, dmu, dnu
+
+
+class _RowShardedFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Q, K, V, log_mu, log_nu, eps, mask, x_res, K_iter, lam, cg, group):
+        sh = _Sharded(Q, K, V, eps, log_mu, log_nu, K_iter, lam, mask, None, None, x_res, cg, group)
+        O, xc, lu, lv = sh.forward()
+        ctx.sh = sh
+        ctx.in_dtype = Q.dtype
+        ctx.mark_non_differentiable(lu, lv)
+        if xc is None:
+            xc = O.new_zeros(0)
+        return O, xc, lu, lv
+
+    @staticmethod
+    def backward(ctx, dO, dxc, _dlu, _dlv):
+        sh = ctx.sh
+        need_marg = ctx.needs_input_grad[3] or ctx.needs_input_grad[4]
+        if dO is None:
+            dO = torch.zeros_like(sh.O)
+        dQ, dK, dV, dmu, dnu = sh.backward(dO, dxc if sh.xr is not None else None, need_marg)
+        cast = lambda t: t.to(ctx.in_dtype)  # noqa: E731
+        return (cast(dQ), cast(dK), cast(dV), dmu, dnu, None, None, None, None, None, None, None)
+
+
+def row_sharded_flash_sinkhorn(Q, K, V, eps, log_mu, log_nu, K_iter: int = 7, lam: float = 1.0, mask=None,
+                               x_res=None, cg_opts: dict | None = None, group=None):
+    """flash_sinkhorn (sinkhorn_kernel.flash_sinkhorn) with the rows of every
+    problem split over the ranks of `group`.  Every rank passes the same full
+    (B, H, N, d) inputs and receives the same full outputs (O, x_centroid or
+    None, log_u, log_v); backward gives the full gradients on every rank.
+    Uses the streamed kernels (d = 32 or 64; no position / geometry terms)."""
+    from deepfold.model.kernels.sinkhorn_kernel import CG_DEFAULTS
+
+    cg = dict(CG_DEFAULTS)
+    if cg_opts:
+        cg.update(cg_opts)
+    if not (lam > 0.0) or math.isnan(lam):
+        raise ValueError("lam must be positive (inf for the balanced problem)")
+    O, xc, lu, lv = _RowShardedFn.apply(Q, K, V, log_mu, log_nu, eps, mask, x_res, int(K_iter), float(lam), cg,
+                                        group)
+    return O, (xc if x_res is not None else None), lu, lv

@@ -158,6 +158,51 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace,
 int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a,
             void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Row-sharded runs (several GPUs per problem).  dfs_stream_op runs one phase of
+ * the streamed forward or backward on a range of rows [row_begin, row_end) (for
+ * the column phases: of columns).  dfs_fwd / dfs_bwd on one GPU are exactly
+ * these phases over all rows, in the order below; a run sharded over G GPUs
+ * gives each GPU one range and all-gathers the workspace vectors a range phase
+ * produced (listed per phase) before the next phase.  Every GPU holds Q, K, V,
+ * dO and the marginals in full.  The workspace is dfs_workspace_size's
+ * fwd_bytes (forward phases) or bwd_bytes (backward phases); its vectors are
+ * (B*H, N) fp32 slots at slot * B*H*N floats (numbers below).
+ *
+ * Forward: FWD_INIT; K_iter x { FWD_ROWS (gather slot F and log_u),
+ *          FWD_COLS (gather slot G and log_v) }; FWD_OUT (O, x_centroid rows).
+ * Backward: BWD_PREP; BWD_ROWSTATS (gather M, R, D); BWD_ROWDERIVE;
+ *          BWD_COLSTATS (gather C, GV); BWD_SETUP; BWD_PT_T (gather S);
+ *          BWD_CGINIT; (max_iter + 1) x { BWD_P_U (gather T); BWD_PT_T (gather S);
+ *          BWD_CGSTEP_FIRST the first time, BWD_CGSTEP after };
+ *          BWD_P_X (gather S); BWD_FINAL; BWD_DQ (dQ rows); BWD_DKV (dK, dV rows).
+ * --------------------------------------------------------------------------- */
+enum {
+  DFS_OP_FWD_INIT = 0, DFS_OP_FWD_ROWS = 1, DFS_OP_FWD_COLS = 2, DFS_OP_FWD_OUT = 3,
+  DFS_OP_BWD_PREP = 10, DFS_OP_BWD_ROWSTATS = 11, DFS_OP_BWD_ROWDERIVE = 12, DFS_OP_BWD_COLSTATS = 13,
+  DFS_OP_BWD_SETUP = 14, DFS_OP_BWD_PT_T = 15, DFS_OP_BWD_CGINIT = 16, DFS_OP_BWD_P_U = 17,
+  DFS_OP_BWD_CGSTEP_FIRST = 18, DFS_OP_BWD_CGSTEP = 19, DFS_OP_BWD_P_X = 20, DFS_OP_BWD_FINAL = 21,
+  DFS_OP_BWD_DQ = 22, DFS_OP_BWD_DKV = 23
+};
+/* workspace slots gathered between phases */
+enum { DFS_WS_FWD_F = 0, DFS_WS_FWD_G = 1 };
+enum {
+  DFS_WS_BWD_F = 0, DFS_WS_BWD_G = 1, DFS_WS_BWD_M = 2, DFS_WS_BWD_R = 3, DFS_WS_BWD_D = 4,
+  DFS_WS_BWD_C = 7, DFS_WS_BWD_GV = 8, DFS_WS_BWD_T = 19, DFS_WS_BWD_S = 20,
+  /* after the DFS_WS_BWD_NSLOTS vector slots come DFS_WS_BWD_NSCALARS floats per
+   * problem, then one int32 CG stop flag per problem (nonzero once that
+   * problem's solve has stopped; identical on every GPU of a sharded run) */
+  DFS_WS_BWD_NSLOTS = 22, DFS_WS_BWD_NSCALARS = 8
+};
+
+/* One phase of the streamed path on rows (columns) [row_begin, row_end).
+ * Forward phases read `fa` (and ignore `cg`, `ba`), backward phases `cg` and
+ * `ba`.  Any N and d the streamed kernels accept (d = 32 or 64).  New for
+ * multi-GPU row sharding of long sequences; the reference has no sharded path. */
+int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const dfs_fwd_args* fa,
+                  const dfs_bwd_args* ba, int row_begin, int row_end, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* Size of the library's fixed device scratch used by dfs_fwd_static: 16 MiB,
  * i.e. streamed problems with B*H*N up to 1,048,576 (the forward needs
  * 16 bytes of workspace per (batch, head, point)). */
