@@ -8,7 +8,14 @@ zero start.  On N GPUs every rank runs its own (batch, head) shard of that size
 (weak scaling, no data-path collective); the reported value is whole-job
 calls/s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4]
+
+``--config 3`` (B=8 H=16 padded N=1024 d=64, variable lengths, eps 0.5, 50
+iterations, kappa < 1) spreads the (batch, head) problems over the ranks with a
+length^2-balanced partition; ``--config 4`` (B=1 H=16 N=8192 d=64, 30
+iterations, CG tol 1e-5 / max 40) splits every problem's rows over the ranks
+with NCCL all-gathers of the potentials each half-iteration.  Both are strong
+scaling: one call is the whole configuration's forward + backward.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 oracle restatement in ``oracle/``, float32, all host threads) on the same
@@ -322,6 +329,186 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+# ---------------------------------------------------------------- configs 3 and 4
+BIG = {
+    3: dict(B=8, H=16, N=1024, d=64, eps=0.5, K_iter=50, lam=1.0, cg_rtol=1e-6, cg_max_iter=50, varlen=True),
+    4: dict(B=1, H=16, N=8192, d=64, eps=1.0, K_iter=30, lam=float("inf"), cg_rtol=1e-5, cg_max_iter=40,
+            varlen=False),
+}
+
+
+def big_inputs(c, seed=0):
+    """Seeded host inputs of config 3 / 4 (identical on every rank)."""
+    g = torch.Generator().manual_seed(seed)
+    B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+    host = {k: torch.randn(B, H, N, d, generator=g).to(torch.bfloat16) for k in ("Q", "K", "V", "dO")}
+    if c["varlen"]:
+        lengths = torch.randint(64, N + 1, (B,), generator=g)
+        mask = (torch.arange(N)[None, :] < lengths[:, None]).float()
+        lms = []
+        for _ in range(2):
+            z = torch.randn(B, H, N, generator=g)
+            z = torch.where(mask[:, None, :] > 0, z, torch.full_like(z, -1e30))
+            lms.append(torch.where(mask[:, None, :] > 0, torch.log_softmax(z, -1), torch.full_like(z, -1e9)))
+        lmu, lnu = lms
+    else:
+        lengths = torch.full((B,), N)
+        mask = None
+        lmu = torch.full((B, H, N), -math.log(N))
+        lnu = lmu.clone()
+    return host, [int(x) for x in lengths], mask, lmu, lnu
+
+
+def run_big(args):
+    from deepfold.model.kernels.sinkhorn_bhshard import bh_sharded_flash_sinkhorn, partition_problems
+    from deepfold.model.kernels.sinkhorn_kernel import last_cg_report
+    from deepfold.model.kernels.sinkhorn_rowshard import last_rowshard_report, row_range, \
+        row_sharded_flash_sinkhorn
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    c = BIG[args.config]
+    B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+    host, lengths, mask, lmu, lnu = big_inputs(c)
+    host = {k: v.pin_memory() for k, v in host.items()}
+    eps = torch.full((H,), c["eps"], device=dev)
+    mask_d = None if mask is None else mask.to(dev)
+    lmu_d, lnu_d = lmu.to(dev), lnu.to(dev)
+    cg = dict(rtol=c["cg_rtol"], atol=0.0, max_iter=c["cg_max_iter"])
+    chunks = partition_problems(lengths, H, world)[rank] if args.config == 3 else None
+    r0, r1, _ = row_range(N, world, rank)
+
+    def step(inp):
+        leaves = [inp[k].requires_grad_(True) for k in ("Q", "K", "V")]
+        if args.config == 4:
+            O, _, _, _ = row_sharded_flash_sinkhorn(*leaves, eps, lmu_d, lnu_d, K_iter=c["K_iter"], lam=c["lam"],
+                                                    mask=mask_d, cg_opts=cg)
+            grads = torch.autograd.grad(O, leaves, grad_outputs=inp["dO"].float())
+            return [g[:, :, r0:r1] for g in grads]   # this rank's rows (all ranks hold all)
+        res = bh_sharded_flash_sinkhorn(chunks, *leaves, eps, lmu_d, lnu_d, c["K_iter"], c["lam"], mask=mask_d,
+                                        cg_opts=cg)
+        if not res:
+            return []
+        outs = [r[3] for r in res]
+        gos = [inp["dO"][b:b + 1, h0:h1].float() for b, h0, h1, *_ in res]
+        grads = torch.autograd.grad(outs, leaves, grad_outputs=gos)
+        return [g[b:b + 1, h0:h1] for g in grads for b, h0, h1, *_ in res]
+
+    dev_in = {k: v.to(dev) for k, v in host.items()}
+    for _ in range(args.warmup):
+        step(dev_in)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step(dev_in)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    # e2e: host inputs copied in and this rank's gradients copied out every step
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = 0
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    outs = [torch.empty(gt.shape, dtype=gt.dtype, pin_memory=True) for gt in step(dev_in)]
+    torch.cuda.synchronize()
+    e2.record(stream)
+    for _ in range(args.steps):
+        inp = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        grads = step(inp)
+        d2h = 0
+        for out, gt in zip(outs, grads):
+            out.copy_(gt, non_blocking=True)
+            d2h += out.numel() * out.element_size()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    clocks = sampler.stop() if sampler else None
+    rep = last_rowshard_report() if args.config == 4 else last_cg_report()
+    n_cg = float(rep["cg_iters"].float().mean()) if rep else 0.0
+    status = (int(rep["status"].item()) | int(rep["fwd_status"].item())) if rep else 0
+    if rank == 0:
+        peak, _, peak_src = load_peaks()
+        per = N * N * d * B * H
+        f_call = ((4 * c["K_iter"] + 4) + (14 + 2 * n_cg)) * per
+        value = args.steps / (ms * 1e-3)
+        per_gpu_tf = f_call * value / world / 1e12
+        name = (f"config{args.config}: flash-Sinkhorn fwd+IFT-bwd B={B} H={H} N={N} d={d} bf16 eps={c['eps']} "
+                f"K={c['K_iter']} " + ("padded var-len, softmax marginals, lam=1" if c["varlen"] else
+                                       "uniform marginals, balanced") +
+                f", CG tol {c['cg_rtol']} max {c['cg_max_iter']}")
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": f"synthetic (seeded N(0,1); BASELINE config {args.config} shapes)",
+            "config": {"workload": name, "global_batch": B, "heads": H, "seq_len": N, "head_dim": d,
+                       "parallelism": (f"(batch,head)-shard x{world}, length^2-balanced" if args.config == 3
+                                       else f"row-shard x{world}, NCCL all-gather per half-iteration"),
+                       "l2": "inputs and per-call working set exceed L2 (streamed N x N recompute)"},
+            "tflops": {"algorithmic_per_call": round(f_call / 1e12, 4), "cg_iters_mean": n_cg,
+                       "achieved_per_gpu": round(per_gpu_tf, 3), "frac_of_bf16_peak": round(per_gpu_tf / peak, 5)},
+            "roofline": {"bound": "tensor", "kernel": "streamed passes (whole fwd+bwd step)",
+                         "achieved": round(per_gpu_tf, 3), "peak": peak, "peak_source": peak_src,
+                         "unit": "TFLOP/s", "frac": round(per_gpu_tf / peak, 5), "traffic": None},
+            "e2e": {"value": round(args.steps / (e2e_ms * 1e-3), 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "device_status": status,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_big(args.config, c, lengths, seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def cpu_baseline_big(cfg_id, c, lengths, seconds=15.0):
+    """Oracle (float32 numpy) on one (batch, head) problem of a smaller length L,
+    scaled by sum over problems of (L_bh / L)^2 to whole-configuration calls/s."""
+    from oracle import sinkhorn_oracle as orc
+    L = 512 if cfg_id == 3 else 1024
+    r = np.random.default_rng(3)
+    Q, K, V = (r.standard_normal((1, 1, L, c["d"])).astype(np.float32) for _ in range(3))
+    dO = r.standard_normal((1, L, c["d"])).astype(np.float32)
+    lm = np.full((1, 1, L), -math.log(L), np.float32)
+    lam = 1e6 if math.isinf(c["lam"]) else c["lam"]
+
+    def call():
+        with orc.precision(np.float32):
+            orc.flash_sinkhorn_attn(Q, K, V, None, None, None, None, np.full(1, c["eps"], np.float32), None, lm, lm,
+                                    K_iter=c["K_iter"], lam=lam, with_grad=True, dO_flat=dO)
+
+    call()
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds:
+        call()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    scale = sum(c["H"] * (Lb / L) ** 2 for Lb in lengths)
+    return {"value": round(1.0 / (dt * scale), 6), "unit": UNIT, "cores": len(os.sched_getaffinity(0)),
+            "kind": "port", "sample": f"{n} oracle calls (fwd + unrolled bwd, float32) on one problem of N={L}, "
+                                      f"d={c['d']}, K={c['K_iter']}, scaled by sum (L_bh/{L})^2 = {scale:.1f}",
+            "cpu": _cpu_model()}
+
+
 def _oracle_call(orc, inp):
     """One fwd + unrolled bwd of the oracle on the config-2 workload."""
     c = CFG
@@ -409,11 +596,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config in BIG:
+        run_big(args)
     else:
         run_ours(args)
 

@@ -31,7 +31,7 @@ import torch.distributed as dist
 
 from deepfold import _native as nat
 
-__all__ = ["row_range", "RowGather", "row_sharded_flash_sinkhorn"]
+__all__ = ["row_range", "RowGather", "row_sharded_flash_sinkhorn", "last_rowshard_report"]
 
 
 def row_range(N: int, world: int, rank: int) -> tuple[int, int, int]:
@@ -187,7 +187,18 @@ class _Sharded:
         for t in (dQ, dK, dV):
             g(t.view(P, N, d))
         self.report = dict(cg_iters=iters, cg_residual=resid, status=status, fwd_status=self.fstatus)
+        _last_report.clear()
+        _last_report.update(self.report)
         return dQ, dK, dV, dmu, dnu
+
+
+_last_report: dict = {}
+
+
+def last_rowshard_report() -> dict:
+    """Device tensors (cg_iters, cg_residual, status, fwd_status) of the most
+    recent row-sharded backward on this rank."""
+    return dict(_last_report)
 
 
 class _RowShardedFn(torch.autograd.Function):

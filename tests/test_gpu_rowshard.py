@@ -49,3 +49,31 @@ def test_two_gpu_row_sharded_matches_single_gpu():
     env = dict(os.environ, RS_N="1000", NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_bh_chunks_on_streams_match_full_batch():
+    """(batch, head) chunks from the length^2 partition, run on a stream pool,
+    give the outputs and gradients of one full-batch call."""
+    from deepfold.model.kernels.sinkhorn_bhshard import bh_sharded_flash_sinkhorn, partition_problems
+
+    lengths = [600, 200, 520]
+    inp = make_inputs(3, 4, 600, 64, seed=41, eps=0.5, uniform=False, lengths=lengths)
+    cg = dict(rtol=1e-6, atol=0.0, max_iter=40)
+    leaves = [inp[k].clone().requires_grad_(True) for k in ("Q", "K", "V")]
+    O, _, lu, lv = flash_sinkhorn(*leaves, None, None, None, inp["eps"], None, inp["log_mu"], inp["log_nu"],
+                                  K_iter=20, lam=1.0, mask=inp["mask"], cg_opts=cg)
+    ref_g = torch.autograd.grad(O, leaves, grad_outputs=inp["dO"])
+    leaves2 = [inp[k].clone().requires_grad_(True) for k in ("Q", "K", "V")]
+    outs, gos = [], []
+    for chunks in partition_problems(lengths, 4, 3):   # every rank's chunks, run here one after another
+        res = bh_sharded_flash_sinkhorn(chunks, *leaves2, inp["eps"], inp["log_mu"], inp["log_nu"], 20, 1.0,
+                                        mask=inp["mask"], cg_opts=cg)
+        for b, h0, h1, Oc, luc, lvc in res:
+            assert float((Oc - O[b:b + 1, h0:h1]).detach().abs().max()) <= 1e-5
+            assert float((luc - lu[b:b + 1, h0:h1]).abs().max()) <= 1e-5
+            outs.append(Oc)
+            gos.append(inp["dO"][b:b + 1, h0:h1])
+    got_g = torch.autograd.grad(outs, leaves2, grad_outputs=gos)
+    torch.cuda.synchronize()
+    for a, b in zip(ref_g, got_g):
+        assert float((a - b).abs().max()) <= 1e-5
