@@ -420,4 +420,43 @@ DFS_DEV float reduce8_rows(float (&a)[8], int lane) {
   return d;
 }
 
+// [lo, hi): the smallest range of positions that holds every valid point of
+// batch element bb under a (B, N) mask (nonzero = valid); [0, N) without a
+// mask, [0, 0) when no point is valid.  Block-wide: every thread of a CTA of NT
+// threads calls it; red is 2 * NT / 32 ints of shared memory.
+template <int NT>
+DFS_DEV void valid_extent(const float* mask, int bb, int N, int* red, int& lo, int& hi) {
+  if (mask == nullptr) {
+    lo = 0;
+    hi = N;
+    return;
+  }
+  const float* mrow = mask + static_cast<size_t>(bb) * N;
+  int l = N, h = -1;
+#pragma unroll 4
+  for (int j = threadIdx.x; j < N; j += NT) {
+    const bool v = mrow[j] != 0.0f;
+    l = v ? min(l, j) : l;
+    h = v ? j : h;
+  }
+  l = __reduce_min_sync(0xffffffffu, l);
+  h = __reduce_max_sync(0xffffffffu, h);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    red[warp] = l;
+    red[NT / 32 + warp] = h;
+  }
+  __syncthreads();
+  l = N;
+  h = -1;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) {
+    l = min(l, red[w]);
+    h = max(h, red[NT / 32 + w]);
+  }
+  __syncthreads();  // red may be reused
+  lo = h < 0 ? 0 : l;
+  hi = h + 1;
+}
+
 }  // namespace dfs

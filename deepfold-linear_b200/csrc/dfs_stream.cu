@@ -101,6 +101,16 @@ __global__ void __launch_bounds__(kSThreads) stream_kernel(const StreamParams p)
   const bool rin = row < p.row_end && row < N;
   const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
   int err = 0;
+  // Only the column tiles that hold a valid point are visited: a masked column
+  // contributes exactly nothing (its bias is -inf), so the others are skipped,
+  // and a block with no valid row visits none (its rows' results are the
+  // masked-row values).
+  int vlo, vhi;
+  valid_extent<kSThreads>(p.mask, bb, N, reinterpret_cast<int*>(base + Cfg::OFF_BAR + 32), vlo, vhi);
+  const int rhi = min(min(r0 + 128, p.row_end), N);
+  const bool live = max(r0, vlo) < min(rhi, vhi);
+  const int t_begin = live ? vlo / kSTile : 0;
+  const int ntiles = live ? (vhi + kSTile - 1) / kSTile - t_begin : 0;
 
   if (warp == 0) tmem_alloc(tslot, 256);
   if (tid == 0) {
@@ -127,7 +137,6 @@ __global__ void __launch_bounds__(kSThreads) stream_kernel(const StreamParams p)
   }
   float cx = 0.0f, cy = 0.0f, cz = 0.0f;  // centroid accumulators
 
-  const int ntiles = (N + kSTile - 1) / kSTile;
   // operands of tile t into buffer b; column bias into slot t % 3 (read by the
   // epilogue of tile t, two barriers after the last read of that slot)
   auto stage = [&](int t, int b) {
@@ -203,27 +212,30 @@ __global__ void __launch_bounds__(kSThreads) stream_kernel(const StreamParams p)
   };
 
   if constexpr (!kOut) {
-    stage(0, 0);
-    fence_async_smem();
-    __syncthreads();
-    issue_s(0);
+    if (ntiles > 0) {
+      stage(t_begin, 0);
+      fence_async_smem();
+      __syncthreads();
+      issue_s(0);
+    }
 #pragma unroll 1
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      if (t + 1 < ntiles) stage(t + 1, b ^ 1);  // buffer b^1: its MMA (tile t-1) completed
+    for (int u = 0; u < ntiles; ++u) {
+      const int t = t_begin + u, b = u & 1;
+      if (u + 1 < ntiles) stage(t + 1, b ^ 1);  // buffer b^1: its MMA (tile t-1) completed
       fence_async_smem();
       wait_bar(b);
       tc_fence_before();
       __syncthreads();  // tile t+1 staged by all; epilogue t-1 (TMEM b^1) finished by all
       tc_fence_after();
-      if (t + 1 < ntiles) issue_s(b ^ 1);
+      if (u + 1 < ntiles) issue_s(b ^ 1);
       epilogue(t, b);
     }
   } else {
     // one buffer: S tile -> T_norm tile (shared memory) -> O += T_norm V
 #pragma unroll 1
-    for (int t = 0; t < ntiles; ++t) {
-      if (t > 0) wait_bar(1);  // O MMA of tile t-1 done: T and V^T buffers free
+    for (int u = 0; u < ntiles; ++u) {
+      const int t = t_begin + u;
+      if (u > 0) wait_bar(1);  // O MMA of tile t-1 done: T and V^T buffers free
       stage(t, 0);
       fence_async_smem();
       tc_fence_before();
@@ -237,11 +249,11 @@ __global__ void __launch_bounds__(kSThreads) stream_kernel(const StreamParams p)
       __syncthreads();
       tc_fence_after();
       if (tid == 0) {
-        issue_mma<128, D, kSTile>(tbase + kSTile, Ts, Vt, t > 0);
+        issue_mma<128, D, kSTile>(tbase + kSTile, Ts, Vt, u > 0);
         mma_commit(&mbar[1]);
       }
     }
-    wait_bar(1);
+    if (ntiles > 0) wait_bar(1);  // (no tile: every row is masked, O is written as 0)
   }
 
   // ---------------------------------------------------------------- results

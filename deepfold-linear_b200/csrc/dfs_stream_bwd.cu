@@ -110,6 +110,15 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
   const bool rin = row < p.row_end && row < N;
   const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
   int err = 0;
+  // Only the column tiles that hold a valid point are visited (a masked column
+  // has a -inf potential: P = T_norm = 0 there, so it adds exactly nothing);
+  // a block with no valid row visits none and writes the masked-row values.
+  int vlo, vhi;
+  valid_extent<kBThreads>(p.mask, bb, N, reinterpret_cast<int*>(base + Cfg::OFF_BAR + 32), vlo, vhi);
+  const int rhi = min(min(r0 + 128, p.row_end), N);
+  const bool live = max(r0, vlo) < min(rhi, vhi);
+  const int t_begin = live ? vlo / TW : 0;
+  const int ntiles = live ? (vhi + TW - 1) / TW - t_begin : 0;
 
   if (warp == 0) tmem_alloc(tslot, 256);
   if (tid == 0) {
@@ -150,7 +159,6 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
   const bool has_x = p.xvec != nullptr && p.rxvec != nullptr;
   float s0 = 0.0f, s1 = 0.0f, mrun = -1.0e30f;  // running results
 
-  const int ntiles = (N + TW - 1) / TW;
   uint32_t ph0 = 0, ph1 = 0;
   auto wait_bar = [&](int b) {
     const uint32_t par = b == 0 ? ph0 : ph1;
@@ -160,9 +168,9 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
   };
 
 #pragma unroll 1
-  for (int t = 0; t < ntiles; ++t) {
-    const int c0 = t * TW;
-    if (kAcc && t > 0) wait_bar(1);  // accumulation MMAs of tile t-1 done: their operands are free
+  for (int u = 0; u < ntiles; ++u) {
+    const int c0 = (t_begin + u) * TW;
+    if (kAcc && u > 0) wait_bar(1);  // accumulation MMAs of tile t-1 done: their operands are free
     // ---- stage the tile
     ldt(Bs, p.Bop, p.b_f32, c0, RTW{}, NoT{});
     if constexpr (kDT) ldt(B2s, p.B2op, p.b2_f32, c0, RTW{}, NoT{});
@@ -293,8 +301,8 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
     tc_fence_after();
     if constexpr (kAcc) {
       if (tid == 0) {
-        issue_mma<128, D, TW>(t_a0, dSs, B3s, t > 0);
-        if constexpr (kTwo) issue_mma<128, D, TW>(t_a1, TTs, B4s, t > 0);
+        issue_mma<128, D, TW>(t_a0, dSs, B3s, u > 0);
+        if constexpr (kTwo) issue_mma<128, D, TW>(t_a1, TTs, B4s, u > 0);
         mma_commit(&mbar[1]);
       }
     }
@@ -302,7 +310,7 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
 
   // ---------------------------------------------------------------- results
   if constexpr (kAcc) {
-    wait_bar(1);
+    if (ntiles > 0) wait_bar(1);  // (no tile: every row is masked and written as 0)
 #pragma unroll
     for (int a = 0; a < (kTwo ? 2 : 1); ++a) {
       float* dst_base = a == 0 ? p.acc0 : p.acc1;
@@ -619,9 +627,11 @@ size_t stream_bwd_workspace(int B, int H, int N) {
   return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256;
 }
 
-static_assert(WS_F == DFS_WS_BWD_F && WS_G == DFS_WS_BWD_G && WS_M == DFS_WS_BWD_M && WS_R == DFS_WS_BWD_R &&
-                  WS_D == DFS_WS_BWD_D && WS_C == DFS_WS_BWD_C && WS_GV == DFS_WS_BWD_GV && WS_T == DFS_WS_BWD_T &&
-                  WS_S == DFS_WS_BWD_S && WS_NUM == DFS_WS_BWD_NSLOTS && SC_NUM == DFS_WS_BWD_NSCALARS,
+constexpr bool same_slot(int a, int b) { return a == b; }
+static_assert(same_slot(WS_F, DFS_WS_BWD_F) && same_slot(WS_G, DFS_WS_BWD_G) && same_slot(WS_M, DFS_WS_BWD_M) &&
+                  same_slot(WS_R, DFS_WS_BWD_R) && same_slot(WS_D, DFS_WS_BWD_D) && same_slot(WS_C, DFS_WS_BWD_C) &&
+                  same_slot(WS_GV, DFS_WS_BWD_GV) && same_slot(WS_T, DFS_WS_BWD_T) && same_slot(WS_S, DFS_WS_BWD_S) &&
+                  same_slot(WS_NUM, DFS_WS_BWD_NSLOTS) && same_slot(SC_NUM, DFS_WS_BWD_NSCALARS),
               "workspace slots named in include/dfsink.h");
 
 // One phase of the streamed backward on rows (or, for the column phases,

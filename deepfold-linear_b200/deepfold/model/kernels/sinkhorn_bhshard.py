@@ -2,19 +2,20 @@
 
 BASELINE config 3 (B=8, H=16, padded N=1024, true lengths L_b in [64, 1024])
 holds B*H independent optimal-transport problems whose cost grows like L_b^2.
-``partition_problems`` balances that cost over the ranks and keeps each rank's
-heads of one batch element contiguous, so every chunk it hands out is a plain
-view Q[b, h0:h1] of the full tensors: no copies, no data-path collective.  The
-order is by decreasing length (the longest-processing-time rule), each rank
-takes a contiguous run of (b, h) pairs of about total/world cost, so the
-imbalance is at most one problem's cost.
+``partition_problems`` balances that cost over the ranks: the (b, h) pairs are
+ordered by decreasing length (the longest-processing-time rule) and each rank
+takes a contiguous run of about total/world cost, so the imbalance is at most
+one problem's cost.  No data-path collective is needed.  ``rank_blocks`` turns
+a rank's run into at most three rectangles of the length-sorted batch, so a
+rank issues at most three kernel sequences per call, whatever B and H are: the
+streamed path's cost per call is dominated by its launch count at these sizes.
 """
 
 from __future__ import annotations
 
 import torch
 
-__all__ = ["partition_problems", "bh_sharded_flash_sinkhorn"]
+__all__ = ["partition_problems", "rank_blocks", "bh_sharded_flash_sinkhorn"]
 
 
 def partition_problems(lengths, H: int, world: int):
@@ -46,6 +47,25 @@ def partition_problems(lengths, H: int, world: int):
     return out
 
 
+def rank_blocks(lengths, H: int, world: int, rank: int):
+    """This rank's share of partition_problems as rectangles of the batch sorted
+    by decreasing length: returns (order, blocks) with `order` the batch
+    permutation and blocks (s0, s1, h0, h1) over sorted positions [s0, s1) and
+    heads [h0, h1).  Whole batch elements merge into one block, so a rank has at
+    most three blocks (a partial element at each end of its run)."""
+    order = sorted(range(len(lengths)), key=lambda b: -int(lengths[b]))
+    pos = {b: i for i, b in enumerate(order)}
+    blocks = []
+    for b, h0, h1 in partition_problems(lengths, H, world)[rank]:
+        sp = pos[b]
+        if (blocks and h0 == 0 and h1 == H and blocks[-1][1] == sp and blocks[-1][2] == 0
+                and blocks[-1][3] == H):
+            blocks[-1] = (blocks[-1][0], sp + 1, 0, H)
+        else:
+            blocks.append((sp, sp + 1, h0, h1))
+    return order, blocks
+
+
 _streams: dict = {}
 
 
@@ -56,32 +76,38 @@ def _stream_pool(device, n):
     return _streams[key]
 
 
-def bh_sharded_flash_sinkhorn(chunks, Q, K, V, eps, log_mu, log_nu, K_iter, lam, mask=None, cg_opts=None,
-                              n_streams: int = 4):
-    """Run flash_sinkhorn on this rank's chunks (from partition_problems) of the
-    full (B, H, N, d) inputs; returns [(b, h0, h1, O, log_u, log_v)] with O etc.
-    of shape (1, h1-h0, N, ...).  Gradients flow to the full Q, K, V through the
-    views.  The chunks are independent, so they run on a pool of `n_streams`
-    CUDA streams (one chunk alone may not fill the GPU); autograd runs each
-    chunk's backward on the stream of its forward, and the outputs are ordered
-    after all of them on the current stream."""
+def bh_sharded_flash_sinkhorn(Q, K, V, eps, log_mu, log_nu, K_iter, lam, lengths, world: int = 1, rank: int = 0,
+                              mask=None, cg_opts=None, n_streams: int = 3):
+    """This rank's (batch, head) share of flash_sinkhorn on the full (B, H, N, d)
+    inputs.  The batch is first put in decreasing-length order (one gather,
+    differentiable), then each block of rank_blocks runs as one call on a pool
+    of `n_streams` CUDA streams (independent problems; autograd replays each
+    backward on its forward's stream).  Returns (order, results) with results
+    [(s0, s1, h0, h1, O, log_u, log_v)], O of shape (s1-s0, h1-h0, N, d) over the
+    sorted batch positions; gradients reach the full Q, K, V."""
     from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn
 
+    order, blocks = rank_blocks(lengths, Q.shape[1], world, rank)
+    if not blocks:
+        return order, []
+    idx = torch.tensor(order, device=Q.device)
+    Qs, Ks, Vs = (t.index_select(0, idx) for t in (Q, K, V))
+    lmu, lnu = log_mu.index_select(0, idx), log_nu.index_select(0, idx)
+    ms = None if mask is None else mask.index_select(0, idx)
     cur = torch.cuda.current_stream(Q.device)
-    pool = _stream_pool(Q.device, n_streams) if len(chunks) > 1 else [cur]
+    pool = _stream_pool(Q.device, n_streams) if len(blocks) > 1 else [cur]
     res = []
-    for i, (b, h0, h1) in enumerate(chunks):
+    for i, (s0, s1, h0, h1) in enumerate(blocks):
         s = pool[i % len(pool)]
         s.wait_stream(cur)
         with torch.cuda.stream(s):
-            O, _, lu, lv = flash_sinkhorn(Q[b:b + 1, h0:h1], K[b:b + 1, h0:h1], V[b:b + 1, h0:h1], None, None,
-                                          None, eps[h0:h1], None, log_mu[b:b + 1, h0:h1], log_nu[b:b + 1, h0:h1],
-                                          K_iter=K_iter, lam=lam, mask=None if mask is None else mask[b:b + 1],
-                                          cg_opts=cg_opts)
+            O, _, lu, lv = flash_sinkhorn(Qs[s0:s1, h0:h1], Ks[s0:s1, h0:h1], Vs[s0:s1, h0:h1], None, None, None,
+                                          eps[h0:h1], None, lmu[s0:s1, h0:h1], lnu[s0:s1, h0:h1], K_iter=K_iter,
+                                          lam=lam, mask=None if ms is None else ms[s0:s1], cg_opts=cg_opts)
         for t in (O, lu, lv):
             t.record_stream(cur)
-        res.append((b, h0, h1, O, lu, lv))
+        res.append((s0, s1, h0, h1, O, lu, lv))
     for s in pool:
         if s is not cur:
             cur.wait_stream(s)
-    return res
+    return order, res

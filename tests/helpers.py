@@ -10,9 +10,10 @@ from oracle import sinkhorn_oracle as orc
 
 
 def make_inputs(B, H, N, d, *, seed=0, dtype=torch.bfloat16, eps=1.0, uniform=True, lengths=None,
-                device="cuda"):
+                valid=None, device="cuda"):
     """Q, K, V ~ N(0,1) cast to `dtype`; marginals uniform or softmax(N(0,1)) over
-    valid positions (padded entries -1e9); optional per-sample valid lengths."""
+    valid positions (padded entries -1e9); optional per-sample valid lengths, or
+    an explicit (B, N) 0/1 mask `valid` of any pattern."""
     g = torch.Generator().manual_seed(seed)
     Q = torch.randn(B, H, N, d, generator=g).to(dtype)
     K = torch.randn(B, H, N, d, generator=g).to(dtype)
@@ -22,6 +23,8 @@ def make_inputs(B, H, N, d, *, seed=0, dtype=torch.bfloat16, eps=1.0, uniform=Tr
         mask = torch.zeros(B, N)
         for b, L in enumerate(lengths):
             mask[b, :L] = 1.0
+    if valid is not None:
+        mask = valid.float().cpu()
     valid = torch.ones(B, N) if mask is None else mask
     if uniform:
         cnt = valid.sum(-1, keepdim=True)

@@ -5,7 +5,7 @@ import random
 
 import pytest
 
-from deepfold.model.kernels.sinkhorn_bhshard import partition_problems
+from deepfold.model.kernels.sinkhorn_bhshard import partition_problems, rank_blocks
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
@@ -31,3 +31,24 @@ def test_partition_covers_balances_and_keeps_views_contiguous(world):
         total = sum(loads)
         biggest = max(lengths) ** 2
         assert max(loads) <= total / world + biggest + 1e-9
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_rank_blocks_are_rectangles_of_the_sorted_batch(world):
+    rng = random.Random(100 + world)
+    for _ in range(20):
+        B, H = rng.randint(1, 9), rng.choice([1, 4, 16])
+        lengths = [rng.randint(64, 1024) for _ in range(B)]
+        covered = set()
+        for r in range(world):
+            order, blocks = rank_blocks(lengths, H, world, r)
+            assert sorted(order) == list(range(B))
+            assert all(lengths[order[i]] >= lengths[order[i + 1]] for i in range(B - 1))
+            assert len(blocks) <= 3
+            for s0, s1, h0, h1 in blocks:
+                assert s0 < s1 and h0 < h1 and (s1 - s0 == 1 or (h0, h1) == (0, H))
+                for sp in range(s0, s1):
+                    for h in range(h0, h1):
+                        assert (order[sp], h) not in covered
+                        covered.add((order[sp], h))
+        assert covered == {(b, h) for b in range(B) for h in range(H)}

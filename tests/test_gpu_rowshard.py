@@ -51,10 +51,11 @@ def test_two_gpu_row_sharded_matches_single_gpu():
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
-def test_bh_chunks_on_streams_match_full_batch():
-    """(batch, head) chunks from the length^2 partition, run on a stream pool,
-    give the outputs and gradients of one full-batch call."""
-    from deepfold.model.kernels.sinkhorn_bhshard import bh_sharded_flash_sinkhorn, partition_problems
+def test_bh_blocks_on_streams_match_full_batch():
+    """The (batch, head) share of every rank of a 3-GPU partition, run here one
+    after another (sorted batch, blocks on a stream pool), gives the outputs
+    and gradients of one full-batch call."""
+    from deepfold.model.kernels.sinkhorn_bhshard import bh_sharded_flash_sinkhorn
 
     lengths = [600, 200, 520]
     inp = make_inputs(3, 4, 600, 64, seed=41, eps=0.5, uniform=False, lengths=lengths)
@@ -65,14 +66,16 @@ def test_bh_chunks_on_streams_match_full_batch():
     ref_g = torch.autograd.grad(O, leaves, grad_outputs=inp["dO"])
     leaves2 = [inp[k].clone().requires_grad_(True) for k in ("Q", "K", "V")]
     outs, gos = [], []
-    for chunks in partition_problems(lengths, 4, 3):   # every rank's chunks, run here one after another
-        res = bh_sharded_flash_sinkhorn(chunks, *leaves2, inp["eps"], inp["log_mu"], inp["log_nu"], 20, 1.0,
-                                        mask=inp["mask"], cg_opts=cg)
-        for b, h0, h1, Oc, luc, lvc in res:
-            assert float((Oc - O[b:b + 1, h0:h1]).detach().abs().max()) <= 1e-5
-            assert float((luc - lu[b:b + 1, h0:h1]).abs().max()) <= 1e-5
-            outs.append(Oc)
-            gos.append(inp["dO"][b:b + 1, h0:h1])
+    for rank in range(3):
+        order, res = bh_sharded_flash_sinkhorn(*leaves2, inp["eps"], inp["log_mu"], inp["log_nu"], 20, 1.0,
+                                               lengths, 3, rank, mask=inp["mask"], cg_opts=cg)
+        for s0, s1, h0, h1, Oc, luc, lvc in res:
+            for k, sp in enumerate(range(s0, s1)):
+                b = order[sp]
+                assert float((Oc[k] - O[b, h0:h1]).detach().abs().max()) <= 1e-5
+                assert float((luc[k] - lu[b, h0:h1]).abs().max()) <= 1e-5
+                outs.append(Oc[k])
+                gos.append(inp["dO"][b, h0:h1])
     got_g = torch.autograd.grad(outs, leaves2, grad_outputs=gos)
     torch.cuda.synchronize()
     for a, b in zip(ref_g, got_g):

@@ -45,6 +45,26 @@ def test_stream_padded_varlen_unbalanced():
     assert mask[1, 333:].sum() == 0
 
 
+def gapped_mask(N):
+    """Batch 0: valid on [200, 260) and [300, 590) only (a leading gap longer than a
+    tile, a hole, fully masked row blocks at both ends); batch 1: all valid."""
+    m = torch.zeros(2, N)
+    m[0, 200:260] = 1.0
+    m[0, 300:590] = 1.0
+    m[1] = 1.0
+    return m
+
+
+def test_stream_gapped_mask_skips_empty_tiles():
+    """Tiles and row blocks outside a batch element's valid range are skipped;
+    results still match the oracle, and masked rows are exact zeros."""
+    inp = make_inputs(2, 2, 896, 64, seed=9, eps=0.5, uniform=False, valid=gapped_mask(896))
+    O, _, lu, lv, _ = check_forward(inp, 25, 1.0)
+    m = inp["mask"].cpu().numpy()[0] == 0
+    assert np.all(O.cpu().numpy()[0][:, m] == 0.0)
+    assert np.all(lu.cpu().numpy()[0][:, m] == 0.0) and np.all(lv.cpu().numpy()[0][:, m] == 0.0)
+
+
 def test_stream_d32_ragged_tile():
     """d = 32 beyond the resident range, N not a multiple of the 128-column tile."""
     inp = make_inputs(1, 3, 700, 32, seed=5, eps=1.0)
@@ -87,6 +107,14 @@ def test_stream_backward_padded_unbalanced_marginals():
     check(g, ref)
     for k in ("dlog_mu", "dlog_nu"):
         assert rel_err(g[k], ref[k]) <= 2e-2, k
+
+
+def test_stream_backward_gapped_mask():
+    """Backward with a gapped, non-prefix mask (empty tiles and row blocks skipped)."""
+    inp = make_inputs(2, 2, 896, 64, seed=13, eps=0.5, uniform=False, valid=gapped_mask(896))
+    g = grads(inp, 60, 1.0)
+    _, ref = oracle_run(inp, 60, 1.0)
+    check(g, ref)
 
 
 def test_stream_backward_d32_ragged():
