@@ -83,7 +83,7 @@ int check_stream_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspac
   if (p->cost_mode != DFS_COST_QK || a->pos_weight || a->w_dist || p->threshold > 0.0f || a->T_norm ||
       (a->x_centroid && !a->O))
     return DFS_ERR_UNSUPPORTED;
-  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
+  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N, p->d) || !aligned16(workspace))
     return DFS_ERR_WORKSPACE;
   return DFS_OK;
 }
@@ -108,7 +108,7 @@ int check_bwd_args(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_
 // streamed path: no position / geometry terms and none of their gradients
 int check_stream_bwd(const dfs_problem* p, const dfs_bwd_args* a, void* workspace, size_t workspace_bytes) {
   if (a->pos_weight || a->w_dist || a->dx_res || a->dpos_weight || a->dw_dist) return DFS_ERR_UNSUPPORTED;
-  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
+  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N, p->d) || !aligned16(workspace))
     return DFS_ERR_WORKSPACE;
   return DFS_OK;
 }
@@ -138,9 +138,9 @@ int dfs_max_n(int d) { return (d == 32 || d == 64) ? kStreamMaxN : 0; }
 int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes) {
   if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
   const bool res = resident(p);
-  if (fwd_bytes) *fwd_bytes = res ? 0 : stream_fwd_workspace(p->B, p->H, p->N);
+  if (fwd_bytes) *fwd_bytes = res ? 0 : stream_fwd_workspace(p->B, p->H, p->N, p->d);
   if (bwd_bytes)
-    *bwd_bytes = res ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : stream_bwd_workspace(p->B, p->H, p->N);
+    *bwd_bytes = res ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : stream_bwd_workspace(p->B, p->H, p->N, p->d);
   return DFS_OK;
 }
 

@@ -85,12 +85,85 @@ size_t resident_fwd_smem(int N, int d);
 cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
 cudaError_t stream_fwd_op(int op, const FwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
 cudaError_t stream_bwd_op(int op, const BwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
-size_t stream_fwd_workspace(int B, int H, int N);
+size_t stream_fwd_workspace(int B, int H, int N, int d);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
 cudaError_t launch_stream_bwd(const BwdParams& p, float* ws, cudaStream_t st);
-size_t stream_bwd_workspace(int B, int H, int N);
+size_t stream_bwd_workspace(int B, int H, int N, int d);
 size_t resident_bwd_smem(int N, int d);
 size_t resident_bwd_workspace(int B, int H, int N, int d);
+// TMA-staged row passes of the streamed path (dfs_stream_tma.cu): one launch
+// reduces every row of [row_begin, row_end) over all columns of S = A B^T.
+enum TilePass { TL_LSE = 0, TL_ROWSTATS = 1, TL_MATVEC = 2 };
+struct TileArgs {
+  const void* A;           // (BH, N, d) row operand
+  const void* Bop;         // (BH, N, d) column operand
+  int dtype, d;
+  const float* eps;
+  const float* mask;
+  const float* col_bias;   // (BH, N) column potential, log2 units
+  const float* col_vec;    // MATVEC: v
+  const float* row_bias;   // ROWSTATS, MATVEC: row potential, log2 units
+  const float* row_marg;   // LSE: natural-log row marginal
+  const float* row_scale;  // MATVEC: per-row factor, or null
+  const int32_t* done;     // MATVEC: per-problem skip flags, or null
+  float* row_out;
+  float* row_out_nat;
+  float* row_R;
+  int32_t* status;
+  int B, H, N, row_begin, row_end;
+  float lam;
+};
+// True when the TMA-staged kernels cover this operand type, head dim, length
+// (N >= 128) and the two operand addresses (16-byte aligned); otherwise the
+// register-staged kernels run the pass.
+bool tile_path_ok(int dtype, int d, int N, const void* a, const void* b);
+cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st);
+
+// TMA-staged tile passes of the streamed backward (dfs_stream_bwd_tma.cu) on
+// fp32 copies of the operands kept in the backward workspace.
+struct BtCopies {
+  float* Qf;   // (BH, N, d) row-major fp32 copies
+  float* Kf;
+  float* Vf;
+  float* dOf;
+  float* QT;   // (BH, d, N) transposed fp32 copies
+  float* KT;
+  float* dOT;
+};
+struct BtArgs {
+  const float* A;    // row operands (BH, N, d): S = A B^T, dT = A2 B2^T
+  const float* A2;
+  const float* Bop;  // column operands (BH, N, d)
+  const float* B2;
+  const float* B3;   // transposed accumulation operand (BH, d, N)
+  int d;
+  const float* eps;
+  const float* mask;
+  const float* tv[5];
+  int pot_mask;
+  const float* xvec;
+  int xvec_per_head;
+  const float* rv[5];
+  const float* rxvec;
+  int rxvec_per_head;
+  float* out0;
+  float* out1;
+  float* out2;
+  float* acc;
+  float acc_scale;
+  int32_t* status;
+  int B, H, N, row_begin, row_end;
+};
+enum BtPass { BTP_ROW = 0, BTP_COL = 1, BTP_DQ = 2, BTP_DK = 3, BTP_OUT = 4 };
+size_t bt_copies_bytes(int B, int H, int N, int d);
+bool bt_path_ok(int d, int N, const void* ws);
+BtCopies bt_copies(float* region, int B, int H, int N, int d);
+cudaError_t bt_prep(const BwdParams& bp, const BtCopies& c, cudaStream_t st);
+// fp32 copies of one (BH, N, d) operand: row-major and / or transposed (either may be null)
+cudaError_t bt_convert(const void* src, int dtype, float* row_out, float* t_out, int BH, int N, int d,
+                       cudaStream_t st);
+cudaError_t launch_bt_pass(int mode, const BtArgs& a, cudaStream_t st);
+
 cudaError_t launch_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K,
                                 cudaStream_t st);
 

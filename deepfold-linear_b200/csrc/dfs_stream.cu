@@ -331,8 +331,11 @@ cudaError_t launch_stream(int mode, int d, const StreamParams& p, cudaStream_t s
   return cudaErrorInvalidValue;
 }
 
-size_t stream_fwd_workspace(int B, int H, int N) {
-  return 4 * sizeof(float) * static_cast<size_t>(B) * H * N;  // f, g (log2), m, R
+// f, g (log2), m, R; then fp32 copies Q, K (row-major) and V^T (transposed)
+// for the TMA-staged transport-output pass
+size_t stream_fwd_workspace(int B, int H, int N, int d) {
+  const size_t n = static_cast<size_t>(B) * H * N;
+  return 4 * sizeof(float) * n + 3 * sizeof(float) * n * d + 256;
 }
 
 // One phase of the streamed forward on rows [r0, r1) (the whole problem for a
@@ -365,6 +368,30 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
   p.row_begin = r0;
   p.row_end = r1;
   p.lam = fp.lam;
+  // the TMA-staged kernels take the row passes whenever they cover the operands
+  const bool tma = tile_path_ok(fp.in_dtype, fp.d, fp.N, fp.Q, fp.K);
+  TileArgs ta{};
+  ta.dtype = fp.in_dtype;
+  ta.d = fp.d;
+  ta.eps = fp.eps;
+  ta.mask = fp.mask;
+  ta.status = fp.status;
+  ta.B = fp.B;
+  ta.H = fp.H;
+  ta.N = fp.N;
+  ta.row_begin = r0;
+  ta.row_end = r1;
+  ta.lam = fp.lam;
+  if (tma && (op == DFS_OP_FWD_ROWS || op == DFS_OP_FWD_COLS)) {
+    const bool rows = op == DFS_OP_FWD_ROWS;  // the column half-update is the row pass on S^T
+    ta.A = rows ? fp.Q : fp.K;
+    ta.Bop = rows ? fp.K : fp.Q;
+    ta.col_bias = rows ? gw : fw;
+    ta.row_marg = rows ? fp.log_mu : fp.log_nu;
+    ta.row_out = rows ? fw : gw;
+    ta.row_out_nat = rows ? fp.log_u : fp.log_v;
+    return launch_tile_pass(TL_LSE, ta, st);
+  }
   if (op == DFS_OP_FWD_ROWS) {
     p.Aop = fp.Q;
     p.Bop = fp.K;
@@ -391,7 +418,55 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     p.row_bias = fw;
     p.row_out = mw;
     p.row_R = Rw;
-    cudaError_t e = launch_stream(SM_ROWSTATS, fp.d, p, st);
+    cudaError_t e;
+    if (tma) {
+      ta.A = fp.Q;
+      ta.Bop = fp.K;
+      ta.col_bias = gw;
+      ta.row_bias = fw;
+      ta.row_out = mw;
+      ta.row_R = Rw;
+      e = launch_tile_pass(TL_ROWSTATS, ta, st);
+      if (e != cudaSuccess) return e;
+      if (bt_path_ok(fp.d, fp.N, ws)) {
+        // O = T_norm V by the TMA-staged tile pass on fp32 copies of Q, K and V^T
+        float* cp = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws + 4 * n) + 255) & ~uintptr_t(255));
+        const size_t nd = n * fp.d;
+        float* Qf = cp;
+        float* Kf = cp + nd;
+        float* VT = cp + 2 * nd;
+        const int BH = fp.B * fp.H;
+        e = bt_convert(fp.Q, fp.in_dtype, Qf, nullptr, BH, fp.N, fp.d, st);
+        if (e == cudaSuccess) e = bt_convert(fp.K, fp.in_dtype, Kf, nullptr, BH, fp.N, fp.d, st);
+        if (e == cudaSuccess) e = bt_convert(fp.V, fp.in_dtype, nullptr, VT, BH, fp.N, fp.d, st);
+        if (e != cudaSuccess) return e;
+        BtArgs ba{};
+        ba.A = Qf;
+        ba.Bop = Kf;
+        ba.B3 = VT;
+        ba.d = fp.d;
+        ba.eps = fp.eps;
+        ba.mask = fp.mask;
+        ba.tv[0] = gw;
+        ba.pot_mask = 1;
+        ba.xvec = fp.x_centroid != nullptr ? fp.x_res : nullptr;
+        ba.rv[0] = fw;
+        ba.rv[1] = mw;
+        ba.rv[2] = Rw;
+        ba.out0 = fp.x_centroid;
+        ba.acc = fp.O;
+        ba.acc_scale = 1.0f;
+        ba.status = fp.status;
+        ba.B = fp.B;
+        ba.H = fp.H;
+        ba.N = fp.N;
+        ba.row_begin = r0;
+        ba.row_end = r1;
+        return launch_bt_pass(BTP_OUT, ba, st);
+      }
+    } else {
+      e = launch_stream(SM_ROWSTATS, fp.d, p, st);
+    }
     if (e != cudaSuccess) return e;
     p.Vop = fp.V;
     p.row_m = mw;

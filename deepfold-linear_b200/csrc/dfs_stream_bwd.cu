@@ -622,9 +622,11 @@ __global__ void __launch_bounds__(kVThreads) sb_final_kernel(VecParams p) {
   }
 }
 
-size_t stream_bwd_workspace(int B, int H, int N) {
+// Slots, per-problem scalars, CG flags and iteration counts, then the fp32
+// operand copies of the TMA-staged tile passes.
+size_t stream_bwd_workspace(int B, int H, int N, int d) {
   const size_t n = static_cast<size_t>(B) * H * N, bh = static_cast<size_t>(B) * H;
-  return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256;
+  return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256 + bt_copies_bytes(B, H, N, d);
 }
 
 constexpr bool same_slot(int a, int b) { return a == b; }
@@ -652,6 +654,22 @@ static_assert(same_slot(WS_F, DFS_WS_BWD_F) && same_slot(WS_G, DFS_WS_BWD_G) && 
 //   BWD_FINAL                    w1, null-space shift, dlog_mu, dlog_nu, CG report
 //   BWD_DQ         rows          dQ
 //   BWD_DKV        columns       dK, dV
+static TileArgs tile_args(const BwdParams& bp, int r0, int r1) {
+  TileArgs ta{};
+  ta.dtype = bp.in_dtype;
+  ta.d = bp.d;
+  ta.eps = bp.eps;
+  ta.mask = bp.mask;
+  ta.status = bp.status;
+  ta.B = bp.B;
+  ta.H = bp.H;
+  ta.N = bp.N;
+  ta.row_begin = r0;
+  ta.row_end = r1;
+  ta.lam = bp.lam;
+  return ta;
+}
+
 cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r1, cudaStream_t st) {
   const int B = bp.B, H = bp.H, N = bp.N, d = bp.d;
   const size_t n = static_cast<size_t>(B) * H * N, nbh = static_cast<size_t>(B) * H;
@@ -681,6 +699,20 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   const unsigned eblocks = static_cast<unsigned>((n + 255) / 256);
   const unsigned pblocks = static_cast<unsigned>(nbh);
 
+  // TMA-staged tile passes on fp32 copies placed after the CG state
+  const bool bt = bt_path_ok(d, N, wsp);
+  const BtCopies cp = bt_copies(reinterpret_cast<float*>(v.iters + nbh), B, H, N, d);
+  BtArgs ba{};
+  ba.d = d;
+  ba.eps = bp.eps;
+  ba.mask = bp.mask;
+  ba.status = bp.status;
+  ba.B = B;
+  ba.H = H;
+  ba.N = N;
+  ba.row_begin = r0;
+  ba.row_end = r1;
+
   StreamBwdParams q{};
   q.dtype = bp.in_dtype;
   q.eps = bp.eps;
@@ -691,10 +723,22 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   q.row_begin = r0;
   q.row_end = r1;
   switch (op) {
-    case DFS_OP_BWD_PREP:
+    case DFS_OP_BWD_PREP: {
       sb_prep_kernel<<<eblocks, 256, 0, st>>>(v);
-      return cudaGetLastError();
+      cudaError_t e = cudaGetLastError();
+      if (e == cudaSuccess && bt) e = bt_prep(bp, cp, st);
+      return e;
+    }
     case DFS_OP_BWD_ROWSTATS:  // m, R, D
+      if (bt) {
+        ba.A = cp.Qf; ba.A2 = cp.dOf; ba.Bop = cp.Kf; ba.B2 = cp.Vf;
+        ba.tv[0] = slot(WS_G); ba.pot_mask = 1;
+        ba.rv[0] = slot(WS_F);
+        ba.xvec = bp.dxc ? bp.x_res : nullptr; ba.xvec_per_head = 0;
+        ba.rxvec = bp.dxc; ba.rxvec_per_head = 1;
+        ba.out0 = slot(WS_M); ba.out1 = slot(WS_R); ba.out2 = slot(WS_D);
+        return launch_bt_pass(BTP_ROW, ba, st);
+      }
       q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V;
       q.tv[0] = slot(WS_G);
       q.rv[0] = slot(WS_F);
@@ -705,7 +749,18 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
     case DFS_OP_BWD_ROWDERIVE:
       sb_rowderive_kernel<<<eblocks, 256, 0, st>>>(v);
       return cudaGetLastError();
-    case DFS_OP_BWD_COLSTATS:  // c, g_v
+    case DFS_OP_BWD_COLSTATS:  // c, g_v (and, on the TMA-staged path, dV = T_norm^T dO)
+      if (bt) {
+        ba.A = cp.Kf; ba.A2 = cp.Vf; ba.Bop = cp.Qf; ba.B2 = cp.dOf; ba.B3 = cp.dOT;
+        ba.tv[0] = slot(WS_F); ba.tv[1] = slot(WS_FM); ba.tv[2] = slot(WS_INVR); ba.tv[3] = slot(WS_D);
+        ba.pot_mask = 3;
+        ba.rv[0] = slot(WS_G);
+        ba.xvec = bp.dxc; ba.xvec_per_head = 1;
+        ba.rxvec = bp.dxc ? bp.x_res : nullptr; ba.rxvec_per_head = 0;
+        ba.out0 = slot(WS_C); ba.out1 = slot(WS_GV);
+        ba.acc = bp.dV; ba.acc_scale = 1.0f;
+        return launch_bt_pass(BTP_COL, ba, st);
+      }
       q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
       q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);
       q.rv[0] = slot(WS_G);
@@ -721,6 +776,15 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       return cudaGetLastError();
     case DFS_OP_BWD_P_U:   // t = D1^-1 P u2 (problems whose CG has stopped are skipped)
     case DFS_OP_BWD_P_X:   // s = P x2
+      if (tile_path_ok(bp.in_dtype, d, N, bp.Q, bp.K)) {
+        TileArgs ta = tile_args(bp, r0, r1);
+        ta.A = bp.Q; ta.Bop = bp.K;
+        ta.col_bias = slot(WS_G); ta.col_vec = slot(op == DFS_OP_BWD_P_U ? WS_U2 : WS_X2);
+        ta.row_bias = slot(WS_F); ta.row_scale = op == DFS_OP_BWD_P_U ? slot(WS_D1I) : nullptr;
+        ta.done = op == DFS_OP_BWD_P_U ? v.done : nullptr;
+        ta.row_out = slot(op == DFS_OP_BWD_P_U ? WS_T : WS_S);
+        return launch_tile_pass(TL_MATVEC, ta, st);
+      }
       q.Aop = bp.Q; q.Bop = bp.K;
       q.tv[0] = slot(WS_G); q.tv[1] = slot(op == DFS_OP_BWD_P_U ? WS_U2 : WS_X2);
       q.rv[0] = slot(WS_F); q.rv[1] = op == DFS_OP_BWD_P_U ? slot(WS_D1I) : nullptr;
@@ -728,6 +792,15 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       q.out0 = slot(op == DFS_OP_BWD_P_U ? WS_T : WS_S);
       return launch_stream_bwd_pass(SB_MATVEC, d, q, st);
     case DFS_OP_BWD_PT_T:  // s = P^T t (skips stopped problems once the CG has started)
+      if (tile_path_ok(bp.in_dtype, d, N, bp.K, bp.Q)) {
+        TileArgs ta = tile_args(bp, r0, r1);
+        ta.A = bp.K; ta.Bop = bp.Q;
+        ta.col_bias = slot(WS_F); ta.col_vec = slot(WS_T);
+        ta.row_bias = slot(WS_G);
+        ta.done = v.done;
+        ta.row_out = slot(WS_S);
+        return launch_tile_pass(TL_MATVEC, ta, st);
+      }
       q.Aop = bp.K; q.Bop = bp.Q;
       q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_T);
       q.rv[0] = slot(WS_G);
@@ -742,6 +815,16 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       sb_final_kernel<<<pblocks, kVThreads, 0, st>>>(v);
       return cudaGetLastError();
     case DFS_OP_BWD_DQ:    // dQ = dS K / (eps_h sqrt d)
+      if (bt) {
+        ba.A = cp.Qf; ba.A2 = cp.dOf; ba.Bop = cp.Kf; ba.B2 = cp.Vf; ba.B3 = cp.KT;
+        ba.tv[0] = slot(WS_G); ba.tv[1] = slot(WS_X2); ba.pot_mask = 1;
+        ba.rv[0] = slot(WS_F); ba.rv[1] = slot(WS_FM); ba.rv[2] = slot(WS_INVR); ba.rv[3] = slot(WS_D);
+        ba.rv[4] = slot(WS_W1);
+        ba.xvec = bp.dxc ? bp.x_res : nullptr; ba.xvec_per_head = 0;
+        ba.rxvec = bp.dxc; ba.rxvec_per_head = 1;
+        ba.acc = bp.dQ; ba.acc_scale = -1.0f;
+        return launch_bt_pass(BTP_DQ, ba, st);
+      }
       q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V; q.B3op = bp.K;
       q.tv[0] = slot(WS_G); q.tv[1] = slot(WS_X2);
       q.rv[0] = slot(WS_F); q.rv[1] = slot(WS_FM); q.rv[2] = slot(WS_INVR); q.rv[3] = slot(WS_D);
@@ -751,7 +834,17 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       q.acc0 = bp.dQ;
       q.acc_scale0 = -1.0f;  // negative: 1/(eps_h sqrt d) of the problem's head
       return launch_stream_bwd_pass(SB_DQ, d, q, st);
-    case DFS_OP_BWD_DKV:   // dK = dS^T Q / (eps_h sqrt d), dV = T_norm^T dO
+    case DFS_OP_BWD_DKV:   // dK = dS^T Q / (eps_h sqrt d), dV = T_norm^T dO (dV already done on the TMA path)
+      if (bt) {
+        ba.A = cp.Kf; ba.A2 = cp.Vf; ba.Bop = cp.Qf; ba.B2 = cp.dOf; ba.B3 = cp.QT;
+        ba.tv[0] = slot(WS_F); ba.tv[1] = slot(WS_FM); ba.tv[2] = slot(WS_INVR); ba.tv[3] = slot(WS_D);
+        ba.tv[4] = slot(WS_W1); ba.pot_mask = 3;
+        ba.rv[0] = slot(WS_G); ba.rv[1] = slot(WS_X2);
+        ba.xvec = bp.dxc; ba.xvec_per_head = 1;
+        ba.rxvec = bp.dxc ? bp.x_res : nullptr; ba.rxvec_per_head = 0;
+        ba.acc = bp.dK; ba.acc_scale = -1.0f;
+        return launch_bt_pass(BTP_DK, ba, st);
+      }
       q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
       q.B3op = bp.Q; q.B4op = bp.dO; q.b4_f32 = 1;
       q.tv[0] = slot(WS_F); q.tv[1] = slot(WS_FM); q.tv[2] = slot(WS_INVR); q.tv[3] = slot(WS_D);

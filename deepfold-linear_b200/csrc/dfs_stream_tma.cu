@@ -1,0 +1,422 @@
+// dfs_stream_tma.cu -- TMA-staged, warp-specialised row passes of the streamed
+// path for sm_100a.
+//
+// Three passes dominate a streamed call: the Sinkhorn half-update (a row
+// log-sum-exp, run twice per iteration: rows, then the same pass on S^T), the
+// row statistics of the transport output, and the plan-vector product of the
+// IFT conjugate-gradient solve (twice per CG iteration).  All three stream the
+// columns of S = A B^T past a block of 128 rows and reduce each row on the fly:
+//
+//   LSE       f_i = kappa (a_i - LSE_j(x_ij)),          x = S' + g_j  (log2 units)
+//   ROWSTATS  m_i = f_i + max_j x_ij, R_i = sum_j exp2(x_ij - max_j x_ij)
+//   MATVEC    y_i = c_i sum_j exp2(x_ij + f_i) v_j
+//
+// (S' = S log2(e) / (eps sqrt d); a masked column has g_j = -inf.)  One CTA per
+// block of 128 rows; its ten warps split the work so that no thread that does
+// arithmetic ever waits on global memory:
+//
+//   warp 8      producer: one TMA load of the row block (A), then column tiles
+//               of B (128 rows of the column operand) into a ring of NS stages,
+//               with the tile's column bias (and vector) staged beside it
+//   warp 9      MMA: S tile = A B_tile^T, tcgen05.mma kind::f16 (bf16 / fp16
+//               operands, exactly the reference's products of bf16 inputs) or
+//               kind::tf32 (fp32 operands), fp32 into one of two TMEM buffers
+//   warps 0-7   epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (thread =
+//               row) and columns 64 (w / 4) .. + 63 of every tile with
+//               tcgen05.ld, folding them into a running reduction per row;
+//               the two halves of each row are merged at the end
+//
+// Two epilogue warps per lane quadrant, and two CTAs per SM, give every SM
+// sub-partition four warps of exp2 / FMA work to interleave.
+//
+// The MMA of tile t+1 runs while the epilogue works on tile t.  Operands are
+// K-major with 128-byte swizzle, the layout TMA writes for a box 128 bytes wide;
+// a 256-byte row (fp32, d = 64) is two such boxes side by side.  The kernels
+// cover 128- and 256-byte operand rows (d = 64, or fp32 with d = 32); other
+// shapes, and operands not aligned to 16 bytes, keep the register-staged
+// kernels of dfs_stream.cu / dfs_stream_bwd.cu.
+#include <mutex>
+
+#include "dfs_tma.cuh"
+
+namespace dfs {
+
+constexpr int kTThreads = 320;  // warps 0-7 epilogue, 8 producer, 9 MMA
+constexpr int kTEpi = 256;      // epilogue threads
+constexpr int kTProducer = 8, kTMma = 9;
+constexpr int kTCols = 128;     // columns per tile
+
+struct TileParams {
+  CUtensorMap tmA;         // row operand, (BH, N, d) viewed as the 3-D tensor {d, N, BH}
+  CUtensorMap tmB;         // column operand, same view
+  const float* eps;        // (H,)
+  const float* mask;       // (B, N) nonzero = valid, or null
+  const float* col_bias;   // (BH, N) potential of the columns, log2 units
+  const float* col_vec;    // MATVEC: (BH, N) the vector v
+  const float* row_bias;   // ROWSTATS, MATVEC: (BH, N) potential of the rows, log2 units
+  const float* row_marg;   // LSE: (BH, N) natural-log marginal of the rows
+  const float* row_scale;  // MATVEC: (BH, N) factor c_i, or null (1)
+  const int32_t* done;     // MATVEC: (BH) skip problems whose flag is nonzero, or null
+  float* row_out;          // LSE: potential (log2); ROWSTATS: m; MATVEC: y
+  float* row_out_nat;      // LSE: the potential in natural-log units, or null
+  float* row_R;            // ROWSTATS: R
+  int32_t* status;         // DFS_ERR_DEVICE_TIMEOUT is OR-ed in if a wait gives up, or null
+  int B, H, N;
+  int row_begin, row_end;  // rows this launch handles
+  float lam;
+};
+
+template <int DT, int D>
+struct TileCfg {
+  static constexpr int ESZ = DT == DFS_F32 ? 4 : 2;
+  static constexpr int RB = D * ESZ;       // bytes per operand row
+  static_assert(RB == 128 || RB == 256, "128- or 256-byte operand rows");
+  static constexpr int G = RB / 128;       // 128-byte swizzle atoms across a row
+  static constexpr int KSTEPS = RB / 32;   // one MMA per 32 bytes of K
+  static constexpr uint32_t GROUP = 128u * 128u;  // bytes of one atom column of a 128-row tile
+  static constexpr uint32_t TILE = 128u * RB;     // bytes of a 128-row tile
+  static constexpr int NS = RB == 128 ? 4 : 2;    // stages of the column-tile ring
+  static constexpr uint32_t OFF_A = 0;
+  static constexpr uint32_t OFF_B = OFF_A + TILE;
+  static constexpr uint32_t OFF_CB = OFF_B + NS * TILE;   // NS x 128 column bias
+  static constexpr uint32_t OFF_CV = OFF_CB + NS * 512u;  // NS x 128 column vector
+  static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 2 x 128 partials of the second column half
+  static constexpr uint32_t OFF_BAR = OFF_MRG + 1024u;
+  static constexpr uint32_t NBAR = 2 * NS + 5;            // full, empty, sfull x2, sempty x2, afull
+  static constexpr uint32_t OFF_SLOT = OFF_BAR + 8 * NBAR;
+  static constexpr uint32_t OFF_RED = OFF_SLOT + 16;
+  static constexpr uint32_t NEED = OFF_RED + 4u * 2 * (kTThreads / 32) + 1024;  // + alignment slack
+  // at least 80 KB: at most two CTAs per SM, whose 2 x 256 TMEM columns always fit
+  static constexpr uint32_t SMEM = NEED > 81920u ? NEED : 81920u;
+  static_assert(NEED <= 113u * 1024u, "two CTAs per SM");
+};
+
+// Rows [row0, row0 + 128) of problem `prob` into a tile buffer (G boxes of 128
+// bytes x 128 rows; rows beyond N arrive as zeros).
+template <int DT, int D>
+DFS_DEV void tma_tile(uint32_t dst, const CUtensorMap* tm, int row0, int prob, uint32_t bar) {
+  using C = TileCfg<DT, D>;
+#pragma unroll
+  for (int g = 0; g < C::G; ++g) tma_load_3d(dst + g * C::GROUP, tm, g * (128 / C::ESZ), row0, prob, bar);
+}
+
+// S (128 x 128, TMEM) = A (128 x d) B (128 x d)^T from two K-major swizzled tiles.
+template <int DT, int D>
+DFS_DEV void tile_mma(uint32_t d_tmem, uint32_t a_s, uint32_t b_s) {
+  using C = TileCfg<DT, D>;
+  const uint64_t a0 = sw128_desc(a_s, 16, 1024), b0 = sw128_desc(b_s, 16, 1024);
+#pragma unroll
+  for (int kk = 0; kk < C::KSTEPS; ++kk) {
+    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * C::GROUP + (kk & 3) * 32) >> 4);
+    if constexpr (DT == DFS_F32)
+      mma_tf32(d_tmem, a0 + off, b0 + off, idesc_tf32(128, kTCols, 0, 0), kk > 0 ? 1u : 0u);
+    else
+      mma_f16(d_tmem, a0 + off, b0 + off, idesc_f16(128, kTCols, DT == DFS_BF16), kk > 0 ? 1u : 0u);
+  }
+}
+
+template <int MODE, int DT, int D>
+__global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constant__ TileParams p) {
+  using C = TileCfg<DT, D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sA = smem_u32(base + C::OFF_A), sB = smem_u32(base + C::OFF_B);
+  float* cbs = reinterpret_cast<float*>(base + C::OFF_CB);
+  float* cvs = reinterpret_cast<float*>(base + C::OFF_CV);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + C::OFF_BAR);  // [NS] tile staged
+  uint64_t* empty = full + C::NS;                                      // [NS] tile consumed
+  uint64_t* sfull = empty + C::NS;                                     // [2] S buffer written
+  uint64_t* sempty = sfull + 2;                                        // [2] S buffer read
+  uint64_t* afull = sempty + 2;                                        // row block staged
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(base + C::OFF_SLOT);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nrb = (p.row_end - p.row_begin + 127) / 128;
+  const int prob = blockIdx.x / nrb, rb = blockIdx.x % nrb;
+  if (MODE == TL_MATVEC && p.done != nullptr && p.done[prob] != 0) return;  // uniform over the CTA
+  const int bb = prob / p.H, hh = prob % p.H;
+  const int N = p.N;
+  const size_t bh = static_cast<size_t>(prob);
+  const int r0 = p.row_begin + 128 * rb;
+  // only column tiles holding a valid point are visited (a masked column adds
+  // exactly nothing); a block without a valid row visits none
+  int vlo, vhi;
+  valid_extent<kTThreads>(p.mask, bb, N, reinterpret_cast<int*>(base + C::OFF_RED), vlo, vhi);
+  const int rhi = min(min(r0 + 128, p.row_end), N);
+  const bool live = max(r0, vlo) < min(rhi, vhi);
+  const int t_begin = live ? vlo / kTCols : 0;
+  const int ntiles = live ? (vhi + kTCols - 1) / kTCols - t_begin : 0;
+
+  if (warp == 0) tmem_alloc(tslot, 256);
+  if (tid == 32 * kTProducer) {
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(&full[s], 32);     // every producer lane (bias stores); the TMA bytes as transactions
+      mbar_init(&empty[s], 1 + 8);  // MMA completion + the 8 epilogue warps (bias reads)
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sfull[b], 1);
+      mbar_init(&sempty[b], 8);
+    }
+    mbar_init(afull, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  int err = 0;
+
+  if (warp == kTProducer) {
+    // ------------------------------------------------------------ producer
+    if (ntiles > 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(smem_u32(afull), C::TILE);
+        tma_tile<DT, D>(sA, &p.tmA, r0, prob, smem_u32(afull));
+      }
+      // the tile's column bias (and vector), 4 columns per lane, fetched one tile
+      // ahead so that their global latency overlaps the wait for a free stage
+      float pc[4], pw[4];
+      auto fetch = [&](int u) {
+        const int c0 = (t_begin + u) * kTCols;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j = c0 + lane + 32 * q;
+          const bool cin = j < N;
+          const bool cok = cin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + j] != 0.0f);
+          pc[q] = cok ? p.col_bias[bh * N + j] : -INFINITY;
+          if constexpr (MODE == TL_MATVEC) pw[q] = cin ? p.col_vec[bh * N + j] : 0.0f;
+        }
+      };
+      fetch(0);
+#pragma unroll 1
+      for (int u = 0; u < ntiles; ++u) {
+        const int s = u % C::NS;
+        if (u >= C::NS && !mbar_wait(&empty[s], ((u / C::NS) - 1) & 1)) err = 1;
+        const int c0 = (t_begin + u) * kTCols;
+        if (lane == 0) {
+          mbar_expect_tx(smem_u32(&full[s]), C::TILE);
+          tma_tile<DT, D>(sB + s * C::TILE, &p.tmB, c0, prob, smem_u32(&full[s]));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          cbs[s * 128 + lane + 32 * q] = pc[q];
+          if constexpr (MODE == TL_MATVEC) cvs[s * 128 + lane + 32 * q] = pw[q];
+        }
+        mbar_arrive(&full[s]);
+        if (u + 1 < ntiles) fetch(u + 1);
+      }
+      // the last stages' releases: every MMA completion has arrived before exit
+      for (int u = max(0, ntiles - C::NS); u < ntiles; ++u)
+        if (!mbar_wait(&empty[u % C::NS], (u / C::NS) & 1)) err = 1;
+    }
+  } else if (warp == kTMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (ntiles > 0) {
+      if (!mbar_wait(afull, 0)) err = 1;
+#pragma unroll 1
+      for (int u = 0; u < ntiles; ++u) {
+        const int s = u % C::NS, b = u & 1;
+        if (!mbar_wait(&full[s], (u / C::NS) & 1)) err = 1;
+        if (u >= 2 && !mbar_wait(&sempty[b], ((u >> 1) - 1) & 1)) err = 1;
+        tc_fence_after();
+        if (lane == 0) {
+          tile_mma<DT, D>(tbase + b * kTCols, sA, sB + s * C::TILE);
+          mma_commit(&sfull[b]);
+          mma_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3, half = warp >> 2;
+    const int lrow = 32 * quad + lane, row = r0 + lrow;
+    const bool rin = row < p.row_end && row < N;
+    const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
+    const float eps_h = p.eps[hh];
+    const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
+    const float fi = (MODE != TL_LSE && rin) ? p.row_bias[bh * N + row] : 0.0f;
+    const uint32_t tlane = static_cast<uint32_t>(32 * quad) << 16;
+    float m = kNeg, sum = 0.0f;  // running max and sum of this half's columns (LSE, ROWSTATS)
+    float acc = 0.0f;            // MATVEC
+#pragma unroll 1
+    for (int u = 0; u < ntiles; ++u) {
+      const int s = u % C::NS, b = u & 1;
+      if (!mbar_wait(&full[s], (u / C::NS) & 1)) err = 1;  // the producer's bias stores
+      if (!mbar_wait(&sfull[b], (u >> 1) & 1)) err = 1;
+      tc_fence_after();
+#pragma unroll 1
+      for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
+        float v[32];
+        tmem_ld32(tbase + tlane + b * kTCols + 32 * ch, v);
+        const float* cb = cbs + s * 128 + 32 * ch;
+        if constexpr (MODE == TL_MATVEC) {
+          const float* cv = cvs + s * 128 + 32 * ch;
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 0; k < 32; ++k) a[k & 3] = fmaf(ex2(fmaf(v[k], scale, cb[k] + fi)), cv[k], a[k & 3]);
+          acc += (a[0] + a[1]) + (a[2] + a[3]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = fmaf(v[k], scale, cb[k]);
+          float mx[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mx[q] = fmaxf(fmaxf(v[4 * q], v[4 * q + 1]), fmaxf(v[4 * q + 2], v[4 * q + 3]));
+          const float cm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+          const float mn = fmaxf(m, cm);
+          float a[4] = {sum * ex2(m - mn), 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 0; k < 32; ++k) a[k & 3] += ex2(v[k] - mn);
+          m = mn;
+          sum = (a[0] + a[1]) + (a[2] + a[3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sempty[b]);
+        mbar_arrive(&empty[s]);
+      }
+    }
+    // merge the two column halves of each row (epilogue threads only)
+    float* mrg = reinterpret_cast<float*>(base + C::OFF_MRG);
+    if (half == 1) {
+      mrg[lrow] = MODE == TL_MATVEC ? acc : m;
+      mrg[128 + lrow] = sum;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
+    if (half == 0 && rin) {
+      const size_t o = bh * N + row;
+      if constexpr (MODE == TL_MATVEC) {
+        acc += mrg[lrow];
+        p.row_out[o] = rok ? acc * (p.row_scale != nullptr ? p.row_scale[o] : 1.0f) : 0.0f;
+      } else {
+        const float m2 = mrg[lrow], s2 = mrg[128 + lrow];
+        const float mm = fmaxf(m, m2);
+        sum = sum * ex2(m - mm) + s2 * ex2(m2 - mm);
+        m = mm;
+        if constexpr (MODE == TL_LSE) {
+          const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
+          float f = 0.0f;
+          if (rok && sum > 0.0f) f = kap * (p.row_marg[o] * kLog2e - (m + lg2(sum)));
+          p.row_out[o] = f;
+          if (p.row_out_nat) p.row_out_nat[o] = f * kLn2;
+        } else {
+          p.row_out[o] = rok ? m + fi : 0.0f;
+          p.row_R[o] = rok ? sum : 0.0f;
+        }
+      }
+    }
+  }
+  if (err && p.status != nullptr) atomicOr(p.status, DFS_ERR_DEVICE_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
+// ---------------------------------------------------------------- host side
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool tmap_available() { return encode_fn() != nullptr; }
+
+bool make_tmap(CUtensorMap* tm, const void* ptr, int dtype, int inner, int rows, int BH, int box_inner,
+               int box_rows) {
+  const int esz = dtype == DFS_F32 ? 4 : 2;
+  if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || box_inner * esz != 128) return false;
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const CUtensorMapDataType ty = dtype == DFS_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == DFS_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(BH)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner) * esz, static_cast<cuuint64_t>(rows) * inner * esz};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows), 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(tm, ty, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
+template <int MODE, int DT, int D>
+cudaError_t launch_tile_mdd(const TileParams& p, cudaStream_t st) {
+  using C = TileCfg<DT, D>;
+  auto kern = tile_kernel<MODE, DT, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int nrb = (p.row_end - p.row_begin + 127) / 128;
+  kern<<<p.B * p.H * nrb, kTThreads, C::SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_tile_m(int dtype, int d, const TileParams& p, cudaStream_t st) {
+  if (d == 64) {
+    if (dtype == DFS_BF16) return launch_tile_mdd<MODE, DFS_BF16, 64>(p, st);
+    if (dtype == DFS_F16) return launch_tile_mdd<MODE, DFS_F16, 64>(p, st);
+    return launch_tile_mdd<MODE, DFS_F32, 64>(p, st);
+  }
+  return launch_tile_mdd<MODE, DFS_F32, 32>(p, st);
+}
+
+}  // namespace
+
+bool tile_path_ok(int dtype, int d, int N, const void* a, const void* b) {
+  const bool shape = (d == 64 || (d == 32 && dtype == DFS_F32)) && N >= 128;  // boxes of 128 rows
+  return shape && a != nullptr && b != nullptr &&
+         ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u) == 0 && encode_fn() != nullptr;
+}
+
+cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
+  if (t.row_end <= t.row_begin) return cudaSuccess;
+  TileParams p{};
+  const int box_inner = t.dtype == DFS_F32 ? 32 : 64;  // 128 bytes
+  if (!make_tmap(&p.tmA, t.A, t.dtype, t.d, t.N, t.B * t.H, box_inner, 128) ||
+      !make_tmap(&p.tmB, t.Bop, t.dtype, t.d, t.N, t.B * t.H, box_inner, 128))
+    return cudaErrorInvalidValue;
+  p.eps = t.eps;
+  p.mask = t.mask;
+  p.col_bias = t.col_bias;
+  p.col_vec = t.col_vec;
+  p.row_bias = t.row_bias;
+  p.row_marg = t.row_marg;
+  p.row_scale = t.row_scale;
+  p.done = t.done;
+  p.row_out = t.row_out;
+  p.row_out_nat = t.row_out_nat;
+  p.row_R = t.row_R;
+  p.status = t.status;
+  p.B = t.B;
+  p.H = t.H;
+  p.N = t.N;
+  p.row_begin = t.row_begin;
+  p.row_end = t.row_end;
+  p.lam = t.lam;
+  if (mode == TL_LSE) return launch_tile_m<TL_LSE>(t.dtype, t.d, p, st);
+  if (mode == TL_ROWSTATS) return launch_tile_m<TL_ROWSTATS>(t.dtype, t.d, p, st);
+  return launch_tile_m<TL_MATVEC>(t.dtype, t.d, p, st);
+}
+
+}  // namespace dfs

@@ -1,0 +1,53 @@
+// dfs_tma.cuh -- TMA staging helpers shared by the warp-specialised streamed
+// kernels (dfs_stream_tma.cu, dfs_stream_bwd_tma.cu).
+#pragma once
+
+#include <cuda.h>
+
+#include "dfs_slab.cuh"
+
+namespace dfs {
+
+// Instruction descriptor, kind::f16 (fp16 or bf16 operands), fp32 accumulate,
+// both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+DFS_DEV void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+
+// Adds `bytes` to the transaction count of the current phase without arriving.
+DFS_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+DFS_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// TMA load of the box at element coordinates (x, y, z) into shared memory,
+// completion counted in bytes on `bar`.  No multicast.
+DFS_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+// Tensor map of a row-major (BH, rows, inner) tensor of `dtype` elements as the
+// 3-D tensor {inner, rows, BH}, boxes of box_inner x box_rows x 1 elements with
+// 128-byte swizzle (box_inner x element size must be 128 bytes).  False when
+// the address is not 16-byte aligned or the driver refuses the map.
+bool make_tmap(CUtensorMap* tm, const void* ptr, int dtype, int inner, int rows, int BH, int box_inner, int box_rows);
+// True when cuTensorMapEncodeTiled could be obtained from the driver.
+bool tmap_available();
+
+}  // namespace dfs
