@@ -44,6 +44,7 @@ namespace dfs {
 constexpr int kTThreads = 320;  // warps 0-7 epilogue, 8 producer, 9 MMA
 constexpr int kTEpi = 256;      // epilogue threads
 constexpr int kTProducer = 8, kTMma = 9;
+constexpr float kLag = 16.0f;   // log2 headroom of the lagged exponent reference
 constexpr int kTCols = 128;     // columns per tile
 
 struct TileParams {
@@ -80,8 +81,8 @@ struct TileCfg {
   static constexpr uint32_t OFF_B = OFF_A + TILE;
   static constexpr uint32_t OFF_CB = OFF_B + NS * TILE;   // NS x 128 column bias
   static constexpr uint32_t OFF_CV = OFF_CB + NS * 512u;  // NS x 128 column vector
-  static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 2 x 128 partials of the second column half
-  static constexpr uint32_t OFF_BAR = OFF_MRG + 1024u;
+  static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 3 x 128 partials of the second column half
+  static constexpr uint32_t OFF_BAR = OFF_MRG + 1536u;
   static constexpr uint32_t NBAR = 2 * NS + 5;            // full, empty, sfull x2, sempty x2, afull
   static constexpr uint32_t OFF_SLOT = OFF_BAR + 8 * NBAR;
   static constexpr uint32_t OFF_RED = OFF_SLOT + 16;
@@ -237,7 +238,9 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
     const float fi = (MODE != TL_LSE && rin) ? p.row_bias[bh * N + row] : 0.0f;
     const uint32_t tlane = static_cast<uint32_t>(32 * quad) << 16;
-    float m = kNeg, sum = 0.0f;  // running max and sum of this half's columns (LSE, ROWSTATS)
+    // running reference, exact maximum and sum of exp2(x - reference) of this
+    // half's columns (LSE, ROWSTATS)
+    float m = kNeg, mt = kNeg, sum = 0.0f;
     float acc = 0.0f;            // MATVEC
 #pragma unroll 1
     for (int u = 0; u < ntiles; ++u) {
@@ -245,10 +248,15 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
       if (!mbar_wait(&full[s], (u / C::NS) & 1)) err = 1;  // the producer's bias stores
       if (!mbar_wait(&sfull[b], (u >> 1) & 1)) err = 1;
       tc_fence_after();
-#pragma unroll 1
-      for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
+      // the second chunk's TMEM load overlaps the first chunk's arithmetic
+      uint32_t r0v[32], r1v[32];
+      tmem_ld32_async(tbase + tlane + b * kTCols + 64 * half, r0v);
+      tmem_wait_ld(r0v);
+      tmem_ld32_async(tbase + tlane + b * kTCols + 64 * half + 32, r1v);
+      auto chunk = [&](uint32_t (&rv32)[32], int ch) {
         float v[32];
-        tmem_ld32(tbase + tlane + b * kTCols + 32 * ch, v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(rv32[k]);
         const float* cb = cbs + s * 128 + 32 * ch;
         if constexpr (MODE == TL_MATVEC) {
           const float* cv = cvs + s * 128 + 32 * ch;
@@ -259,19 +267,33 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         } else {
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] = fmaf(v[k], scale, cb[k]);
+          // exponents against the running reference m (a maximum of the earlier
+          // columns), so they need not wait for this chunk's maximum, which is
+          // reduced alongside; a chunk whose maximum exceeds m by more than kLag
+          // (the first one, and rarely any other) moves the reference and is
+          // summed again.  The sum then stays within [1, N 2^kLag].
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 0; k < 32; ++k) a[k & 3] += ex2(v[k] - m);
           float mx[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) mx[q] = fmaxf(fmaxf(v[4 * q], v[4 * q + 1]), fmaxf(v[4 * q + 2], v[4 * q + 3]));
           const float cm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                  fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-          const float mn = fmaxf(m, cm);
-          float a[4] = {sum * ex2(m - mn), 0.0f, 0.0f, 0.0f};
+          mt = fmaxf(mt, cm);
+          if (cm > m + kLag) {
+            a[0] = a[1] = a[2] = a[3] = 0.0f;
 #pragma unroll
-          for (int k = 0; k < 32; ++k) a[k & 3] += ex2(v[k] - mn);
-          m = mn;
-          sum = (a[0] + a[1]) + (a[2] + a[3]);
+            for (int k = 0; k < 32; ++k) a[k & 3] += ex2(v[k] - cm);
+            sum *= ex2(m - cm);
+            m = cm;
+          }
+          sum += (a[0] + a[1]) + (a[2] + a[3]);
         }
-      }
+      };
+      chunk(r0v, 2 * half);
+      tmem_wait_ld(r1v);
+      chunk(r1v, 2 * half + 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -284,6 +306,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     if (half == 1) {
       mrg[lrow] = MODE == TL_MATVEC ? acc : m;
       mrg[128 + lrow] = sum;
+      mrg[256 + lrow] = mt;
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
     if (half == 0 && rin) {
@@ -296,6 +319,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         const float mm = fmaxf(m, m2);
         sum = sum * ex2(m - mm) + s2 * ex2(m2 - mm);
         m = mm;
+        mt = fmaxf(mt, mrg[256 + lrow]);
         if constexpr (MODE == TL_LSE) {
           const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
           float f = 0.0f;
@@ -303,8 +327,9 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
           p.row_out[o] = f;
           if (p.row_out_nat) p.row_out_nat[o] = f * kLn2;
         } else {
-          p.row_out[o] = rok ? m + fi : 0.0f;
-          p.row_R[o] = rok ? sum : 0.0f;
+          // the row maximum itself and the sum relative to it
+          p.row_out[o] = rok ? mt + fi : 0.0f;
+          p.row_R[o] = rok ? sum * ex2(m - mt) : 0.0f;
         }
       }
     }
