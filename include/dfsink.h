@@ -172,10 +172,12 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
  * Forward: FWD_INIT; K_iter x { FWD_ROWS (gather slot F and log_u),
  *          FWD_COLS (gather slot G and log_v) }; FWD_OUT (O, x_centroid rows).
  * Backward: BWD_PREP; BWD_ROWSTATS (gather M, R, D); BWD_ROWDERIVE;
- *          BWD_COLSTATS (gather C, GV); BWD_SETUP; BWD_PT_T (gather S);
+ *          BWD_COLSTATS (gather C, GV; writes the dV rows where the TMA-staged
+ *          passes run: d = 32 or 64, N >= 128, N % 4 == 0); BWD_SETUP; BWD_PT_T (gather S);
  *          BWD_CGINIT; (max_iter + 1) x { BWD_P_U (gather T); BWD_PT_T (gather S);
  *          BWD_CGSTEP_FIRST the first time, BWD_CGSTEP after };
- *          BWD_P_X (gather S); BWD_FINAL; BWD_DQ (dQ rows); BWD_DKV (dK, dV rows).
+ *          BWD_P_X (gather S); BWD_FINAL; BWD_DQ (dQ rows); BWD_DKV (dK rows, and
+ *          dV rows where BWD_COLSTATS did not write them).
  * --------------------------------------------------------------------------- */
 enum {
   DFS_OP_FWD_INIT = 0, DFS_OP_FWD_ROWS = 1, DFS_OP_FWD_COLS = 2, DFS_OP_FWD_OUT = 3,
@@ -203,9 +205,10 @@ int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const d
                   const dfs_bwd_args* ba, int row_begin, int row_end, void* workspace,
                   size_t workspace_bytes, void* stream);
 
-/* Size of the library's fixed device scratch used by dfs_fwd_static: 16 MiB,
- * i.e. streamed problems with B*H*N up to 1,048,576 (the forward needs
- * 16 bytes of workspace per (batch, head, point)). */
+/* Size of the library's fixed device scratch used by dfs_fwd_static: 16 MiB.
+ * The streamed forward needs 16 + 12 d bytes of workspace per (batch, head,
+ * point) plus 256 (dfs_workspace_size), e.g. B*H*N up to ~20,000 points at
+ * d = 64. */
 #define DFS_STATIC_SCRATCH_BYTES (16u << 20)
 
 /* Forward for callers that cannot allocate device memory.  No counterpart in
