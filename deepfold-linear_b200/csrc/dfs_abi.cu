@@ -190,6 +190,58 @@ int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const d
   return DFS_ERR_INVALID_ARGUMENT;
 }
 
+int dfs_peer_alloc(size_t bytes, void** ptr, dfs_ipc_handle* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0) return DFS_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return DFS_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return DFS_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == sizeof(handle->bytes), "IPC handle size");
+  memcpy(handle->bytes, &h, sizeof(h));
+  *ptr = p;
+  return DFS_OK;
+}
+
+int dfs_peer_open(const dfs_ipc_handle* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return DFS_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->bytes, sizeof(h));
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? DFS_OK : DFS_ERR_CUDA;
+}
+
+int dfs_peer_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? DFS_OK : DFS_ERR_CUDA; }
+
+int dfs_peer_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? DFS_OK : DFS_ERR_CUDA; }
+
+int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int row_begin, int row_end,
+                       void* workspace, size_t workspace_bytes, const dfs_peer_set* peers, void* stream) {
+  if (!dims_ok(p) || !streamed(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  if (op < DFS_OP_FWD_INIT || op > DFS_OP_FWD_OUT || peers == nullptr) return DFS_ERR_INVALID_ARGUMENT;
+  if (row_begin < 0 || row_end < row_begin || row_end > p->N) return DFS_ERR_INVALID_ARGUMENT;
+  if (peers->npeers < 1 || peers->npeers > DFS_MAX_PEERS || peers->self < 0 || peers->self >= peers->npeers)
+    return DFS_ERR_INVALID_ARGUMENT;
+  if (peers->ws[peers->self] != workspace) return DFS_ERR_INVALID_ARGUMENT;
+  for (int k = 0; k < peers->npeers; ++k)
+    if (peers->ws[k] == nullptr || (reinterpret_cast<uintptr_t>(peers->ws[k]) & 255u) != 0)
+      return DFS_ERR_INVALID_ARGUMENT;
+  int rc;
+  if ((rc = check_fwd_args(p, fa)) != DFS_OK) return rc;
+  if ((rc = check_stream_fwd(p, fa, workspace, workspace_bytes)) != DFS_OK) return rc;
+  if (!tile_path_ok(p->in_dtype, p->d, p->N, fa->Q, fa->K)) return DFS_ERR_UNSUPPORTED;
+  PeerInfo pi{};
+  pi.npeers = peers->npeers;
+  pi.self = peers->self;
+  for (int k = 0; k < peers->npeers; ++k) pi.ws[k] = peers->ws[k];
+  pi.wait_for = peers->wait_for;
+  return cuda_status(stream_fwd_op(op, fwd_params(p, fa), static_cast<float*>(workspace), row_begin, row_end,
+                                   static_cast<cudaStream_t>(stream), &pi));
+}
+
 int dfs_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K, void* stream) {
   if (!A || !B || !D || which < 0 || which > 2) return DFS_ERR_INVALID_ARGUMENT;
   if (M != 64 || K <= 0 || K % 8 || N <= 0 || N > 384 || N % 32) return DFS_ERR_INVALID_ARGUMENT;

@@ -83,7 +83,15 @@ struct BwdParams {
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
 size_t resident_fwd_smem(int N, int d);
 cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
-cudaError_t stream_fwd_op(int op, const FwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
+// Peer exchange of a row-sharded forward: every GPU's workspace (same layout,
+// 256-byte aligned bases) and the cumulative arrival count the phase waits for.
+struct PeerInfo {
+  int npeers, self;
+  void* ws[DFS_MAX_PEERS];
+  unsigned long long wait_for;
+};
+cudaError_t stream_fwd_op(int op, const FwdParams& p, float* ws, int r0, int r1, cudaStream_t st,
+                          const PeerInfo* peers = nullptr);
 cudaError_t stream_bwd_op(int op, const BwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
 size_t stream_fwd_workspace(int B, int H, int N, int d);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
@@ -110,9 +118,22 @@ struct TileArgs {
   float* row_out_nat;
   float* row_R;
   int32_t* status;
+  float* split;            // tile_split_bytes() of scratch for column splits (counters zeroed
+                           // by tile_split_reset), or null: one CTA per row block
+  // peer exchange (LSE only): row_out's slot in every GPU's workspace, their arrival
+  // counters, and this GPU's counter to wait on before reading (npeers = 0: none)
+  int npeers;
+  float* peer_out[DFS_MAX_PEERS];
+  unsigned long long* peer_cnt[DFS_MAX_PEERS];
+  const unsigned long long* wait_cnt;
+  unsigned long long wait_for;
   int B, H, N, row_begin, row_end;
   float lam;
 };
+size_t tile_split_bytes(int B, int H, int N);
+// Raises each of the n counters once (system-scope release), one thread.
+cudaError_t peer_signal(unsigned long long* const* cnt, int n, cudaStream_t st);
+cudaError_t tile_split_reset(float* split, int B, int H, int N, cudaStream_t st);
 // True when the TMA-staged kernels cover this operand type, head dim, length
 // (N >= 128) and the two operand addresses (16-byte aligned); otherwise the
 // register-staged kernels run the pass.

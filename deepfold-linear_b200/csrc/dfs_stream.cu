@@ -333,10 +333,18 @@ cudaError_t launch_stream(int mode, int d, const StreamParams& p, cudaStream_t s
 
 // f, g (log2), m, R; then fp32 copies Q, K (row-major) and V^T (transposed)
 // for the TMA-staged transport-output pass
+// ... then the column-split scratch and a 64-byte slot whose first 8 bytes are
+// the peer-exchange arrival counter
 size_t stream_fwd_workspace(int B, int H, int N, int d) {
   const size_t n = static_cast<size_t>(B) * H * N;
-  return 4 * sizeof(float) * n + 3 * sizeof(float) * n * d + 256;
+  return 4 * sizeof(float) * n + 256 + 3 * sizeof(float) * n * d + 256 + tile_split_bytes(B, H, N) + 128;
 }
+
+namespace {
+float* align256(float* p) {
+  return reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
+}
+}  // namespace
 
 // One phase of the streamed forward on rows [r0, r1) (the whole problem for a
 // single GPU; a row range per GPU when the rows are sharded, with the
@@ -346,17 +354,32 @@ size_t stream_fwd_workspace(int B, int H, int N, int d) {
 //   FWD_ROWS  f = kappa (a - LSE_j(S' + g)) for rows [r0, r1); also log_u there
 //   FWD_COLS  g = kappa (b - LSE_i(S' + f)) for columns [r0, r1); also log_v there
 //   FWD_OUT   row statistics, O and x_centroid for rows [r0, r1)
-cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1, cudaStream_t st) {
+cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1, cudaStream_t st,
+                          const PeerInfo* peers) {
   const size_t n = static_cast<size_t>(fp.B) * fp.H * fp.N;
   float* fw = ws;
   float* gw = ws + n;
   float* mw = ws + 2 * n;
   float* Rw = ws + 3 * n;
+  float* copies = align256(ws + 4 * n);                            // Q, K, V^T fp32
+  float* split = align256(copies + 3 * n * static_cast<size_t>(fp.d));  // column-split scratch
+  unsigned long long* counter = reinterpret_cast<unsigned long long*>(
+      (reinterpret_cast<uintptr_t>(split) + tile_split_bytes(fp.B, fp.H, fp.N) + 63) & ~uintptr_t(63));
+  // the same byte offset in another GPU's workspace
+  auto at_peer = [&](int k, const void* own) {
+    return static_cast<char*>(peers->ws[k]) + (static_cast<const char*>(own) - reinterpret_cast<char*>(ws));
+  };
+  unsigned long long* cnts[DFS_MAX_PEERS] = {};
+  if (peers != nullptr)
+    for (int k = 0; k < peers->npeers; ++k) cnts[k] = reinterpret_cast<unsigned long long*>(at_peer(k, counter));
   if (op == DFS_OP_FWD_INIT) {
     const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
     stream_init_kernel<<<blocks, 256, 0, st>>>(fw, fp.log_u, fp.log_u_init, n);
     stream_init_kernel<<<blocks, 256, 0, st>>>(gw, fp.log_v, fp.log_v_init, n);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = tile_split_reset(split, fp.B, fp.H, fp.N, st);
+    if (e == cudaSuccess && peers != nullptr) e = peer_signal(cnts, peers->npeers, st);
+    return e;
   }
   StreamParams p{};
   p.dtype = fp.in_dtype;
@@ -382,6 +405,12 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
   ta.row_begin = r0;
   ta.row_end = r1;
   ta.lam = fp.lam;
+  ta.split = split;
+  if (peers != nullptr) {
+    if (!tma) return cudaErrorNotSupported;
+    ta.wait_cnt = counter;
+    ta.wait_for = peers->wait_for;
+  }
   if (tma && (op == DFS_OP_FWD_ROWS || op == DFS_OP_FWD_COLS)) {
     const bool rows = op == DFS_OP_FWD_ROWS;  // the column half-update is the row pass on S^T
     ta.A = rows ? fp.Q : fp.K;
@@ -390,6 +419,13 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     ta.row_marg = rows ? fp.log_mu : fp.log_nu;
     ta.row_out = rows ? fw : gw;
     ta.row_out_nat = rows ? fp.log_u : fp.log_v;
+    if (peers != nullptr) {
+      ta.npeers = peers->npeers;
+      for (int k = 0; k < peers->npeers; ++k) {
+        ta.peer_out[k] = reinterpret_cast<float*>(at_peer(k, ta.row_out));
+        ta.peer_cnt[k] = cnts[k];
+      }
+    }
     return launch_tile_pass(TL_LSE, ta, st);
   }
   if (op == DFS_OP_FWD_ROWS) {
@@ -430,7 +466,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
       if (e != cudaSuccess) return e;
       if (bt_path_ok(fp.d, fp.N, ws)) {
         // O = T_norm V by the TMA-staged tile pass on fp32 copies of Q, K and V^T
-        float* cp = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ws + 4 * n) + 255) & ~uintptr_t(255));
+        float* cp = copies;
         const size_t nd = n * fp.d;
         float* Qf = cp;
         float* Kf = cp + nd;

@@ -45,6 +45,7 @@ constexpr int kTThreads = 320;  // warps 0-7 epilogue, 8 producer, 9 MMA
 constexpr int kTEpi = 256;      // epilogue threads
 constexpr int kTProducer = 8, kTMma = 9;
 constexpr float kLag = 16.0f;   // log2 headroom of the lagged exponent reference
+constexpr int kMaxSplit = 4;    // column splits of a row block (small grids)
 constexpr int kTCols = 128;     // columns per tile
 
 struct TileParams {
@@ -62,8 +63,18 @@ struct TileParams {
   float* row_out_nat;      // LSE: the potential in natural-log units, or null
   float* row_R;            // ROWSTATS: R
   int32_t* status;         // DFS_ERR_DEVICE_TIMEOUT is OR-ed in if a wait gives up, or null
+  // peer exchange (LSE): every GPU's copy of row_out, their arrival counters,
+  // and this GPU's counter with the count to wait for before reading
+  int npeers;
+  float* peer_out[DFS_MAX_PEERS];
+  unsigned long long* peer_cnt[DFS_MAX_PEERS];
+  const unsigned long long* wait_cnt;
+  unsigned long long wait_for;
+  float* part;             // nsplit > 1: (nsplit, 3, BH, N) partial results of the column splits
+  unsigned* counter;       // nsplit > 1: (BH * row blocks) arrival counters, zero between launches
   int B, H, N;
   int row_begin, row_end;  // rows this launch handles
+  int nsplit;              // CTAs per row block, each over a contiguous share of the column tiles
   float lam;
 };
 
@@ -81,8 +92,8 @@ struct TileCfg {
   static constexpr uint32_t OFF_B = OFF_A + TILE;
   static constexpr uint32_t OFF_CB = OFF_B + NS * TILE;   // NS x 128 column bias
   static constexpr uint32_t OFF_CV = OFF_CB + NS * 512u;  // NS x 128 column vector
-  static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 3 x 128 partials of the second column half
-  static constexpr uint32_t OFF_BAR = OFF_MRG + 1536u;
+  static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 3 x 128 partials of the second half, a flag
+  static constexpr uint32_t OFF_BAR = OFF_MRG + 1536u + 16u;
   static constexpr uint32_t NBAR = 2 * NS + 5;            // full, empty, sfull x2, sempty x2, afull
   static constexpr uint32_t OFF_SLOT = OFF_BAR + 8 * NBAR;
   static constexpr uint32_t OFF_RED = OFF_SLOT + 16;
@@ -133,7 +144,8 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nrb = (p.row_end - p.row_begin + 127) / 128;
-  const int prob = blockIdx.x / nrb, rb = blockIdx.x % nrb;
+  const int blk = blockIdx.x / p.nsplit, sp = blockIdx.x % p.nsplit;
+  const int prob = blk / nrb, rb = blk % nrb;
   if (MODE == TL_MATVEC && p.done != nullptr && p.done[prob] != 0) return;  // uniform over the CTA
   const int bb = prob / p.H, hh = prob % p.H;
   const int N = p.N;
@@ -145,8 +157,11 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
   valid_extent<kTThreads>(p.mask, bb, N, reinterpret_cast<int*>(base + C::OFF_RED), vlo, vhi);
   const int rhi = min(min(r0 + 128, p.row_end), N);
   const bool live = max(r0, vlo) < min(rhi, vhi);
-  const int t_begin = live ? vlo / kTCols : 0;
-  const int ntiles = live ? (vhi + kTCols - 1) / kTCols - t_begin : 0;
+  // this CTA's contiguous share of the row block's column tiles
+  const int t_all = live ? (vhi + kTCols - 1) / kTCols - vlo / kTCols : 0;
+  const int t_q = t_all / p.nsplit, t_r = t_all % p.nsplit;
+  const int t_begin = (live ? vlo / kTCols : 0) + sp * t_q + min(sp, t_r);
+  const int ntiles = t_q + (sp < t_r ? 1 : 0);
 
   if (warp == 0) tmem_alloc(tslot, 256);
   if (tid == 32 * kTProducer) {
@@ -161,12 +176,23 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     mbar_init(afull, 1);
     fence_mbar_init();
   }
+  int err = 0;
+  if (p.wait_cnt != nullptr && tid == 0) {
+    // peer exchange: the potentials this phase reads are complete on this GPU
+    // once every GPU's previous phase has raised the counter (bounded wait)
+    uint64_t t0 = 0;
+    for (uint32_t it = 0; ld_acquire_sys_u64(p.wait_cnt) < p.wait_for; ++it) {
+      if (it == 0) t0 = global_ns();
+      else if ((it & 63u) == 0 && global_ns() - t0 > kWaitNs) { err = 1; break; }
+      __nanosleep(64);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
-  int err = 0;
 
+  bool final_cta_of_block = true;  // this CTA writes the block's results (column splits: the last one)
   if (warp == kTProducer) {
     // ------------------------------------------------------------ producer
     if (ntiles > 0) {
@@ -184,7 +210,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
           const int j = c0 + lane + 32 * q;
           const bool cin = j < N;
           const bool cok = cin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + j] != 0.0f);
-          pc[q] = cok ? p.col_bias[bh * N + j] : -INFINITY;
+          pc[q] = cok ? __ldcg(p.col_bias + bh * N + j) : -INFINITY;  // L2: peers may have written it
           if constexpr (MODE == TL_MATVEC) pw[q] = cin ? p.col_vec[bh * N + j] : 0.0f;
         }
       };
@@ -236,7 +262,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
     const float eps_h = p.eps[hh];
     const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
-    const float fi = (MODE != TL_LSE && rin) ? p.row_bias[bh * N + row] : 0.0f;
+    const float fi = (MODE != TL_LSE && rin) ? __ldcg(p.row_bias + bh * N + row) : 0.0f;
     const uint32_t tlane = static_cast<uint32_t>(32 * quad) << 16;
     // running reference, exact maximum and sum of exp2(x - reference) of this
     // half's columns (LSE, ROWSTATS)
@@ -309,22 +335,77 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
       mrg[256 + lrow] = mt;
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
-    if (half == 0 && rin) {
-      const size_t o = bh * N + row;
+    bool final_cta = true;
+    if (half == 0) {
       if constexpr (MODE == TL_MATVEC) {
         acc += mrg[lrow];
-        p.row_out[o] = rok ? acc * (p.row_scale != nullptr ? p.row_scale[o] : 1.0f) : 0.0f;
       } else {
         const float m2 = mrg[lrow], s2 = mrg[128 + lrow];
         const float mm = fmaxf(m, m2);
         sum = sum * ex2(m - mm) + s2 * ex2(m2 - mm);
         m = mm;
         mt = fmaxf(mt, mrg[256 + lrow]);
+      }
+    }
+    if (p.nsplit > 1) {
+      // column-split row block: publish this CTA's partials; the last CTA of the
+      // block to arrive merges all of them and re-arms the counter
+      const size_t pn = static_cast<size_t>(p.B) * p.H * N;
+      const size_t o = bh * N + row;
+      if (half == 0 && rin) {
+        p.part[(static_cast<size_t>(sp) * 3 + 0) * pn + o] = MODE == TL_MATVEC ? acc : m;
+        p.part[(static_cast<size_t>(sp) * 3 + 1) * pn + o] = sum;
+        p.part[(static_cast<size_t>(sp) * 3 + 2) * pn + o] = mt;
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
+      volatile int* flag = reinterpret_cast<volatile int*>(mrg + 384);
+      if (tid == 0) {
+        const unsigned prev = atomicAdd(&p.counter[blk], 1u);
+        const int last = prev == static_cast<unsigned>(p.nsplit - 1);
+        if (last) p.counter[blk] = 0u;  // every CTA of this block has arrived
+        *flag = last;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
+      final_cta = *flag != 0;
+      final_cta_of_block = final_cta;
+      if (final_cta) {
+        __threadfence();
+        if (half == 0 && rin) {
+          m = kNeg;
+          sum = 0.0f;
+          mt = kNeg;
+          acc = 0.0f;
+          for (int q = 0; q < p.nsplit; ++q) {
+            const float a0 = __ldcg(p.part + (static_cast<size_t>(q) * 3 + 0) * pn + o);
+            const float a1 = __ldcg(p.part + (static_cast<size_t>(q) * 3 + 1) * pn + o);
+            const float a2 = __ldcg(p.part + (static_cast<size_t>(q) * 3 + 2) * pn + o);
+            if constexpr (MODE == TL_MATVEC) {
+              acc += a0;
+            } else {
+              const float mm = fmaxf(m, a0);
+              sum = sum * ex2(m - mm) + a1 * ex2(a0 - mm);
+              m = mm;
+              mt = fmaxf(mt, a2);
+            }
+          }
+        }
+      }
+    }
+    if (final_cta && half == 0 && rin) {
+      const size_t o = bh * N + row;
+      if constexpr (MODE == TL_MATVEC) {
+        p.row_out[o] = rok ? acc * (p.row_scale != nullptr ? p.row_scale[o] : 1.0f) : 0.0f;
+      } else {
         if constexpr (MODE == TL_LSE) {
           const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
           float f = 0.0f;
           if (rok && sum > 0.0f) f = kap * (p.row_marg[o] * kLog2e - (m + lg2(sum)));
-          p.row_out[o] = f;
+          if (p.npeers > 0) {
+            for (int k = 0; k < p.npeers; ++k) p.peer_out[k][o] = f;  // NVLink stores, own copy included
+          } else {
+            p.row_out[o] = f;
+          }
           if (p.row_out_nat) p.row_out_nat[o] = f * kLn2;
         } else {
           // the row maximum itself and the sum relative to it
@@ -333,6 +414,13 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         }
       }
     }
+  }
+  if (MODE == TL_LSE && p.npeers > 0 && warp < kTEpi / 32) {
+    // every GPU's copy of this block's rows is written: raise every counter once
+    __threadfence_system();
+    asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
+    if (tid == 0 && final_cta_of_block)
+      for (int k = 0; k < p.npeers; ++k) atomicAdd_system(p.peer_cnt[k], 1ull);
   }
   if (err && p.status != nullptr) atomicOr(p.status, DFS_ERR_DEVICE_TIMEOUT);
   tc_fence_before();
@@ -392,7 +480,7 @@ cudaError_t launch_tile_mdd(const TileParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nrb = (p.row_end - p.row_begin + 127) / 128;
-  kern<<<p.B * p.H * nrb, kTThreads, C::SMEM, st>>>(p);
+  kern<<<p.B * p.H * nrb * p.nsplit, kTThreads, C::SMEM, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -407,6 +495,37 @@ cudaError_t launch_tile_m(int dtype, int d, const TileParams& p, cudaStream_t st
 }
 
 }  // namespace
+
+// Raises up to DFS_MAX_PEERS counters once each (pointers by value: no device
+// array to stage).
+__global__ void peer_signal_one(unsigned long long* c0, unsigned long long* c1, unsigned long long* c2,
+                                unsigned long long* c3, unsigned long long* c4, unsigned long long* c5,
+                                unsigned long long* c6, unsigned long long* c7, int n) {
+  unsigned long long* c[8] = {c0, c1, c2, c3, c4, c5, c6, c7};
+  __threadfence_system();
+  for (int k = 0; k < n && k < 8; ++k) atomicAdd_system(c[k], 1ull);
+}
+
+cudaError_t peer_signal(unsigned long long* const* cnt, int n, cudaStream_t st) {
+  struct Ptrs {
+    unsigned long long* c[DFS_MAX_PEERS];
+  } ptrs{};
+  for (int k = 0; k < n && k < DFS_MAX_PEERS; ++k) ptrs.c[k] = cnt[k];
+  peer_signal_one<<<1, 1, 0, st>>>(ptrs.c[0], ptrs.c[1], ptrs.c[2], ptrs.c[3], ptrs.c[4], ptrs.c[5], ptrs.c[6],
+                                   ptrs.c[7], n);
+  return cudaGetLastError();
+}
+
+size_t tile_split_bytes(int B, int H, int N) {
+  const size_t n = static_cast<size_t>(B) * H * N;
+  return sizeof(float) * kMaxSplit * 3 * n + sizeof(unsigned) * static_cast<size_t>(B) * H * ((N + 127) / 128);
+}
+
+cudaError_t tile_split_reset(float* split, int B, int H, int N, cudaStream_t st) {
+  const size_t n = static_cast<size_t>(B) * H * N;
+  return cudaMemsetAsync(split + static_cast<size_t>(kMaxSplit) * 3 * n, 0,
+                         sizeof(unsigned) * static_cast<size_t>(B) * H * ((N + 127) / 128), st);
+}
 
 bool tile_path_ok(int dtype, int d, int N, const void* a, const void* b) {
   const bool shape = (d == 64 || (d == 32 && dtype == DFS_F32)) && N >= 128;  // boxes of 128 rows
@@ -439,6 +558,28 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
   p.row_begin = t.row_begin;
   p.row_end = t.row_end;
   p.lam = t.lam;
+  p.npeers = t.npeers;
+  for (int k = 0; k < DFS_MAX_PEERS; ++k) {
+    p.peer_out[k] = t.peer_out[k];
+    p.peer_cnt[k] = t.peer_cnt[k];
+  }
+  p.wait_cnt = t.wait_cnt;
+  p.wait_for = t.wait_for;
+  // Column splits when the row blocks alone cannot fill the GPU: as many as fit
+  // in one wave of two CTAs per SM, at most kMaxSplit, never more than the tiles.
+  p.nsplit = 1;
+  if (t.split != nullptr) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long blocks = static_cast<long>(t.B) * t.H * ((t.row_end - t.row_begin + 127) / 128);
+    const int fit = static_cast<int>((2L * sms) / (blocks > 0 ? blocks : 1));
+    const int tiles = (t.N + kTCols - 1) / kTCols;
+    p.nsplit = max(1, min(min(fit, kMaxSplit), tiles));
+    if (p.nsplit > 1) {
+      p.part = t.split;
+      p.counter = reinterpret_cast<unsigned*>(t.split + static_cast<size_t>(kMaxSplit) * 3 * t.B * t.H * t.N);
+    }
+  }
   if (mode == TL_LSE) return launch_tile_m<TL_LSE>(t.dtype, t.d, p, st);
   if (mode == TL_ROWSTATS) return launch_tile_m<TL_ROWSTATS>(t.dtype, t.d, p, st);
   return launch_tile_m<TL_MATVEC>(t.dtype, t.d, p, st);

@@ -71,8 +71,21 @@ class DfsBwdArgs(ctypes.Structure):
         "dpos_weight", "dw_dist", "cg_iters", "cg_residual", "status")]
 
 
+class DfsIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+DFS_MAX_PEERS = 8
+
+
+class DfsPeerSet(ctypes.Structure):
+    _fields_ = [("npeers", ctypes.c_int32), ("self", ctypes.c_int32),
+                ("ws", ctypes.c_void_p * DFS_MAX_PEERS), ("wait_for", ctypes.c_uint64)]
+
+
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
-                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op")
+                    "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op",
+                    "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer")
 
 # phases of the streamed path for row-sharded runs (include/dfsink.h)
 DFS_OP_FWD_INIT, DFS_OP_FWD_ROWS, DFS_OP_FWD_COLS, DFS_OP_FWD_OUT = 0, 1, 2, 3
@@ -198,6 +211,19 @@ def lib() -> ctypes.CDLL:
                                         ctypes.c_int, _P, ctypes.c_size_t, _P]
             L.dfs_fwd_static.restype = ctypes.c_int
             L.dfs_fwd_static.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs), _P]
+            L.dfs_peer_alloc.restype = ctypes.c_int
+            L.dfs_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p),
+                                         ctypes.POINTER(DfsIpcHandle)]
+            L.dfs_peer_open.restype = ctypes.c_int
+            L.dfs_peer_open.argtypes = [ctypes.POINTER(DfsIpcHandle), ctypes.POINTER(ctypes.c_void_p)]
+            L.dfs_peer_close.restype = ctypes.c_int
+            L.dfs_peer_close.argtypes = [_P]
+            L.dfs_peer_free.restype = ctypes.c_int
+            L.dfs_peer_free.argtypes = [_P]
+            L.dfs_stream_op_peer.restype = ctypes.c_int
+            L.dfs_stream_op_peer.argtypes = [ctypes.c_int, ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs),
+                                             ctypes.c_int, ctypes.c_int, _P, ctypes.c_size_t,
+                                             ctypes.POINTER(DfsPeerSet), _P]
             L.dfs_selftest_mma.restype = ctypes.c_int
             L.dfs_selftest_mma.argtypes = [ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, _P]

@@ -17,21 +17,33 @@ vectors a phase produced are all-gathered before the next one:
   solve together without a further collective.
 
 Outputs (O, potentials, gradients) are all-gathered too, so every rank ends
-with the same full tensors a single GPU would produce.  Where the reference
+with the same full tensors a single GPU would produce.
+
+On NCCL groups whose shapes the TMA-staged kernels cover, the forward's
+half-updates exchange their potentials without any collective: each rank's
+forward workspace is a device buffer shared with the other ranks through CUDA
+IPC (``_PeerWorkspace``), and the half-update kernel stores its rows of the new
+potential straight into every rank's copy over NVLink and raises every rank's
+arrival counter; the next half-update waits on its own counter
+(``dfs_stream_op_peer``).  ``DFS_ROWSHARD_EXCHANGE=collective`` selects the
+all-gather exchange instead.  Where the reference
 runs on one device only (src/deepfold/model/kernels/sinkhorn_kernel.py), this
 module has no counterpart there.
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
+import os
 
 import torch
 import torch.distributed as dist
 
 from deepfold import _native as nat
 
-__all__ = ["row_range", "RowGather", "row_sharded_flash_sinkhorn", "last_rowshard_report"]
+__all__ = ["row_range", "RowGather", "arrivals_per_half_update", "row_sharded_flash_sinkhorn",
+           "last_rowshard_report"]
 
 
 def row_range(N: int, world: int, rank: int) -> tuple[int, int, int]:
@@ -71,6 +83,62 @@ class RowGather:
         return x
 
 
+def arrivals_per_half_update(P: int, N: int, world: int) -> int:
+    """Counter arrivals one peer-exchange half-update raises on every rank: each
+    rank's kernel signals once per block of 128 rows of each of the P problems
+    in its row range (the column-split CTAs of a block signal once, through the
+    block's last CTA)."""
+    total = 0
+    for r in range(world):
+        r0, r1, _ = row_range(N, world, r)
+        total += P * (-(-(r1 - r0) // 128))
+    return total
+
+
+class _PeerWorkspace:
+    """This rank's forward workspace, shared with every rank of the group through
+    CUDA IPC (allocated zero-filled by the library, handles all-gathered over
+    the group), and the cumulative count of arrivals its counter has been told
+    to expect -- identical on every rank, since all ranks run the same phases."""
+
+    def __init__(self, nbytes: int, group, device: torch.device):
+        L = nat.lib()
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        p, h = ctypes.c_void_p(), nat.DfsIpcHandle()
+        nat.check(L.dfs_peer_alloc(nbytes, ctypes.byref(p), ctypes.byref(h)), "dfs_peer_alloc")
+        self.ptr = p.value
+        mine = torch.tensor(list(bytes(h.bytes)), dtype=torch.uint8, device=device)
+        every = torch.empty(self.world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().tolist()
+        self.ws = []
+        for r in range(self.world):
+            if r == self.rank:
+                self.ws.append(self.ptr)
+                continue
+            hr = nat.DfsIpcHandle()
+            for i, v in enumerate(every[64 * r:64 * (r + 1)]):
+                hr.bytes[i] = v
+            q = ctypes.c_void_p()
+            nat.check(L.dfs_peer_open(ctypes.byref(hr), ctypes.byref(q)), "dfs_peer_open")
+            self.ws.append(q.value)
+        self.arrived = 0
+        self.peers = nat.DfsPeerSet(npeers=self.world, self=self.rank)
+        for k, w in enumerate(self.ws):
+            self.peers.ws[k] = w
+
+
+_peer_ws: dict = {}
+
+
+def _peer_workspace(nbytes: int, group, device: torch.device) -> _PeerWorkspace:
+    key = (nbytes, device.index, id(group))
+    if key not in _peer_ws:
+        with torch.cuda.device(device):  # the buffer and the peer mappings belong to this GPU
+            _peer_ws[key] = _PeerWorkspace(nbytes, group, device)
+    return _peer_ws[key]
+
+
 def _slot(ws: torch.Tensor, k: int, P: int, N: int) -> torch.Tensor:
     return ws[k * P * N:(k + 1) * P * N].view(P, N)
 
@@ -107,22 +175,25 @@ class _Sharded:
         self.xc = torch.empty(B, H, N, 3, **fo) if self.xr is not None else None
         self.lu, self.lv = torch.empty(B, H, N, **fo), torch.empty(B, H, N, **fo)
         self.fstatus = torch.zeros(1, device=dev, dtype=torch.int32)
-        ws = torch.empty(max(self.fwd_bytes // 4, 1), **fo)
         fa = nat.DfsFwdArgs(Q=nat.ptr(self.Q), K=nat.ptr(self.K), V=nat.ptr(self.V), x_res=nat.ptr(self.xr),
                             eps=nat.ptr(self.eps), log_mu=nat.ptr(self.lmu), log_nu=nat.ptr(self.lnu),
                             log_u_init=nat.ptr(self.lui), log_v_init=nat.ptr(self.lvi), mask=nat.ptr(self.mask),
                             O=nat.ptr(self.O), x_centroid=nat.ptr(self.xc), log_u=nat.ptr(self.lu),
                             log_v=nat.ptr(self.lv), status=nat.ptr(self.fstatus))
         g, r0, r1 = self.gather, self.gather.r0, self.gather.r1
-        run = lambda op, a, b: self._op(op, a, b, fa=fa, ws=ws, nbytes=self.fwd_bytes)  # noqa: E731
-        run(nat.DFS_OP_FWD_INIT, 0, N)
-        f, gg = _slot(ws, nat.DFS_WS_FWD_F, P, N), _slot(ws, nat.DFS_WS_FWD_G, P, N)
-        for _ in range(self.K_iter):
-            run(nat.DFS_OP_FWD_ROWS, r0, r1)
-            g(f)
-            run(nat.DFS_OP_FWD_COLS, r0, r1)
-            g(gg)
-        run(nat.DFS_OP_FWD_OUT, r0, r1)
+        if self._peer_exchange():
+            self._forward_peer(fa, r0, r1)
+        else:
+            ws = torch.empty(max(self.fwd_bytes // 4, 1), **fo)
+            run = lambda op, a, b: self._op(op, a, b, fa=fa, ws=ws, nbytes=self.fwd_bytes)  # noqa: E731
+            run(nat.DFS_OP_FWD_INIT, 0, N)
+            f, gg = _slot(ws, nat.DFS_WS_FWD_F, P, N), _slot(ws, nat.DFS_WS_FWD_G, P, N)
+            for _ in range(self.K_iter):
+                run(nat.DFS_OP_FWD_ROWS, r0, r1)
+                g(f)
+                run(nat.DFS_OP_FWD_COLS, r0, r1)
+                g(gg)
+            run(nat.DFS_OP_FWD_OUT, r0, r1)
         if self.K_iter > 0:
             g(self.lu.view(P, N))
             g(self.lv.view(P, N))
@@ -130,6 +201,36 @@ class _Sharded:
         if self.xc is not None:
             g(self.xc.view(P, N, 3))
         return self.O, self.xc, self.lu, self.lv
+
+    def _peer_exchange(self) -> bool:
+        """Half-updates exchange their potentials through peer memory (NCCL group of
+        several GPUs, shapes on the TMA-staged kernels) unless disabled."""
+        g = self.gather
+        if g.world < 2 or not g.nccl or os.environ.get("DFS_ROWSHARD_EXCHANGE", "peer") != "peer":
+            return False
+        tma = (self.d == 64 or (self.d == 32 and self.Q.dtype == torch.float32)) and self.N >= 128
+        return tma and g.world <= nat.DFS_MAX_PEERS
+
+    def _forward_peer(self, fa, r0, r1):
+        """The forward's phase loop with the peer exchange (every rank in lockstep)."""
+        pw = _peer_workspace(self.fwd_bytes, self.group, self.Q.device)
+        L = nat.lib()
+        world = self.gather.world
+        blocks = arrivals_per_half_update(self.P, self.N, world)
+
+        def run(op, a, b, wait):
+            pw.peers.wait_for = wait
+            nat.check(L.dfs_stream_op_peer(op, self.prob, fa, a, b, pw.ptr, self.fwd_bytes, pw.peers,
+                                           self.stream), f"dfs_stream_op_peer({op})")
+
+        run(nat.DFS_OP_FWD_INIT, 0, self.N, 0)
+        pw.arrived += world  # every rank's init raised every counter once
+        for _ in range(self.K_iter):
+            run(nat.DFS_OP_FWD_ROWS, r0, r1, pw.arrived)
+            pw.arrived += blocks
+            run(nat.DFS_OP_FWD_COLS, r0, r1, pw.arrived)
+            pw.arrived += blocks
+        run(nat.DFS_OP_FWD_OUT, r0, r1, pw.arrived)
 
     def backward(self, dO, dxc, need_marg: bool):
         dev = self.Q.device

@@ -228,6 +228,47 @@ int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const d
  *     be serialised by the caller.  Nothing in it needs to start at zero. */
 int dfs_fwd_static(const dfs_problem* p, const dfs_fwd_args* a, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Peer exchange for row-sharded forwards (one process per GPU, GPUs linked by
+ * NVLink / NVSwitch).  Instead of gathering the potential slices with a
+ * collective after every half-iteration, the half-update kernel of each GPU
+ * stores its new potentials straight into the forward workspace of every GPU
+ * of the run and raises an arrival counter there; the next phase waits on its
+ * own counter before it reads.  The workspaces are device buffers shared
+ * between the processes through CUDA IPC: each process allocates its own with
+ * dfs_peer_alloc (zero-filled), the processes exchange the 64-byte handles
+ * (an all-gather), and each maps the others' with dfs_peer_open.  New for
+ * multi-GPU row sharding; the reference has no sharded path.
+ * --------------------------------------------------------------------------- */
+#define DFS_MAX_PEERS 8
+typedef struct { unsigned char bytes[64]; } dfs_ipc_handle;
+
+int dfs_peer_alloc(size_t bytes, void** ptr, dfs_ipc_handle* handle);
+int dfs_peer_open(const dfs_ipc_handle* handle, void** ptr);
+int dfs_peer_close(void* ptr);  /* unmaps a buffer mapped by dfs_peer_open */
+int dfs_peer_free(void* ptr);   /* frees a buffer from dfs_peer_alloc */
+
+typedef struct {
+  int32_t npeers;           /* GPUs in the run (<= DFS_MAX_PEERS), this one included */
+  int32_t self;             /* this GPU's index in ws[] */
+  void* ws[DFS_MAX_PEERS];  /* every GPU's forward workspace (own one included), same problem */
+  uint64_t wait_for;        /* arrivals the phase waits for on its own counter before reading */
+} dfs_peer_set;
+
+/* One forward phase (DFS_OP_FWD_*) with peer exchange.  FWD_INIT also raises
+ * every GPU's counter once (a later call's stores then wait until this call
+ * has started everywhere, i.e. the previous call has finished); FWD_ROWS and
+ * FWD_COLS store the new potentials of rows [row_begin, row_end) into every
+ * workspace and raise every counter once per block of 128 rows of each
+ * problem; FWD_ROWS, FWD_COLS and FWD_OUT first wait until their own counter
+ * reaches peers->wait_for (bounded: a timeout sets DFS_ERR_DEVICE_TIMEOUT in
+ * the status word).  Counters accumulate for the life of the workspace, so all
+ * GPUs must pass the same cumulative wait_for sequence.  Only where the
+ * TMA-staged passes run (d = 64, or fp32 with d = 32; N >= 128; 16-byte aligned
+ * operands); elsewhere DFS_ERR_UNSUPPORTED. */
+int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int row_begin, int row_end,
+                       void* workspace, size_t workspace_bytes, const dfs_peer_set* peers, void* stream);
+
 /* Self-test of the tensor-core building blocks: runs the three tcgen05 MMA
  * operand layouts the kernels use on caller-provided data (see csrc). */
 int dfs_selftest_mma(int which, const float* A, const float* B, float* D,

@@ -35,26 +35,32 @@ def main():
     lm = lm[:, None, :].expand(B, H, N).contiguous()
     eps = torch.full((H,), 0.5, device=dev)
     cg = dict(rtol=1e-6, atol=0.0, max_iter=40)
-    outs = []
-    for fn in (flash_sinkhorn, row_sharded_flash_sinkhorn):
+    outs = {}
+    # single GPU, then the row-sharded run with each exchange of the half-updates'
+    # potentials (peer memory, the default; NCCL all-gathers), twice each so that
+    # a second call reuses the peer workspace and its counters
+    for name in ("single", "peer", "peer", "collective"):
+        os.environ["DFS_ROWSHARD_EXCHANGE"] = name
         leaves = [t.clone().requires_grad_(True) for t in (Q, K, V)]
-        if fn is flash_sinkhorn:
-            O, _, lu, lv = fn(*leaves, None, None, None, eps, None, lm, lm, K_iter=30, lam=1.0, mask=mask,
-                              cg_opts=cg)
+        if name == "single":
+            O, _, lu, lv = flash_sinkhorn(*leaves, None, None, None, eps, None, lm, lm, K_iter=30, lam=1.0,
+                                          mask=mask, cg_opts=cg)
         else:
-            O, _, lu, lv = fn(*leaves, eps, lm, lm, K_iter=30, lam=1.0, mask=mask, cg_opts=cg)
+            O, _, lu, lv = row_sharded_flash_sinkhorn(*leaves, eps, lm, lm, K_iter=30, lam=1.0, mask=mask,
+                                                      cg_opts=cg)
         grads = torch.autograd.grad(O, leaves, grad_outputs=dO)
-        outs.append([O, lu, lv] + [t.float() for t in grads])
+        outs[name] = [O, lu, lv] + [t.float() for t in grads]
     torch.cuda.synchronize()
     bad = []
-    for name, a, b, tol in zip(("O", "log_u", "log_v", "dQ", "dK", "dV"), outs[0], outs[1],
-                               (2e-3, 1e-3, 1e-3, 5e-3, 5e-3, 5e-3)):
-        if name.startswith("d"):
-            err = float((a - b).norm() / b.norm().clamp_min(1e-30))
-        else:
-            err = float((a - b).abs().max())
-        if not (err <= tol):
-            bad.append(f"{name} {err:.3e}")
+    for mode in ("peer", "collective"):
+        for name, a, b, tol in zip(("O", "log_u", "log_v", "dQ", "dK", "dV"), outs["single"], outs[mode],
+                                   (2e-3, 1e-3, 1e-3, 5e-3, 5e-3, 5e-3)):
+            if name.startswith("d"):
+                err = float((a - b).norm() / b.norm().clamp_min(1e-30))
+            else:
+                err = float((a - b).abs().max())
+            if not (err <= tol):
+                bad.append(f"{mode} {name} {err:.3e}")
     flag = torch.tensor([len(bad)], device=dev)
     dist.all_reduce(flag)
     print(f"rank {rank}: {'ok' if not bad else 'MISMATCH ' + ', '.join(bad)}", flush=True)

@@ -62,3 +62,17 @@ def test_row_gather_gloo(world, N):
         p.join(timeout=120)
         assert p.exitcode == 0
     assert list(out) == [1] * world
+
+
+@pytest.mark.parametrize("N,world", [(8192, 8), (1000, 2), (1000, 3), (129, 2), (128, 4), (300, 8)])
+def test_peer_arrivals_match_the_kernel_launch_grid(N, world):
+    """The host's expected arrivals per half-update equal the row blocks every
+    rank's launch covers (launch grid: P * ceil(rows / 128) blocks per rank)."""
+    from deepfold.model.kernels.sinkhorn_rowshard import arrivals_per_half_update, row_range
+    P = 5
+    blocks = 0
+    for r in range(world):
+        r0, r1, _ = row_range(N, world, r)
+        rows = r1 - r0
+        blocks += P * ((rows + 127) // 128 if rows > 0 else 0)
+    assert arrivals_per_half_update(P, N, world) == blocks
