@@ -62,6 +62,60 @@ def flops_per_call(n_cg_mean):
     return fwd, bwd, useful
 
 
+class CopyPipeline:
+    """Host<->device copies of an end-to-end loop, overlapped with the compute of
+    the neighbouring steps: the inputs of step i+1 are copied in on a side stream
+    while step i computes (two device input buffers), and the results of step i
+    are read back on the side stream while step i+1 computes.  Every step still
+    copies its own inputs in from pinned host memory and its own results out
+    inside the timed region (the end event waits for the last read-back)."""
+
+    def __init__(self, host: dict, device, compute):
+        self.host, self.compute = host, compute
+        self.side = torch.cuda.Stream(device)
+        self.bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()}
+                     for _ in range(2)]
+        self.loaded = [torch.cuda.Event() for _ in range(2)]
+        self.freed = [None, None]
+        self.outs = [None, None]
+
+    def start(self):
+        """Call after recording the start event: the first inputs go in behind it."""
+        self.side.wait_stream(self.compute)
+        self.prefetch(0)
+
+    def prefetch(self, i):
+        b = i % 2
+        with torch.cuda.stream(self.side):
+            if self.freed[b] is not None:
+                self.side.wait_event(self.freed[b])
+            for k, v in self.host.items():
+                self.bufs[b][k].copy_(v, non_blocking=True)
+            self.loaded[b].record(self.side)
+
+    def inputs(self, i):
+        self.compute.wait_event(self.loaded[i % 2])
+        return self.bufs[i % 2]
+
+    def finish_step(self, i, results):
+        """Step i's compute is queued: release its input buffer and read its results back."""
+        b = i % 2
+        done = torch.cuda.Event()
+        done.record(self.compute)
+        self.freed[b] = done
+        if self.outs[b] is None:
+            self.outs[b] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in results]
+        self.side.wait_event(done)
+        with torch.cuda.stream(self.side):
+            for o, r in zip(self.outs[b], results):
+                r.record_stream(self.side)
+                o.copy_(r, non_blocking=True)
+        return sum(o.numel() * o.element_size() for o in self.outs[b])
+
+    def end(self):
+        self.compute.wait_stream(self.side)
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -258,6 +312,8 @@ def run_ours(args):
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = sum(v.numel() * v.element_size() for v in out_host.values())
 
+    # (steps of ~0.15 ms: copies on the compute stream in order keep the host
+    # work per step minimal, which an overlapped copy pipeline does not)
     def step_e2e():
         dev_in = {k: host[k].to(dev, non_blocking=True) for k in host}
         Q = dev_in["Q"].requires_grad_(True)
@@ -422,16 +478,27 @@ def run_big(args):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    outs = [torch.empty(gt.shape, dtype=gt.dtype, pin_memory=True) for gt in step(dev_in)]
+
+    pipe = CopyPipeline(host, dev, stream)  # buffers (pinned read-back ones included) made once, outside timing
+
+    def run_e2e(n):
+        nbytes = 0
+        pipe.start()
+        for i in range(n):
+            if i + 1 < n:
+                pipe.prefetch(i + 1)
+            inp = {k: v.detach() for k, v in pipe.inputs(i).items()}
+            nbytes = pipe.finish_step(i, step(inp))
+        pipe.end()
+        return nbytes
+
+    run_e2e(2)  # both buffer sets allocated and used once
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize()
     e2.record(stream)
-    for _ in range(args.steps):
-        inp = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-        grads = step(inp)
-        d2h = 0
-        for out, gt in zip(outs, grads):
-            out.copy_(gt, non_blocking=True)
-            d2h += out.numel() * out.element_size()
+    d2h = run_e2e(args.steps)
     e3.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e2.elapsed_time(e3)
