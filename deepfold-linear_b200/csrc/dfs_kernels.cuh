@@ -118,6 +118,7 @@ struct TileArgs {
   float* row_out_nat;
   float* row_R;
   int32_t* status;
+  const int2* extent;      // (B) valid extents of the mask (compute_extents), or null: scan the mask
   float* split;            // tile_split_bytes() of scratch for column splits (counters zeroed
                            // by tile_split_reset), or null: one CTA per row block
   // peer exchange (LSE only): row_out's slot in every GPU's workspace, their arrival
@@ -131,6 +132,9 @@ struct TileArgs {
   float lam;
 };
 size_t tile_split_bytes(int B, int H, int N);
+// Per batch element, the smallest range [lo, hi) of positions holding every
+// valid point of the mask ([0, 0) when none is valid), into out[B].
+cudaError_t compute_extents(const float* mask, int B, int N, int2* out, cudaStream_t st);
 // Raises each of the n counters once (system-scope release), one thread.
 cudaError_t peer_signal(unsigned long long* const* cnt, int n, cudaStream_t st);
 cudaError_t tile_split_reset(float* split, int B, int H, int N, cudaStream_t st);
@@ -173,6 +177,7 @@ struct BtArgs {
   float* acc;
   float acc_scale;
   int32_t* status;
+  const int2* extent;      // (B) valid extents of the mask, or null
   int B, H, N, row_begin, row_end;
 };
 enum BtPass { BTP_ROW = 0, BTP_COL = 1, BTP_DQ = 2, BTP_DK = 3, BTP_OUT = 4 };

@@ -333,11 +333,12 @@ cudaError_t launch_stream(int mode, int d, const StreamParams& p, cudaStream_t s
 
 // f, g (log2), m, R; then fp32 copies Q, K (row-major) and V^T (transposed)
 // for the TMA-staged transport-output pass
-// ... then the column-split scratch and a 64-byte slot whose first 8 bytes are
-// the peer-exchange arrival counter
+// ... then the column-split scratch, a 64-byte slot whose first 8 bytes are
+// the peer-exchange arrival counter, and the mask's valid extent per batch element
 size_t stream_fwd_workspace(int B, int H, int N, int d) {
   const size_t n = static_cast<size_t>(B) * H * N;
-  return 4 * sizeof(float) * n + 256 + 3 * sizeof(float) * n * d + 256 + tile_split_bytes(B, H, N) + 128;
+  return 4 * sizeof(float) * n + 256 + 3 * sizeof(float) * n * d + 256 + tile_split_bytes(B, H, N) + 128 +
+         sizeof(int2) * static_cast<size_t>(B);
 }
 
 namespace {
@@ -369,6 +370,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
   auto at_peer = [&](int k, const void* own) {
     return static_cast<char*>(peers->ws[k]) + (static_cast<const char*>(own) - reinterpret_cast<char*>(ws));
   };
+  int2* extents = reinterpret_cast<int2*>(reinterpret_cast<char*>(counter) + 64);
   unsigned long long* cnts[DFS_MAX_PEERS] = {};
   if (peers != nullptr)
     for (int k = 0; k < peers->npeers; ++k) cnts[k] = reinterpret_cast<unsigned long long*>(at_peer(k, counter));
@@ -378,6 +380,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     stream_init_kernel<<<blocks, 256, 0, st>>>(gw, fp.log_v, fp.log_v_init, n);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = tile_split_reset(split, fp.B, fp.H, fp.N, st);
+    if (e == cudaSuccess) e = compute_extents(fp.mask, fp.B, fp.N, extents, st);
     if (e == cudaSuccess && peers != nullptr) e = peer_signal(cnts, peers->npeers, st);
     return e;
   }
@@ -406,6 +409,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
   ta.row_end = r1;
   ta.lam = fp.lam;
   ta.split = split;
+  ta.extent = fp.mask != nullptr ? extents : nullptr;
   if (peers != nullptr) {
     if (!tma) return cudaErrorNotSupported;
     ta.wait_cnt = counter;
@@ -493,6 +497,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
         ba.acc = fp.O;
         ba.acc_scale = 1.0f;
         ba.status = fp.status;
+        ba.extent = ta.extent;
         ba.B = fp.B;
         ba.H = fp.H;
         ba.N = fp.N;

@@ -627,7 +627,7 @@ __global__ void __launch_bounds__(kVThreads) sb_final_kernel(VecParams p) {
 size_t stream_bwd_workspace(int B, int H, int N, int d) {
   const size_t n = static_cast<size_t>(B) * H * N, bh = static_cast<size_t>(B) * H;
   return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256 + bt_copies_bytes(B, H, N, d) +
-         256 + tile_split_bytes(B, H, N);
+         256 + tile_split_bytes(B, H, N) + 64 + sizeof(int2) * static_cast<size_t>(B);
 }
 
 constexpr bool same_slot(int a, int b) { return a == b; }
@@ -655,9 +655,10 @@ static_assert(same_slot(WS_F, DFS_WS_BWD_F) && same_slot(WS_G, DFS_WS_BWD_G) && 
 //   BWD_FINAL                    w1, null-space shift, dlog_mu, dlog_nu, CG report
 //   BWD_DQ         rows          dQ
 //   BWD_DKV        columns       dK, dV
-static TileArgs tile_args(const BwdParams& bp, int r0, int r1, float* split) {
+static TileArgs tile_args(const BwdParams& bp, int r0, int r1, float* split, const int2* ext) {
   TileArgs ta{};
   ta.split = split;
+  ta.extent = ext;
   ta.dtype = bp.in_dtype;
   ta.d = bp.d;
   ta.eps = bp.eps;
@@ -707,6 +708,10 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   // column-split scratch of the plan-vector products, after the copies
   float* split = reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(cp.dOT + static_cast<size_t>(n) * d) + 255) & ~uintptr_t(255));
+  // the mask's valid extent per batch element, after the split scratch
+  int2* extents = reinterpret_cast<int2*>(
+      (reinterpret_cast<uintptr_t>(split) + tile_split_bytes(B, H, N) + 63) & ~uintptr_t(63));
+  const int2* ext = bp.mask != nullptr ? extents : nullptr;
   BtArgs ba{};
   ba.d = d;
   ba.eps = bp.eps;
@@ -717,6 +722,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   ba.N = N;
   ba.row_begin = r0;
   ba.row_end = r1;
+  ba.extent = ext;
 
   StreamBwdParams q{};
   q.dtype = bp.in_dtype;
@@ -733,6 +739,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       cudaError_t e = cudaGetLastError();
       if (e == cudaSuccess && bt) e = bt_prep(bp, cp, st);
       if (e == cudaSuccess) e = tile_split_reset(split, B, H, N, st);
+      if (e == cudaSuccess) e = compute_extents(bp.mask, B, N, extents, st);
       return e;
     }
     case DFS_OP_BWD_ROWSTATS:  // m, R, D
@@ -783,7 +790,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
     case DFS_OP_BWD_P_U:   // t = D1^-1 P u2 (problems whose CG has stopped are skipped)
     case DFS_OP_BWD_P_X:   // s = P x2
       if (tile_path_ok(bp.in_dtype, d, N, bp.Q, bp.K)) {
-        TileArgs ta = tile_args(bp, r0, r1, split);
+        TileArgs ta = tile_args(bp, r0, r1, split, ext);
         ta.A = bp.Q; ta.Bop = bp.K;
         ta.col_bias = slot(WS_G); ta.col_vec = slot(op == DFS_OP_BWD_P_U ? WS_U2 : WS_X2);
         ta.row_bias = slot(WS_F); ta.row_scale = op == DFS_OP_BWD_P_U ? slot(WS_D1I) : nullptr;
@@ -799,7 +806,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       return launch_stream_bwd_pass(SB_MATVEC, d, q, st);
     case DFS_OP_BWD_PT_T:  // s = P^T t (skips stopped problems once the CG has started)
       if (tile_path_ok(bp.in_dtype, d, N, bp.K, bp.Q)) {
-        TileArgs ta = tile_args(bp, r0, r1, split);
+        TileArgs ta = tile_args(bp, r0, r1, split, ext);
         ta.A = bp.K; ta.Bop = bp.Q;
         ta.col_bias = slot(WS_F); ta.col_vec = slot(WS_T);
         ta.row_bias = slot(WS_G);

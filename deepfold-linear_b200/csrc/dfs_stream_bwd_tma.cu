@@ -64,6 +64,7 @@ struct BTileParams {
   float* acc;             // (BH, N, d) accumulated result (COL: dV; DQ: dQ; DK: dK)
   float acc_scale;        // < 0: 1 / (eps_h sqrt d)
   int32_t* status;
+  const int2* extent;     // (B) valid extents of the mask, or null (scan the mask)
   int B, H, N, row_begin, row_end;
 };
 
@@ -126,9 +127,38 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
   // only the column tiles holding a valid point are visited (a masked column
   // contributes exactly nothing); a block without a valid row visits none
   int vlo, vhi;
-  valid_extent<kBTThreads>(p.mask, bb, N, reinterpret_cast<int*>(base + C::OFF_RED), vlo, vhi);
+  valid_extent<kBTThreads>(p.extent, p.mask, bb, N, reinterpret_cast<int*>(base + C::OFF_RED), vlo, vhi);
   const int rhi = min(min(r0 + 128, p.row_end), N);
   const bool live = max(r0, vlo) < min(rhi, vhi);
+  if (!live) {
+    // no valid row: the block's results are the masked-row zeros, written
+    // before any set-up
+    for (int i = tid; i < rhi - r0; i += kBTThreads) {
+      const size_t o = bh * N + r0 + i;
+      if constexpr (MODE == BT_ROW) {
+        p.out0[o] = 0.0f;
+        p.out1[o] = 0.0f;
+        p.out2[o] = 0.0f;
+      } else if constexpr (MODE == BT_COL) {
+        p.out0[o] = 0.0f;
+        p.out1[o] = 0.0f;
+      } else if constexpr (MODE == BT_OUT) {
+        if (p.out0 != nullptr) {
+          p.out0[o * 3] = 0.0f;
+          p.out0[o * 3 + 1] = 0.0f;
+          p.out0[o * 3 + 2] = 0.0f;
+        }
+      }
+      if constexpr (kAcc) {
+        if (p.acc != nullptr) {
+          float4* dst = reinterpret_cast<float4*>(p.acc + o * D);
+#pragma unroll
+          for (int q = 0; q < D / 4; ++q) dst[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+    return;
+  }
   const int t_begin = live ? vlo / kBTW : 0;
   const int ntiles = live ? (vhi + kBTW - 1) / kBTW - t_begin : 0;
 
@@ -577,6 +607,7 @@ cudaError_t launch_bt_pass(int mode, const BtArgs& a, cudaStream_t st) {
   p.acc = a.acc;
   p.acc_scale = a.acc_scale;
   p.status = a.status;
+  p.extent = a.extent;
   p.B = a.B;
   p.H = a.H;
   p.N = a.N;

@@ -70,6 +70,7 @@ struct TileParams {
   unsigned long long* peer_cnt[DFS_MAX_PEERS];
   const unsigned long long* wait_cnt;
   unsigned long long wait_for;
+  const int2* extent;      // (B) valid extents of the mask, or null (scan the mask)
   float* part;             // nsplit > 1: (nsplit, 3, BH, N) partial results of the column splits
   unsigned* counter;       // nsplit > 1: (BH * row blocks) arrival counters, zero between launches
   int B, H, N;
@@ -154,9 +155,49 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
   // only column tiles holding a valid point are visited (a masked column adds
   // exactly nothing); a block without a valid row visits none
   int vlo, vhi;
-  valid_extent<kTThreads>(p.mask, bb, N, reinterpret_cast<int*>(base + C::OFF_RED), vlo, vhi);
+  valid_extent<kTThreads>(p.extent, p.mask, bb, N, reinterpret_cast<int*>(base + C::OFF_RED), vlo, vhi);
   const int rhi = min(min(r0 + 128, p.row_end), N);
   const bool live = max(r0, vlo) < min(rhi, vhi);
+  if (!live) {
+    // No valid row in this block: its rows' results are the masked-row values.
+    // The block's first CTA writes them (in a peer exchange to every GPU, after
+    // the same wait as any CTA, with the block's one signal); every CTA of the
+    // block returns before any set-up.
+    if (sp == 0) {
+      int derr = 0;
+      if (p.wait_cnt != nullptr && tid == 0) {
+        uint64_t t0 = 0;
+        for (uint32_t it = 0; ld_acquire_sys_u64(p.wait_cnt) < p.wait_for; ++it) {
+          if (it == 0) t0 = global_ns();
+          else if ((it & 63u) == 0 && global_ns() - t0 > kWaitNs) { derr = 1; break; }
+          __nanosleep(64);
+        }
+      }
+      __syncthreads();
+      for (int i = tid; i < rhi - r0; i += kTThreads) {
+        const size_t o = bh * N + r0 + i;
+        if constexpr (MODE == TL_LSE) {
+          if (p.npeers > 0) {
+            for (int k = 0; k < p.npeers; ++k) p.peer_out[k][o] = 0.0f;
+          } else {
+            p.row_out[o] = 0.0f;
+          }
+          if (p.row_out_nat) p.row_out_nat[o] = 0.0f;
+        } else {
+          p.row_out[o] = 0.0f;
+          if constexpr (MODE == TL_ROWSTATS) p.row_R[o] = 0.0f;
+        }
+      }
+      if (MODE == TL_LSE && p.npeers > 0) {
+        __threadfence_system();
+        __syncthreads();
+        if (tid == 0)
+          for (int k = 0; k < p.npeers; ++k) atomicAdd_system(p.peer_cnt[k], 1ull);
+      }
+      if (derr && tid == 0 && p.status != nullptr) atomicOr(p.status, DFS_ERR_DEVICE_TIMEOUT);
+    }
+    return;
+  }
   // this CTA's contiguous share of the row block's column tiles
   const int t_all = live ? (vhi + kTCols - 1) / kTCols - vlo / kTCols : 0;
   const int t_q = t_all / p.nsplit, t_r = t_all % p.nsplit;
@@ -516,6 +557,19 @@ cudaError_t peer_signal(unsigned long long* const* cnt, int n, cudaStream_t st) 
   return cudaGetLastError();
 }
 
+__global__ void extent_kernel(const float* mask, int N, int2* out) {
+  __shared__ int red[16];
+  int lo, hi;
+  valid_extent<256>(mask, blockIdx.x, N, red, lo, hi);
+  if (threadIdx.x == 0) out[blockIdx.x] = make_int2(lo, hi);
+}
+
+cudaError_t compute_extents(const float* mask, int B, int N, int2* out, cudaStream_t st) {
+  if (mask == nullptr || B <= 0) return cudaSuccess;
+  extent_kernel<<<B, 256, 0, st>>>(mask, N, out);
+  return cudaGetLastError();
+}
+
 size_t tile_split_bytes(int B, int H, int N) {
   const size_t n = static_cast<size_t>(B) * H * N;
   return sizeof(float) * kMaxSplit * 3 * n + sizeof(unsigned) * static_cast<size_t>(B) * H * ((N + 127) / 128);
@@ -565,16 +619,33 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
   }
   p.wait_cnt = t.wait_cnt;
   p.wait_for = t.wait_for;
-  // Column splits when the row blocks alone cannot fill the GPU: as many as fit
-  // in one wave of two CTAs per SM, at most kMaxSplit, never more than the tiles.
+  p.extent = t.extent;
+  // Column splits.  A grid of fewer row blocks than one wave (two CTAs per SM)
+  // gets as many splits as fit in that wave.  A larger grid of long rows (16
+  // tiles or more) gets the split count, up to kMaxSplit, whose last wave wastes
+  // least: equal CTAs run in waves, so 1024 blocks on 296 slots take 4 waves for
+  // 3.46 waves of work, while 2 splits take 7 waves for 6.92.
   p.nsplit = 1;
   if (t.split != nullptr) {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long slots = 2L * sms;
     const long blocks = static_cast<long>(t.B) * t.H * ((t.row_end - t.row_begin + 127) / 128);
-    const int fit = static_cast<int>((2L * sms) / (blocks > 0 ? blocks : 1));
     const int tiles = (t.N + kTCols - 1) / kTCols;
-    p.nsplit = max(1, min(min(fit, kMaxSplit), tiles));
+    if (blocks < slots) {
+      const int fit = static_cast<int>(slots / (blocks > 0 ? blocks : 1));
+      p.nsplit = max(1, min(min(fit, kMaxSplit), tiles));
+    } else if (tiles >= 16) {
+      double best = 1e30;
+      for (int ns = 1; ns <= kMaxSplit; ++ns) {
+        const long waves = (blocks * ns + slots - 1) / slots;
+        const double cost = static_cast<double>(waves) / ns + (ns > 1 ? 0.02 : 0.0);  // + merge
+        if (cost < best - 1e-9) {
+          best = cost;
+          p.nsplit = ns;
+        }
+      }
+    }
     if (p.nsplit > 1) {
       p.part = t.split;
       p.counter = reinterpret_cast<unsigned*>(t.split + static_cast<size_t>(kMaxSplit) * 3 * t.B * t.H * t.N);

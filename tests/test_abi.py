@@ -62,8 +62,8 @@ def test_host_side_validation(lib):
     assert lib.dfs_workspace_size(big, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
     # f, g, m, R (fp32, N each), fp32 copies of Q, K and V^T (N x d each), column-split
     # partials (4 splits x 3 values x N fp32) and counters (one per 128-row block), alignment slack,
-    # and the peer-exchange arrival counter's slot
-    assert fb.value == 4 * 4 * 4096 + 3 * 4 * 4096 * 32 + 4 * 3 * 4 * 4096 + 4 * (4096 // 128) + 2 * 256 + 128
+    # the peer-exchange arrival counter's slot and one (lo, hi) valid extent per batch element
+    assert fb.value == 4 * 4 * 4096 + 3 * 4 * 4096 * 32 + 4 * 3 * 4 * 4096 + 4 * (4096 // 128) + 2 * 256 + 128 + 8
     huge = nat.make_problem(1, 1, 1 << 17, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
     assert lib.dfs_fwd(huge, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
     odd_d = nat.make_problem(1, 1, 128, 48, __import__("torch").bfloat16, 20, 1.0, 10.0)
