@@ -46,6 +46,9 @@ constexpr int kTEpi = 256;      // epilogue threads
 constexpr int kTProducer = 8, kTMma = 9;
 constexpr float kLag = 16.0f;   // log2 headroom of the lagged exponent reference
 constexpr int kMaxSplit = 4;    // column splits of a row block (small grids)
+// bf16 / fp16 passes: one exponential in kPolyEvery runs as a polynomial on the
+// FMA pipes (ex2_poly) instead of the MUFU, whose throughput bounds these passes
+constexpr int kPolyEvery = 5;  // (k = 4, 9, 14, ...: spread over the four partial sums)
 constexpr int kTCols = 128;     // columns per tile
 
 struct TileParams {
@@ -94,7 +97,14 @@ struct TileCfg {
   static constexpr uint32_t OFF_CB = OFF_B + NS * TILE;   // NS x 128 column bias
   static constexpr uint32_t OFF_CV = OFF_CB + NS * 512u;  // NS x 128 column vector
   static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 3 x 128 partials of the second half, a flag
-  static constexpr uint32_t OFF_BAR = OFF_MRG + 1536u + 16u;
+  // bf16 / fp16 operands: the column bias rides in the MMA as one more K = 16
+  // slice (A: ones, B: the bias in three bf16 parts), in the no-swizzle
+  // core-matrix layout, 128 rows x 32 bytes = 4 KB per tile
+  static constexpr bool kExt = DT != DFS_F32;
+  static constexpr uint32_t EXT = 4096u;
+  static constexpr uint32_t OFF_AX = OFF_MRG + 1536u + 16u + 112u;  // 128-byte aligned
+  static constexpr uint32_t OFF_BX = OFF_AX + (kExt ? EXT : 0u);
+  static constexpr uint32_t OFF_BAR = OFF_BX + (kExt ? NS * EXT : 0u);
   static constexpr uint32_t NBAR = 2 * NS + 5;            // full, empty, sfull x2, sempty x2, afull
   static constexpr uint32_t OFF_SLOT = OFF_BAR + 8 * NBAR;
   static constexpr uint32_t OFF_RED = OFF_SLOT + 16;
@@ -217,6 +227,20 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     mbar_init(afull, 1);
     fence_mbar_init();
   }
+  if constexpr (C::kExt) {
+    // extension operand A: rows [1, 1, 1, 0 ...] (B rows are written whole by
+    // the producer, per tile)
+    uint32_t* ax = reinterpret_cast<uint32_t*>(base + C::OFF_AX);
+    const uint32_t one = DT == DFS_BF16 ? 0x3F80u : 0x3C00u;
+    for (int i = tid; i < static_cast<int>(C::EXT / 4); i += kTThreads) {
+      // 32-bit word i holds elements (2i, 2i+1) of the layout: element k of row r sits at
+      // ((r / 8) * 2 + k / 8) * 64 + (r % 8) * 8 + k % 8 (in 2-byte units)
+      const int e = 2 * i, kchunk = (e >> 6) & 1, k = (kchunk << 3) | (e & 7);
+      const uint32_t lo = k < 3 ? one : 0u, hi = (k + 1) < 3 ? one : 0u;
+      ax[i] = lo | (hi << 16);
+    }
+    fence_async_smem();
+  }
   int err = 0;
   if (p.wait_cnt != nullptr && tid == 0) {
     // peer exchange: the potentials this phase reads are complete on this GPU
@@ -241,6 +265,8 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         mbar_arrive_expect_tx(smem_u32(afull), C::TILE);
         tma_tile<DT, D>(sA, &p.tmA, r0, prob, smem_u32(afull));
       }
+      const float inv_scale = p.eps[hh] * sqrtf(static_cast<float>(D)) / kLog2e;  // 1 / scale
+      (void)inv_scale;
       // the tile's column bias (and vector), 4 columns per lane, fetched one tile
       // ahead so that their global latency overlaps the wait for a free stage
       float pc[4], pw[4];
@@ -267,9 +293,43 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          cbs[s * 128 + lane + 32 * q] = pc[q];
-          if constexpr (MODE == TL_MATVEC) cvs[s * 128 + lane + 32 * q] = pw[q];
+          const int c = lane + 32 * q;
+          if constexpr (C::kExt) {
+            // bias / scale as three bf16 / fp16 parts hi + mid + lo (a masked column: -inf, 0, 0)
+            const float y = pc[q] * inv_scale;
+            float r1 = 0.0f, r2 = 0.0f;
+            uint32_t h0, h1, h2;
+            if constexpr (DT == DFS_BF16) {
+              const __nv_bfloat16 b0 = __float2bfloat16_rn(y);
+              const bool fin = y > -1e30f;
+              r1 = fin ? y - __bfloat162float(b0) : 0.0f;
+              const __nv_bfloat16 b1 = __float2bfloat16_rn(r1);
+              r2 = fin ? r1 - __bfloat162float(b1) : 0.0f;
+              const __nv_bfloat16 b2 = __float2bfloat16_rn(r2);
+              h0 = __bfloat16_as_ushort(b0);
+              h1 = __bfloat16_as_ushort(b1);
+              h2 = __bfloat16_as_ushort(b2);
+            } else {
+              const __half b0 = __float2half_rn(y);
+              const bool fin = y > -1e30f;
+              r1 = fin ? y - __half2float(b0) : 0.0f;
+              const __half b1 = __float2half_rn(r1);
+              r2 = fin ? r1 - __half2float(b1) : 0.0f;
+              const __half b2 = __float2half_rn(r2);
+              h0 = __half_as_ushort(b0);
+              h1 = __half_as_ushort(b1);
+              h2 = __half_as_ushort(b2);
+            }
+            // row c: elements 0-7 (core matrix of K chunk 0) and 8-15 (chunk 1, zeros)
+            uint4* row = reinterpret_cast<uint4*>(base + C::OFF_BX + s * C::EXT + (c >> 3) * 256 + (c & 7) * 16);
+            row[0] = make_uint4(h0 | (h1 << 16), h2, 0u, 0u);
+            row[8] = make_uint4(0u, 0u, 0u, 0u);
+          } else {
+            cbs[s * 128 + c] = pc[q];
+          }
+          if constexpr (MODE == TL_MATVEC) cvs[s * 128 + c] = pw[q];
         }
+        if constexpr (C::kExt) fence_async_smem();  // the MMA reads the extension rows
         mbar_arrive(&full[s]);
         if (u + 1 < ntiles) fetch(u + 1);
       }
@@ -289,6 +349,10 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         tc_fence_after();
         if (lane == 0) {
           tile_mma<DT, D>(tbase + b * kTCols, sA, sB + s * C::TILE);
+          if constexpr (C::kExt)  // + the column bias: ones x (bias parts), K = 16
+            mma_f16(tbase + b * kTCols, noswz_desc(smem_u32(base + C::OFF_AX), 128, 256),
+                    noswz_desc(smem_u32(base + C::OFF_BX + s * C::EXT), 128, 256),
+                    idesc_f16(128, kTCols, DT == DFS_BF16), 1u);
           mma_commit(&sfull[b]);
           mma_commit(&empty[s]);
         }
@@ -325,12 +389,45 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
 #pragma unroll
         for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(rv32[k]);
         const float* cb = cbs + s * 128 + 32 * ch;
-        if constexpr (MODE == TL_MATVEC) {
+        if constexpr (MODE == TL_MATVEC && C::kExt) {
+          // v = S + g / scale (the column bias came with the MMA)
+          const float* cv = cvs + s * 128 + 32 * ch;
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const float x = fmaf(v[k], scale, fi);
+            a[k & 3] = fmaf((k % kPolyEvery == kPolyEvery - 1) ? ex2_poly(x) : ex2(x), cv[k], a[k & 3]);
+          }
+          acc += (a[0] + a[1]) + (a[2] + a[3]);
+        } else if constexpr (MODE == TL_MATVEC) {
           const float* cv = cvs + s * 128 + 32 * ch;
           float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
           for (int k = 0; k < 32; ++k) a[k & 3] = fmaf(ex2(fmaf(v[k], scale, cb[k] + fi)), cv[k], a[k & 3]);
           acc += (a[0] + a[1]) + (a[2] + a[3]);
+        } else if constexpr (C::kExt) {
+          // v = S + g / scale: x - m = v scale - m is one FMA per element; the
+          // chunk maximum is taken on v (scale > 0).  Same lagged reference as below.
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          const float nm = -m;
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            a[k & 3] += (k % kPolyEvery == kPolyEvery - 1) ? ex2_poly(fmaf(v[k], scale, nm)) : ex2(fmaf(v[k], scale, nm));
+          float mx[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mx[q] = fmaxf(fmaxf(v[4 * q], v[4 * q + 1]), fmaxf(v[4 * q + 2], v[4 * q + 3]));
+          const float cm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale;
+          mt = fmaxf(mt, cm);
+          if (cm > m + kLag) {
+            a[0] = a[1] = a[2] = a[3] = 0.0f;
+            const float ncm = -cm;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) a[k & 3] += ex2(fmaf(v[k], scale, ncm));
+            sum *= ex2(m - cm);
+            m = cm;
+          }
+          sum += (a[0] + a[1]) + (a[2] + a[3]);
         } else {
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] = fmaf(v[k], scale, cb[k]);

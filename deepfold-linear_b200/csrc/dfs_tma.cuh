@@ -36,6 +36,43 @@ DFS_DEV void tmem_wait_ld(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])::"memory");
 }
 
+// Shared-memory matrix descriptor of a K-major operand without swizzle: core
+// matrices of 8 rows x 16 bytes stored contiguously (128 bytes), lbo = byte
+// stride between core matrices adjacent in K, sbo = between those adjacent in
+// M / N.
+DFS_DEV uint64_t noswz_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100; layout type 0 = no swizzle
+  return d;
+}
+
+// 2^x on the FMA and integer pipes, to take part of the exponentials off the
+// MUFU (which runs 16 of them per clock per SM against 128 FMAs).  Cody-Waite
+// style: x = j + f with j = round(x) by the 1.5 * 2^23 rounding trick (j lands
+// in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f by a degree-5
+// polynomial whose coefficients are a relative-error minimax fit on
+// [-0.5, 0.5] (iteratively reweighted least squares in float64, rounded to
+// fp32); 2^j by adding j to the exponent field.  Maximum relative error
+// 2.1e-7 over [-125, 16] (fp32 evaluation with FMA), about that of ex2.approx.
+// x is clamped below at -125 so the result stays a normal float: there it
+// returns 2^-125 (about 2.4e-38) instead of a smaller value or zero, which is
+// below the rounding of any sum it joins whose largest term is >= 1.
+DFS_DEV float ex2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float j = t - 12582912.0f;
+  const float f = x - j;
+  float p = fmaf(0.00132764445f, f, 0.00967553724f);
+  p = fmaf(p, f, 0.0555071346f);
+  p = fmaf(p, f, 0.240221202f);
+  p = fmaf(p, f, 0.693146944f);
+  p = fmaf(p, f, 1.00000012f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 // 64-bit load with system-scope acquire (a counter raised by other GPUs).
 DFS_DEV unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;
