@@ -99,6 +99,7 @@ template <int MODE, int D>
 __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_constant__ BTileParams p) {
   using C = BTileCfg<MODE, D>;
   constexpr bool kAcc = C::kAcc, kDT = C::kDT;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch (see launch_dependent)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* sA = reinterpret_cast<float*>(base + C::OFF_A);
@@ -529,8 +530,7 @@ cudaError_t launch_bt_md(const BTileParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nrb = (p.row_end - p.row_begin + 127) / 128;
-  kern<<<p.B * p.H * nrb, kBTThreads, C::SMEM, st>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(kern, dim3(p.B * p.H * nrb), dim3(kBTThreads), C::SMEM, st, p);
 }
 
 template <int MODE>

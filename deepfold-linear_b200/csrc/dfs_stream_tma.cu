@@ -141,6 +141,10 @@ DFS_DEV void tile_mma(uint32_t d_tmem, uint32_t a_s, uint32_t b_s) {
 template <int MODE, int DT, int D>
 __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constant__ TileParams p) {
   using C = TileCfg<DT, D>;
+  // launched as a programmatic dependent of the previous kernel on the stream:
+  // its grid is set up while that kernel drains; nothing is read before this
+  // wait returns, i.e. before the previous kernel's results are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sA = smem_u32(base + C::OFF_A), sB = smem_u32(base + C::OFF_B);
@@ -618,8 +622,7 @@ cudaError_t launch_tile_mdd(const TileParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nrb = (p.row_end - p.row_begin + 127) / 128;
-  kern<<<p.B * p.H * nrb * p.nsplit, kTThreads, C::SMEM, st>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(kern, dim3(p.B * p.H * nrb * p.nsplit), dim3(kTThreads), C::SMEM, st, p);
 }
 
 template <int MODE>

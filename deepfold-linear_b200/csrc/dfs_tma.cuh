@@ -99,6 +99,28 @@ DFS_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int x, int y, int 
       : "memory");
 }
 
+// Launches a kernel as a programmatic dependent of the previous work on the
+// stream (programmatic stream serialization): its grid may be launched and set
+// up while the previous kernel's last CTAs run.  The kernel must execute
+// griddepcontrol.wait before it reads anything the previous kernel wrote; no
+// kernel here triggers its dependents early, so a dependent grid starts only
+// once every CTA of its predecessor has been launched.
+template <typename Params>
+cudaError_t launch_dependent(void (*kern)(Params), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 // Tensor map of a row-major (BH, rows, inner) tensor of `dtype` elements as the
 // 3-D tensor {inner, rows, BH}, boxes of box_inner x box_rows x 1 elements with
 // 128-byte swizzle (box_inner x element size must be 128 bytes).  False when
