@@ -20,7 +20,7 @@
 // null-space shift and marginal gradients) run as one CTA per problem.
 #include <type_traits>
 
-#include "dfs_slab.cuh"
+#include "dfs_tma.cuh"
 
 namespace dfs {
 
@@ -433,6 +433,7 @@ DFS_DEV void block_sum3(float& a, float& b, float& c, float* red) {
 
 // phase 0: potentials into log2 units (elementwise over BH N)
 __global__ void sb_prep_kernel(VecParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -445,6 +446,7 @@ __global__ void sb_prep_kernel(VecParams p) {
 // after SB_ROW: f - m, 1/(R + 1e-6), the row block d1 = r/kappa (r = R 2^m) and
 // b1 = dL/df = rowsum(E) = D (1 - R/(R + 1e-6))
 __global__ void sb_rowderive_kernel(VecParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -465,6 +467,7 @@ __global__ void sb_rowderive_kernel(VecParams p) {
 // after SB_COL (one CTA per problem): d2 = c/kappa, the kappa = 1 projection of
 // the right-hand side onto the range of the singular system, and t = D1^-1 b1
 __global__ void __launch_bounds__(kVThreads) sb_setup_kernel(VecParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   __shared__ float red[32];
   const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
   const int prob = blockIdx.x, bb = prob / p.H, hh = prob % p.H, N = p.N;
@@ -501,6 +504,7 @@ __global__ void __launch_bounds__(kVThreads) sb_setup_kernel(VecParams p) {
 
 // after s = P^T D1^-1 b1: the reduced right-hand side r2 = b2 - s; x2 = 0; u2 = D2^-1 r2
 __global__ void sb_cginit_kernel(VecParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   const size_t n = static_cast<size_t>(p.B) * p.H * p.N;
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -519,6 +523,7 @@ __global__ void sb_cginit_kernel(VecParams p) {
 // scalars, then the vector updates for the next product (same recurrence as
 // the resident backward).
 __global__ void __launch_bounds__(kVThreads) sb_cgstep_kernel(VecParams p, int first) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   __shared__ float red[32];
   const int prob = blockIdx.x;
   if (p.done[prob]) return;
@@ -590,6 +595,7 @@ __global__ void __launch_bounds__(kVThreads) sb_cgstep_kernel(VecParams p, int f
 // After q = P x2 (in WS_S): w1 = D1^-1 (b1 - q); for kappa = 1 the null-space
 // shift t = -sum(r w1)/sum(r); marginal gradients; CG report (one CTA per problem).
 __global__ void __launch_bounds__(kVThreads) sb_final_kernel(VecParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   __shared__ float red[32];
   const int prob = blockIdx.x, bb = prob / p.H, hh = prob % p.H, N = p.N;
   const size_t n = static_cast<size_t>(p.B) * p.H * N;
@@ -735,8 +741,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   q.row_end = r1;
   switch (op) {
     case DFS_OP_BWD_PREP: {
-      sb_prep_kernel<<<eblocks, 256, 0, st>>>(v);
-      cudaError_t e = cudaGetLastError();
+      cudaError_t e = launch_dependent(sb_prep_kernel, dim3(eblocks), dim3(256), 0, st, v);
       if (e == cudaSuccess && bt) e = bt_prep(bp, cp, st);
       if (e == cudaSuccess) e = tile_split_reset(split, B, H, N, st);
       if (e == cudaSuccess) e = compute_extents(bp.mask, B, N, extents, st);
@@ -760,8 +765,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       q.out0 = slot(WS_M); q.out1 = slot(WS_R); q.out2 = slot(WS_D);
       return launch_stream_bwd_pass(SB_ROW, d, q, st);
     case DFS_OP_BWD_ROWDERIVE:
-      sb_rowderive_kernel<<<eblocks, 256, 0, st>>>(v);
-      return cudaGetLastError();
+      return launch_dependent(sb_rowderive_kernel, dim3(eblocks), dim3(256), 0, st, v);
     case DFS_OP_BWD_COLSTATS:  // c, g_v (and, on the TMA-staged path, dV = T_norm^T dO)
       if (bt) {
         ba.A = cp.Kf; ba.A2 = cp.Vf; ba.Bop = cp.Qf; ba.B2 = cp.dOf; ba.B3 = cp.dOT;
@@ -782,11 +786,9 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       q.out0 = slot(WS_C); q.out1 = slot(WS_GV);
       return launch_stream_bwd_pass(SB_COL, d, q, st);
     case DFS_OP_BWD_SETUP:
-      sb_setup_kernel<<<pblocks, kVThreads, 0, st>>>(v);
-      return cudaGetLastError();
+      return launch_dependent(sb_setup_kernel, dim3(pblocks), dim3(kVThreads), 0, st, v);
     case DFS_OP_BWD_CGINIT:
-      sb_cginit_kernel<<<eblocks, 256, 0, st>>>(v);
-      return cudaGetLastError();
+      return launch_dependent(sb_cginit_kernel, dim3(eblocks), dim3(256), 0, st, v);
     case DFS_OP_BWD_P_U:   // t = D1^-1 P u2 (problems whose CG has stopped are skipped)
     case DFS_OP_BWD_P_X:   // s = P x2
       if (tile_path_ok(bp.in_dtype, d, N, bp.Q, bp.K)) {
@@ -822,11 +824,10 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       return launch_stream_bwd_pass(SB_MATVEC, d, q, st);
     case DFS_OP_BWD_CGSTEP_FIRST:
     case DFS_OP_BWD_CGSTEP:
-      sb_cgstep_kernel<<<pblocks, kVThreads, 0, st>>>(v, op == DFS_OP_BWD_CGSTEP_FIRST ? 1 : 0);
-      return cudaGetLastError();
+      return launch_dependent(sb_cgstep_kernel, dim3(pblocks), dim3(kVThreads), 0, st, v,
+                              op == DFS_OP_BWD_CGSTEP_FIRST ? 1 : 0);
     case DFS_OP_BWD_FINAL:
-      sb_final_kernel<<<pblocks, kVThreads, 0, st>>>(v);
-      return cudaGetLastError();
+      return launch_dependent(sb_final_kernel, dim3(pblocks), dim3(kVThreads), 0, st, v);
     case DFS_OP_BWD_DQ:    // dQ = dS K / (eps_h sqrt d)
       if (bt) {
         ba.A = cp.Qf; ba.A2 = cp.dOf; ba.Bop = cp.Kf; ba.B2 = cp.Vf; ba.B3 = cp.KT;

@@ -105,9 +105,9 @@ DFS_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int x, int y, int 
 // griddepcontrol.wait before it reads anything the previous kernel wrote; no
 // kernel here triggers its dependents early, so a dependent grid starts only
 // once every CTA of its predecessor has been launched.
-template <typename Params>
-cudaError_t launch_dependent(void (*kern)(Params), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                             const Params& p) {
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -118,7 +118,7 @@ cudaError_t launch_dependent(void (*kern)(Params), dim3 grid, dim3 block, size_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
 }
 
 // Tensor map of a row-major (BH, rows, inner) tensor of `dtype` elements as the
