@@ -146,8 +146,10 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv") if os.path.isdir(
-            os.path.join(ROOT, "gpurun_out")) else f"/tmp/dfs_clocks_{os.getpid()}.csv"
+        # the raw samples go where DFS_CLOCK_LOG_DIR points (kept for inspection), else to a temp file
+        log_dir = os.environ.get("DFS_CLOCK_LOG_DIR")
+        self.path = (os.path.join(log_dir, f"clocks_rank{index}.csv") if log_dir
+                     else f"/tmp/dfs_clocks_{os.getpid()}_{index}.csv")
 
     def start(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
