@@ -22,12 +22,32 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? DFS_OK : DFS_ERR_CUDA
 // the kernels read Q, K, V and dO in 16-byte chunks
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// cluster-resident kernels (S kept on chip): d = 32, N <= 384; streamed
-// kernels (S recomputed tile by tile): d = 32 or 64, N <= kStreamMaxN
+// cluster-resident kernels (S kept on chip): d <= 32, N <= 384; streamed
+// kernels (S recomputed tile by tile): d <= 64, N <= kStreamMaxN.  The kernels
+// are instantiated for head dims 32 and 64; other head dims run zero-padded to
+// the next one (dfs_pad.cu), on copies at the front of the workspace.
 constexpr int kResidentMaxN = 384;
 constexpr int kStreamMaxN = 1 << 16;
-bool resident(const dfs_problem* p) { return p->d == 32 && p->N <= kResidentMaxN; }
-bool streamed(const dfs_problem* p) { return (p->d == 32 || p->d == 64) && p->N <= kStreamMaxN; }
+int kdim(const dfs_problem* p) { return kernel_head_dim(p->d); }
+bool padded(const dfs_problem* p) { return kdim(p) != p->d; }
+bool resident(const dfs_problem* p) { return kdim(p) == 32 && p->N <= kResidentMaxN; }
+bool streamed(const dfs_problem* p) { return kdim(p) != 0 && p->N <= kStreamMaxN; }
+
+size_t elem_bytes(int dtype) { return dtype == DFS_F32 ? 4 : 2; }
+size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+size_t padded_elems(const dfs_problem* p) { return static_cast<size_t>(p->B) * p->H * p->N * kdim(p); }
+// zero-padded copies at the front of the workspace: Q, K, V (input type), then
+// O (forward) or dO, dQ, dK, dV (backward), fp32; each region 256-byte aligned
+size_t pad_fwd_bytes(const dfs_problem* p) {
+  if (!padded(p)) return 0;
+  const size_t nd = padded_elems(p);
+  return 3 * round256(nd * elem_bytes(p->in_dtype)) + round256(nd * 4);
+}
+size_t pad_bwd_bytes(const dfs_problem* p) {
+  if (!padded(p)) return 0;
+  const size_t nd = padded_elems(p);
+  return 3 * round256(nd * elem_bytes(p->in_dtype)) + 4 * round256(nd * 4);
+}
 
 FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
   FwdParams q;
@@ -42,6 +62,7 @@ FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
   q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
   q.cost_mode = p->cost_mode; q.K_iter = p->K_iter; q.check_every = p->check_every > 0 ? p->check_every : 1;
   q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
+  q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
   return q;
 }
 
@@ -59,6 +80,7 @@ BwdParams bwd_params(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bw
   q.B = p->B; q.H = p->H; q.N = p->N; q.d = p->d; q.in_dtype = p->in_dtype;
   q.cg_max_iter = cg->max_iter; q.cg_rtol = cg->rtol; q.cg_atol = cg->atol;
   q.lam = p->lam; q.r_0 = p->r_0;
+  q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
   return q;
 }
 
@@ -72,7 +94,8 @@ int check_fwd_args(const dfs_problem* p, const dfs_fwd_args* a) {
   if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
-  if (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V))
+  // the kernels read the operands in 16-byte chunks (padded ones are copies)
+  if (!padded(p) && (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V)))
     return DFS_ERR_INVALID_ARGUMENT;
   return DFS_OK;
 }
@@ -83,7 +106,7 @@ int check_stream_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspac
   if (p->cost_mode != DFS_COST_QK || a->pos_weight || a->w_dist || p->threshold > 0.0f || a->T_norm ||
       (a->x_centroid && !a->O))
     return DFS_ERR_UNSUPPORTED;
-  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N, p->d) || !aligned16(workspace))
+  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N, kdim(p)) || !aligned16(workspace))
     return DFS_ERR_WORKSPACE;
   return DFS_OK;
 }
@@ -98,17 +121,17 @@ int check_bwd_args(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_
   if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
-  if (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) || !aligned16(a->dQ) ||
-      !aligned16(a->dK) || !aligned16(a->dV))
-    return DFS_ERR_INVALID_ARGUMENT;
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
+  if (!padded(p) && (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) ||
+                     !aligned16(a->dQ) || !aligned16(a->dK) || !aligned16(a->dV)))
+    return DFS_ERR_INVALID_ARGUMENT;
   return DFS_OK;
 }
 
 // streamed path: no position / geometry terms and none of their gradients
 int check_stream_bwd(const dfs_problem* p, const dfs_bwd_args* a, void* workspace, size_t workspace_bytes) {
   if (a->pos_weight || a->w_dist || a->dx_res || a->dpos_weight || a->dw_dist) return DFS_ERR_UNSUPPORTED;
-  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N, p->d) || !aligned16(workspace))
+  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N, kdim(p)) || !aligned16(workspace))
     return DFS_ERR_WORKSPACE;
   return DFS_OK;
 }
@@ -133,14 +156,17 @@ const char* dfs_status_string(int s) {
   }
 }
 
-int dfs_max_n(int d) { return (d == 32 || d == 64) ? kStreamMaxN : 0; }
+int dfs_max_n(int d) { return kernel_head_dim(d) != 0 ? kStreamMaxN : 0; }
 
 int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes) {
   if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
+  if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   const bool res = resident(p);
-  if (fwd_bytes) *fwd_bytes = res ? 0 : stream_fwd_workspace(p->B, p->H, p->N, p->d);
+  const int dk = kdim(p);
+  if (fwd_bytes) *fwd_bytes = pad_fwd_bytes(p) + (res ? 0 : stream_fwd_workspace(p->B, p->H, p->N, dk));
   if (bwd_bytes)
-    *bwd_bytes = res ? resident_bwd_workspace(p->B, p->H, p->N, p->d) : stream_bwd_workspace(p->B, p->H, p->N, p->d);
+    *bwd_bytes = pad_bwd_bytes(p) +
+                 (res ? resident_bwd_workspace(p->B, p->H, p->N, dk) : stream_bwd_workspace(p->B, p->H, p->N, dk));
   return DFS_OK;
 }
 
@@ -148,31 +174,98 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
             void* stream) {
   int rc = check_fwd_args(p, a);
   if (rc != DFS_OK) return rc;
-  if (!resident(p) && (rc = check_stream_fwd(p, a, workspace, workspace_bytes)) != DFS_OK) return rc;
-  const FwdParams q = fwd_params(p, a);
-  if (!resident(p))
-    return cuda_status(launch_stream_fwd(q, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream)));
-  return cuda_status(launch_resident_fwd(q, static_cast<cudaStream_t>(stream)));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // padded head dim: copies at the front of the workspace, the kernels' share after them
+  const size_t pad = pad_fwd_bytes(p);
+  if (pad > 0 && (workspace == nullptr || workspace_bytes < pad || !aligned16(workspace))) return DFS_ERR_WORKSPACE;
+  char* const ws = static_cast<char*>(workspace);
+  void* const kws = pad > 0 ? static_cast<void*>(ws + pad) : workspace;
+  const size_t kbytes = workspace_bytes - pad;
+  if (!resident(p) && (rc = check_stream_fwd(p, a, kws, kbytes)) != DFS_OK) return rc;
+  FwdParams q = fwd_params(p, a);
+  const size_t rows = static_cast<size_t>(p->B) * p->H * p->N;
+  float* Op = nullptr;
+  if (pad > 0) {
+    const int dk = kdim(p);
+    const size_t es = elem_bytes(p->in_dtype), opb = round256(padded_elems(p) * es);
+    char* Qp = ws;
+    char* Kp = ws + opb;
+    char* Vp = ws + 2 * opb;
+    Op = reinterpret_cast<float*>(ws + 3 * opb);
+    cudaError_t e = cudaSuccess;
+    if (a->Q) e = pad_rows(a->Q, Qp, static_cast<int>(es), rows, p->d, dk, st);
+    if (e == cudaSuccess && a->K) e = pad_rows(a->K, Kp, static_cast<int>(es), rows, p->d, dk, st);
+    if (e == cudaSuccess && a->V) e = pad_rows(a->V, Vp, static_cast<int>(es), rows, p->d, dk, st);
+    if (e != cudaSuccess) return DFS_ERR_CUDA;
+    q.d = dk;
+    q.Q = a->Q ? Qp : nullptr;
+    q.K = a->K ? Kp : nullptr;
+    q.V = a->V ? Vp : nullptr;
+    q.O = a->O ? Op : nullptr;
+  }
+  const cudaError_t e = resident(p) ? launch_resident_fwd(q, st) : launch_stream_fwd(q, static_cast<float*>(kws), st);
+  if (e != cudaSuccess) return DFS_ERR_CUDA;
+  if (pad > 0 && a->O) return cuda_status(unpad_rows(Op, a->O, rows, p->d, kdim(p), st));
+  return DFS_OK;
 }
 
 int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a, void* workspace,
             size_t workspace_bytes, void* stream) {
   int rc = check_bwd_args(p, cg, a);
   if (rc != DFS_OK) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t pad = pad_bwd_bytes(p);
+  if (pad > 0 && (workspace == nullptr || workspace_bytes < pad || !aligned16(workspace))) return DFS_ERR_WORKSPACE;
+  char* const ws = static_cast<char*>(workspace);
+  void* const kws = pad > 0 ? static_cast<void*>(ws + pad) : workspace;
+  const size_t kbytes = workspace_bytes - pad;
   if (!resident(p)) {
-    if ((rc = check_stream_bwd(p, a, workspace, workspace_bytes)) != DFS_OK) return rc;
-    return cuda_status(launch_stream_bwd(bwd_params(p, cg, a, workspace), static_cast<float*>(workspace),
-                                         static_cast<cudaStream_t>(stream)));
+    if ((rc = check_stream_bwd(p, a, kws, kbytes)) != DFS_OK) return rc;
+  } else {
+    const size_t need = resident_bwd_workspace(p->B, p->H, p->N, kdim(p));
+    if (need > 0 && (kws == nullptr || kbytes < need)) return DFS_ERR_WORKSPACE;
   }
-  const size_t need = resident_bwd_workspace(p->B, p->H, p->N, p->d);
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return DFS_ERR_WORKSPACE;
-  return cuda_status(launch_resident_bwd(bwd_params(p, cg, a, workspace), static_cast<cudaStream_t>(stream)));
+  BwdParams q = bwd_params(p, cg, a, kws);
+  const size_t rows = static_cast<size_t>(p->B) * p->H * p->N;
+  float* grads[3] = {nullptr, nullptr, nullptr};  // padded dQ, dK, dV
+  if (pad > 0) {
+    const int dk = kdim(p);
+    const size_t es = elem_bytes(p->in_dtype), opb = round256(padded_elems(p) * es);
+    const size_t fb = round256(padded_elems(p) * 4);
+    char* Qp = ws;
+    char* Kp = ws + opb;
+    char* Vp = ws + 2 * opb;
+    float* dOp = reinterpret_cast<float*>(ws + 3 * opb);
+    for (int k = 0; k < 3; ++k) grads[k] = reinterpret_cast<float*>(ws + 3 * opb + (k + 1) * fb);
+    cudaError_t e = pad_rows(a->Q, Qp, static_cast<int>(es), rows, p->d, dk, st);
+    if (e == cudaSuccess) e = pad_rows(a->K, Kp, static_cast<int>(es), rows, p->d, dk, st);
+    if (e == cudaSuccess) e = pad_rows(a->V, Vp, static_cast<int>(es), rows, p->d, dk, st);
+    if (e == cudaSuccess) e = pad_rows(a->dO, dOp, 4, rows, p->d, dk, st);
+    if (e != cudaSuccess) return DFS_ERR_CUDA;
+    q.d = dk;
+    q.Q = Qp;
+    q.K = Kp;
+    q.V = Vp;
+    q.dO = dOp;
+    q.dQ = a->dQ ? grads[0] : nullptr;
+    q.dK = a->dK ? grads[1] : nullptr;
+    q.dV = a->dV ? grads[2] : nullptr;
+  }
+  const cudaError_t e = resident(p) ? launch_resident_bwd(q, st) : launch_stream_bwd(q, static_cast<float*>(kws), st);
+  if (e != cudaSuccess) return DFS_ERR_CUDA;
+  if (pad > 0) {
+    float* outs[3] = {a->dQ, a->dK, a->dV};
+    for (int k = 0; k < 3; ++k)
+      if (outs[k] && unpad_rows(grads[k], outs[k], rows, p->d, kdim(p), st) != cudaSuccess) return DFS_ERR_CUDA;
+  }
+  return DFS_OK;
 }
 
 int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const dfs_fwd_args* fa,
                   const dfs_bwd_args* ba, int row_begin, int row_end, void* workspace, size_t workspace_bytes,
                   void* stream) {
-  if (!dims_ok(p) || !streamed(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  // the phases keep no padded copies between calls: head dims 32 and 64 only
+  if (!dims_ok(p) || !streamed(p) || padded(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
   if (row_begin < 0 || row_end < row_begin || row_end > p->N) return DFS_ERR_INVALID_ARGUMENT;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
@@ -220,7 +313,7 @@ int dfs_peer_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? DFS_OK : DF
 
 int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int row_begin, int row_end,
                        void* workspace, size_t workspace_bytes, const dfs_peer_set* peers, void* stream) {
-  if (!dims_ok(p) || !streamed(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  if (!dims_ok(p) || !streamed(p) || padded(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
   if (op < DFS_OP_FWD_INIT || op > DFS_OP_FWD_OUT || peers == nullptr) return DFS_ERR_INVALID_ARGUMENT;
   if (row_begin < 0 || row_end < row_begin || row_end > p->N) return DFS_ERR_INVALID_ARGUMENT;
   if (peers->npeers < 1 || peers->npeers > DFS_MAX_PEERS || peers->self < 0 || peers->self >= peers->npeers)

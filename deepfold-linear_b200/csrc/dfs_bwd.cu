@@ -95,8 +95,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   const float eps_h = p.eps[hh];
   const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
   const float s_scale = kLog2e / eps_h;
-  const float qk_scale = s_scale * rsqrtf(static_cast<float>(DH));
-  const float grad_scale = rsqrtf(static_cast<float>(DH)) / eps_h;   // dS -> dQ, dK
+  const float qk_scale = s_scale * p.qk_scale;
+  const float grad_scale = p.qk_scale / eps_h;   // dS -> dQ, dK
   const float w_h = p.w_dist ? p.w_dist[hh] : 0.0f;
   int err = 0;
   uint32_t mma_phase = 0;

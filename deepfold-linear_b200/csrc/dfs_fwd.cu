@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     const float wq = p.w_dist ? p.w_dist[hq] : 0.0f;
     __syncthreads();
     if (p.cost_mode == DFS_COST_QK)
-      drain_m64<NP>(Ts, *tslot, 0, ssc * rsqrtf(static_cast<float>(DH)), warp, lane);
+      drain_m64<NP>(Ts, *tslot, 0, ssc * p.qk_scale, warp, lane);
     else
       dense_cost_to_stage<NP>(Ts, p.C, static_cast<size_t>(bq) * p.H + hq, p.N, r0, ssc, tid);
     if (p.pos_weight != nullptr || (p.x_res != nullptr && wq != 0.0f)) {

@@ -46,6 +46,7 @@ struct FwdParams {
   float* T_out;
   int B, H, N, d, in_dtype, cost_mode, K_iter, check_every;
   float lam, r_0, threshold;
+  float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
 };
 
 struct BwdParams {
@@ -78,6 +79,7 @@ struct BwdParams {
   float* ws;               // workspace: per-CTA partials of the shared-parameter grads
   int B, H, N, d, in_dtype, cg_max_iter;
   float lam, r_0, cg_rtol, cg_atol;
+  float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
 };
 
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
@@ -130,6 +132,7 @@ struct TileArgs {
   unsigned long long wait_for;
   int B, H, N, row_begin, row_end;
   float lam;
+  float qk_scale;          // 1/sqrt(d) of the cost
 };
 size_t tile_split_bytes(int B, int H, int N);
 // Per batch element, the smallest range [lo, hi) of positions holding every
@@ -179,6 +182,7 @@ struct BtArgs {
   int32_t* status;
   const int2* extent;      // (B) valid extents of the mask, or null
   int B, H, N, row_begin, row_end;
+  float qk_scale;          // 1/sqrt(d) of the cost
 };
 enum BtPass { BTP_ROW = 0, BTP_COL = 1, BTP_DQ = 2, BTP_DK = 3, BTP_OUT = 4 };
 size_t bt_copies_bytes(int B, int H, int N, int d);
@@ -189,6 +193,12 @@ cudaError_t bt_prep(const BwdParams& bp, const BtCopies& c, cudaStream_t st);
 cudaError_t bt_convert(const void* src, int dtype, float* row_out, float* t_out, int BH, int N, int d,
                        cudaStream_t st);
 cudaError_t launch_bt_pass(int mode, const BtArgs& a, cudaStream_t st);
+
+// Head dims other than 32 / 64 (dfs_pad.cu): the instantiated head dim a
+// problem with head dim d runs on (0 when d > 64), and the zero-padding copies.
+int kernel_head_dim(int d);
+cudaError_t pad_rows(const void* src, void* dst, int esize, size_t rows, int d, int dk, cudaStream_t st);
+cudaError_t unpad_rows(const float* src, float* dst, size_t rows, int d, int dk, cudaStream_t st);
 
 cudaError_t launch_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K,
                                 cudaStream_t st);

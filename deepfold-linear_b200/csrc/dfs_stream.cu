@@ -52,6 +52,7 @@ struct StreamParams {
   int B, H, N;
   int row_begin, row_end; // rows this launch handles ([0, N) unless sharded)
   float lam;
+  float qk_scale;         // 1/sqrt(d) of the cost
 };
 
 template <int MODE, int D>
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(kSThreads) stream_kernel(const StreamParams p)
   const size_t bh = static_cast<size_t>(prob);
   const int r0 = p.row_begin + 128 * rb, row = r0 + tid;
   const float eps_h = p.eps[hh];
-  const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
+  const float scale = kLog2e * p.qk_scale / eps_h;
   const float kap = isinf(p.lam) ? 1.0f : p.lam / (p.lam + eps_h);
   const bool rin = row < p.row_end && row < N;
   const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
@@ -394,6 +395,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
   p.row_begin = r0;
   p.row_end = r1;
   p.lam = fp.lam;
+  p.qk_scale = fp.qk_scale;
   // the TMA-staged kernels take the row passes whenever they cover the operands
   const bool tma = tile_path_ok(fp.in_dtype, fp.d, fp.N, fp.Q, fp.K);
   TileArgs ta{};
@@ -408,6 +410,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
   ta.row_begin = r0;
   ta.row_end = r1;
   ta.lam = fp.lam;
+  ta.qk_scale = fp.qk_scale;
   ta.split = split;
   ta.extent = fp.mask != nullptr ? extents : nullptr;
   if (peers != nullptr) {
@@ -486,6 +489,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
         ba.B3 = VT;
         ba.d = fp.d;
         ba.eps = fp.eps;
+        ba.qk_scale = fp.qk_scale;
         ba.mask = fp.mask;
         ba.tv[0] = gw;
         ba.pot_mask = 1;

@@ -55,6 +55,7 @@ struct StreamBwdParams {
   float acc_scale0, acc_scale1;
   int B, H, N;
   int row_begin, row_end;
+  float qk_scale;                 // 1/sqrt(d) of the cost
 };
 
 template <int MODE, int D>
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
   const size_t bh = static_cast<size_t>(prob);
   const int r0 = p.row_begin + 128 * rb, row = r0 + tid;
   const float eps_h = p.eps[hh];
-  const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
+  const float scale = kLog2e * p.qk_scale / eps_h;
   const bool rin = row < p.row_end && row < N;
   const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
   int err = 0;
@@ -315,7 +316,7 @@ __global__ void __launch_bounds__(kBThreads) stream_bwd_kernel(const StreamBwdPa
     for (int a = 0; a < (kTwo ? 2 : 1); ++a) {
       float* dst_base = a == 0 ? p.acc0 : p.acc1;
       float sc = a == 0 ? p.acc_scale0 : p.acc_scale1;
-      if (sc < 0.0f) sc = 1.0f / (eps_h * sqrtf(static_cast<float>(D)));  // dS -> dQ, dK
+      if (sc < 0.0f) sc = p.qk_scale / eps_h;  // dS -> dQ, dK
 #pragma unroll
       for (int g = 0; g < D / 16; ++g) {
         float v[16];
@@ -676,6 +677,7 @@ static TileArgs tile_args(const BwdParams& bp, int r0, int r1, float* split, con
   ta.row_begin = r0;
   ta.row_end = r1;
   ta.lam = bp.lam;
+  ta.qk_scale = bp.qk_scale;
   return ta;
 }
 
@@ -721,6 +723,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   BtArgs ba{};
   ba.d = d;
   ba.eps = bp.eps;
+  ba.qk_scale = bp.qk_scale;
   ba.mask = bp.mask;
   ba.status = bp.status;
   ba.B = B;
@@ -733,6 +736,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   StreamBwdParams q{};
   q.dtype = bp.in_dtype;
   q.eps = bp.eps;
+  q.qk_scale = bp.qk_scale;
   q.mask = bp.mask;
   q.B = B;
   q.H = H;

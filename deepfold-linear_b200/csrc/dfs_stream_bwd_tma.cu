@@ -66,6 +66,7 @@ struct BTileParams {
   int32_t* status;
   const int2* extent;     // (B) valid extents of the mask, or null (scan the mask)
   int B, H, N, row_begin, row_end;
+  float qk_scale;         // 1/sqrt(d) of the cost
 };
 
 template <int MODE, int D>
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
     const bool rin = row < p.row_end && row < N;
     const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
     const float eps_h = p.eps[hh];
-    const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
+    const float scale = kLog2e * p.qk_scale / eps_h;
     float rv[5];
 #pragma unroll
     for (int k = 0; k < 5; ++k) rv[k] = (rin && p.rv[k] != nullptr) ? p.rv[k][bh * N + row] : 0.0f;
@@ -477,7 +478,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       if (ntiles > 0 && !mbar_wait(dsempty, (ntiles - 1) & 1)) err = 1;  // last accumulation MMA done
       tc_fence_after();
       float sc = p.acc_scale;
-      if (sc < 0.0f) sc = 1.0f / (eps_h * sqrtf(static_cast<float>(D)));
+      if (sc < 0.0f) sc = p.qk_scale / eps_h;
       if (16 * part < D) {
         float v[16];
         tmem_ld16(t_acc + tlane + 16 * part, v);
@@ -591,6 +592,7 @@ cudaError_t launch_bt_pass(int mode, const BtArgs& a, cudaStream_t st) {
                   (mode == BT_ROW || make_tmap(&p.tmB3, a.B3, DFS_F32, a.N, a.d, BH, 32, a.d));
   if (!ok) return cudaErrorInvalidValue;
   p.eps = a.eps;
+  p.qk_scale = a.qk_scale;
   p.mask = a.mask;
   for (int k = 0; k < 5; ++k) {
     p.tv[k] = a.tv[k];

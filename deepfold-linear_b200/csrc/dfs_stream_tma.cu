@@ -80,6 +80,7 @@ struct TileParams {
   int row_begin, row_end;  // rows this launch handles
   int nsplit;              // CTAs per row block, each over a contiguous share of the column tiles
   float lam;
+  float qk_scale;          // 1/sqrt(d) of the cost
 };
 
 template <int DT, int D>
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         mbar_arrive_expect_tx(smem_u32(afull), C::TILE);
         tma_tile<DT, D>(sA, &p.tmA, r0, prob, smem_u32(afull));
       }
-      const float inv_scale = p.eps[hh] * sqrtf(static_cast<float>(D)) / kLog2e;  // 1 / scale
+      const float inv_scale = p.eps[hh] / (kLog2e * p.qk_scale);  // 1 / scale
       (void)inv_scale;
       // the tile's column bias (and vector), 4 columns per lane, fetched one tile
       // ahead so that their global latency overlaps the wait for a free stage
@@ -370,7 +371,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     const bool rin = row < p.row_end && row < N;
     const bool rok = rin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + row] != 0.0f);
     const float eps_h = p.eps[hh];
-    const float scale = kLog2e / (eps_h * sqrtf(static_cast<float>(D)));
+    const float scale = kLog2e * p.qk_scale / eps_h;
     const float fi = (MODE != TL_LSE && rin) ? __ldcg(p.row_bias + bh * N + row) : 0.0f;
     const uint32_t tlane = static_cast<uint32_t>(32 * quad) << 16;
     // running reference, exact maximum and sum of exp2(x - reference) of this
@@ -712,6 +713,7 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
   p.row_begin = t.row_begin;
   p.row_end = t.row_end;
   p.lam = t.lam;
+  p.qk_scale = t.qk_scale;
   p.npeers = t.npeers;
   for (int k = 0; k < DFS_MAX_PEERS; ++k) {
     p.peer_out[k] = t.peer_out[k];

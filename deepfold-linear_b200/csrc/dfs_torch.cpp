@@ -7,9 +7,21 @@
 // C ABI on the current stream; nothing here computes.  Doing this in C++
 // rather than Python keeps the per-call host cost to a few allocations, so the
 // GPU, not the interpreter, bounds a training step.
+//
+// Errors the kernels find on the device (a bounded wait that gave up,
+// non-finite potentials, a CG solve that hit its iteration cap) are OR-ed into
+// a device status word per call.  Reading it at once would synchronise every
+// call, so each call copies its word to pinned host memory on its stream and
+// records an event; the next call (or check_status) reads every word whose
+// event has completed and raises RuntimeError for an error bit, or warns for
+// DFS_WARN_CG_NOT_CONVERGED.  check_status(true) waits for all of them.
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CUDAEvent.h>
+#include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <deque>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -47,6 +59,58 @@ std::vector<Tensor>& last_report() {
   return r;
 }
 
+// ---------------------------------------------------------------- device status
+struct PendingStatus {
+  Tensor host;                 // pinned int32 copy of the call's device status word
+  at::cuda::CUDAEvent done;    // recorded after the copy
+  const char* what;
+};
+std::mutex g_status_mu;
+std::deque<PendingStatus>& pending_status() {
+  static std::deque<PendingStatus> q;
+  return q;
+}
+
+// Queue the status word of a call launched on `stream` for checking.
+void enqueue_status(const Tensor& status, const char* what, const at::cuda::CUDAStream& stream) {
+  Tensor host = at::empty({1}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
+  host.copy_(status, /*non_blocking=*/true);  // on the current stream, which is `stream`
+  PendingStatus ps{host, at::cuda::CUDAEvent(cudaEventDisableTiming), what};
+  ps.done.record(stream);
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  pending_status().push_back(std::move(ps));
+}
+
+// Read the status words of finished calls (all of them with wait = true, in
+// call order); raise for device errors, warn for an unconverged CG solve.
+void check_status(bool wait) {
+  std::string err;
+  {
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    auto& q = pending_status();
+    while (!q.empty()) {
+      PendingStatus& ps = q.front();
+      if (wait)
+        ps.done.synchronize();
+      else if (!ps.done.query())
+        break;
+      const int v = ps.host.data_ptr<int32_t>()[0];
+      const char* what = ps.what;
+      q.pop_front();
+      if (v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)) {
+        if (err.empty())
+          err = std::string("a previous ") + what + " call reported a device error: " +
+                dfs_status_string(v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)) + " (status " +
+                std::to_string(v) + ")";
+      } else if (v & DFS_WARN_CG_NOT_CONVERGED) {
+        TORCH_WARN("a previous ", what, " call: ", dfs_status_string(DFS_WARN_CG_NOT_CONVERGED),
+                   " for some problem; its gradient is the last CG iterate");
+      }
+    }
+  }
+  TORCH_CHECK(err.empty(), err);
+}
+
 struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
   // Arguments (positions in the gradient list backward returns): 0 Q, 1 K, 2 V,
   // 3 x_res, 4 pos_weight, 5 pos_bins, 6 eps, 7 w_dist, 8 log_mu, 9 log_nu,
@@ -64,9 +128,12 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
                 "deepfold B200 Sinkhorn ops run on CUDA tensors only (no CPU path)");
     TORCH_CHECK(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(),
                 "Q, K, V must share the shape (B, H, N, d)");
+    TORCH_CHECK(K.device() == Q.device() && V.device() == Q.device(), "Q, K, V must be on one device");
+    const c10::cuda::CUDAGuard guard(Q.device());  // launches, attributes and streams of Q's device
+    check_status(false);
     const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
     TORCH_CHECK(N <= dfs_max_n(static_cast<int>(d)), "N=", N, ", d=", d,
-                " is outside the resident kernels' range (N <= ", dfs_max_n(static_cast<int>(d)), ")");
+                " is outside the kernels' range (head dim <= 64, N <= ", dfs_max_n(static_cast<int>(d)), ")");
     const auto st = Q.scalar_type();
     const auto cdt = (st == at::kBFloat16 || st == at::kHalf || st == at::kFloat) ? st : at::kFloat;
     const Tensor Qc = Q.contiguous().to(cdt), Kc = K.contiguous().to(cdt), Vc = V.contiguous().to(cdt);
@@ -115,8 +182,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     size_t fwd_ws = 0, bwd_ws = 0;  // the streamed path (large N, d = 64) needs scratch
     check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
     Tensor ws = fwd_ws ? at::empty({static_cast<int64_t>((fwd_ws + 3) / 4)}, fo) : Tensor();
-    const cudaStream_t stream = at::cuda::getCurrentCUDAStream(Q.device().index()).stream();
-    check_rc(dfs_fwd(&prob, &a, ws.defined() ? ws.data_ptr() : nullptr, fwd_ws, stream), "dfs_fwd");
+    const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(Q.device().index());
+    check_rc(dfs_fwd(&prob, &a, ws.defined() ? ws.data_ptr() : nullptr, fwd_ws, cstream.stream()), "dfs_fwd");
+    enqueue_status(status, "flash_sinkhorn forward", cstream);
 
     ctx->save_for_backward({Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv});
     ctx->saved_data["K_iter"] = K_iter;
@@ -144,6 +212,8 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
 
   static variable_list backward(AutogradContext* ctx, variable_list grads) {
     const auto saved = ctx->get_saved_variables();
+    const c10::cuda::CUDAGuard guard(saved[0].device());
+    check_status(false);
     const Tensor &Qc = saved[0], &Kc = saved[1], &Vc = saved[2], &xr = saved[3], &pw = saved[4],
                  &pb = saved[5], &epsc = saved[6], &wd = saved[7], &lmu = saved[8], &lnu = saved[9],
                  &mk = saved[10], &lu = saved[11], &lv = saved[12];
@@ -210,8 +280,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     size_t fwd_ws = 0, bwd_ws = 0;
     check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
     Tensor ws = bwd_ws ? at::empty({static_cast<int64_t>((bwd_ws + 3) / 4)}, fo) : Tensor();
-    const cudaStream_t stream = at::cuda::getCurrentCUDAStream(Qc.device().index()).stream();
-    check_rc(dfs_bwd(&prob, &cg, &a, ws.defined() ? ws.data_ptr() : nullptr, bwd_ws, stream), "dfs_bwd");
+    const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(Qc.device().index());
+    check_rc(dfs_bwd(&prob, &cg, &a, ws.defined() ? ws.data_ptr() : nullptr, bwd_ws, cstream.stream()), "dfs_bwd");
+    enqueue_status(status, "flash_sinkhorn backward", cstream);
     last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
 
     // gradients in the dtype of the forward's inputs
@@ -242,8 +313,13 @@ std::vector<Tensor> flash_sinkhorn_autograd(Tensor Q, Tensor K, Tensor V, c10::o
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "native autograd glue for libdfsink (flash Sinkhorn forward / IFT backward)";
-  m.def("flash_sinkhorn", &flash_sinkhorn_autograd,
+  // torch::wrap_pybind_function: TORCH_WARN becomes a Python warning, errors the
+  // matching Python exceptions
+  m.def("flash_sinkhorn", torch::wrap_pybind_function(flash_sinkhorn_autograd),
         "FlashSinkhornFn.apply: returns [O, x_centroid, log_u, log_v], or [O, log_u, log_v] without x_res");
   m.def("last_report", []() { return last_report(); },
         "[cg_iters, cg_residual, status, fwd_status] of the most recent backward");
+  m.def("check_status", torch::wrap_pybind_function(check_status), py::arg("wait") = true,
+        "read the device status of finished calls (all calls with wait=True); raise RuntimeError for a "
+        "device error, warn for an unconverged CG solve");
 }

@@ -23,11 +23,12 @@ INCLUDE_DIR = os.path.join(os.path.dirname(ROOT_DIR), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libdfsink.so")
 SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_stream.cu", "dfs_stream_bwd.cu", "dfs_stream_tma.cu",
-           "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu"]
+           "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu", "dfs_pad.cu"]
 HEADERS = ["dfs_device.cuh", "dfs_kernels.cuh", "dfs_slab.cuh", "dfs_tma.cuh"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-              "-Xcompiler", "-fPIC", "-shared"]
+              "-Xcompiler", "-fPIC"]
+OBJ_DIR = os.path.join(LIB_DIR, "_obj")
 
 # status codes (include/dfsink.h)
 DFS_OK = 0
@@ -113,13 +114,38 @@ def _stale() -> bool:
 
 
 def build_library(force: bool = False, verbose: bool = False) -> str:
-    """Compile ``libdfsink.so`` for sm_100a into the package (in-tree)."""
+    """Compile ``libdfsink.so`` for sm_100a into the package (in-tree).
+
+    Each source is compiled to an object file of its own (in parallel; only
+    sources newer than their object, or any header, are recompiled), then the
+    objects are linked into the shared library.
+    """
     if not force and not _stale():
         return LIB_PATH
-    os.makedirs(LIB_DIR, exist_ok=True)
+    from concurrent.futures import ThreadPoolExecutor
+
+    os.makedirs(OBJ_DIR, exist_ok=True)
     nvcc = os.environ.get("NVCC", "nvcc")
+    hdr_time = max(os.path.getmtime(f) for f in [os.path.join(CSRC_DIR, h) for h in HEADERS]
+                   + [os.path.join(INCLUDE_DIR, "dfsink.h")])
+
+    def compile_one(src: str) -> str:
+        s = os.path.join(CSRC_DIR, src)
+        o = os.path.join(OBJ_DIR, src.replace(".cu", ".o"))
+        if not force and os.path.exists(o) and os.path.getmtime(o) >= max(os.path.getmtime(s), hdr_time):
+            return o
+        tmp_o = o + ".tmp.%d" % os.getpid()
+        cmd = [nvcc] + NVCC_FLAGS + ["-I", INCLUDE_DIR, "-c", s, "-o", tmp_o]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        os.replace(tmp_o, o)
+        return o
+
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 4)) as pool:
+        objs = list(pool.map(compile_one, SOURCES))
     tmp = LIB_PATH + ".tmp.%d" % os.getpid()
-    cmd = [nvcc] + NVCC_FLAGS + ["-I", INCLUDE_DIR] + [os.path.join(CSRC_DIR, f) for f in SOURCES] + ["-o", tmp]
+    cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp] + objs
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

@@ -7,7 +7,8 @@ Sinkhorn transport (``flash_sinkhorn``, CUDA only) and applies the
 ``sigmoid(G)`` gate, the (B, N, H*d) permutation and the padding mask exactly as
 the reference does (flash_sinkhorn_attn.py:776-795).  The reference's silent
 CPU fallback (``FlashSinkhornAttn``, :751-774) does not exist here: CPU tensors
-raise.
+are computed on the current CUDA device (results come back on the CPU), and
+without a CUDA device the call raises.
 """
 
 from __future__ import annotations
@@ -44,8 +45,13 @@ def flash_sinkhorn_attn(Q_ln, K_ln, V, G, x_res, pos_weight, pos_bins, eps, w_di
     O_avg, x_centroid, log_u, log_v = flash_sinkhorn(
         Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu, K_iter=K_iter,
         lam=lam, r_0=r_0, log_u_init=log_u_init, log_v_init=log_v_init, mask=mask, cg_opts=cg_opts)
-    o_gated = torch.sigmoid(G.float()) * O_avg
+    o_gated = torch.sigmoid(G.to(O_avg.device).float()) * O_avg
+    mask = mask.to(O_avg.device)
     o_flat = o_gated.permute(0, 2, 1, 3).reshape(B, N, H * d) * mask.unsqueeze(-1)
+    # padded duals are exactly 0 (the kernels write 0 there); the product keeps
+    # the reference's own zeroing (flash_sinkhorn_attn.py:792-794)
+    log_u = log_u * mask.unsqueeze(1)
+    log_v = log_v * mask.unsqueeze(1)
     if unbatched:
         return (o_flat.squeeze(0), None if x_centroid is None else x_centroid.squeeze(0),
                 log_u.squeeze(0), log_v.squeeze(0))

@@ -16,7 +16,13 @@ Differences from the reference, all deliberate:
   ``compute_transport_output`` (sinkhorn.py:175-177).
 * Gradients with respect to ``log_u``/``log_v`` outputs are ignored, as in the
   reference backward (sinkhorn_kernel.py:2086).
-* CUDA tensors only; there is no CPU path.
+* There is no CPU path.  CPU tensors (as the reference's own tests pass them)
+  are computed on the current CUDA device and the results moved back to the
+  CPU, differentiably; without a CUDA device the call raises.
+* Head dims other than 32 and 64 (up to 64) run zero-padded inside the library.
+* Device-side errors (a bounded wait that gave up, non-finite potentials) are
+  raised as RuntimeError by the next call, or at once by ``check_status()``;
+  a CG solve that reached ``max_iter`` gives a warning.
 """
 
 from __future__ import annotations
@@ -27,7 +33,7 @@ import torch
 
 from deepfold import _native as nat
 
-__all__ = ["flash_sinkhorn", "CG_DEFAULTS", "last_cg_report"]
+__all__ = ["flash_sinkhorn", "CG_DEFAULTS", "last_cg_report", "check_status"]
 
 # CG stopping rule of the backward: ||r|| <= max(atol, rtol * ||r0||), as in
 # deepfold.utils.cg.conjugate_gradient.
@@ -39,6 +45,21 @@ def last_cg_report() -> dict:
     recent backward."""
     rep = nat.ext().last_report()
     return dict(zip(("cg_iters", "cg_residual", "status", "fwd_status"), rep))
+
+
+def check_status(wait: bool = True) -> None:
+    """Read the device status of the finished forward / backward calls (all of
+    them, after waiting, with ``wait``): RuntimeError for a device error, a
+    warning for a CG solve that reached its iteration cap."""
+    nat.ext().check_status(bool(wait))
+
+
+def _to_cuda(args: dict) -> dict:
+    """CPU tensors of a call moved to the current CUDA device (autograd follows)."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("deepfold B200 Sinkhorn ops run on a CUDA device; none is available (no CPU path)")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    return {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in args.items()}
 
 
 def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu,
@@ -56,6 +77,15 @@ def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_
     unbatched (H,N,d) inputs give unbatched outputs.
     """
     del BLOCK_N
+    if not Q_ln.is_cuda:
+        a = _to_cuda(dict(Q_ln=Q_ln, K_ln=K_ln, V=V, x_res=x_res, pos_weight=pos_weight, pos_bins=pos_bins,
+                          eps=eps, w_dist=w_dist, log_mu=log_mu, log_nu=log_nu, log_u_init=log_u_init,
+                          log_v_init=log_v_init, mask=mask))
+        out = flash_sinkhorn(a["Q_ln"], a["K_ln"], a["V"], a["x_res"], a["pos_weight"], a["pos_bins"], a["eps"],
+                             a["w_dist"], a["log_mu"], a["log_nu"], K_iter=K_iter, lam=lam, r_0=r_0,
+                             log_u_init=a["log_u_init"], log_v_init=a["log_v_init"], mask=a["mask"],
+                             cg_opts=cg_opts)
+        return tuple(None if t is None else t.cpu() for t in out)
     unbatched = Q_ln.dim() == 3
     if unbatched:
         Q_ln, K_ln, V = Q_ln.unsqueeze(0), K_ln.unsqueeze(0), V.unsqueeze(0)

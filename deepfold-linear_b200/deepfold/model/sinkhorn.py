@@ -16,7 +16,9 @@ Sinkhorn loop never leaves the GPU:
 
 The backward of these two entry points is not provided (the reference differentiates
 them with autograd through K dense iterations); use ``flash_sinkhorn`` for
-gradients.
+gradients.  CPU tensors (as the reference's tests pass them) are computed on the
+current CUDA device and the results returned on the CPU.  Head dims of V up to
+32 run (zero-padded inside the library), N up to 384.
 """
 
 from __future__ import annotations
@@ -26,6 +28,24 @@ import torch
 from deepfold import _native as nat
 
 __all__ = ["sinkhorn_solve", "compute_transport_output"]
+
+
+def _on_gpu(fn):
+    """Run ``fn`` on the current CUDA device when its cost tensor is on the CPU,
+    returning CPU results (there is no CPU path)."""
+    def wrapped(*args, **kw):
+        first = args[0] if args else None
+        if not isinstance(first, torch.Tensor) or first.is_cuda:
+            return fn(*args, **kw)
+        if not torch.cuda.is_available():
+            raise RuntimeError("deepfold B200 Sinkhorn ops run on a CUDA device; none is available (no CPU path)")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        mv = lambda t: t.to(dev) if isinstance(t, torch.Tensor) else t  # noqa: E731
+        out = fn(*[mv(a) for a in args], **{k: mv(v) for k, v in kw.items()})
+        return tuple(None if t is None else t.cpu() for t in out)
+    wrapped.__doc__ = fn.__doc__
+    wrapped.__name__ = fn.__name__
+    return wrapped
 
 
 def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshold, check_every,
@@ -45,8 +65,8 @@ def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshol
     Vp = None
     if V is not None:
         d = V.shape[-1]
-        if d != 32:
-            raise ValueError("compute_transport_output supports head dim 32")
+        if d > 32:
+            raise ValueError("compute_transport_output supports head dims up to 32")
         Vp = f32(V)
     lu = torch.empty(B, H, N, device=dev, dtype=torch.float32)
     lv = torch.empty(B, H, N, device=dev, dtype=torch.float32)
@@ -66,6 +86,7 @@ def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshol
     return lu, lv, O, xc, T
 
 
+@_on_gpu
 def sinkhorn_solve(C, log_mu, log_nu, eps, lam: float = 1.0, K: int = 7, log_u_init=None,
                    log_v_init=None, threshold: float | None = None, check_every: int = 2, mask=None):
     """Log-domain Sinkhorn on a dense cost (H,N,N) or (B,H,N,N); returns (log_u, log_v)."""
@@ -84,6 +105,7 @@ def sinkhorn_solve(C, log_mu, log_nu, eps, lam: float = 1.0, K: int = 7, log_u_i
     return lu, lv
 
 
+@_on_gpu
 def compute_transport_output(V, G, log_u, log_v, C, eps, x_res=None, mask=None):
     """Gated transport output, T_norm and centroid (sinkhorn.py:115-198).
 

@@ -11,8 +11,8 @@
  *
  * Conventions
  *   - Every pointer is a device pointer unless stated otherwise; every tensor is
- *     dense row-major (C-contiguous) with the shape given beside it.  Q, K, V,
- *     dO, O, dQ, dK and dV must be 16-byte aligned.
+ *     dense row-major (C-contiguous) with the shape given beside it.  With head
+ *     dim 32 or 64, Q, K, V, dO, O, dQ, dK and dV must be 16-byte aligned.
  *   - The caller owns all memory.  No entry point allocates device memory; the
  *     scratch a call needs is passed in as `workspace` (size from
  *     dfs_workspace_size).
@@ -134,10 +134,15 @@ int dfs_abi_version(void);
 /* Text for a status code or an OR of device status bits. */
 const char* dfs_status_string(int status);
 
-/* Largest N accepted for head dim d (0 if d is unsupported).  d = 32 and
- * N <= 384 run on the cluster-resident kernels (the log-kernel stays on chip);
- * larger N and d = 64 run on the streamed kernels, which recompute it tile by
- * tile and need a workspace (dfs_workspace_size). */
+/* Largest N accepted for head dim d (0 if d is unsupported: d > 64).  d <= 32
+ * and N <= 384 run on the cluster-resident kernels (the log-kernel stays on
+ * chip); larger N and 32 < d <= 64 run on the streamed kernels, which
+ * recompute it tile by tile and need a workspace (dfs_workspace_size).  The
+ * kernels are built for head dims 32 and 64; any other d <= 64 (e.g. the
+ * reference tests' d = 8) runs on zero-padded copies of the operands made in
+ * the workspace (padding adds exact zeros to every product; the logit scale
+ * stays 1/sqrt(d)), and the padded columns of O and of the gradients are
+ * dropped. */
 int dfs_max_n(int d);
 
 /* Bytes of device workspace dfs_fwd / dfs_bwd need for problem p. */
@@ -199,16 +204,21 @@ enum {
 
 /* One phase of the streamed path on rows (columns) [row_begin, row_end).
  * Forward phases read `fa` (and ignore `cg`, `ba`), backward phases `cg` and
- * `ba`.  Any N and d the streamed kernels accept (d = 32 or 64).  New for
+ * `ba`.  Any N the streamed kernels accept, head dims 32 and 64 only (the phases
+ * keep no padded copies between calls).  New for
  * multi-GPU row sharding of long sequences; the reference has no sharded path. */
 int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const dfs_fwd_args* fa,
                   const dfs_bwd_args* ba, int row_begin, int row_end, void* workspace,
                   size_t workspace_bytes, void* stream);
 
 /* Size of the library's fixed device scratch used by dfs_fwd_static: 16 MiB.
- * The streamed forward needs 16 + 12 d bytes of workspace per (batch, head,
- * point) plus 256 (dfs_workspace_size), e.g. B*H*N up to ~20,000 points at
- * d = 64. */
+ * dfs_workspace_size's fwd_bytes is the authority on what a problem needs: the
+ * streamed forward takes 64 + 12 d bytes per (batch, head, point) -- potentials
+ * and row statistics, fp32 operand copies, the column-split partials -- plus
+ * 4 bytes per block of 128 rows and under 1 KB fixed, i.e. B*H*N up to about
+ * 20,000 points at d = 64 or 37,000 at d = 32; head dims other than 32 and 64
+ * add their zero-padded copies.  Cluster-resident problems (N <= 384, d = 32)
+ * need none. */
 #define DFS_STATIC_SCRATCH_BYTES (16u << 20)
 
 /* Forward for callers that cannot allocate device memory.  No counterpart in

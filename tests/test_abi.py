@@ -39,7 +39,9 @@ def test_version_and_strings(lib):
     assert nat.status_string(nat.DFS_OK) == "ok"
     assert "workspace" in nat.status_string(nat.DFS_ERR_WORKSPACE)
     assert nat.max_n(32) >= 384
-    assert nat.max_n(48) == 0
+    # head dims up to 64 run (others zero-padded to 32 or 64); beyond 64 nothing
+    assert nat.max_n(8) == nat.max_n(48) == nat.max_n(64) == 1 << 16
+    assert nat.max_n(96) == 0 and nat.max_n(0) == 0
 
 
 def test_struct_sizes_match_header_layout():
@@ -66,8 +68,19 @@ def test_host_side_validation(lib):
     assert fb.value == 4 * 4 * 4096 + 3 * 4 * 4096 * 32 + 4 * 3 * 4 * 4096 + 4 * (4096 // 128) + 2 * 256 + 128 + 8
     huge = nat.make_problem(1, 1, 1 << 17, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
     assert lib.dfs_fwd(huge, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
-    odd_d = nat.make_problem(1, 1, 128, 48, __import__("torch").bfloat16, 20, 1.0, 10.0)
-    assert lib.dfs_fwd(odd_d, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
+    wide_d = nat.make_problem(1, 1, 128, 96, __import__("torch").bfloat16, 20, 1.0, 10.0)
+    assert lib.dfs_fwd(wide_d, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
+    # a padded head dim needs its zero-padded copies even on the resident path:
+    # Q, K, V (bf16) and O (fp32) at d = 32, each region rounded up to 256 bytes
+    odd_d = nat.make_problem(2, 4, 16, 8, __import__("torch").bfloat16, 3, 1.0, 10.0)
+    assert lib.dfs_fwd(odd_d, fake, None, 0, None) == nat.DFS_ERR_WORKSPACE
+    assert lib.dfs_workspace_size(odd_d, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
+    nd = 2 * 4 * 16 * 32
+    assert fb.value == 3 * 2 * nd + 4 * nd  # already multiples of 256
+    assert bb.value == 3 * 2 * nd + 4 * 4 * nd
+    # the phase API keeps no padded copies between calls
+    assert lib.dfs_stream_op(nat.DFS_OP_FWD_INIT, odd_d, None, fake, None, 0, 16, None, 0, None) == \
+        nat.DFS_ERR_UNSUPPORTED
     bad = nat.make_problem(1, 1, 64, 32, __import__("torch").bfloat16, 20, -1.0, 10.0)
     assert lib.dfs_fwd(bad, fake, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
     cg = nat.DfsCgParams(rtol=1e-6, atol=1e-6, max_iter=-1)

@@ -84,7 +84,7 @@ def test_static_scratch_forward_matches_dfs_fwd_on_two_calls():
 
 
 def test_static_scratch_rejects_problems_beyond_its_size():
-    big = nat.make_problem(8, 16, 16384, 64, torch.bfloat16, 10, 1.0, 10.0)  # needs 32 MiB
+    big = nat.make_problem(8, 16, 16384, 64, torch.bfloat16, 10, 1.0, 10.0)  # needs about 1.7 GB
     fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
     L = nat.lib()
     assert L.dfs_workspace_size(big, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
