@@ -1,25 +1,30 @@
 #!/usr/bin/env python
 """Benchmark of the B200 flash-Sinkhorn path (one JSON line on rank 0).
 
-A step is one forward + IFT backward of flash-Sinkhorn attention on BASELINE
-configuration 2: B=2, H=8, N=384, d=32, bf16 Q/K/V ~ N(0,1), eps=1, 20
-iterations, uniform marginals, upstream dO ~ N(0,1), CG tol 1e-6 / max 50 /
-zero start.  On N GPUs every rank runs its own (batch, head) shard of that size
-(weak scaling, no data-path collective); the reported value is whole-job
-calls/s.
+On one GPU a step is one forward + IFT backward of flash-Sinkhorn attention at
+B=2, H=8, N=384, d=32 (the configuration the headline metric is quoted on):
+bf16 Q/K/V ~ N(0,1), eps=1, 20 iterations, uniform marginals, upstream
+dO ~ N(0,1), CG tol 1e-6 / max 50 / zero start.  The line also carries a
+single-GPU measurement of the long-sequence workload below (``config4_1gpu``),
+the N = 1 point of its strong-scaling curve.
+
+On N > 1 GPUs (torchrun, one rank per GPU) the default workload is the
+long-sequence row-sharded one: B=1 H=16 N=8192 d=64, 30 iterations, CG tol
+1e-5 / max 40, every problem's rows split over the ranks, potentials exchanged
+through NVLink peer stores each half-iteration (strong scaling: one call is the
+whole configuration's forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4]
 
-``--config 3`` (B=8 H=16 padded N=1024 d=64, variable lengths, eps 0.5, 50
-iterations, kappa < 1) spreads the (batch, head) problems over the ranks with a
-length^2-balanced partition; ``--config 4`` (B=1 H=16 N=8192 d=64, 30
-iterations, CG tol 1e-5 / max 40) splits every problem's rows over the ranks
-with NCCL all-gathers of the potentials each half-iteration.  Both are strong
-scaling: one call is the whole configuration's forward + backward.
+``--config 3`` (B=8 H=16 padded N=1024 d=64, variable lengths, softmax
+marginals, eps 0.5, 50 iterations) spreads the (batch, head) problems over the
+ranks with a length^2-balanced partition (no data-path collective).
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-oracle restatement in ``oracle/``, float32, all host threads) on the same
-workload and prints the same metric.
+``--impl reference`` times the reference's own CPU path -- dense cost,
+sinkhorn_solve, compute_transport_output and torch autograd, restated in
+``oracle/sinkhorn_torch.py`` because the reference source does not travel with
+this repository -- in float32 on all host threads, on the same workload, and
+prints the same metric.
 """
 
 from __future__ import annotations
@@ -140,11 +145,22 @@ def profile_traffic():
     return None
 
 
-class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+def gpu_bus_id(dev) -> str:
+    """PCI bus id of a torch device, in nvidia-smi's form: nvidia-smi counts GPUs by
+    physical index and ignores CUDA_VISIBLE_DEVICES, so the torch index can name
+    another GPU; the bus id cannot."""
+    p = torch.cuda.get_device_properties(dev)
+    return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
 
-    def __init__(self, index):
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region, of the GPU
+    this process runs on (selected by PCI bus id)."""
+
+    def __init__(self, dev):
+        index = dev.index
         self.index = index
+        self.bus_id = gpu_bus_id(dev)
         self.proc = None
         # the raw samples go where DFS_CLOCK_LOG_DIR points (kept for inspection), else to a temp file
         log_dir = os.environ.get("DFS_CLOCK_LOG_DIR")
@@ -158,7 +174,7 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "200"], stdout=self.fh,
+                                          "-i", self.bus_id, "-lms", "200"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -190,7 +206,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "gpu_pci_bus_id": self.bus_id}
 
 
 def dist_setup(n_gpus):
@@ -285,7 +301,7 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     # ---- timed region: value (inputs resident in HBM, L2 flushed between steps)
-    sampler = ClockSampler(dev.index) if rank == 0 else None
+    sampler = ClockSampler(dev) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
@@ -379,8 +395,10 @@ def run_ours(args):
             "device_status": status,
             "clocks": clocks,
         }
+        if world == 1 and not args.no_config4:
+            line["config4_1gpu"] = config4_single_gpu(dev)
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(2, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
@@ -389,10 +407,54 @@ def run_ours(args):
 
 # ---------------------------------------------------------------- configs 3 and 4
 BIG = {
-    3: dict(B=8, H=16, N=1024, d=64, eps=0.5, K_iter=50, lam=1.0, cg_rtol=1e-6, cg_max_iter=50, varlen=True),
+    3: dict(B=8, H=16, N=1024, d=64, eps=0.5, K_iter=50, lam=float("inf"), cg_rtol=1e-6, cg_max_iter=50,
+            varlen=True),
     4: dict(B=1, H=16, N=8192, d=64, eps=1.0, K_iter=30, lam=float("inf"), cg_rtol=1e-5, cg_max_iter=40,
             varlen=False),
 }
+
+
+def config4_single_gpu(dev, steps=5, warmup=3):
+    """The long-sequence workload (B=1 H=16 N=8192 d=64, fwd + bwd) on this one GPU
+    through the public op: the N = 1 point of the row-sharded strong-scaling runs
+    (bench.py --gpus N > 1).  Inputs resident, CUDA events around `steps` calls."""
+    from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn, last_cg_report
+    c = BIG[4]
+    host, _, _, lmu, lnu = big_inputs(c)
+    inp = {k: v.to(dev) for k, v in host.items()}
+    eps = torch.full((c["H"],), c["eps"], device=dev)
+    lmu, lnu = lmu.to(dev), lnu.to(dev)
+    cg = dict(rtol=c["cg_rtol"], atol=0.0, max_iter=c["cg_max_iter"])
+
+    def step():
+        leaves = [inp[k].requires_grad_(True) for k in ("Q", "K", "V")]
+        O, _, _, _ = flash_sinkhorn(*leaves, None, None, None, eps, None, lmu, lnu, K_iter=c["K_iter"], lam=c["lam"],
+                                    cg_opts=cg)
+        torch.autograd.grad(O, leaves, grad_outputs=inp["dO"].float())
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    rep = last_cg_report()
+    return {"workload": big_workload_name(4), "value": round(1e3 / ms, 4), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "steps": steps, "warmup": warmup,
+            "cg_iters_mean": float(rep["cg_iters"].float().mean()) if rep else None}
+
+
+def big_workload_name(cfg_id):
+    c = BIG[cfg_id]
+    return (f"config{cfg_id}: flash-Sinkhorn fwd+IFT-bwd B={c['B']} H={c['H']} N={c['N']} d={c['d']} bf16 "
+            f"eps={c['eps']} K={c['K_iter']} " +
+            ("padded var-len, softmax marginals, balanced" if c["varlen"] else "uniform marginals, balanced") +
+            f", CG tol {c['cg_rtol']} max {c['cg_max_iter']}")
 
 
 def big_inputs(c, seed=0):
@@ -458,7 +520,7 @@ def run_big(args):
     for _ in range(args.warmup):
         step(dev_in)
     torch.cuda.synchronize()
-    sampler = ClockSampler(dev.index) if rank == 0 else None
+    sampler = ClockSampler(dev) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
@@ -518,10 +580,7 @@ def run_big(args):
         f_call = ((4 * c["K_iter"] + 4) + (14 + 2 * n_cg)) * per
         value = args.steps / (ms * 1e-3)
         per_gpu_tf = f_call * value / world / 1e12
-        name = (f"config{args.config}: flash-Sinkhorn fwd+IFT-bwd B={B} H={H} N={N} d={d} bf16 eps={c['eps']} "
-                f"K={c['K_iter']} " + ("padded var-len, softmax marginals, lam=1" if c["varlen"] else
-                                       "uniform marginals, balanced") +
-                f", CG tol {c['cg_rtol']} max {c['cg_max_iter']}")
+        name = big_workload_name(args.config)
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
@@ -543,79 +602,72 @@ def run_big(args):
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_big(args.config, c, lengths, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(args.config, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
-def cpu_baseline_big(cfg_id, c, lengths, seconds=15.0):
-    """Oracle (float32 numpy) on one (batch, head) problem of a smaller length L,
-    scaled by sum over problems of (L_bh / L)^2 to whole-configuration calls/s."""
-    from oracle import sinkhorn_oracle as orc
-    L = 512 if cfg_id == 3 else 1024
-    r = np.random.default_rng(3)
-    Q, K, V = (r.standard_normal((1, 1, L, c["d"])).astype(np.float32) for _ in range(3))
-    dO = r.standard_normal((1, L, c["d"])).astype(np.float32)
-    lm = np.full((1, 1, L), -math.log(L), np.float32)
-    lam = 1e6 if math.isinf(c["lam"]) else c["lam"]
+def _ref_threads() -> int:
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    return n
 
-    def call():
-        with orc.precision(np.float32):
-            orc.flash_sinkhorn_attn(Q, K, V, None, None, None, None, np.full(1, c["eps"], np.float32), None, lm, lm,
-                                    K_iter=c["K_iter"], lam=lam, with_grad=True, dO_flat=dO)
 
-    call()
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < seconds:
-        call()
-        n += 1
-    dt = (time.perf_counter() - t0) / n
+def _ref_problem(B, H, N, d, K_iter, lam, eps, seed, mask=None, lmu=None, lnu=None):
+    """Seeded inputs of one reference-path call (bf16-rounded values in fp32,
+    as the GPU arm sees them)."""
+    g = torch.Generator().manual_seed(seed)
+    Q, K, V, dO = (torch.randn(B, H, N, d, generator=g).to(torch.bfloat16).float() for _ in range(4))
+    lm = torch.full((B, H, N), -math.log(N))
+    return dict(Q=Q, K=K, V=V, dO=dO, eps=torch.full((H,), float(eps)), log_mu=lm if lmu is None else lmu,
+                log_nu=lm if lnu is None else lnu, K_iter=K_iter, lam=1e6 if math.isinf(lam) else lam, mask=mask)
+
+
+def _ref_call(prob):
+    """One forward + autograd backward of the reference's CPU path (dense cost,
+    sinkhorn_solve, compute_transport_output, torch autograd), restated in
+    oracle/sinkhorn_torch.py, float32."""
+    from oracle import sinkhorn_torch as ort
+    ort.attn_fwd_bwd(prob["Q"], prob["K"], prob["V"], prob["eps"], prob["log_mu"], prob["log_nu"], prob["K_iter"],
+                     prob["lam"], prob["dO"], dtype=torch.float32, mask=prob["mask"])
+
+
+def _ref_sample(cfg_id):
+    """(problem, calls of the whole configuration one sample call stands for, text).
+    Config 2 is timed whole.  For configs 3 and 4 (dense N x N autograd state of
+    up to ~20 GB per head) one problem of a smaller length L is timed and the
+    time scaled by sum over the configuration's problems of (L_bh / L)^2."""
+    if cfg_id == 2:
+        c = CFG
+        prob = _ref_problem(c["B"], c["H"], c["N"], c["d"], c["K_iter"], float("inf"), c["eps"], 7)
+        return prob, 1.0, f"whole config-2 calls (B={c['B']} H={c['H']} N={c['N']} d={c['d']})"
+    c = BIG[cfg_id]
+    L = 512 if cfg_id == 3 else 2048
+    prob = _ref_problem(1, 1, L, c["d"], c["K_iter"], c["lam"], c["eps"], 3)
+    _, lengths, _, _, _ = big_inputs(c)
     scale = sum(c["H"] * (Lb / L) ** 2 for Lb in lengths)
-    return {"value": round(1.0 / (dt * scale), 6), "unit": UNIT, "cores": len(os.sched_getaffinity(0)),
-            "kind": "port", "sample": f"{n} oracle calls (fwd + unrolled bwd, float32) on one problem of N={L}, "
-                                      f"d={c['d']}, K={c['K_iter']}, scaled by sum (L_bh/{L})^2 = {scale:.1f}",
-            "cpu": _cpu_model()}
+    return prob, 1.0 / scale, (f"one (batch, head) problem of N={L}, d={c['d']}, K={c['K_iter']}, scaled by "
+                               f"sum over the config's problems of (L_bh/{L})^2 = {scale:.1f}")
 
 
-def _oracle_call(orc, inp):
-    """One fwd + unrolled bwd of the oracle on the config-2 workload."""
-    c = CFG
-    Q, K, V, dO = inp
-    H, N = c["H"], c["N"]
-    lm = np.full((c["B"], H, N), -math.log(N), np.float32)
-    with orc.precision(np.float32):
-        orc.flash_sinkhorn_attn(Q, K, V, None, None, None, None, np.full(H, c["eps"], np.float32), None,
-                                lm, lm, K_iter=c["K_iter"], lam=float("inf"), with_grad=True, dO_flat=dO)
-
-
-def _oracle_inputs():
-    c = CFG
-    r = np.random.default_rng(7)
-    shp = (c["B"], c["H"], c["N"], c["d"])
-    Q, K, V = (r.standard_normal(shp).astype(np.float32) for _ in range(3))
-    dO = r.standard_normal((c["B"], c["N"], c["H"] * c["d"])).astype(np.float32)
-    return Q, K, V, dO
-
-
-def cpu_baseline(seconds=15.0):
-    """Oracle (reference algorithm restated in numpy, float32) timed on a bounded
-    sample: whole config-2 calls repeated until ~`seconds` have elapsed."""
-    from oracle import sinkhorn_oracle as orc
-    inp = _oracle_inputs()
-    _oracle_call(orc, inp)  # warm-up
+def cpu_baseline(cfg_id=2, seconds=15.0):
+    """The reference's CPU path timed on a bounded sample (~`seconds` of work)."""
+    cores = _ref_threads()
+    prob, per_call, what = _ref_sample(cfg_id)
+    _ref_call(prob)  # warm-up
     t0 = time.perf_counter()
     n = 0
     while True:
-        _oracle_call(orc, inp)
+        _ref_call(prob)
         n += 1
         if time.perf_counter() - t0 > seconds:
             break
-    dt = time.perf_counter() - t0
-    return {"value": round(n / dt, 4), "unit": UNIT, "cores": len(os.sched_getaffinity(0)), "kind": "port",
-            "sample": f"{n} full config-2 calls (fwd + unrolled bwd, float32 numpy) in {dt:.1f} s",
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(per_call / dt, 6), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} calls of the reference's torch CPU path (dense cost + sinkhorn_solve + "
+                      f"compute_transport_output + autograd, float32, restated in oracle/sinkhorn_torch.py): {what}",
             "cpu": _cpu_model()}
 
 
@@ -635,27 +687,33 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    from oracle import sinkhorn_oracle as orc
-    inp = _oracle_inputs()
+    cores = _ref_threads()
+    prob, per_call, what = _ref_sample(args.config)
     for _ in range(args.warmup):
-        _oracle_call(orc, inp)
+        _ref_call(prob)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        _oracle_call(orc, inp)
-    dt = time.perf_counter() - t0
-    value = args.steps / dt
-    cores = len(os.sched_getaffinity(0))
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,1); BASELINE config 2 shapes)",
-            "config": {"workload": workload_name(), "global_batch": CFG["B"], "heads": CFG["H"],
-                       "seq_len": CFG["N"], "head_dim": CFG["d"], "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{args.steps} full config-2 calls (fwd + unrolled bwd), oracle "
-                                       "restatement of the reference algorithm, float32 numpy",
+        _ref_call(prob)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = per_call / dt
+    if args.config == 2:
+        c = CFG
+        workload, shape = workload_name(), dict(global_batch=c["B"], heads=c["H"], seq_len=c["N"], head_dim=c["d"])
+    else:
+        c = BIG[args.config]
+        workload, shape = big_workload_name(args.config), dict(global_batch=c["B"], heads=c["H"], seq_len=c["N"],
+                                                               head_dim=c["d"])
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / value, 3),
+            "higher_is_better": True, "scaling": "weak" if args.config == 2 else "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded values in float32)",
+            "config": dict(workload=workload, parallelism="cpu", **shape),
+            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} calls of the reference's torch CPU path (dense cost + "
+                                       "sinkhorn_solve + compute_transport_output + autograd, float32, restated "
+                                       f"in oracle/sinkhorn_torch.py): {what}",
                              "cpu": _cpu_model()},
-            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -667,8 +725,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2)
+    ap.add_argument("--no-config4", action="store_true", help="skip the single-GPU long-sequence point")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=None,
+                    help="default: 2 on one GPU, 4 (long-sequence row shards) on several")
     args = ap.parse_args()
+    if args.config is None:
+        args.config = 4 if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus > 1 else 2
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

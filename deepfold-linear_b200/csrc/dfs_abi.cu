@@ -24,29 +24,69 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // cluster-resident kernels (S kept on chip): d <= 32, N <= 384; streamed
 // kernels (S recomputed tile by tile): d <= 64, N <= kStreamMaxN.  The kernels
-// are instantiated for head dims 32 and 64; other head dims run zero-padded to
-// the next one (dfs_pad.cu), on copies at the front of the workspace.
+// are instantiated for head dims 32 and 64.  Operands are transformed on copies
+// at the front of the workspace (dfs_pad.cu) when
+//   XF_PAD      the head dim is another one: zero-padded to the next one;
+//   XF_SPLIT_QK fp32 Q, K, V with 3 d <= 64: bf16 hi / lo parts along the
+//               contraction dimension (exact products instead of tf32 ones);
+//   XF_SPLIT_V  fp32 V of the dense-cost path with 2 d <= 32: V = [Vhi Vlo].
 constexpr int kResidentMaxN = 384;
 constexpr int kStreamMaxN = 1 << 16;
-int kdim(const dfs_problem* p) { return kernel_head_dim(p->d); }
-bool padded(const dfs_problem* p) { return kdim(p) != p->d; }
+enum { XF_NONE = 0, XF_PAD = 1, XF_SPLIT_QK = 2, XF_SPLIT_V = 3 };
+int xform(const dfs_problem* p) {
+  if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_QK && 3 * p->d <= 64) return XF_SPLIT_QK;
+  if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_DENSE && 2 * p->d <= 32) return XF_SPLIT_V;
+  return kernel_head_dim(p->d) != p->d ? XF_PAD : XF_NONE;
+}
+int kdim(const dfs_problem* p) {
+  const int x = xform(p);
+  return kernel_head_dim(x == XF_SPLIT_QK ? 3 * p->d : x == XF_SPLIT_V ? 2 * p->d : p->d);
+}
+bool padded(const dfs_problem* p) { return xform(p) != XF_NONE; }
 bool resident(const dfs_problem* p) { return kdim(p) == 32 && p->N <= kResidentMaxN; }
 bool streamed(const dfs_problem* p) { return kdim(p) != 0 && p->N <= kStreamMaxN; }
 
 size_t elem_bytes(int dtype) { return dtype == DFS_F32 ? 4 : 2; }
 size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 size_t padded_elems(const dfs_problem* p) { return static_cast<size_t>(p->B) * p->H * p->N * kdim(p); }
-// zero-padded copies at the front of the workspace: Q, K, V (input type), then
+// element type of the kernels' Q, K, V: bf16 parts when split
+int kernel_dtype(const dfs_problem* p) {
+  const int x = xform(p);
+  return (x == XF_SPLIT_QK || x == XF_SPLIT_V) ? DFS_BF16 : p->in_dtype;
+}
+// transformed copies at the front of the workspace: Q, K, V (kernel type), then
 // O (forward) or dO, dQ, dK, dV (backward), fp32; each region 256-byte aligned
 size_t pad_fwd_bytes(const dfs_problem* p) {
   if (!padded(p)) return 0;
   const size_t nd = padded_elems(p);
-  return 3 * round256(nd * elem_bytes(p->in_dtype)) + round256(nd * 4);
+  return 3 * round256(nd * elem_bytes(kernel_dtype(p))) + round256(nd * 4);
 }
 size_t pad_bwd_bytes(const dfs_problem* p) {
   if (!padded(p)) return 0;
   const size_t nd = padded_elems(p);
-  return 3 * round256(nd * elem_bytes(p->in_dtype)) + 4 * round256(nd * 4);
+  return 3 * round256(nd * elem_bytes(kernel_dtype(p))) + 4 * round256(nd * 4);
+}
+
+// Transformed copy of one operand (Q: which = 0, K: 1, V: 2) into dst.
+cudaError_t transform_operand(const dfs_problem* p, int which, const void* src, void* dst, size_t rows,
+                              cudaStream_t st) {
+  const int x = xform(p), dk = kdim(p);
+  if (x == XF_SPLIT_QK) {
+    static const int parts[3][3] = {{1, 1, 2}, {1, 2, 1}, {1, 2, 0}};  // Q' = [hi hi lo], K' = [hi lo hi], V' = [hi lo 0]
+    return split_rows(static_cast<const float*>(src), dst, rows, p->d, dk, parts[which][0], parts[which][1],
+                      parts[which][2], st);
+  }
+  if (x == XF_SPLIT_V) return split_rows(static_cast<const float*>(src), dst, rows, p->d, dk, 1, 2, 0, st);
+  return pad_rows(src, dst, static_cast<int>(elem_bytes(p->in_dtype)), rows, p->d, dk, st);
+}
+// Output column blocks summed back into (rows, d): O and dQ take blocks 0 and 1
+// of a split problem, dK blocks 0 and 2, dV block 0; padded problems block 0.
+int fold_blocks(const dfs_problem* p, char what) {
+  const int x = xform(p);
+  if (x == XF_NONE || x == XF_PAD) return 1;
+  if (what == 'O' || what == 'Q') return 3;
+  if (what == 'K') return 5;
+  return 1;
 }
 
 FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
@@ -187,17 +227,18 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   float* Op = nullptr;
   if (pad > 0) {
     const int dk = kdim(p);
-    const size_t es = elem_bytes(p->in_dtype), opb = round256(padded_elems(p) * es);
+    const size_t opb = round256(padded_elems(p) * elem_bytes(kernel_dtype(p)));
     char* Qp = ws;
     char* Kp = ws + opb;
     char* Vp = ws + 2 * opb;
     Op = reinterpret_cast<float*>(ws + 3 * opb);
     cudaError_t e = cudaSuccess;
-    if (a->Q) e = pad_rows(a->Q, Qp, static_cast<int>(es), rows, p->d, dk, st);
-    if (e == cudaSuccess && a->K) e = pad_rows(a->K, Kp, static_cast<int>(es), rows, p->d, dk, st);
-    if (e == cudaSuccess && a->V) e = pad_rows(a->V, Vp, static_cast<int>(es), rows, p->d, dk, st);
+    if (a->Q) e = transform_operand(p, 0, a->Q, Qp, rows, st);
+    if (e == cudaSuccess && a->K) e = transform_operand(p, 1, a->K, Kp, rows, st);
+    if (e == cudaSuccess && a->V) e = transform_operand(p, 2, a->V, Vp, rows, st);
     if (e != cudaSuccess) return DFS_ERR_CUDA;
     q.d = dk;
+    q.in_dtype = kernel_dtype(p);
     q.Q = a->Q ? Qp : nullptr;
     q.K = a->K ? Kp : nullptr;
     q.V = a->V ? Vp : nullptr;
@@ -205,7 +246,7 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   }
   const cudaError_t e = resident(p) ? launch_resident_fwd(q, st) : launch_stream_fwd(q, static_cast<float*>(kws), st);
   if (e != cudaSuccess) return DFS_ERR_CUDA;
-  if (pad > 0 && a->O) return cuda_status(unpad_rows(Op, a->O, rows, p->d, kdim(p), st));
+  if (pad > 0 && a->O) return cuda_status(fold_rows(Op, a->O, rows, p->d, kdim(p), fold_blocks(p, 'O'), st));
   return DFS_OK;
 }
 
@@ -230,19 +271,21 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   float* grads[3] = {nullptr, nullptr, nullptr};  // padded dQ, dK, dV
   if (pad > 0) {
     const int dk = kdim(p);
-    const size_t es = elem_bytes(p->in_dtype), opb = round256(padded_elems(p) * es);
+    const size_t opb = round256(padded_elems(p) * elem_bytes(kernel_dtype(p)));
     const size_t fb = round256(padded_elems(p) * 4);
     char* Qp = ws;
     char* Kp = ws + opb;
     char* Vp = ws + 2 * opb;
     float* dOp = reinterpret_cast<float*>(ws + 3 * opb);
     for (int k = 0; k < 3; ++k) grads[k] = reinterpret_cast<float*>(ws + 3 * opb + (k + 1) * fb);
-    cudaError_t e = pad_rows(a->Q, Qp, static_cast<int>(es), rows, p->d, dk, st);
-    if (e == cudaSuccess) e = pad_rows(a->K, Kp, static_cast<int>(es), rows, p->d, dk, st);
-    if (e == cudaSuccess) e = pad_rows(a->V, Vp, static_cast<int>(es), rows, p->d, dk, st);
-    if (e == cudaSuccess) e = pad_rows(a->dO, dOp, 4, rows, p->d, dk, st);
+    cudaError_t e = transform_operand(p, 0, a->Q, Qp, rows, st);
+    if (e == cudaSuccess) e = transform_operand(p, 1, a->K, Kp, rows, st);
+    if (e == cudaSuccess) e = transform_operand(p, 2, a->V, Vp, rows, st);
+    // dO' = [dO dO 0] against V' = [Vhi Vlo 0] (split), or dO zero-padded
+    if (e == cudaSuccess) e = dup_rows(a->dO, dOp, rows, p->d, dk, xform(p) == XF_SPLIT_QK ? 2 : 1, st);
     if (e != cudaSuccess) return DFS_ERR_CUDA;
     q.d = dk;
+    q.in_dtype = kernel_dtype(p);
     q.Q = Qp;
     q.K = Kp;
     q.V = Vp;
@@ -255,8 +298,10 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   if (e != cudaSuccess) return DFS_ERR_CUDA;
   if (pad > 0) {
     float* outs[3] = {a->dQ, a->dK, a->dV};
+    const char what[3] = {'Q', 'K', 'V'};
     for (int k = 0; k < 3; ++k)
-      if (outs[k] && unpad_rows(grads[k], outs[k], rows, p->d, kdim(p), st) != cudaSuccess) return DFS_ERR_CUDA;
+      if (outs[k] && fold_rows(grads[k], outs[k], rows, p->d, kdim(p), fold_blocks(p, what[k]), st) != cudaSuccess)
+        return DFS_ERR_CUDA;
   }
   return DFS_OK;
 }

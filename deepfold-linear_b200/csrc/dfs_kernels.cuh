@@ -194,11 +194,17 @@ cudaError_t bt_convert(const void* src, int dtype, float* row_out, float* t_out,
                        cudaStream_t st);
 cudaError_t launch_bt_pass(int mode, const BtArgs& a, cudaStream_t st);
 
-// Head dims other than 32 / 64 (dfs_pad.cu): the instantiated head dim a
-// problem with head dim d runs on (0 when d > 64), and the zero-padding copies.
+// Operand transforms (dfs_pad.cu): the instantiated head dim a problem of head
+// dim d runs on (0 when d > 64); zero padding of (rows, d) to (rows, dk);
+// the bf16 hi / lo split of fp32 operands into column blocks (part 0 zero,
+// 1 hi, 2 lo); side-by-side copies of fp32 rows; the sum of selected column
+// blocks of width d (bit b of `blocks`: block b) back into (rows, d).
 int kernel_head_dim(int d);
 cudaError_t pad_rows(const void* src, void* dst, int esize, size_t rows, int d, int dk, cudaStream_t st);
-cudaError_t unpad_rows(const float* src, float* dst, size_t rows, int d, int dk, cudaStream_t st);
+cudaError_t split_rows(const float* src, void* dst, size_t rows, int d, int dk, int p0, int p1, int p2,
+                       cudaStream_t st);
+cudaError_t dup_rows(const float* src, float* dst, size_t rows, int d, int dk, int copies, cudaStream_t st);
+cudaError_t fold_rows(const float* src, float* dst, size_t rows, int d, int dk, int blocks, cudaStream_t st);
 
 cudaError_t launch_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K,
                                 cudaStream_t st);

@@ -10,17 +10,17 @@
 //
 // Errors the kernels find on the device (a bounded wait that gave up,
 // non-finite potentials, a CG solve that hit its iteration cap) are OR-ed into
-// a device status word per call.  Reading it at once would synchronise every
-// call, so each call copies its word to pinned host memory on its stream and
-// records an event; the next call (or check_status) reads every word whose
-// event has completed and raises RuntimeError for an error bit, or warns for
-// DFS_WARN_CG_NOT_CONVERGED.  check_status(true) waits for all of them.
+// a sticky status word per device.  Reading it at once would synchronise every
+// call; instead the word is read back asynchronously and checked at the start
+// of the next call, which raises for an error bit; warning bits
+// (DFS_WARN_CG_NOT_CONVERGED) and a synchronous read go to Python through
+// take_status (see DeviceStatus below).
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAEvent.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
-#include <deque>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -53,62 +53,102 @@ T* ptr_or_null(const Tensor& t) {
   return t.defined() ? static_cast<T*>(t.data_ptr()) : nullptr;
 }
 
-// Most recent backward's per-problem CG report (device tensors).
+// Most recent backward's per-problem CG report (device tensors).  Held in a
+// heap object that is never destroyed: tensors and CUDA events must not be
+// torn down by static destructors after the CUDA runtime has shut down.
 std::vector<Tensor>& last_report() {
-  static std::vector<Tensor> r;
-  return r;
+  static auto* r = new std::vector<Tensor>();
+  return *r;
 }
 
 // ---------------------------------------------------------------- device status
-struct PendingStatus {
-  Tensor host;                 // pinned int32 copy of the call's device status word
-  at::cuda::CUDAEvent done;    // recorded after the copy
-  const char* what;
+// One sticky int32 status word per device: every forward and backward call
+// hands it to the library, whose kernels OR their error bits into it.  After a
+// call, if no read-back is in flight, the word is copied to pinned host memory
+// on the call's stream and an event recorded; the next call (or check_status)
+// reads the copy once its event has completed, and on a nonzero value clears
+// the word and raises (errors) or warns (DFS_WARN_CG_NOT_CONVERGED).  So a
+// call costs at most one 4-byte copy and no synchronisation.  All of it lives
+// in never-destroyed heap objects (see last_report).
+constexpr int kMaxDevices = 64;
+struct DeviceStatus {
+  Tensor word;            // (1,) int32 on the device, sticky
+  int32_t* mirror = nullptr;  // pinned host copy
+  cudaEvent_t copied = nullptr;
+  bool in_flight = false;
 };
 std::mutex g_status_mu;
-std::deque<PendingStatus>& pending_status() {
-  static std::deque<PendingStatus> q;
-  return q;
-}
+DeviceStatus* g_status[kMaxDevices] = {};
 
-// Queue the status word of a call launched on `stream` for checking.
-void enqueue_status(const Tensor& status, const char* what, const at::cuda::CUDAStream& stream) {
-  Tensor host = at::empty({1}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
-  host.copy_(status, /*non_blocking=*/true);  // on the current stream, which is `stream`
-  PendingStatus ps{host, at::cuda::CUDAEvent(cudaEventDisableTiming), what};
-  ps.done.record(stream);
-  std::lock_guard<std::mutex> lock(g_status_mu);
-  pending_status().push_back(std::move(ps));
-}
-
-// Read the status words of finished calls (all of them with wait = true, in
-// call order); raise for device errors, warn for an unconverged CG solve.
-void check_status(bool wait) {
-  std::string err;
-  {
-    std::lock_guard<std::mutex> lock(g_status_mu);
-    auto& q = pending_status();
-    while (!q.empty()) {
-      PendingStatus& ps = q.front();
-      if (wait)
-        ps.done.synchronize();
-      else if (!ps.done.query())
-        break;
-      const int v = ps.host.data_ptr<int32_t>()[0];
-      const char* what = ps.what;
-      q.pop_front();
-      if (v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)) {
-        if (err.empty())
-          err = std::string("a previous ") + what + " call reported a device error: " +
-                dfs_status_string(v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)) + " (status " +
-                std::to_string(v) + ")";
-      } else if (v & DFS_WARN_CG_NOT_CONVERGED) {
-        TORCH_WARN("a previous ", what, " call: ", dfs_status_string(DFS_WARN_CG_NOT_CONVERGED),
-                   " for some problem; its gradient is the last CG iterate");
-      }
-    }
+DeviceStatus& device_status(const at::Device& dev) {
+  const int i = dev.index();
+  TORCH_CHECK(i >= 0 && i < kMaxDevices, "device index out of range");
+  if (g_status[i] == nullptr) {
+    auto* ds = new DeviceStatus();
+    ds->word = at::zeros({1}, at::TensorOptions().device(dev).dtype(at::kInt));
+    TORCH_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&ds->mirror), sizeof(int32_t), cudaHostAllocDefault) ==
+                    cudaSuccess, "cudaHostAlloc failed");
+    *ds->mirror = 0;
+    TORCH_CHECK(cudaEventCreateWithFlags(&ds->copied, cudaEventDisableTiming) == cudaSuccess,
+                "cudaEventCreate failed");
+    g_status[i] = ds;
   }
-  TORCH_CHECK(err.empty(), err);
+  return *g_status[i];
+}
+
+// After a call on `stream` (the current device's): start a read-back of the
+// word unless one is in flight.  Caller holds g_status_mu.
+void start_readback(DeviceStatus& ds, cudaStream_t stream) {
+  if (ds.in_flight) return;
+  if (cudaMemcpyAsync(ds.mirror, ds.word.data_ptr<int32_t>(), sizeof(int32_t), cudaMemcpyDeviceToHost, stream) !=
+          cudaSuccess ||
+      cudaEventRecord(ds.copied, stream) != cudaSuccess)
+    return;
+  ds.in_flight = true;
+}
+
+// Read the status word of a device (wait: its value once the current stream
+// has drained; otherwise the last completed read-back, or 0).  A nonzero value
+// clears the word.  Returns the bits.
+int poll_device_status(const at::Device& dev, bool wait) {
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  DeviceStatus& ds = device_status(dev);
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev.index()).stream();
+  if (wait) {
+    if (!ds.in_flight) start_readback(ds, stream);
+    if (!ds.in_flight) return 0;
+    cudaEventSynchronize(ds.copied);
+  } else if (!ds.in_flight || cudaEventQuery(ds.copied) != cudaSuccess) {
+    return 0;
+  }
+  ds.in_flight = false;
+  const int v = *ds.mirror;
+  if (v != 0) {
+    *ds.mirror = 0;
+    cudaMemsetAsync(ds.word.data_ptr<int32_t>(), 0, sizeof(int32_t), stream);
+  }
+  return v;
+}
+
+// Warning bits seen by the checks inside calls, handed to Python by
+// take_status (Python turns them into warnings).
+std::atomic<int> g_seen_warn{0};
+
+// The check at the start of every forward and backward: raise for device
+// errors of earlier calls; keep warning bits for take_status.
+void check_device_status(const at::Device& dev) {
+  const int v = poll_device_status(dev, false);
+  g_seen_warn.fetch_or(v & DFS_WARN_CG_NOT_CONVERGED);
+  TORCH_CHECK(!(v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)),
+              "a previous flash_sinkhorn call reported a device error: ",
+              dfs_status_string(v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)), " (status ", v, ")");
+}
+
+// For Python: the status bits of the current device (see poll_device_status)
+// together with the warning bits kept by earlier checks.
+int take_status(bool wait) {
+  const int v = poll_device_status(at::Device(at::kCUDA, c10::cuda::current_device()), wait);
+  return v | g_seen_warn.exchange(0);
 }
 
 struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
@@ -130,7 +170,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
                 "Q, K, V must share the shape (B, H, N, d)");
     TORCH_CHECK(K.device() == Q.device() && V.device() == Q.device(), "Q, K, V must be on one device");
     const c10::cuda::CUDAGuard guard(Q.device());  // launches, attributes and streams of Q's device
-    check_status(false);
+    check_device_status(Q.device());
     const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
     TORCH_CHECK(N <= dfs_max_n(static_cast<int>(d)), "N=", N, ", d=", d,
                 " is outside the kernels' range (head dim <= 64, N <= ", dfs_max_n(static_cast<int>(d)), ")");
@@ -147,7 +187,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor O = at::empty({B, H, N, d}, fo);
     Tensor xc = xr.defined() ? at::empty({B, H, N, 3}, fo) : Tensor();
     Tensor lu = at::empty({B, H, N}, fo), lv = at::empty({B, H, N}, fo);
-    Tensor status = at::zeros({1}, Q.options().dtype(at::kInt));
+    Tensor status = device_status(Q.device()).word;
 
     dfs_problem prob{};
     prob.B = static_cast<int32_t>(B);
@@ -184,7 +224,10 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor ws = fwd_ws ? at::empty({static_cast<int64_t>((fwd_ws + 3) / 4)}, fo) : Tensor();
     const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(Q.device().index());
     check_rc(dfs_fwd(&prob, &a, ws.defined() ? ws.data_ptr() : nullptr, fwd_ws, cstream.stream()), "dfs_fwd");
-    enqueue_status(status, "flash_sinkhorn forward", cstream);
+    {
+      std::lock_guard<std::mutex> lock(g_status_mu);
+      start_readback(device_status(Q.device()), cstream.stream());
+    }
 
     ctx->save_for_backward({Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv});
     ctx->saved_data["K_iter"] = K_iter;
@@ -213,7 +256,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
   static variable_list backward(AutogradContext* ctx, variable_list grads) {
     const auto saved = ctx->get_saved_variables();
     const c10::cuda::CUDAGuard guard(saved[0].device());
-    check_status(false);
+    check_device_status(saved[0].device());
     const Tensor &Qc = saved[0], &Kc = saved[1], &Vc = saved[2], &xr = saved[3], &pw = saved[4],
                  &pb = saved[5], &epsc = saved[6], &wd = saved[7], &lmu = saved[8], &lnu = saved[9],
                  &mk = saved[10], &lu = saved[11], &lv = saved[12];
@@ -236,7 +279,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor dnu = needs("e_nu") ? at::empty({B, H, N}, fo) : Tensor();
     Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
     Tensor resid = at::empty({B * H}, fo);
-    Tensor status = at::zeros({1}, Qc.options().dtype(at::kInt));
+    Tensor status = device_status(Qc.device()).word;
 
     dfs_problem prob{};
     prob.B = static_cast<int32_t>(B);
@@ -282,7 +325,10 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor ws = bwd_ws ? at::empty({static_cast<int64_t>((bwd_ws + 3) / 4)}, fo) : Tensor();
     const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(Qc.device().index());
     check_rc(dfs_bwd(&prob, &cg, &a, ws.defined() ? ws.data_ptr() : nullptr, bwd_ws, cstream.stream()), "dfs_bwd");
-    enqueue_status(status, "flash_sinkhorn backward", cstream);
+    {
+      std::lock_guard<std::mutex> lock(g_status_mu);
+      start_readback(device_status(Qc.device()), cstream.stream());
+    }
     last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
 
     // gradients in the dtype of the forward's inputs
@@ -313,13 +359,12 @@ std::vector<Tensor> flash_sinkhorn_autograd(Tensor Q, Tensor K, Tensor V, c10::o
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "native autograd glue for libdfsink (flash Sinkhorn forward / IFT backward)";
-  // torch::wrap_pybind_function: TORCH_WARN becomes a Python warning, errors the
-  // matching Python exceptions
-  m.def("flash_sinkhorn", torch::wrap_pybind_function(flash_sinkhorn_autograd),
+  m.def("flash_sinkhorn", &flash_sinkhorn_autograd,
         "FlashSinkhornFn.apply: returns [O, x_centroid, log_u, log_v], or [O, log_u, log_v] without x_res");
   m.def("last_report", []() { return last_report(); },
-        "[cg_iters, cg_residual, status, fwd_status] of the most recent backward");
-  m.def("check_status", torch::wrap_pybind_function(check_status), py::arg("wait") = true,
-        "read the device status of finished calls (all calls with wait=True); raise RuntimeError for a "
-        "device error, warn for an unconverged CG solve");
+        "[cg_iters, cg_residual, status, fwd_status] of the most recent backward (status: the device's sticky "
+        "status word, the OR of every call's bits since the last check)");
+  m.def("take_status", &take_status, py::arg("wait") = true,
+        "status bits of the current device's calls since the last read (after the stream drains with "
+        "wait=True), plus warning bits seen by the checks inside calls; the bits are cleared");
 }

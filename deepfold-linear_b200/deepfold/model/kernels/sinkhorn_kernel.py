@@ -28,6 +28,7 @@ Differences from the reference, all deliberate:
 from __future__ import annotations
 
 import math
+import warnings
 
 import torch
 
@@ -47,11 +48,24 @@ def last_cg_report() -> dict:
     return dict(zip(("cg_iters", "cg_residual", "status", "fwd_status"), rep))
 
 
+def _raise_or_warn(bits: int) -> None:
+    errs = bits & (nat.DFS_ERR_DEVICE_TIMEOUT | nat.DFS_ERR_NUMERIC)
+    if bits & nat.DFS_WARN_CG_NOT_CONVERGED:
+        warnings.warn("a previous flash_sinkhorn backward: CG reached max_iter for some problem; its gradient "
+                      "is the last CG iterate", RuntimeWarning, stacklevel=3)
+    if errs:
+        raise RuntimeError(f"a previous flash_sinkhorn call reported a device error: {nat.status_string(errs)} "
+                           f"(status {bits})")
+
+
 def check_status(wait: bool = True) -> None:
-    """Read the device status of the finished forward / backward calls (all of
-    them, after waiting, with ``wait``): RuntimeError for a device error, a
-    warning for a CG solve that reached its iteration cap."""
-    nat.ext().check_status(bool(wait))
+    """Read the device status of the forward / backward calls made so far on the
+    current device (all of them, once the current stream has drained, with
+    ``wait``; otherwise those whose status has already been read back):
+    RuntimeError for a device error, a RuntimeWarning for a CG solve that
+    reached its iteration cap.  Calls raise for earlier device errors by
+    themselves; this makes the check immediate."""
+    _raise_or_warn(int(nat.ext().take_status(bool(wait))))
 
 
 def _to_cuda(args: dict) -> dict:
@@ -106,10 +120,12 @@ def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_
         raise ValueError("lam must be positive (inf for the balanced problem)")
     # native autograd function FlashSinkhornFn (csrc/dfs_torch.cpp): validates,
     # allocates and calls dfs_fwd / dfs_bwd of libdfsink on the current stream
-    out = nat.ext().flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu,
+    ext = nat.ext()
+    out = ext.flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu,
                                    log_nu, log_u_init, log_v_init, mask, int(K_iter), float(lam),
                                    float(r_0), float(cg["rtol"]), float(cg["atol"]), int(cg["max_iter"]))
     out = tuple(out) if len(out) == 4 else (out[0], None, out[1], out[2])
+    _raise_or_warn(int(ext.take_status(False)))  # warnings found by the call's own check
     if unbatched:
         return tuple(None if t is None else t.squeeze(0) for t in out)
     return out

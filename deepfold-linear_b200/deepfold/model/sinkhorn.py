@@ -82,7 +82,9 @@ def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshol
         log_u_init=nat.ptr(lui), log_v_init=nat.ptr(lvi), mask=nat.ptr(mk), O=nat.ptr(O),
         x_centroid=nat.ptr(xc), log_u=nat.ptr(lu), log_v=nat.ptr(lv), status=nat.ptr(status),
         T_norm=nat.ptr(T))
-    nat.check(nat.lib().dfs_fwd(prob, args, None, 0, nat.stream_ptr(dev)), "dfs_fwd")
+    fwd_bytes, _ = nat.workspace_bytes(prob)  # copies of V when its head dim is transformed
+    ws = torch.empty((fwd_bytes + 3) // 4, device=dev, dtype=torch.float32) if fwd_bytes else None
+    nat.check(nat.lib().dfs_fwd(prob, args, nat.ptr(ws), fwd_bytes, nat.stream_ptr(dev)), "dfs_fwd")
     return lu, lv, O, xc, T
 
 

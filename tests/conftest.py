@@ -17,3 +17,20 @@ for p in (ROOT, PKG_ROOT):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+import pytest  # noqa: E402
+
+
+@pytest.fixture(autouse=True)
+def _clear_device_status(request):
+    """Each GPU test starts with the device's sticky status word at 0 (a test
+    that provokes a device error or a CG cap must not leak it into the next)."""
+    if request.node.get_closest_marker("gpu") is not None:
+        import torch
+
+        if torch.cuda.is_available():
+            from deepfold import _native as nat
+
+            nat.ext().take_status(True)
+    yield

@@ -87,8 +87,11 @@ def run_dense(torch, ref, inp, K_iter, lam, r_0, use_gate, mask=None):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("DEEPFOLD_REF_SRC", "/root/reference/src"))
+    ap.add_argument("--ref", default=os.environ.get("DEEPFOLD_REF_SRC"),
+                    help="the reference's src directory (or set DEEPFOLD_REF_SRC)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref <reference src directory> or set DEEPFOLD_REF_SRC")
     sys.path.insert(0, args.ref)
     import torch  # noqa: E402
     from deepfold.model.sinkhorn import compute_transport_output, sinkhorn_solve  # noqa: E402

@@ -6,7 +6,9 @@
   is set in the status word, and the context stays usable.
 * Non-finite input: a NaN in Q makes every column sum non-finite; the resident
   forward re-stabilises once, still fails, and reports DFS_ERR_NUMERIC, which the
-  op raises as RuntimeError (on the next call, or at once with check_status()).
+  op raises as RuntimeError once the status has been read back: at once with
+  check_status(), otherwise from the call that finds it (the next one, or the
+  bad call itself if the read-back has already landed when it returns).
 * A CG solve capped at one iteration reports DFS_WARN_CG_NOT_CONVERGED, which
   the op turns into a warning.
 """
@@ -72,21 +74,21 @@ def test_non_finite_input_raises():
     inp = make_inputs(1, 2, 96, 32, seed=4)
     Q = inp["Q"].clone()
     Q[0, 1, 7, 3] = float("nan")
-    flash_sinkhorn(Q, inp["K"], inp["V"], None, None, None, inp["eps"], None, inp["log_mu"], inp["log_nu"],
-                   K_iter=5, lam=float("inf"))
     with pytest.raises(RuntimeError, match="non-finite"):
+        flash_sinkhorn(Q, inp["K"], inp["V"], None, None, None, inp["eps"], None, inp["log_mu"], inp["log_nu"],
+                       K_iter=5, lam=float("inf"))
         check_status()
-    check_status()  # reported once; the queue is empty again
+    check_status()  # reported once: the status word starts again from 0
 
 
 def test_non_finite_input_raises_on_the_next_call():
     inp = make_inputs(1, 2, 96, 32, seed=5)
     Q = inp["Q"].clone()
     Q[0, 0, 0, 0] = float("inf")
-    flash_sinkhorn(Q, inp["K"], inp["V"], None, None, None, inp["eps"], None, inp["log_mu"], inp["log_nu"],
-                   K_iter=5, lam=float("inf"))
-    torch.cuda.synchronize()  # the status copy has landed
     with pytest.raises(RuntimeError, match="device error"):
+        flash_sinkhorn(Q, inp["K"], inp["V"], None, None, None, inp["eps"], None, inp["log_mu"], inp["log_nu"],
+                       K_iter=5, lam=float("inf"))
+        torch.cuda.synchronize()  # the status read-back has landed
         flash_sinkhorn(inp["Q"], inp["K"], inp["V"], None, None, None, inp["eps"], None, inp["log_mu"],
                        inp["log_nu"], K_iter=5, lam=float("inf"))
     check_status()
@@ -99,6 +101,6 @@ def test_cg_iteration_cap_warns(N, d):
     O, _, _, _ = flash_sinkhorn(*leaves, None, None, None, inp["eps"], None, inp["log_mu"], inp["log_nu"],
                                 K_iter=20, lam=float("inf"), cg_opts=dict(max_iter=1, rtol=1e-12, atol=0.0))
     (O * inp["dO"]).sum().backward()
-    with pytest.warns(UserWarning, match="max_iter"):
+    with pytest.warns(RuntimeWarning, match="max_iter"):
         check_status()
     assert all(torch.isfinite(t.grad).all() for t in leaves)
