@@ -11,10 +11,10 @@
 // Errors the kernels find on the device (a bounded wait that gave up,
 // non-finite potentials, a CG solve that hit its iteration cap) are OR-ed into
 // a sticky status word per device.  Reading it at once would synchronise every
-// call; instead the word is read back asynchronously and checked at the start
-// of the next call, which raises for an error bit; warning bits
-// (DFS_WARN_CG_NOT_CONVERGED) and a synchronous read go to Python through
-// take_status (see DeviceStatus below).
+// call; instead the word is read back asynchronously and picked up by the next
+// call, and the bits go to Python through take_status, where the op raises
+// RuntimeError for an error bit and warns for DFS_WARN_CG_NOT_CONVERGED (see
+// DeviceStatus below).
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAEvent.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -130,25 +130,21 @@ int poll_device_status(const at::Device& dev, bool wait) {
   return v;
 }
 
-// Warning bits seen by the checks inside calls, handed to Python by
-// take_status (Python turns them into warnings).
-std::atomic<int> g_seen_warn{0};
+// Status bits picked up by the checks inside calls (the backward runs on
+// autograd's worker threads, away from Python), handed to Python by
+// take_status: the op's Python wrapper raises for error bits and warns for
+// DFS_WARN_CG_NOT_CONVERGED after each call, so no exception is thrown from
+// here.
+std::atomic<int> g_seen{0};
 
-// The check at the start of every forward and backward: raise for device
-// errors of earlier calls; keep warning bits for take_status.
-void check_device_status(const at::Device& dev) {
-  const int v = poll_device_status(dev, false);
-  g_seen_warn.fetch_or(v & DFS_WARN_CG_NOT_CONVERGED);
-  TORCH_CHECK(!(v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)),
-              "a previous flash_sinkhorn call reported a device error: ",
-              dfs_status_string(v & (DFS_ERR_DEVICE_TIMEOUT | DFS_ERR_NUMERIC)), " (status ", v, ")");
-}
+// The check at the start of every forward and backward.
+void check_device_status(const at::Device& dev) { g_seen.fetch_or(poll_device_status(dev, false)); }
 
 // For Python: the status bits of the current device (see poll_device_status)
-// together with the warning bits kept by earlier checks.
+// together with the bits kept by the checks inside calls; all are cleared.
 int take_status(bool wait) {
   const int v = poll_device_status(at::Device(at::kCUDA, c10::cuda::current_device()), wait);
-  return v | g_seen_warn.exchange(0);
+  return v | g_seen.exchange(0);
 }
 
 struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
@@ -169,11 +165,11 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     TORCH_CHECK(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(),
                 "Q, K, V must share the shape (B, H, N, d)");
     TORCH_CHECK(K.device() == Q.device() && V.device() == Q.device(), "Q, K, V must be on one device");
-    const c10::cuda::CUDAGuard guard(Q.device());  // launches, attributes and streams of Q's device
-    check_device_status(Q.device());
     const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
     TORCH_CHECK(N <= dfs_max_n(static_cast<int>(d)), "N=", N, ", d=", d,
                 " is outside the kernels' range (head dim <= 64, N <= ", dfs_max_n(static_cast<int>(d)), ")");
+    const c10::cuda::CUDAGuard guard(Q.device());  // launches, attributes and streams of Q's device
+    check_device_status(Q.device());
     const auto st = Q.scalar_type();
     const auto cdt = (st == at::kBFloat16 || st == at::kHalf || st == at::kFloat) ? st : at::kFloat;
     const Tensor Qc = Q.contiguous().to(cdt), Kc = K.contiguous().to(cdt), Vc = V.contiguous().to(cdt);

@@ -21,8 +21,9 @@ Differences from the reference, all deliberate:
   CPU, differentiably; without a CUDA device the call raises.
 * Head dims other than 32 and 64 (up to 64) run zero-padded inside the library.
 * Device-side errors (a bounded wait that gave up, non-finite potentials) are
-  raised as RuntimeError by the next call, or at once by ``check_status()``;
-  a CG solve that reached ``max_iter`` gives a warning.
+  raised as RuntimeError by the first call that returns after the status has
+  been read back (the status is read asynchronously), or at once by
+  ``check_status()``; a CG solve that reached ``max_iter`` gives a warning.
 """
 
 from __future__ import annotations

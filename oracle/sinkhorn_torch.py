@@ -141,3 +141,107 @@ def marginal_residuals(Q, K, eps, log_u, log_v, log_mu, log_nu, mask=None):
     r = (P.sum(-1) - log_mu.double().exp()).abs().masked_fill(~valid, 0)
     c = (P.sum(-2) - log_nu.double().exp()).abs().masked_fill(~valid, 0)
     return float(r.max()), float(c.max())
+
+
+# --------------------------------------------------------------------------
+# one problem, float64, implicit-function-theorem adjoint (no autograd state)
+# --------------------------------------------------------------------------
+
+def problem_fwd_bwd_ift(q, k, v, dO, eps: float, a, b, K_iter: int, lam: float, mask=None, cg_tol=1e-12,
+                        cg_max_iter=2000):
+    """Forward and gradient of sum(O * dO) for one (N, d) problem, in the dtype of
+    its inputs (float64 for checking), without autograd: the reference's loop
+    (sinkhorn.py:82-96) and transport (sinkhorn.py:152-195), then the
+    transport adjoint and the implicit-function-theorem adjoint of the fixed
+    point -- the same formulation as oracle/sinkhorn_oracle.py's
+    transport_backward / ift_backward, for problems (N = 8192) whose unrolled
+    autograd state would not fit in host memory.  At a converged forward it
+    equals the reference's unrolled gradient.
+
+    Returns dict(O, log_u, log_v, dQ, dK, dV, marg_row, marg_col)."""
+    N, d = q.shape
+    kap = 1.0 if math.isinf(lam) else lam / (lam + eps)
+    valid = torch.ones(N, dtype=torch.bool) if mask is None else mask > 0.5
+    mb = torch.zeros(N, dtype=q.dtype) if mask is None else (1.0 - mask.to(q.dtype)) * MASK_BIAS
+    S = (q @ k.T) / (math.sqrt(d) * eps)          # S = -C / eps
+    f = torch.zeros(N, dtype=q.dtype)
+    g = torch.zeros(N, dtype=q.dtype)
+    for _ in range(K_iter):
+        f = kap * (a - torch.logsumexp(S + (g + mb)[None, :], dim=1))
+        g = kap * (b - torch.logsumexp(S + (f + mb)[:, None], dim=0))
+    # transport (running max over masked columns, 1e-6 in the normaliser)
+    score = f[:, None] + S + (g + mb)[None, :]
+    m, am = score.max(dim=1, keepdim=True)
+    T = torch.exp(score - m)
+    del score
+    Ts = T.sum(1)
+    den = Ts + NORM_EPS
+    Tn = T / den[:, None]
+    Tn = Tn * valid[:, None]
+    O = Tn @ v
+    # transport adjoint: dS_direct, df = row sums, dg = column sums, dV
+    dOm = dO * valid[:, None]
+    Tbar_n = (dOm @ v.T) * valid[:, None]
+    dV = Tn.T @ dOm
+    del Tn
+    Tbar = Tbar_n / den[:, None] - ((Tbar_n * T).sum(1) / den ** 2)[:, None]
+    del Tbar_n
+    sbar = Tbar * T
+    # the row maximum's own term (nonzero only through the 1e-6 of the normaliser)
+    sbar.scatter_add_(1, am, -(Tbar * T).sum(1, keepdim=True))
+    del Tbar, T
+    df, dg = sbar.sum(1), sbar.sum(0)
+    # IFT system [[diag(r)/kappa, P], [P^T, diag(c)/kappa]] w = [df; dg]
+    P = torch.exp(f[:, None] + S + g[None, :]) * valid[:, None] * valid[None, :]
+    r, c = P.sum(1), P.sum(0)
+    dr = torch.where(valid, r / kap, torch.ones_like(r))
+    dc = torch.where(valid, c / kap, torch.ones_like(c))
+    rhs = torch.cat([torch.where(valid, df, 0 * df), torch.where(valid, dg, 0 * dg)])
+    nv = int(valid.sum())
+    if kap >= 1.0 and nv > 0:
+        s = (rhs[:N][valid].sum() - rhs[N:][valid].sum()) / (2 * nv)
+        rhs[:N] = torch.where(valid, rhs[:N] - s, rhs[:N])
+        rhs[N:] = torch.where(valid, rhs[N:] + s, rhs[N:])
+
+    def mv(w):
+        return torch.cat([dr * w[:N] + P @ w[N:], P.T @ w[:N] + dc * w[N:]])
+
+    dinv = 1.0 / torch.cat([dr, dc])
+    w = torch.zeros(2 * N, dtype=q.dtype)
+    res = rhs.clone()
+    z = dinv * res
+    p = z.clone()
+    rz = res @ z
+    nrm0 = float(torch.linalg.norm(res))
+    for _ in range(cg_max_iter):
+        if nrm0 == 0.0:
+            break
+        Ap = mv(p)
+        dd = float(p @ Ap)
+        if dd == 0.0:
+            break
+        al = rz / dd
+        w = w + al * p
+        res = res - al * Ap
+        if float(torch.linalg.norm(res)) <= cg_tol * nrm0:
+            break
+        z = dinv * res
+        rz_new = res @ z
+        p = z + (rz_new / rz) * p
+        rz = rz_new
+    w1, w2 = w[:N] * valid, w[N:] * valid
+    if kap >= 1.0 and nv > 0:
+        t = -(r * w1).sum() / r.sum()
+        w1 = (w1 + t) * valid
+        w2 = (w2 - t) * valid
+    dS = sbar - P * (w1[:, None] + w2[None, :])
+    del sbar
+    marg_r = float(((r - a.exp()).abs() * valid).max())
+    marg_c = float(((c - b.exp()).abs() * valid).max())
+    del P
+    dC_scale = 1.0 / (math.sqrt(d) * eps)          # dS/dQ = K / (sqrt(d) eps)
+    dQ = (dS @ k) * dC_scale
+    dK = (dS.T @ q) * dC_scale
+    fo = f * valid
+    go = g * valid
+    return dict(O=O, log_u=fo, log_v=go, dQ=dQ, dK=dK, dV=dV, marg_row=marg_r, marg_col=marg_c)

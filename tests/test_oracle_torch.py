@@ -101,3 +101,31 @@ def test_agrees_with_numpy_oracle_balanced_inf():
     assert rel(dQ, gr["dQ"]) < 1e-9 and rel(dK, gr["dK"]) < 1e-9 and rel(dV, gr["dV"]) < 1e-9
     r, c = ort.marginal_residuals(Q, K, eps, lu, lv, lm, lm)
     assert r < 1e-6 and c < 1e-6
+
+
+@pytest.mark.parametrize("lam,masked", [(math.inf, False), (1.0, True)])
+def test_problem_ift_matches_numpy_oracle(lam, masked):
+    """The torch float64 IFT checker (used at N = 8192) against the numpy oracle's
+    IFT adjoint on a small problem, balanced and unbalanced with padding."""
+    g = torch.Generator().manual_seed(11)
+    N, d, eps, K_it = 48, 16, 0.7, 60
+    q, k, v, dO = (torch.randn(N, d, generator=g, dtype=torch.float64) for _ in range(4))
+    mask = torch.ones(N, dtype=torch.float64)
+    if masked:
+        mask[37:] = 0
+    cnt = float(mask.sum())
+    a = torch.where(mask > 0, torch.log_softmax(torch.randn(N, generator=g, dtype=torch.float64)
+                                                .masked_fill(mask == 0, -1e30), 0), torch.full((N,), -1e9,
+                                                                                         dtype=torch.float64))
+    b = torch.where(mask > 0, torch.full((N,), -math.log(cnt), dtype=torch.float64),
+                    torch.full((N,), -1e9, dtype=torch.float64))
+    out = ort.problem_fwd_bwd_ift(q, k, v, dO, eps, a, b, K_it, lam, mask=mask if masked else None)
+    res, gr = orc.flash_sinkhorn_attn(q[None, None].numpy(), k[None, None].numpy(), v[None, None].numpy(), None,
+                                      None, None, None, np.array([eps]), None, a[None, None].numpy(),
+                                      b[None, None].numpy(), K_iter=K_it, lam=lam,
+                                      mask=mask[None].numpy() if masked else None, with_grad=True,
+                                      dO_flat=dO[None].numpy(), grad_mode="ift")
+    assert rel(out["O"], res.O_avg[0, 0]) < 1e-10
+    assert np.max(np.abs(out["log_u"].numpy() - res.log_u[0, 0])) < 1e-9
+    for key in ("dQ", "dK", "dV"):
+        assert rel(out[key], gr[key][0, 0]) < 1e-8, key
