@@ -17,7 +17,6 @@
 // DeviceStatus below).
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAEvent.h>
-#include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include <atomic>
@@ -60,6 +59,24 @@ std::vector<Tensor>& last_report() {
   static auto* r = new std::vector<Tensor>();
   return *r;
 }
+
+// Makes a device current for a scope and restores the previous one, with the
+// plain runtime calls.  (Unwinding an exception through c10::cuda::CUDAGuard's
+// destructor crashed this extension on the B200 boxes, so the guard is not
+// used; argument checks that throw also come before the switch.)
+struct DeviceSwitch {
+  int prev = -1;
+  explicit DeviceSwitch(const at::Device& dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev.index()) cudaSetDevice(dev.index());
+  }
+  ~DeviceSwitch() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+  DeviceSwitch(const DeviceSwitch&) = delete;
+  DeviceSwitch& operator=(const DeviceSwitch&) = delete;
+};
 
 // ---------------------------------------------------------------- device status
 // One sticky int32 status word per device: every forward and backward call
@@ -107,17 +124,19 @@ void start_readback(DeviceStatus& ds, cudaStream_t stream) {
   ds.in_flight = true;
 }
 
-// Read the status word of a device (wait: its value once the current stream
-// has drained; otherwise the last completed read-back, or 0).  A nonzero value
-// clears the word.  Returns the bits.
+// Read the status word of a device (wait: its value once all work on the
+// device has finished, read synchronously; otherwise the last completed
+// read-back, or 0).  A nonzero value clears the word.  Returns the bits.
 int poll_device_status(const at::Device& dev, bool wait) {
   std::lock_guard<std::mutex> lock(g_status_mu);
   DeviceStatus& ds = device_status(dev);
   const cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev.index()).stream();
   if (wait) {
-    if (!ds.in_flight) start_readback(ds, stream);
-    if (!ds.in_flight) return 0;
-    cudaEventSynchronize(ds.copied);
+    // an in-flight read-back may predate the latest calls (a call starts none
+    // while one is in flight): drain the device and read the word itself
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(ds.mirror, ds.word.data_ptr<int32_t>(), sizeof(int32_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return 0;
   } else if (!ds.in_flight || cudaEventQuery(ds.copied) != cudaSuccess) {
     return 0;
   }
@@ -168,7 +187,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
     TORCH_CHECK(N <= dfs_max_n(static_cast<int>(d)), "N=", N, ", d=", d,
                 " is outside the kernels' range (head dim <= 64, N <= ", dfs_max_n(static_cast<int>(d)), ")");
-    const c10::cuda::CUDAGuard guard(Q.device());  // launches, attributes and streams of Q's device
+    const DeviceSwitch guard(Q.device());  // launches, attributes and streams of Q's device
     check_device_status(Q.device());
     const auto st = Q.scalar_type();
     const auto cdt = (st == at::kBFloat16 || st == at::kHalf || st == at::kFloat) ? st : at::kFloat;
@@ -251,7 +270,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
 
   static variable_list backward(AutogradContext* ctx, variable_list grads) {
     const auto saved = ctx->get_saved_variables();
-    const c10::cuda::CUDAGuard guard(saved[0].device());
+    const DeviceSwitch guard(saved[0].device());
     check_device_status(saved[0].device());
     const Tensor &Qc = saved[0], &Kc = saved[1], &Vc = saved[2], &xr = saved[3], &pw = saved[4],
                  &pb = saved[5], &epsc = saved[6], &wd = saved[7], &lmu = saved[8], &lnu = saved[9],
