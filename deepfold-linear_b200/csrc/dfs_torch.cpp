@@ -21,6 +21,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -32,8 +33,17 @@ using at::Tensor;
 using torch::autograd::AutogradContext;
 using torch::autograd::variable_list;
 
+// Errors are thrown as std::runtime_error (pybind11 raises RuntimeError) with
+// the message built here: a TORCH_CHECK whose message formats a number crashed
+// the process in this torch build, inside any extension.
+[[noreturn]] void fail(const std::string& msg) { throw std::runtime_error(msg); }
+void require(bool ok, const char* msg) {
+  if (!ok) fail(msg);
+}
+
 void check_rc(int rc, const char* what) {
-  TORCH_CHECK(rc == DFS_OK, what, " failed: ", dfs_status_string(rc), " (code ", rc, ")");
+  if (rc != DFS_OK)
+    fail(std::string(what) + " failed: " + dfs_status_string(rc) + " (code " + std::to_string(rc) + ")");
 }
 
 int dtype_code(at::ScalarType t) {
@@ -61,9 +71,7 @@ std::vector<Tensor>& last_report() {
 }
 
 // Makes a device current for a scope and restores the previous one, with the
-// plain runtime calls.  (Unwinding an exception through c10::cuda::CUDAGuard's
-// destructor crashed this extension on the B200 boxes, so the guard is not
-// used; argument checks that throw also come before the switch.)
+// plain runtime calls.
 struct DeviceSwitch {
   int prev = -1;
   explicit DeviceSwitch(const at::Device& dev) {
@@ -99,15 +107,14 @@ DeviceStatus* g_status[kMaxDevices] = {};
 
 DeviceStatus& device_status(const at::Device& dev) {
   const int i = dev.index();
-  TORCH_CHECK(i >= 0 && i < kMaxDevices, "device index out of range");
+  require(i >= 0 && i < kMaxDevices, "device index out of range");
   if (g_status[i] == nullptr) {
     auto* ds = new DeviceStatus();
     ds->word = at::zeros({1}, at::TensorOptions().device(dev).dtype(at::kInt));
-    TORCH_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&ds->mirror), sizeof(int32_t), cudaHostAllocDefault) ==
-                    cudaSuccess, "cudaHostAlloc failed");
+    require(cudaHostAlloc(reinterpret_cast<void**>(&ds->mirror), sizeof(int32_t), cudaHostAllocDefault) ==
+                cudaSuccess, "cudaHostAlloc failed");
     *ds->mirror = 0;
-    TORCH_CHECK(cudaEventCreateWithFlags(&ds->copied, cudaEventDisableTiming) == cudaSuccess,
-                "cudaEventCreate failed");
+    require(cudaEventCreateWithFlags(&ds->copied, cudaEventDisableTiming) == cudaSuccess, "cudaEventCreate failed");
     g_status[i] = ds;
   }
   return *g_status[i];
@@ -179,14 +186,16 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
                                c10::optional<Tensor> log_u_init, c10::optional<Tensor> log_v_init,
                                c10::optional<Tensor> mask, int64_t K_iter, double lam, double r_0,
                                double cg_rtol, double cg_atol, int64_t cg_max_iter) {
-    TORCH_CHECK(Q.is_cuda() && K.is_cuda() && V.is_cuda(),
+    require(Q.is_cuda() && K.is_cuda() && V.is_cuda(),
                 "deepfold B200 Sinkhorn ops run on CUDA tensors only (no CPU path)");
-    TORCH_CHECK(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(),
+    require(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(),
                 "Q, K, V must share the shape (B, H, N, d)");
-    TORCH_CHECK(K.device() == Q.device() && V.device() == Q.device(), "Q, K, V must be on one device");
+    require(K.device() == Q.device() && V.device() == Q.device(), "Q, K, V must be on one device");
     const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
-    TORCH_CHECK(N <= dfs_max_n(static_cast<int>(d)), "N=", N, ", d=", d,
-                " is outside the kernels' range (head dim <= 64, N <= ", dfs_max_n(static_cast<int>(d)), ")");
+    if (N > dfs_max_n(static_cast<int>(d)))
+      fail("N=" + std::to_string(N) + ", d=" + std::to_string(d) +
+           " is outside the kernels' range (head dim <= 64, N <= " + std::to_string(dfs_max_n(static_cast<int>(d))) +
+           ")");
     const DeviceSwitch guard(Q.device());  // launches, attributes and streams of Q's device
     check_device_status(Q.device());
     const auto st = Q.scalar_type();
@@ -279,7 +288,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
       const int64_t e = ctx->saved_data[key].toInt();
       return e >= 0 && ctx->needs_input_grad(static_cast<size_t>(e));
     };
-    TORCH_CHECK(!((needs("e_x") && xr.defined()) || (needs("e_pw") && pw.defined()) ||
+    require(!((needs("e_x") && xr.defined()) || (needs("e_pw") && pw.defined()) ||
                   (needs("e_wd") && wd.defined())),
                 "gradients for x_res / pos_weight / w_dist are not implemented by the B200 backward yet; "
                 "pass them without requires_grad");

@@ -104,3 +104,23 @@ def test_cg_iteration_cap_warns(N, d):
     with pytest.warns(RuntimeWarning, match="max_iter"):
         check_status()
     assert all(torch.isfinite(t.grad).all() for t in leaves)
+
+
+def test_argument_errors_raise_cleanly():
+    """Host-side rejections (head dim beyond 64; an invalid lam caught by the
+    library's own validation) raise RuntimeError with the library's message."""
+    from deepfold import _native as nat
+
+    ext = nat.ext()
+    dev = torch.device("cuda")
+    lm = torch.zeros(1, 1, 64, device=dev)
+    wide = torch.zeros(1, 1, 64, 96, device=dev)
+    with pytest.raises(RuntimeError, match="outside the kernels' range"):
+        ext.flash_sinkhorn(wide, wide, wide, None, None, None, torch.ones(1, device=dev), None, lm, lm, None, None,
+                           None, 5, float("inf"), 10.0, 1e-6, 0.0, 50)
+    x = torch.zeros(1, 1, 64, 32, device=dev)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        ext.flash_sinkhorn(x, x, x, None, None, None, torch.ones(1, device=dev), None, lm, lm, None, None, None, 5,
+                           -1.0, 10.0, 1e-6, 0.0, 50)
+    with pytest.raises(ValueError, match="lam"):
+        flash_sinkhorn(x, x, x, None, None, None, torch.ones(1, device=dev), None, lm, lm, K_iter=5, lam=-1.0)

@@ -243,7 +243,9 @@ def test_dense_unbatched_matches_batched():
         tr = orc.transport_problem(S, ub[0][h].double().numpy(), ub[1][h].double().numpy(), V[h].numpy(), x.numpy())
         sig = 1.0 / (1.0 + np.exp(-G[h].double().numpy()))
         assert max_abs(T[h].numpy(), tr.Tn) <= 1e-5
-        assert max_abs(o.numpy().reshape(8, 4, 16)[:, h], sig * tr.O) <= 1e-4
+        # T_norm enters the tensor-core product O = T_norm V as tf32 (2^-11 relative), as
+        # the reference's tl.dot does on the GPU
+        assert max_abs(o.numpy().reshape(8, 4, 16)[:, h], sig * tr.O) <= 1e-3
         assert max_abs(xc[h].numpy(), tr.xc) <= 1e-4
 
 
