@@ -27,14 +27,16 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // are instantiated for head dims 32 and 64.  Operands are transformed on copies
 // at the front of the workspace (dfs_pad.cu) when
 //   XF_PAD      the head dim is another one: zero-padded to the next one;
-//   XF_SPLIT_QK fp32 Q, K, V with 3 d <= 64: bf16 hi / lo parts along the
+//   XF_SPLIT_QK fp32 Q, K, V whose tripled head dim stays in the same kernel
+//               family (3 d <= 32 for d <= 32, i.e. d <= 10; 3 d <= 64 for
+//               32 < d <= 64 never holds): bf16 hi / lo parts along the
 //               contraction dimension (exact products instead of tf32 ones);
 //   XF_SPLIT_V  fp32 V of the dense-cost path with 2 d <= 32: V = [Vhi Vlo].
 constexpr int kResidentMaxN = 384;
 constexpr int kStreamMaxN = 1 << 16;
 enum { XF_NONE = 0, XF_PAD = 1, XF_SPLIT_QK = 2, XF_SPLIT_V = 3 };
 int xform(const dfs_problem* p) {
-  if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_QK && 3 * p->d <= 64) return XF_SPLIT_QK;
+  if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_QK && 3 * p->d <= 32) return XF_SPLIT_QK;
   if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_DENSE && 2 * p->d <= 32) return XF_SPLIT_V;
   return kernel_head_dim(p->d) != p->d ? XF_PAD : XF_NONE;
 }

@@ -34,6 +34,19 @@
 // Every row or column is owned by exactly one CTA: no atomics, deterministic.
 // Element loops over the register slab are branch-free; optional terms (dxc,
 // bias) are separate rolled passes over the shared-memory tile.
+//
+// Gradients of the shared cost parameters (sinkhorn_kernel.py:2366-2382 of the
+// reference returns them): with dC = -dS / eps,
+//   dw_h    = sum_ij dC_ij dist_ij / (r_0 + dist_ij)
+//   dx_i    = sum_j dC_ij c_ij (x_i - x_j) + sum_j dC_ji c_ji (x_i - x_j) + (T_norm^T dxc)_i,
+//             c_ij = w_h r_0 / ((r_0 + dist_ij)^2 dist_ij)
+//   dpos[h, b] = sum over the entries with bins_ij = b of dC_ij
+// are accumulated from the staged dS tile of phase 5 (row part, dw, bins), the
+// staged T_norm^T of phase 7 (centroid part) and the staged dS^T of phase 8
+// (column part), per slab row and per CTA into the workspace; the bin histogram
+// is summed in 64-bit fixed point (scale from the tile's largest |dC|), so its
+// integer atomics are exact and order-free.  resident_costgrad_finalize sums the
+// partials over heads, CTAs and batch elements in a fixed order.
 #include "dfs_slab.cuh"
 
 namespace dfs {
@@ -64,6 +77,24 @@ struct BwdCfg {
   static_assert(kWarps * 2u * NP * 4 <= 4u * NP * DH, "column partials must fit the K/V region");
   static_assert(NP + DH <= 512, "TMEM columns");
 };
+
+// Workspace of the shared-parameter gradients (floats): per (batch, head,
+// point) the three dx partials, then per (batch, head, CTA) the dw partial and
+// the 68 position-bin partials.
+struct CostGradWs {
+  float* dx;    // (B*H, N, 3)
+  float* dw;    // (B*H, C)
+  float* dpos;  // (B*H, C, 68)
+};
+__host__ __device__ inline CostGradWs costgrad_ws(float* ws, int B, int H, int N) {
+  const size_t bh = static_cast<size_t>(B) * H, C = (N + 63) / 64;
+  CostGradWs w;
+  w.dx = ws;
+  w.dw = ws + bh * N * 3;
+  w.dpos = w.dw + bh * C;
+  return w;
+}
+constexpr int kBins = 68;
 
 template <int C, int DH>
 __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdParams p) {
@@ -548,6 +579,98 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     issue_abt_split<DH, NP, kGradAcc>(tbase, Ts, KV);  // dQ = dS K
     mma_commit(mbar);
   }
+  // shared-parameter gradients from the staged dS while the tensor core reads it
+  // (the exchange buffers are free from here on: cg_* scratch lives there)
+  const bool geo_grad = p.x_res != nullptr && (p.dw_dist != nullptr || (p.dx_res != nullptr && w_h != 0.0f));
+  const bool pos_grad = p.dpos_weight != nullptr && p.pos_bins != nullptr;
+  const bool cost_grad = geo_grad || pos_grad || p.dx_res != nullptr;
+  float* cg_dx = reinterpret_cast<float*>(base + Cfg::OFF_XR);                                // 3 x 64
+  unsigned long long* cg_hist = reinterpret_cast<unsigned long long*>(base + Cfg::OFF_XR + 1024);  // 68
+  float* cg_red = reinterpret_cast<float*>(base + Cfg::OFF_XR + 1600);                        // 32
+  const float inv_eps = 1.0f / eps_h;
+  // dx share sum_j dC_ij c_ij (x_row - x_col) of the staged tile's slab rows
+  // (lanes over the N columns), added to cg_dx; with `bins`, the tile's dw
+  // partial (returned, per thread) and fixed-point histogram (scale `hscale`)
+  auto geo_rows = [&](bool transposed, bool with_bins, float hscale) -> float {
+    float dw = 0.0f;
+#pragma unroll 1
+    for (int r = 0; r < kRpw; ++r) {
+      const int li = kRpw * warp + r, gi = row0 + li;
+      float ax = 0.0f, ay = 0.0f, az = 0.0f;
+      if (gi < N) {
+        const float x0 = rowv[BR_X0 * 64 + li], x1 = rowv[BR_X1 * 64 + li], x2 = rowv[BR_X2 * 64 + li];
+        const int32_t* brow = pos_grad && with_bins ? p.pos_bins + (static_cast<size_t>(bb) * N + gi) * N : nullptr;
+#pragma unroll 2
+        for (int j = lane; j < N; j += 32) {
+          const float dC = -Ts[sw_off(li, j, 64) >> 2] * inv_eps;
+          if (geo_grad) {
+            const float d0 = x0 - colv[BC_X0 * NP + j], d1 = x1 - colv[BC_X1 * NP + j], d2 = x2 - colv[BC_X2 * NP + j];
+            const float dist = sqrtf(d0 * d0 + d1 * d1 + d2 * d2 + 1e-8f);
+            const float rd = 1.0f / (p.r_0 + dist);
+            if (with_bins) dw = fmaf(dC, dist * rd, dw);
+            const float cf = dC * w_h * p.r_0 * rd * rd / dist;
+            ax = fmaf(cf, d0, ax);
+            ay = fmaf(cf, d1, ay);
+            az = fmaf(cf, d2, az);
+          }
+          if (brow != nullptr) {
+            const unsigned bin = static_cast<unsigned>(brow[j]);  // bins outside [0, 68) add nothing
+            const long long q = __float2ll_rn(dC * hscale);
+            if (bin < static_cast<unsigned>(kBins)) atomicAdd(&cg_hist[bin], static_cast<unsigned long long>(q));
+          }
+        }
+      }
+      ax = warp_sum(ax);
+      ay = warp_sum(ay);
+      az = warp_sum(az);
+      if (lane == 0) {
+        cg_dx[li] += ax;
+        cg_dx[64 + li] += ay;
+        cg_dx[128 + li] += az;
+      }
+    }
+    (void)transposed;
+    return dw;
+  };
+  if (cost_grad) {
+    for (int i = tid; i < 3 * 64; i += kThreads) cg_dx[i] = 0.0f;
+    for (int i = tid; i < kBins; i += kThreads) cg_hist[i] = 0ull;
+    // fixed-point scale of the histogram: the tile's largest |dC| maps to 2^46,
+    // so that the sum of up to 64 x 384 < 2^15 terms stays below 2^62
+    float hscale = 0.0f;
+    if (pos_grad) {
+      float mx = 0.0f;
+#pragma unroll 1
+      for (int idx = tid; idx < 64 * NP; idx += kThreads) mx = fmaxf(mx, fabsf(Ts[sw_off(idx / NP, idx % NP, 64) >> 2]));
+      mx = warp_max(mx);
+      if (lane == 0) cg_red[warp] = mx;
+    }
+    __syncthreads();
+    if (pos_grad) {
+      float mx = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, cg_red[w]);
+      mx *= inv_eps;
+      int ex = 0;
+      frexpf(mx, &ex);  // mx < 2^ex
+      hscale = mx > 0.0f ? ldexpf(1.0f, 46 - ex) : 0.0f;
+    }
+    const float dwp = geo_rows(false, true, hscale);
+    __syncthreads();  // cg_red reused
+    const float dws = warp_sum(dwp);
+    if (lane == 0) cg_red[warp] = dws;
+    __syncthreads();
+    const size_t cta = static_cast<size_t>(prob) * C + crank;
+    const CostGradWs cw = costgrad_ws(p.ws, p.B, p.H, N);
+    if (tid == 0 && p.dw_dist != nullptr) {
+      float s = 0.0f;
+      for (int w = 0; w < kWarps; ++w) s += cg_red[w];
+      cw.dw[cta] = s;
+    }
+    if (pos_grad && tid < kBins)
+      cw.dpos[cta * kBins + tid] =
+          hscale > 0.0f ? static_cast<float>(static_cast<double>(static_cast<long long>(cg_hist[tid])) / hscale) : 0.0f;
+  }
   mma_wait();
   if (p.dQ) drain_rows_to_global<DH, kGradAcc>(tbase, 0, p.dQ, bh * N, row0, N, grad_scale, warp, lane);
 
@@ -602,6 +725,31 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
 #pragma unroll
     for (int r = 0; r < kRpw; ++r) Ts[sw_off(kRpw * warp + r, i, 64) >> 2] = P[r][k] * inv;
   }
+  if (cost_grad && p.dx_res != nullptr && p.dxc != nullptr) {
+    // centroid share (T_norm^T dxc)_j for the slab rows j (each warp its own rows,
+    // from its own stores above)
+    __syncwarp();
+#pragma unroll 1
+    for (int r = 0; r < kRpw; ++r) {
+      const int lj = kRpw * warp + r;
+      float ax = 0.0f, ay = 0.0f, az = 0.0f;
+      for (int i = lane; i < N; i += 32) {
+        const float t = Ts[sw_off(lj, i, 64) >> 2];
+        const float* dx = p.dxc + (bh * N + i) * 3;
+        ax = fmaf(t, dx[0], ax);
+        ay = fmaf(t, dx[1], ay);
+        az = fmaf(t, dx[2], az);
+      }
+      ax = warp_sum(ax);
+      ay = warp_sum(ay);
+      az = warp_sum(az);
+      if (lane == 0) {
+        cg_dx[lj] += ax;
+        cg_dx[64 + lj] += ay;
+        cg_dx[128 + lj] += az;
+      }
+    }
+  }
   mma_wait();
   __syncthreads();
   load_operand_f32_t<DH, NP>(KV, p.dO, bh * N, 0, N, tid);            // dO^T (DH x NP)
@@ -651,6 +799,19 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     issue_abt_split<DH, NP, kGradAcc>(tbase, Ts, KV);  // dK = dS^T Q
     mma_commit(mbar);
   }
+  if (cost_grad && p.dx_res != nullptr) {
+    // column share: slab rows are cost columns j, lanes run over the rows i;
+    // dx_j += sum_i dC_ij c_ij (x_j - x_i) (dist and c are symmetric in i, j)
+    if (geo_grad && w_h != 0.0f) geo_rows(true, false, 0.0f);
+    __syncthreads();
+    if (tid < 64 && row0 + tid < N) {
+      const CostGradWs cw = costgrad_ws(p.ws, p.B, p.H, N);
+      float* o = cw.dx + (bh * N + row0 + tid) * 3;
+      o[0] = cg_dx[tid];
+      o[1] = cg_dx[64 + tid];
+      o[2] = cg_dx[128 + tid];
+    }
+  }
   mma_wait();
   if (p.dK) drain_rows_to_global<DH, kGradAcc>(tbase, 0, p.dK, bh * N, row0, N, grad_scale, warp, lane);
 
@@ -660,6 +821,34 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   __syncthreads();
   if (warp == 0) tmem_dealloc(tbase, 512);
   cluster_sync();  // peers may read this CTA's exchange buffers until here
+}
+
+// Sums of the shared-parameter gradient partials in a fixed order: dx_res over
+// heads, dw_dist and dpos_weight over batch elements and CTAs.
+__global__ void resident_costgrad_finalize(const BwdParams p, int C) {
+  const CostGradWs cw = costgrad_ws(p.ws, p.B, p.H, p.N);
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int ndx = p.dx_res != nullptr ? p.B * p.N * 3 : 0;
+  const int ndw = p.dw_dist != nullptr ? p.H : 0;
+  const int npos = p.dpos_weight != nullptr ? p.H * kBins : 0;
+  if (t < ndx) {
+    const int b = t / (p.N * 3), rem = t % (p.N * 3);
+    float s = 0.0f;
+    for (int h = 0; h < p.H; ++h) s += cw.dx[(static_cast<size_t>(b) * p.H + h) * p.N * 3 + rem];
+    p.dx_res[t] = s;
+  } else if (t < ndx + ndw) {
+    const int h = t - ndx;
+    float s = 0.0f;
+    for (int b = 0; b < p.B; ++b)
+      for (int c = 0; c < C; ++c) s += cw.dw[(static_cast<size_t>(b) * p.H + h) * C + c];
+    p.dw_dist[h] = s;
+  } else if (t < ndx + ndw + npos) {
+    const int u = t - ndx - ndw, h = u / kBins, bin = u % kBins;
+    float s = 0.0f;
+    for (int b = 0; b < p.B; ++b)
+      for (int c = 0; c < C; ++c) s += cw.dpos[((static_cast<size_t>(b) * p.H + h) * C + c) * kBins + bin];
+    p.dpos_weight[u] = s;
+  }
 }
 
 template <int C, int DH>
@@ -686,15 +875,21 @@ static cudaError_t launch_bwd_cd(const BwdParams& p, cudaStream_t st) {
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st) {
   const int C = (p.N + 63) / 64;
   if (p.d != 32) return cudaErrorInvalidValue;
+  cudaError_t e;
   switch (C) {
-    case 1: return launch_bwd_cd<1, 32>(p, st);
-    case 2: return launch_bwd_cd<2, 32>(p, st);
-    case 3: return launch_bwd_cd<3, 32>(p, st);
-    case 4: return launch_bwd_cd<4, 32>(p, st);
-    case 5: return launch_bwd_cd<5, 32>(p, st);
-    case 6: return launch_bwd_cd<6, 32>(p, st);
+    case 1: e = launch_bwd_cd<1, 32>(p, st); break;
+    case 2: e = launch_bwd_cd<2, 32>(p, st); break;
+    case 3: e = launch_bwd_cd<3, 32>(p, st); break;
+    case 4: e = launch_bwd_cd<4, 32>(p, st); break;
+    case 5: e = launch_bwd_cd<5, 32>(p, st); break;
+    case 6: e = launch_bwd_cd<6, 32>(p, st); break;
     default: return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess) return e;
+  const int n = (p.dx_res ? p.B * p.N * 3 : 0) + (p.dw_dist ? p.H : 0) + (p.dpos_weight ? p.H * kBins : 0);
+  if (n == 0) return cudaSuccess;
+  resident_costgrad_finalize<<<(n + 255) / 256, 256, 0, st>>>(p, C);
+  return cudaGetLastError();
 }
 
 size_t resident_bwd_smem(int N, int d) {
@@ -710,6 +905,9 @@ size_t resident_bwd_smem(int N, int d) {
   }
 }
 
-size_t resident_bwd_workspace(int, int, int, int) { return 0; }
+size_t resident_bwd_workspace(int B, int H, int N, int) {
+  const size_t bh = static_cast<size_t>(B) * H, C = (N + 63) / 64;
+  return sizeof(float) * (bh * N * 3 + bh * C + bh * C * kBins);
+}
 
 }  // namespace dfs

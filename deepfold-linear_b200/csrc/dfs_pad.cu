@@ -9,7 +9,7 @@
 //
 // fp32 split.  Tensor-core products of fp32 operands run as tf32 (10 explicit
 // mantissa bits), which costs ~1e-3 relative accuracy in the logits.  For fp32
-// inputs with 3 d <= 64 the library instead writes each operand as a sum of two
+// inputs with 3 d <= 32 the library instead writes each operand as a sum of two
 // bf16 parts, x = hi + lo (hi = bf16(x), lo = bf16(x - hi); 16 mantissa bits),
 // and concatenates the parts along the contraction dimension:
 //     Q' = [Qhi Qhi Qlo],  K' = [Khi Klo Khi],  V' = [Vhi Vlo 0],  dO' = [dO dO 0]

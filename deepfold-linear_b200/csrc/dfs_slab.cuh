@@ -110,7 +110,8 @@ DFS_DEV void add_cost_bias_stage(float* Ts, const BiasArgs& a, int tid) {
     if (a.pos_weight) {
       const size_t bi = a.transposed ? (static_cast<size_t>(a.bb) * a.N + gj) * a.N + gi
                                      : (static_cast<size_t>(a.bb) * a.N + gi) * a.N + gj;
-      bias += a.pos_weight[a.hh * 68 + a.pos_bins[bi]];
+      const unsigned bin = static_cast<unsigned>(a.pos_bins[bi]);  // bins outside [0, 68) add nothing
+      bias += bin < 68u ? a.pos_weight[a.hh * 68 + bin] : 0.0f;
     }
     if (a.geo) {
       const float d0 = a.xrow[li] - a.xcol[gj], d1 = a.xrow[64 + li] - a.xcol[NP + gj],

@@ -262,6 +262,12 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     ctx->saved_data["cg_max_iter"] = cg_max_iter;
     ctx->saved_data["fwd_status"] = status;
     ctx->saved_data["in_dtype"] = static_cast<int64_t>(Q.scalar_type());
+    auto dtype_of = [](const c10::optional<Tensor>& t) {
+      return static_cast<int64_t>(t.has_value() && t->defined() ? t->scalar_type() : at::kFloat);
+    };
+    ctx->saved_data["x_dtype"] = dtype_of(x_res);
+    ctx->saved_data["pw_dtype"] = dtype_of(pos_weight);
+    ctx->saved_data["wd_dtype"] = dtype_of(w_dist);
     int64_t edge = 3;  // Q, K, V are edges 0..2
     auto next_edge = [&](bool present) -> int64_t { return present ? edge++ : -1; };
     ctx->saved_data["e_x"] = next_edge(x_res.has_value());
@@ -288,10 +294,6 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
       const int64_t e = ctx->saved_data[key].toInt();
       return e >= 0 && ctx->needs_input_grad(static_cast<size_t>(e));
     };
-    require(!((needs("e_x") && xr.defined()) || (needs("e_pw") && pw.defined()) ||
-                  (needs("e_wd") && wd.defined())),
-                "gradients for x_res / pos_weight / w_dist are not implemented by the B200 backward yet; "
-                "pass them without requires_grad");
     const int64_t B = Qc.size(0), H = Qc.size(1), N = Qc.size(2), d = Qc.size(3);
     const auto fo = Qc.options().dtype(at::kFloat);
     const Tensor dOc = grads[0].defined() ? grads[0].contiguous().to(at::kFloat) : at::zeros({B, H, N, d}, fo);
@@ -301,6 +303,10 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor dV = ctx->needs_input_grad(2) ? at::empty({B, H, N, d}, fo) : Tensor();
     Tensor dmu = needs("e_mu") ? at::empty({B, H, N}, fo) : Tensor();
     Tensor dnu = needs("e_nu") ? at::empty({B, H, N}, fo) : Tensor();
+    // gradients of the shared cost parameters (reference: sinkhorn_kernel.py:2366-2382)
+    Tensor dxr = (needs("e_x") && xr.defined()) ? at::empty({B, N, 3}, fo) : Tensor();
+    Tensor dpw = (needs("e_pw") && pw.defined() && pb.defined()) ? at::empty({H, 68}, fo) : Tensor();
+    Tensor dwd = (needs("e_wd") && wd.defined() && xr.defined()) ? at::empty({H}, fo) : Tensor();
     Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
     Tensor resid = at::empty({B * H}, fo);
     Tensor status = device_status(Qc.device()).word;
@@ -341,6 +347,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     a.dV = ptr_or_null<float>(dV);
     a.dlog_mu = ptr_or_null<float>(dmu);
     a.dlog_nu = ptr_or_null<float>(dnu);
+    a.dx_res = ptr_or_null<float>(dxr);
+    a.dpos_weight = ptr_or_null<float>(dpw);
+    a.dw_dist = ptr_or_null<float>(dwd);
     a.cg_iters = iters.data_ptr<int32_t>();
     a.cg_residual = resid.data_ptr<float>();
     a.status = status.data_ptr<int32_t>();
@@ -362,6 +371,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     out[0] = cast(dQ);
     out[1] = cast(dK);
     out[2] = cast(dV);
+    out[3] = dxr.defined() ? dxr.to(static_cast<at::ScalarType>(ctx->saved_data["x_dtype"].toInt())) : dxr;
+    out[4] = dpw.defined() ? dpw.to(static_cast<at::ScalarType>(ctx->saved_data["pw_dtype"].toInt())) : dpw;
+    out[7] = dwd.defined() ? dwd.to(static_cast<at::ScalarType>(ctx->saved_data["wd_dtype"].toInt())) : dwd;
     out[8] = dmu;
     out[9] = dnu;
     return out;

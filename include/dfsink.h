@@ -142,7 +142,7 @@ const char* dfs_status_string(int status);
  * reference tests' d = 8) runs on zero-padded copies of the operands made in
  * the workspace (padding adds exact zeros to every product; the logit scale
  * stays 1/sqrt(d)), and the padded columns of O and of the gradients are
- * dropped.  fp32 Q, K, V with 3 d <= 64 are likewise rewritten in the
+ * dropped.  fp32 Q, K, V with d <= 10 are likewise rewritten in the
  * workspace as bf16 hi / lo parts along the contraction dimension
  * ([Qhi Qhi Qlo] [Khi Klo Khi]^T), so that their tensor-core products are exact
  * bf16 products (about 2^-16 relative) rather than tf32 ones (2^-11); the

@@ -77,7 +77,10 @@ def test_host_side_validation(lib):
     assert lib.dfs_workspace_size(odd_d, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
     nd = 2 * 4 * 16 * 32
     assert fb.value == 3 * 2 * nd + 4 * nd  # already multiples of 256
-    assert bb.value == 3 * 2 * nd + 4 * 4 * nd
+    # backward: Q, K, V, dO, dQ, dK, dV copies, then the resident kernels' partials of
+    # the shared-parameter gradients: dx (3 per point), dw and 68 bin sums per CTA
+    bh, cta = 2 * 4, 1
+    assert bb.value == 3 * 2 * nd + 4 * 4 * nd + 4 * (bh * 16 * 3 + bh * cta + bh * cta * 68)
     # the phase API keeps no padded copies between calls
     assert lib.dfs_stream_op(nat.DFS_OP_FWD_INIT, odd_d, None, fake, None, 0, 16, None, 0, None) == \
         nat.DFS_ERR_UNSUPPORTED
