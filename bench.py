@@ -376,7 +376,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) Q/K/V/dO; BASELINE config 2 shapes)",
+            "data": "synthetic (seeded N(0,1) Q/K/V/dO; B=2 H=8 N=384 d=32)",
             "config": {"workload": workload_name(), "global_batch": CFG["B"] * world,
                        "heads": CFG["H"], "seq_len": CFG["N"], "head_dim": CFG["d"],
                        "parallelism": f"(batch,head)-shard x{world}",
@@ -585,7 +585,7 @@ def run_big(args):
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": f"synthetic (seeded N(0,1); BASELINE config {args.config} shapes)",
+            "data": f"synthetic (seeded N(0,1); B={B} H={H} N={N} d={d})",
             "config": {"workload": name, "global_batch": B, "heads": H, "seq_len": N, "head_dim": d,
                        "parallelism": (f"(batch,head)-shard x{world}, length^2-balanced" if args.config == 3
                                        else f"row-shard x{world}, NCCL all-gather per half-iteration"),

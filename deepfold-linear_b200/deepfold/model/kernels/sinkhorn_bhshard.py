@@ -1,6 +1,6 @@
 """(batch, head)-sharded flash Sinkhorn: independent problems spread over GPUs.
 
-BASELINE config 3 (B=8, H=16, padded N=1024, true lengths L_b in [64, 1024])
+The padded variable-length configuration (B=8, H=16, padded N=1024, true lengths L_b in [64, 1024])
 holds B*H independent optimal-transport problems whose cost grows like L_b^2.
 ``partition_problems`` balances that cost over the ranks: the (b, h) pairs are
 ordered by decreasing length (the longest-processing-time rule) and each rank

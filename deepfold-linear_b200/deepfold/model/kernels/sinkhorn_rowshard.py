@@ -1,6 +1,6 @@
 """Row-sharded flash Sinkhorn: one long-sequence problem set over several GPUs.
 
-BASELINE config 4 (B=1, H=16, N=8192, d=64) splits the query rows of every
+The long-sequence configuration (B=1, H=16, N=8192, d=64) splits the query rows of every
 (batch, head) problem evenly over the GPUs of a ``torch.distributed`` group
 (NCCL over NVLink).  Every GPU holds Q, K, V, dO and the marginals in full
 (N x d per head: a few MB) and owns one contiguous range of rows, which is also

@@ -283,8 +283,10 @@ typedef struct {
 int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int row_begin, int row_end,
                        void* workspace, size_t workspace_bytes, const dfs_peer_set* peers, void* stream);
 
-/* Self-test of the tensor-core building blocks: runs the three tcgen05 MMA
- * operand layouts the kernels use on caller-provided data (see csrc). */
+/* TEST-ONLY entry point, not part of the operator surface: runs one of the
+ * three tcgen05 MMA operand layouts the kernels use on caller-provided data
+ * (D = A B^T, M = 64), so the test suite can check each layout against a
+ * plain matrix product.  No counterpart in the reference. */
 int dfs_selftest_mma(int which, const float* A, const float* B, float* D,
                      int M, int N, int K, void* stream);
 

@@ -1,4 +1,4 @@
-"""(batch, head) partition of BASELINE config 3 on CPU: every problem once,
+"""(batch, head) partition of the padded var-len configuration (B=8, H=16, N=1024) on CPU: every problem once,
 contiguous head ranges, and a cost imbalance of at most one problem."""
 
 import random

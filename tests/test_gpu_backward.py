@@ -4,7 +4,7 @@ At converged configurations the reference gradient (autograd through all K
 iterations) and the implicit-function-theorem gradient agree, so the kernel is
 compared with the oracle's unrolled gradient; for unconverged settings it is
 compared with the oracle's IFT gradient, which is what it computes.
-Tolerance: relative error <= 5e-3.
+Tolerance: relative error <= 5e-3 (the gradient bar of the parity criterion).
 """
 
 import numpy as np

@@ -7,7 +7,7 @@
 * a converged balanced case at d=32 against the oracle's unrolled gradient, the
   reference's own autograd semantics;
 * bitwise reproducibility (the bin histogram is summed in fixed point).
-Tolerance: relative error <= 5e-3.
+Tolerance: relative error <= 5e-3 (the gradient bar of the parity criterion).
 """
 
 import math

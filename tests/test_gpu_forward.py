@@ -1,6 +1,6 @@
 """Forward parity of the CUDA flash-Sinkhorn path against the CPU oracle.
 
-Tolerances: output max-abs error <= 2e-3 with bf16
+Tolerances (the parity criterion): output max-abs error <= 2e-3 with bf16
 inputs and fp32 potentials; row and column marginal residuals <= 1e-4.
 """
 

@@ -1,8 +1,8 @@
 """Parity of the streamed kernels (problems beyond the cluster-resident range:
-N > 384 or d = 64, i.e. BASELINE configs 3 and 4) against the CPU oracle.
+N > 384 or d = 64, e.g. the var-len B=8 H=16 N=1024 and long N=8192 configurations) against the CPU oracle.
 
 Same tolerances as the resident path: output max-abs <= 2e-3, marginal
-residuals <= 1e-4.
+residuals <= 1e-4 (the parity criterion).
 """
 
 import numpy as np
