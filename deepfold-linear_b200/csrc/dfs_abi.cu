@@ -35,14 +35,28 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr int kResidentMaxN = 384;
 constexpr int kStreamMaxN = 1 << 16;
 enum { XF_NONE = 0, XF_PAD = 1, XF_SPLIT_QK = 2, XF_SPLIT_V = 3 };
-int xform(const dfs_problem* p) {
+// the fp32 split of a problem (XF_SPLIT_QK / XF_SPLIT_V), or XF_NONE
+int split_kind(const dfs_problem* p) {
   if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_QK && 3 * p->d <= 32) return XF_SPLIT_QK;
   if (p->in_dtype == DFS_F32 && p->cost_mode == DFS_COST_DENSE && 2 * p->d <= 32) return XF_SPLIT_V;
-  return kernel_head_dim(p->d) != p->d ? XF_PAD : XF_NONE;
+  return XF_NONE;
+}
+int kdim(const dfs_problem* p);
+int xform(const dfs_problem* p) {
+  const int x = split_kind(p);
+  if (x != XF_NONE) return x;
+  return kdim(p) != p->d ? XF_PAD : XF_NONE;
+}
+// position / geometry terms of a streamed problem (bits of dfs_problem.cost_terms)
+bool streamed_terms(const dfs_problem* p) {
+  return p->cost_mode == DFS_COST_QK && p->N > kResidentMaxN && (p->cost_terms & (DFS_TERM_POS | DFS_TERM_GEO)) != 0;
 }
 int kdim(const dfs_problem* p) {
-  const int x = xform(p);
-  return kernel_head_dim(x == XF_SPLIT_QK ? 3 * p->d : x == XF_SPLIT_V ? 2 * p->d : p->d);
+  const int x = split_kind(p);
+  const int k = kernel_head_dim(x == XF_SPLIT_QK ? 3 * p->d : x == XF_SPLIT_V ? 2 * p->d : p->d);
+  // streamed problems with cost terms run on the TMA-staged passes, built for
+  // 128- and 256-byte operand rows: head dim 64 (zero-padded from d <= 32)
+  return (k == 32 && streamed_terms(p)) ? 64 : k;
 }
 bool padded(const dfs_problem* p) { return xform(p) != XF_NONE; }
 bool resident(const dfs_problem* p) { return kdim(p) == 32 && p->N <= kResidentMaxN; }
@@ -105,6 +119,7 @@ FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
   q.cost_mode = p->cost_mode; q.K_iter = p->K_iter; q.check_every = p->check_every > 0 ? p->check_every : 1;
   q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
   q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
+  q.cost_terms = p->cost_terms;
   return q;
 }
 
@@ -123,6 +138,7 @@ BwdParams bwd_params(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bw
   q.cg_max_iter = cg->max_iter; q.cg_rtol = cg->rtol; q.cg_atol = cg->atol;
   q.lam = p->lam; q.r_0 = p->r_0;
   q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
+  q.cost_terms = p->cost_terms;
   return q;
 }
 
@@ -142,13 +158,27 @@ int check_fwd_args(const dfs_problem* p, const dfs_fwd_args* a) {
   return DFS_OK;
 }
 
-// streamed path: QK cost with masks, marginals, kappa and warm starts; the
-// position / geometry terms, early stopping and the dense plan are resident-only
+// The position / geometry terms of the streamed path run on the TMA-staged
+// passes only: N >= 128 and N % 4 == 0 (the transposed fp32 copies), operand
+// rows of 128 or 256 bytes.
+bool terms_path_ok(const dfs_problem* p) {
+  const int dk = kdim(p);
+  const int dt = kernel_dtype(p);
+  return p->N >= 128 && p->N % 4 == 0 && (dk == 64 || dt == DFS_F32) && tmap_available();
+}
+
+// streamed path: QK cost with masks, marginals, kappa, warm starts and the
+// position / geometry terms the problem declares; early stopping and the dense
+// plan are resident-only
 int check_stream_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t workspace_bytes) {
-  if (p->cost_mode != DFS_COST_QK || a->pos_weight || a->w_dist || p->threshold > 0.0f || a->T_norm ||
-      (a->x_centroid && !a->O))
+  if (p->cost_mode != DFS_COST_QK || p->threshold > 0.0f || a->T_norm || (a->x_centroid && !a->O))
     return DFS_ERR_UNSUPPORTED;
-  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N, kdim(p)) || !aligned16(workspace))
+  const bool pos = a->pos_weight != nullptr, geo = a->x_res != nullptr && a->w_dist != nullptr;
+  if ((pos && !(p->cost_terms & DFS_TERM_POS)) || (geo && !(p->cost_terms & DFS_TERM_GEO)))
+    return DFS_ERR_INVALID_ARGUMENT;  // the workspace layout depends on the declared terms
+  if ((pos || geo) && !terms_path_ok(p)) return DFS_ERR_UNSUPPORTED;
+  if (workspace == nullptr || workspace_bytes < stream_fwd_workspace(p->B, p->H, p->N, kdim(p), p->cost_terms) ||
+      !aligned16(workspace))
     return DFS_ERR_WORKSPACE;
   return DFS_OK;
 }
@@ -170,10 +200,17 @@ int check_bwd_args(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_
   return DFS_OK;
 }
 
-// streamed path: no position / geometry terms and none of their gradients
+// streamed path: the declared position / geometry terms and the gradients of
+// x_res, pos_weight, w_dist (their shares need the declared workspace)
 int check_stream_bwd(const dfs_problem* p, const dfs_bwd_args* a, void* workspace, size_t workspace_bytes) {
-  if (a->pos_weight || a->w_dist || a->dx_res || a->dpos_weight || a->dw_dist) return DFS_ERR_UNSUPPORTED;
-  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N, kdim(p)) || !aligned16(workspace))
+  const bool pos = a->pos_weight != nullptr, geo = a->x_res != nullptr && a->w_dist != nullptr;
+  if ((pos && !(p->cost_terms & DFS_TERM_POS)) || (geo && !(p->cost_terms & DFS_TERM_GEO)))
+    return DFS_ERR_INVALID_ARGUMENT;
+  const bool shared_grads = a->dx_res != nullptr || a->dpos_weight != nullptr || a->dw_dist != nullptr;
+  if (shared_grads && p->cost_terms == 0) return DFS_ERR_INVALID_ARGUMENT;
+  if ((pos || geo || shared_grads) && !terms_path_ok(p)) return DFS_ERR_UNSUPPORTED;
+  if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N, kdim(p), p->cost_terms) ||
+      !aligned16(workspace))
     return DFS_ERR_WORKSPACE;
   return DFS_OK;
 }
@@ -205,10 +242,10 @@ int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_byte
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   const bool res = resident(p);
   const int dk = kdim(p);
-  if (fwd_bytes) *fwd_bytes = pad_fwd_bytes(p) + (res ? 0 : stream_fwd_workspace(p->B, p->H, p->N, dk));
+  if (fwd_bytes) *fwd_bytes = pad_fwd_bytes(p) + (res ? 0 : stream_fwd_workspace(p->B, p->H, p->N, dk, p->cost_terms));
   if (bwd_bytes)
-    *bwd_bytes = pad_bwd_bytes(p) +
-                 (res ? resident_bwd_workspace(p->B, p->H, p->N, dk) : stream_bwd_workspace(p->B, p->H, p->N, dk));
+    *bwd_bytes = pad_bwd_bytes(p) + (res ? resident_bwd_workspace(p->B, p->H, p->N, dk)
+                                         : stream_bwd_workspace(p->B, p->H, p->N, dk, p->cost_terms));
   return DFS_OK;
 }
 
@@ -311,8 +348,10 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
 int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const dfs_fwd_args* fa,
                   const dfs_bwd_args* ba, int row_begin, int row_end, void* workspace, size_t workspace_bytes,
                   void* stream) {
-  // the phases keep no padded copies between calls: head dims 32 and 64 only
-  if (!dims_ok(p) || !streamed(p) || padded(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  // the phases keep no padded copies between calls (head dims 32 and 64 only) and
+  // take no position / geometry terms (their gradient shares need one GPU's rows)
+  if (!dims_ok(p) || !streamed(p) || padded(p) || (p->cost_terms & (DFS_TERM_POS | DFS_TERM_GEO)))
+    return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
   if (row_begin < 0 || row_end < row_begin || row_end > p->N) return DFS_ERR_INVALID_ARGUMENT;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
@@ -360,7 +399,8 @@ int dfs_peer_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? DFS_OK : DF
 
 int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int row_begin, int row_end,
                        void* workspace, size_t workspace_bytes, const dfs_peer_set* peers, void* stream) {
-  if (!dims_ok(p) || !streamed(p) || padded(p)) return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  if (!dims_ok(p) || !streamed(p) || padded(p) || (p->cost_terms & (DFS_TERM_POS | DFS_TERM_GEO)))
+    return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
   if (op < DFS_OP_FWD_INIT || op > DFS_OP_FWD_OUT || peers == nullptr) return DFS_ERR_INVALID_ARGUMENT;
   if (row_begin < 0 || row_end < row_begin || row_end > p->N) return DFS_ERR_INVALID_ARGUMENT;
   if (peers->npeers < 1 || peers->npeers > DFS_MAX_PEERS || peers->self < 0 || peers->self >= peers->npeers)

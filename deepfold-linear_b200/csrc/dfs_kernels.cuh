@@ -23,6 +23,32 @@ DFS_DEV float load_f32(const void* p, size_t i, int dtype) {
   return reinterpret_cast<const float*>(p)[i];
 }
 
+// Optional cost terms on the streamed passes.  Each element (r, c) of a pass
+// (rows r, columns c of S = A B^T; for the passes on S^T the rows are the cost's
+// columns) adds, in log2 units,
+//     pwS[bins(r, c)] + wS * t(r, c),  t = dist / (r_0 + dist),
+//     dist = sqrt(|x_r - x_c|^2 + 1e-8)            (sinkhorn_kernel.py:59-129)
+// with pwS = -pos_weight[h] log2(e) / eps_h and wS = -w_h log2(e) / eps_h.  The
+// bins come from a per-call uint8 table in the pass's orientation (rows of
+// kBinRow bytes; entries outside [0, 68), and the padding, hold 68, a bin
+// whose weight is 0); the distance is computed from the coordinates.
+constexpr int kBinCount = 68;
+struct CostTerms {
+  const uint8_t* bins;      // (B, N, bin_stride) uint8 in the pass's orientation, or null
+  int bin_stride;           // bytes per row of the table (N rounded up to 128)
+  const float* pos_weight;  // (H, 68) with bins
+  const float* x;           // (B, N, 3) coordinates with the geometry term, or null
+  const float* w_dist;      // (H,) with x
+  float r_0;
+};
+// Shares of the shared-parameter gradients written by the streamed gradient
+// passes (null: not wanted), summed by stream_costgrad_finalize.
+struct CostGradOut {
+  float* dx;    // (BH, N, 3) this pass's share of dx per row
+  float* dw;    // (BH, N) per-row share of dw_dist
+  float* dpos;  // (BH, row blocks, 68) per-CTA bin sums
+};
+
 struct FwdParams {
   const void* Q;
   const void* K;
@@ -47,6 +73,7 @@ struct FwdParams {
   int B, H, N, d, in_dtype, cost_mode, K_iter, check_every;
   float lam, r_0, threshold;
   float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
+  int cost_terms;          // DFS_TERM_* declared by the problem (workspace layout of the streamed path)
 };
 
 struct BwdParams {
@@ -80,6 +107,7 @@ struct BwdParams {
   int B, H, N, d, in_dtype, cg_max_iter;
   float lam, r_0, cg_rtol, cg_atol;
   float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
+  int cost_terms;          // DFS_TERM_* declared by the problem (workspace layout of the streamed path)
 };
 
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
@@ -95,10 +123,20 @@ struct PeerInfo {
 cudaError_t stream_fwd_op(int op, const FwdParams& p, float* ws, int r0, int r1, cudaStream_t st,
                           const PeerInfo* peers = nullptr);
 cudaError_t stream_bwd_op(int op, const BwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
-size_t stream_fwd_workspace(int B, int H, int N, int d);
+size_t stream_fwd_workspace(int B, int H, int N, int d, int terms = 0);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
 cudaError_t launch_stream_bwd(const BwdParams& p, float* ws, cudaStream_t st);
-size_t stream_bwd_workspace(int B, int H, int N, int d);
+size_t stream_bwd_workspace(int B, int H, int N, int d, int terms = 0);
+// Per-call tables of the cost terms (dfs_stream.cu): bytes of one uint8 bin
+// table, and the launch that builds the table and its transpose.
+size_t cost_bins_bytes(int B, int N);
+int cost_bin_stride(int N);
+cudaError_t build_cost_bins(const int32_t* pos_bins, int B, int N, uint8_t* bins, uint8_t* bins_t, cudaStream_t st);
+// The cost terms of a pass from the operator's inputs (position term when
+// pos_weight and the tables are given, geometry term when x_res and w_dist
+// are): `transposed` for the passes on S^T, whose rows are the cost's columns.
+CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float* w_dist, float r_0, int N,
+                        const uint8_t* bins, const uint8_t* bins_t, bool transposed);
 size_t resident_bwd_smem(int N, int d);
 size_t resident_bwd_workspace(int B, int H, int N, int d);
 // TMA-staged row passes of the streamed path (dfs_stream_tma.cu): one launch
@@ -133,6 +171,7 @@ struct TileArgs {
   int B, H, N, row_begin, row_end;
   float lam;
   float qk_scale;          // 1/sqrt(d) of the cost
+  CostTerms ct;            // optional cost terms in this pass's orientation (bins / x null: none)
 };
 size_t tile_split_bytes(int B, int H, int N);
 // Per batch element, the smallest range [lo, hi) of positions holding every
@@ -145,6 +184,8 @@ cudaError_t tile_split_reset(float* split, int B, int H, int N, cudaStream_t st)
 // (N >= 128) and the two operand addresses (16-byte aligned); otherwise the
 // register-staged kernels run the pass.
 bool tile_path_ok(int dtype, int d, int N, const void* a, const void* b);
+// True when the driver provides cuTensorMapEncodeTiled (the TMA-staged passes).
+bool tmap_available();
 cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st);
 
 // TMA-staged tile passes of the streamed backward (dfs_stream_bwd_tma.cu) on
@@ -183,6 +224,8 @@ struct BtArgs {
   const int2* extent;      // (B) valid extents of the mask, or null
   int B, H, N, row_begin, row_end;
   float qk_scale;          // 1/sqrt(d) of the cost
+  CostTerms ct;            // optional cost terms in this pass's orientation
+  CostGradOut cg;          // DQ / DK / COL: shares of the shared-parameter gradients, or null
 };
 enum BtPass { BTP_ROW = 0, BTP_COL = 1, BTP_DQ = 2, BTP_DK = 3, BTP_OUT = 4 };
 size_t bt_copies_bytes(int B, int H, int N, int d);

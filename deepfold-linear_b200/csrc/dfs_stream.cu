@@ -332,21 +332,79 @@ cudaError_t launch_stream(int mode, int d, const StreamParams& p, cudaStream_t s
   return cudaErrorInvalidValue;
 }
 
-// f, g (log2), m, R; then fp32 copies Q, K (row-major) and V^T (transposed)
-// for the TMA-staged transport-output pass
-// ... then the column-split scratch, a 64-byte slot whose first 8 bytes are
-// the peer-exchange arrival counter, and the mask's valid extent per batch element
-size_t stream_fwd_workspace(int B, int H, int N, int d) {
-  const size_t n = static_cast<size_t>(B) * H * N;
-  return 4 * sizeof(float) * n + 256 + 3 * sizeof(float) * n * d + 256 + tile_split_bytes(B, H, N) + 128 +
-         sizeof(int2) * static_cast<size_t>(B);
+// ---------------------------------------------------------------- cost-term tables
+int cost_bin_stride(int N) { return (N + 127) / 128 * 128; }
+size_t cost_bins_bytes(int B, int N) { return static_cast<size_t>(B) * N * cost_bin_stride(N); }
+
+// pos_bins (B, N, N) int32 -> table (B, N, stride) uint8 and its transpose
+// (entry [b][j][i] = bins[b][i][j]); bins outside [0, 68) and the padding
+// columns hold 68, whose weight the passes take as 0.  32 x 32 tiles through
+// shared memory, one block per tile of the (stride x stride) square.
+__global__ void cost_bins_kernel(const int32_t* __restrict__ bins, int N, int stride, uint8_t* __restrict__ t,
+                                 uint8_t* __restrict__ tt) {
+  __shared__ uint8_t tile[32][33];
+  const size_t b = blockIdx.z;
+  const int i0 = blockIdx.y * 32, j0 = blockIdx.x * 32, tx = threadIdx.x;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int i = i0 + r, j = j0 + tx;
+    uint8_t v = kBinCount;
+    if (i < N && j < N) {
+      const unsigned x = static_cast<unsigned>(bins[(b * N + i) * N + j]);
+      v = x < static_cast<unsigned>(kBinCount) ? static_cast<uint8_t>(x) : static_cast<uint8_t>(kBinCount);
+    }
+    if (i < N && j < stride) t[(b * N + i) * stride + j] = v;
+    tile[r][tx] = v;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int j = j0 + r, i = i0 + tx;
+    if (j < N && i < stride) tt[(b * N + j) * stride + i] = tile[tx][r];
+  }
+}
+
+cudaError_t build_cost_bins(const int32_t* pos_bins, int B, int N, uint8_t* bins, uint8_t* bins_t, cudaStream_t st) {
+  const int stride = cost_bin_stride(N);
+  cost_bins_kernel<<<dim3(stride / 32, stride / 32, B), dim3(32, 8), 0, st>>>(pos_bins, N, stride, bins, bins_t);
+  return cudaGetLastError();
 }
 
 namespace {
 float* align256(float* p) {
   return reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
 }
+size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 }  // namespace
+
+// f, g (log2), m, R; then fp32 copies Q, K (row-major) and V^T (transposed)
+// for the TMA-staged transport-output pass
+// ... then the column-split scratch, a 64-byte slot whose first 8 bytes are
+// the peer-exchange arrival counter, the mask's valid extent per batch element,
+// and, with the position term, the uint8 bin table and its transpose
+size_t stream_fwd_workspace(int B, int H, int N, int d, int terms) {
+  const size_t n = static_cast<size_t>(B) * H * N;
+  size_t bytes = 4 * sizeof(float) * n + 256 + 3 * sizeof(float) * n * d + 256 + tile_split_bytes(B, H, N) + 128 +
+                 sizeof(int2) * static_cast<size_t>(B);
+  if (terms & DFS_TERM_POS) bytes += 256 + 2 * round256(cost_bins_bytes(B, N));
+  return bytes;
+}
+
+// The cost terms of a pass from the forward / backward inputs: `transposed` for
+// the passes on S^T (their rows are the cost's columns).
+CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float* w_dist, float r_0, int N,
+                        const uint8_t* bins, const uint8_t* bins_t, bool transposed) {
+  CostTerms c{};
+  if (pos_weight != nullptr && bins != nullptr) {
+    c.bins = transposed ? bins_t : bins;
+    c.bin_stride = cost_bin_stride(N);
+    c.pos_weight = pos_weight;
+  }
+  if (x_res != nullptr && w_dist != nullptr) {
+    c.x = x_res;
+    c.w_dist = w_dist;
+  }
+  c.r_0 = r_0;
+  return c;
+}
 
 // One phase of the streamed forward on rows [r0, r1) (the whole problem for a
 // single GPU; a row range per GPU when the rows are sharded, with the
@@ -372,6 +430,15 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     return static_cast<char*>(peers->ws[k]) + (static_cast<const char*>(own) - reinterpret_cast<char*>(ws));
   };
   int2* extents = reinterpret_cast<int2*>(reinterpret_cast<char*>(counter) + 64);
+  uint8_t* bins = nullptr;  // position-bin tables (row orientation, transposed)
+  uint8_t* bins_t = nullptr;
+  if (fp.cost_terms & DFS_TERM_POS) {
+    bins = reinterpret_cast<uint8_t*>(align256(reinterpret_cast<float*>(extents + fp.B)));
+    bins_t = bins + round256(cost_bins_bytes(fp.B, fp.N));
+  }
+  auto terms = [&](bool transposed) {
+    return cost_terms_of(fp.pos_weight, fp.x_res, fp.w_dist, fp.r_0, fp.N, bins, bins_t, transposed);
+  };
   unsigned long long* cnts[DFS_MAX_PEERS] = {};
   if (peers != nullptr)
     for (int k = 0; k < peers->npeers; ++k) cnts[k] = reinterpret_cast<unsigned long long*>(at_peer(k, counter));
@@ -382,6 +449,8 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = tile_split_reset(split, fp.B, fp.H, fp.N, st);
     if (e == cudaSuccess) e = compute_extents(fp.mask, fp.B, fp.N, extents, st);
+    if (e == cudaSuccess && bins != nullptr && fp.pos_bins != nullptr)
+      e = build_cost_bins(fp.pos_bins, fp.B, fp.N, bins, bins_t, st);
     if (e == cudaSuccess && peers != nullptr) e = peer_signal(cnts, peers->npeers, st);
     return e;
   }
@@ -426,6 +495,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     ta.row_marg = rows ? fp.log_mu : fp.log_nu;
     ta.row_out = rows ? fw : gw;
     ta.row_out_nat = rows ? fp.log_u : fp.log_v;
+    ta.ct = terms(!rows);
     if (peers != nullptr) {
       ta.npeers = peers->npeers;
       for (int k = 0; k < peers->npeers; ++k) {
@@ -469,6 +539,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
       ta.row_bias = fw;
       ta.row_out = mw;
       ta.row_R = Rw;
+      ta.ct = terms(false);
       e = launch_tile_pass(TL_ROWSTATS, ta, st);
       if (e != cudaSuccess) return e;
       if (bt_path_ok(fp.d, fp.N, ws)) {
@@ -502,6 +573,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
         ba.acc_scale = 1.0f;
         ba.status = fp.status;
         ba.extent = ta.extent;
+        ba.ct = terms(false);
         ba.B = fp.B;
         ba.H = fp.H;
         ba.N = fp.N;

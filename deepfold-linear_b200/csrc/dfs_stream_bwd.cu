@@ -630,11 +630,62 @@ __global__ void __launch_bounds__(kVThreads) sb_final_kernel(VecParams p) {
 }
 
 // Slots, per-problem scalars, CG flags and iteration counts, then the fp32
-// operand copies of the TMA-staged tile passes.
-size_t stream_bwd_workspace(int B, int H, int N, int d) {
+// operand copies of the TMA-staged tile passes, the column-split scratch, the
+// mask's valid extents; with cost terms, the bin tables (position term) and
+// the shares of the shared-parameter gradients (CostGradWs below).
+namespace {
+size_t rnd256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+// dx shares of the three gradient passes (rows, columns, centroid), the per-row
+// dw share, the per-CTA bin sums
+size_t costgrad_floats(int B, int H, int N) {
   const size_t n = static_cast<size_t>(B) * H * N, bh = static_cast<size_t>(B) * H;
-  return sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256 + bt_copies_bytes(B, H, N, d) +
-         256 + tile_split_bytes(B, H, N) + 64 + sizeof(int2) * static_cast<size_t>(B);
+  return 3 * 3 * n + n + bh * ((N + 127) / 128) * kBinCount;
+}
+}  // namespace
+
+size_t stream_bwd_workspace(int B, int H, int N, int d, int terms) {
+  const size_t n = static_cast<size_t>(B) * H * N, bh = static_cast<size_t>(B) * H;
+  size_t bytes = sizeof(float) * (WS_NUM * n + SC_NUM * bh) + 2 * sizeof(int32_t) * bh + 256 +
+                 bt_copies_bytes(B, H, N, d) + 256 + tile_split_bytes(B, H, N) + 64 + sizeof(int2) * static_cast<size_t>(B);
+  if (terms & DFS_TERM_POS) bytes += 256 + 2 * rnd256(cost_bins_bytes(B, N));
+  if (terms) bytes += 256 + sizeof(float) * costgrad_floats(B, H, N);
+  return bytes;
+}
+
+// Sums of the gradient shares in a fixed order: dx_res over heads (the row,
+// column and centroid shares whose bits are set in `shares`), dw_dist over
+// batch elements and rows, dpos_weight over batch elements and row blocks.
+__global__ void stream_costgrad_finalize(const float* dx_row, const float* dx_col, const float* dx_t,
+                                         const float* dw, const float* dpos, int shares, int B, int H, int N,
+                                         float* dx_res, float* dw_dist, float* dpos_weight) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nrb = (N + 127) / 128;
+  const int ndx = dx_res != nullptr ? B * N * 3 : 0;
+  const int ndw = dw_dist != nullptr ? H : 0;
+  const int npos = dpos_weight != nullptr ? H * kBinCount : 0;
+  if (t < ndx) {
+    const int b = t / (N * 3), rem = t % (N * 3);
+    float s = 0.0f;
+    for (int h = 0; h < H; ++h) {
+      const size_t o = (static_cast<size_t>(b) * H + h) * N * 3 + rem;
+      if (shares & 1) s += dx_row[o];
+      if (shares & 2) s += dx_col[o];
+      if (shares & 4) s += dx_t[o];
+    }
+    dx_res[t] = s;
+  } else if (t < ndx + ndw) {
+    const int h = t - ndx;
+    float s = 0.0f;
+    for (int b = 0; b < B; ++b)
+      for (int i = 0; i < N; ++i) s += dw[(static_cast<size_t>(b) * H + h) * N + i];
+    dw_dist[h] = s;
+  } else if (t < ndx + ndw + npos) {
+    const int u = t - ndx - ndw, h = u / kBinCount, bin = u % kBinCount;
+    float s = 0.0f;
+    for (int b = 0; b < B; ++b)
+      for (int r = 0; r < nrb; ++r) s += dpos[((static_cast<size_t>(b) * H + h) * nrb + r) * kBinCount + bin];
+    dpos_weight[u] = s;
+  }
 }
 
 constexpr bool same_slot(int a, int b) { return a == b; }
@@ -720,6 +771,29 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   int2* extents = reinterpret_cast<int2*>(
       (reinterpret_cast<uintptr_t>(split) + tile_split_bytes(B, H, N) + 63) & ~uintptr_t(63));
   const int2* ext = bp.mask != nullptr ? extents : nullptr;
+  // cost-term tables and gradient shares, after the extents
+  uint8_t* bins = nullptr;
+  uint8_t* bins_t = nullptr;
+  float* cgw = nullptr;
+  {
+    uint8_t* q8 = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(extents + B) + 255) & ~uintptr_t(255));
+    if (bp.cost_terms & DFS_TERM_POS) {
+      bins = q8;
+      bins_t = bins + rnd256(cost_bins_bytes(B, N));
+      q8 = bins_t + rnd256(cost_bins_bytes(B, N));
+    }
+    if (bp.cost_terms) cgw = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(q8) + 255) & ~uintptr_t(255));
+  }
+  const bool geo = bp.x_res != nullptr && bp.w_dist != nullptr;
+  auto terms = [&](bool transposed) {
+    return cost_terms_of(bp.pos_weight, geo ? bp.x_res : nullptr, bp.w_dist, bp.r_0, N, bins, bins_t, transposed);
+  };
+  float* cg_dx_row = cgw;
+  float* cg_dx_col = cgw ? cgw + 3 * n : nullptr;
+  float* cg_dx_t = cgw ? cgw + 6 * n : nullptr;
+  float* cg_dw = cgw ? cgw + 9 * n : nullptr;
+  float* cg_dpos = cgw ? cgw + 10 * n : nullptr;
+  const bool want_dx = cgw != nullptr && bp.dx_res != nullptr;
   BtArgs ba{};
   ba.d = d;
   ba.eps = bp.eps;
@@ -749,6 +823,8 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       if (e == cudaSuccess && bt) e = bt_prep(bp, cp, st);
       if (e == cudaSuccess) e = tile_split_reset(split, B, H, N, st);
       if (e == cudaSuccess) e = compute_extents(bp.mask, B, N, extents, st);
+      if (e == cudaSuccess && bins != nullptr && bp.pos_bins != nullptr)
+        e = build_cost_bins(bp.pos_bins, B, N, bins, bins_t, st);
       return e;
     }
     case DFS_OP_BWD_ROWSTATS:  // m, R, D
@@ -759,6 +835,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ba.xvec = bp.dxc ? bp.x_res : nullptr; ba.xvec_per_head = 0;
         ba.rxvec = bp.dxc; ba.rxvec_per_head = 1;
         ba.out0 = slot(WS_M); ba.out1 = slot(WS_R); ba.out2 = slot(WS_D);
+        ba.ct = terms(false);
         return launch_bt_pass(BTP_ROW, ba, st);
       }
       q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V;
@@ -780,6 +857,8 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ba.rxvec = bp.dxc ? bp.x_res : nullptr; ba.rxvec_per_head = 0;
         ba.out0 = slot(WS_C); ba.out1 = slot(WS_GV);
         ba.acc = bp.dV; ba.acc_scale = 1.0f;
+        ba.ct = terms(true);
+        if (want_dx && bp.dxc != nullptr) ba.cg.dx = cg_dx_t;  // centroid share T_norm^T dxc
         return launch_bt_pass(BTP_COL, ba, st);
       }
       q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
@@ -802,6 +881,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ta.row_bias = slot(WS_F); ta.row_scale = op == DFS_OP_BWD_P_U ? slot(WS_D1I) : nullptr;
         ta.done = op == DFS_OP_BWD_P_U ? v.done : nullptr;
         ta.row_out = slot(op == DFS_OP_BWD_P_U ? WS_T : WS_S);
+        ta.ct = terms(false);
         return launch_tile_pass(TL_MATVEC, ta, st);
       }
       q.Aop = bp.Q; q.Bop = bp.K;
@@ -818,6 +898,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ta.row_bias = slot(WS_G);
         ta.done = v.done;
         ta.row_out = slot(WS_S);
+        ta.ct = terms(true);
         return launch_tile_pass(TL_MATVEC, ta, st);
       }
       q.Aop = bp.K; q.Bop = bp.Q;
@@ -841,6 +922,10 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ba.xvec = bp.dxc ? bp.x_res : nullptr; ba.xvec_per_head = 0;
         ba.rxvec = bp.dxc; ba.rxvec_per_head = 1;
         ba.acc = bp.dQ; ba.acc_scale = -1.0f;
+        ba.ct = terms(false);
+        if (want_dx && geo) ba.cg.dx = cg_dx_row;
+        if (cgw != nullptr && bp.dw_dist != nullptr && geo) ba.cg.dw = cg_dw;
+        if (cgw != nullptr && bp.dpos_weight != nullptr && bins != nullptr) ba.cg.dpos = cg_dpos;
         return launch_bt_pass(BTP_DQ, ba, st);
       }
       q.Aop = bp.Q; q.Bop = bp.K; q.A2op = bp.dO; q.a2_f32 = 1; q.B2op = bp.V; q.B3op = bp.K;
@@ -861,7 +946,24 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ba.xvec = bp.dxc; ba.xvec_per_head = 1;
         ba.rxvec = bp.dxc ? bp.x_res : nullptr; ba.rxvec_per_head = 0;
         ba.acc = bp.dK; ba.acc_scale = -1.0f;
-        return launch_bt_pass(BTP_DK, ba, st);
+        ba.ct = terms(true);
+        if (want_dx && geo) ba.cg.dx = cg_dx_col;
+        cudaError_t e = launch_bt_pass(BTP_DK, ba, st);
+        if (e != cudaSuccess || cgw == nullptr) return e;
+        // the shared-parameter gradients from the shares of the DQ, DK and COL passes
+        const int shares = (want_dx && geo ? 3 : 0) | (want_dx && bp.dxc != nullptr ? 4 : 0);
+        float* dx_out = want_dx ? bp.dx_res : nullptr;
+        float* dw_out = geo ? bp.dw_dist : nullptr;
+        float* dpos_out = bins != nullptr ? bp.dpos_weight : nullptr;
+        if (dx_out != nullptr && shares == 0) {  // x_res enters neither the cost nor the loss
+          if ((e = cudaMemsetAsync(dx_out, 0, sizeof(float) * B * N * 3, st)) != cudaSuccess) return e;
+          dx_out = nullptr;
+        }
+        const int cnt = (dx_out ? B * N * 3 : 0) + (dw_out ? H : 0) + (dpos_out ? H * kBinCount : 0);
+        if (cnt == 0) return cudaSuccess;
+        stream_costgrad_finalize<<<(cnt + 255) / 256, 256, 0, st>>>(cg_dx_row, cg_dx_col, cg_dx_t, cg_dw, cg_dpos,
+                                                                    shares, B, H, N, dx_out, dw_out, dpos_out);
+        return cudaGetLastError();
       }
       q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;
       q.B3op = bp.Q; q.B4op = bp.dO; q.b4_f32 = 1;

@@ -67,9 +67,17 @@ struct BTileParams {
   const int2* extent;     // (B) valid extents of the mask, or null (scan the mask)
   int B, H, N, row_begin, row_end;
   float qk_scale;         // 1/sqrt(d) of the cost
+  CostTerms ct;           // optional position / geometry terms in this pass's orientation
+  CostGradOut cg;         // DQ / DK / COL: shares of the shared-parameter gradients (null: none)
 };
 
-template <int MODE, int D>
+// Fixed point of the per-warp bin histograms: a warp's largest |dC| so far
+// maps below 2^kHistBits, so the sum of its at most 32 rows x 16 columns x
+// 1024 tiles (2^19) terms stays below 2^59.  A larger maximum later shifts the
+// sums right (deterministically) to the new scale.
+constexpr int kHistBits = 40;
+
+template <int MODE, int D, bool TERMS = false>
 struct BTileCfg {
   static constexpr bool kAcc = MODE != BT_ROW;
   static constexpr bool kDT = MODE != BT_OUT;        // second product dT = A2 B2^T
@@ -78,7 +86,7 @@ struct BTileCfg {
   static constexpr uint32_t BTILE = 64u * D * 4;     // 64-row operand
   static constexpr uint32_t B3TILE = 64u * D * 4;    // d rows x 64 columns
   static constexpr int NS = 2, NS3 = 2;
-  static constexpr int NVEC = 8;                     // tv0..4, x 3-vector
+  static constexpr int NVEC = TERMS ? 11 : 8;        // tv0..4, x 3-vector (+ the columns' coordinates)
   static constexpr uint32_t VEC = NVEC * kBTW * 4;
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_A2 = ATILE;
@@ -87,8 +95,13 @@ struct BTileCfg {
   static constexpr uint32_t OFF_B3 = OFF_B + NS * SB;
   static constexpr uint32_t OFF_DS = OFF_B3 + (kAcc ? NS3 * B3TILE : 0u);   // 128 x 64 fp32
   static constexpr uint32_t OFF_VEC = OFF_DS + (kAcc ? 128u * kBTW * 4 : 0u);
-  static constexpr uint32_t OFF_MRG = OFF_VEC + NS * VEC;                // 3 parts x 3 values x 128
-  static constexpr uint32_t OFF_BAR = OFF_MRG + 3 * 3 * 128 * 4;
+  static constexpr int NMRG = TERMS ? 4 : 3;                          // values merged per row
+  static constexpr uint32_t OFF_MRG = OFF_VEC + NS * VEC;                // 3 parts x NMRG values x 128
+  static constexpr uint32_t OFF_PW = OFF_MRG + 3 * NMRG * 128 * 4;       // TERMS: 69 scaled bin weights
+  static constexpr bool kHist = TERMS && MODE == BT_DQ;
+  static constexpr uint32_t OFF_HIST = OFF_PW + (TERMS ? 288u : 0u);     // DQ: 16 warps x 68 int64 bin sums
+  static constexpr uint32_t OFF_HF = OFF_HIST + (kHist ? kBEpiWarps * 68u * 8u : 0u);  // DQ: 16 x 68 floats
+  static constexpr uint32_t OFF_BAR = OFF_HF + (kHist ? kBEpiWarps * 68u * 4u : 0u);
   static constexpr uint32_t NBAR = 2 * NS + 2 * NS3 + 4 + 3;          // + sfull/sempty x2, ds x2, a
   static constexpr uint32_t OFF_SLOT = OFF_BAR + 8 * NBAR;
   static constexpr uint32_t OFF_RED = OFF_SLOT + 16;
@@ -96,9 +109,9 @@ struct BTileCfg {
   static_assert(SMEM <= 232448u, "shared memory");
 };
 
-template <int MODE, int D>
+template <int MODE, int D, bool TERMS>
 __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_constant__ BTileParams p) {
-  using C = BTileCfg<MODE, D>;
+  using C = BTileCfg<MODE, D, TERMS>;
   constexpr bool kAcc = C::kAcc, kDT = C::kDT;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch (see launch_dependent)
   extern __shared__ uint8_t smem_raw[];
@@ -223,6 +236,11 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
             pv[h][5 + x] = (p.xvec != nullptr && cin)
                                ? p.xvec[((p.xvec_per_head ? bh : static_cast<size_t>(bb)) * N + j) * 3 + x]
                                : 0.0f;
+          if constexpr (TERMS) {
+#pragma unroll
+            for (int x = 0; x < 3; ++x)
+              pv[h][8 + x] = (p.ct.x != nullptr && cin) ? p.ct.x[(static_cast<size_t>(bb) * N + j) * 3 + x] : 0.0f;
+          }
         }
       };
       fetch(0);
@@ -329,6 +347,36 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       for (int c = 0; c < 3; ++c) rx[c] = p.rxvec[o * 3 + c];
     }
     const uint32_t tlane = static_cast<uint32_t>(32 * quad) << 16;
+    // optional cost terms: bin weights scaled to -log2(e)/eps (entry 68: 0), this
+    // row's coordinates; gradient shares of the shared cost parameters
+    float* pws = reinterpret_cast<float*>(base + C::OFF_PW);
+    const bool use_bins = TERMS && p.ct.bins != nullptr, use_geo = TERMS && p.ct.x != nullptr;
+    float xi[3] = {0.0f, 0.0f, 0.0f}, wS = 0.0f, w_h = 0.0f;
+    const uint8_t* brow = nullptr;
+    float gdx[3] = {0.0f, 0.0f, 0.0f}, gdw = 0.0f;  // this row's dx share and dw share (this part)
+    const bool want_geo_grad = TERMS && use_geo && (p.cg.dx != nullptr || p.cg.dw != nullptr) &&
+                               (MODE == BT_DQ || MODE == BT_DK);
+    const bool want_hist = C::kHist && use_bins && p.cg.dpos != nullptr;
+    const bool want_cent_grad = MODE == BT_COL && p.cg.dx != nullptr && p.xvec != nullptr;
+    const float inv_eps = 1.0f / eps_h;
+    unsigned long long* whist = reinterpret_cast<unsigned long long*>(base + C::OFF_HIST) + warp * 68;
+    int e_cur = -1000;  // exponent of this warp's histogram scale (-1000: nothing added yet)
+    if constexpr (TERMS) {
+      const float nsc = -kLog2e * inv_eps;
+      if (use_bins && tid <= kBinCount) pws[tid] = tid < kBinCount ? p.ct.pos_weight[hh * kBinCount + tid] * nsc : 0.0f;
+      if (use_geo) {
+        w_h = p.ct.w_dist[hh];
+        wS = w_h * nsc;
+        if (rin) {
+#pragma unroll
+          for (int c = 0; c < 3; ++c) xi[c] = p.ct.x[(static_cast<size_t>(bb) * N + row) * 3 + c];
+        }
+      }
+      if (use_bins && rin) brow = p.ct.bins + (static_cast<size_t>(bb) * N + row) * p.ct.bin_stride;
+      if (want_hist)
+        for (int b2 = lane; b2 < 68; b2 += 32) whist[b2] = 0ull;
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kBEpiWarps) : "memory");  // pws written
+    }
     // running results of this column part (BT_OUT: the three x_centroid sums)
     float m = MODE == BT_OUT ? 0.0f : kNeg, s0 = 0.0f, s1 = 0.0f;
     const float out_fm = rv[0] - rv[1];              // BT_OUT: f_i - m_i
@@ -337,6 +385,8 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
 #pragma unroll 1
     for (int u = 0; u < ntiles; ++u) {
       const int s = u % C::NS, b = u & 1;
+      uint4 bq = make_uint4(0u, 0u, 0u, 0u);  // this row's 16 bins of the tile's part (loaded ahead)
+      if (TERMS && brow != nullptr) bq = __ldg(reinterpret_cast<const uint4*>(brow + (t_begin + u) * kBTW + 16 * part));
       if (!mbar_wait(&full[s], (u / C::NS) & 1)) err = 1;  // vectors
       if (!mbar_wait(&sfull[b], (u >> 1) & 1)) err = 1;
       tc_fence_after();
@@ -347,6 +397,29 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[b]);
       const float* vb = vecs + s * (C::VEC / 4) + 16 * part;
+      // the cost terms of this row's 16 columns (log2 units), 0 without terms
+      float tm[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) tm[k] = 0.0f;
+      if constexpr (TERMS) {
+        const uint32_t bw[4] = {bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          float t = 0.0f;
+          if (use_bins) t = pws[(bw[k >> 2] >> (8 * (k & 3))) & 0xffu];
+          if (use_geo) {
+            const float d0 = xi[0] - vb[8 * kBTW + k], d1 = xi[1] - vb[9 * kBTW + k], d2 = xi[2] - vb[10 * kBTW + k];
+            const float dist = sqrtf(fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, 1e-8f))));
+            t = fmaf(wS, __fdividef(dist, p.ct.r_0 + dist), t);
+          }
+          tm[k] = t;
+        }
+      }
+      // adds this column's term (compile-time nothing without TERMS)
+      auto with_term = [&](float x, int k) {
+        if constexpr (TERMS) return x + tm[k];
+        else return x;
+      };
       float dt[16];
       if constexpr (kDT) {
 #pragma unroll
@@ -359,7 +432,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       if constexpr (MODE == BT_ROW) {
         // rv0 = f_i; tv0 = g_j
 #pragma unroll
-        for (int k = 0; k < 16; ++k) sv[k] = fmaf(sv[k], scale, vb[k] + rv[0]);
+        for (int k = 0; k < 16; ++k) sv[k] = with_term(fmaf(sv[k], scale, vb[k] + rv[0]), k);
         float mx[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) mx[q] = fmaxf(fmaxf(sv[4 * q], sv[4 * q + 1]), fmaxf(sv[4 * q + 2], sv[4 * q + 3]));
@@ -379,18 +452,26 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
         // thread = column j: rv0 = g_j; tile i: tv0 = f, tv1 = f - m, tv2 = 1/(R+1e-6), tv3 = D
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          const float sc = fmaf(sv[k], scale, rv[0]);
+          const float sc = with_term(fmaf(sv[k], scale, rv[0]), k);
           const float P = ex2(sc + vb[k]);
           const float T = ex2(sc + vb[kBTW + k]) * vb[2 * kBTW + k];
           s0 += P;
           s1 = fmaf(T, dt[k] - vb[3 * kBTW + k], s1);
           out[k] = rok ? T : 0.0f;
         }
+        if (want_cent_grad) {  // centroid share: dx_j += sum_i T_ij dxc_i (dxc staged as the tile's 3-vectors)
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            gdx[0] = fmaf(out[k], vb[5 * kBTW + k], gdx[0]);
+            gdx[1] = fmaf(out[k], vb[6 * kBTW + k], gdx[1]);
+            gdx[2] = fmaf(out[k], vb[7 * kBTW + k], gdx[2]);
+          }
+        }
       } else if constexpr (MODE == BT_DQ) {
         // rv0 = f, rv1 = f - m, rv2 = 1/(R+1e-6), rv3 = D, rv4 = w1; tv0 = g, tv1 = w2
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          const float sc = fmaf(sv[k], scale, vb[k]);
+          const float sc = with_term(fmaf(sv[k], scale, vb[k]), k);
           const float P = ex2(sc + rv[0]);
           const float T = ex2(sc + rv[1]) * rv[2];
           out[k] = rok ? T * (dt[k] - rv[3]) - P * (rv[4] + vb[kBTW + k]) : 0.0f;
@@ -399,7 +480,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
         // rv0 = f, rv1 = m, rv2 = R (rows); tv0 = g, tv 5..7 = x_j
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          const float T = rok ? ex2(fmaf(sv[k], scale, vb[k]) + out_fm) * out_inv : 0.0f;
+          const float T = rok ? ex2(with_term(fmaf(sv[k], scale, vb[k]) + out_fm, k)) * out_inv : 0.0f;
           out[k] = T;
           if (col_x) {
             m = fmaf(T, vb[5 * kBTW + k], m);
@@ -412,10 +493,59 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
         // tv3 = D, tv4 = w1
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
-          const float sc = fmaf(sv[k], scale, rv[0]);
+          const float sc = with_term(fmaf(sv[k], scale, rv[0]), k);
           const float P = ex2(sc + vb[k]);
           const float T = ex2(sc + vb[kBTW + k]) * vb[2 * kBTW + k];
           out[k] = rok ? T * (dt[k] - vb[3 * kBTW + k]) - P * (vb[4 * kBTW + k] + rv[1]) : 0.0f;
+        }
+      }
+      if constexpr (TERMS && (MODE == BT_DQ || MODE == BT_DK)) {
+        // gradient shares from dS (natural units; dC = -dS / eps): geometry per row
+        // (DQ: rows i, columns j; DK: rows j, columns i -- dist and c are symmetric)
+        if (want_geo_grad) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float dC = -out[k] * inv_eps;
+            const float d0 = xi[0] - vb[8 * kBTW + k], d1 = xi[1] - vb[9 * kBTW + k], d2 = xi[2] - vb[10 * kBTW + k];
+            const float dist = sqrtf(fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, 1e-8f))));
+            const float rd = __fdividef(1.0f, p.ct.r_0 + dist);
+            if (MODE == BT_DQ) gdw = fmaf(dC, dist * rd, gdw);
+            const float cf = __fdividef(dC * w_h * p.ct.r_0 * rd * rd, dist);
+            gdx[0] = fmaf(cf, d0, gdx[0]);
+            gdx[1] = fmaf(cf, d1, gdx[1]);
+            gdx[2] = fmaf(cf, d2, gdx[2]);
+          }
+        }
+        if constexpr (C::kHist) {
+          if (want_hist) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(out[k]));
+            amax = warp_max(amax * inv_eps);
+            if (amax > 0.0f) {
+              int e = 0;
+              frexpf(amax, &e);  // amax < 2^e, the same in every lane
+              if (e > e_cur) {
+                if (e_cur > -1000) {
+                  const int sh = min(e - e_cur, 63);
+                  for (int b2 = lane; b2 < 68; b2 += 32)
+                    whist[b2] = static_cast<unsigned long long>(static_cast<long long>(whist[b2]) >> sh);
+                }
+                e_cur = e;
+                __syncwarp();
+              }
+              const float hsc = ldexpf(1.0f, kHistBits - e_cur);
+              const uint32_t bw[4] = {bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+              for (int k = 0; k < 16; ++k) {
+                const unsigned bin = (bw[k >> 2] >> (8 * (k & 3))) & 0xffu;
+                const long long q = __float2ll_rn(-out[k] * inv_eps * hsc);
+                if (bin < static_cast<unsigned>(kBinCount) && q != 0)
+                  atomicAdd(&whist[bin], static_cast<unsigned long long>(q));
+              }
+              __syncwarp();
+            }
+          }
         }
       }
       if constexpr (kAcc) {
@@ -434,7 +564,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
     // ---- per-row results: merge the four column parts
     if constexpr (MODE == BT_ROW || MODE == BT_COL || MODE == BT_OUT) {
       if (part > 0) {
-        float* mp = mrg + (part - 1) * 3 * 128;
+        float* mp = mrg + (part - 1) * C::NMRG * 128;
         mp[lrow] = m;
         mp[128 + lrow] = s0;
         mp[256 + lrow] = s1;
@@ -443,7 +573,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       if (part == 0 && rin) {
 #pragma unroll
         for (int q = 0; q < 3; ++q) {
-          const float* mp = mrg + q * 3 * 128;
+          const float* mp = mrg + q * C::NMRG * 128;
           if constexpr (MODE == BT_ROW) {
             const float m2 = mp[lrow], mm = fmaxf(m, m2);
             const float a = ex2(m - mm), c = ex2(m2 - mm);
@@ -470,6 +600,54 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
         } else {
           p.out0[o] = rok ? s0 : 0.0f;  // c
           p.out1[o] = rok ? s1 : 0.0f;  // g_v
+        }
+      }
+    }
+    // ---- shares of the shared-parameter gradients: merge the four column parts per row
+    if constexpr (TERMS || MODE == BT_COL) {
+      if (p.cg.dx != nullptr || p.cg.dw != nullptr) {
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kBEpiWarps) : "memory");  // mrg free again
+        constexpr int NV = C::NMRG >= 4 ? 4 : 3;
+        if (part > 0) {
+          float* mp = mrg + (part - 1) * C::NMRG * 128;
+          mp[lrow] = gdx[0];
+          mp[128 + lrow] = gdx[1];
+          mp[256 + lrow] = gdx[2];
+          if constexpr (NV == 4) mp[384 + lrow] = gdw;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kBEpiWarps) : "memory");
+        if (part == 0 && rin) {
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            const float* mp = mrg + q * C::NMRG * 128;
+            gdx[0] += mp[lrow];
+            gdx[1] += mp[128 + lrow];
+            gdx[2] += mp[256 + lrow];
+            if constexpr (NV == 4) gdw += mp[384 + lrow];
+          }
+          const size_t o = bh * N + row;
+          if (p.cg.dx != nullptr) {
+            p.cg.dx[o * 3] = rok ? gdx[0] : 0.0f;
+            p.cg.dx[o * 3 + 1] = rok ? gdx[1] : 0.0f;
+            p.cg.dx[o * 3 + 2] = rok ? gdx[2] : 0.0f;
+          }
+          if (MODE == BT_DQ && p.cg.dw != nullptr) p.cg.dw[o] = rok ? gdw : 0.0f;
+        }
+      }
+    }
+    if constexpr (C::kHist) {
+      // the bin sums: each warp's histogram to floats, then the 16 warps in order
+      if (want_hist) {
+        float* hf = reinterpret_cast<float*>(base + C::OFF_HF);
+        const float back = e_cur > -1000 ? ldexpf(1.0f, e_cur - kHistBits) : 0.0f;
+        for (int b2 = lane; b2 < 68; b2 += 32)
+          hf[warp * 68 + b2] = static_cast<float>(static_cast<double>(static_cast<long long>(whist[b2])) * back);
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kBEpiWarps) : "memory");
+        if (tid < kBinCount) {
+          float t = 0.0f;
+          for (int w = 0; w < kBEpiWarps; ++w) t += hf[w * 68 + tid];
+          const int nrb_all = (p.row_end - p.row_begin + 127) / 128;
+          p.cg.dpos[(bh * nrb_all + rb) * kBinCount + tid] = t;
         }
       }
     }
@@ -524,10 +702,10 @@ __global__ void bt_prep_kernel(const void* src, int dtype, float* row_out, float
 // ---------------------------------------------------------------- host side
 namespace {
 
-template <int MODE, int D>
+template <int MODE, int D, bool TERMS>
 cudaError_t launch_bt_md(const BTileParams& p, cudaStream_t st) {
-  using C = BTileCfg<MODE, D>;
-  auto kern = btile_kernel<MODE, D>;
+  using C = BTileCfg<MODE, D, TERMS>;
+  auto kern = btile_kernel<MODE, D, TERMS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nrb = (p.row_end - p.row_begin + 127) / 128;
@@ -536,7 +714,9 @@ cudaError_t launch_bt_md(const BTileParams& p, cudaStream_t st) {
 
 template <int MODE>
 cudaError_t launch_bt_m(int d, const BTileParams& p, cudaStream_t st) {
-  return d == 64 ? launch_bt_md<MODE, 64>(p, st) : launch_bt_md<MODE, 32>(p, st);
+  if (p.ct.bins != nullptr || p.ct.x != nullptr)
+    return d == 64 ? launch_bt_md<MODE, 64, true>(p, st) : launch_bt_md<MODE, 32, true>(p, st);
+  return d == 64 ? launch_bt_md<MODE, 64, false>(p, st) : launch_bt_md<MODE, 32, false>(p, st);
 }
 
 }  // namespace
@@ -615,6 +795,8 @@ cudaError_t launch_bt_pass(int mode, const BtArgs& a, cudaStream_t st) {
   p.N = a.N;
   p.row_begin = a.row_begin;
   p.row_end = a.row_end;
+  p.ct = a.ct;
+  p.cg = a.cg;
   switch (mode) {
     case BT_ROW: return launch_bt_m<BT_ROW>(a.d, p, st);
     case BT_COL: return launch_bt_m<BT_COL>(a.d, p, st);

@@ -81,9 +81,12 @@ struct TileParams {
   int nsplit;              // CTAs per row block, each over a contiguous share of the column tiles
   float lam;
   float qk_scale;          // 1/sqrt(d) of the cost
+  CostTerms ct;            // optional position / geometry terms in this pass's orientation
 };
 
-template <int DT, int D>
+// TERMS: the variant with the optional cost terms (a 3-stage ring when rows are
+// 128 bytes, to make room for the staged column coordinates and bin weights)
+template <int DT, int D, bool TERMS = false>
 struct TileCfg {
   static constexpr int ESZ = DT == DFS_F32 ? 4 : 2;
   static constexpr int RB = D * ESZ;       // bytes per operand row
@@ -92,12 +95,14 @@ struct TileCfg {
   static constexpr int KSTEPS = RB / 32;   // one MMA per 32 bytes of K
   static constexpr uint32_t GROUP = 128u * 128u;  // bytes of one atom column of a 128-row tile
   static constexpr uint32_t TILE = 128u * RB;     // bytes of a 128-row tile
-  static constexpr int NS = RB == 128 ? 4 : 2;    // stages of the column-tile ring
+  static constexpr int NS = RB == 128 ? (TERMS ? 3 : 4) : 2;  // stages of the column-tile ring
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_B = OFF_A + TILE;
   static constexpr uint32_t OFF_CB = OFF_B + NS * TILE;   // NS x 128 column bias
   static constexpr uint32_t OFF_CV = OFF_CB + NS * 512u;  // NS x 128 column vector
-  static constexpr uint32_t OFF_MRG = OFF_CV + NS * 512u;  // 3 x 128 partials of the second half, a flag
+  static constexpr uint32_t OFF_CX = OFF_CV + NS * 512u;                 // TERMS: NS x 3 x 128 column coordinates
+  static constexpr uint32_t OFF_PW = OFF_CX + (TERMS ? NS * 1536u : 0u);  // TERMS: 69 scaled bin weights (+ pad)
+  static constexpr uint32_t OFF_MRG = OFF_PW + (TERMS ? 288u : 0u);       // 3 x 128 partials of the second half, a flag
   // bf16 / fp16 operands: the column bias rides in the MMA as one more K = 16
   // slice (A: ones, B: the bias in three bf16 parts), in the no-swizzle
   // core-matrix layout, 128 rows x 32 bytes = 4 KB per tile
@@ -139,9 +144,9 @@ DFS_DEV void tile_mma(uint32_t d_tmem, uint32_t a_s, uint32_t b_s) {
   }
 }
 
-template <int MODE, int DT, int D>
+template <int MODE, int DT, int D, bool TERMS>
 __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constant__ TileParams p) {
-  using C = TileCfg<DT, D>;
+  using C = TileCfg<DT, D, TERMS>;
   // launched as a programmatic dependent of the previous kernel on the stream:
   // its grid is set up while that kernel drains; nothing is read before this
   // wait returns, i.e. before the previous kernel's results are visible
@@ -274,7 +279,8 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
       (void)inv_scale;
       // the tile's column bias (and vector), 4 columns per lane, fetched one tile
       // ahead so that their global latency overlaps the wait for a free stage
-      float pc[4], pw[4];
+      float pc[4], pw[4], px[3][4];
+      const float* xg = TERMS ? p.ct.x : nullptr;  // geometry term: the columns' coordinates, staged beside the tile
       auto fetch = [&](int u) {
         const int c0 = (t_begin + u) * kTCols;
 #pragma unroll
@@ -284,6 +290,10 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
           const bool cok = cin && (p.mask == nullptr || p.mask[static_cast<size_t>(bb) * N + j] != 0.0f);
           pc[q] = cok ? __ldcg(p.col_bias + bh * N + j) : -INFINITY;  // L2: peers may have written it
           if constexpr (MODE == TL_MATVEC) pw[q] = cin ? p.col_vec[bh * N + j] : 0.0f;
+          if (xg != nullptr) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) px[c][q] = cin ? xg[(static_cast<size_t>(bb) * N + j) * 3 + c] : 0.0f;
+          }
         }
       };
       fetch(0);
@@ -333,6 +343,11 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
             cbs[s * 128 + c] = pc[q];
           }
           if constexpr (MODE == TL_MATVEC) cvs[s * 128 + c] = pw[q];
+          if (TERMS && xg != nullptr) {
+            float* cx = reinterpret_cast<float*>(base + C::OFF_CX) + s * 384;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) cx[k * 128 + c] = px[k][q];
+          }
         }
         if constexpr (C::kExt) fence_async_smem();  // the MMA reads the extension rows
         mbar_arrive(&full[s]);
@@ -374,6 +389,29 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     const float scale = kLog2e * p.qk_scale / eps_h;
     const float fi = (MODE != TL_LSE && rin) ? __ldcg(p.row_bias + bh * N + row) : 0.0f;
     const uint32_t tlane = static_cast<uint32_t>(32 * quad) << 16;
+    // optional cost terms: bin weights scaled to -log2(e)/eps in shared memory
+    // (entry 68, the table's "no bin", is 0), this row's coordinates
+    const bool use_bins = TERMS && p.ct.bins != nullptr, use_geo = TERMS && p.ct.x != nullptr;
+    constexpr bool has_terms = TERMS;
+    float* pws = reinterpret_cast<float*>(base + C::OFF_PW);
+    const float* cxs = reinterpret_cast<const float*>(base + C::OFF_CX);
+    float xi0 = 0.0f, xi1 = 0.0f, xi2 = 0.0f, wS = 0.0f;
+    const uint8_t* brow = nullptr;
+    if constexpr (has_terms) {
+      const float nsc = -kLog2e / eps_h;
+      if (use_bins && tid <= kBinCount) pws[tid] = tid < kBinCount ? p.ct.pos_weight[hh * kBinCount + tid] * nsc : 0.0f;
+      if (use_geo) {
+        wS = p.ct.w_dist[hh] * nsc;
+        if (rin) {
+          const float* xr = p.ct.x + (static_cast<size_t>(bb) * N + row) * 3;
+          xi0 = xr[0];
+          xi1 = xr[1];
+          xi2 = xr[2];
+        }
+      }
+      if (use_bins && rin) brow = p.ct.bins + (static_cast<size_t>(bb) * N + row) * p.ct.bin_stride;
+      asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");  // pws written
+    }
     // running reference, exact maximum and sum of exp2(x - reference) of this
     // half's columns (LSE, ROWSTATS)
     float m = kNeg, mt = kNeg, sum = 0.0f;
@@ -381,6 +419,13 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
 #pragma unroll 1
     for (int u = 0; u < ntiles; ++u) {
       const int s = u % C::NS, b = u & 1;
+      // this row's bins of the tile's columns of this half (64 bytes), loaded ahead of the waits
+      uint4 bq[4] = {};
+      if (TERMS && brow != nullptr) {
+        const uint4* src = reinterpret_cast<const uint4*>(brow + (t_begin + u) * kTCols + 64 * half);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bq[q] = __ldg(src + q);
+      }
       if (!mbar_wait(&full[s], (u / C::NS) & 1)) err = 1;  // the producer's bias stores
       if (!mbar_wait(&sfull[b], (u >> 1) & 1)) err = 1;
       tc_fence_after();
@@ -389,7 +434,53 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
       tmem_ld32_async(tbase + tlane + b * kTCols + 64 * half, r0v);
       tmem_wait_ld(r0v);
       tmem_ld32_async(tbase + tlane + b * kTCols + 64 * half + 32, r1v);
+      // with cost terms: x = S' + column bias (+ row bias for MATVEC) + term, then the
+      // plain reductions below on x
+      auto chunk_terms = [&](uint32_t (&rv32)[32], int ch) {
+        const float* cb = cbs + s * 128 + 32 * ch;
+        const float* xs = cxs + s * 384 + 32 * ch;
+        const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bq[2 * (ch & 1)]);
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          float t = C::kExt ? 0.0f : cb[k];
+          if constexpr (MODE == TL_MATVEC) t += fi;
+          if (use_bins) t += pws[(bw[k >> 2] >> (8 * (k & 3))) & 0xffu];
+          if (use_geo) {
+            const float d0 = xi0 - xs[k], d1 = xi1 - xs[128 + k], d2 = xi2 - xs[256 + k];
+            const float dist = sqrtf(fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, 1e-8f))));
+            t = fmaf(wS, __fdividef(dist, p.ct.r_0 + dist), t);
+          }
+          x[k] = fmaf(__uint_as_float(rv32[k]), scale, t);
+        }
+        if constexpr (MODE == TL_MATVEC) {
+          const float* cv = cvs + s * 128 + 32 * ch;
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 0; k < 32; ++k) a[k & 3] = fmaf(ex2(x[k]), cv[k], a[k & 3]);
+          acc += (a[0] + a[1]) + (a[2] + a[3]);
+        } else {
+          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+          for (int k = 0; k < 32; ++k) a[k & 3] += ex2(x[k] - m);
+          float cm = kNeg;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) cm = fmaxf(cm, x[k]);
+          mt = fmaxf(mt, cm);
+          if (cm > m + kLag) {
+            a[0] = a[1] = a[2] = a[3] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) a[k & 3] += ex2(x[k] - cm);
+            sum *= ex2(m - cm);
+            m = cm;
+          }
+          sum += (a[0] + a[1]) + (a[2] + a[3]);
+        }
+      };
       auto chunk = [&](uint32_t (&rv32)[32], int ch) {
+        if constexpr (has_terms) {
+          chunk_terms(rv32, ch);
+        } else {
         float v[32];
 #pragma unroll
         for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(rv32[k]);
@@ -459,6 +550,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
           }
           sum += (a[0] + a[1]) + (a[2] + a[3]);
         }
+        }  // no cost terms
       };
       chunk(r0v, 2 * half);
       tmem_wait_ld(r1v);
@@ -616,24 +708,30 @@ bool make_tmap(CUtensorMap* tm, const void* ptr, int dtype, int inner, int rows,
 
 namespace {
 
-template <int MODE, int DT, int D>
+template <int MODE, int DT, int D, bool TERMS>
 cudaError_t launch_tile_mdd(const TileParams& p, cudaStream_t st) {
-  using C = TileCfg<DT, D>;
-  auto kern = tile_kernel<MODE, DT, D>;
+  using C = TileCfg<DT, D, TERMS>;
+  auto kern = tile_kernel<MODE, DT, D, TERMS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int nrb = (p.row_end - p.row_begin + 127) / 128;
   return launch_dependent(kern, dim3(p.B * p.H * nrb * p.nsplit), dim3(kTThreads), C::SMEM, st, p);
 }
 
+template <int MODE, bool TERMS>
+cudaError_t launch_tile_mt(int dtype, int d, const TileParams& p, cudaStream_t st) {
+  if (d == 64) {
+    if (dtype == DFS_BF16) return launch_tile_mdd<MODE, DFS_BF16, 64, TERMS>(p, st);
+    if (dtype == DFS_F16) return launch_tile_mdd<MODE, DFS_F16, 64, TERMS>(p, st);
+    return launch_tile_mdd<MODE, DFS_F32, 64, TERMS>(p, st);
+  }
+  return launch_tile_mdd<MODE, DFS_F32, 32, TERMS>(p, st);
+}
+
 template <int MODE>
 cudaError_t launch_tile_m(int dtype, int d, const TileParams& p, cudaStream_t st) {
-  if (d == 64) {
-    if (dtype == DFS_BF16) return launch_tile_mdd<MODE, DFS_BF16, 64>(p, st);
-    if (dtype == DFS_F16) return launch_tile_mdd<MODE, DFS_F16, 64>(p, st);
-    return launch_tile_mdd<MODE, DFS_F32, 64>(p, st);
-  }
-  return launch_tile_mdd<MODE, DFS_F32, 32>(p, st);
+  if (p.ct.bins != nullptr || p.ct.x != nullptr) return launch_tile_mt<MODE, true>(dtype, d, p, st);
+  return launch_tile_mt<MODE, false>(dtype, d, p, st);
 }
 
 }  // namespace
@@ -714,6 +812,7 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
   p.row_end = t.row_end;
   p.lam = t.lam;
   p.qk_scale = t.qk_scale;
+  p.ct = t.ct;
   p.npeers = t.npeers;
   for (int k = 0; k < DFS_MAX_PEERS; ++k) {
     p.peer_out[k] = t.peer_out[k];

@@ -173,6 +173,16 @@ int take_status(bool wait) {
   return v | g_seen.exchange(0);
 }
 
+// DFS_TERM_* bits of the optional inputs a call passes (the streamed kernels
+// size their workspace by them)
+int32_t cost_terms_of(const Tensor& pw, const Tensor& pb, const Tensor& xr, const Tensor& wd) {
+  int32_t t = 0;
+  if (pw.defined() && pb.defined()) t |= DFS_TERM_POS;
+  if (xr.defined() && wd.defined()) t |= DFS_TERM_GEO;
+  if (xr.defined()) t |= DFS_TERM_XRES;
+  return t;
+}
+
 struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
   // Arguments (positions in the gradient list backward returns): 0 Q, 1 K, 2 V,
   // 3 x_res, 4 pos_weight, 5 pos_bins, 6 eps, 7 w_dist, 8 log_mu, 9 log_nu,
@@ -224,6 +234,8 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     prob.check_every = 2;
     prob.lam = static_cast<float>(lam);
     prob.r_0 = static_cast<float>(r_0);
+    prob.cost_terms = cost_terms_of(pw, pb, xr, wd);
+    ctx->saved_data["cost_terms"] = static_cast<int64_t>(prob.cost_terms);
     dfs_fwd_args a{};
     a.Q = Qc.data_ptr();
     a.K = Kc.data_ptr();
@@ -322,6 +334,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     prob.check_every = 2;
     prob.lam = static_cast<float>(ctx->saved_data["lam"].toDouble());
     prob.r_0 = static_cast<float>(ctx->saved_data["r_0"].toDouble());
+    prob.cost_terms = static_cast<int32_t>(ctx->saved_data["cost_terms"].toInt());
     dfs_cg_params cg{};
     cg.rtol = static_cast<float>(ctx->saved_data["cg_rtol"].toDouble());
     cg.atol = static_cast<float>(ctx->saved_data["cg_atol"].toDouble());

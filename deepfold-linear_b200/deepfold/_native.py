@@ -51,7 +51,10 @@ class DfsProblem(ctypes.Structure):
                 ("d", ctypes.c_int32), ("in_dtype", ctypes.c_int32), ("cost_mode", ctypes.c_int32),
                 ("K_iter", ctypes.c_int32), ("check_every", ctypes.c_int32),
                 ("lam", ctypes.c_float), ("r_0", ctypes.c_float), ("threshold", ctypes.c_float),
-                ("reserved", ctypes.c_float)]
+                ("cost_terms", ctypes.c_int32)]
+
+
+DFS_TERM_POS, DFS_TERM_GEO, DFS_TERM_XRES = 1, 2, 4
 
 
 class DfsFwdArgs(ctypes.Structure):
@@ -285,11 +288,12 @@ def dtype_code(dt: torch.dtype) -> int:
 
 
 def make_problem(B, H, N, d, dtype, K_iter, lam, r_0, cost_mode=DFS_COST_QK, threshold=None,
-                 check_every=2) -> DfsProblem:
+                 check_every=2, cost_terms=0) -> DfsProblem:
     return DfsProblem(B=B, H=H, N=N, d=d, in_dtype=dtype_code(dtype), cost_mode=cost_mode,
                       K_iter=int(K_iter), check_every=int(check_every),
                       lam=float(lam) if not math.isinf(lam) else float("inf"), r_0=float(r_0),
-                      threshold=float(threshold) if threshold is not None else 0.0, reserved=0.0)
+                      threshold=float(threshold) if threshold is not None else 0.0,
+                      cost_terms=int(cost_terms))
 
 
 def workspace_bytes(prob: DfsProblem) -> tuple[int, int]:

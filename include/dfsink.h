@@ -67,8 +67,19 @@ typedef struct {
   float lam;              /* marginal penalty; kappa = lam/(lam+eps); +inf -> 1   */
   float r_0;              /* geometry scale r_0                                    */
   float threshold;        /* L-inf early-stop tolerance on the potentials; <= 0 off */
-  float reserved;
+  int32_t cost_terms;     /* DFS_TERM_* bits: the optional cost terms the calls pass */
 } dfs_problem;
+
+/* dfs_problem.cost_terms: which optional inputs the calls of this problem pass.
+ * The streamed kernels (N > 384 or head dim > 32) keep per-call tables for them
+ * in the workspace, so dfs_workspace_size must know; a streamed call whose
+ * arguments carry a term its problem does not declare is rejected with
+ * DFS_ERR_INVALID_ARGUMENT.  (0 = none, the plain -QK^T/sqrt(d) cost.) */
+enum {
+  DFS_TERM_POS = 1,   /* pos_weight / pos_bins: position-bin term                 */
+  DFS_TERM_GEO = 2,   /* x_res with w_dist: geometry term                         */
+  DFS_TERM_XRES = 4   /* x_res given (centroid; its gradient dx_res)              */
+};
 
 typedef struct {
   /* inputs */

@@ -1,0 +1,111 @@
+"""Position-bin and geometry cost terms on the streamed path (N > 384), forward
+and all seven gradients, against the oracle.
+
+The reference adds both terms to every cost tile at any N
+(sinkhorn_kernel.py:59-129) and returns the gradients of x_res, pos_weight and
+w_dist beside dQ, dK, dV (:2366-2382).  Here problems beyond the resident
+range take the TMA-staged tile passes with the terms; head dims <= 32 run
+zero-padded on the d = 64 kernels.  Tolerances: outputs 2e-3 max-abs,
+gradients 5e-3 relative (the parity criterion).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import max_abs, rel_err
+from oracle import sinkhorn_oracle as orc
+
+from deepfold.model.kernels.flash_sinkhorn_attn import flash_sinkhorn_attn
+
+pytestmark = pytest.mark.gpu
+
+TOL = 5e-3
+
+
+def _inputs(B, H, N, d, seed, lengths=None):
+    r = np.random.default_rng(seed)
+    z = dict(Q=r.standard_normal((B, H, N, d)), K=r.standard_normal((B, H, N, d)),
+             V=r.standard_normal((B, H, N, d)), G=r.standard_normal((B, H, N, d)),
+             x=4.0 * r.standard_normal((B, N, 3)), pos_w=0.5 * r.standard_normal((H, 68)),
+             bins=r.integers(0, 68, (B, N, N)).astype(np.int32), eps=np.linspace(0.7, 1.3, H),
+             w=np.linspace(0.2, 0.8, H), dO=r.standard_normal((B, N, H * d)), dxc=r.standard_normal((B, H, N, 3)))
+    # bf16 operands, so that the products are exact on every path
+    for k in ("Q", "K", "V"):
+        z[k] = torch.tensor(z[k]).to(torch.bfloat16).float().numpy()
+    mask = None
+    if lengths is None:
+        lm = np.full((B, H, N), -math.log(N))
+        z["lmu"], z["lnu"] = lm, lm.copy()
+    else:
+        mask = np.zeros((B, N))
+        for b, L in enumerate(lengths):
+            mask[b, :L] = 1.0
+        lm = np.where(mask[:, None, :] > 0, -np.log(mask.sum(1))[:, None, None], -1e9)
+        z["lmu"], z["lnu"] = np.broadcast_to(lm, (B, H, N)).copy(), np.broadcast_to(lm, (B, H, N)).copy()
+    z["mask"] = mask
+    return {k: (v.astype(np.float32) if isinstance(v, np.ndarray) and v.dtype.kind == "f" else v) for k, v in z.items()}
+
+
+def _run(z, K_iter, lam, dtype=torch.bfloat16, grads=True):
+    dev = torch.device("cuda")
+    t = lambda k: torch.tensor(z[k], device=dev)  # noqa: E731
+    qkv = [t(k).to(dtype).requires_grad_(grads) for k in ("Q", "K", "V")]
+    G, x, pw, w = (t(k).requires_grad_(grads) for k in ("G", "x", "pos_w", "w"))
+    mask = None if z["mask"] is None else t("mask")
+    o, xc, lu, lv = flash_sinkhorn_attn(*qkv, G, x, pw, t("bins"), t("eps"), w, t("lmu"), t("lnu"), K_iter=K_iter,
+                                        lam=lam, r_0=10.0, mask=mask, cg_opts=dict(rtol=1e-7, max_iter=200))
+    out = dict(o=o.detach().cpu().numpy(), xc=xc.detach().cpu().numpy(), lu=lu.cpu().numpy(), lv=lv.cpu().numpy())
+    if grads:
+        ((o * t("dO")).sum() + (xc * t("dxc")).sum()).backward()
+        torch.cuda.synchronize()
+        for name, leaf in zip(("dQ", "dK", "dV", "dG", "dx", "dpos", "dw"), (*qkv, G, x, pw, w)):
+            out[name] = leaf.grad.float().cpu().numpy()
+    return out
+
+
+def _oracle(z, K_iter, lam, mode):
+    res, gr = orc.flash_sinkhorn_attn(z["Q"], z["K"], z["V"], z["G"], z["x"], z["pos_w"], z["bins"], z["eps"], z["w"],
+                                      z["lmu"], z["lnu"], K_iter=K_iter, lam=lam, r_0=10.0, mask=z["mask"],
+                                      with_grad=True, dO_flat=z["dO"], dxc=z["dxc"], grad_mode=mode)
+    return res, gr
+
+
+def _check_forward(g, res):
+    assert max_abs(g["o"], res.o_flat) <= 2e-3
+    assert max_abs(g["xc"], res.xc) <= 2e-3
+    assert max_abs(g["lu"], res.log_u) <= 2e-3
+    assert max_abs(g["lv"], res.log_v) <= 2e-3
+
+
+@pytest.mark.parametrize("d", [32, 64])
+def test_stream_terms_converged_all_gradients(d):
+    """N = 520 (> 384: streamed; d = 32 runs zero-padded to 64), balanced, converged:
+    outputs and all seven gradients against the reference's unrolled gradient."""
+    z = _inputs(1, 2, 520, d, seed=d)
+    g = _run(z, 80, math.inf)
+    res, gr = _oracle(z, 80, math.inf, "unrolled")
+    _check_forward(g, res)
+    for k in ("dQ", "dK", "dV", "dG", "dx", "dpos", "dw"):
+        assert rel_err(g[k], gr[k]) <= TOL, f"{k}: {rel_err(g[k], gr[k]):.3e}"
+
+
+def test_stream_terms_padded_varlen_unbalanced():
+    """Padded variable lengths with masks, lam = 1, at the implicit gradient's fixed point."""
+    z = _inputs(2, 2, 640, 64, seed=3, lengths=[640, 333])
+    g = _run(z, 60, 1.0)
+    res, gr = _oracle(z, 60, 1.0, "ift")
+    _check_forward(g, res)
+    for k in ("dQ", "dK", "dV", "dG", "dx", "dpos", "dw"):
+        assert rel_err(g[k], gr[k]) <= TOL, f"{k}: {rel_err(g[k], gr[k]):.3e}"
+    assert np.all(g["o"][1, 333:] == 0) and np.all(g["lu"][1, :, 333:] == 0)
+
+
+def test_stream_terms_gradients_are_bitwise_reproducible():
+    z = _inputs(1, 2, 512, 64, seed=9)
+    a = _run(z, 30, 1.0)
+    b = _run(z, 30, 1.0)
+    for k in ("dx", "dpos", "dw", "dQ", "dK", "dV"):
+        assert np.array_equal(a[k], b[k]), k
