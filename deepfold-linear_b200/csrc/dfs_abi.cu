@@ -120,6 +120,7 @@ FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
   q.lam = p->lam; q.r_0 = p->r_0; q.threshold = p->threshold;
   q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
   q.cost_terms = p->cost_terms;
+  q.r_head = a->r_head;
   return q;
 }
 
@@ -139,6 +140,8 @@ BwdParams bwd_params(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bw
   q.lam = p->lam; q.r_0 = p->r_0;
   q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
   q.cost_terms = p->cost_terms;
+  q.r_head = a->r_head;
+  q.dr_head = a->dr_head;
   return q;
 }
 
@@ -191,6 +194,7 @@ int check_bwd_args(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_
   if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (a->dxc && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->dr_head && (!a->x_res || !a->w_dist)) return DFS_ERR_INVALID_ARGUMENT;
   if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
   if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
@@ -206,7 +210,8 @@ int check_stream_bwd(const dfs_problem* p, const dfs_bwd_args* a, void* workspac
   const bool pos = a->pos_weight != nullptr, geo = a->x_res != nullptr && a->w_dist != nullptr;
   if ((pos && !(p->cost_terms & DFS_TERM_POS)) || (geo && !(p->cost_terms & DFS_TERM_GEO)))
     return DFS_ERR_INVALID_ARGUMENT;
-  const bool shared_grads = a->dx_res != nullptr || a->dpos_weight != nullptr || a->dw_dist != nullptr;
+  const bool shared_grads =
+      a->dx_res != nullptr || a->dpos_weight != nullptr || a->dw_dist != nullptr || a->dr_head != nullptr;
   if (shared_grads && p->cost_terms == 0) return DFS_ERR_INVALID_ARGUMENT;
   if ((pos || geo || shared_grads) && !terms_path_ok(p)) return DFS_ERR_UNSUPPORTED;
   if (workspace == nullptr || workspace_bytes < stream_bwd_workspace(p->B, p->H, p->N, kdim(p), p->cost_terms) ||

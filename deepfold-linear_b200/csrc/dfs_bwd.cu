@@ -37,11 +37,13 @@
 //
 // Gradients of the shared cost parameters (sinkhorn_kernel.py:2366-2382 of the
 // reference returns them): with dC = -dS / eps,
-//   dw_h    = sum_ij dC_ij dist_ij / (r_0 + dist_ij)
+//   dw_h    = sum_ij dC_ij dist_ij / (r_h + dist_ij)
+//   dr_h    = -w_h sum_ij dC_ij dist_ij / (r_h + dist_ij)^2
 //   dx_i    = sum_j dC_ij c_ij (x_i - x_j) + sum_j dC_ji c_ji (x_i - x_j) + (T_norm^T dxc)_i,
-//             c_ij = w_h r_0 / ((r_0 + dist_ij)^2 dist_ij)
+//             c_ij = w_h r_h / ((r_h + dist_ij)^2 dist_ij)
 //   dpos[h, b] = sum over the entries with bins_ij = b of dC_ij
-// are accumulated from the staged dS tile of phase 5 (row part, dw, bins), the
+// (r_h = r_head[h], or r_0) are accumulated from the staged dS tile of phase 5
+// (row part, dw, dr, bins), the
 // staged T_norm^T of phase 7 (centroid part) and the staged dS^T of phase 8
 // (column part), per slab row and per CTA into the workspace; the bin histogram
 // is summed in 64-bit fixed point (scale from the tile's largest |dC|), so its
@@ -76,15 +78,17 @@ struct BwdCfg {
   static_assert(SMEM <= 232448u, "exceeds the 227 KB of shared memory a CTA can use");
   static_assert(kWarps * 2u * NP * 4 <= 4u * NP * DH, "column partials must fit the K/V region");
   static_assert(NP + DH <= 512, "TMEM columns");
+  static_assert(8u * C * RS >= 1600u + 4u * 2 * kWarps, "cost-gradient scratch must fit the exchange slots");
 };
 
 // Workspace of the shared-parameter gradients (floats): per (batch, head,
-// point) the three dx partials, then per (batch, head, CTA) the dw partial and
-// the 68 position-bin partials.
+// point) the three dx partials, then per (batch, head, CTA) the dw partial, the
+// 68 position-bin partials and the dr partial.
 struct CostGradWs {
   float* dx;    // (B*H, N, 3)
   float* dw;    // (B*H, C)
   float* dpos;  // (B*H, C, 68)
+  float* dr;    // (B*H, C)
 };
 __host__ __device__ inline CostGradWs costgrad_ws(float* ws, int B, int H, int N) {
   const size_t bh = static_cast<size_t>(B) * H, C = (N + 63) / 64;
@@ -92,6 +96,7 @@ __host__ __device__ inline CostGradWs costgrad_ws(float* ws, int B, int H, int N
   w.dx = ws;
   w.dw = ws + bh * N * 3;
   w.dpos = w.dw + bh * C;
+  w.dr = w.dpos + bh * C * 68;
   return w;
 }
 constexpr int kBins = 68;
@@ -129,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   const float qk_scale = s_scale * p.qk_scale;
   const float grad_scale = p.qk_scale / eps_h;   // dS -> dQ, dK
   const float w_h = p.w_dist ? p.w_dist[hh] : 0.0f;
+  const float r_h = p.r_head != nullptr ? p.r_head[hh] : p.r_0;  // geometry scale of this head
   int err = 0;
   uint32_t mma_phase = 0;
 
@@ -226,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
     bias.xcol = colv + BC_X0 * NP;
     bias.geo = p.x_res != nullptr && w_h != 0.0f;
     bias.w_h = w_h;
-    bias.r_0 = p.r_0;
+    bias.r_0 = r_h;
     bias.s_scale = s_scale;
     bias.bb = bb;
     bias.hh = hh;
@@ -581,7 +587,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   }
   // shared-parameter gradients from the staged dS while the tensor core reads it
   // (the exchange buffers are free from here on: cg_* scratch lives there)
-  const bool geo_grad = p.x_res != nullptr && (p.dw_dist != nullptr || (p.dx_res != nullptr && w_h != 0.0f));
+  const bool geo_grad = p.x_res != nullptr && (p.dw_dist != nullptr || p.dr_head != nullptr ||
+                                               (p.dx_res != nullptr && w_h != 0.0f));
   const bool pos_grad = p.dpos_weight != nullptr && p.pos_bins != nullptr;
   const bool cost_grad = geo_grad || pos_grad || p.dx_res != nullptr;
   float* cg_dx = reinterpret_cast<float*>(base + Cfg::OFF_XR);                                // 3 x 64
@@ -589,10 +596,10 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   float* cg_red = reinterpret_cast<float*>(base + Cfg::OFF_XR + 1600);                        // 32
   const float inv_eps = 1.0f / eps_h;
   // dx share sum_j dC_ij c_ij (x_row - x_col) of the staged tile's slab rows
-  // (lanes over the N columns), added to cg_dx; with `bins`, the tile's dw
-  // partial (returned, per thread) and fixed-point histogram (scale `hscale`)
-  auto geo_rows = [&](bool transposed, bool with_bins, float hscale) -> float {
-    float dw = 0.0f;
+  // (lanes over the N columns), added to cg_dx; with `bins`, the tile's dw and
+  // dr partials (returned, per thread) and fixed-point histogram (scale `hscale`)
+  auto geo_rows = [&](bool transposed, bool with_bins, float hscale) -> float2 {
+    float dw = 0.0f, dr = 0.0f;
 #pragma unroll 1
     for (int r = 0; r < kRpw; ++r) {
       const int li = kRpw * warp + r, gi = row0 + li;
@@ -606,9 +613,13 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
           if (geo_grad) {
             const float d0 = x0 - colv[BC_X0 * NP + j], d1 = x1 - colv[BC_X1 * NP + j], d2 = x2 - colv[BC_X2 * NP + j];
             const float dist = sqrtf(d0 * d0 + d1 * d1 + d2 * d2 + 1e-8f);
-            const float rd = 1.0f / (p.r_0 + dist);
-            if (with_bins) dw = fmaf(dC, dist * rd, dw);
-            const float cf = dC * w_h * p.r_0 * rd * rd / dist;
+            const float rd = 1.0f / (r_h + dist);
+            if (with_bins) {
+              const float t = dC * dist * rd;
+              dw += t;
+              dr = fmaf(t, rd, dr);
+            }
+            const float cf = dC * w_h * r_h * rd * rd / dist;
             ax = fmaf(cf, d0, ax);
             ay = fmaf(cf, d1, ay);
             az = fmaf(cf, d2, az);
@@ -630,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       }
     }
     (void)transposed;
-    return dw;
+    return make_float2(dw, dr);
   };
   if (cost_grad) {
     for (int i = tid; i < 3 * 64; i += kThreads) cg_dx[i] = 0.0f;
@@ -655,10 +666,13 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       frexpf(mx, &ex);  // mx < 2^ex
       hscale = mx > 0.0f ? ldexpf(1.0f, 46 - ex) : 0.0f;
     }
-    const float dwp = geo_rows(false, true, hscale);
+    const float2 dwp = geo_rows(false, true, hscale);
     __syncthreads();  // cg_red reused
-    const float dws = warp_sum(dwp);
-    if (lane == 0) cg_red[warp] = dws;
+    const float dws = warp_sum(dwp.x), drs = warp_sum(dwp.y);
+    if (lane == 0) {
+      cg_red[warp] = dws;
+      cg_red[kWarps + warp] = drs;
+    }
     __syncthreads();
     const size_t cta = static_cast<size_t>(prob) * C + crank;
     const CostGradWs cw = costgrad_ws(p.ws, p.B, p.H, N);
@@ -666,6 +680,11 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       float s = 0.0f;
       for (int w = 0; w < kWarps; ++w) s += cg_red[w];
       cw.dw[cta] = s;
+    }
+    if (tid == 32 && p.dr_head != nullptr) {
+      float s = 0.0f;
+      for (int w = 0; w < kWarps; ++w) s += cg_red[kWarps + w];
+      cw.dr[cta] = -w_h * s;
     }
     if (pos_grad && tid < kBins)
       cw.dpos[cta * kBins + tid] =
@@ -831,6 +850,7 @@ __global__ void resident_costgrad_finalize(const BwdParams p, int C) {
   const int ndx = p.dx_res != nullptr ? p.B * p.N * 3 : 0;
   const int ndw = p.dw_dist != nullptr ? p.H : 0;
   const int npos = p.dpos_weight != nullptr ? p.H * kBins : 0;
+  const int ndr = p.dr_head != nullptr ? p.H : 0;
   if (t < ndx) {
     const int b = t / (p.N * 3), rem = t % (p.N * 3);
     float s = 0.0f;
@@ -848,6 +868,12 @@ __global__ void resident_costgrad_finalize(const BwdParams p, int C) {
     for (int b = 0; b < p.B; ++b)
       for (int c = 0; c < C; ++c) s += cw.dpos[((static_cast<size_t>(b) * p.H + h) * C + c) * kBins + bin];
     p.dpos_weight[u] = s;
+  } else if (t < ndx + ndw + npos + ndr) {
+    const int h = t - ndx - ndw - npos;
+    float s = 0.0f;
+    for (int b = 0; b < p.B; ++b)
+      for (int c = 0; c < C; ++c) s += cw.dr[(static_cast<size_t>(b) * p.H + h) * C + c];
+    p.dr_head[h] = s;
   }
 }
 
@@ -886,7 +912,8 @@ cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st) {
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;
-  const int n = (p.dx_res ? p.B * p.N * 3 : 0) + (p.dw_dist ? p.H : 0) + (p.dpos_weight ? p.H * kBins : 0);
+  const int n = (p.dx_res ? p.B * p.N * 3 : 0) + (p.dw_dist ? p.H : 0) + (p.dpos_weight ? p.H * kBins : 0) +
+                (p.dr_head ? p.H : 0);
   if (n == 0) return cudaSuccess;
   resident_costgrad_finalize<<<(n + 255) / 256, 256, 0, st>>>(p, C);
   return cudaGetLastError();
@@ -907,7 +934,7 @@ size_t resident_bwd_smem(int N, int d) {
 
 size_t resident_bwd_workspace(int B, int H, int N, int) {
   const size_t bh = static_cast<size_t>(B) * H, C = (N + 63) / 64;
-  return sizeof(float) * (bh * N * 3 + bh * C + bh * C * kBins);
+  return sizeof(float) * (bh * N * 3 + 2 * bh * C + bh * C * kBins);
 }
 
 }  // namespace dfs

@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
       bias.xcol = colv + CV_X0 * NP;
       bias.geo = p.x_res != nullptr && wq != 0.0f;
       bias.w_h = wq;
-      bias.r_0 = p.r_0;
+      bias.r_0 = p.r_head != nullptr ? p.r_head[hq] : p.r_0;
       bias.s_scale = ssc;
       bias.bb = bq;
       bias.hh = hq;

@@ -26,7 +26,7 @@ DFS_DEV float load_f32(const void* p, size_t i, int dtype) {
 // Optional cost terms on the streamed passes.  Each element (r, c) of a pass
 // (rows r, columns c of S = A B^T; for the passes on S^T the rows are the cost's
 // columns) adds, in log2 units,
-//     pwS[bins(r, c)] + wS * t(r, c),  t = dist / (r_0 + dist),
+//     pwS[bins(r, c)] + wS * t(r, c),  t = dist / (r_h + dist),
 //     dist = sqrt(|x_r - x_c|^2 + 1e-8)            (sinkhorn_kernel.py:59-129)
 // with pwS = -pos_weight[h] log2(e) / eps_h and wS = -w_h log2(e) / eps_h.  The
 // bins come from a per-call uint8 table in the pass's orientation (rows of
@@ -40,12 +40,16 @@ struct CostTerms {
   const float* x;           // (B, N, 3) coordinates with the geometry term, or null
   const float* w_dist;      // (H,) with x
   float r_0;
+  const float* r_head;      // (H,) per-head geometry scale r_h, or null: r_0
 };
+// geometry scale of head h
+DFS_DEV float geo_scale(const CostTerms& t, int h) { return t.r_head != nullptr ? t.r_head[h] : t.r_0; }
 // Shares of the shared-parameter gradients written by the streamed gradient
 // passes (null: not wanted), summed by stream_costgrad_finalize.
 struct CostGradOut {
   float* dx;    // (BH, N, 3) this pass's share of dx per row
   float* dw;    // (BH, N) per-row share of dw_dist
+  float* dr;    // (BH, N) per-row share of sum dC dist / (r_h + dist)^2 (dr_head = -w_h times it)
   float* dpos;  // (BH, row blocks, 68) per-CTA bin sums
 };
 
@@ -74,6 +78,7 @@ struct FwdParams {
   float lam, r_0, threshold;
   float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
   int cost_terms;          // DFS_TERM_* declared by the problem (workspace layout of the streamed path)
+  const float* r_head;     // (H,) per-head geometry scale, or null: r_0
 };
 
 struct BwdParams {
@@ -108,6 +113,8 @@ struct BwdParams {
   float lam, r_0, cg_rtol, cg_atol;
   float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
   int cost_terms;          // DFS_TERM_* declared by the problem (workspace layout of the streamed path)
+  const float* r_head;     // (H,) per-head geometry scale, or null: r_0
+  float* dr_head;          // (H,) gradient of r_head (or of r_0 per head), or null
 };
 
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
@@ -135,7 +142,8 @@ cudaError_t build_cost_bins(const int32_t* pos_bins, int B, int N, uint8_t* bins
 // The cost terms of a pass from the operator's inputs (position term when
 // pos_weight and the tables are given, geometry term when x_res and w_dist
 // are): `transposed` for the passes on S^T, whose rows are the cost's columns.
-CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float* w_dist, float r_0, int N,
+CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float* w_dist, float r_0,
+                        const float* r_head, int N,
                         const uint8_t* bins, const uint8_t* bins_t, bool transposed);
 size_t resident_bwd_smem(int N, int d);
 size_t resident_bwd_workspace(int B, int H, int N, int d);

@@ -84,7 +84,7 @@ DFS_DEV void regs_to_stage(const float (&E)[kRpw][NS], float* Ts, int warp, int 
 }
 
 // Position / geometry terms of the cost, folded into the slab as
-// S' -= (pos_weight[h, bins_ij] + w_h dist_ij / (r_0 + dist_ij)) * s_scale
+// S' -= (pos_weight[h, bins_ij] + w_h dist_ij / (r_h + dist_ij)) * s_scale
 // (src/deepfold/model/kernels/sinkhorn_kernel.py:107-127).
 struct BiasArgs {
   const float* pos_weight;   // (H, 68) or null
@@ -92,7 +92,7 @@ struct BiasArgs {
   const float* xrow;         // smem, 3 x 64 row coordinates (x, y, z planes)
   const float* xcol;         // smem, 3 x NP column coordinates
   bool geo;                  // geometry term present
-  float w_h, r_0, s_scale;
+  float w_h, r_0, s_scale;   // r_0: this head's geometry scale r_h
   int bb, hh, N, row0;
   bool transposed;           // slab rows are cost columns (bins read as [col][row])
 };

@@ -390,8 +390,8 @@ size_t stream_fwd_workspace(int B, int H, int N, int d, int terms) {
 
 // The cost terms of a pass from the forward / backward inputs: `transposed` for
 // the passes on S^T (their rows are the cost's columns).
-CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float* w_dist, float r_0, int N,
-                        const uint8_t* bins, const uint8_t* bins_t, bool transposed) {
+CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float* w_dist, float r_0,
+                        const float* r_head, int N, const uint8_t* bins, const uint8_t* bins_t, bool transposed) {
   CostTerms c{};
   if (pos_weight != nullptr && bins != nullptr) {
     c.bins = transposed ? bins_t : bins;
@@ -403,6 +403,7 @@ CostTerms cost_terms_of(const float* pos_weight, const float* x_res, const float
     c.w_dist = w_dist;
   }
   c.r_0 = r_0;
+  c.r_head = r_head;
   return c;
 }
 
@@ -437,7 +438,7 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     bins_t = bins + round256(cost_bins_bytes(fp.B, fp.N));
   }
   auto terms = [&](bool transposed) {
-    return cost_terms_of(fp.pos_weight, fp.x_res, fp.w_dist, fp.r_0, fp.N, bins, bins_t, transposed);
+    return cost_terms_of(fp.pos_weight, fp.x_res, fp.w_dist, fp.r_0, fp.r_head, fp.N, bins, bins_t, transposed);
   };
   unsigned long long* cnts[DFS_MAX_PEERS] = {};
   if (peers != nullptr)

@@ -636,10 +636,10 @@ __global__ void __launch_bounds__(kVThreads) sb_final_kernel(VecParams p) {
 namespace {
 size_t rnd256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 // dx shares of the three gradient passes (rows, columns, centroid), the per-row
-// dw share, the per-CTA bin sums
+// dw share, the per-CTA bin sums, the per-row dr share
 size_t costgrad_floats(int B, int H, int N) {
   const size_t n = static_cast<size_t>(B) * H * N, bh = static_cast<size_t>(B) * H;
-  return 3 * 3 * n + n + bh * ((N + 127) / 128) * kBinCount;
+  return 3 * 3 * n + n + bh * ((N + 127) / 128) * kBinCount + n;
 }
 }  // namespace
 
@@ -654,15 +654,18 @@ size_t stream_bwd_workspace(int B, int H, int N, int d, int terms) {
 
 // Sums of the gradient shares in a fixed order: dx_res over heads (the row,
 // column and centroid shares whose bits are set in `shares`), dw_dist over
-// batch elements and rows, dpos_weight over batch elements and row blocks.
+// batch elements and rows, dpos_weight over batch elements and row blocks,
+// dr_head over batch elements and rows.
 __global__ void stream_costgrad_finalize(const float* dx_row, const float* dx_col, const float* dx_t,
-                                         const float* dw, const float* dpos, int shares, int B, int H, int N,
-                                         float* dx_res, float* dw_dist, float* dpos_weight) {
+                                         const float* dw, const float* dpos, const float* dr, int shares, int B,
+                                         int H, int N, float* dx_res, float* dw_dist, float* dpos_weight,
+                                         float* dr_head) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   const int nrb = (N + 127) / 128;
   const int ndx = dx_res != nullptr ? B * N * 3 : 0;
   const int ndw = dw_dist != nullptr ? H : 0;
   const int npos = dpos_weight != nullptr ? H * kBinCount : 0;
+  const int ndr = dr_head != nullptr ? H : 0;
   if (t < ndx) {
     const int b = t / (N * 3), rem = t % (N * 3);
     float s = 0.0f;
@@ -685,6 +688,12 @@ __global__ void stream_costgrad_finalize(const float* dx_row, const float* dx_co
     for (int b = 0; b < B; ++b)
       for (int r = 0; r < nrb; ++r) s += dpos[((static_cast<size_t>(b) * H + h) * nrb + r) * kBinCount + bin];
     dpos_weight[u] = s;
+  } else if (t < ndx + ndw + npos + ndr) {
+    const int h = t - ndx - ndw - npos;
+    float s = 0.0f;
+    for (int b = 0; b < B; ++b)
+      for (int i = 0; i < N; ++i) s += dr[(static_cast<size_t>(b) * H + h) * N + i];
+    dr_head[h] = s;
   }
 }
 
@@ -786,13 +795,15 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
   }
   const bool geo = bp.x_res != nullptr && bp.w_dist != nullptr;
   auto terms = [&](bool transposed) {
-    return cost_terms_of(bp.pos_weight, geo ? bp.x_res : nullptr, bp.w_dist, bp.r_0, N, bins, bins_t, transposed);
+    return cost_terms_of(bp.pos_weight, geo ? bp.x_res : nullptr, bp.w_dist, bp.r_0, bp.r_head, N, bins, bins_t,
+                         transposed);
   };
   float* cg_dx_row = cgw;
   float* cg_dx_col = cgw ? cgw + 3 * n : nullptr;
   float* cg_dx_t = cgw ? cgw + 6 * n : nullptr;
   float* cg_dw = cgw ? cgw + 9 * n : nullptr;
   float* cg_dpos = cgw ? cgw + 10 * n : nullptr;
+  float* cg_dr = cgw ? cg_dpos + static_cast<size_t>(B) * H * ((N + 127) / 128) * kBinCount : nullptr;
   const bool want_dx = cgw != nullptr && bp.dx_res != nullptr;
   BtArgs ba{};
   ba.d = d;
@@ -925,6 +936,7 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         ba.ct = terms(false);
         if (want_dx && geo) ba.cg.dx = cg_dx_row;
         if (cgw != nullptr && bp.dw_dist != nullptr && geo) ba.cg.dw = cg_dw;
+        if (cgw != nullptr && bp.dr_head != nullptr && geo) ba.cg.dr = cg_dr;
         if (cgw != nullptr && bp.dpos_weight != nullptr && bins != nullptr) ba.cg.dpos = cg_dpos;
         return launch_bt_pass(BTP_DQ, ba, st);
       }
@@ -955,14 +967,17 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
         float* dx_out = want_dx ? bp.dx_res : nullptr;
         float* dw_out = geo ? bp.dw_dist : nullptr;
         float* dpos_out = bins != nullptr ? bp.dpos_weight : nullptr;
+        float* dr_out = geo ? bp.dr_head : nullptr;
         if (dx_out != nullptr && shares == 0) {  // x_res enters neither the cost nor the loss
           if ((e = cudaMemsetAsync(dx_out, 0, sizeof(float) * B * N * 3, st)) != cudaSuccess) return e;
           dx_out = nullptr;
         }
-        const int cnt = (dx_out ? B * N * 3 : 0) + (dw_out ? H : 0) + (dpos_out ? H * kBinCount : 0);
+        const int cnt =
+            (dx_out ? B * N * 3 : 0) + (dw_out ? H : 0) + (dpos_out ? H * kBinCount : 0) + (dr_out ? H : 0);
         if (cnt == 0) return cudaSuccess;
         stream_costgrad_finalize<<<(cnt + 255) / 256, 256, 0, st>>>(cg_dx_row, cg_dx_col, cg_dx_t, cg_dw, cg_dpos,
-                                                                    shares, B, H, N, dx_out, dw_out, dpos_out);
+                                                                    cg_dr, shares, B, H, N, dx_out, dw_out,
+                                                                    dpos_out, dr_out);
         return cudaGetLastError();
       }
       q.Aop = bp.K; q.Bop = bp.Q; q.A2op = bp.V; q.B2op = bp.dO; q.b2_f32 = 1;

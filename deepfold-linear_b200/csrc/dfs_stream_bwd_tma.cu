@@ -95,7 +95,7 @@ struct BTileCfg {
   static constexpr uint32_t OFF_B3 = OFF_B + NS * SB;
   static constexpr uint32_t OFF_DS = OFF_B3 + (kAcc ? NS3 * B3TILE : 0u);   // 128 x 64 fp32
   static constexpr uint32_t OFF_VEC = OFF_DS + (kAcc ? 128u * kBTW * 4 : 0u);
-  static constexpr int NMRG = TERMS ? 4 : 3;                          // values merged per row
+  static constexpr int NMRG = TERMS ? 5 : 3;                          // values merged per row (dx, dw, dr)
   static constexpr uint32_t OFF_MRG = OFF_VEC + NS * VEC;                // 3 parts x NMRG values x 128
   static constexpr uint32_t OFF_PW = OFF_MRG + 3 * NMRG * 128 * 4;       // TERMS: 69 scaled bin weights
   static constexpr bool kHist = TERMS && MODE == BT_DQ;
@@ -351,10 +351,11 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
     // row's coordinates; gradient shares of the shared cost parameters
     float* pws = reinterpret_cast<float*>(base + C::OFF_PW);
     const bool use_bins = TERMS && p.ct.bins != nullptr, use_geo = TERMS && p.ct.x != nullptr;
-    float xi[3] = {0.0f, 0.0f, 0.0f}, wS = 0.0f, w_h = 0.0f;
+    float xi[3] = {0.0f, 0.0f, 0.0f}, wS = 0.0f, w_h = 0.0f, r_h = 1.0f;
     const uint8_t* brow = nullptr;
-    float gdx[3] = {0.0f, 0.0f, 0.0f}, gdw = 0.0f;  // this row's dx share and dw share (this part)
-    const bool want_geo_grad = TERMS && use_geo && (p.cg.dx != nullptr || p.cg.dw != nullptr) &&
+    // this row's dx, dw and dr shares (this part); gdr sums dC dist / (r_h + dist)^2
+    float gdx[3] = {0.0f, 0.0f, 0.0f}, gdw = 0.0f, gdr = 0.0f;
+    const bool want_geo_grad = TERMS && use_geo && (p.cg.dx != nullptr || p.cg.dw != nullptr || p.cg.dr != nullptr) &&
                                (MODE == BT_DQ || MODE == BT_DK);
     const bool want_hist = C::kHist && use_bins && p.cg.dpos != nullptr;
     const bool want_cent_grad = MODE == BT_COL && p.cg.dx != nullptr && p.xvec != nullptr;
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       if (use_bins && tid <= kBinCount) pws[tid] = tid < kBinCount ? p.ct.pos_weight[hh * kBinCount + tid] * nsc : 0.0f;
       if (use_geo) {
         w_h = p.ct.w_dist[hh];
+        r_h = geo_scale(p.ct, hh);
         wS = w_h * nsc;
         if (rin) {
 #pragma unroll
@@ -410,7 +412,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
           if (use_geo) {
             const float d0 = xi[0] - vb[8 * kBTW + k], d1 = xi[1] - vb[9 * kBTW + k], d2 = xi[2] - vb[10 * kBTW + k];
             const float dist = sqrtf(fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, 1e-8f))));
-            t = fmaf(wS, __fdividef(dist, p.ct.r_0 + dist), t);
+            t = fmaf(wS, __fdividef(dist, r_h + dist), t);
           }
           tm[k] = t;
         }
@@ -508,9 +510,13 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
             const float dC = -out[k] * inv_eps;
             const float d0 = xi[0] - vb[8 * kBTW + k], d1 = xi[1] - vb[9 * kBTW + k], d2 = xi[2] - vb[10 * kBTW + k];
             const float dist = sqrtf(fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, 1e-8f))));
-            const float rd = __fdividef(1.0f, p.ct.r_0 + dist);
-            if (MODE == BT_DQ) gdw = fmaf(dC, dist * rd, gdw);
-            const float cf = __fdividef(dC * w_h * p.ct.r_0 * rd * rd, dist);
+            const float rd = __fdividef(1.0f, r_h + dist);
+            if (MODE == BT_DQ) {
+              const float t = dC * dist * rd;
+              gdw += t;
+              gdr = fmaf(t, rd, gdr);
+            }
+            const float cf = __fdividef(dC * w_h * r_h * rd * rd, dist);
             gdx[0] = fmaf(cf, d0, gdx[0]);
             gdx[1] = fmaf(cf, d1, gdx[1]);
             gdx[2] = fmaf(cf, d2, gdx[2]);
@@ -605,15 +611,18 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
     }
     // ---- shares of the shared-parameter gradients: merge the four column parts per row
     if constexpr (TERMS || MODE == BT_COL) {
-      if (p.cg.dx != nullptr || p.cg.dw != nullptr) {
+      if (p.cg.dx != nullptr || p.cg.dw != nullptr || p.cg.dr != nullptr) {
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kBEpiWarps) : "memory");  // mrg free again
-        constexpr int NV = C::NMRG >= 4 ? 4 : 3;
+        constexpr int NV = C::NMRG;
         if (part > 0) {
           float* mp = mrg + (part - 1) * C::NMRG * 128;
           mp[lrow] = gdx[0];
           mp[128 + lrow] = gdx[1];
           mp[256 + lrow] = gdx[2];
-          if constexpr (NV == 4) mp[384 + lrow] = gdw;
+          if constexpr (NV == 5) {
+            mp[384 + lrow] = gdw;
+            mp[512 + lrow] = gdr;
+          }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kBEpiWarps) : "memory");
         if (part == 0 && rin) {
@@ -623,7 +632,10 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
             gdx[0] += mp[lrow];
             gdx[1] += mp[128 + lrow];
             gdx[2] += mp[256 + lrow];
-            if constexpr (NV == 4) gdw += mp[384 + lrow];
+            if constexpr (NV == 5) {
+              gdw += mp[384 + lrow];
+              gdr += mp[512 + lrow];
+            }
           }
           const size_t o = bh * N + row;
           if (p.cg.dx != nullptr) {
@@ -632,6 +644,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
             p.cg.dx[o * 3 + 2] = rok ? gdx[2] : 0.0f;
           }
           if (MODE == BT_DQ && p.cg.dw != nullptr) p.cg.dw[o] = rok ? gdw : 0.0f;
+          if (MODE == BT_DQ && p.cg.dr != nullptr) p.cg.dr[o] = rok ? -w_h * gdr : 0.0f;
         }
       }
     }

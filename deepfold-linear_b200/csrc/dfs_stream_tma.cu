@@ -395,13 +395,14 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     constexpr bool has_terms = TERMS;
     float* pws = reinterpret_cast<float*>(base + C::OFF_PW);
     const float* cxs = reinterpret_cast<const float*>(base + C::OFF_CX);
-    float xi0 = 0.0f, xi1 = 0.0f, xi2 = 0.0f, wS = 0.0f;
+    float xi0 = 0.0f, xi1 = 0.0f, xi2 = 0.0f, wS = 0.0f, r_h = 1.0f;
     const uint8_t* brow = nullptr;
     if constexpr (has_terms) {
       const float nsc = -kLog2e / eps_h;
       if (use_bins && tid <= kBinCount) pws[tid] = tid < kBinCount ? p.ct.pos_weight[hh * kBinCount + tid] * nsc : 0.0f;
       if (use_geo) {
         wS = p.ct.w_dist[hh] * nsc;
+        r_h = geo_scale(p.ct, hh);
         if (rin) {
           const float* xr = p.ct.x + (static_cast<size_t>(bb) * N + row) * 3;
           xi0 = xr[0];
@@ -449,7 +450,7 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
           if (use_geo) {
             const float d0 = xi0 - xs[k], d1 = xi1 - xs[128 + k], d2 = xi2 - xs[256 + k];
             const float dist = sqrtf(fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, 1e-8f))));
-            t = fmaf(wS, __fdividef(dist, p.ct.r_0 + dist), t);
+            t = fmaf(wS, __fdividef(dist, r_h + dist), t);
           }
           x[k] = fmaf(__uint_as_float(rv32[k]), scale, t);
         }

@@ -2,7 +2,8 @@
 //
 // FlashSinkhornFn is the autograd function behind deepfold's flash_sinkhorn
 // (reference: FlashSinkhornFunction, src/deepfold/model/kernels/
-// sinkhorn_kernel.py:1923-2382).  Its forward and backward validate shapes,
+// sinkhorn_kernel.py:1923-2382); BalancedTransportFn the one behind
+// balanced_sinkhorn_transport(_dual) (flash_sinkhorn_transport.py:287-545).  Its forward and backward validate shapes,
 // allocate outputs with the caching allocator and call dfs_fwd / dfs_bwd of the
 // C ABI on the current stream; nothing here computes.  Doing this in C++
 // rather than Python keeps the per-call host cost to a few allocations, so the
@@ -19,7 +20,10 @@
 #include <ATen/cuda/CUDAEvent.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cmath>
+#include <limits>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -393,6 +397,287 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
   }
 };
 
+// Balanced Sinkhorn transport of the reference's trunk block
+// (BalancedSinkhornFn / BalancedSinkhornDualFn, src/deepfold/model/kernels/
+// flash_sinkhorn_transport.py:287-545): cosine cost
+//     C_ij = (1 - w_h)(1 - q_i.k_j) + w_h dist_ij / (r_h + dist_ij),
+//     w_h = sigmoid(alpha_h),  r_h = max(|r_param_h|, 0.1),
+// K_iter x (column update, row update) with uniform marginals, then
+// x_centroid = T_norm x and (dual) h_centroid = T_norm V.  It runs on the same
+// library calls as flash_sinkhorn, after a change of parameters:
+//   - the constant (1 - w_h) of C shifts every logit of a problem equally and
+//     cancels in T_norm (the potentials absorb it), so only
+//     -C/eps = (1-w) q.k / eps - w g / eps matters, which is the library's
+//     cost -C'/eps' with C' = -q.k/sqrt(D) + w' g at
+//         eps' = eps / ((1 - w) sqrt(D)),   w' = w / ((1 - w) sqrt(D))
+//     (D the head dim the library runs, the larger of d and V's width, the
+//     narrower operands zero-padded -- exact for every product);
+//   - the per-head r_h is the library's r_head;
+//   - the reference updates the columns first.  The library's iteration is
+//     rows first, so the first call runs it on the transposed problem (Q and K
+//     swapped; the geometry term, the masks and the uniform marginals are
+//     symmetric), whose rows are the original columns: K_iter x (column, row)
+//     exactly.  A second call with K_iter = 0 and those potentials as warm
+//     starts writes T_norm x and T_norm V;
+//   - the marginals: 1/n_b per valid point.  The reference's device path uses
+//     one batch-mean constant instead; a constant change of the marginals only
+//     shifts the column potential and leaves T_norm unchanged.
+// The backward is the library's implicit-function gradient at those
+// potentials; the gradients of alpha_h and r_h follow by the chain rule:
+//     dL/dalpha_h = w_h (-sum_{b,i} q_i.dq_i + dw'_h / sqrt(D)),
+//     dL/dr_param_h = dL/dr_h sign(r_param_h) [|r_param_h| >= 0.1]
+// (the first because dL/dS summed over a problem is 0: a constant logit shift
+// changes nothing).  Padded rows (mask 0) of both outputs are 0.
+struct BalancedTransportFn : public torch::autograd::Function<BalancedTransportFn> {
+  // Arguments: 0 Q, 1 K, 2 x_res, 3 V (optional), 4 eps, 5 alpha_h, 6 r_h,
+  // 7 mask (optional), 8 K_iter, 9 cg_rtol, 10 cg_atol, 11 cg_max_iter.
+  static variable_list forward(AutogradContext* ctx, Tensor Q, Tensor K, Tensor x_res, c10::optional<Tensor> V,
+                               Tensor eps, Tensor alpha_h, Tensor r_h, c10::optional<Tensor> mask, int64_t K_iter,
+                               double cg_rtol, double cg_atol, int64_t cg_max_iter) {
+    require(Q.is_cuda() && K.is_cuda() && x_res.is_cuda(),
+            "deepfold B200 Sinkhorn ops run on CUDA tensors only (no CPU path)");
+    require(Q.dim() == 4 && K.sizes() == Q.sizes(), "Q_s and K_s must share the shape (B, H, N, d_h)");
+    const int64_t B = Q.size(0), H = Q.size(1), N = Q.size(2), d = Q.size(3);
+    require(x_res.dim() == 3 && x_res.size(0) == B && x_res.size(1) == N && x_res.size(2) == 3,
+            "x_res must have the shape (B, N, 3)");
+    const bool dual = V.has_value() && V->defined();
+    const int64_t dv = dual ? V->size(3) : d;
+    if (dual)
+      require(V->dim() == 4 && V->size(0) == B && V->size(1) == H && V->size(2) == N,
+              "V_h must have the shape (B, H, N, D_V)");
+    const int64_t D = std::max(d, dv);
+    if (D > 64 || N > dfs_max_n(static_cast<int>(D)))
+      fail("N=" + std::to_string(N) + ", head dim " + std::to_string(D) +
+           " is outside the kernels' range (head dim <= 64)");
+    require(eps.numel() == H && alpha_h.numel() == H && r_h.numel() == H, "eps, alpha_h and r_h must have H entries");
+    require(K_iter >= 0, "K_iter must be >= 0");
+    if (mask.has_value() && mask->defined())
+      require(mask->dim() == 2 && mask->size(0) == B && mask->size(1) == N, "mask must have the shape (B, N)");
+    const DeviceSwitch guard(Q.device());
+    check_device_status(Q.device());
+    const auto st = Q.scalar_type();
+    const auto cdt = (st == at::kBFloat16 || st == at::kHalf || st == at::kFloat) ? st : at::kFloat;
+    auto widen = [&](const Tensor& t) {
+      const Tensor c = t.contiguous().to(cdt);
+      return t.size(3) < D ? at::constant_pad_nd(c, {0, D - t.size(3)}).contiguous() : c;
+    };
+    const Tensor Qc = widen(Q), Kc = widen(K);
+    const Tensor Vc = dual ? widen(*V) : Tensor();
+    const auto fo = Q.options().dtype(at::kFloat);
+    const Tensor xr = x_res.contiguous().to(at::kFloat);
+    const Tensor w = at::sigmoid(alpha_h.reshape({H}).to(at::kFloat));
+    const Tensor rh = r_h.reshape({H}).to(at::kFloat);
+    const Tensor r = at::clamp_min(at::abs(rh), 0.1).contiguous();
+    const double qs = 1.0 / std::sqrt(static_cast<double>(D));
+    const Tensor epsp = (eps.reshape({H}).to(at::kFloat) * qs / (1.0 - w)).contiguous();
+    const Tensor wdp = (w * qs / (1.0 - w)).contiguous();
+    Tensor mk, counts;
+    if (mask.has_value() && mask->defined()) {
+      mk = (mask->to(at::kFloat) > 0.5).to(at::kFloat).contiguous();
+      counts = at::clamp_min(mk.sum(1), 1.0);
+    } else {
+      counts = at::full({B}, static_cast<double>(N), fo);
+    }
+    const Tensor lm = (-at::log(counts)).view({B, 1, 1}).expand({B, H, N}).contiguous();
+    Tensor lu_t = at::empty({B, H, N}, fo), lv_t = at::empty({B, H, N}, fo);
+    Tensor lu = at::empty({B, H, N}, fo), lv = at::empty({B, H, N}, fo);
+    Tensor O = at::empty({B, H, N, D}, fo), xc = at::empty({B, H, N, 3}, fo);
+    Tensor status = device_status(Q.device()).word;
+
+    dfs_problem prob{};
+    prob.B = static_cast<int32_t>(B);
+    prob.H = static_cast<int32_t>(H);
+    prob.N = static_cast<int32_t>(N);
+    prob.d = static_cast<int32_t>(D);
+    prob.in_dtype = dtype_code(cdt);
+    prob.cost_mode = DFS_COST_QK;
+    prob.K_iter = static_cast<int32_t>(K_iter);
+    prob.check_every = 2;
+    prob.lam = std::numeric_limits<float>::infinity();
+    prob.r_0 = 1.0f;  // unused: r_head is given
+    prob.cost_terms = DFS_TERM_GEO | DFS_TERM_XRES;
+    size_t fwd_ws = 0, bwd_ws = 0;
+    check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
+    Tensor ws = fwd_ws ? at::empty({static_cast<int64_t>((fwd_ws + 3) / 4)}, fo) : Tensor();
+    const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(Q.device().index());
+    // 1. the potentials: rows of the transposed problem are the original columns
+    dfs_fwd_args a{};
+    a.Q = Kc.data_ptr();
+    a.K = Qc.data_ptr();
+    a.x_res = xr.data_ptr<float>();
+    a.eps = epsp.data_ptr<float>();
+    a.w_dist = wdp.data_ptr<float>();
+    a.r_head = r.data_ptr<float>();
+    a.log_mu = lm.data_ptr<float>();
+    a.log_nu = lm.data_ptr<float>();
+    a.mask = ptr_or_null<const float>(mk);
+    a.log_u = lv_t.data_ptr<float>();  // column potential of the original problem
+    a.log_v = lu_t.data_ptr<float>();
+    a.status = status.data_ptr<int32_t>();
+    check_rc(dfs_fwd(&prob, &a, ws.defined() ? ws.data_ptr() : nullptr, fwd_ws, cstream.stream()), "dfs_fwd");
+    // 2. T_norm x and T_norm V from those potentials (the single variant passes Q
+    //    as V and drops O: the streamed kernels write x_centroid with O)
+    dfs_problem out_prob = prob;
+    out_prob.K_iter = 0;
+    dfs_fwd_args o{};
+    o.Q = Qc.data_ptr();
+    o.K = Kc.data_ptr();
+    o.V = dual ? Vc.data_ptr() : Qc.data_ptr();
+    o.x_res = a.x_res;
+    o.eps = a.eps;
+    o.w_dist = a.w_dist;
+    o.r_head = a.r_head;
+    o.log_mu = a.log_mu;
+    o.log_nu = a.log_nu;
+    o.log_u_init = lu_t.data_ptr<float>();
+    o.log_v_init = lv_t.data_ptr<float>();
+    o.mask = a.mask;
+    o.O = O.data_ptr<float>();
+    o.x_centroid = xc.data_ptr<float>();
+    o.log_u = lu.data_ptr<float>();
+    o.log_v = lv.data_ptr<float>();
+    o.status = a.status;
+    check_rc(dfs_fwd(&out_prob, &o, ws.defined() ? ws.data_ptr() : nullptr, fwd_ws, cstream.stream()), "dfs_fwd");
+    {
+      std::lock_guard<std::mutex> lock(g_status_mu);
+      start_readback(device_status(Q.device()), cstream.stream());
+    }
+
+    ctx->save_for_backward({Qc, Kc, Vc, xr, epsp, wdp, r, lm, mk, lu, lv, w, rh});
+    ctx->saved_data["K_iter"] = K_iter;
+    ctx->saved_data["cg_rtol"] = cg_rtol;
+    ctx->saved_data["cg_atol"] = cg_atol;
+    ctx->saved_data["cg_max_iter"] = cg_max_iter;
+    ctx->saved_data["fwd_status"] = status;
+    ctx->saved_data["d"] = d;
+    ctx->saved_data["dv"] = dv;
+    ctx->saved_data["q_dtype"] = static_cast<int64_t>(Q.scalar_type());
+    ctx->saved_data["x_dtype"] = static_cast<int64_t>(x_res.scalar_type());
+    ctx->saved_data["v_dtype"] = static_cast<int64_t>(dual ? V->scalar_type() : Q.scalar_type());
+    ctx->saved_data["a_dtype"] = static_cast<int64_t>(alpha_h.scalar_type());
+    ctx->saved_data["r_dtype"] = static_cast<int64_t>(r_h.scalar_type());
+    int64_t edge = 3;  // Q, K, x_res are edges 0..2
+    ctx->saved_data["e_v"] = dual ? edge++ : int64_t(-1);
+    if (V.has_value() && !dual) ++edge;
+    ++edge;  // eps
+    ctx->saved_data["e_alpha"] = edge++;
+    ctx->saved_data["e_r"] = edge++;
+    // outputs in fp32 (float64 for float64 inputs), as the reference's device path
+    // returns them (it computes on fp32 copies)
+    const auto out_dt = st == at::kDouble ? at::kDouble : at::kFloat;
+    const Tensor xo = xc.to(out_dt);
+    if (!dual) return {xo};
+    return {xo, O.narrow(3, 0, dv).to(out_dt)};
+  }
+
+  static variable_list backward(AutogradContext* ctx, variable_list grads) {
+    const auto saved = ctx->get_saved_variables();
+    const DeviceSwitch guard(saved[0].device());
+    check_device_status(saved[0].device());
+    const Tensor &Qc = saved[0], &Kc = saved[1], &Vc = saved[2], &xr = saved[3], &epsp = saved[4],
+                 &wdp = saved[5], &r = saved[6], &lm = saved[7], &mk = saved[8], &lu = saved[9], &lv = saved[10],
+                 &w = saved[11], &rh = saved[12];
+    const bool dual = Vc.defined();
+    auto needs = [&](const char* key) {
+      const int64_t e = ctx->saved_data[key].toInt();
+      return e >= 0 && ctx->needs_input_grad(static_cast<size_t>(e));
+    };
+    const int64_t B = Qc.size(0), H = Qc.size(1), N = Qc.size(2), D = Qc.size(3);
+    const int64_t d = ctx->saved_data["d"].toInt(), dv = ctx->saved_data["dv"].toInt();
+    const auto fo = Qc.options().dtype(at::kFloat);
+    const bool want_alpha = needs("e_alpha"), want_r = needs("e_r");
+    const Tensor dxc = grads[0].defined() ? grads[0].contiguous().to(at::kFloat) : Tensor();
+    Tensor dO;
+    if (dual && grads.size() > 1 && grads[1].defined()) {
+      dO = grads[1].contiguous().to(at::kFloat);
+      if (dv < D) dO = at::constant_pad_nd(dO, {0, D - dv}).contiguous();
+    } else {
+      dO = at::zeros({B, H, N, D}, fo);
+    }
+    Tensor dQ = (ctx->needs_input_grad(0) || want_alpha) ? at::empty({B, H, N, D}, fo) : Tensor();
+    Tensor dK = ctx->needs_input_grad(1) ? at::empty({B, H, N, D}, fo) : Tensor();
+    Tensor dV = (dual && needs("e_v")) ? at::empty({B, H, N, D}, fo) : Tensor();
+    Tensor dx = ctx->needs_input_grad(2) ? at::empty({B, N, 3}, fo) : Tensor();
+    Tensor dwd = want_alpha ? at::empty({H}, fo) : Tensor();
+    Tensor dr = want_r ? at::empty({H}, fo) : Tensor();
+    Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
+    Tensor resid = at::empty({B * H}, fo);
+    Tensor status = device_status(Qc.device()).word;
+
+    dfs_problem prob{};
+    prob.B = static_cast<int32_t>(B);
+    prob.H = static_cast<int32_t>(H);
+    prob.N = static_cast<int32_t>(N);
+    prob.d = static_cast<int32_t>(D);
+    prob.in_dtype = dtype_code(Qc.scalar_type());
+    prob.cost_mode = DFS_COST_QK;
+    prob.K_iter = static_cast<int32_t>(ctx->saved_data["K_iter"].toInt());
+    prob.check_every = 2;
+    prob.lam = std::numeric_limits<float>::infinity();
+    prob.r_0 = 1.0f;
+    prob.cost_terms = DFS_TERM_GEO | DFS_TERM_XRES;
+    dfs_cg_params cg{};
+    cg.rtol = static_cast<float>(ctx->saved_data["cg_rtol"].toDouble());
+    cg.atol = static_cast<float>(ctx->saved_data["cg_atol"].toDouble());
+    cg.max_iter = static_cast<int32_t>(ctx->saved_data["cg_max_iter"].toInt());
+    dfs_bwd_args a{};
+    a.Q = Qc.data_ptr();
+    a.K = Kc.data_ptr();
+    a.V = dual ? Vc.data_ptr() : Qc.data_ptr();
+    a.x_res = xr.data_ptr<float>();
+    a.eps = epsp.data_ptr<float>();
+    a.w_dist = wdp.data_ptr<float>();
+    a.r_head = r.data_ptr<float>();
+    a.log_mu = lm.data_ptr<float>();
+    a.log_nu = lm.data_ptr<float>();
+    a.mask = ptr_or_null<const float>(mk);
+    a.log_u = lu.data_ptr<float>();
+    a.log_v = lv.data_ptr<float>();
+    a.dO = dO.data_ptr<float>();
+    a.dxc = ptr_or_null<const float>(dxc);
+    a.dQ = ptr_or_null<float>(dQ);
+    a.dK = ptr_or_null<float>(dK);
+    a.dV = ptr_or_null<float>(dV);
+    a.dx_res = ptr_or_null<float>(dx);
+    a.dw_dist = ptr_or_null<float>(dwd);
+    a.dr_head = ptr_or_null<float>(dr);
+    a.cg_iters = iters.data_ptr<int32_t>();
+    a.cg_residual = resid.data_ptr<float>();
+    a.status = status.data_ptr<int32_t>();
+    size_t fwd_ws = 0, bwd_ws = 0;
+    check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
+    Tensor ws = bwd_ws ? at::empty({static_cast<int64_t>((bwd_ws + 3) / 4)}, fo) : Tensor();
+    const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(Qc.device().index());
+    check_rc(dfs_bwd(&prob, &cg, &a, ws.defined() ? ws.data_ptr() : nullptr, bwd_ws, cstream.stream()), "dfs_bwd");
+    {
+      std::lock_guard<std::mutex> lock(g_status_mu);
+      start_readback(device_status(Qc.device()), cstream.stream());
+    }
+    last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
+
+    auto as = [&](const Tensor& g, const char* key) {
+      return g.to(static_cast<at::ScalarType>(ctx->saved_data[key].toInt()));
+    };
+    variable_list out(12);
+    if (dQ.defined() && ctx->needs_input_grad(0)) out[0] = as(dQ.narrow(3, 0, d), "q_dtype");
+    if (dK.defined()) out[1] = as(dK.narrow(3, 0, d), "q_dtype");
+    if (dx.defined()) out[2] = as(dx, "x_dtype");
+    if (dV.defined()) out[3] = as(dV.narrow(3, 0, dv), "v_dtype");
+    if (want_alpha) {
+      const Tensor qdq = (Qc.to(at::kFloat) * dQ).sum({0, 2, 3});
+      out[5] = as(w * (dwd * (1.0 / std::sqrt(static_cast<double>(D))) - qdq), "a_dtype");
+    }
+    if (want_r) out[6] = as(dr * at::sign(rh) * (at::abs(rh) >= 0.1).to(at::kFloat), "r_dtype");
+    return out;
+  }
+};
+
+std::vector<Tensor> balanced_transport_autograd(Tensor Q, Tensor K, Tensor x_res, c10::optional<Tensor> V,
+                                                Tensor eps, Tensor alpha_h, Tensor r_h, c10::optional<Tensor> mask,
+                                                int64_t K_iter, double cg_rtol, double cg_atol, int64_t cg_max_iter) {
+  return BalancedTransportFn::apply(Q, K, x_res, V, eps, alpha_h, r_h, mask, K_iter, cg_rtol, cg_atol, cg_max_iter);
+}
+
 std::vector<Tensor> flash_sinkhorn_autograd(Tensor Q, Tensor K, Tensor V, c10::optional<Tensor> x_res,
                                             c10::optional<Tensor> pos_weight, c10::optional<Tensor> pos_bins,
                                             Tensor eps, c10::optional<Tensor> w_dist, Tensor log_mu,
@@ -410,6 +695,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "native autograd glue for libdfsink (flash Sinkhorn forward / IFT backward)";
   m.def("flash_sinkhorn", &flash_sinkhorn_autograd,
         "FlashSinkhornFn.apply: returns [O, x_centroid, log_u, log_v], or [O, log_u, log_v] without x_res");
+  m.def("balanced_transport", &balanced_transport_autograd,
+        "BalancedTransportFn.apply: returns [x_centroid], or [x_centroid, h_centroid] with V");
   m.def("last_report", []() { return last_report(); },
         "[cg_iters, cg_residual, status, fwd_status] of the most recent backward (status: the device's sticky "
         "status word, the OR of every call's bits since the last check)");

@@ -60,7 +60,8 @@ DFS_TERM_POS, DFS_TERM_GEO, DFS_TERM_XRES = 1, 2, 4
 class DfsFwdArgs(ctypes.Structure):
     _fields_ = [(n, _P) for n in (
         "Q", "K", "V", "C", "x_res", "pos_weight", "pos_bins", "eps", "w_dist", "log_mu", "log_nu",
-        "log_u_init", "log_v_init", "mask", "O", "x_centroid", "log_u", "log_v", "status", "T_norm")]
+        "log_u_init", "log_v_init", "mask", "O", "x_centroid", "log_u", "log_v", "status", "T_norm",
+        "r_head")]
 
 
 class DfsCgParams(ctypes.Structure):
@@ -72,7 +73,7 @@ class DfsBwdArgs(ctypes.Structure):
     _fields_ = [(n, _P) for n in (
         "Q", "K", "V", "x_res", "pos_weight", "pos_bins", "eps", "w_dist", "log_mu", "log_nu", "mask",
         "log_u", "log_v", "dO", "dxc", "dQ", "dK", "dV", "dlog_mu", "dlog_nu", "dx_res",
-        "dpos_weight", "dw_dist", "cg_iters", "cg_residual", "status")]
+        "dpos_weight", "dw_dist", "cg_iters", "cg_residual", "status", "r_head", "dr_head")]
 
 
 class DfsIpcHandle(ctypes.Structure):

@@ -4,7 +4,8 @@
  * One (batch, head) pair is one optimal-transport problem.  For each problem
  * the library runs the log-domain (un)balanced Sinkhorn iteration of the
  * reference (vv137/deepfold-linear) on the log-kernel S = -C/eps with
- *     C_ij = -q_i.k_j/sqrt(d) + pos_weight[h, bins_ij] + w_h * dist_ij/(r_0+dist_ij),
+ *     C_ij = -q_i.k_j/sqrt(d) + pos_weight[h, bins_ij] + w_h * dist_ij/(r_h+dist_ij),
+ * (r_h = r_head[h] when given, else the problem's r_0),
  * produces the row-normalised transport output O = T_norm V (and the optional
  * centroid T_norm x), and differentiates it with the implicit-function theorem,
  * solving the adjoint system by conjugate gradient on the device.
@@ -35,7 +36,7 @@
 extern "C" {
 #endif
 
-#define DFS_ABI_VERSION 1
+#define DFS_ABI_VERSION 2
 
 /* return / status codes */
 enum {
@@ -105,6 +106,7 @@ typedef struct {
   int32_t* status;          /* device int32, error bits OR-ed in; or NULL            */
   float* T_norm;            /* (B,H,N,N) row-normalised plan, or NULL (materialises  */
                             /* the plan: only for the dense compute_transport_output)*/
+  const float* r_head;      /* (H,) per-head geometry scale r_h (> 0), or NULL: r_0  */
 } dfs_fwd_args;
 
 typedef struct {
@@ -137,6 +139,9 @@ typedef struct {
   int32_t* cg_iters;
   float* cg_residual;
   int32_t* status;
+  /* per-head geometry scale (same as the forward's) and its gradient */
+  const float* r_head;      /* (H,) r_h, or NULL: r_0                                */
+  float* dr_head;           /* (H,) dL/dr_h, or NULL; needs x_res and w_dist         */
 } dfs_bwd_args;
 
 /* Library ABI version (DFS_ABI_VERSION of the build). */

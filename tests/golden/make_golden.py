@@ -1,4 +1,5 @@
-"""Generate the golden vectors that pin ``oracle/sinkhorn_oracle.py``.
+"""Generate the golden vectors that pin ``oracle/sinkhorn_oracle.py``,
+``oracle/sinkhorn_torch.py`` and ``oracle/transport_torch.py``.
 
 Run from the repository root on a machine that has the reference source:
 
@@ -8,7 +9,9 @@ Every output stored here is produced by the reference's own torch code
 (``deepfold.model.sinkhorn.sinkhorn_solve`` / ``compute_transport_output``,
 ``deepfold.model.kernels.flash_sinkhorn_attn.flash_sinkhorn_attn`` on CPU, and
 torch autograd through them, the gradient oracle the reference itself uses in
-tests/test_triton_fallback_consistency.py:316-355).  Inputs are drawn here from
+tests/test_triton_fallback_consistency.py:316-355; for the balanced transport,
+``deepfold.model.kernels.flash_sinkhorn_transport``'s Triton kernels executed by
+Triton's CPU interpreter, and its CPU path).  Inputs are drawn here from
 seeded numpy generators and saved alongside, so the fixtures are
 self-contained and the GPU box never needs the reference.
 """
@@ -17,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import os
+import subprocess
 import sys
 
 import numpy as np
@@ -89,6 +93,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("DEEPFOLD_REF_SRC"),
                     help="the reference's src directory (or set DEEPFOLD_REF_SRC)")
+    ap.add_argument("--balanced-only", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if not args.ref:
         ap.error("pass --ref <reference src directory> or set DEEPFOLD_REF_SRC")
@@ -107,6 +112,10 @@ def main():
         arrs.update({f"meta_{k}": np.asarray(v) for k, v in meta.items()})
         np.savez_compressed(path, **arrs)
         print(name, os.path.getsize(path), "bytes")
+
+    if args.balanced_only:
+        balanced_fixtures(torch, save)
+        return
 
     # 1) pure QK^T cost, balanced, converged: dense path + autograd
     r = np.random.default_rng(101)
@@ -210,6 +219,63 @@ def main():
         outs["log_v_" + key] = lv.numpy()
     save("solve_early_stop", dict(C=C, log_mu=lmu, log_nu=lnu, eps=eps), outs,
          K_iter=100, lam=1.0)
+
+    env = dict(os.environ, TRITON_INTERPRET="1")
+    subprocess.run([sys.executable, os.path.abspath(__file__), "--ref", args.ref, "--balanced-only"], env=env,
+                   check=True)
+
+
+def balanced_fixtures(torch, save):
+    # 6) balanced transport of the trunk block (flash_sinkhorn_transport.py):
+    #    the reference's device path -- its Triton kernels, forward and unrolled
+    #    backward, run by Triton's CPU interpreter -- on a padded batch, and its
+    #    CPU path (_sinkhorn_cpu under autograd) through the public API.  Triton
+    #    reads the interpreter flag when its modules are imported, so this runs
+    #    in a child process of its own (the flag would reroute the CPU paths of
+    #    the fixtures above).
+    from deepfold.model.kernels import flash_sinkhorn_transport as fst  # noqa: E402
+    r = np.random.default_rng(23)
+    B, H, N, d = 2, 4, 40, 16
+    mask = np.ones((B, N), np.float32)
+    mask[1, 27:] = 0
+    unit = lambda a: a / np.linalg.norm(a, axis=-1, keepdims=True)  # noqa: E731
+    inp = dict(Q=unit(r.standard_normal((B, H, N, d))), K=unit(r.standard_normal((B, H, N, d))),
+               x=r.standard_normal((B, N, 3)) * 4.0, V=r.standard_normal((B, H, N, d)),
+               eps=np.array([0.5, 1.0, 2.0, 4.0]), alpha=r.standard_normal(H),
+               r_h=np.array([10.0, 3.0, 6.0, 0.5]), gxc=r.standard_normal((B, H, N, 3)),
+               ghc=r.standard_normal((B, H, N, d)), mask=mask)
+    inp = {k: v.astype(np.float32) for k, v in inp.items()}
+    T = lambda k, g=False: _t(inp[k], torch, g)  # noqa: E731
+    out = {}
+    leaves = dict(Q=T("Q", True), K=T("K", True), x=T("x", True), V=T("V", True), alpha=T("alpha", True),
+                  r_h=T("r_h", True))
+    xc, hc = fst.BalancedSinkhornDualFn.apply(leaves["Q"], leaves["K"], leaves["x"], leaves["V"], T("eps"),
+                                              leaves["alpha"], leaves["r_h"], 20, T("mask"))
+    ((xc * T("gxc")).sum() + (hc * T("ghc")).sum()).backward()
+    out.update(dual_xc=xc.detach().numpy(), dual_hc=hc.detach().numpy())
+    out.update({f"dual_d{k}": v.grad.numpy() for k, v in leaves.items()})
+    leaves = dict(Q=T("Q", True), K=T("K", True), x=T("x", True), alpha=T("alpha", True), r_h=T("r_h", True))
+    xc = fst.BalancedSinkhornFn.apply(leaves["Q"], leaves["K"], leaves["x"], T("eps"), leaves["alpha"],
+                                      leaves["r_h"], 20, T("mask"))
+    (xc * T("gxc")).sum().backward()
+    out["single_xc"] = xc.detach().numpy()
+    out.update({f"single_d{k}": v.grad.numpy() for k, v in leaves.items()})
+    save("balanced_device", inp, out, K_iter=20)
+
+    #    CPU path through the public API, no mask; r_h with a negative entry and
+    #    one below the 0.1 clamp
+    inp2 = {k: v for k, v in inp.items() if k != "mask"}
+    inp2["r_h"] = np.array([10.0, -4.0, 0.05, 2.0], np.float32)
+    T = lambda k, g=False: _t(inp2[k], torch, g)  # noqa: E731
+    leaves = dict(Q=T("Q", True), K=T("K", True), x=T("x", True), V=T("V", True), alpha=T("alpha", True),
+                  r_h=T("r_h", True))
+    xc, hc = fst.balanced_sinkhorn_transport_dual(leaves["Q"], leaves["K"], leaves["x"], leaves["V"], T("eps"),
+                                                  leaves["alpha"], leaves["r_h"], K_iter=20)
+    ((xc * T("gxc")).sum() + (hc * T("ghc")).sum()).backward()
+    out = dict(xc=xc.detach().numpy(), hc=hc.detach().numpy())
+    out.update({f"d{k}": v.grad.numpy() for k, v in leaves.items()})
+    save("balanced_cpu", inp2, out, K_iter=20)
+
 
 
 if __name__ == "__main__":

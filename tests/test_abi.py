@@ -35,7 +35,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_version_and_strings(lib):
-    assert lib.dfs_abi_version() == 1
+    assert lib.dfs_abi_version() == 2
     assert nat.status_string(nat.DFS_OK) == "ok"
     assert "workspace" in nat.status_string(nat.DFS_ERR_WORKSPACE)
     assert nat.max_n(32) >= 384
@@ -47,8 +47,8 @@ def test_version_and_strings(lib):
 def test_struct_sizes_match_header_layout():
     # every pointer field is 8 bytes; the problem block is 8 int32 + 4 floats
     assert ctypes.sizeof(nat.DfsProblem) == 48
-    assert ctypes.sizeof(nat.DfsFwdArgs) == 20 * 8
-    assert ctypes.sizeof(nat.DfsBwdArgs) == 26 * 8
+    assert ctypes.sizeof(nat.DfsFwdArgs) == 21 * 8
+    assert ctypes.sizeof(nat.DfsBwdArgs) == 28 * 8
     assert ctypes.sizeof(nat.DfsCgParams) == 16
 
 
@@ -78,9 +78,9 @@ def test_host_side_validation(lib):
     nd = 2 * 4 * 16 * 32
     assert fb.value == 3 * 2 * nd + 4 * nd  # already multiples of 256
     # backward: Q, K, V, dO, dQ, dK, dV copies, then the resident kernels' partials of
-    # the shared-parameter gradients: dx (3 per point), dw and 68 bin sums per CTA
+    # the shared-parameter gradients: dx (3 per point), dw, 68 bin sums and dr per CTA
     bh, cta = 2 * 4, 1
-    assert bb.value == 3 * 2 * nd + 4 * 4 * nd + 4 * (bh * 16 * 3 + bh * cta + bh * cta * 68)
+    assert bb.value == 3 * 2 * nd + 4 * 4 * nd + 4 * (bh * 16 * 3 + 2 * bh * cta + bh * cta * 68)
     # the phase API keeps no padded copies between calls
     assert lib.dfs_stream_op(nat.DFS_OP_FWD_INIT, odd_d, None, fake, None, 0, 16, None, 0, None) == \
         nat.DFS_ERR_UNSUPPORTED
