@@ -14,11 +14,15 @@ long-sequence row-sharded one: B=1 H=16 N=8192 d=64, 30 iterations, CG tol
 through NVLink peer stores each half-iteration (strong scaling: one call is the
 whole configuration's forward + backward).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|transport]
 
 ``--config 3`` (B=8 H=16 padded N=1024 d=64, variable lengths, softmax
 marginals, eps 0.5, 50 iterations) spreads the (batch, head) problems over the
 ranks with a length^2-balanced partition (no data-path collective).
+
+``--config transport`` times the trunk block's balanced transport
+(balanced_sinkhorn_transport, fwd+bwd) at the shapes the reference publishes
+timings for (B=1 H=16 d_h=32 K=20, N = 64 ... 768) and prints them beside those.
 
 ``--impl reference`` times the reference's own CPU path -- dense cost,
 sinkhorn_solve, compute_transport_output and torch autograd, restated in
@@ -717,6 +721,74 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- balanced transport
+# The reference's published timing of its balanced transport (Triton forward +
+# unrolled Triton backward, x_centroid only), B=1 H=16 d_h=32 K=20, on an
+# unnamed GPU: ms per fwd+bwd by N.
+TRANSPORT_PUBLISHED_MS = {64: 1.6, 256: 4.5, 512: 8.3, 768: 21.4}
+
+
+def run_transport(args):
+    """fwd+bwd of balanced_sinkhorn_transport (the trunk block's call) through the
+    public API at the shapes the reference publishes, fp32 unit-norm Q/K,
+    x ~ 4 N(0,1), per-head eps 0.5/1/2/4, alpha ~ N(0,1), r_h = 10, full mask;
+    CUDA events around each step, L2 flushed between steps."""
+    import torch.nn.functional as F
+    from deepfold import _native as nat
+    from deepfold.model.kernels.flash_sinkhorn_transport import balanced_sinkhorn_transport
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nat.lib()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    B, H, d, K_iter = 1, 16, 32, 20
+    per_n = {}
+    sampler = ClockSampler(dev)
+    sampler.start()
+    time.sleep(0.3)
+    for N, pub in TRANSPORT_PUBLISHED_MS.items():
+        g = torch.Generator().manual_seed(N)
+        Q = F.normalize(torch.randn(B, H, N, d, generator=g), dim=-1).to(dev).requires_grad_(True)
+        K = F.normalize(torch.randn(B, H, N, d, generator=g), dim=-1).to(dev).requires_grad_(True)
+        x = (torch.randn(B, N, 3, generator=g) * 4.0).to(dev).requires_grad_(True)
+        eps = torch.tensor([0.5] * 4 + [1.0] * 4 + [2.0] * 4 + [4.0] * 4, device=dev)
+        alpha = torch.randn(H, generator=g).to(dev).requires_grad_(True)
+        r_h = torch.full((H,), 10.0, device=dev, requires_grad=True)
+        mask = torch.ones(B, N, device=dev)
+        gxc = torch.randn(B, H, N, 3, generator=g).to(dev)
+
+        def step():
+            xc = balanced_sinkhorn_transport(Q, K, x, eps, alpha, r_h, K_iter=K_iter, mask=mask)
+            torch.autograd.backward(xc, gxc)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            ms.append((e0, e1))
+        torch.cuda.synchronize()
+        t = sorted(a.elapsed_time(b) for a, b in ms)
+        med = t[len(t) // 2]
+        per_n[N] = {"ms_median": round(med, 4), "ms_mean": round(sum(t) / len(t), 4),
+                    "reference_published_ms": pub, "speedup_vs_published": round(pub / med, 1)}
+    clocks = sampler.stop()
+    line = {"metric": "balanced transport fwd+bwd ms (B=1 H=16 d_h=32 K=20, fp32)", "value": per_n[768]["ms_median"],
+            "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "vs_baseline": round(per_n[768]["ms_median"] / TRANSPORT_PUBLISHED_MS[768], 5), "dtype": "f32",
+            "data": "synthetic (seeded unit-norm Q/K, N(0,1) x, alpha)",
+            "config": {"workload": "balanced_sinkhorn_transport fwd+bwd, x_centroid only, N=64/256/512/768",
+                       "l2": "flushed between timed steps"},
+            "per_N": per_n, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -726,9 +798,21 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config4", action="store_true", help="skip the single-GPU long-sequence point")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=None,
-                    help="default: 2 on one GPU, 4 (long-sequence row shards) on several")
+    ap.add_argument("--config", choices=["2", "3", "4", "transport"], default=None,
+                    help="default: 2 on one GPU, 4 (long-sequence row shards) on several; 'transport': the "
+                         "balanced transport at the reference's published shapes (one GPU)")
     args = ap.parse_args()
+    if args.config == "transport":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the transport mode times this build only; "
+                              "the reference's published timings are printed beside it"}))
+            return
+        if args.warmup < 3:
+            args.warmup = 3
+        run_transport(args)
+        return
+    if args.config is not None:
+        args.config = int(args.config)
     if args.config is None:
         args.config = 4 if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus > 1 else 2
     if args.warmup < 3:

@@ -307,7 +307,11 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
   if (!resident(p)) {
     if ((rc = check_stream_bwd(p, a, kws, kbytes)) != DFS_OK) return rc;
   } else {
-    const size_t need = resident_bwd_workspace(p->B, p->H, p->N, kdim(p));
+    // the resident kernels use the workspace only for the partials of the
+    // shared-parameter gradients
+    const bool shared = a->dx_res != nullptr || a->dpos_weight != nullptr || a->dw_dist != nullptr ||
+                        a->dr_head != nullptr;
+    const size_t need = shared ? resident_bwd_workspace(p->B, p->H, p->N, kdim(p)) : 0;
     if (need > 0 && (kws == nullptr || kbytes < need)) return DFS_ERR_WORKSPACE;
   }
   BwdParams q = bwd_params(p, cg, a, kws);

@@ -18,6 +18,7 @@
 //   SB_DKV     columns: dK += dS^T Q, dV += T_norm^T dO
 // Per-problem vector steps (setup of the CG system, one CG iteration, the
 // null-space shift and marginal gradients) run as one CTA per problem.
+#include <mutex>
 #include <type_traits>
 
 #include "dfs_tma.cuh"
@@ -384,7 +385,9 @@ enum {
   WS_F = 0, WS_G, WS_M, WS_R, WS_D, WS_FM, WS_INVR, WS_C, WS_GV, WS_D1I, WS_B1, WS_D2, WS_D2I,
   WS_X2, WS_R2, WS_P2, WS_S2, WS_U2, WS_W2, WS_T, WS_S, WS_W1, WS_NUM
 };
-enum { SC_GAM = 0, SC_ALPHA, SC_BETA, SC_TOL2, SC_RR, SC_NUM = 8 };
+// SC_LOOP: problem 0's entry holds the round count (int32) of the
+// device-terminated CG loop (sb_loopcond_kernel)
+enum { SC_GAM = 0, SC_ALPHA, SC_BETA, SC_TOL2, SC_RR, SC_LOOP = 7, SC_NUM = 8 };
 
 constexpr int kVThreads = 256;
 
@@ -590,6 +593,27 @@ __global__ void __launch_bounds__(kVThreads) sb_cgstep_kernel(VecParams p, int f
     const float r = ws[WS_R2 * n + o + i] - alpha * ss;
     ws[WS_R2 * n + o + i] = r;
     ws[WS_U2 * n + o + i] = r * ws[WS_D2I * n + o + i];
+  }
+}
+
+// Condition of the device-terminated CG loop (a WHILE node of a CUDA graph
+// whose body is one CG round): 1 while some problem's solve still runs.  The
+// round count is capped independently of the flags (every solve stops within
+// max_iter rounds by itself), so the loop ends after at most max_rounds
+// rounds whatever the flags say.  `reset`: the launch before the loop.
+__global__ void sb_loopcond_kernel(const int32_t* done, int nprob, int32_t* rounds, int max_rounds, int reset,
+                                   cudaGraphConditionalHandle cond) {
+  __shared__ int any;
+  if (threadIdx.x == 0) any = 0;
+  __syncthreads();
+  int mine = 0;
+  for (int i = threadIdx.x; i < nprob; i += blockDim.x) mine |= done[i] == 0;
+  if (mine) any = 1;  // every writer stores the same value
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int r = reset ? 0 : rounds[0] + 1;
+    rounds[0] = r;
+    cudaGraphSetConditional(cond, (any != 0 && r < max_rounds) ? 1u : 0u);
   }
 }
 
@@ -998,6 +1022,107 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
 }
 
 // The whole streamed backward on one GPU: every phase over all rows.
+namespace {
+
+// A private stream per device on which the CG loop's body is recorded (stream
+// capture records launches without running them; the caller's stream may be
+// the legacy default stream, which cannot be captured).
+constexpr int kCaptureDevices = 64;
+cudaStream_t capture_stream(int dev) {
+  static std::mutex mu;
+  static cudaStream_t streams[kCaptureDevices] = {};
+  if (dev < 0 || dev >= kCaptureDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (streams[dev] == nullptr) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) return nullptr;
+    if (cur != dev && cudaSetDevice(dev) != cudaSuccess) return nullptr;
+    cudaStream_t s = nullptr;
+    const cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (cur != dev) cudaSetDevice(cur);
+    if (e != cudaSuccess) return nullptr;
+    streams[dev] = s;
+  }
+  return streams[dev];
+}
+
+// CG rounds 1 .. max_iter as one CUDA graph launched on `st`: a kernel that
+// sets the loop condition, then a WHILE node whose body is one round
+// (t = D1^-1 P u, s = P^T t, the CG step, the condition again).  The loop stops
+// on the device as soon as every problem's solve has stopped, so no launches
+// run after convergence and the host never waits.  Returns false (and leaves
+// nothing queued) when the runtime cannot build or launch such a graph; the
+// caller then issues the rounds one by one.
+bool cg_loop_graph(const BwdParams& bp, float* wsp, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;  // inside the caller's own capture: plain launches
+  }
+  int dev = 0;
+  if (cudaStreamGetDevice(st, &dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  cudaStream_t cap = capture_stream(dev);
+  if (cap == nullptr) return false;
+  static std::mutex capture_mu;  // one recording at a time on the shared capture streams
+  std::lock_guard<std::mutex> lock(capture_mu);
+  const size_t n = static_cast<size_t>(bp.B) * bp.H * bp.N, nbh = static_cast<size_t>(bp.B) * bp.H;
+  float* sc = wsp + WS_NUM * n;
+  int32_t* done = reinterpret_cast<int32_t*>(sc + SC_NUM * nbh);
+  int32_t* rounds = reinterpret_cast<int32_t*>(sc + SC_LOOP);
+  const int nprob = static_cast<int>(nbh), max_rounds = bp.cg_max_iter;
+  cudaGraph_t g = nullptr, body = nullptr;
+  cudaGraphExec_t ex = nullptr;
+  cudaGraphNode_t first = nullptr, loop = nullptr;
+  bool ok = cudaGraphCreate(&g, 0) == cudaSuccess;
+  cudaGraphConditionalHandle cond = 0;
+  ok = ok && cudaGraphConditionalHandleCreate(&cond, g, 0, cudaGraphCondAssignDefault) == cudaSuccess;
+  if (ok) {
+    int reset = 1;
+    void* args[] = {&done, const_cast<int*>(&nprob), &rounds, const_cast<int*>(&max_rounds), &reset, &cond};
+    cudaKernelNodeParams kp = {};
+    kp.func = reinterpret_cast<void*>(sb_loopcond_kernel);
+    kp.gridDim = dim3(1);
+    kp.blockDim = dim3(256);
+    kp.kernelParams = args;
+    ok = cudaGraphAddKernelNode(&first, g, nullptr, 0, &kp) == cudaSuccess;
+  }
+  if (ok) {
+    cudaGraphNodeParams np = {};
+    np.type = cudaGraphNodeTypeConditional;
+    np.conditional.handle = cond;
+    np.conditional.type = cudaGraphCondTypeWhile;
+    np.conditional.size = 1;
+    ok = cudaGraphAddNode(&loop, g, &first, 1, &np) == cudaSuccess;
+    if (ok) body = np.conditional.phGraph_out[0];
+  }
+  if (ok) ok = cudaStreamBeginCaptureToGraph(cap, body, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed) ==
+               cudaSuccess;
+  if (ok) {
+    cudaError_t e = stream_bwd_op(DFS_OP_BWD_P_U, bp, wsp, 0, bp.N, cap);
+    if (e == cudaSuccess) e = stream_bwd_op(DFS_OP_BWD_PT_T, bp, wsp, 0, bp.N, cap);
+    if (e == cudaSuccess) e = stream_bwd_op(DFS_OP_BWD_CGSTEP, bp, wsp, 0, bp.N, cap);
+    if (e == cudaSuccess) {
+      sb_loopcond_kernel<<<1, 256, 0, cap>>>(done, nprob, rounds, max_rounds, 0, cond);
+      e = cudaGetLastError();
+    }
+    cudaGraph_t captured = nullptr;
+    const cudaError_t ee = cudaStreamEndCapture(cap, &captured);
+    ok = e == cudaSuccess && ee == cudaSuccess;
+  }
+  if (ok) ok = cudaGraphInstantiate(&ex, g, 0) == cudaSuccess;
+  if (ok) ok = cudaGraphLaunch(ex, st) == cudaSuccess;
+  // an executable graph destroyed while in flight is freed once it completes
+  if (ex != nullptr) cudaGraphExecDestroy(ex);
+  if (g != nullptr) cudaGraphDestroy(g);
+  if (!ok) cudaGetLastError();  // the failure is handled by the caller's fallback
+  return ok;
+}
+
+}  // namespace
+
 cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) {
   const int N = bp.N;
   cudaError_t e = cudaSuccess;
@@ -1011,10 +1136,17 @@ cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) 
   run(DFS_OP_BWD_SETUP);
   run(DFS_OP_BWD_PT_T);   // s = P^T D1^-1 b1 (no problem has stopped yet)
   run(DFS_OP_BWD_CGINIT);
-  for (int it = 0; it <= bp.cg_max_iter; ++it) {
-    run(DFS_OP_BWD_P_U);
-    run(DFS_OP_BWD_PT_T);
-    run(it == 0 ? DFS_OP_BWD_CGSTEP_FIRST : DFS_OP_BWD_CGSTEP);
+  run(DFS_OP_BWD_P_U);    // the first CG round
+  run(DFS_OP_BWD_PT_T);
+  run(DFS_OP_BWD_CGSTEP_FIRST);
+  // rounds 1 .. max_iter: a device-terminated loop, or one by one where the
+  // runtime cannot run it (rounds after convergence then exit early per problem)
+  if (e == cudaSuccess && bp.cg_max_iter > 0 && !cg_loop_graph(bp, wsp, st)) {
+    for (int it = 1; it <= bp.cg_max_iter; ++it) {
+      run(DFS_OP_BWD_P_U);
+      run(DFS_OP_BWD_PT_T);
+      run(DFS_OP_BWD_CGSTEP);
+    }
   }
   run(DFS_OP_BWD_P_X);
   run(DFS_OP_BWD_FINAL);
