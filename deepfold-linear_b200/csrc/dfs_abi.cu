@@ -121,6 +121,9 @@ FwdParams fwd_params(const dfs_problem* p, const dfs_fwd_args* a) {
   q.qk_scale = 1.0f / std::sqrt(static_cast<float>(p->d));
   q.cost_terms = p->cost_terms;
   q.r_head = a->r_head;
+  q.chain_id = a->chain_id;
+  q.global_idx = a->global_idx;
+  q.bond_matrix = a->bond_matrix;
   return q;
 }
 
@@ -142,8 +145,18 @@ BwdParams bwd_params(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bw
   q.cost_terms = p->cost_terms;
   q.r_head = a->r_head;
   q.dr_head = a->dr_head;
+  q.chain_id = a->chain_id;
+  q.global_idx = a->global_idx;
+  q.bond_matrix = a->bond_matrix;
   return q;
 }
+
+// position bins: the int32 table, or all three compute_bins inputs, or nothing
+bool bins_args_ok(const int32_t* table, const int32_t* chain, const int32_t* gidx, const uint8_t* bond) {
+  const int parts = (chain != nullptr) + (gidx != nullptr) + (bond != nullptr);
+  return parts == 0 || (parts == 3 && table == nullptr);
+}
+bool has_bins(const int32_t* table, const int32_t* chain) { return table != nullptr || chain != nullptr; }
 
 // argument checks shared by dfs_fwd and the forward phases
 int check_fwd_args(const dfs_problem* p, const dfs_fwd_args* a) {
@@ -152,7 +165,8 @@ int check_fwd_args(const dfs_problem* p, const dfs_fwd_args* a) {
   if (p->cost_mode == DFS_COST_QK && (!a->Q || !a->K)) return DFS_ERR_INVALID_ARGUMENT;
   if (p->cost_mode == DFS_COST_DENSE && !a->C) return DFS_ERR_INVALID_ARGUMENT;
   if (a->O && !a->V) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (!bins_args_ok(a->pos_bins, a->chain_id, a->global_idx, a->bond_matrix)) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->pos_weight && !has_bins(a->pos_bins, a->chain_id)) return DFS_ERR_INVALID_ARGUMENT;
   if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   // the kernels read the operands in 16-byte chunks (padded ones are copies)
@@ -191,11 +205,12 @@ int check_bwd_args(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_
   if (p->cost_mode != DFS_COST_QK) return DFS_ERR_UNSUPPORTED;
   if (!a->Q || !a->K || !a->V || !a->eps || !a->log_mu || !a->log_nu || !a->log_u || !a->log_v || !a->dO)
     return DFS_ERR_INVALID_ARGUMENT;
-  if (a->pos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (!bins_args_ok(a->pos_bins, a->chain_id, a->global_idx, a->bond_matrix)) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->pos_weight && !has_bins(a->pos_bins, a->chain_id)) return DFS_ERR_INVALID_ARGUMENT;
   if (a->dxc && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if ((a->dx_res || a->dw_dist) && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
   if (a->dr_head && (!a->x_res || !a->w_dist)) return DFS_ERR_INVALID_ARGUMENT;
-  if (a->dpos_weight && !a->pos_bins) return DFS_ERR_INVALID_ARGUMENT;
+  if (a->dpos_weight && !has_bins(a->pos_bins, a->chain_id)) return DFS_ERR_INVALID_ARGUMENT;
   if (cg->max_iter < 0) return DFS_ERR_INVALID_ARGUMENT;
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   if (!padded(p) && (!aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V) || !aligned16(a->dO) ||
@@ -429,6 +444,15 @@ int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int
   pi.wait_for = peers->wait_for;
   return cuda_status(stream_fwd_op(op, fwd_params(p, fa), static_cast<float*>(workspace), row_begin, row_end,
                                    static_cast<cudaStream_t>(stream), &pi));
+}
+
+int dfs_compute_bins(int B, int N, const int32_t* chain_id, const int32_t* global_idx,
+                     const uint8_t* bond_matrix, int32_t* out, void* stream) {
+  if (B < 0 || N < 0) return DFS_ERR_INVALID_ARGUMENT;
+  if (static_cast<size_t>(B) * N == 0) return DFS_OK;
+  if (!chain_id || !global_idx || !bond_matrix || !out) return DFS_ERR_INVALID_ARGUMENT;
+  return cuda_status(compute_bins_table(chain_id, global_idx, bond_matrix, B, N, out,
+                                        static_cast<cudaStream_t>(stream)));
 }
 
 int dfs_selftest_mma(int which, const float* A, const float* B, float* D, int M, int N, int K, void* stream) {

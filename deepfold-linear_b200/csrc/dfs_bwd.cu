@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   auto add_bias = [&](bool transposed) {
     BiasArgs bias;
     bias.pos_weight = p.pos_weight;
-    bias.pos_bins = p.pos_bins;
+    bias.bins = bin_source(p);
     bias.xrow = rowv + BR_X0 * 64;
     bias.xcol = colv + BC_X0 * NP;
     bias.geo = p.x_res != nullptr && w_h != 0.0f;
@@ -589,7 +589,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
   // (the exchange buffers are free from here on: cg_* scratch lives there)
   const bool geo_grad = p.x_res != nullptr && (p.dw_dist != nullptr || p.dr_head != nullptr ||
                                                (p.dx_res != nullptr && w_h != 0.0f));
-  const bool pos_grad = p.dpos_weight != nullptr && p.pos_bins != nullptr;
+  const BinSource bsrc = bin_source(p);
+  const bool pos_grad = p.dpos_weight != nullptr && bins_given(bsrc);
   const bool cost_grad = geo_grad || pos_grad || p.dx_res != nullptr;
   float* cg_dx = reinterpret_cast<float*>(base + Cfg::OFF_XR);                                // 3 x 64
   unsigned long long* cg_hist = reinterpret_cast<unsigned long long*>(base + Cfg::OFF_XR + 1024);  // 68
@@ -606,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
       float ax = 0.0f, ay = 0.0f, az = 0.0f;
       if (gi < N) {
         const float x0 = rowv[BR_X0 * 64 + li], x1 = rowv[BR_X1 * 64 + li], x2 = rowv[BR_X2 * 64 + li];
-        const int32_t* brow = pos_grad && with_bins ? p.pos_bins + (static_cast<size_t>(bb) * N + gi) * N : nullptr;
+        const bool hist = pos_grad && with_bins;
 #pragma unroll 2
         for (int j = lane; j < N; j += 32) {
           const float dC = -Ts[sw_off(li, j, 64) >> 2] * inv_eps;
@@ -624,8 +625,8 @@ __global__ void __launch_bounds__(kThreads, 1) resident_bwd_kernel(const BwdPara
             ay = fmaf(cf, d1, ay);
             az = fmaf(cf, d2, az);
           }
-          if (brow != nullptr) {
-            const unsigned bin = static_cast<unsigned>(brow[j]);  // bins outside [0, 68) add nothing
+          if (hist) {
+            const unsigned bin = static_cast<unsigned>(bin_at(bsrc, bb, N, gi, j));  // outside [0, 68): nothing
             const long long q = __float2ll_rn(dC * hscale);
             if (bin < static_cast<unsigned>(kBins)) atomicAdd(&cg_hist[bin], static_cast<unsigned long long>(q));
           }

@@ -12,6 +12,7 @@
 #include "../../include/dfsink.h"
 
 #define DFS_DEV __device__ __forceinline__
+#define DFS_DEV_HOST_INLINE __host__ __device__ inline
 
 namespace dfs {
 

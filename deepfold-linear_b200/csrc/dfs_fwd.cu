@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) resident_fwd_kernel(const FwdPara
     if (p.pos_weight != nullptr || (p.x_res != nullptr && wq != 0.0f)) {
       BiasArgs bias;
       bias.pos_weight = p.pos_weight;
-      bias.pos_bins = p.pos_bins;
+      bias.bins = bin_source(p);
       bias.xrow = rowv + RV_X0 * 64;
       bias.xcol = colv + CV_X0 * NP;
       bias.geo = p.x_res != nullptr && wq != 0.0f;

@@ -17,6 +17,30 @@ constexpr int kGradAcc = 1;
 // stabilised kernel matrix is rebuilt: row/column sums then stay above 2^-60.
 constexpr float kDrift = 30.0f;
 
+// Where the position bins of a problem come from: a (B, N, N) int32 table, or
+// the inputs of the reference's compute_bins (src/deepfold/model/
+// position_encoding.py:7-52), evaluated per pair:
+//   same chain, no bond:  clamp(gidx_i - gidx_j, -32, 32) + 32    (0 .. 64)
+//   other chain, no bond: 65;  same chain, bond: 66;  other chain, bond: 67
+struct BinSource {
+  const int32_t* table;   // (B, N, N) or null
+  const int32_t* chain;   // (B, N) chain id, with gidx and bond when table is null
+  const int32_t* gidx;    // (B, N) global residue index
+  const uint8_t* bond;    // (B, N, N) covalent bond adjacency, 0 / 1
+};
+DFS_DEV_HOST_INLINE bool bins_given(const BinSource& s) { return s.table != nullptr || s.chain != nullptr; }
+// bin of pair (i, j) of batch element b; values outside [0, 68) come from a table only
+DFS_DEV int bin_at(const BinSource& s, size_t b, int N, int i, int j) {
+  const size_t ij = (b * N + i) * static_cast<size_t>(N) + j;
+  if (s.table != nullptr) return s.table[ij];
+  const size_t bi = b * N + i, bj = b * N + j;
+  const bool same = s.chain[bi] == s.chain[bj];
+  if (s.bond[ij] != 0) return same ? 66 : 67;
+  if (!same) return 65;
+  const long long sep = static_cast<long long>(s.gidx[bi]) - s.gidx[bj];
+  return static_cast<int>(sep < -32 ? 0 : sep > 32 ? 64 : sep + 32);
+}
+
 DFS_DEV float load_f32(const void* p, size_t i, int dtype) {
   if (dtype == DFS_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
   if (dtype == DFS_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
@@ -79,7 +103,13 @@ struct FwdParams {
   float qk_scale;          // 1/sqrt(d) of the caller's head dim (kernels may run d zero-padded)
   int cost_terms;          // DFS_TERM_* declared by the problem (workspace layout of the streamed path)
   const float* r_head;     // (H,) per-head geometry scale, or null: r_0
+  const int32_t* chain_id; // position bins from compute_bins' inputs (with pos_bins null)
+  const int32_t* global_idx;
+  const uint8_t* bond_matrix;
 };
+DFS_DEV_HOST_INLINE BinSource bin_source(const FwdParams& p) {
+  return BinSource{p.pos_bins, p.chain_id, p.global_idx, p.bond_matrix};
+}
 
 struct BwdParams {
   const void* Q;
@@ -115,7 +145,13 @@ struct BwdParams {
   int cost_terms;          // DFS_TERM_* declared by the problem (workspace layout of the streamed path)
   const float* r_head;     // (H,) per-head geometry scale, or null: r_0
   float* dr_head;          // (H,) gradient of r_head (or of r_0 per head), or null
+  const int32_t* chain_id; // position bins from compute_bins' inputs (with pos_bins null)
+  const int32_t* global_idx;
+  const uint8_t* bond_matrix;
 };
+DFS_DEV_HOST_INLINE BinSource bin_source(const BwdParams& p) {
+  return BinSource{p.pos_bins, p.chain_id, p.global_idx, p.bond_matrix};
+}
 
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
 size_t resident_fwd_smem(int N, int d);
@@ -138,7 +174,10 @@ size_t stream_bwd_workspace(int B, int H, int N, int d, int terms = 0);
 // table, and the launch that builds the table and its transpose.
 size_t cost_bins_bytes(int B, int N);
 int cost_bin_stride(int N);
-cudaError_t build_cost_bins(const int32_t* pos_bins, int B, int N, uint8_t* bins, uint8_t* bins_t, cudaStream_t st);
+cudaError_t build_cost_bins(const BinSource& src, int B, int N, uint8_t* bins, uint8_t* bins_t, cudaStream_t st);
+// compute_bins of the reference into a (B, N, N) int32 table
+cudaError_t compute_bins_table(const int32_t* chain, const int32_t* gidx, const uint8_t* bond, int B, int N,
+                               int32_t* out, cudaStream_t st);
 // The cost terms of a pass from the operator's inputs (position term when
 // pos_weight and the tables are given, geometry term when x_res and w_dist
 // are): `transposed` for the passes on S^T, whose rows are the cost's columns.

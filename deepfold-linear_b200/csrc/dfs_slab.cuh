@@ -88,7 +88,7 @@ DFS_DEV void regs_to_stage(const float (&E)[kRpw][NS], float* Ts, int warp, int 
 // (src/deepfold/model/kernels/sinkhorn_kernel.py:107-127).
 struct BiasArgs {
   const float* pos_weight;   // (H, 68) or null
-  const int32_t* pos_bins;   // (B, N, N)
+  BinSource bins;            // position bins (table or compute_bins inputs)
   const float* xrow;         // smem, 3 x 64 row coordinates (x, y, z planes)
   const float* xcol;         // smem, 3 x NP column coordinates
   bool geo;                  // geometry term present
@@ -108,9 +108,9 @@ DFS_DEV void add_cost_bias_stage(float* Ts, const BiasArgs& a, int tid) {
     if (gi >= a.N || gj >= a.N) continue;
     float bias = 0.0f;
     if (a.pos_weight) {
-      const size_t bi = a.transposed ? (static_cast<size_t>(a.bb) * a.N + gj) * a.N + gi
-                                     : (static_cast<size_t>(a.bb) * a.N + gi) * a.N + gj;
-      const unsigned bin = static_cast<unsigned>(a.pos_bins[bi]);  // bins outside [0, 68) add nothing
+      const unsigned bin = static_cast<unsigned>(a.transposed ? bin_at(a.bins, a.bb, a.N, gj, gi)
+                                                              : bin_at(a.bins, a.bb, a.N, gi, gj));
+      // bins outside [0, 68) add nothing
       bias += bin < 68u ? a.pos_weight[a.hh * 68 + bin] : 0.0f;
     }
     if (a.geo) {

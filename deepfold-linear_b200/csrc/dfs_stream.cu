@@ -336,11 +336,12 @@ cudaError_t launch_stream(int mode, int d, const StreamParams& p, cudaStream_t s
 int cost_bin_stride(int N) { return (N + 127) / 128 * 128; }
 size_t cost_bins_bytes(int B, int N) { return static_cast<size_t>(B) * N * cost_bin_stride(N); }
 
-// pos_bins (B, N, N) int32 -> table (B, N, stride) uint8 and its transpose
-// (entry [b][j][i] = bins[b][i][j]); bins outside [0, 68) and the padding
-// columns hold 68, whose weight the passes take as 0.  32 x 32 tiles through
-// shared memory, one block per tile of the (stride x stride) square.
-__global__ void cost_bins_kernel(const int32_t* __restrict__ bins, int N, int stride, uint8_t* __restrict__ t,
+// position bins (a (B, N, N) int32 table, or compute_bins' inputs evaluated
+// per pair) -> table (B, N, stride) uint8 and its transpose (entry [b][j][i] =
+// bins[b][i][j]); bins outside [0, 68) and the padding columns hold 68, whose
+// weight the passes take as 0.  32 x 32 tiles through shared memory, one block
+// per tile of the (stride x stride) square.
+__global__ void cost_bins_kernel(const BinSource src, int N, int stride, uint8_t* __restrict__ t,
                                  uint8_t* __restrict__ tt) {
   __shared__ uint8_t tile[32][33];
   const size_t b = blockIdx.z;
@@ -349,7 +350,7 @@ __global__ void cost_bins_kernel(const int32_t* __restrict__ bins, int N, int st
     const int i = i0 + r, j = j0 + tx;
     uint8_t v = kBinCount;
     if (i < N && j < N) {
-      const unsigned x = static_cast<unsigned>(bins[(b * N + i) * N + j]);
+      const unsigned x = static_cast<unsigned>(bin_at(src, b, N, i, j));
       v = x < static_cast<unsigned>(kBinCount) ? static_cast<uint8_t>(x) : static_cast<uint8_t>(kBinCount);
     }
     if (i < N && j < stride) t[(b * N + i) * stride + j] = v;
@@ -362,9 +363,31 @@ __global__ void cost_bins_kernel(const int32_t* __restrict__ bins, int N, int st
   }
 }
 
-cudaError_t build_cost_bins(const int32_t* pos_bins, int B, int N, uint8_t* bins, uint8_t* bins_t, cudaStream_t st) {
+cudaError_t build_cost_bins(const BinSource& src, int B, int N, uint8_t* bins, uint8_t* bins_t, cudaStream_t st) {
   const int stride = cost_bin_stride(N);
-  cost_bins_kernel<<<dim3(stride / 32, stride / 32, B), dim3(32, 8), 0, st>>>(pos_bins, N, stride, bins, bins_t);
+  cost_bins_kernel<<<dim3(stride / 32, stride / 32, B), dim3(32, 8), 0, st>>>(src, N, stride, bins, bins_t);
+  return cudaGetLastError();
+}
+
+// compute_bins (position_encoding.py:7-52) into an int32 table: one thread per
+// pair, rows of a block's 256 consecutive pairs of one batch element
+__global__ void compute_bins_kernel(const BinSource src, int B, int N, int32_t* __restrict__ out) {
+  const size_t nn = static_cast<size_t>(N) * N, total = nn * B;
+  for (size_t k = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < total;
+       k += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t b = k / nn, r = k - b * nn;
+    const int i = static_cast<int>(r / N), j = static_cast<int>(r - static_cast<size_t>(i) * N);
+    out[k] = bin_at(src, b, N, i, j);
+  }
+}
+
+cudaError_t compute_bins_table(const int32_t* chain, const int32_t* gidx, const uint8_t* bond, int B, int N,
+                               int32_t* out, cudaStream_t st) {
+  const size_t total = static_cast<size_t>(B) * N * N;
+  if (total == 0) return cudaSuccess;
+  const size_t blocks = (total + 255) / 256;
+  const unsigned g = static_cast<unsigned>(blocks < 148u * 32u ? blocks : 148u * 32u);
+  compute_bins_kernel<<<g, 256, 0, st>>>(BinSource{nullptr, chain, gidx, bond}, B, N, out);
   return cudaGetLastError();
 }
 
@@ -450,8 +473,8 @@ cudaError_t stream_fwd_op(int op, const FwdParams& fp, float* ws, int r0, int r1
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = tile_split_reset(split, fp.B, fp.H, fp.N, st);
     if (e == cudaSuccess) e = compute_extents(fp.mask, fp.B, fp.N, extents, st);
-    if (e == cudaSuccess && bins != nullptr && fp.pos_bins != nullptr)
-      e = build_cost_bins(fp.pos_bins, fp.B, fp.N, bins, bins_t, st);
+    if (e == cudaSuccess && bins != nullptr && bins_given(bin_source(fp)))
+      e = build_cost_bins(bin_source(fp), fp.B, fp.N, bins, bins_t, st);
     if (e == cudaSuccess && peers != nullptr) e = peer_signal(cnts, peers->npeers, st);
     return e;
   }

@@ -858,8 +858,8 @@ cudaError_t stream_bwd_op(int op, const BwdParams& bp, float* wsp, int r0, int r
       if (e == cudaSuccess && bt) e = bt_prep(bp, cp, st);
       if (e == cudaSuccess) e = tile_split_reset(split, B, H, N, st);
       if (e == cudaSuccess) e = compute_extents(bp.mask, B, N, extents, st);
-      if (e == cudaSuccess && bins != nullptr && bp.pos_bins != nullptr)
-        e = build_cost_bins(bp.pos_bins, B, N, bins, bins_t, st);
+      if (e == cudaSuccess && bins != nullptr && bins_given(bin_source(bp)))
+        e = build_cost_bins(bin_source(bp), B, N, bins, bins_t, st);
       return e;
     }
     case DFS_OP_BWD_ROWSTATS:  // m, R, D

@@ -179,9 +179,10 @@ int take_status(bool wait) {
 
 // DFS_TERM_* bits of the optional inputs a call passes (the streamed kernels
 // size their workspace by them)
-int32_t cost_terms_of(const Tensor& pw, const Tensor& pb, const Tensor& xr, const Tensor& wd) {
+int32_t cost_terms_of(const Tensor& pw, const Tensor& pb, const Tensor& xr, const Tensor& wd,
+                      const Tensor& chain = Tensor()) {
   int32_t t = 0;
-  if (pw.defined() && pb.defined()) t |= DFS_TERM_POS;
+  if (pw.defined() && (pb.defined() || chain.defined())) t |= DFS_TERM_POS;
   if (xr.defined() && wd.defined()) t |= DFS_TERM_GEO;
   if (xr.defined()) t |= DFS_TERM_XRES;
   return t;
@@ -191,15 +192,18 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
   // Arguments (positions in the gradient list backward returns): 0 Q, 1 K, 2 V,
   // 3 x_res, 4 pos_weight, 5 pos_bins, 6 eps, 7 w_dist, 8 log_mu, 9 log_nu,
   // 10 log_u_init, 11 log_v_init, 12 mask, 13 K_iter, 14 lam, 15 r_0, 16 cg_rtol,
-  // 17 cg_atol, 18 cg_max_iter.  needs_input_grad counts only the tensors that
-  // were passed (absent optionals are no autograd edge), so the forward records
-  // each argument's edge index.
+  // 17 cg_atol, 18 cg_max_iter, 19 chain_id, 20 global_idx, 21 bond_matrix (the
+  // inputs of compute_bins, in place of pos_bins).  needs_input_grad counts only
+  // the tensors that were passed (absent optionals are no autograd edge), so the
+  // forward records each argument's edge index.
   static variable_list forward(AutogradContext* ctx, Tensor Q, Tensor K, Tensor V, c10::optional<Tensor> x_res,
                                c10::optional<Tensor> pos_weight, c10::optional<Tensor> pos_bins, Tensor eps,
                                c10::optional<Tensor> w_dist, Tensor log_mu, Tensor log_nu,
                                c10::optional<Tensor> log_u_init, c10::optional<Tensor> log_v_init,
                                c10::optional<Tensor> mask, int64_t K_iter, double lam, double r_0,
-                               double cg_rtol, double cg_atol, int64_t cg_max_iter) {
+                               double cg_rtol, double cg_atol, int64_t cg_max_iter,
+                               c10::optional<Tensor> chain_id, c10::optional<Tensor> global_idx,
+                               c10::optional<Tensor> bond_matrix) {
     require(Q.is_cuda() && K.is_cuda() && V.is_cuda(),
                 "deepfold B200 Sinkhorn ops run on CUDA tensors only (no CPU path)");
     require(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(),
@@ -216,8 +220,20 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     const auto cdt = (st == at::kBFloat16 || st == at::kHalf || st == at::kFloat) ? st : at::kFloat;
     const Tensor Qc = Q.contiguous().to(cdt), Kc = K.contiguous().to(cdt), Vc = V.contiguous().to(cdt);
     const Tensor xr = f32(x_res), pw = f32(pos_weight);
-    Tensor pb;
+    Tensor pb, ch, gx, bd;
     if (pw.defined() && pos_bins.has_value() && pos_bins->defined()) pb = pos_bins->contiguous().to(at::kInt);
+    const bool bins_inputs = chain_id.has_value() && chain_id->defined();
+    if (pw.defined() && !pb.defined() && bins_inputs) {
+      require(global_idx.has_value() && global_idx->defined() && bond_matrix.has_value() && bond_matrix->defined(),
+              "chain_id, global_idx and bond_matrix are given together");
+      require(chain_id->dim() == 2 && chain_id->size(0) == B && chain_id->size(1) == N &&
+                  global_idx->sizes() == chain_id->sizes() && bond_matrix->dim() == 3 &&
+                  bond_matrix->size(0) == B && bond_matrix->size(1) == N && bond_matrix->size(2) == N,
+              "chain_id, global_idx must be (B, N) and bond_matrix (B, N, N)");
+      ch = chain_id->contiguous().to(at::kInt);
+      gx = global_idx->contiguous().to(at::kInt);
+      bd = bond_matrix->contiguous().to(at::kByte);
+    }
     const Tensor epsc = eps.contiguous().to(at::kFloat), wd = f32(w_dist);
     const Tensor lmu = log_mu.contiguous().to(at::kFloat), lnu = log_nu.contiguous().to(at::kFloat);
     const Tensor lui = f32(log_u_init), lvi = f32(log_v_init), mk = f32(mask);
@@ -238,7 +254,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     prob.check_every = 2;
     prob.lam = static_cast<float>(lam);
     prob.r_0 = static_cast<float>(r_0);
-    prob.cost_terms = cost_terms_of(pw, pb, xr, wd);
+    prob.cost_terms = cost_terms_of(pw, pb, xr, wd, ch);
     ctx->saved_data["cost_terms"] = static_cast<int64_t>(prob.cost_terms);
     dfs_fwd_args a{};
     a.Q = Qc.data_ptr();
@@ -254,6 +270,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     a.log_u_init = ptr_or_null<const float>(lui);
     a.log_v_init = ptr_or_null<const float>(lvi);
     a.mask = ptr_or_null<const float>(mk);
+    a.chain_id = ptr_or_null<const int32_t>(ch);
+    a.global_idx = ptr_or_null<const int32_t>(gx);
+    a.bond_matrix = ptr_or_null<const uint8_t>(bd);
     a.O = O.data_ptr<float>();
     a.x_centroid = ptr_or_null<float>(xc);
     a.log_u = lu.data_ptr<float>();
@@ -269,7 +288,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
       start_readback(device_status(Q.device()), cstream.stream());
     }
 
-    ctx->save_for_backward({Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv});
+    ctx->save_for_backward({Qc, Kc, Vc, xr, pw, pb, epsc, wd, lmu, lnu, mk, lu, lv, ch, gx, bd});
     ctx->saved_data["K_iter"] = K_iter;
     ctx->saved_data["lam"] = lam;
     ctx->saved_data["r_0"] = r_0;
@@ -305,7 +324,8 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     check_device_status(saved[0].device());
     const Tensor &Qc = saved[0], &Kc = saved[1], &Vc = saved[2], &xr = saved[3], &pw = saved[4],
                  &pb = saved[5], &epsc = saved[6], &wd = saved[7], &lmu = saved[8], &lnu = saved[9],
-                 &mk = saved[10], &lu = saved[11], &lv = saved[12];
+                 &mk = saved[10], &lu = saved[11], &lv = saved[12], &ch = saved[13], &gx = saved[14],
+                 &bd = saved[15];
     auto needs = [&](const char* key) {
       const int64_t e = ctx->saved_data[key].toInt();
       return e >= 0 && ctx->needs_input_grad(static_cast<size_t>(e));
@@ -321,7 +341,8 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor dnu = needs("e_nu") ? at::empty({B, H, N}, fo) : Tensor();
     // gradients of the shared cost parameters (reference: sinkhorn_kernel.py:2366-2382)
     Tensor dxr = (needs("e_x") && xr.defined()) ? at::empty({B, N, 3}, fo) : Tensor();
-    Tensor dpw = (needs("e_pw") && pw.defined() && pb.defined()) ? at::empty({H, 68}, fo) : Tensor();
+    Tensor dpw = (needs("e_pw") && pw.defined() && (pb.defined() || ch.defined())) ? at::empty({H, 68}, fo)
+                                                                                   : Tensor();
     Tensor dwd = (needs("e_wd") && wd.defined() && xr.defined()) ? at::empty({H}, fo) : Tensor();
     Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
     Tensor resid = at::empty({B * H}, fo);
@@ -355,6 +376,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     a.log_mu = lmu.data_ptr<float>();
     a.log_nu = lnu.data_ptr<float>();
     a.mask = ptr_or_null<const float>(mk);
+    a.chain_id = ptr_or_null<const int32_t>(ch);
+    a.global_idx = ptr_or_null<const int32_t>(gx);
+    a.bond_matrix = ptr_or_null<const uint8_t>(bd);
     a.log_u = lu.data_ptr<float>();
     a.log_v = lv.data_ptr<float>();
     a.dO = dOc.data_ptr<float>();
@@ -384,7 +408,7 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     // gradients in the dtype of the forward's inputs
     const auto in_dt = static_cast<at::ScalarType>(ctx->saved_data["in_dtype"].toInt());
     auto cast = [&](const Tensor& g) { return g.defined() ? g.to(in_dt) : g; };
-    variable_list out(19);
+    variable_list out(22);
     out[0] = cast(dQ);
     out[1] = cast(dK);
     out[2] = cast(dV);
@@ -684,9 +708,31 @@ std::vector<Tensor> flash_sinkhorn_autograd(Tensor Q, Tensor K, Tensor V, c10::o
                                             Tensor log_nu, c10::optional<Tensor> log_u_init,
                                             c10::optional<Tensor> log_v_init, c10::optional<Tensor> mask,
                                             int64_t K_iter, double lam, double r_0, double cg_rtol,
-                                            double cg_atol, int64_t cg_max_iter) {
+                                            double cg_atol, int64_t cg_max_iter, c10::optional<Tensor> chain_id,
+                                            c10::optional<Tensor> global_idx, c10::optional<Tensor> bond_matrix) {
   return FlashSinkhornFn::apply(Q, K, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu, log_u_init,
-                                log_v_init, mask, K_iter, lam, r_0, cg_rtol, cg_atol, cg_max_iter);
+                                log_v_init, mask, K_iter, lam, r_0, cg_rtol, cg_atol, cg_max_iter, chain_id,
+                                global_idx, bond_matrix);
+}
+
+// compute_bins of the reference on the device: (B, N, N) int32
+Tensor compute_bins_cuda(Tensor chain_id, Tensor global_idx, Tensor bond_matrix) {
+  require(chain_id.is_cuda() && global_idx.is_cuda() && bond_matrix.is_cuda(),
+          "compute_bins runs on CUDA tensors only (no CPU path)");
+  require(chain_id.dim() == 2 && global_idx.sizes() == chain_id.sizes() && bond_matrix.dim() == 3 &&
+              bond_matrix.size(0) == chain_id.size(0) && bond_matrix.size(1) == chain_id.size(1) &&
+              bond_matrix.size(2) == chain_id.size(1),
+          "compute_bins: chain_id, global_idx (B, N) and bond_matrix (B, N, N)");
+  const DeviceSwitch guard(chain_id.device());
+  const int64_t B = chain_id.size(0), N = chain_id.size(1);
+  const Tensor ch = chain_id.contiguous().to(at::kInt), gx = global_idx.contiguous().to(at::kInt);
+  const Tensor bd = bond_matrix.contiguous().to(at::kByte);
+  Tensor out = at::empty({B, N, N}, chain_id.options().dtype(at::kInt));
+  const at::cuda::CUDAStream cstream = at::cuda::getCurrentCUDAStream(chain_id.device().index());
+  check_rc(dfs_compute_bins(static_cast<int>(B), static_cast<int>(N), ch.data_ptr<int32_t>(), gx.data_ptr<int32_t>(),
+                            bd.data_ptr<uint8_t>(), out.data_ptr<int32_t>(), cstream.stream()),
+           "dfs_compute_bins");
+  return out;
 }
 
 }  // namespace
@@ -694,7 +740,13 @@ std::vector<Tensor> flash_sinkhorn_autograd(Tensor Q, Tensor K, Tensor V, c10::o
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "native autograd glue for libdfsink (flash Sinkhorn forward / IFT backward)";
   m.def("flash_sinkhorn", &flash_sinkhorn_autograd,
-        "FlashSinkhornFn.apply: returns [O, x_centroid, log_u, log_v], or [O, log_u, log_v] without x_res");
+        "FlashSinkhornFn.apply: returns [O, x_centroid, log_u, log_v], or [O, log_u, log_v] without x_res",
+        py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("x_res"), py::arg("pos_weight"), py::arg("pos_bins"),
+        py::arg("eps"), py::arg("w_dist"), py::arg("log_mu"), py::arg("log_nu"), py::arg("log_u_init"),
+        py::arg("log_v_init"), py::arg("mask"), py::arg("K_iter"), py::arg("lam"), py::arg("r_0"),
+        py::arg("cg_rtol"), py::arg("cg_atol"), py::arg("cg_max_iter"), py::arg("chain_id") = py::none(),
+        py::arg("global_idx") = py::none(), py::arg("bond_matrix") = py::none());
+  m.def("compute_bins", &compute_bins_cuda, "compute_bins of the reference on the device: (B, N, N) int32");
   m.def("balanced_transport", &balanced_transport_autograd,
         "BalancedTransportFn.apply: returns [x_centroid], or [x_centroid, h_centroid] with V");
   m.def("last_report", []() { return last_report(); },

@@ -61,7 +61,7 @@ class DfsFwdArgs(ctypes.Structure):
     _fields_ = [(n, _P) for n in (
         "Q", "K", "V", "C", "x_res", "pos_weight", "pos_bins", "eps", "w_dist", "log_mu", "log_nu",
         "log_u_init", "log_v_init", "mask", "O", "x_centroid", "log_u", "log_v", "status", "T_norm",
-        "r_head")]
+        "r_head", "chain_id", "global_idx", "bond_matrix")]
 
 
 class DfsCgParams(ctypes.Structure):
@@ -73,7 +73,8 @@ class DfsBwdArgs(ctypes.Structure):
     _fields_ = [(n, _P) for n in (
         "Q", "K", "V", "x_res", "pos_weight", "pos_bins", "eps", "w_dist", "log_mu", "log_nu", "mask",
         "log_u", "log_v", "dO", "dxc", "dQ", "dK", "dV", "dlog_mu", "dlog_nu", "dx_res",
-        "dpos_weight", "dw_dist", "cg_iters", "cg_residual", "status", "r_head", "dr_head")]
+        "dpos_weight", "dw_dist", "cg_iters", "cg_residual", "status", "r_head", "dr_head",
+        "chain_id", "global_idx", "bond_matrix")]
 
 
 class DfsIpcHandle(ctypes.Structure):
@@ -90,7 +91,8 @@ class DfsPeerSet(ctypes.Structure):
 
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
                     "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op",
-                    "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer")
+                    "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer",
+                    "dfs_compute_bins")
 
 # phases of the streamed path for row-sharded runs (include/dfsink.h)
 DFS_OP_FWD_INIT, DFS_OP_FWD_ROWS, DFS_OP_FWD_COLS, DFS_OP_FWD_OUT = 0, 1, 2, 3
@@ -254,6 +256,8 @@ def lib() -> ctypes.CDLL:
             L.dfs_stream_op_peer.argtypes = [ctypes.c_int, ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs),
                                              ctypes.c_int, ctypes.c_int, _P, ctypes.c_size_t,
                                              ctypes.POINTER(DfsPeerSet), _P]
+            L.dfs_compute_bins.restype = ctypes.c_int
+            L.dfs_compute_bins.argtypes = [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]
             L.dfs_selftest_mma.restype = ctypes.c_int
             L.dfs_selftest_mma.argtypes = [ctypes.c_int, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, _P]

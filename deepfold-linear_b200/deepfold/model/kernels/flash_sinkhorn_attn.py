@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import torch
 
-from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn
+from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn, unsqueeze_bins
 
 __all__ = ["flash_sinkhorn_attn"]
 
@@ -27,13 +27,14 @@ def flash_sinkhorn_attn(Q_ln, K_ln, V, G, x_res, pos_weight, pos_bins, eps, w_di
 
     Unbatched: Q_ln (H,N,d), x_res (N,3), pos_bins (N,N) ... -> o (N,H*d),
     x_centroid (H,N,3), log_u (H,N), log_v (H,N).  Batched: leading B.
-    mask: (B,N) or (N,), 1 = real, 0 = padding.
+    mask: (B,N) or (N,), 1 = real, 0 = padding.  pos_bins may also be the
+    tuple (chain_id, global_idx, bond_matrix) of compute_bins' inputs.
     """
     unbatched = Q_ln.dim() == 3
     if unbatched:
         Q_ln, K_ln, V, G = Q_ln.unsqueeze(0), K_ln.unsqueeze(0), V.unsqueeze(0), G.unsqueeze(0)
         x_res = x_res.unsqueeze(0)
-        pos_bins = pos_bins.unsqueeze(0)
+        pos_bins = unsqueeze_bins(pos_bins)
         log_mu, log_nu = log_mu.unsqueeze(0), log_nu.unsqueeze(0)
         log_u_init = None if log_u_init is None else log_u_init.unsqueeze(0)
         log_v_init = None if log_v_init is None else log_v_init.unsqueeze(0)

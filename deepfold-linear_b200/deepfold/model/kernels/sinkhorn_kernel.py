@@ -20,6 +20,10 @@ Differences from the reference, all deliberate:
   are computed on the current CUDA device and the results moved back to the
   CPU, differentiably; without a CUDA device the call raises.
 * Head dims other than 32 and 64 (up to 64) run zero-padded inside the library.
+* ``pos_bins`` may also be the tuple ``(chain_id, global_idx, bond_matrix)`` of
+  ``compute_bins``' inputs (src/deepfold/model/position_encoding.py:7): the
+  kernels then evaluate each pair's bin themselves and no (B, N, N) int32 table
+  is built.
 * Device-side errors (a bounded wait that gave up, non-finite potentials) are
   raised as RuntimeError by the first call that returns after the status has
   been read back (the status is read asynchronously), or at once by
@@ -70,11 +74,28 @@ def check_status(wait: bool = True) -> None:
 
 
 def _to_cuda(args: dict) -> dict:
-    """CPU tensors of a call moved to the current CUDA device (autograd follows)."""
+    """CPU tensors of a call (also inside tuples) moved to the current CUDA device
+    (autograd follows)."""
     if not torch.cuda.is_available():
         raise RuntimeError("deepfold B200 Sinkhorn ops run on a CUDA device; none is available (no CPU path)")
     dev = torch.device("cuda", torch.cuda.current_device())
-    return {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in args.items()}
+
+    def mv(v):
+        if isinstance(v, torch.Tensor):
+            return v.to(dev)
+        if isinstance(v, (tuple, list)):
+            return tuple(mv(t) for t in v)
+        return v
+    return {k: mv(v) for k, v in args.items()}
+
+
+def unsqueeze_bins(pos_bins):
+    """pos_bins (a table or compute_bins' inputs) with a leading batch dim."""
+    if pos_bins is None:
+        return None
+    if isinstance(pos_bins, (tuple, list)):
+        return tuple(t.unsqueeze(0) for t in pos_bins)
+    return pos_bins.unsqueeze(0)
 
 
 def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu, log_nu,
@@ -105,7 +126,7 @@ def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_
     if unbatched:
         Q_ln, K_ln, V = Q_ln.unsqueeze(0), K_ln.unsqueeze(0), V.unsqueeze(0)
         x_res = None if x_res is None else x_res.unsqueeze(0)
-        pos_bins = None if pos_bins is None else pos_bins.unsqueeze(0)
+        pos_bins = unsqueeze_bins(pos_bins)
         log_mu, log_nu = log_mu.unsqueeze(0), log_nu.unsqueeze(0)
         log_u_init = None if log_u_init is None else log_u_init.unsqueeze(0)
         log_v_init = None if log_v_init is None else log_v_init.unsqueeze(0)
@@ -121,10 +142,15 @@ def flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_
         raise ValueError("lam must be positive (inf for the balanced problem)")
     # native autograd function FlashSinkhornFn (csrc/dfs_torch.cpp): validates,
     # allocates and calls dfs_fwd / dfs_bwd of libdfsink on the current stream
+    chain = gidx = bond = None
+    if isinstance(pos_bins, (tuple, list)):
+        chain, gidx, bond = pos_bins  # bins evaluated in the kernels
+        pos_bins = None
     ext = nat.ext()
     out = ext.flash_sinkhorn(Q_ln, K_ln, V, x_res, pos_weight, pos_bins, eps, w_dist, log_mu,
-                                   log_nu, log_u_init, log_v_init, mask, int(K_iter), float(lam),
-                                   float(r_0), float(cg["rtol"]), float(cg["atol"]), int(cg["max_iter"]))
+                             log_nu, log_u_init, log_v_init, mask, int(K_iter), float(lam),
+                             float(r_0), float(cg["rtol"]), float(cg["atol"]), int(cg["max_iter"]),
+                             chain, gidx, bond)
     out = tuple(out) if len(out) == 4 else (out[0], None, out[1], out[2])
     _raise_or_warn(int(ext.take_status(False)))  # warnings found by the call's own check
     if unbatched:

@@ -90,7 +90,8 @@ typedef struct {
   const float* C;           /* (B,H,N,N) dense cost, DFS_COST_DENSE                  */
   const float* x_res;       /* (B,N,3) or NULL: no geometry term, no centroid        */
   const float* pos_weight;  /* (H,68) or NULL: no position term                      */
-  const int32_t* pos_bins;  /* (B,N,N) int32 in [0,68), required with pos_weight     */
+  const int32_t* pos_bins;  /* (B,N,N) int32 in [0,68); with pos_weight, this or the */
+                            /* compute_bins inputs at the end of this structure      */
   const float* eps;         /* (H,) entropic regularisation                          */
   const float* w_dist;      /* (H,) geometry weight, or NULL                         */
   const float* log_mu;      /* (B,H,N) log row marginals                             */
@@ -107,6 +108,11 @@ typedef struct {
   float* T_norm;            /* (B,H,N,N) row-normalised plan, or NULL (materialises  */
                             /* the plan: only for the dense compute_transport_output)*/
   const float* r_head;      /* (H,) per-head geometry scale r_h (> 0), or NULL: r_0  */
+  /* position bins computed in the kernels from the inputs of compute_bins, in   */
+  /* place of pos_bins (which must then be NULL): all three or none              */
+  const int32_t* chain_id;     /* (B,N) chain identifier per point                 */
+  const int32_t* global_idx;   /* (B,N) global residue index                       */
+  const uint8_t* bond_matrix;  /* (B,N,N) covalent bond adjacency, 0 / 1           */
 } dfs_fwd_args;
 
 typedef struct {
@@ -142,6 +148,8 @@ typedef struct {
   /* per-head geometry scale (same as the forward's) and its gradient */
   const float* r_head;      /* (H,) r_h, or NULL: r_0                                */
   float* dr_head;           /* (H,) dL/dr_h, or NULL; needs x_res and w_dist         */
+  /* in place of pos_bins, as in dfs_fwd_args */
+  const int32_t* chain_id; const int32_t* global_idx; const uint8_t* bond_matrix;
 } dfs_bwd_args;
 
 /* Library ABI version (DFS_ABI_VERSION of the build). */
@@ -182,6 +190,16 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace,
  *   K-step adjoint it equals at a converged fixed point. */
 int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a,
             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Position bins of the reference's compute_bins (src/deepfold/model/
+ * position_encoding.py:7-52) into a (B,N,N) int32 table `out`:
+ *   same chain, no bond: clamp(gidx_i - gidx_j, -32, 32) + 32;  other chain, no
+ *   bond: 65;  same chain, bond: 66;  other chain, bond: 67.
+ * chain_id, global_idx (B,N) int32; bond_matrix (B,N,N) uint8 (0 / 1).  The
+ * forward and backward can evaluate the same per pair instead (the chain_id /
+ * global_idx / bond_matrix arguments), without the N x N int32 table. */
+int dfs_compute_bins(int B, int N, const int32_t* chain_id, const int32_t* global_idx,
+                     const uint8_t* bond_matrix, int32_t* out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Row-sharded runs (several GPUs per problem).  dfs_stream_op runs one phase of

@@ -20,6 +20,8 @@ so the same torch computation is written out here:
 * ``compute_transport_output``  -- sinkhorn.py:115-198 (running-max plan,
          T / (sum T + 1e-6), padded rows zeroed, sigmoid(G) gate, centroid)
 * gradients: torch autograd through all of it, exactly as the reference does.
+* ``compute_bins``              -- position_encoding.py:7-52 (the pair bins the
+         position term gathers)
 
 One deliberate extension: ``lam = inf`` gives kappa = 1 (the reference's
 lam/(lam+eps) is NaN there); callers that want the reference's own arithmetic
@@ -54,6 +56,19 @@ def cost(Q, K, x=None, pos_weight=None, bins=None, w_dist=None, r_0: float = 10.
     if pos_weight is not None and bins is not None:
         C = C + pos_weight[:, bins.long()].permute(1, 0, 2, 3)
     return C
+
+
+def compute_bins(chain_id, global_idx, bond_matrix):
+    """position_encoding.py:7-52: the 68-bin position / bond code of every pair,
+    (N, N) or (B, N, N) int32."""
+    unb = chain_id.dim() == 1
+    if unb:
+        chain_id, global_idx, bond_matrix = chain_id[None], global_idx[None], bond_matrix[None]
+    same = chain_id[:, :, None] == chain_id[:, None, :]
+    bond = bond_matrix.bool()
+    sep = (global_idx[:, :, None] - global_idx[:, None, :]).clamp(-32, 32) + 32
+    bins = torch.where(bond, torch.where(same, 66, 67), torch.where(same, sep, 65)).to(torch.int32)
+    return bins[0] if unb else bins
 
 
 def sinkhorn_solve(C, log_mu, log_nu, eps, lam=1.0, K=7, log_u_init=None, log_v_init=None, threshold=None,

@@ -220,6 +220,20 @@ def main():
     save("solve_early_stop", dict(C=C, log_mu=lmu, log_nu=lnu, eps=eps), outs,
          K_iter=100, lam=1.0)
 
+    # 7) position bins: the reference's compute_bins (position_encoding.py:7-52)
+    #    on chains with gaps in the residue index, sparse bonds, batched and not
+    from deepfold.model.position_encoding import compute_bins  # noqa: E402
+    r = np.random.default_rng(31)
+    B, N = 2, 57
+    chain = np.sort(r.integers(0, 3, (B, N)), axis=1).astype(np.int64)
+    gidx = np.cumsum(r.integers(1, 4, (B, N)), axis=1).astype(np.int64) - 30
+    bond = r.random((B, N, N)) < 0.04
+    bond = bond | bond.transpose(0, 2, 1)
+    bins = compute_bins(torch.tensor(chain), torch.tensor(gidx), torch.tensor(bond))
+    bins1 = compute_bins(torch.tensor(chain[0]), torch.tensor(gidx[0]), torch.tensor(bond[0]))
+    save("position_bins", dict(chain_id=chain, global_idx=gidx, bond=bond),
+         dict(bins=bins.numpy(), bins_unbatched=bins1.numpy()))
+
     env = dict(os.environ, TRITON_INTERPRET="1")
     subprocess.run([sys.executable, os.path.abspath(__file__), "--ref", args.ref, "--balanced-only"], env=env,
                    check=True)

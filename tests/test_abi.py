@@ -47,8 +47,8 @@ def test_version_and_strings(lib):
 def test_struct_sizes_match_header_layout():
     # every pointer field is 8 bytes; the problem block is 8 int32 + 4 floats
     assert ctypes.sizeof(nat.DfsProblem) == 48
-    assert ctypes.sizeof(nat.DfsFwdArgs) == 21 * 8
-    assert ctypes.sizeof(nat.DfsBwdArgs) == 28 * 8
+    assert ctypes.sizeof(nat.DfsFwdArgs) == 24 * 8
+    assert ctypes.sizeof(nat.DfsBwdArgs) == 31 * 8
     assert ctypes.sizeof(nat.DfsCgParams) == 16
 
 
@@ -113,3 +113,22 @@ def test_native_autograd_rejects_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         ext.flash_sinkhorn(x, x, x, None, None, None, torch.ones(1), None, lm, lm, None, None, None,
                            5, float("inf"), 10.0, 1e-6, 0.0, 50)
+
+
+def test_position_bin_arguments(lib):
+    """pos_bins, or all three compute_bins inputs (chain_id, global_idx,
+    bond_matrix), never both; dfs_compute_bins checks its pointers."""
+    p = nat.make_problem(1, 2, 64, 32, __import__("torch").bfloat16, 5, float("inf"), 10.0)
+    base = dict(Q=16, K=16, V=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16, pos_weight=16)
+    assert lib.dfs_fwd(p, nat.DfsFwdArgs(**base), None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    part = nat.DfsFwdArgs(**base, chain_id=16, global_idx=16)
+    assert lib.dfs_fwd(p, part, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    both = nat.DfsFwdArgs(**base, pos_bins=16, chain_id=16, global_idx=16, bond_matrix=16)
+    assert lib.dfs_fwd(p, both, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    cg = nat.DfsCgParams(rtol=1e-6, atol=1e-6, max_iter=10)
+    bwd = nat.DfsBwdArgs(Q=16, K=16, V=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16, dO=16,
+                         pos_weight=16, dpos_weight=16, chain_id=16)
+    assert lib.dfs_bwd(p, cg, bwd, None, 0, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    assert lib.dfs_compute_bins(2, 8, None, 16, 16, 16, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    assert lib.dfs_compute_bins(-1, 8, 16, 16, 16, 16, None) == nat.DFS_ERR_INVALID_ARGUMENT
+    assert lib.dfs_compute_bins(0, 8, None, None, None, None, None) == nat.DFS_OK

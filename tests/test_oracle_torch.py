@@ -129,3 +129,10 @@ def test_problem_ift_matches_numpy_oracle(lam, masked):
     assert np.max(np.abs(out["log_u"].numpy() - res.log_u[0, 0])) < 1e-9
     for key in ("dQ", "dK", "dV"):
         assert rel(out[key], gr[key][0, 0]) < 1e-8, key
+
+
+def test_golden_compute_bins():
+    z = np.load(os.path.join(GOLD, "position_bins.npz"))
+    ch, gx, bd = (torch.tensor(z["in_" + k]) for k in ("chain_id", "global_idx", "bond"))
+    assert np.array_equal(ort.compute_bins(ch, gx, bd).numpy(), z["out_bins"])
+    assert np.array_equal(ort.compute_bins(ch[0], gx[0], bd[0]).numpy(), z["out_bins_unbatched"])
