@@ -171,6 +171,22 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
           for (int q = 0; q < D / 4; ++q) dst[q] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
+      // this block's shares of the shared-parameter gradients (summed later)
+      if (p.cg.dx != nullptr) {
+        p.cg.dx[o * 3] = 0.0f;
+        p.cg.dx[o * 3 + 1] = 0.0f;
+        p.cg.dx[o * 3 + 2] = 0.0f;
+      }
+      if constexpr (MODE == BT_DQ) {
+        if (p.cg.dw != nullptr) p.cg.dw[o] = 0.0f;
+        if (p.cg.dr != nullptr) p.cg.dr[o] = 0.0f;
+      }
+    }
+    if constexpr (C::kHist) {
+      if (p.cg.dpos != nullptr && p.ct.bins != nullptr && tid < kBinCount) {
+        const int nrb_all = (p.row_end - p.row_begin + 127) / 128;
+        p.cg.dpos[(bh * nrb_all + rb) * kBinCount + tid] = 0.0f;
+      }
     }
     return;
   }

@@ -240,7 +240,8 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     const auto fo = Q.options().dtype(at::kFloat);
     Tensor O = at::empty({B, H, N, d}, fo);
     Tensor xc = xr.defined() ? at::empty({B, H, N, 3}, fo) : Tensor();
-    Tensor lu = at::empty({B, H, N}, fo), lv = at::empty({B, H, N}, fo);
+    const Tensor pot = at::empty({2, B, H, N}, fo);
+    Tensor lu = pot[0], lv = pot[1];
     Tensor status = device_status(Q.device()).word;
 
     dfs_problem prob{};
@@ -313,6 +314,9 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     ctx->saved_data["e_mu"] = next_edge(true);
     ctx->saved_data["e_nu"] = next_edge(true);
     ctx->mark_non_differentiable({lu, lv});
+    // no zero tensors for the outputs whose gradient is absent (the potentials):
+    // the backward takes undefined gradients as zero
+    ctx->set_materialize_grads(false);
     // autograd outputs must be defined tensors: without x_res there is no centroid
     if (xc.defined()) return {O, xc, lu, lv};
     return {O, lu, lv};
@@ -334,9 +338,11 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     const auto fo = Qc.options().dtype(at::kFloat);
     const Tensor dOc = grads[0].defined() ? grads[0].contiguous().to(at::kFloat) : at::zeros({B, H, N, d}, fo);
     const Tensor dxc = (xr.defined() && grads[1].defined()) ? grads[1].contiguous().to(at::kFloat) : Tensor();
-    Tensor dQ = ctx->needs_input_grad(0) ? at::empty({B, H, N, d}, fo) : Tensor();
-    Tensor dK = ctx->needs_input_grad(1) ? at::empty({B, H, N, d}, fo) : Tensor();
-    Tensor dV = ctx->needs_input_grad(2) ? at::empty({B, H, N, d}, fo) : Tensor();
+    // dQ, dK, dV in one buffer: one allocation, and one cast to the inputs' dtype
+    const Tensor gbuf = at::empty({3, B, H, N, d}, fo);
+    const bool want_q = ctx->needs_input_grad(0), want_k = ctx->needs_input_grad(1), want_v = ctx->needs_input_grad(2);
+    float* const g0 = gbuf.data_ptr<float>();
+    const int64_t nd = B * H * N * d;
     Tensor dmu = needs("e_mu") ? at::empty({B, H, N}, fo) : Tensor();
     Tensor dnu = needs("e_nu") ? at::empty({B, H, N}, fo) : Tensor();
     // gradients of the shared cost parameters (reference: sinkhorn_kernel.py:2366-2382)
@@ -344,8 +350,8 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     Tensor dpw = (needs("e_pw") && pw.defined() && (pb.defined() || ch.defined())) ? at::empty({H, 68}, fo)
                                                                                    : Tensor();
     Tensor dwd = (needs("e_wd") && wd.defined() && xr.defined()) ? at::empty({H}, fo) : Tensor();
-    Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
-    Tensor resid = at::empty({B * H}, fo);
+    // CG report: iterations (int32) then residuals (fp32) per problem
+    const Tensor rep = at::empty({2, B * H}, Qc.options().dtype(at::kInt));
     Tensor status = device_status(Qc.device()).word;
 
     dfs_problem prob{};
@@ -383,16 +389,16 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
     a.log_v = lv.data_ptr<float>();
     a.dO = dOc.data_ptr<float>();
     a.dxc = ptr_or_null<const float>(dxc);
-    a.dQ = ptr_or_null<float>(dQ);
-    a.dK = ptr_or_null<float>(dK);
-    a.dV = ptr_or_null<float>(dV);
+    a.dQ = want_q ? g0 : nullptr;
+    a.dK = want_k ? g0 + nd : nullptr;
+    a.dV = want_v ? g0 + 2 * nd : nullptr;
     a.dlog_mu = ptr_or_null<float>(dmu);
     a.dlog_nu = ptr_or_null<float>(dnu);
     a.dx_res = ptr_or_null<float>(dxr);
     a.dpos_weight = ptr_or_null<float>(dpw);
     a.dw_dist = ptr_or_null<float>(dwd);
-    a.cg_iters = iters.data_ptr<int32_t>();
-    a.cg_residual = resid.data_ptr<float>();
+    a.cg_iters = rep.data_ptr<int32_t>();
+    a.cg_residual = reinterpret_cast<float*>(rep.data_ptr<int32_t>() + B * H);
     a.status = status.data_ptr<int32_t>();
     size_t fwd_ws = 0, bwd_ws = 0;
     check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
@@ -403,15 +409,15 @@ struct FlashSinkhornFn : public torch::autograd::Function<FlashSinkhornFn> {
       std::lock_guard<std::mutex> lock(g_status_mu);
       start_readback(device_status(Qc.device()), cstream.stream());
     }
-    last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
+    last_report() = {rep, status, ctx->saved_data["fwd_status"].toTensor()};
 
-    // gradients in the dtype of the forward's inputs
+    // gradients in the dtype of the forward's inputs (one cast for the three)
     const auto in_dt = static_cast<at::ScalarType>(ctx->saved_data["in_dtype"].toInt());
-    auto cast = [&](const Tensor& g) { return g.defined() ? g.to(in_dt) : g; };
+    const Tensor gcast = gbuf.to(in_dt);
     variable_list out(22);
-    out[0] = cast(dQ);
-    out[1] = cast(dK);
-    out[2] = cast(dV);
+    out[0] = want_q ? gcast[0] : Tensor();
+    out[1] = want_k ? gcast[1] : Tensor();
+    out[2] = want_v ? gcast[2] : Tensor();
     out[3] = dxr.defined() ? dxr.to(static_cast<at::ScalarType>(ctx->saved_data["x_dtype"].toInt())) : dxr;
     out[4] = dpw.defined() ? dpw.to(static_cast<at::ScalarType>(ctx->saved_data["pw_dtype"].toInt())) : dpw;
     out[7] = dwd.defined() ? dwd.to(static_cast<at::ScalarType>(ctx->saved_data["wd_dtype"].toInt())) : dwd;
@@ -624,8 +630,7 @@ struct BalancedTransportFn : public torch::autograd::Function<BalancedTransportF
     Tensor dx = ctx->needs_input_grad(2) ? at::empty({B, N, 3}, fo) : Tensor();
     Tensor dwd = want_alpha ? at::empty({H}, fo) : Tensor();
     Tensor dr = want_r ? at::empty({H}, fo) : Tensor();
-    Tensor iters = at::empty({B * H}, Qc.options().dtype(at::kInt));
-    Tensor resid = at::empty({B * H}, fo);
+    const Tensor rep = at::empty({2, B * H}, Qc.options().dtype(at::kInt));  // CG iterations, residuals
     Tensor status = device_status(Qc.device()).word;
 
     dfs_problem prob{};
@@ -665,8 +670,8 @@ struct BalancedTransportFn : public torch::autograd::Function<BalancedTransportF
     a.dx_res = ptr_or_null<float>(dx);
     a.dw_dist = ptr_or_null<float>(dwd);
     a.dr_head = ptr_or_null<float>(dr);
-    a.cg_iters = iters.data_ptr<int32_t>();
-    a.cg_residual = resid.data_ptr<float>();
+    a.cg_iters = rep.data_ptr<int32_t>();
+    a.cg_residual = reinterpret_cast<float*>(rep.data_ptr<int32_t>() + B * H);
     a.status = status.data_ptr<int32_t>();
     size_t fwd_ws = 0, bwd_ws = 0;
     check_rc(dfs_workspace_size(&prob, &fwd_ws, &bwd_ws), "dfs_workspace_size");
@@ -677,7 +682,7 @@ struct BalancedTransportFn : public torch::autograd::Function<BalancedTransportF
       std::lock_guard<std::mutex> lock(g_status_mu);
       start_readback(device_status(Qc.device()), cstream.stream());
     }
-    last_report() = {iters, resid, status, ctx->saved_data["fwd_status"].toTensor()};
+    last_report() = {rep, status, ctx->saved_data["fwd_status"].toTensor()};
 
     auto as = [&](const Tensor& g, const char* key) {
       return g.to(static_cast<at::ScalarType>(ctx->saved_data[key].toInt()));
@@ -750,8 +755,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("balanced_transport", &balanced_transport_autograd,
         "BalancedTransportFn.apply: returns [x_centroid], or [x_centroid, h_centroid] with V");
   m.def("last_report", []() { return last_report(); },
-        "[cg_iters, cg_residual, status, fwd_status] of the most recent backward (status: the device's sticky "
-        "status word, the OR of every call's bits since the last check)");
+        "[report (2, B*H) int32: CG iterations, then the residuals' fp32 bits; status, fwd_status] of the most "
+        "recent backward (status: the device's sticky status word, the OR of every call's bits since the last "
+        "check)");
   m.def("take_status", &take_status, py::arg("wait") = true,
         "status bits of the current device's calls since the last read (after the stream drains with "
         "wait=True), plus warning bits seen by the checks inside calls; the bits are cleared");

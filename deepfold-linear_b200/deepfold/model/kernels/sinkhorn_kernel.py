@@ -50,7 +50,10 @@ def last_cg_report() -> dict:
     """Device tensors (cg_iters, cg_residual, status, fwd_status) of the most
     recent backward."""
     rep = nat.ext().last_report()
-    return dict(zip(("cg_iters", "cg_residual", "status", "fwd_status"), rep))
+    if not rep:
+        return {}
+    cg, status, fwd_status = rep
+    return dict(cg_iters=cg[0], cg_residual=cg[1].view(torch.float32), status=status, fwd_status=fwd_status)
 
 
 def _raise_or_warn(bits: int) -> None:

@@ -109,3 +109,19 @@ def test_stream_terms_gradients_are_bitwise_reproducible():
     b = _run(z, 30, 1.0)
     for k in ("dx", "dpos", "dw", "dQ", "dK", "dV"):
         assert np.array_equal(a[k], b[k]), k
+
+
+def test_stream_terms_no_stale_workspace():
+    """Row blocks without a valid row (a short sample of a padded batch) skip all
+    work; their shares of dx_res, dw_dist and dpos_weight must still be written
+    (as zeros), whatever the workspace held before.  The caching allocator is
+    filled with NaN first, so a stale read shows."""
+    z = _inputs(2, 2, 640, 64, seed=5, lengths=[640, 200])
+    ref = _run(z, 20, 1.0)
+    poison = torch.full((64 << 20,), float("nan"), device="cuda")  # 256 MB of NaN, then freed
+    del poison
+    got = _run(z, 20, 1.0)
+    for k in ("dx", "dpos", "dw", "dQ", "dK", "dV", "o", "xc"):
+        assert np.all(np.isfinite(got[k])), k
+        assert np.array_equal(got[k], ref[k]), k
+    assert np.all(got["dx"][1, 200:] == 0)
