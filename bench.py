@@ -14,7 +14,8 @@ long-sequence row-sharded one: B=1 H=16 N=8192 d=64, 30 iterations, CG tol
 through NVLink peer stores each half-iteration (strong scaling: one call is the
 whole configuration's forward + backward).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|transport]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
+                    [--config 2|3|4|transport]
 
 ``--config 3`` (B=8 H=16 padded N=1024 d=64, variable lengths, softmax
 marginals, eps 0.5, 50 iterations) spreads the (batch, head) problems over the
@@ -24,11 +25,15 @@ ranks with a length^2-balanced partition (no data-path collective).
 (balanced_sinkhorn_transport, fwd+bwd) at the shapes the reference publishes
 timings for (B=1 H=16 d_h=32 K=20, N = 64 ... 768) and prints them beside those.
 
-``--impl reference`` times the reference's own CPU path -- dense cost,
-sinkhorn_solve, compute_transport_output and torch autograd, restated in
-``oracle/sinkhorn_torch.py`` because the reference source does not travel with
-this repository -- in float32 on all host threads, on the same workload, and
-prints the same metric.
+``--impl reference`` times the reference's own CPU path -- dense cost, its
+``sinkhorn_solve`` and ``compute_transport_output``, torch autograd -- from the
+reference package pip-installed into ``baseline/_ref`` (restated in
+``oracle/sinkhorn_torch.py`` where that install is absent), in float32 on all
+host threads, on the same workload, and prints the same metric.
+
+``--impl triton`` times the reference's own GPU path (``flash_sinkhorn``,
+Triton forward and unrolled Triton backward, from ``baseline/_ref``) on this
+GPU on config 2 or 3: the GPU bar, not one of the driver's arms.
 """
 
 from __future__ import annotations
@@ -659,14 +664,51 @@ def _ref_problem(B, H, N, d, K_iter, lam, eps, seed, mask=None, lmu=None, lnu=No
     g = torch.Generator().manual_seed(seed)
     Q, K, V, dO = (torch.randn(B, H, N, d, generator=g).to(torch.bfloat16).float() for _ in range(4))
     lm = torch.full((B, H, N), -math.log(N))
+    # the reference's compute_transport_output always gates (sigmoid(G) * O_avg); G = 0 gates by 1/2
     return dict(Q=Q, K=K, V=V, dO=dO, eps=torch.full((H,), float(eps)), log_mu=lm if lmu is None else lmu,
-                log_nu=lm if lnu is None else lnu, K_iter=K_iter, lam=1e6 if math.isinf(lam) else lam, mask=mask)
+                log_nu=lm if lnu is None else lnu, K_iter=K_iter, lam=1e6 if math.isinf(lam) else lam, mask=mask,
+                G=torch.zeros(B, H, N, d), dO_flat=dO.permute(0, 2, 1, 3).reshape(B, N, H * d).contiguous(),
+                kind="reference" if _REF_ACTIVE else "port")
+
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")   # the reference, pip-installed (git-ignored, travels)
+
+
+def _reference_installed() -> bool:
+    return os.path.isfile(os.path.join(REF_DIR, "deepfold", "model", "sinkhorn.py"))
+
+
+_REF_ACTIVE = False
+
+
+def _use_reference_package():
+    """Put the installed reference first on sys.path (only in processes that never
+    import this build's ``deepfold``: the --impl reference / triton arms)."""
+    global _REF_ACTIVE
+    if "deepfold" in sys.modules:
+        raise RuntimeError("the reference package must be imported before this build's deepfold")
+    sys.path.insert(0, REF_DIR)
+    _REF_ACTIVE = True
 
 
 def _ref_call(prob):
-    """One forward + autograd backward of the reference's CPU path (dense cost,
-    sinkhorn_solve, compute_transport_output, torch autograd), restated in
-    oracle/sinkhorn_torch.py, float32."""
+    """One forward + autograd backward of the reference's CPU path in float32:
+    C = -Q K^T / sqrt(d) (the cost of sinkhorn_kernel.py:59-129 without the
+    optional terms), the reference's own sinkhorn_solve (sinkhorn.py:17) and
+    compute_transport_output (sinkhorn.py:115) from the installed package, torch
+    autograd of sum(o * dO).  Without the installed package the same computation
+    restated in oracle/sinkhorn_torch.py runs instead."""
+    if prob.get("kind") == "reference":
+        from deepfold.model.sinkhorn import compute_transport_output, sinkhorn_solve
+        Q, K, V = (prob[k].detach().clone().requires_grad_(True) for k in ("Q", "K", "V"))
+        d = Q.shape[-1]
+        C = -(Q @ K.transpose(-1, -2)) / math.sqrt(d)
+        lam = prob["lam"]
+        lu, lv = sinkhorn_solve(C, prob["log_mu"], prob["log_nu"], prob["eps"], lam=lam, K=prob["K_iter"],
+                                mask=prob["mask"])
+        o, _, _ = compute_transport_output(V, prob["G"], lu, lv, C, prob["eps"], mask=prob["mask"])
+        torch.autograd.grad(o, (Q, K, V), grad_outputs=prob["dO_flat"])
+        return
     from oracle import sinkhorn_torch as ort
     ort.attn_fwd_bwd(prob["Q"], prob["K"], prob["V"], prob["eps"], prob["log_mu"], prob["log_nu"], prob["K_iter"],
                      prob["lam"], prob["dO"], dtype=torch.float32, mask=prob["mask"])
@@ -690,23 +732,45 @@ def _ref_sample(cfg_id):
                                f"sum over the config's problems of (L_bh/{L})^2 = {scale:.1f}")
 
 
-def cpu_baseline(cfg_id=2, seconds=15.0):
-    """The reference's CPU path timed on a bounded sample (~`seconds` of work)."""
-    cores = _ref_threads()
+def _ref_text(kind, n, what):
+    where = ("the installed reference package" if kind == "reference"
+             else "restated in oracle/sinkhorn_torch.py")
+    return (f"{n} calls of the reference's torch CPU path (dense cost + sinkhorn_solve + compute_transport_output "
+            f"+ autograd, float32, {where}): {what}")
+
+
+def _time_reference(cfg_id, warmup, steps=None, seconds=None):
+    """(seconds per sample call, calls made, problem, per_call, what)."""
     prob, per_call, what = _ref_sample(cfg_id)
-    _ref_call(prob)  # warm-up
+    for _ in range(max(1, warmup)):
+        _ref_call(prob)
     t0 = time.perf_counter()
     n = 0
     while True:
         _ref_call(prob)
         n += 1
-        if time.perf_counter() - t0 > seconds:
+        if (steps is not None and n >= steps) or (seconds is not None and time.perf_counter() - t0 > seconds):
             break
-    dt = (time.perf_counter() - t0) / n
-    return {"value": round(per_call / dt, 6), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n} calls of the reference's torch CPU path (dense cost + sinkhorn_solve + "
-                      f"compute_transport_output + autograd, float32, restated in oracle/sinkhorn_torch.py): {what}",
-            "cpu": _cpu_model()}
+    return (time.perf_counter() - t0) / n, n, prob, per_call, what
+
+
+def cpu_baseline(cfg_id=2, seconds=15.0):
+    """The reference's CPU path timed on a bounded sample (~`seconds` of work): the
+    installed reference package in a child process (this process has already
+    imported this build's ``deepfold``), else the restatement in this process."""
+    if _reference_installed():
+        env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--config",
+                            str(cfg_id), "--warmup", "1", "--ref-seconds", str(seconds)],
+                           env=env, capture_output=True, text=True, timeout=600)
+        for ln in reversed(r.stdout.splitlines()):
+            if ln.startswith("{"):
+                return json.loads(ln)["cpu_baseline"]
+        print(f"cpu_baseline: reference child failed ({r.returncode}): {r.stderr[-500:]}", file=sys.stderr)
+    cores = _ref_threads()
+    dt, n, prob, per_call, what = _time_reference(cfg_id, 1, seconds=seconds)
+    return {"value": round(per_call / dt, 6), "unit": UNIT, "cores": cores, "kind": prob["kind"],
+            "sample": _ref_text(prob["kind"], n, what), "cpu": _cpu_model()}
 
 
 def _cpu_model():
@@ -726,13 +790,10 @@ def run_reference(args):
     if rank != 0:
         return
     cores = _ref_threads()
-    prob, per_call, what = _ref_sample(args.config)
-    for _ in range(args.warmup):
-        _ref_call(prob)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _ref_call(prob)
-    dt = (time.perf_counter() - t0) / args.steps
+    if args.ref_seconds:
+        dt, n, prob, per_call, what = _time_reference(args.config, args.warmup, seconds=args.ref_seconds)
+    else:
+        dt, n, prob, per_call, what = _time_reference(args.config, args.warmup, steps=args.steps)
     value = per_call / dt
     if args.config == 2:
         c = CFG
@@ -742,16 +803,100 @@ def run_reference(args):
         workload, shape = big_workload_name(args.config), dict(global_batch=c["B"], heads=c["H"], seq_len=c["N"],
                                                                head_dim=c["d"])
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / value, 3),
+            "steps": n, "warmup": args.warmup, "ms_per_step": round(1e3 / value, 3),
             "higher_is_better": True, "scaling": "weak" if args.config == 2 else "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded N(0,1), bf16-rounded values in float32)",
             "config": dict(workload=workload, parallelism="cpu", **shape),
-            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{args.steps} calls of the reference's torch CPU path (dense cost + "
-                                       "sinkhorn_solve + compute_transport_output + autograd, float32, restated "
-                                       f"in oracle/sinkhorn_torch.py): {what}",
-                             "cpu": _cpu_model()},
+            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": cores, "kind": prob["kind"],
+                             "sample": _ref_text(prob["kind"], n, what), "cpu": _cpu_model()},
             "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_triton(args):
+    """The reference's own GPU path on this GPU: ``flash_sinkhorn``
+    (sinkhorn_kernel.py:2385; Triton forward, Triton unrolled backward) from the
+    installed reference package, unmodified, on the same seeded workload as this
+    build's arm (config 2, or config 3 with its masks and marginals).  The
+    reference computes in float32 (it casts its inputs); its cost always carries
+    the position and geometry terms, given zero weights here.  CUDA events around
+    each fwd + bwd, L2 flushed between steps.  Not one of the driver's arms: a
+    measurement of the GPU bar."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if not _REF_ACTIVE:
+        print(json.dumps({"impl": "triton-reference", "unavailable": "reference package not installed in "
+                          "baseline/_ref"}))
+        return
+    from deepfold.model.kernels.sinkhorn_kernel import flash_sinkhorn as ref_flash_sinkhorn
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.config == 2:
+        c = dict(CFG, lam=float("inf"), varlen=False)
+        g = torch.Generator().manual_seed(0)
+        B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+        host = {k: torch.randn(B, H, N, d, generator=g).to(torch.bfloat16) for k in ("Q", "K", "V", "dO")}
+        mask = None
+        lmu = torch.full((B, H, N), -math.log(N))
+        lnu = lmu.clone()
+        workload = workload_name()
+    else:
+        c = BIG[args.config]
+        B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+        host, _, mask, lmu, lnu = big_inputs(c)
+        workload = big_workload_name(args.config)
+    lam = 1e6 if math.isinf(c["lam"]) else c["lam"]
+    inp = {k: v.float().to(dev) for k, v in host.items()}
+    x_res = torch.zeros(B, N, 3, device=dev)
+    pos_weight = torch.zeros(H, 68, device=dev)
+    pos_bins = torch.zeros(B, N, N, device=dev, dtype=torch.int32)
+    w_dist = torch.zeros(H, device=dev)
+    eps = torch.full((H,), float(c["eps"]), device=dev)
+    lmu, lnu = lmu.to(dev), lnu.to(dev)
+    mask_d = None if mask is None else mask.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        leaves = [inp[k].detach().requires_grad_(True) for k in ("Q", "K", "V")]
+        O, _, _, _ = ref_flash_sinkhorn(*leaves, x_res, pos_weight, pos_bins, eps, w_dist, lmu, lnu,
+                                        K_iter=c["K_iter"], lam=lam, mask=mask_d)
+        torch.autograd.grad(O, leaves, grad_outputs=inp["dO"])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    fwd_only = []
+    evs = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step()
+        e1.record(stream)
+        evs.append((e0, e1))
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.no_grad():
+            ref_flash_sinkhorn(inp["Q"], inp["K"], inp["V"], x_res, pos_weight, pos_bins, eps, w_dist, lmu, lnu,
+                               K_iter=c["K_iter"], lam=lam, mask=mask_d)
+        e1.record(stream)
+        fwd_only.append((e0, e1))
+    torch.cuda.synchronize()
+    t = sorted(a.elapsed_time(b) for a, b in evs)
+    tf = sorted(a.elapsed_time(b) for a, b in fwd_only)
+    med, medf = t[len(t) // 2], tf[len(tf) // 2]
+    line = {"impl": "triton-reference", "metric": METRIC, "value": round(1e3 / med, 4), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(med, 4),
+            "fwd_ms": round(medf, 4), "higher_is_better": True, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1), bf16-rounded values in float32)",
+            "config": {"workload": workload, "l2": "flushed between timed steps",
+                       "path": "reference flash_sinkhorn (Triton fwd + unrolled Triton bwd), lam=1e6 for balanced"},
+            "gpu": torch.cuda.get_device_name(dev)}
     print(json.dumps(line), flush=True)
 
 
@@ -828,7 +973,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours")
+    ap.add_argument("--ref-seconds", type=float, default=None, help=argparse.SUPPRESS)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config4", action="store_true", help="skip the single-GPU long-sequence point")
@@ -836,8 +982,10 @@ def main():
                     help="default: 2 on one GPU, 4 (long-sequence row shards) on several; 'transport': the "
                          "balanced transport at the reference's published shapes (one GPU)")
     args = ap.parse_args()
+    if args.impl in ("reference", "triton") and _reference_installed():
+        _use_reference_package()
     if args.config == "transport":
-        if args.impl == "reference":
+        if args.impl != "ours":
             print(json.dumps({"impl": "reference", "unavailable": "the transport mode times this build only; "
                               "the reference's published timings are printed beside it"}))
             return
@@ -853,6 +1001,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "triton":
+        run_triton(args)
     elif args.config in BIG:
         run_big(args)
     else:
