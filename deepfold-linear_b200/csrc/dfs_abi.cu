@@ -42,7 +42,9 @@ int split_kind(const dfs_problem* p) {
   return XF_NONE;
 }
 int kdim(const dfs_problem* p);
+bool dense_streamed(const dfs_problem* p);
 int xform(const dfs_problem* p) {
+  if (dense_streamed(p)) return XF_NONE;  // reads C and fp32 V as given
   const int x = split_kind(p);
   if (x != XF_NONE) return x;
   return kdim(p) != p->d ? XF_PAD : XF_NONE;
@@ -61,6 +63,13 @@ int kdim(const dfs_problem* p) {
 bool padded(const dfs_problem* p) { return xform(p) != XF_NONE; }
 bool resident(const dfs_problem* p) { return kdim(p) == 32 && p->N <= kResidentMaxN; }
 bool streamed(const dfs_problem* p) { return kdim(p) != 0 && p->N <= kStreamMaxN; }
+// dense cost outside the resident range: the HBM passes over C (dfs_dense.cu),
+// fp32 V of head dim up to 128
+constexpr int kDenseMaxD = 128;
+bool dense_streamed(const dfs_problem* p) {
+  return p->cost_mode == DFS_COST_DENSE && !(kdim(p) == 32 && p->N <= kResidentMaxN) && p->d <= kDenseMaxD &&
+         p->N <= kStreamMaxN;
+}
 
 size_t elem_bytes(int dtype) { return dtype == DFS_F32 ? 4 : 2; }
 size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -168,6 +177,12 @@ int check_fwd_args(const dfs_problem* p, const dfs_fwd_args* a) {
   if (!bins_args_ok(a->pos_bins, a->chain_id, a->global_idx, a->bond_matrix)) return DFS_ERR_INVALID_ARGUMENT;
   if (a->pos_weight && !has_bins(a->pos_bins, a->chain_id)) return DFS_ERR_INVALID_ARGUMENT;
   if (a->x_centroid && !a->x_res) return DFS_ERR_INVALID_ARGUMENT;
+  if (dense_streamed(p)) {
+    // fp32 V (the dense entry points' values), no position / geometry terms (C holds the whole cost)
+    if (a->V && p->in_dtype != DFS_F32) return DFS_ERR_UNSUPPORTED;
+    if (a->pos_weight || a->w_dist) return DFS_ERR_INVALID_ARGUMENT;
+    return DFS_OK;
+  }
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   // the kernels read the operands in 16-byte chunks (padded ones are copies)
   if (!padded(p) && (!aligned16(a->O) || !aligned16(a->Q) || !aligned16(a->K) || !aligned16(a->V)))
@@ -259,6 +274,11 @@ int dfs_max_n(int d) { return kernel_head_dim(d) != 0 ? kStreamMaxN : 0; }
 
 int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes) {
   if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
+  if (dense_streamed(p)) {
+    if (fwd_bytes) *fwd_bytes = dense_fwd_workspace(p->B, p->H);
+    if (bwd_bytes) *bwd_bytes = 0;  // no backward on the dense-cost path
+    return DFS_OK;
+  }
   if (!resident(p) && !streamed(p)) return DFS_ERR_UNSUPPORTED;
   const bool res = resident(p);
   const int dk = kdim(p);
@@ -274,6 +294,11 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   int rc = check_fwd_args(p, a);
   if (rc != DFS_OK) return rc;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dense_streamed(p)) {
+    if (workspace == nullptr || workspace_bytes < dense_fwd_workspace(p->B, p->H) || !aligned16(workspace))
+      return DFS_ERR_WORKSPACE;
+    return cuda_status(launch_dense_fwd(fwd_params(p, a), workspace, st));
+  }
   // padded head dim: copies at the front of the workspace, the kernels' share after them
   const size_t pad = pad_fwd_bytes(p);
   if (pad > 0 && (workspace == nullptr || workspace_bytes < pad || !aligned16(workspace))) return DFS_ERR_WORKSPACE;

@@ -156,6 +156,10 @@ DFS_DEV_HOST_INLINE BinSource bin_source(const BwdParams& p) {
 cudaError_t launch_resident_fwd(const FwdParams& p, cudaStream_t st);
 size_t resident_fwd_smem(int N, int d);
 cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
+// dense-cost forward streamed from the caller's C (problems outside the
+// resident kernels' range): potentials, O / T_norm / x_centroid, early stop
+size_t dense_fwd_workspace(int B, int H);
+cudaError_t launch_dense_fwd(const FwdParams& p, void* ws, cudaStream_t st);
 // Peer exchange of a row-sharded forward: every GPU's workspace (same layout,
 // 256-byte aligned bases) and the cumulative arrival count the phase waits for.
 struct PeerInfo {

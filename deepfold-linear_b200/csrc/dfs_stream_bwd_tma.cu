@@ -94,7 +94,11 @@ struct BTileCfg {
   static constexpr uint32_t SB = (kDT ? 2 : 1) * BTILE;               // bytes of a ring stage
   static constexpr uint32_t OFF_B3 = OFF_B + NS * SB;
   static constexpr uint32_t OFF_DS = OFF_B3 + (kAcc ? NS3 * B3TILE : 0u);   // 128 x 64 fp32
-  static constexpr uint32_t OFF_VEC = OFF_DS + (kAcc ? 128u * kBTW * 4 : 0u);
+  // BT_OUT: T_norm enters the product as two tiles, its tf32 part and the fp32
+  // remainder, so that O = T_norm V carries ~2^-20 relative error, not tf32's 2^-11
+  static constexpr bool kSplitT = MODE == BT_OUT;
+  static constexpr uint32_t OFF_DS2 = OFF_DS + (kAcc ? 128u * kBTW * 4 : 0u);
+  static constexpr uint32_t OFF_VEC = OFF_DS2 + (kSplitT ? 128u * kBTW * 4 : 0u);
   static constexpr int NMRG = TERMS ? 5 : 3;                          // values merged per row (dx, dw, dr)
   static constexpr uint32_t OFF_MRG = OFF_VEC + NS * VEC;                // 3 parts x NMRG values x 128
   static constexpr uint32_t OFF_PW = OFF_MRG + 3 * NMRG * 128 * 4;       // TERMS: 69 scaled bin weights
@@ -336,8 +340,10 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
         if (!mbar_wait(&full3[s3], (v / C::NS3) & 1)) err = 1;
         tc_fence_after();
         if (lane == 0) {
-          issue_mma<128, D, kBTW>(t_acc, sDS, reinterpret_cast<const float*>(base + C::OFF_B3 + s3 * C::B3TILE),
-                                  v > 0);
+          const float* sB3 = reinterpret_cast<const float*>(base + C::OFF_B3 + s3 * C::B3TILE);
+          issue_mma<128, D, kBTW>(t_acc, sDS, sB3, v > 0);
+          if constexpr (C::kSplitT)
+            issue_mma<128, D, kBTW>(t_acc, reinterpret_cast<const float*>(base + C::OFF_DS2), sB3, true);
           mma_commit(dsempty);
           mma_commit(&empty3[s3]);
         }
@@ -572,10 +578,27 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
       }
       if constexpr (kAcc) {
         if (u >= 1 && !mbar_wait(dsempty, (u - 1) & 1)) err = 1;  // accumulation MMA of tile u-1 done
+        if constexpr (C::kSplitT) {
+          // tf32 part (the 10 mantissa bits the tensor core reads) and the remainder
+          float* sDS2 = reinterpret_cast<float*>(base + C::OFF_DS2);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<float4*>(sDS + (sw_off(lrow, 16 * part + 4 * q, 128) >> 2)) =
-              make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+          for (int q = 0; q < 4; ++q) {
+            float hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hi[e] = __uint_as_float(__float_as_uint(out[4 * q + e]) & 0xFFFFE000u);
+              lo[e] = out[4 * q + e] - hi[e];
+            }
+            const uint32_t o4 = sw_off(lrow, 16 * part + 4 * q, 128) >> 2;
+            *reinterpret_cast<float4*>(sDS + o4) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<float4*>(sDS2 + o4) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float4*>(sDS + (sw_off(lrow, 16 * part + 4 * q, 128) >> 2)) =
+                make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+        }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(dsfull);

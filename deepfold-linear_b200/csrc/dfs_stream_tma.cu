@@ -35,6 +35,7 @@
 // cover 128- and 256-byte operand rows (d = 64, or fp32 with d = 32); other
 // shapes, and operands not aligned to 16 bytes, keep the register-staged
 // kernels of dfs_stream.cu / dfs_stream_bwd.cu.
+#include <cstdlib>
 #include <mutex>
 
 #include "dfs_tma.cuh"
@@ -45,10 +46,18 @@ constexpr int kTThreads = 320;  // warps 0-7 epilogue, 8 producer, 9 MMA
 constexpr int kTEpi = 256;      // epilogue threads
 constexpr int kTProducer = 8, kTMma = 9;
 constexpr float kLag = 16.0f;   // log2 headroom of the lagged exponent reference
-constexpr int kMaxSplit = 4;    // column splits of a row block (small grids)
-// bf16 / fp16 passes: one exponential in kPolyEvery runs as a polynomial on the
-// FMA pipes (ex2_poly) instead of the MUFU, whose throughput bounds these passes
-constexpr int kPolyEvery = 5;  // (k = 4, 9, 14, ...: spread over the four partial sums)
+constexpr int kMaxSplit = 8;    // column splits of a row block (small grids)
+constexpr int kSplitCtas = 4096;  // CTAs of a split launch at most (their partials' scratch)
+// bf16 / fp16 passes: the 32 elements of a chunk are worked in 16 pairs with the
+// packed fp32 pair instructions (one FMA / ADD issue per two elements); the
+// pairs whose bit is set in kPolyPairs take their exponentials as a polynomial
+// on the FMA pipes (ex2_poly2) instead of the MUFU, whose throughput bounds
+// these passes -- 4 of 16 pairs (8 of 32 elements) balance the MUFU's 8 cycles
+// per warp instruction against the issue slots the rest of the chunk needs.
+#ifndef DFS_POLY_PAIRS
+#define DFS_POLY_PAIRS 0x1111u  // pairs 0, 4, 8, 12
+#endif
+constexpr unsigned kPolyPairs = DFS_POLY_PAIRS;
 constexpr int kTCols = 128;     // columns per tile
 
 struct TileParams {
@@ -74,7 +83,7 @@ struct TileParams {
   const unsigned long long* wait_cnt;
   unsigned long long wait_for;
   const int2* extent;      // (B) valid extents of the mask, or null (scan the mask)
-  float* part;             // nsplit > 1: (nsplit, 3, BH, N) partial results of the column splits
+  float* part;             // nsplit > 1: (CTA, 3, 128) partial results of the column splits
   unsigned* counter;       // nsplit > 1: (BH * row blocks) arrival counters, zero between launches
   int B, H, N;
   int row_begin, row_end;  // rows this launch handles
@@ -487,15 +496,19 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(rv32[k]);
         const float* cb = cbs + s * 128 + 32 * ch;
         if constexpr (MODE == TL_MATVEC && C::kExt) {
-          // v = S + g / scale (the column bias came with the MMA)
+          // v = S + g / scale (the column bias came with the MMA); element pairs
           const float* cv = cvs + s * 128 + 32 * ch;
-          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          const float2 sc2 = make_float2(scale, scale), fi2 = make_float2(fi, fi);
+          float2 a0 = make_float2(0.0f, 0.0f), a1 = a0;
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const float x = fmaf(v[k], scale, fi);
-            a[k & 3] = fmaf((k % kPolyEvery == kPolyEvery - 1) ? ex2_poly(x) : ex2(x), cv[k], a[k & 3]);
+          for (int k = 0; k < 32; k += 2) {
+            const float2 x = __ffma2_rn(make_float2(v[k], v[k + 1]), sc2, fi2);
+            const float2 e = ((kPolyPairs >> (k >> 1)) & 1u) ? ex2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+            const float2 w = *reinterpret_cast<const float2*>(cv + k);
+            if ((k >> 1) & 1) a1 = __ffma2_rn(e, w, a1);
+            else a0 = __ffma2_rn(e, w, a0);
           }
-          acc += (a[0] + a[1]) + (a[2] + a[3]);
+          acc += (a0.x + a1.x) + (a0.y + a1.y);
         } else if constexpr (MODE == TL_MATVEC) {
           const float* cv = cvs + s * 128 + 32 * ch;
           float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -505,26 +518,34 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
         } else if constexpr (C::kExt) {
           // v = S + g / scale: x - m = v scale - m is one FMA per element; the
           // chunk maximum is taken on v (scale > 0).  Same lagged reference as below.
-          float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          const float nm = -m;
+          // element pairs: x = v scale - m by one packed FMA, the pair's
+          // exponentials (MUFU or polynomial), two packed partial sums
+          const float2 sc2 = make_float2(scale, scale);
+          float2 nm2 = make_float2(-m, -m);
+          float2 a0 = make_float2(0.0f, 0.0f), a1 = a0;
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            a[k & 3] += (k % kPolyEvery == kPolyEvery - 1) ? ex2_poly(fmaf(v[k], scale, nm)) : ex2(fmaf(v[k], scale, nm));
-          float mx[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) mx[q] = fmaxf(fmaxf(v[4 * q], v[4 * q + 1]), fmaxf(v[4 * q + 2], v[4 * q + 3]));
-          const float cm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale;
+          for (int k = 0; k < 32; k += 2) {
+            const float2 x = __ffma2_rn(make_float2(v[k], v[k + 1]), sc2, nm2);
+            const float2 e = ((kPolyPairs >> (k >> 1)) & 1u) ? ex2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+            if ((k >> 1) & 1) a1 = __fadd2_rn(a1, e);
+            else a0 = __fadd2_rn(a0, e);
+          }
+          const float cm = max32(v) * scale;
           mt = fmaxf(mt, cm);
           if (cm > m + kLag) {
-            a[0] = a[1] = a[2] = a[3] = 0.0f;
-            const float ncm = -cm;
+            a0 = a1 = make_float2(0.0f, 0.0f);
+            nm2 = make_float2(-cm, -cm);
 #pragma unroll
-            for (int k = 0; k < 32; ++k) a[k & 3] += ex2(fmaf(v[k], scale, ncm));
+            for (int k = 0; k < 32; k += 2) {
+              const float2 x = __ffma2_rn(make_float2(v[k], v[k + 1]), sc2, nm2);
+              const float2 e = make_float2(ex2(x.x), ex2(x.y));
+              if ((k >> 1) & 1) a1 = __fadd2_rn(a1, e);
+              else a0 = __fadd2_rn(a0, e);
+            }
             sum *= ex2(m - cm);
             m = cm;
           }
-          sum += (a[0] + a[1]) + (a[2] + a[3]);
+          sum += (a0.x + a1.x) + (a0.y + a1.y);
         } else {
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] = fmaf(v[k], scale, cb[k]);
@@ -586,12 +607,12 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
     if (p.nsplit > 1) {
       // column-split row block: publish this CTA's partials; the last CTA of the
       // block to arrive merges all of them and re-arms the counter
-      const size_t pn = static_cast<size_t>(p.B) * p.H * N;
-      const size_t o = bh * N + row;
+      // this CTA's partials: 3 x 128 floats at its grid index (blk * nsplit + sp)
+      float* mine = p.part + static_cast<size_t>(blockIdx.x) * 384;
       if (half == 0 && rin) {
-        p.part[(static_cast<size_t>(sp) * 3 + 0) * pn + o] = MODE == TL_MATVEC ? acc : m;
-        p.part[(static_cast<size_t>(sp) * 3 + 1) * pn + o] = sum;
-        p.part[(static_cast<size_t>(sp) * 3 + 2) * pn + o] = mt;
+        mine[lrow] = MODE == TL_MATVEC ? acc : m;
+        mine[128 + lrow] = sum;
+        mine[256 + lrow] = mt;
       }
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
@@ -613,9 +634,10 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
           mt = kNeg;
           acc = 0.0f;
           for (int q = 0; q < p.nsplit; ++q) {
-            const float a0 = __ldcg(p.part + (static_cast<size_t>(q) * 3 + 0) * pn + o);
-            const float a1 = __ldcg(p.part + (static_cast<size_t>(q) * 3 + 1) * pn + o);
-            const float a2 = __ldcg(p.part + (static_cast<size_t>(q) * 3 + 2) * pn + o);
+            const float* pq = p.part + (static_cast<size_t>(blk) * p.nsplit + q) * 384;
+            const float a0 = __ldcg(pq + lrow);
+            const float a1 = __ldcg(pq + 128 + lrow);
+            const float a2 = __ldcg(pq + 256 + lrow);
             if constexpr (MODE == TL_MATVEC) {
               acc += a0;
             } else {
@@ -651,12 +673,17 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
       }
     }
   }
-  if (MODE == TL_LSE && p.npeers > 0 && warp < kTEpi / 32) {
-    // every GPU's copy of this block's rows is written: raise every counter once
-    __threadfence_system();
+  if (MODE == TL_LSE && p.npeers > 0 && final_cta_of_block && warp < kTEpi / 32) {
+    // every GPU's copy of this block's rows is written (the epilogue threads'
+    // stores, ordered before thread 0's system-scope fence by the barrier;
+    // the fence is cumulative): raise every counter once.  Only the CTA that
+    // wrote the block's potentials fences; the other column splits wrote only
+    // local partials, already ordered for the merging CTA.
     asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory");
-    if (tid == 0 && final_cta_of_block)
+    if (tid == 0) {
+      __threadfence_system();
       for (int k = 0; k < p.npeers; ++k) atomicAdd_system(p.peer_cnt[k], 1ull);
+    }
   }
   if (err && p.status != nullptr) atomicOr(p.status, DFS_ERR_DEVICE_TIMEOUT);
   tc_fence_before();
@@ -770,14 +797,21 @@ cudaError_t compute_extents(const float* mask, int B, int N, int2* out, cudaStre
   return cudaGetLastError();
 }
 
+namespace {
+// CTAs whose partials the split scratch of a (B, H, N) problem holds: every row
+// block split kMaxSplit ways, capped at kSplitCtas
+size_t split_ctas(int B, int H, int N) {
+  const size_t all = static_cast<size_t>(B) * H * ((N + 127) / 128) * kMaxSplit;
+  return all < static_cast<size_t>(kSplitCtas) ? all : static_cast<size_t>(kSplitCtas);
+}
+}  // namespace
+
 size_t tile_split_bytes(int B, int H, int N) {
-  const size_t n = static_cast<size_t>(B) * H * N;
-  return sizeof(float) * kMaxSplit * 3 * n + sizeof(unsigned) * static_cast<size_t>(B) * H * ((N + 127) / 128);
+  return sizeof(float) * 384 * split_ctas(B, H, N) + sizeof(unsigned) * static_cast<size_t>(B) * H * ((N + 127) / 128);
 }
 
 cudaError_t tile_split_reset(float* split, int B, int H, int N, cudaStream_t st) {
-  const size_t n = static_cast<size_t>(B) * H * N;
-  return cudaMemsetAsync(split + static_cast<size_t>(kMaxSplit) * 3 * n, 0,
+  return cudaMemsetAsync(split + 384 * split_ctas(B, H, N), 0,
                          sizeof(unsigned) * static_cast<size_t>(B) * H * ((N + 127) / 128), st);
 }
 
@@ -822,11 +856,14 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
   p.wait_cnt = t.wait_cnt;
   p.wait_for = t.wait_for;
   p.extent = t.extent;
-  // Column splits.  A grid of fewer row blocks than one wave (two CTAs per SM)
-  // gets as many splits as fit in that wave.  A larger grid of long rows (16
-  // tiles or more) gets the split count, up to kMaxSplit, whose last wave wastes
-  // least: equal CTAs run in waves, so 1024 blocks on 296 slots take 4 waves for
-  // 3.46 waves of work, while 2 splits take 7 waves for 6.92.
+  // Column splits: a row block's column tiles shared by nsplit CTAs, which
+  // publish (reference, sum, max) partials that the block's last CTA merges.
+  // Equal CTAs run in waves of two per SM, so a launch of W waves of CTAs of
+  // T / ns tiles costs about W (T / ns + c0), c0 a CTA's fixed cost (set-up,
+  // pipeline fill, merge) in tile units: 1024 row blocks of 64 tiles take 7
+  // waves of 32 tiles with 2 splits instead of 4 of 64; 512 take 7 waves of 16
+  // with 4.  The split count minimising that estimate is taken, within the
+  // scratch's capacity; DFS_TILE_SPLITS (1-8) overrides it.
   p.nsplit = 1;
   if (t.split != nullptr) {
     int dev = 0, sms = 148;
@@ -834,23 +871,25 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
     const long slots = 2L * sms;
     const long blocks = static_cast<long>(t.B) * t.H * ((t.row_end - t.row_begin + 127) / 128);
     const int tiles = (t.N + kTCols - 1) / kTCols;
-    if (blocks < slots) {
-      const int fit = static_cast<int>(slots / (blocks > 0 ? blocks : 1));
-      p.nsplit = max(1, min(min(fit, kMaxSplit), tiles));
-    } else if (tiles >= 16) {
-      double best = 1e30;
-      for (int ns = 1; ns <= kMaxSplit; ++ns) {
-        const long waves = (blocks * ns + slots - 1) / slots;
-        const double cost = static_cast<double>(waves) / ns + (ns > 1 ? 0.02 : 0.0);  // + merge
-        if (cost < best - 1e-9) {
-          best = cost;
-          p.nsplit = ns;
-        }
+    const long cap = static_cast<long>(split_ctas(t.B, t.H, t.N));
+    const int max_ns = static_cast<int>(min(static_cast<long>(min(kMaxSplit, tiles)), blocks > 0 ? cap / blocks : 1));
+    constexpr double kC0 = 1.5;
+    double best = 1e30;
+    for (int ns = 1; ns <= max_ns; ++ns) {
+      const long waves = (blocks * ns + slots - 1) / slots;
+      const double cost = static_cast<double>(waves) * ((tiles + ns - 1) / ns + (ns > 1 ? kC0 : kC0 - 0.5));
+      if (cost < best - 1e-9) {
+        best = cost;
+        p.nsplit = ns;
       }
+    }
+    if (const char* ov = getenv("DFS_TILE_SPLITS")) {
+      const int want = atoi(ov);
+      if (want >= 1) p.nsplit = min(want, max(max_ns, 1));
     }
     if (p.nsplit > 1) {
       p.part = t.split;
-      p.counter = reinterpret_cast<unsigned*>(t.split + static_cast<size_t>(kMaxSplit) * 3 * t.B * t.H * t.N);
+      p.counter = reinterpret_cast<unsigned*>(t.split + 384 * cap);
     }
   }
   if (mode == TL_LSE) return launch_tile_m<TL_LSE>(t.dtype, t.d, p, st);

@@ -73,6 +73,44 @@ DFS_DEV float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// ex2_poly on two values at once with the packed fp32 pair instructions of
+// sm_100 (fma.rn.f32x2 / add.rn.f32x2: one issue slot for two lanes' worth of
+// FMA work): the same operations in the same order and rounding, so each
+// result is bit-identical to ex2_poly's.
+DFS_DEV float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);  // x - j, exact
+  float2 p = __ffma2_rn(make_float2(0.00132764445f, 0.00132764445f), f,
+                        make_float2(0.00967553724f, 0.00967553724f));
+  p = __ffma2_rn(p, f, make_float2(0.0555071346f, 0.0555071346f));
+  p = __ffma2_rn(p, f, make_float2(0.240221202f, 0.240221202f));
+  p = __ffma2_rn(p, f, make_float2(0.693146944f, 0.693146944f));
+  p = __ffma2_rn(p, f, make_float2(1.00000012f, 1.00000012f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+// max of three floats in one instruction (sm_100), NaN operands ignored as fmaxf does
+DFS_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// maximum of 32 values: 17 three- and two-input max instructions
+DFS_DEV float max32(const float (&v)[32]) {
+  float t[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) t[i] = fmax3(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+  t[10] = fmaxf(v[30], v[31]);
+  const float u0 = fmax3(t[0], t[1], t[2]), u1 = fmax3(t[3], t[4], t[5]), u2 = fmax3(t[6], t[7], t[8]);
+  const float u3 = fmaxf(t[9], t[10]);
+  return fmaxf(fmax3(u0, u1, u2), u3);
+}
+
 // 64-bit load with system-scope acquire (a counter raised by other GPUs).
 DFS_DEV unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;

@@ -23,7 +23,7 @@ INCLUDE_DIR = os.path.join(os.path.dirname(ROOT_DIR), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libdfsink.so")
 SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_stream.cu", "dfs_stream_bwd.cu", "dfs_stream_tma.cu",
-           "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu", "dfs_pad.cu"]
+           "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu", "dfs_pad.cu", "dfs_dense.cu"]
 HEADERS = ["dfs_device.cuh", "dfs_kernels.cuh", "dfs_slab.cuh", "dfs_tma.cuh"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

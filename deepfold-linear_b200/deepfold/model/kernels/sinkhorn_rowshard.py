@@ -271,15 +271,30 @@ class _Sharded:
         run(nat.DFS_OP_BWD_PT_T, r0, r1)
         g(slot(nat.DFS_WS_BWD_S))
         run(nat.DFS_OP_BWD_CGINIT)
+        # The stop flags are identical on every rank (same gathered vectors, same
+        # arithmetic), so all ranks leave the loop after the same iteration.  The
+        # host reads them one iteration late: iteration k is queued before the
+        # flags of k - 1 are tested, so the GPU never idles on that read; the one
+        # extra iteration after convergence skips every converged problem (its
+        # plan products and CG step return at once).
+        stream = torch.cuda.current_stream(dev)
+        flag_bufs = [torch.empty(P, dtype=torch.int32).pin_memory() for _ in range(2)]
+        pending = None
         for it in range(int(self.cg["max_iter"]) + 1):
             run(nat.DFS_OP_BWD_P_U, r0, r1)
             g(slot(nat.DFS_WS_BWD_T))
             run(nat.DFS_OP_BWD_PT_T, r0, r1)
             g(slot(nat.DFS_WS_BWD_S))
             run(nat.DFS_OP_BWD_CGSTEP_FIRST if it == 0 else nat.DFS_OP_BWD_CGSTEP)
-            # identical on every rank (same gathered vectors, same arithmetic): all ranks stop together
-            if bool((done != 0).all()):
-                break
+            buf = flag_bufs[it & 1]
+            buf.copy_(done, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            prev, pending = pending, (ev, buf)
+            if prev is not None:
+                prev[0].synchronize()
+                if bool((prev[1] != 0).all()):
+                    break
         run(nat.DFS_OP_BWD_P_X, r0, r1)
         g(slot(nat.DFS_WS_BWD_S))
         run(nat.DFS_OP_BWD_FINAL)

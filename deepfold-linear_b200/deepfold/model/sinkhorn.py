@@ -14,11 +14,15 @@ Sinkhorn loop never leaves the GPU:
 * ``compute_transport_output``: row-normalised plan T_norm (materialised, as the
   reference returns it), gated output and optional centroid.
 
+Problems of N <= 384 with V head dims up to 32 keep C on chip for the whole
+loop (the cluster-resident kernel); all others -- N up to 65536, V head dims up
+to 128 -- stream C from HBM once per half-iteration (csrc/dfs_dense.cu): the
+cost is the input here, so those passes are bound by HBM bandwidth.
+
 The backward of these two entry points is not provided (the reference differentiates
 them with autograd through K dense iterations); use ``flash_sinkhorn`` for
 gradients.  CPU tensors (as the reference's tests pass them) are computed on the
-current CUDA device and the results returned on the CPU.  Head dims of V up to
-32 run (zero-padded inside the library), N up to 384.
+current CUDA device and the results returned on the CPU.
 """
 
 from __future__ import annotations
@@ -28,6 +32,9 @@ import torch
 from deepfold import _native as nat
 
 __all__ = ["sinkhorn_solve", "compute_transport_output"]
+
+DENSE_MAX_N = 1 << 16  # sequence length the dense-cost kernels accept
+DENSE_MAX_D = 128      # head dim of V in compute_transport_output
 
 
 def _on_gpu(fn):
@@ -52,8 +59,8 @@ def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshol
                 mask, V=None, x_res=None, want_T=False):
     dev = nat.require_cuda(C)
     B, H, N, _ = C.shape
-    if N > nat.max_n(32):
-        raise ValueError(f"N={N} exceeds the resident kernels' range ({nat.max_n(32)})")
+    if N > DENSE_MAX_N:
+        raise ValueError(f"N={N} exceeds the dense-cost kernels' range ({DENSE_MAX_N})")
     if C.requires_grad or (V is not None and V.requires_grad):
         raise NotImplementedError("gradients through the dense-cost entry points are not provided; "
                                   "use flash_sinkhorn")
@@ -65,8 +72,8 @@ def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshol
     Vp = None
     if V is not None:
         d = V.shape[-1]
-        if d > 32:
-            raise ValueError("compute_transport_output supports head dims up to 32")
+        if d > DENSE_MAX_D:
+            raise ValueError(f"compute_transport_output supports head dims up to {DENSE_MAX_D}")
         Vp = f32(V)
     lu = torch.empty(B, H, N, device=dev, dtype=torch.float32)
     lv = torch.empty(B, H, N, device=dev, dtype=torch.float32)

@@ -251,12 +251,12 @@ int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const d
 
 /* Size of the library's fixed device scratch used by dfs_fwd_static: 16 MiB.
  * dfs_workspace_size's fwd_bytes is the authority on what a problem needs: the
- * streamed forward takes 64 + 12 d bytes per (batch, head, point) -- potentials
+ * streamed forward takes 112 + 12 d bytes per (batch, head, point) -- potentials
  * and row statistics, fp32 operand copies, the column-split partials -- plus
  * 4 bytes per block of 128 rows and under 1 KB fixed, i.e. B*H*N up to about
- * 20,000 points at d = 64 or 37,000 at d = 32; head dims other than 32 and 64
+ * 19,000 points at d = 64 or 33,000 at d = 32; head dims other than 32 and 64
  * add their zero-padded copies.  Cluster-resident problems (N <= 384, d = 32)
- * need none. */
+ * need none; dense-cost problems need 12 bytes per (batch, head). */
 #define DFS_STATIC_SCRATCH_BYTES (16u << 20)
 
 /* Forward for callers that cannot allocate device memory.  No counterpart in

@@ -63,13 +63,25 @@ def test_host_side_validation(lib):
     fb, bb = ctypes.c_size_t(0), ctypes.c_size_t(0)
     assert lib.dfs_workspace_size(big, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
     # f, g, m, R (fp32, N each), fp32 copies of Q, K and V^T (N x d each), column-split
-    # partials (4 splits x 3 values x N fp32) and counters (one per 128-row block), alignment slack,
-    # the peer-exchange arrival counter's slot and one (lo, hi) valid extent per batch element
-    assert fb.value == 4 * 4 * 4096 + 3 * 4 * 4096 * 32 + 4 * 3 * 4 * 4096 + 4 * (4096 // 128) + 2 * 256 + 128 + 8
+    # partials (3 x 128 fp32 for each CTA of up to 8 splits per 128-row block) and counters (one per
+    # 128-row block), alignment slack, the peer-exchange arrival counter's slot and one (lo, hi)
+    # valid extent per batch element
+    splits = 8 * (4096 // 128) * 3 * 128 * 4
+    assert fb.value == 4 * 4 * 4096 + 3 * 4 * 4096 * 32 + splits + 4 * (4096 // 128) + 2 * 256 + 128 + 8
     huge = nat.make_problem(1, 1, 1 << 17, 32, __import__("torch").bfloat16, 20, 1.0, 10.0)
     assert lib.dfs_fwd(huge, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
     wide_d = nat.make_problem(1, 1, 128, 96, __import__("torch").bfloat16, 20, 1.0, 10.0)
     assert lib.dfs_fwd(wide_d, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
+    # a dense cost beyond the resident range streams C: a small per-problem workspace,
+    # V head dims up to 128 (fp32), no backward
+    dense = nat.make_problem(2, 3, 1000, 128, __import__("torch").float32, 5, 1.0, 10.0,
+                             cost_mode=nat.DFS_COST_DENSE)
+    assert lib.dfs_workspace_size(dense, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
+    assert fb.value == 256 and bb.value == 0
+    fake_dense = nat.DfsFwdArgs(C=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16)
+    assert lib.dfs_fwd(dense, fake_dense, None, 0, None) == nat.DFS_ERR_WORKSPACE
+    wider = nat.make_problem(1, 1, 1000, 129, __import__("torch").float32, 5, 1.0, 10.0, cost_mode=nat.DFS_COST_DENSE)
+    assert lib.dfs_fwd(wider, fake_dense, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
     # a padded head dim needs its zero-padded copies even on the resident path:
     # Q, K, V (bf16) and O (fp32) at d = 32, each region rounded up to 256 bytes
     odd_d = nat.make_problem(2, 4, 16, 8, __import__("torch").bfloat16, 3, 1.0, 10.0)

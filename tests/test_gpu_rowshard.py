@@ -54,7 +54,10 @@ def test_two_gpu_row_sharded_matches_single_gpu():
 def test_bh_blocks_on_streams_match_full_batch():
     """The (batch, head) share of every rank of a 3-GPU partition, run here one
     after another (sorted batch, blocks on a stream pool), gives the outputs
-    and gradients of one full-batch call."""
+    and gradients of one full-batch call.  The grids differ (a smaller batch
+    gets more column splits per row block), so each row's sums are added in
+    another order: agreement to rounding, 1e-4 after 20 iterations at eps 0.5,
+    and to one bf16 unit for the bf16 gradients."""
     from deepfold.model.kernels.sinkhorn_bhshard import bh_sharded_flash_sinkhorn
 
     lengths = [600, 200, 520]
@@ -72,11 +75,14 @@ def test_bh_blocks_on_streams_match_full_batch():
         for s0, s1, h0, h1, Oc, luc, lvc in res:
             for k, sp in enumerate(range(s0, s1)):
                 b = order[sp]
-                assert float((Oc[k] - O[b, h0:h1]).detach().abs().max()) <= 1e-5
-                assert float((luc[k] - lu[b, h0:h1]).abs().max()) <= 1e-5
+                assert float((Oc[k] - O[b, h0:h1]).detach().abs().max()) <= 1e-4
+                assert float((luc[k] - lu[b, h0:h1]).abs().max()) <= 1e-4
                 outs.append(Oc[k])
                 gos.append(inp["dO"][b, h0:h1])
     got_g = torch.autograd.grad(outs, leaves2, grad_outputs=gos)
     torch.cuda.synchronize()
     for a, b in zip(ref_g, got_g):
-        assert float((a - b).abs().max()) <= 1e-5
+        # the gradients come back in the leaves' dtype (bf16): nearly equal fp32
+        # values may round to neighbouring bf16 values, one unit in the last place
+        a, b = a.float(), b.float()
+        assert bool(((a - b).abs() <= 1e-4 + a.abs() * 2.0 ** -8).all())
