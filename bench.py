@@ -60,6 +60,17 @@ CFG = dict(B=2, H=8, N=384, d=32, eps=1.0, K_iter=20, cg_rtol=1e-6, cg_max_iter=
 L2_FLUSH_BYTES = 256 << 20       # > 126 MB L2: written between timed steps
 
 
+def quiet_gc():
+    """Collect once and move every object alive now out of the collector's view
+    (gc.freeze): a full cyclic collection over the interpreter's heap (torch's
+    objects included) pauses the host for tens of milliseconds, and on several
+    GPUs the other ranks wait for the paused one inside the next collective.
+    Called after set-up and warm-up, before any timed region."""
+    import gc
+    gc.collect()
+    gc.freeze()
+
+
 def workload_name():
     c = CFG
     return (f"config2: flash-Sinkhorn fwd+IFT-bwd B={c['B']} H={c['H']} N={c['N']} d={c['d']} bf16 "
@@ -304,16 +315,17 @@ def run_ours(args):
         e2.record(stream)
         return e0, e1, e2
 
+    # the clock sampler starts before the warm-up (nvidia-smi's start-up stays out of the timed steps)
+    sampler = ClockSampler(dev) if rank == 0 else None
+    if sampler:
+        sampler.start()
     for _ in range(args.warmup):
         step_resident()
         step_kernels()
     torch.cuda.synchronize()
+    quiet_gc()
 
     # ---- timed region: value (inputs resident in HBM, L2 flushed between steps)
-    sampler = ClockSampler(dev) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -478,6 +490,7 @@ def config4_single_gpu(dev, steps=5, warmup=3):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    quiet_gc()
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -560,13 +573,15 @@ def run_big(args):
                 for g in grads for s0, s1, h0, h1, *_ in res]
 
     dev_in = {k: v.to(dev) for k, v in host.items()}
-    for _ in range(args.warmup):
-        step(dev_in)
-    torch.cuda.synchronize()
+    # the clock sampler starts before the warm-up: nvidia-smi's start-up queries
+    # every GPU of the host, which must not fall into the timed steps
     sampler = ClockSampler(dev) if rank == 0 else None
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+    for _ in range(args.warmup):
+        step(dev_in)
+    torch.cuda.synchronize()
+    quiet_gc()
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
