@@ -858,12 +858,12 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
   p.extent = t.extent;
   // Column splits: a row block's column tiles shared by nsplit CTAs, which
   // publish (reference, sum, max) partials that the block's last CTA merges.
-  // Equal CTAs run in waves of two per SM, so a launch of W waves of CTAs of
-  // T / ns tiles costs about W (T / ns + c0), c0 a CTA's fixed cost (set-up,
-  // pipeline fill, merge) in tile units: 1024 row blocks of 64 tiles take 7
-  // waves of 32 tiles with 2 splits instead of 4 of 64; 512 take 7 waves of 16
-  // with 4.  The split count minimising that estimate is taken, within the
-  // scratch's capacity; DFS_TILE_SPLITS (1-8) overrides it.
+  // The count aims at about 3.5 waves of CTAs (two per SM) while each CTA keeps
+  // enough tiles to amortise its set-up and the merge (16 of long rows, 4 of
+  // short ones).  Measured on the N = 8192 half-update (B = 1, H = 16) over the
+  // row ranges of 1/2/4/8 GPUs, the best counts were 1, 2, 4 and 2-4 (1024, 512,
+  // 256 and 128 row blocks); this rule picks 1, 2, 4, 4.  DFS_TILE_SPLITS (1-8)
+  // overrides it, within the scratch's capacity.
   p.nsplit = 1;
   if (t.split != nullptr) {
     int dev = 0, sms = 148;
@@ -872,20 +872,15 @@ cudaError_t launch_tile_pass(int mode, const TileArgs& t, cudaStream_t st) {
     const long blocks = static_cast<long>(t.B) * t.H * ((t.row_end - t.row_begin + 127) / 128);
     const int tiles = (t.N + kTCols - 1) / kTCols;
     const long cap = static_cast<long>(split_ctas(t.B, t.H, t.N));
-    const int max_ns = static_cast<int>(min(static_cast<long>(min(kMaxSplit, tiles)), blocks > 0 ? cap / blocks : 1));
-    constexpr double kC0 = 1.5;
-    double best = 1e30;
-    for (int ns = 1; ns <= max_ns; ++ns) {
-      const long waves = (blocks * ns + slots - 1) / slots;
-      const double cost = static_cast<double>(waves) * ((tiles + ns - 1) / ns + (ns > 1 ? kC0 : kC0 - 0.5));
-      if (cost < best - 1e-9) {
-        best = cost;
-        p.nsplit = ns;
-      }
-    }
+    const int min_tiles = tiles >= 32 ? 16 : 4;
+    const int max_ns = static_cast<int>(min(static_cast<long>(max(1, min(kMaxSplit, tiles / min_tiles))),
+                                            blocks > 0 ? max(1L, cap / blocks) : 1L));
+    const long want = blocks > 0 ? (7 * slots) / (2 * blocks) : 1;
+    p.nsplit = static_cast<int>(max(1L, min(want, static_cast<long>(max_ns))));
     if (const char* ov = getenv("DFS_TILE_SPLITS")) {
-      const int want = atoi(ov);
-      if (want >= 1) p.nsplit = min(want, max(max_ns, 1));
+      const int n = atoi(ov);
+      const long fit = blocks > 0 ? cap / blocks : 1;
+      if (n >= 1) p.nsplit = static_cast<int>(max(1L, min(static_cast<long>(min(n, min(kMaxSplit, tiles))), fit)));
     }
     if (p.nsplit > 1) {
       p.part = t.split;

@@ -24,12 +24,15 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     rank = dist.get_rank()
     dev = torch.device("cuda", local)
-    B, H, N, d = 1, 4, int(os.environ.get("RS_N", "1000")), 64
+    # B = 1 splits the forward's interleaved problem groups by head, B = 2 by batch element
+    B, H, N, d = int(os.environ.get("RS_B", "1")), 4, int(os.environ.get("RS_N", "1000")), 64
     g = torch.Generator().manual_seed(5)
     Q, K, V = (torch.randn(B, H, N, d, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
     dO = torch.randn(B, H, N, d, generator=g).to(dev)
     mask = torch.ones(B, N)
     mask[0, N - 37:] = 0.0
+    if B > 1:
+        mask[1, N // 2:] = 0.0
     mask = mask.to(dev)
     lm = torch.where(mask > 0, -torch.log(mask.sum(-1, keepdim=True)), torch.full_like(mask, -1e9))
     lm = lm[:, None, :].expand(B, H, N).contiguous()

@@ -43,10 +43,12 @@ def test_phase_api_on_one_gpu_reproduces_streamed_path():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_row_sharded_matches_single_gpu():
+@pytest.mark.parametrize("batch", [1, 2])
+def test_two_gpu_row_sharded_matches_single_gpu(batch):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29531", os.path.join(ROOT, "tests", "rowshard_worker.py")]
-    env = dict(os.environ, RS_N="1000", NCCL_NVLS_ENABLE="0")
+           "--master-addr", "127.0.0.1", "--master-port", str(29531 + batch),
+           os.path.join(ROOT, "tests", "rowshard_worker.py")]
+    env = dict(os.environ, RS_N="1000", RS_B=str(batch), NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
