@@ -15,7 +15,7 @@ through NVLink peer stores each half-iteration (strong scaling: one call is the
 whole configuration's forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
-                    [--config 2|3|4|transport]
+                    [--config 2|3|4|transport|dense]
 
 ``--config 3`` (B=8 H=16 padded N=1024 d=64, variable lengths, softmax
 marginals, eps 0.5, 50 iterations) spreads the (batch, head) problems over the
@@ -24,6 +24,10 @@ ranks with a length^2-balanced partition (no data-path collective).
 ``--config transport`` times the trunk block's balanced transport
 (balanced_sinkhorn_transport, fwd+bwd) at the shapes the reference publishes
 timings for (B=1 H=16 d_h=32 K=20, N = 64 ... 768) and prints them beside those.
+
+``--config dense`` times the dense-cost entry points beyond the resident range
+(sinkhorn_solve + compute_transport_output on a given 1 GiB fp32 cost, B=1 H=16
+N=4096) against the measured HBM bandwidth.
 
 ``--impl reference`` times the reference's own CPU path -- dense cost, its
 ``sinkhorn_solve`` and ``compute_transport_output``, torch autograd -- from the
@@ -983,6 +987,66 @@ def run_transport(args):
     print(json.dumps(line), flush=True)
 
 
+DENSE = dict(B=1, H=16, N=4096, d=64, eps=1.0, K_iter=20)
+
+
+def run_dense(args):
+    """The dense-cost entry points beyond the resident range: sinkhorn_solve +
+    compute_transport_output on a given fp32 cost C (B=1 H=16 N=4096: 1 GiB),
+    V head dim 64, K=20, uniform marginals, balanced.  Each half-update streams
+    C once (4 bytes per pair), the transport pass twice and writes T_norm; the
+    roofline is those bytes at the measured HBM bandwidth.  Forward only (the
+    dense entry points have no gradients)."""
+    from deepfold.model.sinkhorn import compute_transport_output, sinkhorn_solve
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = DENSE
+    B, H, N, d = c["B"], c["H"], c["N"], c["d"]
+    g = torch.Generator().manual_seed(0)
+    C = torch.rand(B, H, N, N, generator=g).to(dev)
+    lm = torch.full((B, H, N), -math.log(N), device=dev)
+    eps = torch.full((H,), c["eps"], device=dev)
+    V = torch.randn(B, H, N, d, generator=g).to(dev)
+    G = torch.zeros(B, H, N, d, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        lu, lv = sinkhorn_solve(C, lm, lm, eps, lam=float("inf"), K=c["K_iter"])
+        return compute_transport_output(V, G, lu, lv, C, eps)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    quiet_gc()
+    sampler = ClockSampler(dev)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop()
+    pairs = B * H * N * N
+    # bytes per call: 2K half-updates reading C, the transport pass reading C twice and writing T_norm
+    nbytes = (2 * c["K_iter"] + 3) * 4 * pairs
+    _, peak, peak_src = load_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {"metric": "dense-cost sinkhorn_solve + compute_transport_output calls/s", "value": round(1e3 / ms, 4),
+            "unit": "calls/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32",
+            "data": f"synthetic (uniform C in [0,1), N(0,1) V; B={B} H={H} N={N} d={d})",
+            "config": {"workload": f"dense sinkhorn_solve K={c['K_iter']} + compute_transport_output, B={B} H={H} "
+                                   f"N={N} d={d}, balanced", "l2": "C (1 GiB) exceeds L2"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "peak_source": peak_src,
+                         "unit": "GB/s", "frac": round(gbs / peak, 4), "bytes_per_call": nbytes},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -993,7 +1057,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config4", action="store_true", help="skip the single-GPU long-sequence point")
-    ap.add_argument("--config", choices=["2", "3", "4", "transport"], default=None,
+    ap.add_argument("--config", choices=["2", "3", "4", "transport", "dense"], default=None,
                     help="default: 2 on one GPU, 4 (long-sequence row shards) on several; 'transport': the "
                          "balanced transport at the reference's published shapes (one GPU)")
     args = ap.parse_args()
@@ -1007,6 +1071,12 @@ def main():
         if args.warmup < 3:
             args.warmup = 3
         run_transport(args)
+        return
+    if args.config == "dense":
+        if args.impl != "ours":
+            print(json.dumps({"impl": "reference", "unavailable": "the dense mode times this build only"}))
+            return
+        run_dense(args)
         return
     if args.config is not None:
         args.config = int(args.config)

@@ -275,7 +275,7 @@ int dfs_max_n(int d) { return kernel_head_dim(d) != 0 ? kStreamMaxN : 0; }
 int dfs_workspace_size(const dfs_problem* p, size_t* fwd_bytes, size_t* bwd_bytes) {
   if (!dims_ok(p)) return DFS_ERR_INVALID_ARGUMENT;
   if (dense_streamed(p)) {
-    if (fwd_bytes) *fwd_bytes = dense_fwd_workspace(p->B, p->H);
+    if (fwd_bytes) *fwd_bytes = dense_fwd_workspace(p->B, p->H, p->N);
     if (bwd_bytes) *bwd_bytes = 0;  // no backward on the dense-cost path
     return DFS_OK;
   }
@@ -295,7 +295,7 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   if (rc != DFS_OK) return rc;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dense_streamed(p)) {
-    if (workspace == nullptr || workspace_bytes < dense_fwd_workspace(p->B, p->H) || !aligned16(workspace))
+    if (workspace == nullptr || workspace_bytes < dense_fwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
       return DFS_ERR_WORKSPACE;
     return cuda_status(launch_dense_fwd(fwd_params(p, a), workspace, st));
   }

@@ -14,10 +14,12 @@
 //   transport      one warp per row, 8 rows per CTA: pass 1 the row's max and
 //                  sum, pass 2 T_norm_ij per column, O_i += T_norm_ij V_j with
 //                  the CTA's V tile staged in shared memory, x_centroid.
-// The arithmetic follows the reference's: log K = -C / eps (an IEEE division),
-// masks as additive -1e9 biases, kappa = lam / (lam + eps) (1 for lam = inf),
-// T = exp(score - rowmax), T_norm = T / (sum T + 1e-6), padded rows of T_norm
-// and padded potentials zeroed.
+// The arithmetic follows the reference's formulas -- log K = -C / eps, masks as
+// additive -1e9 biases, kappa = lam / (lam + eps) (1 for lam = inf), T =
+// exp(score - rowmax), T_norm = T / (sum T + 1e-6), padded rows of T_norm and
+// padded potentials zeroed -- in log2 units with ex2 on the MUFU (below), so
+// that a pass costs about one FMA and one exponential per element and is bound
+// by HBM, not by the arithmetic.
 //
 // Early stopping (threshold > 0): on every check_every-th iteration the passes
 // record each problem's largest |change| of log_u and log_v; a one-CTA kernel
@@ -42,6 +44,8 @@ struct DenseArgs {
   float* lv;            // log_v
   unsigned* diff;       // (2, BH) largest |change| as float bits (check iterations)
   int* done;            // (BH) converged problems
+  float* rmax;          // transport row statistics (B,H,N): exact maximum of the score, log2 units
+  float* rsum;          // and the sum of exp2(score - maximum)
   int B, H, N;
   float lam;
   int check;            // this pass records |change|
@@ -53,21 +57,41 @@ __device__ __forceinline__ float bias_of(const float* mask, int b, int N, int j)
   return mask == nullptr ? 0.0f : (1.0f - mask[static_cast<size_t>(b) * N + j]) * kMaskBias;
 }
 
-// online log-sum-exp state: running max m and sum s of exp(x - m)
-__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
-  if (x > m) {
-    s = s * expf(m - x) + 1.0f;  // m = -inf first: exp(-inf) = 0
-    m = x;
-  } else if (x > -INFINITY) {  // (-inf, -inf): nothing to add
-    s += expf(x - m);
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The passes work in log2 units: x = (-C / eps + potential + bias) log2(e) is one
+// FMA per element, c * (-log2(e) / eps) + (potential + bias) log2(e), and each
+// exponential one ex2 on the MUFU.  The running reference m lags the maximum by
+// up to kLag: a group of four elements moves it only when its own maximum
+// exceeds m + kLag, so the sum of exp2(x - m) stays within [1, N 2^kLag] and the
+// common case has no branch.  The result is ln(sum exp(...)) = (m + log2 s) ln 2.
+constexpr float kLag = 16.0f;  // (kLog2e, kLn2: dfs_device.cuh)
+
+__device__ __forceinline__ void lse_push4(float& m, float& s, float x0, float x1, float x2, float x3) {
+  const float mx = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
+  if (mx > m + kLag) {  // the first group with a finite value, and rarely any other
+    s *= ex2f(m - mx);  // m = -inf first: exp2(-inf) = 0
+    m = mx;
   }
+  if (m > -INFINITY) s += (ex2f(x0 - m) + ex2f(x1 - m)) + (ex2f(x2 - m) + ex2f(x3 - m));
+}
+__device__ __forceinline__ void lse_push1(float& m, float& s, float x) {
+  if (x > m + kLag) {
+    s *= ex2f(m - x);
+    m = x;
+  }
+  if (m > -INFINITY) s += ex2f(x - m);
 }
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
   if (m2 > m) {
-    s = s * expf(m - m2) + s2;
+    s = s * ex2f(m - m2) + s2;
     m = m2;
   } else if (m2 > -INFINITY) {
-    s += s2 * expf(m2 - m);
+    s += s2 * ex2f(m2 - m);
   }
 }
 
@@ -76,8 +100,13 @@ __device__ __forceinline__ void record_change(unsigned* slot, float a) {
   atomicMax(slot, __float_as_uint(a));
 }
 
-// f_i = kappa (log_mu_i - LSE_j(-C_ij / eps + g_j + colbias_j)), one warp per row
-template <bool VEC>
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// f_i = kappa (log_mu_i - LSE_j(-C_ij / eps + g_j + colbias_j)), one warp per row.
+// STAT: the transport's row statistics instead, on the score f_i - C_ij / eps +
+// g_j + colbias_j (log2 units): its exact maximum into a.rmax and the sum of
+// exp2(score - maximum) into a.rsum.
+template <bool VEC, bool STAT>
 __global__ void __launch_bounds__(kDenseThreads) dense_row_kernel(const DenseArgs a) {
   const int lane = threadIdx.x & 31;
   const size_t rows = static_cast<size_t>(a.B) * a.H * a.N;
@@ -89,29 +118,66 @@ __global__ void __launch_bounds__(kDenseThreads) dense_row_kernel(const DenseArg
     if (a.done != nullptr && a.done[prob]) continue;  // uniform over the warp
     const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
     const float eps = a.eps[h];
+    const float sc = -kLog2e / eps;
     const float* c = a.C + r * N;
     const float* g = a.lv + prob * N;
-    float m = -INFINITY, s = 0.0f;
+    const float* mk = a.mask == nullptr ? nullptr : a.mask + static_cast<size_t>(b) * N;
+    const float ui = STAT ? a.lu[r] : 0.0f;
+    float m = -INFINITY, s = 0.0f, mt = -INFINITY;
     if constexpr (VEC) {
-      for (int j = 4 * lane; j < N; j += 128) {
-        const float4 cv = __ldcs(reinterpret_cast<const float4*>(c + j));
-        const float4 gv = *reinterpret_cast<const float4*>(g + j);
-        lse_push(m, s, -cv.x / eps + gv.x + bias_of(a.mask, b, N, j));
-        lse_push(m, s, -cv.y / eps + gv.y + bias_of(a.mask, b, N, j + 1));
-        lse_push(m, s, -cv.z / eps + gv.z + bias_of(a.mask, b, N, j + 2));
-        lse_push(m, s, -cv.w / eps + gv.w + bias_of(a.mask, b, N, j + 3));
+      // four 16-byte loads of C in flight per lane before any is consumed
+      auto group = [&](const float4& cv, int j) {
+        float4 t = ld4(g + j);
+        if constexpr (STAT) {
+          t.x += ui;
+          t.y += ui;
+          t.z += ui;
+          t.w += ui;
+        }
+        if (mk != nullptr) {
+          const float4 mv = ld4(mk + j);
+          t.x += (1.0f - mv.x) * kMaskBias;
+          t.y += (1.0f - mv.y) * kMaskBias;
+          t.z += (1.0f - mv.z) * kMaskBias;
+          t.w += (1.0f - mv.w) * kMaskBias;
+        }
+        const float x0 = fmaf(cv.x, sc, t.x * kLog2e), x1 = fmaf(cv.y, sc, t.y * kLog2e),
+                    x2 = fmaf(cv.z, sc, t.z * kLog2e), x3 = fmaf(cv.w, sc, t.w * kLog2e);
+        if constexpr (STAT) mt = fmaxf(mt, fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+        lse_push4(m, s, x0, x1, x2, x3);
+      };
+      int j = 4 * lane;
+      for (; j + 384 < N; j += 512) {
+        float4 cv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) cv[u] = __ldcs(reinterpret_cast<const float4*>(c + j + 128 * u));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) group(cv[u], j + 128 * u);
       }
+      for (; j < N; j += 128) group(__ldcs(reinterpret_cast<const float4*>(c + j)), j);
     } else {
-      for (int j = lane; j < N; j += 32) lse_push(m, s, -__ldcs(c + j) / eps + g[j] + bias_of(a.mask, b, N, j));
+      for (int j = lane; j < N; j += 32) {
+        const float x = fmaf(__ldcs(c + j), sc, (ui + g[j] + bias_of(a.mask, b, N, j)) * kLog2e);
+        if constexpr (STAT) mt = fmaxf(mt, x);
+        lse_push1(m, s, x);
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
       lse_merge(m, s, m2, s2);
+      if constexpr (STAT) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+    }
+    if constexpr (STAT) {
+      if (lane == 0) {
+        a.rmax[r] = mt;
+        a.rsum[r] = mt > -INFINITY ? s * ex2f(m - mt) : 0.0f;
+      }
+      continue;
     }
     if (lane == 0) {
       const size_t i = r;
-      const float f = kappa_of(a.lam, eps) * (a.mu[i] - (m + logf(s)));
+      const float f = kappa_of(a.lam, eps) * (a.mu[i] - (m + __log2f(s)) * kLn2);
       if (a.check) record_change(a.diff + prob, fabsf(f - a.lu[i]));
       a.lu[i] = f;
     }
@@ -132,6 +198,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_col_kernel(const DenseArg
   if (a.done != nullptr && a.done[prob]) return;  // uniform over the CTA
   const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
   const float eps = a.eps[h];
+  const float sc = -kLog2e / eps;
   const float* f = a.lu + prob * N;
   float m[PER], s[PER];
 #pragma unroll
@@ -140,20 +207,43 @@ __global__ void __launch_bounds__(kDenseThreads) dense_col_kernel(const DenseArg
     s[q] = 0.0f;
   }
   const int j = j0 + PER * lane;
-  for (int i = warp; i < N; i += 8) {
-    const float* c = a.C + (prob * N + i) * N;
-    const float fi = f[i] + bias_of(a.mask, b, N, i);
-    if constexpr (VEC) {
-      if (j < N) {
-        const float4 cv = __ldcs(reinterpret_cast<const float4*>(c + j));
-        lse_push(m[0], s[0], -cv.x / eps + fi);
-        lse_push(m[1], s[1], -cv.y / eps + fi);
-        lse_push(m[2], s[2], -cv.z / eps + fi);
-        lse_push(m[3], s[3], -cv.w / eps + fi);
+  if (j < N) {
+    const float* cb = a.C + prob * N * static_cast<size_t>(N) + j;
+    auto row = [&](int i, const float4& cv) {
+      const float ti = (f[i] + bias_of(a.mask, b, N, i)) * kLog2e;
+      lse_push1(m[0], s[0], fmaf(cv.x, sc, ti));
+      if constexpr (VEC) {
+        lse_push1(m[1], s[1], fmaf(cv.y, sc, ti));
+        lse_push1(m[2], s[2], fmaf(cv.z, sc, ti));
+        lse_push1(m[3], s[3], fmaf(cv.w, sc, ti));
       }
-    } else {
-      if (j < N) lse_push(m[0], s[0], -__ldcs(c + j) / eps + fi);
+    };
+    auto load = [&](int i) {
+      if constexpr (VEC) return __ldcs(reinterpret_cast<const float4*>(cb + static_cast<size_t>(i) * N));
+      else return make_float4(__ldcs(cb + static_cast<size_t>(i) * N), 0.0f, 0.0f, 0.0f);
+    };
+    // rows warp, warp + 8, ...: four loads in flight per thread before any is
+    // consumed, and each column's four new values pushed as one group
+    int i = warp;
+    for (; i + 24 < N; i += 32) {
+      float4 cv[4];
+      float ti[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) cv[u] = load(i + 8 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ti[u] = (f[i + 8 * u] + bias_of(a.mask, b, N, i + 8 * u)) * kLog2e;
+      lse_push4(m[0], s[0], fmaf(cv[0].x, sc, ti[0]), fmaf(cv[1].x, sc, ti[1]), fmaf(cv[2].x, sc, ti[2]),
+                fmaf(cv[3].x, sc, ti[3]));
+      if constexpr (VEC) {
+        lse_push4(m[1], s[1], fmaf(cv[0].y, sc, ti[0]), fmaf(cv[1].y, sc, ti[1]), fmaf(cv[2].y, sc, ti[2]),
+                  fmaf(cv[3].y, sc, ti[3]));
+        lse_push4(m[2], s[2], fmaf(cv[0].z, sc, ti[0]), fmaf(cv[1].z, sc, ti[1]), fmaf(cv[2].z, sc, ti[2]),
+                  fmaf(cv[3].z, sc, ti[3]));
+        lse_push4(m[3], s[3], fmaf(cv[0].w, sc, ti[0]), fmaf(cv[1].w, sc, ti[1]), fmaf(cv[2].w, sc, ti[2]),
+                  fmaf(cv[3].w, sc, ti[3]));
+      }
     }
+    for (; i < N; i += 8) row(i, load(i));
   }
 #pragma unroll
   for (int q = 0; q < PER; ++q) {
@@ -167,7 +257,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_col_kernel(const DenseArg
     float mm = sm[0][t], sv = ss[0][t];
     for (int w = 1; w < 8; ++w) lse_merge(mm, sv, sm[w][t], ss[w][t]);
     const size_t o = prob * N + jj;
-    const float g = kappa_of(a.lam, eps) * (a.nu[o] - (mm + logf(sv)));
+    const float g = kappa_of(a.lam, eps) * (a.nu[o] - (mm + __log2f(sv)) * kLn2);
     if (a.check) record_change(a.diff + static_cast<size_t>(a.B) * a.H + prob, fabsf(g - a.lv[o]));
     a.lv[o] = g;
   }
@@ -219,13 +309,17 @@ __global__ void dense_finish_kernel(const float* mask, float* lu, float* lv, int
 
 namespace {
 
-// compute_transport_output (sinkhorn.py:152-195) on a dense cost: one warp per
-// row, 8 rows per CTA.  score_ij = log_u_i + (-C_ij / eps) + log_v_j + colbias_j;
-// pass 1: the row's max m and sum s of exp(score - m); pass 2 per tile of 32
-// columns: T_norm_ij = exp(score_ij - m) / (s + 1e-6) (0 on a padded row),
-// written when asked for, O_i += T_norm_ij V_j (the tile of V staged in shared
-// memory once per CTA, lane k accumulating dims k, k + 32, ...), centroid
-// sum_j T_norm_ij x_j.  DV = ceil(d / 32) accumulators per lane.
+// compute_transport_output (sinkhorn.py:152-195) on a dense cost, after the
+// row statistics (dense_row_kernel<., true>: each row's exact score maximum mt
+// and sum of exp2(score - mt)).  A CTA takes 128 rows of one problem and walks
+// the columns in chunks of 64.  Per chunk: T_norm_ij = exp2(score_ij - mt_i) /
+// (sum_i + 1e-6) (0 on a padded row) from coalesced 16-byte loads of C (thread
+// t: rows t / 16 + 16 m, columns 4 (t % 16) ...), written out when T_norm is
+// asked for, added into the rows' centroid partials and staged in shared memory
+// beside the chunk's 64 rows of V; then O = T_norm V as a register-blocked
+// product, thread t accumulating rows 4 (t / 8) .. + 3 and head dims DPT (t % 8)
+// .. + DPT - 1 with packed pair FMAs (16 pair FMAs per 6 shared-memory loads at
+// DPT = 8).
 struct DenseOutArgs {
   const float* C;
   const float* V;     // (B,H,N,d) fp32 or null
@@ -234,89 +328,159 @@ struct DenseOutArgs {
   const float* mask;
   const float* lu;
   const float* lv;
+  const float* rmax;  // row statistics of the score (log2 units)
+  const float* rsum;
   float* O;           // (B,H,N,d)
   float* T;           // (B,H,N,N) or null
   float* xc;          // (B,H,N,3) or null
   int B, H, N, d;
 };
 
-template <int DV>
+constexpr int kOutRows = 128, kOutCols = 64, kOutTS = kOutCols + 4;  // T tile row stride (floats)
+
+template <int DPT>
+size_t dense_out_smem() {
+  return sizeof(float) * (static_cast<size_t>(kOutRows) * kOutTS + static_cast<size_t>(kOutCols) * 8 * DPT);
+}
+
+template <int DPT, bool VEC>  // DPT: O's head dims per thread (d <= 8 DPT)
 __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOutArgs a) {
-  extern __shared__ float vt[];  // [32][d] tile of V
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int DP = 8 * DPT;
+  extern __shared__ float4 smo4[];
+  float* Ts = reinterpret_cast<float*>(smo4);     // [128][68]
+  float* Vs = Ts + kOutRows * kOutTS;             // [64][DP] (dims beyond d zero)
+  const int tid = threadIdx.x, lane = tid & 31;
   const int N = a.N, d = a.d;
-  const int rblocks = (N + 7) / 8;
+  const int rblocks = (N + kOutRows - 1) / kOutRows;
   const size_t prob = blockIdx.x / rblocks;
-  const int i = (blockIdx.x % rblocks) * 8 + warp;
+  const int i0 = (blockIdx.x % rblocks) * kOutRows;
   const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
-  const bool row_ok = i < N;  // rows past N still help stage V
-  const float eps = a.eps[h];
-  const size_t r = prob * N + (row_ok ? i : 0);
-  const float* c = a.C + r * N;
+  const float sc = -kLog2e / a.eps[h];
   const float* g = a.lv + prob * N;
-  const float ui = row_ok ? a.lu[r] : 0.0f;
-  float m = -INFINITY, s = 0.0f;
-  if (row_ok)
-    for (int j = lane; j < N; j += 32) lse_push(m, s, ui + (-c[j] / eps) + g[j] + bias_of(a.mask, b, N, j));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    lse_merge(m, s, m2, s2);
-  }
-  const float rmask = (a.mask == nullptr || !row_ok) ? 1.0f : a.mask[static_cast<size_t>(b) * N + i];
-  float acc[DV];
-#pragma unroll
-  for (int q = 0; q < DV; ++q) acc[q] = 0.0f;
-  float cx = 0.0f, cy = 0.0f, cz = 0.0f;
   const float* xb = a.x != nullptr ? a.x + static_cast<size_t>(b) * N * 3 : nullptr;
-  for (int j0 = 0; j0 < N; j0 += 32) {
-    const int j = j0 + lane;
-    float t = 0.0f;
-    if (row_ok && j < N) {
-      // the reference's T / (sum + 1e-6), then the padded-row factor
-      t = expf(ui + (-c[j] / eps) + g[j] + bias_of(a.mask, b, N, j) - m) / (s + 1e-6f) * rmask;
-      if (a.T != nullptr) __stcs(a.T + r * N + j, t);
-      if (xb != nullptr) {
-        cx += t * xb[3 * j];
-        cy += t * xb[3 * j + 1];
-        cz += t * xb[3 * j + 2];
-      }
-    }
-    if (a.V != nullptr) {
-      __syncthreads();
-      const float* vsrc = a.V + (prob * N + j0) * d;
-      const int rows = min(32, N - j0);
-      for (int e = threadIdx.x; e < 32 * d; e += kDenseThreads) vt[e] = e < rows * d ? vsrc[e] : 0.0f;
-      __syncthreads();
-#pragma unroll 4
-      for (int cc = 0; cc < 32; ++cc) {
-        const float tc = __shfl_sync(0xffffffffu, t, cc);
+  // T side: rows lrow0 + 16 m (m < 8), columns 4 c4 .. + 3 of each chunk
+  const int lrow0 = tid >> 4, c4 = tid & 15;
+  float ui[8], mt[8], inv[8], cx[8], cy[8], cz[8];
 #pragma unroll
-        for (int q = 0; q < DV; ++q) {
-          const int k = lane + 32 * q;
-          if (k < d) acc[q] = fmaf(tc, vt[cc * d + k], acc[q]);
+  for (int m = 0; m < 8; ++m) {
+    const int i = i0 + lrow0 + 16 * m;
+    const size_t r = prob * N + (i < N ? i : 0);
+    const bool ok = i < N;
+    ui[m] = ok ? a.lu[r] : 0.0f;
+    mt[m] = ok ? a.rmax[r] : 0.0f;
+    const float rm = (!ok) ? 0.0f : (a.mask == nullptr ? 1.0f : a.mask[static_cast<size_t>(b) * N + i]);
+    inv[m] = ok ? rm / (a.rsum[r] + 1e-6f) : 0.0f;
+    cx[m] = cy[m] = cz[m] = 0.0f;
+  }
+  // product side: rows 4 rg .. + 3, dims DPT dg .. + DPT - 1
+  const int rg = tid >> 3, dg = tid & 7;
+  float2 acc[4][DPT / 2];
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int q = 0; q < DPT / 2; ++q) acc[m][q] = make_float2(0.0f, 0.0f);
+  for (int j0 = 0; j0 < N; j0 += kOutCols) {
+    const int jc = j0 + 4 * c4;  // this thread's 4 columns
+    float gb[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) gb[e] = (jc + e < N) ? (g[jc + e] + bias_of(a.mask, b, N, jc + e)) : 0.0f;
+    __syncthreads();  // the previous chunk's product is done with Ts / Vs
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int li = lrow0 + 16 * m, i = i0 + li;
+      const float* crow = a.C + (prob * N + (i < N ? i : 0)) * static_cast<size_t>(N);
+      float cv[4];
+      if (VEC && i < N && jc + 4 <= N) {
+        const float4 c = __ldcs(reinterpret_cast<const float4*>(crow + jc));
+        cv[0] = c.x; cv[1] = c.y; cv[2] = c.z; cv[3] = c.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cv[e] = (i < N && jc + e < N) ? __ldcs(crow + jc + e) : 0.0f;
+      }
+      float t[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = jc + e;
+        // the reference's T / (sum + 1e-6), then the padded-row factor (in inv)
+        t[e] = (i < N && j < N) ? ex2f(fmaf(cv[e], sc, (ui[m] + gb[e]) * kLog2e) - mt[m]) * inv[m] : 0.0f;
+        if (xb != nullptr && j < N) {
+          cx[m] = fmaf(t[e], xb[3 * j], cx[m]);
+          cy[m] = fmaf(t[e], xb[3 * j + 1], cy[m]);
+          cz[m] = fmaf(t[e], xb[3 * j + 2], cz[m]);
+        }
+      }
+      *reinterpret_cast<float4*>(Ts + li * kOutTS + 4 * c4) = make_float4(t[0], t[1], t[2], t[3]);
+      if (a.T != nullptr && i < N) {
+        float* trow = a.T + (prob * N + i) * static_cast<size_t>(N);
+        if (VEC && jc + 4 <= N) {
+          __stcs(reinterpret_cast<float4*>(trow + jc), make_float4(t[0], t[1], t[2], t[3]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (jc + e < N) __stcs(trow + jc + e, t[e]);
         }
       }
     }
+    if (a.V == nullptr) continue;  // uniform: no O asked for
+    const float* vsrc = a.V + (prob * N + j0) * static_cast<size_t>(d);
+    const int rows = min(kOutCols, N - j0);
+    for (int e = tid; e < kOutCols * DP; e += kDenseThreads) {
+      const int c = e / DP, k = e - c * DP;
+      Vs[e] = (c < rows && k < d) ? __ldg(vsrc + static_cast<size_t>(c) * d + k) : 0.0f;
+    }
+    __syncthreads();
+    const float* tb = Ts + 4 * rg * kOutTS;
+    const float* vb = Vs + DPT * dg;
+#pragma unroll 4
+    for (int c = 0; c < kOutCols; ++c) {
+      float2 v[DPT / 2];
+#pragma unroll
+      for (int q = 0; q < DPT / 4; ++q) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vb + c * DP + 4 * q);
+        v[2 * q] = make_float2(v4.x, v4.y);
+        v[2 * q + 1] = make_float2(v4.z, v4.w);
+      }
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float tv = tb[m * kOutTS + c];
+        const float2 t2 = make_float2(tv, tv);
+#pragma unroll
+        for (int q = 0; q < DPT / 2; ++q) acc[m][q] = __ffma2_rn(t2, v[q], acc[m][q]);
+      }
+    }
   }
-  if (!row_ok) return;
-  if (a.O != nullptr)
-#pragma unroll
-    for (int q = 0; q < DV; ++q) {
-      const int k = lane + 32 * q;
-      if (k < d) a.O[r * d + k] = acc[q];
-    }
   if (a.xc != nullptr) {
+    // the 16 threads of a row are consecutive lanes of one warp
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      cx += __shfl_xor_sync(0xffffffffu, cx, o);
-      cy += __shfl_xor_sync(0xffffffffu, cy, o);
-      cz += __shfl_xor_sync(0xffffffffu, cz, o);
+    for (int m = 0; m < 8; ++m) {
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        cx[m] += __shfl_xor_sync(0xffffffffu, cx[m], o);
+        cy[m] += __shfl_xor_sync(0xffffffffu, cy[m], o);
+        cz[m] += __shfl_xor_sync(0xffffffffu, cz[m], o);
+      }
+      const int i = i0 + lrow0 + 16 * m;
+      if (c4 == 0 && i < N) {
+        const size_t r = prob * N + i;
+        a.xc[r * 3] = cx[m];
+        a.xc[r * 3 + 1] = cy[m];
+        a.xc[r * 3 + 2] = cz[m];
+      }
     }
-    if (lane == 0) {
-      a.xc[r * 3] = cx;
-      a.xc[r * 3 + 1] = cy;
-      a.xc[r * 3 + 2] = cz;
+  }
+  (void)lane;
+  if (a.O != nullptr) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i = i0 + 4 * rg + m;
+      if (i >= N) continue;
+      float* orow = a.O + (prob * N + i) * static_cast<size_t>(d);
+#pragma unroll
+      for (int q = 0; q < DPT / 2; ++q) {
+        const int k = DPT * dg + 2 * q;
+        if (k < d) orow[k] = acc[m][q].x;
+        if (k + 1 < d) orow[k + 1] = acc[m][q].y;
+      }
     }
   }
 }
@@ -329,9 +493,14 @@ unsigned grid_for(size_t work_items, size_t per_cta) {
 
 }  // namespace
 
-size_t dense_fwd_workspace(int B, int H) {
-  // diff (2 x BH unsigned) and done (BH int), 256-byte rounded
-  return (static_cast<size_t>(3) * B * H * 4 + 255) & ~static_cast<size_t>(255);
+namespace {
+size_t r256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+}  // namespace
+
+size_t dense_fwd_workspace(int B, int H, int N) {
+  // diff (2 x BH unsigned) and done (BH int); the transport's row statistics
+  // (2 x BH x N floats); each region 256-byte aligned
+  return r256(static_cast<size_t>(3) * B * H * 4) + r256(static_cast<size_t>(2) * B * H * N * 4);
 }
 
 cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
@@ -339,19 +508,21 @@ cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
   const size_t n = static_cast<size_t>(BH) * q.N;
   unsigned* diff = static_cast<unsigned*>(ws);
   int* done = reinterpret_cast<int*>(diff + 2 * static_cast<size_t>(BH));
+  float* rmax = reinterpret_cast<float*>(static_cast<char*>(ws) + r256(static_cast<size_t>(3) * BH * 4));
+  float* rsum = rmax + n;
   const bool vec = (q.N % 4) == 0 && (reinterpret_cast<uintptr_t>(q.C) & 15u) == 0;
   dense_init_kernel<<<grid_for(n, 256), 256, 0, st>>>(q.log_u_init, q.log_v_init, q.log_u, q.log_v, n, diff, done,
                                                        BH);
   cudaError_t e = cudaGetLastError();
   DenseArgs a{q.C, q.eps, q.log_mu, q.log_nu, q.mask, q.log_u, q.log_v, diff, q.threshold > 0.0f ? done : nullptr,
-              q.B, q.H, q.N, q.lam, 0};
+              rmax, rsum, q.B, q.H, q.N, q.lam, 0};
   const unsigned grow = grid_for(n, kDenseThreads / 32);
   const int cols = vec ? 128 : 32;
   const unsigned gcol = static_cast<unsigned>(BH) * static_cast<unsigned>((q.N + cols - 1) / cols);
   for (int it = 0; it < q.K_iter && e == cudaSuccess; ++it) {
     a.check = q.threshold > 0.0f && ((it + 1) % q.check_every) == 0;
-    if (vec) dense_row_kernel<true><<<grow, kDenseThreads, 0, st>>>(a);
-    else dense_row_kernel<false><<<grow, kDenseThreads, 0, st>>>(a);
+    if (vec) dense_row_kernel<true, false><<<grow, kDenseThreads, 0, st>>>(a);
+    else dense_row_kernel<false, false><<<grow, kDenseThreads, 0, st>>>(a);
     if (vec) dense_col_kernel<true><<<gcol, kDenseThreads, 0, st>>>(a);
     else dense_col_kernel<false><<<gcol, kDenseThreads, 0, st>>>(a);
     if (a.check) dense_check_kernel<<<1, 256, 0, st>>>(diff, done, BH, q.threshold);
@@ -359,15 +530,26 @@ cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
   }
   if (e != cudaSuccess) return e;
   if (q.O != nullptr || q.T_out != nullptr || q.x_centroid != nullptr) {
+    DenseArgs sa = a;
+    sa.done = nullptr;  // every problem's outputs
+    if (vec) dense_row_kernel<true, true><<<grow, kDenseThreads, 0, st>>>(sa);
+    else dense_row_kernel<false, true><<<grow, kDenseThreads, 0, st>>>(sa);
     DenseOutArgs o{q.C, q.O != nullptr ? static_cast<const float*>(q.V) : nullptr, q.x_res, q.eps, q.mask,
-                   q.log_u, q.log_v, q.O, q.T_out, q.x_centroid, q.B, q.H, q.N, q.d};
-    const unsigned g = static_cast<unsigned>(BH) * static_cast<unsigned>((q.N + 7) / 8);
-    const size_t smem = static_cast<size_t>(32) * q.d * sizeof(float);
-    const int dv = (q.d + 31) / 32;
-    if (dv <= 1) dense_out_kernel<1><<<g, kDenseThreads, smem, st>>>(o);
-    else if (dv == 2) dense_out_kernel<2><<<g, kDenseThreads, smem, st>>>(o);
-    else dense_out_kernel<4><<<g, kDenseThreads, smem, st>>>(o);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+                   q.log_u, q.log_v, rmax, rsum, q.O, q.T_out, q.x_centroid, q.B, q.H, q.N, q.d};
+    const unsigned g = static_cast<unsigned>(BH) * static_cast<unsigned>((q.N + kOutRows - 1) / kOutRows);
+    auto go = [&](auto kern, size_t smem) {
+      cudaError_t e2 = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e2 == cudaSuccess) {
+        kern<<<g, kDenseThreads, smem, st>>>(o);
+        e2 = cudaGetLastError();
+      }
+      return e2;
+    };
+    const int dpt = q.d <= 32 ? 4 : (q.d <= 64 ? 8 : 16);
+    if (dpt == 4) e = vec ? go(dense_out_kernel<4, true>, dense_out_smem<4>()) : go(dense_out_kernel<4, false>, dense_out_smem<4>());
+    else if (dpt == 8) e = vec ? go(dense_out_kernel<8, true>, dense_out_smem<8>()) : go(dense_out_kernel<8, false>, dense_out_smem<8>());
+    else e = vec ? go(dense_out_kernel<16, true>, dense_out_smem<16>()) : go(dense_out_kernel<16, false>, dense_out_smem<16>());
+    if (e != cudaSuccess) return e;
   }
   dense_finish_kernel<<<grid_for(n, 256), 256, 0, st>>>(q.mask, q.log_u, q.log_v, q.B, q.H, q.N, q.status);
   return cudaGetLastError();

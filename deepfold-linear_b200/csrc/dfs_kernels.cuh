@@ -158,7 +158,7 @@ size_t resident_fwd_smem(int N, int d);
 cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
 // dense-cost forward streamed from the caller's C (problems outside the
 // resident kernels' range): potentials, O / T_norm / x_centroid, early stop
-size_t dense_fwd_workspace(int B, int H);
+size_t dense_fwd_workspace(int B, int H, int N);
 cudaError_t launch_dense_fwd(const FwdParams& p, void* ws, cudaStream_t st);
 // Peer exchange of a row-sharded forward: every GPU's workspace (same layout,
 // 256-byte aligned bases) and the cumulative arrival count the phase waits for.

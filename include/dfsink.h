@@ -256,7 +256,7 @@ int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const d
  * 4 bytes per block of 128 rows and under 1 KB fixed, i.e. B*H*N up to about
  * 19,000 points at d = 64 or 33,000 at d = 32; head dims other than 32 and 64
  * add their zero-padded copies.  Cluster-resident problems (N <= 384, d = 32)
- * need none; dense-cost problems need 12 bytes per (batch, head). */
+ * need none; dense-cost problems need 8 bytes per (batch, head, point). */
 #define DFS_STATIC_SCRATCH_BYTES (16u << 20)
 
 /* Forward for callers that cannot allocate device memory.  No counterpart in

@@ -72,12 +72,13 @@ def test_host_side_validation(lib):
     assert lib.dfs_fwd(huge, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
     wide_d = nat.make_problem(1, 1, 128, 96, __import__("torch").bfloat16, 20, 1.0, 10.0)
     assert lib.dfs_fwd(wide_d, fake, None, 0, None) == nat.DFS_ERR_UNSUPPORTED
-    # a dense cost beyond the resident range streams C: a small per-problem workspace,
+    # a dense cost beyond the resident range streams C: a small workspace,
     # V head dims up to 128 (fp32), no backward
     dense = nat.make_problem(2, 3, 1000, 128, __import__("torch").float32, 5, 1.0, 10.0,
                              cost_mode=nat.DFS_COST_DENSE)
     assert lib.dfs_workspace_size(dense, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
-    assert fb.value == 256 and bb.value == 0
+    # per-problem early-stop state (256 bytes here), then the transport's two row statistics per point
+    assert fb.value == 256 + ((2 * 6 * 1000 * 4 + 255) // 256) * 256 and bb.value == 0
     fake_dense = nat.DfsFwdArgs(C=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16)
     assert lib.dfs_fwd(dense, fake_dense, None, 0, None) == nat.DFS_ERR_WORKSPACE
     wider = nat.make_problem(1, 1, 1000, 129, __import__("torch").float32, 5, 1.0, 10.0, cost_mode=nat.DFS_COST_DENSE)
