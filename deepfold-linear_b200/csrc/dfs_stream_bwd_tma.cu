@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kBTThreads, 1) btile_kernel(const __grid_const
   using C = BTileCfg<MODE, D, TERMS>;
   constexpr bool kAcc = C::kAcc, kDT = C::kDT;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch (see launch_dependent)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next pass may launch (it waits first)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* sA = reinterpret_cast<float*>(base + C::OFF_A);

@@ -160,6 +160,10 @@ __global__ void __launch_bounds__(kTThreads, 2) tile_kernel(const __grid_constan
   // its grid is set up while that kernel drains; nothing is read before this
   // wait returns, i.e. before the previous kernel's results are visible
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the next pass on the stream may now be launched and rasterised into the
+  // slots this grid's last wave frees; its first instruction is the same wait,
+  // so it reads nothing before this grid has finished
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sA = smem_u32(base + C::OFF_A), sB = smem_u32(base + C::OFF_B);

@@ -139,10 +139,12 @@ DFS_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* tm, int x, int y, int 
 
 // Launches a kernel as a programmatic dependent of the previous work on the
 // stream (programmatic stream serialization): its grid may be launched and set
-// up while the previous kernel's last CTAs run.  The kernel must execute
-// griddepcontrol.wait before it reads anything the previous kernel wrote; no
-// kernel here triggers its dependents early, so a dependent grid starts only
-// once every CTA of its predecessor has been launched.
+// up while the previous kernel's last CTAs run.  Every kernel launched this way
+// executes griddepcontrol.wait as its first instruction, before it reads or
+// writes anything; the tile passes then trigger their own dependents
+// (griddepcontrol.launch_dependents) at once, so the next pass is launched when
+// every CTA of this one has started and passed its wait -- at most two grids
+// overlap, and the later one only waits until the earlier has finished.
 template <typename... Params, typename... Args>
 cudaError_t launch_dependent(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                              Args&&... args) {
