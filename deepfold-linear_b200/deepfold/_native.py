@@ -23,7 +23,8 @@ INCLUDE_DIR = os.path.join(os.path.dirname(ROOT_DIR), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libdfsink.so")
 SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_stream.cu", "dfs_stream_bwd.cu", "dfs_stream_tma.cu",
-           "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu", "dfs_pad.cu", "dfs_dense.cu"]
+           "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu", "dfs_pad.cu", "dfs_dense.cu",
+           "dfs_peer.cu"]
 HEADERS = ["dfs_device.cuh", "dfs_kernels.cuh", "dfs_slab.cuh", "dfs_tma.cuh"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -92,7 +93,7 @@ class DfsPeerSet(ctypes.Structure):
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
                     "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op",
                     "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer",
-                    "dfs_compute_bins")
+                    "dfs_compute_bins", "dfs_peer_gather_rows")
 
 # phases of the streamed path for row-sharded runs (include/dfsink.h)
 DFS_OP_FWD_INIT, DFS_OP_FWD_ROWS, DFS_OP_FWD_COLS, DFS_OP_FWD_OUT = 0, 1, 2, 3
@@ -256,6 +257,10 @@ def lib() -> ctypes.CDLL:
             L.dfs_stream_op_peer.argtypes = [ctypes.c_int, ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsFwdArgs),
                                              ctypes.c_int, ctypes.c_int, _P, ctypes.c_size_t,
                                              ctypes.POINTER(DfsPeerSet), _P]
+            L.dfs_peer_gather_rows.restype = ctypes.c_int
+            L.dfs_peer_gather_rows.argtypes = [ctypes.POINTER(DfsPeerSet), ctypes.c_size_t, ctypes.c_int,
+                                               ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_size_t, _P, _P]
             L.dfs_compute_bins.restype = ctypes.c_int
             L.dfs_compute_bins.argtypes = [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]
             L.dfs_selftest_mma.restype = ctypes.c_int

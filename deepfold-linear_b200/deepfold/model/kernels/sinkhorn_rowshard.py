@@ -25,8 +25,12 @@ forward workspace is a device buffer shared with the other ranks through CUDA
 IPC (``_PeerWorkspace``), and the half-update kernel stores its rows of the new
 potential straight into every rank's copy over NVLink and raises every rank's
 arrival counter; the next half-update waits on its own counter
-(``dfs_stream_op_peer``).  ``DFS_ROWSHARD_EXCHANGE=collective`` selects the
-all-gather exchange instead.  Where the reference
+(``dfs_stream_op_peer``).  The backward's workspace is shared the same way,
+and its row statistics, column sums and CG vectors are gathered through peer
+memory too (``dfs_peer_gather_rows``: every rank pushes its rows into every
+other rank's copy, raises their counters, and waits on its own); only the final
+dQ, dK, dV go through NCCL.  ``DFS_ROWSHARD_EXCHANGE=collective`` selects the
+all-gather exchange for both instead.  Where the reference
 runs on one device only (src/deepfold/model/kernels/sinkhorn_kernel.py), this
 module has no counterpart there.
 """
@@ -150,12 +154,27 @@ class _PeerWorkspace:
 _peer_ws: dict = {}
 
 
-def _peer_workspace(nbytes: int, group, device: torch.device) -> _PeerWorkspace:
-    key = (nbytes, device.index, id(group))
+def _peer_workspace(nbytes: int, group, device: torch.device, kind: str = "fwd") -> _PeerWorkspace:
+    key = (kind, nbytes, device.index, id(group))
     if key not in _peer_ws:
         with torch.cuda.device(device):  # the buffer and the peer mappings belong to this GPU
             _peer_ws[key] = _PeerWorkspace(nbytes, group, device)
     return _peer_ws[key]
+
+
+class _CudaFloats:
+    """A device buffer the library allocated, described for torch.as_tensor
+    (the CUDA array interface): a float32 vector of n elements at ptr."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+def _device_floats(ptr: int, n: int, device: torch.device) -> torch.Tensor:
+    """A torch view (no copy) of n float32 at ptr on `device`, valid while the
+    buffer lives (peer workspaces live until the process exits)."""
+    with torch.cuda.device(device):
+        return torch.as_tensor(_CudaFloats(ptr, n), device=device)
 
 
 def _slot(ws: torch.Tensor, k: int, P: int, N: int) -> torch.Tensor:
@@ -266,7 +285,15 @@ class _Sharded:
         iters = torch.empty(P, device=dev, dtype=torch.int32)
         resid = torch.empty(P, **fo)
         status = torch.zeros(1, device=dev, dtype=torch.int32)
-        ws = torch.empty(max(self.bwd_bytes // 4, 1), **fo)
+        peer = self._peer_exchange()
+        if peer:
+            # the workspace is shared with every rank (CUDA IPC); its slot gathers
+            # go through peer memory, the arrival counters after the workspace
+            cnt_off = -(-self.bwd_bytes // 256) * 256
+            pwb = _peer_workspace(cnt_off + 256, self.group, dev, kind="bwd")
+            ws = _device_floats(pwb.ptr, max(self.bwd_bytes // 4, 1), dev)
+        else:
+            ws = torch.empty(max(self.bwd_bytes // 4, 1), **fo)
         cgp = nat.DfsCgParams(rtol=float(self.cg["rtol"]), atol=float(self.cg["atol"]),
                               max_iter=int(self.cg["max_iter"]), reserved=0)
         ba = nat.DfsBwdArgs(Q=nat.ptr(self.Q), K=nat.ptr(self.K), V=nat.ptr(self.V), x_res=nat.ptr(self.xr),
@@ -278,20 +305,31 @@ class _Sharded:
         g, r0, r1 = self.gather, self.gather.r0, self.gather.r1
         run = lambda op, a=0, b=N: self._op(op, a, b, ba=ba, ws=ws, nbytes=self.bwd_bytes, cgp=cgp)  # noqa: E731
         slot = lambda k: _slot(ws, k, P, N)  # noqa: E731
+        world = self.gather.world
+
+        def gslot(k):
+            """Every rank's rows of workspace slot k on every rank."""
+            if not peer:
+                g(slot(k))
+                return
+            pwb.arrived += world  # every rank raises every counter once per gather
+            pwb.peers.wait_for = pwb.arrived
+            nat.check(nat.lib().dfs_peer_gather_rows(pwb.peers, k * P * N * 4, P, N, 1, r0, r1, cnt_off,
+                                                     nat.ptr(status), self.stream), "dfs_peer_gather_rows")
         # the per-problem CG stop flags (int32) follow the vector slots and the scalars
         o = nat.DFS_WS_BWD_NSLOTS * P * N + nat.DFS_WS_BWD_NSCALARS * P
         done = ws[o:o + P].view(torch.int32)
         run(nat.DFS_OP_BWD_PREP)
         run(nat.DFS_OP_BWD_ROWSTATS, r0, r1)
         for k in (nat.DFS_WS_BWD_M, nat.DFS_WS_BWD_R, nat.DFS_WS_BWD_D):
-            g(slot(k))
+            gslot(k)
         run(nat.DFS_OP_BWD_ROWDERIVE)
         run(nat.DFS_OP_BWD_COLSTATS, r0, r1)
-        g(slot(nat.DFS_WS_BWD_C))
-        g(slot(nat.DFS_WS_BWD_GV))
+        gslot(nat.DFS_WS_BWD_C)
+        gslot(nat.DFS_WS_BWD_GV)
         run(nat.DFS_OP_BWD_SETUP)
         run(nat.DFS_OP_BWD_PT_T, r0, r1)
-        g(slot(nat.DFS_WS_BWD_S))
+        gslot(nat.DFS_WS_BWD_S)
         run(nat.DFS_OP_BWD_CGINIT)
         # The stop flags are identical on every rank (same gathered vectors, same
         # arithmetic), so all ranks leave the loop after the same iteration.  The
@@ -300,17 +338,16 @@ class _Sharded:
         # extra iteration after convergence skips every converged problem (its
         # plan products and CG step return at once).
         stream = torch.cuda.current_stream(dev)
-        flag_bufs = [torch.empty(P, dtype=torch.int32).pin_memory() for _ in range(2)]
+        flag_bufs, flag_evs = _flag_buffers(P, dev)
         pending = None
         for it in range(int(self.cg["max_iter"]) + 1):
             run(nat.DFS_OP_BWD_P_U, r0, r1)
-            g(slot(nat.DFS_WS_BWD_T))
+            gslot(nat.DFS_WS_BWD_T)
             run(nat.DFS_OP_BWD_PT_T, r0, r1)
-            g(slot(nat.DFS_WS_BWD_S))
+            gslot(nat.DFS_WS_BWD_S)
             run(nat.DFS_OP_BWD_CGSTEP_FIRST if it == 0 else nat.DFS_OP_BWD_CGSTEP)
-            buf = flag_bufs[it & 1]
+            buf, ev = flag_bufs[it & 1], flag_evs[it & 1]
             buf.copy_(done, non_blocking=True)
-            ev = torch.cuda.Event()
             ev.record(stream)
             prev, pending = pending, (ev, buf)
             if prev is not None:
@@ -318,7 +355,7 @@ class _Sharded:
                 if bool((prev[1] != 0).all()):
                     break
         run(nat.DFS_OP_BWD_P_X, r0, r1)
-        g(slot(nat.DFS_WS_BWD_S))
+        gslot(nat.DFS_WS_BWD_S)
         run(nat.DFS_OP_BWD_FINAL)
         run(nat.DFS_OP_BWD_DQ, r0, r1)
         run(nat.DFS_OP_BWD_DKV, r0, r1)
@@ -331,6 +368,19 @@ class _Sharded:
 
 
 _last_report: dict = {}
+_flag_cache: dict = {}
+
+
+def _flag_buffers(P: int, device: torch.device):
+    """Two pinned host buffers for the CG stop flags and two events, made once per
+    (P, device): pinning host memory inside a timed loop can stall the host for
+    milliseconds, and every rank waits for a stalled one.  Reuse is ordered by
+    the stream: a buffer is read only after the event of its own copy."""
+    key = (P, device.index)
+    if key not in _flag_cache:
+        _flag_cache[key] = ([torch.empty(P, dtype=torch.int32).pin_memory() for _ in range(2)],
+                            [torch.cuda.Event() for _ in range(2)])
+    return _flag_cache[key]
 
 
 def last_rowshard_report() -> dict:

@@ -317,6 +317,22 @@ typedef struct {
 int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int row_begin, int row_end,
                        void* workspace, size_t workspace_bytes, const dfs_peer_set* peers, void* stream);
 
+/* Peer-memory gather of row slices, for the phases of a row-sharded backward
+ * (or any buffer every GPU of the run holds at the same layout, e.g. one
+ * shared through dfs_peer_alloc / dfs_peer_open; peers->ws[k] are the
+ * buffers' bases, 256-byte aligned).  The slot at byte slot_offset holds P
+ * problems x N rows x `width` floats; this GPU's rows [row_begin, row_end) of
+ * every problem are stored into every other GPU's buffer, then every GPU's
+ * arrival counter (a uint64 at byte counter_offset of its buffer; the 8 bytes
+ * after it are this GPU's completion counter, zero between calls) is raised
+ * once; finally the stream waits until this GPU's own counter reaches
+ * peers->wait_for (bounded: a timeout sets DFS_ERR_DEVICE_TIMEOUT in *status).
+ * Counters accumulate, so all GPUs pass the same cumulative wait_for sequence
+ * (npeers arrivals per gather).  Replaces, for the row-sharded path, the
+ * all-gather collective between phases; the reference has no sharded path. */
+int dfs_peer_gather_rows(const dfs_peer_set* peers, size_t slot_offset, int P, int N, int width, int row_begin,
+                         int row_end, size_t counter_offset, int32_t* status, void* stream);
+
 /* TEST-ONLY entry point, not part of the operator surface: runs one of the
  * three tcgen05 MMA operand layouts the kernels use on caller-provided data
  * (D = A B^T, M = 64), so the test suite can check each layout against a
