@@ -418,6 +418,31 @@ int dfs_stream_op(int op, const dfs_problem* p, const dfs_cg_params* cg, const d
   return DFS_ERR_INVALID_ARGUMENT;
 }
 
+int dfs_stream_cg_loop_peer(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* ba, int row_begin,
+                            int row_end, void* workspace, size_t workspace_bytes, const dfs_peer_set* peers,
+                            size_t counter_offset, void* stream) {
+  if (!dims_ok(p) || !streamed(p) || padded(p) || (p->cost_terms & (DFS_TERM_POS | DFS_TERM_GEO)))
+    return dims_ok(p) ? DFS_ERR_UNSUPPORTED : DFS_ERR_INVALID_ARGUMENT;
+  if (row_begin < 0 || row_end < row_begin || row_end > p->N || peers == nullptr) return DFS_ERR_INVALID_ARGUMENT;
+  if (peers->npeers < 1 || peers->npeers > DFS_MAX_PEERS || peers->self < 0 || peers->self >= peers->npeers ||
+      peers->ws[peers->self] != workspace || (counter_offset & 7u) != 0 || counter_offset < workspace_bytes)
+    return DFS_ERR_INVALID_ARGUMENT;
+  for (int k = 0; k < peers->npeers; ++k)
+    if (peers->ws[k] == nullptr || (reinterpret_cast<uintptr_t>(peers->ws[k]) & 255u) != 0)
+      return DFS_ERR_INVALID_ARGUMENT;
+  int rc;
+  if ((rc = check_bwd_args(p, cg, ba)) != DFS_OK) return rc;
+  if ((rc = check_stream_bwd(p, ba, workspace, workspace_bytes)) != DFS_OK) return rc;
+  PeerInfo pi{};
+  pi.npeers = peers->npeers;
+  pi.self = peers->self;
+  for (int k = 0; k < peers->npeers; ++k) pi.ws[k] = peers->ws[k];
+  return cg_loop_graph_peer(bwd_params(p, cg, ba, workspace), static_cast<float*>(workspace), row_begin, row_end, pi,
+                            counter_offset, static_cast<cudaStream_t>(stream))
+             ? DFS_OK
+             : DFS_ERR_UNSUPPORTED;
+}
+
 int dfs_peer_alloc(size_t bytes, void** ptr, dfs_ipc_handle* handle) {
   if (ptr == nullptr || handle == nullptr || bytes == 0) return DFS_ERR_INVALID_ARGUMENT;
   *ptr = nullptr;

@@ -170,6 +170,16 @@ struct PeerInfo {
 cudaError_t stream_fwd_op(int op, const FwdParams& p, float* ws, int r0, int r1, cudaStream_t st,
                           const PeerInfo* peers = nullptr);
 cudaError_t stream_bwd_op(int op, const BwdParams& p, float* ws, int r0, int r1, cudaStream_t st);
+// Peer-memory gather of the rows [r0, r1) of a slot (P x N x width floats at
+// slot_offset of every GPU's buffer pi.ws[k]); counters at counter_offset
+// (arrivals, push completion, expected count: device-relative waits).
+cudaError_t peer_gather_rows(const PeerInfo& pi, size_t slot_offset, int P, int N, int width, int row_begin,
+                             int row_end, size_t counter_offset, int32_t* status, cudaStream_t st);
+// The row-sharded backward's CG rounds 1 .. max_iter as one CUDA graph with a
+// device-terminated WHILE loop (plan products on rows [r0, r1), peer gathers
+// of their slots, the CG step); false when no such graph could be built.
+bool cg_loop_graph_peer(const BwdParams& bp, float* ws, int r0, int r1, const PeerInfo& pi, size_t counter_offset,
+                        cudaStream_t st);
 size_t stream_fwd_workspace(int B, int H, int N, int d, int terms = 0);
 cudaError_t launch_resident_bwd(const BwdParams& p, cudaStream_t st);
 cudaError_t launch_stream_bwd(const BwdParams& p, float* ws, cudaStream_t st);

@@ -1123,6 +1123,85 @@ bool cg_loop_graph(const BwdParams& bp, float* wsp, cudaStream_t st) {
 
 }  // namespace
 
+// The same device-terminated loop for one rank of a row-sharded run: each round
+// runs the plan products on this rank's rows, gathers their slots (t, then s)
+// from every rank through peer memory, and takes the CG step.  The stop flags
+// come from the gathered vectors, identical on every rank, so every rank's
+// loop runs the same rounds; the gathers' waits count on the device, so the
+// recorded graph needs no per-round argument and the host never waits.
+bool cg_loop_graph_peer(const BwdParams& bp, float* wsp, int r0, int r1, const PeerInfo& pi, size_t counter_offset,
+                        cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;
+  }
+  int dev = 0;
+  if (cudaStreamGetDevice(st, &dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  cudaStream_t cap = capture_stream(dev);
+  if (cap == nullptr) return false;
+  static std::mutex capture_mu;
+  std::lock_guard<std::mutex> lock(capture_mu);
+  const size_t n = static_cast<size_t>(bp.B) * bp.H * bp.N, nbh = static_cast<size_t>(bp.B) * bp.H;
+  float* sc = wsp + WS_NUM * n;
+  int32_t* done = reinterpret_cast<int32_t*>(sc + SC_NUM * nbh);
+  int32_t* rounds = reinterpret_cast<int32_t*>(sc + SC_LOOP);
+  const int nprob = static_cast<int>(nbh), max_rounds = bp.cg_max_iter;
+  const size_t slot_bytes = sizeof(float) * n;
+  cudaGraph_t g = nullptr, body = nullptr;
+  cudaGraphExec_t ex = nullptr;
+  cudaGraphNode_t first = nullptr, loop = nullptr;
+  bool ok = cudaGraphCreate(&g, 0) == cudaSuccess;
+  cudaGraphConditionalHandle cond = 0;
+  ok = ok && cudaGraphConditionalHandleCreate(&cond, g, 0, cudaGraphCondAssignDefault) == cudaSuccess;
+  if (ok) {
+    int reset = 1;
+    void* args[] = {&done, const_cast<int*>(&nprob), &rounds, const_cast<int*>(&max_rounds), &reset, &cond};
+    cudaKernelNodeParams kp = {};
+    kp.func = reinterpret_cast<void*>(sb_loopcond_kernel);
+    kp.gridDim = dim3(1);
+    kp.blockDim = dim3(256);
+    kp.kernelParams = args;
+    ok = cudaGraphAddKernelNode(&first, g, nullptr, 0, &kp) == cudaSuccess;
+  }
+  if (ok) {
+    cudaGraphNodeParams np = {};
+    np.type = cudaGraphNodeTypeConditional;
+    np.conditional.handle = cond;
+    np.conditional.type = cudaGraphCondTypeWhile;
+    np.conditional.size = 1;
+    ok = cudaGraphAddNode(&loop, g, &first, 1, &np) == cudaSuccess;
+    if (ok) body = np.conditional.phGraph_out[0];
+  }
+  if (ok) ok = cudaStreamBeginCaptureToGraph(cap, body, nullptr, nullptr, 0, cudaStreamCaptureModeRelaxed) ==
+               cudaSuccess;
+  if (ok) {
+    cudaError_t e = stream_bwd_op(DFS_OP_BWD_P_U, bp, wsp, r0, r1, cap);
+    if (e == cudaSuccess)
+      e = peer_gather_rows(pi, WS_T * slot_bytes, nprob, bp.N, 1, r0, r1, counter_offset, bp.status, cap);
+    if (e == cudaSuccess) e = stream_bwd_op(DFS_OP_BWD_PT_T, bp, wsp, r0, r1, cap);
+    if (e == cudaSuccess)
+      e = peer_gather_rows(pi, WS_S * slot_bytes, nprob, bp.N, 1, r0, r1, counter_offset, bp.status, cap);
+    if (e == cudaSuccess) e = stream_bwd_op(DFS_OP_BWD_CGSTEP, bp, wsp, 0, bp.N, cap);
+    if (e == cudaSuccess) {
+      sb_loopcond_kernel<<<1, 256, 0, cap>>>(done, nprob, rounds, max_rounds, 0, cond);
+      e = cudaGetLastError();
+    }
+    cudaGraph_t captured = nullptr;
+    const cudaError_t ee = cudaStreamEndCapture(cap, &captured);
+    ok = e == cudaSuccess && ee == cudaSuccess;
+  }
+  if (ok) ok = cudaGraphInstantiate(&ex, g, 0) == cudaSuccess;
+  if (ok) ok = cudaGraphLaunch(ex, st) == cudaSuccess;
+  if (ex != nullptr) cudaGraphExecDestroy(ex);
+  if (g != nullptr) cudaGraphDestroy(g);
+  if (!ok) cudaGetLastError();
+  return ok;
+}
+
 cudaError_t launch_stream_bwd(const BwdParams& bp, float* wsp, cudaStream_t st) {
   const int N = bp.N;
   cudaError_t e = cudaSuccess;

@@ -93,7 +93,7 @@ class DfsPeerSet(ctypes.Structure):
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
                     "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op",
                     "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer",
-                    "dfs_compute_bins", "dfs_peer_gather_rows")
+                    "dfs_compute_bins", "dfs_peer_gather_rows", "dfs_stream_cg_loop_peer")
 
 # phases of the streamed path for row-sharded runs (include/dfsink.h)
 DFS_OP_FWD_INIT, DFS_OP_FWD_ROWS, DFS_OP_FWD_COLS, DFS_OP_FWD_OUT = 0, 1, 2, 3
@@ -261,6 +261,10 @@ def lib() -> ctypes.CDLL:
             L.dfs_peer_gather_rows.argtypes = [ctypes.POINTER(DfsPeerSet), ctypes.c_size_t, ctypes.c_int,
                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_size_t, _P, _P]
+            L.dfs_stream_cg_loop_peer.restype = ctypes.c_int
+            L.dfs_stream_cg_loop_peer.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsCgParams),
+                                                  ctypes.POINTER(DfsBwdArgs), ctypes.c_int, ctypes.c_int, _P,
+                                                  ctypes.c_size_t, ctypes.POINTER(DfsPeerSet), ctypes.c_size_t, _P]
             L.dfs_compute_bins.restype = ctypes.c_int
             L.dfs_compute_bins.argtypes = [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]
             L.dfs_selftest_mma.restype = ctypes.c_int

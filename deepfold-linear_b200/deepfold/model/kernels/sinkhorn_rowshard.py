@@ -28,8 +28,9 @@ arrival counter; the next half-update waits on its own counter
 (``dfs_stream_op_peer``).  The backward's workspace is shared the same way,
 and its row statistics, column sums and CG vectors are gathered through peer
 memory too (``dfs_peer_gather_rows``: every rank pushes its rows into every
-other rank's copy, raises their counters, and waits on its own); only the final
-dQ, dK, dV go through NCCL.  ``DFS_ROWSHARD_EXCHANGE=collective`` selects the
+other rank's copy, raises their counters, and waits on its own), and so are
+dQ, dK, dV (written into a third shared buffer, gathered, copied out): no
+collective on the data path.  ``DFS_ROWSHARD_EXCHANGE=collective`` selects the
 all-gather exchange for both instead.  Where the reference
 runs on one device only (src/deepfold/model/kernels/sinkhorn_kernel.py), this
 module has no counterpart there.
@@ -213,14 +214,35 @@ class _Sharded:
         self.xc = torch.empty(B, H, N, 3, **fo) if self.xr is not None else None
         self.lu, self.lv = torch.empty(B, H, N, **fo), torch.empty(B, H, N, **fo)
         self.fstatus = torch.zeros(1, device=dev, dtype=torch.int32)
+        peer = self._peer_exchange()
+        outs = [self.O, self.lu, self.lv] + ([self.xc] if self.xc is not None else [])
+        widths = [d, 1, 1, 3]
+        if peer:
+            # the phases write O, log_u, log_v (x_centroid) into a buffer shared with
+            # every rank; their rows are gathered through peer memory and copied out
+            sizes = [P * N * w for w in widths[:len(outs)]]
+            offs = [sum(sizes[:k]) for k in range(len(sizes))]
+            fcnt_off = -(-sum(sizes) * 4 // 256) * 256
+            pwo = _peer_workspace(fcnt_off + 256, self.group, dev, kind="fout")
+            flat = _device_floats(pwo.ptr, sum(sizes), dev)
+            kouts = [flat[o:o + n].view(t.shape) for o, n, t in zip(offs, sizes, outs)]
+        else:
+            kouts = outs
+        kO, klu, klv = kouts[0], kouts[1], kouts[2]
+        kxc = kouts[3] if self.xc is not None else None
         fa = nat.DfsFwdArgs(Q=nat.ptr(self.Q), K=nat.ptr(self.K), V=nat.ptr(self.V), x_res=nat.ptr(self.xr),
                             eps=nat.ptr(self.eps), log_mu=nat.ptr(self.lmu), log_nu=nat.ptr(self.lnu),
                             log_u_init=nat.ptr(self.lui), log_v_init=nat.ptr(self.lvi), mask=nat.ptr(self.mask),
-                            O=nat.ptr(self.O), x_centroid=nat.ptr(self.xc), log_u=nat.ptr(self.lu),
-                            log_v=nat.ptr(self.lv), status=nat.ptr(self.fstatus))
+                            O=nat.ptr(kO), x_centroid=nat.ptr(kxc), log_u=nat.ptr(klu),
+                            log_v=nat.ptr(klv), status=nat.ptr(self.fstatus))
         g, r0, r1 = self.gather, self.gather.r0, self.gather.r1
-        if self._peer_exchange():
+        if peer:
             self._forward_peer(fa, r0, r1)
+            for k, (t, kt) in enumerate(zip(outs, kouts)):
+                nat.check(nat.lib().dfs_peer_gather_rows(pwo.peers, offs[k] * 4, P, N, widths[k], r0, r1, fcnt_off,
+                                                         nat.ptr(self.fstatus), self.stream), "dfs_peer_gather_rows")
+                t.copy_(kt)
+            return self.O, self.xc, self.lu, self.lv
         else:
             ws = torch.empty(max(self.fwd_bytes // 4, 1), **fo)
             run = lambda op, a, b: self._op(op, a, b, fa=fa, ws=ws, nbytes=self.fwd_bytes)  # noqa: E731
@@ -280,12 +302,22 @@ class _Sharded:
         dOc = dO.contiguous().float()
         dxcc = None if (dxc is None or self.xr is None) else dxc.contiguous().float()
         dQ, dK, dV = (torch.empty(B, H, N, d, **fo) for _ in range(3))
+        peer = self._peer_exchange()
+        if peer:
+            # the gradient passes write into a buffer shared with every rank, whose
+            # rows are then gathered through peer memory and copied out
+            gbytes = 3 * P * N * d * 4
+            gcnt_off = -(-gbytes // 256) * 256
+            pwg = _peer_workspace(gcnt_off + 256, self.group, dev, kind="grad")
+            gview = _device_floats(pwg.ptr, 3 * P * N * d, dev).view(3, B, H, N, d)
+            kQ, kK, kV = gview[0], gview[1], gview[2]
+        else:
+            kQ, kK, kV = dQ, dK, dV
         dmu = torch.empty(B, H, N, **fo) if need_marg else None
         dnu = torch.empty(B, H, N, **fo) if need_marg else None
         iters = torch.empty(P, device=dev, dtype=torch.int32)
         resid = torch.empty(P, **fo)
         status = torch.zeros(1, device=dev, dtype=torch.int32)
-        peer = self._peer_exchange()
         if peer:
             # the workspace is shared with every rank (CUDA IPC); its slot gathers
             # go through peer memory, the arrival counters after the workspace
@@ -299,21 +331,19 @@ class _Sharded:
         ba = nat.DfsBwdArgs(Q=nat.ptr(self.Q), K=nat.ptr(self.K), V=nat.ptr(self.V), x_res=nat.ptr(self.xr),
                             eps=nat.ptr(self.eps), log_mu=nat.ptr(self.lmu), log_nu=nat.ptr(self.lnu),
                             mask=nat.ptr(self.mask), log_u=nat.ptr(self.lu), log_v=nat.ptr(self.lv),
-                            dO=nat.ptr(dOc), dxc=nat.ptr(dxcc), dQ=nat.ptr(dQ), dK=nat.ptr(dK), dV=nat.ptr(dV),
+                            dO=nat.ptr(dOc), dxc=nat.ptr(dxcc), dQ=nat.ptr(kQ), dK=nat.ptr(kK), dV=nat.ptr(kV),
                             dlog_mu=nat.ptr(dmu), dlog_nu=nat.ptr(dnu), cg_iters=nat.ptr(iters),
                             cg_residual=nat.ptr(resid), status=nat.ptr(status))
         g, r0, r1 = self.gather, self.gather.r0, self.gather.r1
         run = lambda op, a=0, b=N: self._op(op, a, b, ba=ba, ws=ws, nbytes=self.bwd_bytes, cgp=cgp)  # noqa: E731
         slot = lambda k: _slot(ws, k, P, N)  # noqa: E731
-        world = self.gather.world
 
         def gslot(k):
             """Every rank's rows of workspace slot k on every rank."""
             if not peer:
                 g(slot(k))
                 return
-            pwb.arrived += world  # every rank raises every counter once per gather
-            pwb.peers.wait_for = pwb.arrived
+            # every rank runs the same gathers in the same order: the waits count on the device
             nat.check(nat.lib().dfs_peer_gather_rows(pwb.peers, k * P * N * 4, P, N, 1, r0, r1, cnt_off,
                                                      nat.ptr(status), self.stream), "dfs_peer_gather_rows")
         # the per-problem CG stop flags (int32) follow the vector slots and the scalars
@@ -338,9 +368,26 @@ class _Sharded:
         # extra iteration after convergence skips every converged problem (its
         # plan products and CG step return at once).
         stream = torch.cuda.current_stream(dev)
+        first_round = 0
+        if peer:
+            # round 0 phase by phase, then every later round inside one graph whose
+            # loop stops on the device: no host read of the stop flags at all
+            run(nat.DFS_OP_BWD_P_U, r0, r1)
+            gslot(nat.DFS_WS_BWD_T)
+            run(nat.DFS_OP_BWD_PT_T, r0, r1)
+            gslot(nat.DFS_WS_BWD_S)
+            run(nat.DFS_OP_BWD_CGSTEP_FIRST)
+            rc = nat.lib().dfs_stream_cg_loop_peer(self.prob, cgp, ba, r0, r1, ws.data_ptr(), self.bwd_bytes,
+                                                   pwb.peers, cnt_off, self.stream)
+            if rc == nat.DFS_OK:
+                first_round = None
+            elif rc == nat.DFS_ERR_UNSUPPORTED:
+                first_round = 1  # no conditional graphs here: the host loop below from round 1
+            else:
+                nat.check(rc, "dfs_stream_cg_loop_peer")
         flag_bufs, flag_evs = _flag_buffers(P, dev)
         pending = None
-        for it in range(int(self.cg["max_iter"]) + 1):
+        for it in (range(first_round, int(self.cg["max_iter"]) + 1) if first_round is not None else ()):
             run(nat.DFS_OP_BWD_P_U, r0, r1)
             gslot(nat.DFS_WS_BWD_T)
             run(nat.DFS_OP_BWD_PT_T, r0, r1)
@@ -359,8 +406,14 @@ class _Sharded:
         run(nat.DFS_OP_BWD_FINAL)
         run(nat.DFS_OP_BWD_DQ, r0, r1)
         run(nat.DFS_OP_BWD_DKV, r0, r1)
-        for t in (dQ, dK, dV):
-            g(t.view(P, N, d))
+        if peer:
+            for k, t in enumerate((dQ, dK, dV)):
+                nat.check(nat.lib().dfs_peer_gather_rows(pwg.peers, k * P * N * d * 4, P, N, d, r0, r1, gcnt_off,
+                                                         nat.ptr(status), self.stream), "dfs_peer_gather_rows")
+                t.copy_(gview[k])
+        else:
+            for t in (dQ, dK, dV):
+                g(t.view(P, N, d))
         self.report = dict(cg_iters=iters, cg_residual=resid, status=status, fwd_status=self.fstatus)
         _last_report.clear()
         _last_report.update(self.report)

@@ -324,14 +324,31 @@ int dfs_stream_op_peer(int op, const dfs_problem* p, const dfs_fwd_args* fa, int
  * problems x N rows x `width` floats; this GPU's rows [row_begin, row_end) of
  * every problem are stored into every other GPU's buffer, then every GPU's
  * arrival counter (a uint64 at byte counter_offset of its buffer; the 8 bytes
- * after it are this GPU's completion counter, zero between calls) is raised
- * once; finally the stream waits until this GPU's own counter reaches
- * peers->wait_for (bounded: a timeout sets DFS_ERR_DEVICE_TIMEOUT in *status).
- * Counters accumulate, so all GPUs pass the same cumulative wait_for sequence
- * (npeers arrivals per gather).  Replaces, for the row-sharded path, the
+ * after it are the push's completion counter, zero between calls, then the
+ * expected count; 24 bytes in all, zero at allocation) is raised
+ * once; finally the stream waits until this GPU's own counter reaches its
+ * expected count plus npeers (bounded: a timeout sets DFS_ERR_DEVICE_TIMEOUT in
+ * *status).  The expected count is a uint64 at counter_offset + 16 that the
+ * wait itself advances, so all GPUs must run the same gathers on a buffer in
+ * the same order; peers->wait_for is not used.  Replaces, for the row-sharded path, the
  * all-gather collective between phases; the reference has no sharded path. */
 int dfs_peer_gather_rows(const dfs_peer_set* peers, size_t slot_offset, int P, int N, int width, int row_begin,
                          int row_end, size_t counter_offset, int32_t* status, void* stream);
+
+/* The CG rounds after the first (what the loop of DFS_OP_BWD_P_U, the gather
+ * of slot DFS_WS_BWD_T, DFS_OP_BWD_PT_T, the gather of DFS_WS_BWD_S and
+ * DFS_OP_BWD_CGSTEP would do, up to cg->max_iter rounds) for one GPU of a
+ * row-sharded backward, as one CUDA graph launched on `stream` whose WHILE loop
+ * stops on the device once every problem's solve has stopped: the host neither
+ * waits nor reads flags.  The backward workspace must be the buffer every GPU
+ * shares (peers->ws[self] == workspace) with the dfs_peer_gather_rows counters
+ * at counter_offset (>= workspace_bytes); every GPU calls it at the same point.
+ * DFS_ERR_UNSUPPORTED when no such graph can be built (inside the caller's own
+ * stream capture, or a runtime without conditional graph nodes): the caller
+ * then runs the rounds phase by phase.  New for multi-GPU row sharding. */
+int dfs_stream_cg_loop_peer(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* ba, int row_begin,
+                            int row_end, void* workspace, size_t workspace_bytes, const dfs_peer_set* peers,
+                            size_t counter_offset, void* stream);
 
 /* TEST-ONLY entry point, not part of the operator surface: runs one of the
  * three tcgen05 MMA operand layouts the kernels use on caller-provided data
