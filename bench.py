@@ -650,7 +650,8 @@ def run_big(args):
             "data": f"synthetic (seeded N(0,1); B={B} H={H} N={N} d={d})",
             "config": {"workload": name, "global_batch": B, "heads": H, "seq_len": N, "head_dim": d,
                        "parallelism": (f"(batch,head)-shard x{world}, length^2-balanced" if args.config == 3
-                                       else f"row-shard x{world}, NCCL all-gather per half-iteration"),
+                                       else f"row-shard x{world}, peer-memory exchange over NVLink (no "
+                                            "collective on the data path)"),
                        "l2": "inputs and per-call working set exceed L2 (streamed N x N recompute)"},
             "tflops": {"algorithmic_per_call": round(f_call / 1e12, 4), "counted_on": "sum_b L_b^2 (true lengths)",
                        "cg_iters_mean": n_cg,
