@@ -555,4 +555,32 @@ cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Iterations it_begin + 1 .. it_end of the plain loop (no early stop) on a
+// history of potentials (slot 2i = log_u after iteration i, slot 2i + 1 =
+// log_v), each iteration reading its inputs from the previous slots: the
+// forward that the dense gradients (dfs_dense_grad.cu) reverse.
+cudaError_t launch_dense_iterations(const float* C, const float* eps, const float* mu, const float* nu,
+                                    const float* mask, int B, int H, int N, float lam, float* hist, int it_begin,
+                                    int it_end, cudaStream_t st) {
+  const int BH = B * H;
+  const size_t n = static_cast<size_t>(BH) * N;
+  const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
+  DenseArgs a{C, eps, mu, nu, mask, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, B, H, N, lam, 0};
+  const unsigned grow = grid_for(n, kDenseThreads / 32);
+  const int cols = vec ? 128 : 32;
+  const unsigned gcol = static_cast<unsigned>(BH) * static_cast<unsigned>((N + cols - 1) / cols);
+  cudaError_t e = cudaSuccess;
+  for (int it = it_begin + 1; it <= it_end && e == cudaSuccess; ++it) {
+    a.lu = hist + static_cast<size_t>(2 * it) * n;      // u_it (written)
+    a.lv = hist + static_cast<size_t>(2 * it - 1) * n;  // v_it-1 (read)
+    if (vec) dense_row_kernel<true, false><<<grow, kDenseThreads, 0, st>>>(a);
+    else dense_row_kernel<false, false><<<grow, kDenseThreads, 0, st>>>(a);
+    a.lv = hist + static_cast<size_t>(2 * it + 1) * n;  // v_it (written from u_it)
+    if (vec) dense_col_kernel<true><<<gcol, kDenseThreads, 0, st>>>(a);
+    else dense_col_kernel<false><<<gcol, kDenseThreads, 0, st>>>(a);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
 }  // namespace dfs

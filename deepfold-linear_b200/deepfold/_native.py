@@ -24,7 +24,7 @@ LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libdfsink.so")
 SOURCES = ["dfs_abi.cu", "dfs_fwd.cu", "dfs_bwd.cu", "dfs_stream.cu", "dfs_stream_bwd.cu", "dfs_stream_tma.cu",
            "dfs_stream_bwd_tma.cu", "dfs_selftest.cu", "dfs_noalloc.cu", "dfs_pad.cu", "dfs_dense.cu",
-           "dfs_peer.cu"]
+           "dfs_dense_grad.cu", "dfs_peer.cu"]
 HEADERS = ["dfs_device.cuh", "dfs_kernels.cuh", "dfs_slab.cuh", "dfs_tma.cuh"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -93,7 +93,8 @@ class DfsPeerSet(ctypes.Structure):
 EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_workspace_size",
                     "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op",
                     "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer",
-                    "dfs_compute_bins", "dfs_peer_gather_rows", "dfs_stream_cg_loop_peer")
+                    "dfs_compute_bins", "dfs_peer_gather_rows", "dfs_stream_cg_loop_peer",
+                    "dfs_dense_iterate", "dfs_dense_solve_bwd", "dfs_dense_transport_bwd")
 
 # phases of the streamed path for row-sharded runs (include/dfsink.h)
 DFS_OP_FWD_INIT, DFS_OP_FWD_ROWS, DFS_OP_FWD_COLS, DFS_OP_FWD_OUT = 0, 1, 2, 3
@@ -265,6 +266,13 @@ def lib() -> ctypes.CDLL:
             L.dfs_stream_cg_loop_peer.argtypes = [ctypes.POINTER(DfsProblem), ctypes.POINTER(DfsCgParams),
                                                   ctypes.POINTER(DfsBwdArgs), ctypes.c_int, ctypes.c_int, _P,
                                                   ctypes.c_size_t, ctypes.POINTER(DfsPeerSet), ctypes.c_size_t, _P]
+            _I, _F = ctypes.c_int, ctypes.c_float
+            L.dfs_dense_iterate.restype = ctypes.c_int
+            L.dfs_dense_iterate.argtypes = [_I, _I, _I, _F] + [_P] * 8 + [_I, _I] + [_P] * 5
+            L.dfs_dense_solve_bwd.restype = ctypes.c_int
+            L.dfs_dense_solve_bwd.argtypes = [_I, _I, _I, _I, _F] + [_P] * 15
+            L.dfs_dense_transport_bwd.restype = ctypes.c_int
+            L.dfs_dense_transport_bwd.argtypes = [_I, _I, _I] + [_P] * 5
             L.dfs_compute_bins.restype = ctypes.c_int
             L.dfs_compute_bins.argtypes = [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]
             L.dfs_selftest_mma.restype = ctypes.c_int

@@ -191,6 +191,48 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace,
 int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a,
             void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Gradients of the dense-cost entry points ----
+ * The reference differentiates sinkhorn_solve and compute_transport_output by
+ * autograd through their dense tensor ops (src/deepfold/model/sinkhorn.py:
+ * 17-112, 115-198).  These three calls give the same gradients as explicit
+ * passes over C.  All tensors are fp32, contiguous, on the stream's device;
+ * shapes are (B,H,N,N) for C, (B,H,N) for potentials and marginals, (H,) for
+ * eps, (B,N) for mask (may be NULL).  N <= 65536.
+ *
+ * dfs_dense_iterate: iterations it_begin+1 .. it_end of sinkhorn_solve's loop
+ * (sinkhorn.py:82-96, without its early stop), every iterate kept in `hist`,
+ * (2K + 2) x B*H*N floats for K iterations in all: slot 2i holds log_u after
+ * iteration i, slot 2i+1 log_v (slot 0 / 1 the warm start, written from
+ * log_u_init / log_v_init -- zeros when NULL -- when it_begin == 0).
+ * log_u / log_v receive slot it_end with padded entries zeroed
+ * (sinkhorn.py:107-110).  change (1 float, may be NULL) receives the largest
+ * |change| of log_u and log_v in iteration it_end over the whole batch: the
+ * reference's stop test (sinkhorn.py:99-103), which the caller evaluates
+ * between calls to stop where the reference stops. */
+int dfs_dense_iterate(int B, int H, int N, float lam, const float* C, const float* eps, const float* log_mu,
+                      const float* log_nu, const float* log_u_init, const float* log_v_init, const float* mask,
+                      float* hist, int it_begin, int it_end, float* log_u, float* log_v, float* change,
+                      int32_t* status, void* stream);
+
+/* dfs_dense_solve_bwd: the adjoint of `iters` iterations recorded in hist by
+ * dfs_dense_iterate.  g_log_u / g_log_v: gradients of the returned log_u /
+ * log_v (NULL: zero).  Writes dC, dlog_mu, dlog_nu, dlog_u_init, dlog_v_init
+ * (each may be NULL when not wanted).  scratch: 3 x B*H*N floats.  eps and lam
+ * get no gradient (eps is a fixed per-head constant in the reference). */
+int dfs_dense_solve_bwd(int B, int H, int N, int iters, float lam, const float* C, const float* eps,
+                        const float* log_mu, const float* log_nu, const float* mask, const float* hist,
+                        const float* g_log_u, const float* g_log_v, float* dC, float* dlog_mu, float* dlog_nu,
+                        float* dlog_u_init, float* dlog_v_init, float* scratch, void* stream);
+
+/* dfs_dense_transport_bwd: the softmax backward of compute_transport_output's
+ * T_norm (sinkhorn.py:163-176).  dT holds dL/dT_norm (B,H,N,N) on entry -- the
+ * caller forms it from the gradients of o, x_centroid and T_norm (plain
+ * batched products with V and x_res) -- and dL/dC on return; dlog_v
+ * (may be NULL) receives dL/dlog_v.  dL/dlog_u is zero: log_u cancels in
+ * score - rowmax. */
+int dfs_dense_transport_bwd(int B, int H, int N, const float* T_norm, float* dT, const float* eps, float* dlog_v,
+                            void* stream);
+
 /* Position bins of the reference's compute_bins (src/deepfold/model/
  * position_encoding.py:7-52) into a (B,N,N) int32 table `out`:
  *   same chain, no bond: clamp(gidx_i - gidx_j, -32, 32) + 32;  other chain, no

@@ -145,3 +145,23 @@ def test_position_bin_arguments(lib):
     assert lib.dfs_compute_bins(2, 8, None, 16, 16, 16, None) == nat.DFS_ERR_INVALID_ARGUMENT
     assert lib.dfs_compute_bins(-1, 8, 16, 16, 16, 16, None) == nat.DFS_ERR_INVALID_ARGUMENT
     assert lib.dfs_compute_bins(0, 8, None, None, None, None, None) == nat.DFS_OK
+
+
+def test_dense_gradient_entry_points_validate_on_the_host(lib):
+    """The dense-gradient calls reject bad sizes and missing buffers before any
+    device work (no GPU needed)."""
+    E = nat.DFS_ERR_INVALID_ARGUMENT
+    p = 256  # any non-null address: nothing is dereferenced on these paths
+    assert lib.dfs_dense_iterate(0, 1, 8, 1.0, p, p, p, p, None, None, None, p, 0, 1, p, p, None, None, None) == E
+    assert lib.dfs_dense_iterate(1, 1, 8, 1.0, p, p, p, p, None, None, None, p, 2, 1, p, p, None, None, None) == E
+    assert lib.dfs_dense_iterate(1, 1, 1 << 17, 1.0, p, p, p, p, None, None, None, p, 0, 1, p, p, None, None,
+                                 None) == E
+    assert lib.dfs_dense_iterate(1, 1, 8, 0.0, p, p, p, p, None, None, None, p, 0, 1, p, p, None, None, None) == E
+    assert lib.dfs_dense_iterate(1, 1, 8, 1.0, p, p, p, p, None, None, None, None, 0, 1, p, p, None, None,
+                                 None) == E
+    assert lib.dfs_dense_solve_bwd(1, 1, 8, -1, 1.0, p, p, p, p, None, p, None, None, None, None, None, None, None,
+                                   p, None) == E
+    assert lib.dfs_dense_solve_bwd(1, 1, 8, 3, 1.0, p, p, p, p, None, p, None, None, None, None, None, None, None,
+                                   None, None) == E
+    assert lib.dfs_dense_transport_bwd(1, 0, 8, p, p, p, None, None) == E
+    assert lib.dfs_dense_transport_bwd(1, 1, 8, None, p, p, None, None) == E
