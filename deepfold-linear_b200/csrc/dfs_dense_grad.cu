@@ -16,19 +16,17 @@
 //   Pc_rj = exp(Y_rj - b_j + v_i,j / kappa)       (column softmax of step i)
 //   Pr_rj = exp(X_rj - a_r + u_i,r / kappa)       (row softmax of step i)
 //   gu_i,r   = [i = K] gu_up,r - kappa sum_j gv_i,j Pc_rj
-//   gv_i-1,j = [i - 1 = K] ... - kappa sum_r gu_i,r Pr_rj
+//   gv_i-1,j = -kappa sum_r gu_i,r Pr_rj         (gv_K: the upstream adjoint)
 //   dC_rj   += kappa / eps (gv_i,j Pc_rj + gu_i,r Pr_rj)
 //   dlog_mu  = kappa sum_i gu_i,   dlog_nu = kappa sum_i gv_i (i >= 1),
 //   dlog_v_init = gv_0,  dlog_u_init = 0 (u_0 is never read) unless K = 0.
-// The reverse runs as 2K HBM passes over C, alternating
-//   row pass i (one warp per row r):  gu_i from gv_i (a row reduction), and dC
-//        gets both the column-softmax term of step i and the row-softmax term
-//        of step i + 1 (known since the previous pass: it needs gu_i+1, u_i+1
-//        and v_i), so dC is read and written once per iteration -- 12 bytes
-//        per element, 8 in the first pass, which writes dC without reading it;
-//   column pass i (one CTA per 128 columns): gv_i-1 from gu_i (a column
-//        reduction), reading C only -- 4 bytes per element; the last (i = 1)
-//        also adds the row-softmax term of step 1 into dC.
+// The reverse runs as 2K passes over C that only form the adjoints -- a row
+// pass (one warp per row: gu_i from gv_i, a row reduction) and a column pass
+// (one CTA per 128 columns: gv_i-1 from gu_i), each reading C once, 4 bytes
+// per element -- and keeps every gu_i, gv_i; then one tiled pass forms
+//   dC_rj = kappa / eps sum_i (gv_i,j Pc_i,rj + gu_i,r Pr_i,rj)
+// from them, reading C and writing dC once: 2K exponentials per element, so
+// that pass is bound by the exponentials, not by HBM.
 // The upstream adjoints of the returned potentials are multiplied by the mask
 // first: the forward zeroes padded potentials after the loop.
 //
@@ -42,6 +40,11 @@
 // autograd routes to the argmax column, carries sum_j dT_rj T_rj = A 1e-6 /
 // (S + 1e-6)^2 and is dropped: a 1e-6-relative term).
 #include "dfs_kernels.cuh"
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+#include "dfs_tma.cuh"  // ex2_poly2
 
 namespace dfs {
 namespace {
@@ -83,23 +86,21 @@ struct RevArgs {
   const float* mu;      // log_mu (B,H,N)
   const float* nu;      // log_nu
   const float* mask;    // (B,N) or null
-  const float* u;       // row pass: u_i; column pass: u_i
-  const float* v;       // row pass: v_i; column pass: v_i-1
-  const float* g;       // row pass: gv_i; column pass: gu_i
+  const float* u;       // u_i
+  const float* v;       // column pass: v_i-1
+  const float* g;       // column pass: gu_i
+  const float2* yg;     // row pass: per column j of v_i, ((v_i,j / kappa - b_j) log2e, gv_i,j)
   const float* gup;     // row pass, i = K: masked upstream adjoint of u_K (else null)
-  const float* u1;      // row pass, i < K: u_i+1 (else null: no row-softmax term)
-  const float* gu1;     // row pass, i < K: gu_i+1
-  float* gout;          // row pass: gu_i; column pass: gv_i-1
-  float* dC;            // null: C needs no gradient
+  float* gout;          // row pass: gu_i; column pass: gv_i-1 as a plain vector (null: not wanted)
+  float2* ygout;        // column pass: gv_i-1 paired with v_i-1's exponent term, as yg (null: not wanted)
   float* dsum;          // row pass: dlog_mu; column pass: dlog_nu (null: not accumulated)
   int B, H, N;
   float lam;
-  int first;            // row pass: the first (i = K) -- dC and dlog_mu written, not accumulated
-  int dc_rows;          // column pass: add the row-softmax term of this step into dC (i = 1)
+  int first;            // row pass i = K: dlog_mu written, not accumulated
 };
 
-// Row pass of iteration i: one warp per row r, 16-byte loads over j when the
-// rows are 16-byte aligned.
+// Row pass of iteration i: gu_i,r = [i = K] gu_up,r - kappa sum_j gv_i,j Pc_rj,
+// one warp per row r, 16-byte loads over j when the rows are 16-byte aligned.
 template <bool VEC>
 __global__ void __launch_bounds__(kRevThreads) rev_row_kernel(const RevArgs a) {
   const int lane = threadIdx.x & 31;
@@ -110,55 +111,33 @@ __global__ void __launch_bounds__(kRevThreads) rev_row_kernel(const RevArgs a) {
   for (size_t r = warp0; r < rows; r += nwarps) {
     const size_t prob = r / N;
     const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H), i = static_cast<int>(r % N);
-    const float eps = a.eps[h], kap = kappa_of(a.lam, eps), ikap = 1.0f / kap;
-    const float sc = -kLog2e / eps, cdc = kap / eps;
-    const float rb = bias_of(a.mask, b, N, i);
-    // column-softmax exponent: C sc + (u_i,r + rb_r) log2e + (v_i,j / kappa - b_j) log2e
-    const float yr = (a.u[r] + rb) * kLog2e;
-    // row-softmax exponent of step i + 1: C sc + (v_i,j + cb_j) log2e + (u_i+1,r / kappa - a_r) log2e
-    const bool rowterm = a.u1 != nullptr;
-    const float xr = rowterm ? (a.u1[r] * ikap - a.mu[r]) * kLog2e : 0.0f;
-    const float wr = rowterm ? cdc * a.gu1[r] : 0.0f;
+    const float eps = a.eps[h], kap = kappa_of(a.lam, eps);
+    const float sc = -kLog2e / eps;
+    // exponent of Pc: C sc + (u_i,r + rb_r) log2e + (v_i,j / kappa - b_j) log2e
+    const float yr = (a.u[r] + bias_of(a.mask, b, N, i)) * kLog2e;
     const float* c = a.C + r * N;
-    float* dc = a.dC == nullptr ? nullptr : a.dC + r * N;
-    const float* v = a.v + prob * N;
-    const float* nu = a.nu + prob * N;
-    const float* gv = a.g + prob * N;
-    const float* mk = a.mask == nullptr ? nullptr : a.mask + static_cast<size_t>(b) * N;
+    const float* yg = reinterpret_cast<const float*>(a.yg + prob * N);  // (y, g) pairs
     float acc = 0.0f;
-    auto elem = [&](float cj, float vj, float nj, float gj, float cbj, float& dcj) {
-      const float base = cj * sc;
-      const float pc = ex2c(base + fmaf(vj * ikap - nj, kLog2e, yr));
-      const float t = gj * pc;
-      acc += t;
-      float d = cdc * t;
-      if (rowterm) d = fmaf(wr, ex2c(base + fmaf(vj + cbj, kLog2e, xr)), d);
-      dcj = a.first ? d : dcj + d;
-    };
+    auto elem = [&](float cj, float yj, float gj) { acc = fmaf(gj, ex2c(fmaf(cj, sc, yj + yr)), acc); };
     if constexpr (VEC) {
-      for (int j = 4 * lane; j < N; j += 128) {
-        const float4 cv = __ldcs(reinterpret_cast<const float4*>(c + j));
-        const float4 vv = ld4(v + j), nv = ld4(nu + j), gw = ld4(gv + j);
-        float4 cb = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (mk != nullptr) {
-          const float4 m = ld4(mk + j);
-          cb = make_float4((1.0f - m.x) * kMaskBias, (1.0f - m.y) * kMaskBias, (1.0f - m.z) * kMaskBias,
-                           (1.0f - m.w) * kMaskBias);
-        }
-        float4 dv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (dc != nullptr && !a.first) dv = __ldcs(reinterpret_cast<const float4*>(dc + j));
-        elem(cv.x, vv.x, nv.x, gw.x, cb.x, dv.x);
-        elem(cv.y, vv.y, nv.y, gw.y, cb.y, dv.y);
-        elem(cv.z, vv.z, nv.z, gw.z, cb.z, dv.z);
-        elem(cv.w, vv.w, nv.w, gw.w, cb.w, dv.w);
-        if (dc != nullptr) __stcs(reinterpret_cast<float4*>(dc + j), dv);
+      auto group = [&](const float4& cv, int j) {
+        const float4 p0 = ld4(yg + 2 * j), p1 = ld4(yg + 2 * j + 4);
+        elem(cv.x, p0.x, p0.y);
+        elem(cv.y, p0.z, p0.w);
+        elem(cv.z, p1.x, p1.y);
+        elem(cv.w, p1.z, p1.w);
+      };
+      int j = 4 * lane;
+      for (; j + 384 < N; j += 512) {  // four 16-byte loads of C in flight per lane
+        float4 cv[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) cv[q] = __ldcs(reinterpret_cast<const float4*>(c + j + 128 * q));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) group(cv[q], j + 128 * q);
       }
+      for (; j < N; j += 128) group(__ldcs(reinterpret_cast<const float4*>(c + j)), j);
     } else {
-      for (int j = lane; j < N; j += 32) {
-        float dv = (dc != nullptr && !a.first) ? dc[j] : 0.0f;
-        elem(__ldcs(c + j), v[j], nu[j], gv[j], bias_of(a.mask, b, N, j), dv);
-        if (dc != nullptr) dc[j] = dv;
-      }
+      for (int j = lane; j < N; j += 32) elem(__ldcs(c + j), yg[2 * j], yg[2 * j + 1]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -170,9 +149,9 @@ __global__ void __launch_bounds__(kRevThreads) rev_row_kernel(const RevArgs a) {
   }
 }
 
-// Column pass of iteration i: CTA = COLS columns of one problem, warp w takes
-// rows w, w + 8, ...; per-column partial sums added over the warps in a fixed
-// order (deterministic).
+// Column pass of iteration i: gv_i-1,j = -kappa sum_r gu_i,r Pr_rj.  CTA = COLS
+// columns of one problem, warp w takes rows w, w + 8, ...; per-column partial
+// sums added over the warps in a fixed order (deterministic).
 template <bool VEC>
 __global__ void __launch_bounds__(kRevThreads) rev_col_kernel(const RevArgs a) {
   constexpr int COLS = VEC ? 128 : 32, PER = VEC ? 4 : 1;
@@ -184,7 +163,7 @@ __global__ void __launch_bounds__(kRevThreads) rev_col_kernel(const RevArgs a) {
   const int j0 = (blockIdx.x % cblocks) * COLS;
   const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
   const float eps = a.eps[h], kap = kappa_of(a.lam, eps), ikap = 1.0f / kap;
-  const float sc = -kLog2e / eps, cdc = kap / eps;
+  const float sc = -kLog2e / eps;
   const int j = j0 + PER * lane;
   float cb[PER], acc[PER];
 #pragma unroll
@@ -192,39 +171,34 @@ __global__ void __launch_bounds__(kRevThreads) rev_col_kernel(const RevArgs a) {
     cb[q] = (j + q < N) ? (a.v[prob * N + j + q] + bias_of(a.mask, b, N, j + q)) * kLog2e : 0.0f;
     acc[q] = 0.0f;
   }
-  float* dcb = a.dc_rows && a.dC != nullptr ? a.dC + prob * N * static_cast<size_t>(N) + j : nullptr;
   if (j < N) {
     const float* cbase = a.C + prob * N * static_cast<size_t>(N) + j;
     const float* ur = a.u + prob * N;
     const float* mur = a.mu + prob * N;
     const float* gur = a.g + prob * N;
-    for (int i = warp; i < N; i += 8) {
+    auto row = [&](int i, const float4& cv) {
       const float gu = gur[i];
       const float xr = (ur[i] * ikap - mur[i]) * kLog2e;  // u_i,r / kappa - a_r
-      const size_t off = static_cast<size_t>(i) * N;
+      acc[0] = fmaf(gu, ex2c(fmaf(cv.x, sc, cb[0]) + xr), acc[0]);
       if constexpr (VEC) {
-        const float4 cv = __ldcs(reinterpret_cast<const float4*>(cbase + off));
-        const float p0 = ex2c(fmaf(cv.x, sc, cb[0]) + xr), p1 = ex2c(fmaf(cv.y, sc, cb[1]) + xr);
-        const float p2 = ex2c(fmaf(cv.z, sc, cb[2]) + xr), p3 = ex2c(fmaf(cv.w, sc, cb[3]) + xr);
-        acc[0] = fmaf(gu, p0, acc[0]);
-        acc[1] = fmaf(gu, p1, acc[1]);
-        acc[2] = fmaf(gu, p2, acc[2]);
-        acc[3] = fmaf(gu, p3, acc[3]);
-        if (dcb != nullptr) {
-          const float w = cdc * gu;
-          float4 dv = __ldcs(reinterpret_cast<const float4*>(dcb + off));
-          dv.x = fmaf(w, p0, dv.x);
-          dv.y = fmaf(w, p1, dv.y);
-          dv.z = fmaf(w, p2, dv.z);
-          dv.w = fmaf(w, p3, dv.w);
-          __stcs(reinterpret_cast<float4*>(dcb + off), dv);
-        }
-      } else {
-        const float p = ex2c(fmaf(__ldcs(cbase + off), sc, cb[0]) + xr);
-        acc[0] = fmaf(gu, p, acc[0]);
-        if (dcb != nullptr) dcb[off] = fmaf(cdc * gu, p, dcb[off]);
+        acc[1] = fmaf(gu, ex2c(fmaf(cv.y, sc, cb[1]) + xr), acc[1]);
+        acc[2] = fmaf(gu, ex2c(fmaf(cv.z, sc, cb[2]) + xr), acc[2]);
+        acc[3] = fmaf(gu, ex2c(fmaf(cv.w, sc, cb[3]) + xr), acc[3]);
       }
+    };
+    auto load = [&](int i) {
+      if constexpr (VEC) return __ldcs(reinterpret_cast<const float4*>(cbase + static_cast<size_t>(i) * N));
+      else return make_float4(__ldcs(cbase + static_cast<size_t>(i) * N), 0.0f, 0.0f, 0.0f);
+    };
+    int i = warp;
+    for (; i + 24 < N; i += 32) {  // four row segments in flight per thread
+      float4 cv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) cv[u] = load(i + 8 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) row(i + 8 * u, cv[u]);
     }
+    for (; i < N; i += 8) row(i, load(i));
   }
 #pragma unroll
   for (int q = 0; q < PER; ++q) sacc[warp][PER * lane + q] = acc[q];
@@ -236,9 +210,404 @@ __global__ void __launch_bounds__(kRevThreads) rev_col_kernel(const RevArgs a) {
     for (int w = 0; w < 8; ++w) sum += sacc[w][t];
     const float gv = -kap * sum;
     const size_t o = prob * N + jj;
-    a.gout[o] = gv;
+    if (a.gout != nullptr) a.gout[o] = gv;
+    if (a.ygout != nullptr) a.ygout[o] = make_float2((a.v[o] * ikap - a.nu[o]) * kLog2e, gv);
     if (a.dsum != nullptr) a.dsum[o] += kap * gv;
   }
+}
+
+// The cost gradient from every iteration's adjoints at once (after the reverse
+// passes): dC_rj = sum_i w_i,j Pc_i,rj + w'_i,r Pr_i,rj over i = 1 .. K, with
+// the per-row and per-column parts of each exponent and weight staged in
+// shared memory.  A CTA takes a 64 x 64 tile of one problem, thread t the
+// rows 4 (t / 16) .. + 3 and columns 4 (t % 16) .. + 3 (16-byte loads and
+// stores of C and dC), and walks the iterations in chunks of kDcChunk.  Each
+// element costs 2K exponentials and one read of C and one write of dC, so the
+// pass is bound by the exponentials: pairs of elements run on the packed fp32
+// instructions, and the exponentials of the pairs kDcPolyPairs selects are
+// evaluated on the FMA pipes (ex2_poly2) instead of the MUFU.
+constexpr int kDcTile = 64, kDcChunk = 16;
+// POLY: bit p (of the 8 element pairs of a term) puts pair p's exponentials on
+// the FMA pipes.  The default share is set from a sweep on the B200; the
+// environment variable DFS_DC_POLY (0, 2, 3 or 4 pairs of 8) overrides it.
+constexpr int kDcPolyDefault = 0;
+
+struct DcArgs {
+  const float* C;
+  const float* eps;
+  const float* mu;
+  const float* nu;
+  const float* mask;
+  const float* hist;   // slot 2i = u_i, 2i + 1 = v_i
+  const float* gu;     // gu_i at gu + (i - 1) ns, i = 1 .. K
+  const float* gv;     // (y, gv_i) pairs: gv_i,o at gv[2 ((i - 1) ns + o) + 1]
+  size_t ns;           // stride of the scratch slots (floats; n rounded up to 64)
+  float* dC;
+  int B, H, N, K;
+  float lam;
+  const float* shift;  // factored pass: s, s', t, t' planes of ns floats (row / column maxima, log2 units)
+  const unsigned* rng; // factored pass: per problem 4 largest ranges (float bits); null: exact pass only
+  const float* fac;    // factored pass: A, A', B, B' planes of K x ns floats (iteration i at (i - 1) ns)
+};
+
+// Each term of the cost gradient factors over rows and columns:
+//   Pc_i,rj = exp2(c_rj sc) 2^(U_i,r) 2^(Vc_i,j),  Pr_i,rj = exp2(c_rj sc) 2^(Ur_i,r) 2^(Vr_i,j),
+// so dC_rj = exp2(c sc + s_r + t_j) sum_i A_i,r B_i,j + exp2(c sc + s'_r + t'_j) sum_i A'_i,r B'_i,j
+// with A = 2^(U - s), B = w 2^(Vc - t), A' = w' 2^(Ur - s'), B' = 2^(Vr - t'), the shifts s, t
+// (s', t') each row's / column's maximum over the iterations: a rank-2K product, 2K FMAs and two
+// exponentials per element instead of 2K exponentials.  Every factor lies in [2^-range, 1] (times
+// its weight); while the largest row range plus the largest column range of a problem stays within
+// kDcRange, no factor or product leaves the normal fp32 range and the final scale stays below
+// 2^kDcRange (the largest term of each kind is <= 1: a softmax weight).  Problems beyond it (far
+// from converged potentials at a tiny eps) take the exact pass.
+constexpr float kDcRange = 64.0f;
+
+__device__ __forceinline__ bool dc_fast(const unsigned* r) {
+  return __uint_as_float(r[0]) + __uint_as_float(r[2]) <= kDcRange &&
+         __uint_as_float(r[1]) + __uint_as_float(r[3]) <= kDcRange;  // NaN: exact pass
+}
+
+// Shifts, ranges and factors: one thread per (problem, row) and per (problem,
+// column); padded points get shift 0 and factors 0 and take no part in the
+// ranges.  The ranges are reduced over the warp before the atomic when the
+// whole warp holds one problem's rows (or columns).
+__global__ void dc_factor_kernel(const DcArgs a, float* shift, unsigned* rng, float* fac) {
+  const int N = a.N;
+  const size_t n = static_cast<size_t>(a.B) * a.H * N;
+  const size_t kn = static_cast<size_t>(a.K) * a.ns;
+  const size_t total = 2 * n, stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t span = (total + stride - 1) / stride * stride;  // every lane runs the same trip count
+  for (size_t e = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < span; e += stride) {
+    const bool live = e < total;
+    const bool row = e < n;
+    const size_t o = live ? (row ? e : e - n) : 0;
+    const size_t prob = o / N;
+    const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H), q = static_cast<int>(o % N);
+    const float kap = kappa_of(a.lam, a.eps[h]), ikap = 1.0f / kap, cdc = kap / a.eps[h];
+    const bool valid = live && (a.mask == nullptr || a.mask[static_cast<size_t>(b) * N + q] != 0.0f);
+    // row: x0 = U = u_i log2e, x1 = Ur = (u_i / kappa - a) log2e; column: x0 = Vc = (v_i / kappa - b) log2e,
+    // x1 = Vr = v_i-1 log2e (the mask biases are 0 on valid points)
+    auto xs = [&](int i, float& x0, float& x1) {
+      if (row) {
+        const float u = a.hist[static_cast<size_t>(2 * i) * n + o];
+        x0 = u * kLog2e;
+        x1 = (u * ikap - a.mu[o]) * kLog2e;
+      } else {
+        x0 = (a.hist[static_cast<size_t>(2 * i + 1) * n + o] * ikap - a.nu[o]) * kLog2e;
+        x1 = a.hist[static_cast<size_t>(2 * i - 1) * n + o] * kLog2e;
+      }
+    };
+    float m0 = -INFINITY, l0 = INFINITY, m1 = -INFINITY, l1 = INFINITY;
+    if (valid) {
+      for (int i = 1; i <= a.K; ++i) {
+        float x0, x1;
+        xs(i, x0, x1);
+        m0 = fmaxf(m0, x0);
+        l0 = fminf(l0, x0);
+        m1 = fmaxf(m1, x1);
+        l1 = fminf(l1, x1);
+      }
+    }
+    if (live) {
+      shift[(row ? 0 : 2) * a.ns + o] = valid ? m0 : 0.0f;
+      shift[(row ? 1 : 3) * a.ns + o] = valid ? m1 : 0.0f;
+      // factors: rows A = 2^(U - s), A' = w' 2^(Ur - s'); columns B = w 2^(Vc - t), B' = 2^(Vr - t')
+      float* f0 = fac + (row ? 0 : 2) * kn + o;
+      float* f1 = fac + (row ? 1 : 3) * kn + o;
+      for (int i = 1; i <= a.K; ++i) {
+        float v0 = 0.0f, v1 = 0.0f;
+        if (valid) {
+          float x0, x1;
+          xs(i, x0, x1);
+          const size_t so = static_cast<size_t>(i - 1) * a.ns + o;
+          const float w = cdc * (row ? a.gu[so] : a.gv[2 * so + 1]);
+          v0 = ex2f(x0 - m0);
+          v1 = ex2f(x1 - m1);
+          if (row) v1 *= w;
+          else v0 *= w;
+        }
+        f0[static_cast<size_t>(i - 1) * a.ns] = v0;
+        f1[static_cast<size_t>(i - 1) * a.ns] = v1;
+      }
+    }
+    // ranges: >= 0, or NaN / inf for non-finite potentials (kept as +inf: the exact pass)
+    const float r0 = m0 - l0, r1 = m1 - l1;
+    unsigned u0 = valid ? (isnan(r0) ? 0x7f800000u : __float_as_uint(r0)) : 0u;
+    unsigned u1 = valid ? (isnan(r1) ? 0x7f800000u : __float_as_uint(r1)) : 0u;
+    const unsigned long long key = live ? prob * 2 + (row ? 0 : 1) : ~0ull;
+    const unsigned long long key0 = __shfl_sync(0xffffffffu, key, 0);
+    if (__all_sync(0xffffffffu, key == key0)) {
+      u0 = __reduce_max_sync(0xffffffffu, u0);
+      u1 = __reduce_max_sync(0xffffffffu, u1);
+      if ((threadIdx.x & 31) == 0 && live && (u0 | u1)) {
+        atomicMax(rng + 4 * prob + (row ? 0 : 2), u0);
+        atomicMax(rng + 4 * prob + (row ? 1 : 3), u1);
+      }
+    } else if (valid) {
+      atomicMax(rng + 4 * prob + (row ? 0 : 2), u0);
+      atomicMax(rng + 4 * prob + (row ? 1 : 3), u1);
+    }
+  }
+}
+
+// The factored cost-gradient pass: same tiles and thread layout as the exact
+// pass below, the factors of kDcChunk iterations staged per chunk.
+template <bool VEC>
+__global__ void __launch_bounds__(256, 3) dense_dc_fact_kernel(const DcArgs a) {
+  __shared__ float4 srow[2][kDcChunk][kDcTile / 4];  // A, A' for 64 rows
+  __shared__ float4 scol[2][kDcChunk][kDcTile / 4];  // B, B' for 64 columns
+  const int N = a.N;
+  const int tiles = (N + kDcTile - 1) / kDcTile;
+  const size_t prob = blockIdx.x / (static_cast<size_t>(tiles) * tiles);
+  if (!dc_fast(a.rng + 4 * prob)) return;  // uniform over the CTA: the exact pass takes this problem
+  const int tr = static_cast<int>((blockIdx.x / tiles) % tiles), tc = static_cast<int>(blockIdx.x % tiles);
+  const int r0 = tr * kDcTile, c0 = tc * kDcTile;
+  const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
+  const float sc = -kLog2e / a.eps[h];
+  const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+  const int row0 = r0 + 4 * rg, col0 = c0 + 4 * cg;
+  const float* mk = a.mask == nullptr ? nullptr : a.mask + static_cast<size_t>(b) * N;
+  float2 acc1[4][2], acc2[4][2];
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) acc1[rr][0] = acc1[rr][1] = acc2[rr][0] = acc2[rr][1] = make_float2(0.0f, 0.0f);
+  // the tile of C, read first so that its HBM latency overlaps the staging and the products
+  const float* cbase = a.C + prob * static_cast<size_t>(N) * N;
+  float c[4][4];
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = row0 + rr;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) c[rr][cc] = 0.0f;
+    if constexpr (VEC) {
+      if (r < N && col0 < N) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(cbase + static_cast<size_t>(r) * N + col0));
+        c[rr][0] = v.x, c[rr][1] = v.y, c[rr][2] = v.z, c[rr][3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        if (r < N && col0 + cc < N) c[rr][cc] = __ldcs(cbase + static_cast<size_t>(r) * N + col0 + cc);
+    }
+  }
+  const size_t kn = static_cast<size_t>(a.K) * a.ns;
+  for (int i0 = 1; i0 <= a.K; i0 += kDcChunk) {
+    const int nk = min(kDcChunk, a.K - i0 + 1);
+    __syncthreads();
+    // copy the chunk's factors: plane pl (A, A', B, B'), iteration k, 64 rows or columns
+    if constexpr (VEC) {
+      for (int e = threadIdx.x; e < 4 * kDcChunk * (kDcTile / 4); e += 256) {
+        const int pl = e / (kDcChunk * (kDcTile / 4)), rem = e % (kDcChunk * (kDcTile / 4));
+        const int k = rem / (kDcTile / 4), p4 = rem % (kDcTile / 4);
+        const int q = (pl < 2 ? r0 : c0) + 4 * p4;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k < nk && q < N)
+          v = *reinterpret_cast<const float4*>(a.fac + pl * kn + static_cast<size_t>(i0 + k - 1) * a.ns + prob * N + q);
+        (pl < 2 ? srow[pl][k] : scol[pl - 2][k])[p4] = v;
+      }
+    } else {
+      for (int e = threadIdx.x; e < 4 * kDcChunk * kDcTile; e += 256) {
+        const int pl = e / (kDcChunk * kDcTile), rem = e % (kDcChunk * kDcTile);
+        const int k = rem / kDcTile, p = rem % kDcTile;
+        const int q = (pl < 2 ? r0 : c0) + p;
+        const float v = (k < nk && q < N) ? a.fac[pl * kn + static_cast<size_t>(i0 + k - 1) * a.ns + prob * N + q] : 0.0f;
+        reinterpret_cast<float*>(pl < 2 ? &srow[pl][k][0] : &scol[pl - 2][k][0])[p] = v;
+      }
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int k = 0; k < nk; ++k) {
+      const float4 A = srow[0][k][rg], A1 = srow[1][k][rg];
+      const float4 Bv = scol[0][k][cg], B1 = scol[1][k][cg];
+      const float Aa[4] = {A.x, A.y, A.z, A.w}, A1a[4] = {A1.x, A1.y, A1.z, A1.w};
+      const float2 bp[2] = {make_float2(Bv.x, Bv.y), make_float2(Bv.z, Bv.w)};
+      const float2 b1p[2] = {make_float2(B1.x, B1.y), make_float2(B1.z, B1.w)};
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          acc1[rr][h2] = __ffma2_rn(make_float2(Aa[rr], Aa[rr]), bp[h2], acc1[rr][h2]);
+          acc2[rr][h2] = __ffma2_rn(make_float2(A1a[rr], A1a[rr]), b1p[h2], acc2[rr][h2]);
+        }
+    }
+  }
+  // scale by exp2(c sc + shifts) and store; padded rows / columns exactly 0
+  float* dbase = a.dC + prob * static_cast<size_t>(N) * N;
+  float t0[4], t1[4];
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    const int j = col0 + cc;
+    t0[cc] = j < N ? a.shift[2 * a.ns + prob * N + j] : 0.0f;
+    t1[cc] = j < N ? a.shift[3 * a.ns + prob * N + j] : 0.0f;
+  }
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = row0 + rr;
+    if (r >= N) continue;
+    const float s0 = a.shift[prob * N + r], s1 = a.shift[a.ns + prob * N + r];
+    const bool rok = mk == nullptr || mk[r] != 0.0f;
+    const float p1[4] = {acc1[rr][0].x, acc1[rr][0].y, acc1[rr][1].x, acc1[rr][1].y};
+    const float p2[4] = {acc2[rr][0].x, acc2[rr][0].y, acc2[rr][1].x, acc2[rr][1].y};
+    float out[4];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const int j = col0 + cc;
+      const bool ok = rok && j < N && (mk == nullptr || mk[j] != 0.0f);
+      const float base = c[rr][cc] * sc;
+      const float v = ex2f(fminf(base + s0 + t0[cc], 126.0f)) * p1[cc] + ex2f(fminf(base + s1 + t1[cc], 126.0f)) * p2[cc];
+      out[cc] = ok ? v : 0.0f;
+    }
+    if constexpr (VEC) {
+      if (col0 < N)
+        __stcs(reinterpret_cast<float4*>(dbase + static_cast<size_t>(r) * N + col0),
+               make_float4(out[0], out[1], out[2], out[3]));
+    } else {
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        if (col0 + cc < N) dbase[static_cast<size_t>(r) * N + col0 + cc] = out[cc];
+    }
+  }
+}
+
+__device__ __forceinline__ float2 ex2c2(float2 x, bool poly) {
+  x.x = fminf(x.x, 64.0f);
+  x.y = fminf(x.y, 64.0f);
+  if (poly) return ex2_poly2(x);
+  return make_float2(ex2f(x.x), ex2f(x.y));
+}
+
+template <bool VEC, unsigned POLY>
+__global__ void __launch_bounds__(256) dense_dc_kernel(const DcArgs a) {
+  __shared__ float4 srow[3][kDcChunk][kDcTile / 4];  // U, Ur, w' for 64 rows (4 per float4)
+  __shared__ float4 scol[3][kDcChunk][kDcTile / 4];  // Vc, Vr, w for 64 columns
+  const int N = a.N;
+  const int tiles = (N + kDcTile - 1) / kDcTile;
+  const size_t total = static_cast<size_t>(a.B) * a.H * tiles * tiles;
+  // grid-stride over the tiles (a few CTAs per SM): the tiles of problems the
+  // factored pass takes are skipped without a CTA launch each
+  for (size_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
+  const size_t prob = tile / (static_cast<size_t>(tiles) * tiles);
+  if (a.rng != nullptr && dc_fast(a.rng + 4 * prob)) continue;  // uniform over the CTA: the factored pass has it
+  const int tr = static_cast<int>((tile / tiles) % tiles), tc = static_cast<int>(tile % tiles);
+  const int r0 = tr * kDcTile, c0 = tc * kDcTile;
+  const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
+  const float eps = a.eps[h], kap = kappa_of(a.lam, eps), ikap = 1.0f / kap;
+  const float sc = -kLog2e / eps, cdc = kap / eps;
+  const size_t n = static_cast<size_t>(a.B) * a.H * N;
+  const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+  const int row0 = r0 + 4 * rg, col0 = c0 + 4 * cg;
+  const float* cbase = a.C + prob * static_cast<size_t>(N) * N;
+  // base exponents c sc of the thread's 4 x 4 elements, -inf outside the problem
+  float2 base[4][2], acc[4][2];
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = row0 + rr;
+    float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if constexpr (VEC) {
+      if (r < N && col0 < N) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(cbase + static_cast<size_t>(r) * N + col0));
+        c[0] = v.x, c[1] = v.y, c[2] = v.z, c[3] = v.w;
+      }
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const int j = col0 + cc;
+      if constexpr (!VEC) {
+        if (r < N && j < N) c[cc] = __ldcs(cbase + static_cast<size_t>(r) * N + j);
+      }
+      const float x = (r < N && j < N) ? c[cc] * sc : -INFINITY;
+      if (cc & 1) base[rr][cc >> 1].y = x;
+      else base[rr][cc >> 1].x = x;
+    }
+    acc[rr][0] = acc[rr][1] = make_float2(0.0f, 0.0f);
+  }
+  for (int i0 = 1; i0 <= a.K; i0 += kDcChunk) {
+    const int nk = min(kDcChunk, a.K - i0 + 1);
+    __syncthreads();  // the previous chunk's reads are done
+    // stage: thread t fills one (term, row / column) entry per step
+    for (int e = threadIdx.x; e < 2 * kDcChunk * kDcTile; e += 256) {
+      const int side = e / (kDcChunk * kDcTile), rem = e % (kDcChunk * kDcTile);
+      const int k = rem / kDcTile, p = rem % kDcTile;
+      float x0 = 0.0f, x1 = 0.0f, x2 = 0.0f;
+      const int q = (side == 0 ? r0 : c0) + p;
+      if (k < nk && q < N) {
+        const int i = i0 + k;
+        const size_t o = prob * N + q;
+        const float bias = bias_of(a.mask, b, N, q);
+        if (side == 0) {  // row r = q: U = (u_i + rb) log2e, Ur = (u_i / kappa - a) log2e, w' = kappa / eps gu_i
+          const float u = a.hist[static_cast<size_t>(2 * i) * n + o];
+          x0 = (u + bias) * kLog2e;
+          x1 = (u * ikap - a.mu[o]) * kLog2e;
+          x2 = cdc * a.gu[static_cast<size_t>(i - 1) * a.ns + o];
+        } else {          // column j = q: Vc = (v_i / kappa - b) log2e, Vr = (v_i-1 + cb) log2e, w = kappa / eps gv_i
+          const float v = a.hist[static_cast<size_t>(2 * i + 1) * n + o];
+          x0 = (v * ikap - a.nu[o]) * kLog2e;
+          x1 = (a.hist[static_cast<size_t>(2 * i - 1) * n + o] + bias) * kLog2e;
+          x2 = cdc * a.gv[2 * (static_cast<size_t>(i - 1) * a.ns + o) + 1];
+        }
+      }
+      float* dst = reinterpret_cast<float*>(side == 0 ? &srow[0][k][0] : &scol[0][k][0]);
+      const size_t plane = static_cast<size_t>(kDcChunk) * kDcTile;  // floats per value plane
+      dst[p] = x0;
+      dst[plane + p] = x1;
+      dst[2 * plane + p] = x2;
+    }
+    __syncthreads();
+    for (int k = 0; k < nk; ++k) {
+      const float4 U = srow[0][k][rg], Ur = srow[1][k][rg], Wr = srow[2][k][rg];
+      const float4 Vc = scol[0][k][cg], Vr = scol[1][k][cg], Wc = scol[2][k][cg];
+      const float Ua[4] = {U.x, U.y, U.z, U.w}, Ura[4] = {Ur.x, Ur.y, Ur.z, Ur.w};
+      const float Wra[4] = {Wr.x, Wr.y, Wr.z, Wr.w};
+      const float2 vc[2] = {make_float2(Vc.x, Vc.y), make_float2(Vc.z, Vc.w)};
+      const float2 vr[2] = {make_float2(Vr.x, Vr.y), make_float2(Vr.z, Vr.w)};
+      const float2 wc[2] = {make_float2(Wc.x, Wc.y), make_float2(Wc.z, Wc.w)};
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int pair = rr * 2 + h2;  // 8 pairs per term
+          // column-softmax term: exp2(c sc + U_r + Vc_j) weighted by w_j
+          const float2 xc = __fadd2_rn(base[rr][h2], __fadd2_rn(make_float2(Ua[rr], Ua[rr]), vc[h2]));
+          const float2 pc = ex2c2(xc, (POLY >> pair) & 1u);
+          acc[rr][h2] = __ffma2_rn(wc[h2], pc, acc[rr][h2]);
+          // row-softmax term: exp2(c sc + Ur_r + Vr_j) weighted by w'_r
+          const float2 xr = __fadd2_rn(base[rr][h2], __fadd2_rn(make_float2(Ura[rr], Ura[rr]), vr[h2]));
+          const float2 pr = ex2c2(xr, (POLY >> (pair ^ 1)) & 1u);
+          acc[rr][h2] = __ffma2_rn(make_float2(Wra[rr], Wra[rr]), pr, acc[rr][h2]);
+        }
+      }
+    }
+  }
+  // padded rows and columns: exactly 0, as autograd gives them (their terms are
+  // 0 or, on the FMA pipes, 2^-125-sized)
+  if (a.mask != nullptr) {
+    const float* mk = a.mask + static_cast<size_t>(b) * N;
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int r = row0 + rr, j = col0 + cc;
+        const bool keep = r < N && j < N && mk[r] != 0.0f && mk[j] != 0.0f;
+        float2& x = acc[rr][cc >> 1];
+        if (!keep) (cc & 1 ? x.y : x.x) = 0.0f;
+      }
+  }
+  float* dbase = a.dC + prob * static_cast<size_t>(N) * N;
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) {
+    const int r = row0 + rr;
+    if (r >= N) continue;
+    if constexpr (VEC) {
+      if (col0 < N)
+        __stcs(reinterpret_cast<float4*>(dbase + static_cast<size_t>(r) * N + col0),
+               make_float4(acc[rr][0].x, acc[rr][0].y, acc[rr][1].x, acc[rr][1].y));
+    } else {
+      const float v[4] = {acc[rr][0].x, acc[rr][0].y, acc[rr][1].x, acc[rr][1].y};
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        if (col0 + cc < N) dbase[static_cast<size_t>(r) * N + col0 + cc] = v[cc];
+    }
+  }
+  }  // tiles
 }
 
 // u_0, v_0 of the history from the warm start (zeros without one)
@@ -378,17 +747,38 @@ __global__ void __launch_bounds__(kRevThreads) tbwd_col_kernel(const float* dC, 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Scratch of the reverse (floats), slots of ns = n rounded up to 64 floats
+// (every slot 256-byte aligned): gu_i (iters slots), (y, gv_i) pairs (2 iters),
+// the masked upstream adjoint of u_K (1), the factored pass's shifts (4) and
+// factors (4 iters), then 4 x BH per-problem ranges.
+size_t dense_bwd_slot(size_t n) { return (n + 63) / 64 * 64; }
+size_t dense_bwd_scratch_floats(int B, int H, int N, int iters) {
+  const size_t n = static_cast<size_t>(B) * H * N;
+  return static_cast<size_t>(7 * iters + 5) * dense_bwd_slot(n) + 4 * static_cast<size_t>(B) * H;
+}
+
+// ((v_K / kappa - b) log2e, gv_K) pairs from the masked upstream adjoint of v_K; dlog_nu = kappa gv_K
+__global__ void ygv_init_kernel(const float* g, const float* vK, const float* nu, const float* mask, const float* eps,
+                                float lam, int H, int N, size_t n, float2* yg, float* dnu) {
+  for (size_t k = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+       k += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t bh = k / N;
+    const float m = mask != nullptr ? mask[(bh / H) * N + k % N] : 1.0f;
+    const float kap = kappa_of(lam, eps[bh % H]);
+    const float x = g != nullptr ? g[k] * m : 0.0f;
+    yg[k] = make_float2((vK[k] / kap - nu[k]) * kLog2e, x);
+    if (dnu != nullptr) dnu[k] = kap * x;
+  }
+}
+
 }  // namespace
 
-// The reverse of iterations iters .. 1 (scratch: 3 x BH x N floats -- gv, and gu
-// for two consecutive iterations, since a row pass reads gu_i+1 while it writes gu_i).
 cudaError_t launch_dense_solve_bwd(int B, int H, int N, int iters, float lam, const float* C, const float* eps,
                                    const float* mu, const float* nu, const float* mask, const float* hist,
                                    const float* g_lu, const float* g_lv, float* dC, float* dmu, float* dnu,
                                    float* dlui, float* dlvi, float* scratch, cudaStream_t st) {
   const size_t n = static_cast<size_t>(B) * H * N;
-  float* gv = scratch;
-  float* gu[2] = {scratch + n, scratch + 2 * n};
+  const size_t ns = dense_bwd_slot(n);
   const unsigned ge = grid_for(n, 256);
   cudaError_t e = cudaSuccess;
   if (iters == 0) {  // the outputs are the (masked) warm start itself
@@ -399,18 +789,19 @@ cudaError_t launch_dense_solve_bwd(int B, int H, int N, int iters, float lam, co
     if (dnu && (e = cudaMemsetAsync(dnu, 0, n * sizeof(float), st)) != cudaSuccess) return e;
     return cudaGetLastError();
   }
-  // gv_K = the masked upstream adjoint of v_K, dlog_nu = kappa gv_K; gu_up masked into gu[1]
-  masked_adjoint_kernel<<<ge, 256, 0, st>>>(g_lv, mask, eps, lam, H, N, n, gv, dnu);
-  masked_adjoint_kernel<<<ge, 256, 0, st>>>(g_lu, mask, eps, lam, H, N, n, gu[iters & 1 ? 0 : 1], nullptr);
+  auto gu = [&](int i) { return scratch + static_cast<size_t>(i - 1) * ns; };
+  auto gvy = [&](int i) { return reinterpret_cast<float2*>(scratch + static_cast<size_t>(iters + 2 * (i - 1)) * ns); };
+  float* gup = scratch + static_cast<size_t>(3 * iters) * ns;
+  auto slot = [&](int k) { return hist + static_cast<size_t>(k) * n; };
+  ygv_init_kernel<<<ge, 256, 0, st>>>(g_lv, slot(2 * iters + 1), nu, mask, eps, lam, H, N, n, gvy(iters), dnu);
+  masked_adjoint_kernel<<<ge, 256, 0, st>>>(g_lu, mask, eps, lam, H, N, n, gup, nullptr);
   if (dlui && (e = cudaMemsetAsync(dlui, 0, n * sizeof(float), st)) != cudaSuccess) return e;
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const bool vec = (N % 4) == 0 && aligned16(C) && (dC == nullptr || aligned16(dC));
   const unsigned grow = grid_for(n, kRevThreads / 32);
   const int cols = vec ? 128 : 32;
   const unsigned gcol = static_cast<unsigned>(B) * H * static_cast<unsigned>((N + cols - 1) / cols);
-  auto slot = [&](int k) { return hist + static_cast<size_t>(k) * n; };
   for (int i = iters; i >= 1 && e == cudaSuccess; --i) {
-    // gu_i goes to gu[i & 1]; gu_i+1 (or the masked upstream at i = K) sits in gu[(i + 1) & 1]
     RevArgs a{};
     a.C = C;
     a.eps = eps;
@@ -421,33 +812,66 @@ cudaError_t launch_dense_solve_bwd(int B, int H, int N, int iters, float lam, co
     a.H = H;
     a.N = N;
     a.lam = lam;
-    a.dC = dC;
+    // row pass: gu_i from gv_i
     a.u = slot(2 * i);
-    a.v = slot(2 * i + 1);
-    a.g = gv;
-    a.gup = i == iters ? gu[(i + 1) & 1] : nullptr;
-    a.u1 = i == iters ? nullptr : slot(2 * i + 2);
-    a.gu1 = i == iters ? nullptr : gu[(i + 1) & 1];
-    a.gout = gu[i & 1];
+    a.yg = gvy(i);
+    a.gup = i == iters ? gup : nullptr;
+    a.gout = gu(i);
     a.dsum = dmu;
     a.first = i == iters;
     if (vec) rev_row_kernel<true><<<grow, kRevThreads, 0, st>>>(a);
     else rev_row_kernel<false><<<grow, kRevThreads, 0, st>>>(a);
-    // column pass: gv_i-1 from gu_i; the adjoint of the warm start at i = 1
+    // column pass: gv_i-1 from gu_i (the adjoint of the warm start at i = 1)
     RevArgs c = a;
-    c.u = slot(2 * i);
     c.v = slot(2 * i - 1);
-    c.g = gu[i & 1];
-    c.gup = c.u1 = c.gu1 = nullptr;
-    c.gout = i > 1 ? gv : (dlvi != nullptr ? dlvi : gv);
+    c.g = gu(i);
+    c.yg = nullptr;
+    c.gup = nullptr;
+    c.gout = i > 1 ? nullptr : dlvi;
+    c.ygout = i > 1 ? gvy(i - 1) : nullptr;
     c.dsum = i > 1 ? dnu : nullptr;
     c.first = 0;
-    c.dc_rows = i == 1;
-    if (vec) rev_col_kernel<true><<<gcol, kRevThreads, 0, st>>>(c);
-    else rev_col_kernel<false><<<gcol, kRevThreads, 0, st>>>(c);
+    if (i > 1 || dlvi != nullptr) {  // gv_0 is wanted only as the warm start's gradient
+      if (vec) rev_col_kernel<true><<<gcol, kRevThreads, 0, st>>>(c);
+      else rev_col_kernel<false><<<gcol, kRevThreads, 0, st>>>(c);
+    }
     e = cudaGetLastError();
   }
-  return e;
+  if (e != cudaSuccess || dC == nullptr) return e;
+  // the factored pass for the problems whose potentials stay within kDcRange, the exact one for the rest
+  // (DFS_DENSE_DC=exact in the environment: the exact pass for every problem)
+  const char* mode = std::getenv("DFS_DENSE_DC");
+  const bool factored = mode == nullptr || std::strcmp(mode, "exact") != 0;
+  float* shift = scratch + static_cast<size_t>(3 * iters + 1) * ns;
+  float* fac = shift + 4 * ns;
+  unsigned* rng = reinterpret_cast<unsigned*>(fac + static_cast<size_t>(4 * iters) * ns);
+  DcArgs d{C, eps, mu, nu, mask, hist, gu(1), reinterpret_cast<const float*>(gvy(1)), ns, dC, B, H, N, iters, lam,
+           nullptr, nullptr, nullptr};
+  if (factored) {
+    if ((e = cudaMemsetAsync(rng, 0, 4 * static_cast<size_t>(B) * H * sizeof(unsigned), st)) != cudaSuccess)
+      return e;
+    d.shift = shift;
+    d.rng = rng;
+    d.fac = fac;
+    dc_factor_kernel<<<grid_for(2 * n, 256), 256, 0, st>>>(d, shift, rng, fac);
+  }
+  const size_t tiles = static_cast<size_t>((N + kDcTile - 1) / kDcTile);
+  const unsigned gdc = static_cast<unsigned>(static_cast<size_t>(B) * H * tiles * tiles);
+  static const int poly = [] {
+    const char* v = std::getenv("DFS_DC_POLY");
+    return v != nullptr ? std::atoi(v) : kDcPolyDefault;
+  }();
+  auto go = [&](auto kern) { kern<<<gdc, 256, 0, st>>>(d); };
+  if (factored) vec ? go(dense_dc_fact_kernel<true>) : go(dense_dc_fact_kernel<false>);
+  const unsigned gex = static_cast<unsigned>(std::min<size_t>(gdc, 148u * 2u));  // the exact pass: grid-stride
+  auto go_ex = [&](auto kern) { kern<<<gex, 256, 0, st>>>(d); };
+  switch (poly) {
+    case 2: vec ? go_ex(dense_dc_kernel<true, 0x11u>) : go_ex(dense_dc_kernel<false, 0x11u>); break;
+    case 3: vec ? go_ex(dense_dc_kernel<true, 0x15u>) : go_ex(dense_dc_kernel<false, 0x15u>); break;
+    case 4: vec ? go_ex(dense_dc_kernel<true, 0x55u>) : go_ex(dense_dc_kernel<false, 0x55u>); break;
+    default: vec ? go_ex(dense_dc_kernel<true, 0x00u>) : go_ex(dense_dc_kernel<false, 0x00u>); break;
+  }
+  return cudaGetLastError();
 }
 
 }  // namespace dfs
@@ -486,6 +910,11 @@ extern "C" int dfs_dense_iterate(int B, int H, int N, float lam, const float* C,
     e = cudaGetLastError();
   }
   return status_of(e);
+}
+
+extern "C" size_t dfs_dense_solve_bwd_scratch(int B, int H, int N, int iters) {
+  if (!dims_ok(B, H, N) || iters < 0) return 0;
+  return dense_bwd_scratch_floats(B, H, N, iters) * sizeof(float);
 }
 
 extern "C" int dfs_dense_solve_bwd(int B, int H, int N, int iters, float lam, const float* C, const float* eps,

@@ -159,7 +159,8 @@ class _DenseSolveFn(torch.autograd.Function):
         dC = new((B, H, N, N), need[0])
         dmu, dnu = new((B, H, N), need[1]), new((B, H, N), need[2])
         dlui, dlvi = new((B, H, N), need[3]), new((B, H, N), need[4])
-        scratch = torch.empty(3 * B * H * N, device=dev, dtype=torch.float32)
+        nbytes = nat.lib().dfs_dense_solve_bwd_scratch(B, H, N, ctx.iters)
+        scratch = torch.empty((nbytes + 3) // 4, device=dev, dtype=torch.float32)
         gu, gv = _f32(g_lu), _f32(g_lv)
         nat.check(nat.lib().dfs_dense_solve_bwd(
             B, H, N, ctx.iters, ctx.lam, nat.ptr(Cc), nat.ptr(ep), nat.ptr(mu), nat.ptr(nu), nat.ptr(mk),

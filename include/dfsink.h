@@ -217,8 +217,12 @@ int dfs_dense_iterate(int B, int H, int N, float lam, const float* C, const floa
 /* dfs_dense_solve_bwd: the adjoint of `iters` iterations recorded in hist by
  * dfs_dense_iterate.  g_log_u / g_log_v: gradients of the returned log_u /
  * log_v (NULL: zero).  Writes dC, dlog_mu, dlog_nu, dlog_u_init, dlog_v_init
- * (each may be NULL when not wanted).  scratch: 3 x B*H*N floats.  eps and lam
+ * (each may be NULL when not wanted).  scratch: dfs_dense_solve_bwd_scratch bytes, 256-byte aligned.  eps and lam
  * get no gradient (eps is a fixed per-head constant in the reference). */
+/* Bytes of scratch dfs_dense_solve_bwd needs (0 for invalid sizes): about
+ * (7 iters + 5) x 4 bytes per (batch, head, point). */
+size_t dfs_dense_solve_bwd_scratch(int B, int H, int N, int iters);
+
 int dfs_dense_solve_bwd(int B, int H, int N, int iters, float lam, const float* C, const float* eps,
                         const float* log_mu, const float* log_nu, const float* mask, const float* hist,
                         const float* g_log_u, const float* g_log_v, float* dC, float* dlog_mu, float* dlog_nu,

@@ -165,3 +165,12 @@ def test_dense_gradient_entry_points_validate_on_the_host(lib):
                                    None, None) == E
     assert lib.dfs_dense_transport_bwd(1, 0, 8, p, p, p, None, None) == E
     assert lib.dfs_dense_transport_bwd(1, 1, 8, None, p, p, None, None) == E
+
+
+def test_dense_backward_scratch_size(lib):
+    """(7 iters + 5) slots of B*H*N floats rounded up to 64, plus 4 floats per
+    (batch, head); 0 for invalid sizes."""
+    assert lib.dfs_dense_solve_bwd_scratch(1, 1, 8, 3) == ((7 * 3 + 5) * 64 + 4) * 4
+    assert lib.dfs_dense_solve_bwd_scratch(2, 3, 100, 20) == ((7 * 20 + 5) * 640 + 24) * 4
+    assert lib.dfs_dense_solve_bwd_scratch(0, 1, 8, 3) == 0
+    assert lib.dfs_dense_solve_bwd_scratch(1, 1, 8, -1) == 0

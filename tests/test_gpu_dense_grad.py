@@ -72,6 +72,60 @@ def test_solve_gradients_match_unrolled_autograd(N, lam):
     assert float(ours[3][1, :, 401:].abs().max()) == 0.0
 
 
+def _pass_ranges(C, lmu, lnu, lvi, eps, K, mask):
+    """Per head, the two quantities that pick the factored or the exact cost
+    pass (log2 units, valid points): the largest row range over iterations
+    1..K of u_i plus the largest column range of v_i / kappa - log_nu, and the
+    same for u_i / kappa - log_mu and v_i-1 (iterations 0..K-1)."""
+    kap = (1.0 / (1.0 + eps.double()))[None, :, None]
+    us, vs = [], [lvi.double()]
+    for k in range(1, K + 1):
+        u, v = ort.sinkhorn_solve(C.double(), lmu.double(), lnu.double(), eps.double(), K=k,
+                                  log_v_init=lvi.double(), mask=mask.double())
+        us.append(u)
+        vs.append(v)
+    valid = mask[:, None, :].bool().expand_as(us[0])
+    # padded points are zeroed in the returned potentials: only valid ones count
+
+    def rng(xs):
+        xs = torch.stack(xs) * 1.4427
+        r = torch.where(valid, xs.max(0).values - xs.min(0).values, torch.zeros_like(xs[0]))
+        return [float(r[:, h].max()) for h in range(C.shape[1])]
+    ru = rng(us)
+    rvc = rng([v / kap - lnu.double() for v in vs[1:]])
+    rur = rng([u / kap - lmu.double() for u in us])
+    rvr = rng(vs[:-1])
+    return [(ru[h] + rvc[h], rur[h] + rvr[h]) for h in range(C.shape[1])]
+
+
+@pytest.mark.parametrize("mode", ["auto", "exact"])
+def test_solve_gradients_exact_and_factored_cost_pass_in_one_call(mode, monkeypatch):
+    """The cost gradient is formed by a factored (rank-2K) pass while a problem's
+    row and column potentials stay within a 2^64 range over the iterations, else
+    by the exact per-term pass.  eps = 0.02 moves the potentials far (the exact
+    pass), eps = 1 does not (the factored pass): one call runs both.  (The
+    ranges are computed from the float64 oracle's iterates.)  With
+    DFS_DENSE_DC=exact every problem takes the exact pass.  Each head is
+    checked on its own scale."""
+    if mode == "exact":
+        monkeypatch.setenv("DFS_DENSE_DC", "exact")
+    N = 260
+    C, lmu, lnu, _, _, _, _, mask = dense_case(2, 2, N, 8, seed=11, lengths=[N, 200])
+    eps = torch.tensor([0.02, 1.0])
+    g = torch.Generator().manual_seed(5)
+    gu, gv, lvi = (torch.randn(2, 2, N, generator=g) for _ in range(3))
+    lvi = 0.1 * lvi
+    lvi[:, 0] *= 500.0  # head 0 starts far from its fixed point
+    ranges = _pass_ranges(C, lmu, lnu, lvi, eps, 6, mask)
+    assert max(ranges[0]) > 64 and max(ranges[1]) < 64, ranges
+    ours = solve_grads(sinkhorn_solve, C, lmu, lnu, lvi, eps, 1.0, 6, mask, gu, gv, dev=DEV)
+    ref = solve_grads(ort.sinkhorn_solve, C, lmu, lnu, lvi, eps, 1.0, 6, mask, gu, gv, dtype=torch.float64)
+    for hd in range(2):
+        for what, a, b in zip(("log_u", "log_v", "dC", "dlog_mu", "dlog_nu", "dlog_v_init"), ours, ref):
+            close(a[:, hd], b[:, hd], f"{what} head {hd}")
+    assert float(ours[2][1, :, 200:, :].abs().max()) == 0.0
+
+
 def test_solve_gradient_reference_unit_case_on_cpu_tensors():
     """The reference's test_unrolled_gradient case (H=2, N=5, randn cost, K=7,
     loss sum(log_u^2 + log_v^2)) on unbatched CPU tensors."""
