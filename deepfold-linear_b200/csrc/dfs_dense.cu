@@ -14,6 +14,10 @@
 //   transport      one warp per row, 8 rows per CTA: pass 1 the row's max and
 //                  sum, pass 2 T_norm_ij per column, O_i += T_norm_ij V_j with
 //                  the CTA's V tile staged in shared memory, x_centroid.
+// For N <= 8192 one iteration is one read of C instead (dense_fused_kernel):
+// a CTA finishes the row updates of eight rows and folds the same rows, re-read
+// from L1 / L2, into per-column partials kept in shared memory; a small kernel
+// merges the CTAs' partials into the column update.
 // The arithmetic follows the reference's formulas -- log K = -C / eps, masks as
 // additive -1e9 biases, kappa = lam / (lam + eps) (1 for lam = inf), T =
 // exp(score - rowmax), T_norm = T / (sum T + 1e-6), padded rows of T_norm and
@@ -26,6 +30,8 @@
 // then marks the problems whose change is below the threshold done, and the
 // later passes skip them -- each (batch, head) problem stops on its own, as on
 // the resident path.
+#include <algorithm>
+
 #include "dfs_kernels.cuh"
 
 namespace dfs {
@@ -485,6 +491,169 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
   }
 }
 
+// One Sinkhorn iteration in one read of C (N <= kFuseMaxN).  A CTA takes rows
+// [r0, r1) of one problem, eight at a time (one per warp):
+//   pass A  each warp finishes its row's update u_i (the row LSE over j, four
+//           16-byte loads of C in flight per lane, as dense_row_kernel);
+//   pass B  the CTA re-reads the same eight rows -- just fetched, so from L1 /
+//           L2, not HBM -- with thread t owning columns 4t + 1024k, and folds
+//           them into its columns' online (max, sum) of the column update,
+//           kept in shared memory across all the CTA's rows.
+// Each CTA then writes its columns' partial (max, sum); dense_fused_merge adds
+// the CTA partials of a problem into v_i.  HBM traffic per iteration: C once
+// (4 bytes per element) plus 8 bytes per column per CTA of partials, against
+// 8 bytes per element for the separate row and column passes.
+constexpr int kFuseMaxN = 8192;
+
+struct FusePlan {
+  int S;    // CTAs (row ranges) per problem
+  int rpu;  // rows per CTA, a multiple of 8
+};
+
+// CTAs per problem: as many as fill the GPU once (no partial second wave)
+FusePlan fuse_plan(int BH, int N, int slots) {
+  FusePlan p;
+  p.S = std::max(1, std::min(slots / std::max(BH, 1), (N + 7) / 8));
+  p.rpu = ((N + p.S - 1) / p.S + 7) / 8 * 8;
+  p.S = (N + p.rpu - 1) / p.rpu;
+  return p;
+}
+
+size_t fuse_smem(int N) { return static_cast<size_t>(2) * N * sizeof(float) + 16 * sizeof(float); }
+
+template <bool VEC>
+__global__ void __launch_bounds__(kDenseThreads) dense_fused_kernel(const DenseArgs a, FusePlan plan, float* part) {
+  extern __shared__ __align__(16) float fsm[];
+  const int N = a.N;
+  float* cm = fsm;          // column running maximum (log2 units)
+  float* cs = fsm + N;      // column sum of exp2(x - max)
+  float* tw = fsm + 2 * N;  // this group's row terms (u_r + rowbias_r) log2e
+  const size_t prob = blockIdx.x / plan.S;
+  const int r0 = static_cast<int>(blockIdx.x % plan.S) * plan.rpu, r1 = min(N, r0 + plan.rpu);
+  if (a.done != nullptr && a.done[prob]) return;  // uniform over the CTA
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
+  const float eps = a.eps[h];
+  const float sc = -kLog2e / eps, kap = kappa_of(a.lam, eps);
+  const float* g = a.lv + prob * N;
+  const float* mk = a.mask == nullptr ? nullptr : a.mask + static_cast<size_t>(b) * N;
+  const float* cprob = a.C + prob * static_cast<size_t>(N) * N;
+  for (int j = threadIdx.x; j < N; j += kDenseThreads) {
+    cm[j] = -INFINITY;
+    cs[j] = 0.0f;
+  }
+  for (int g0 = r0; g0 < r1; g0 += 8) {
+    // pass A: row update of row g0 + warp
+    const int ri = g0 + warp;
+    if (ri < r1) {
+      const float* c = cprob + static_cast<size_t>(ri) * N;
+      float m = -INFINITY, s = 0.0f;
+      if constexpr (VEC) {
+        auto group = [&](const float4& cv, int j) {
+          float4 t = ld4(g + j);
+          if (mk != nullptr) {
+            const float4 mv = ld4(mk + j);
+            t.x += (1.0f - mv.x) * kMaskBias;
+            t.y += (1.0f - mv.y) * kMaskBias;
+            t.z += (1.0f - mv.z) * kMaskBias;
+            t.w += (1.0f - mv.w) * kMaskBias;
+          }
+          lse_push4(m, s, fmaf(cv.x, sc, t.x * kLog2e), fmaf(cv.y, sc, t.y * kLog2e), fmaf(cv.z, sc, t.z * kLog2e),
+                    fmaf(cv.w, sc, t.w * kLog2e));
+        };
+        int j = 4 * lane;
+        for (; j + 384 < N; j += 512) {
+          float4 cv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) cv[u] = ld4(c + j + 128 * u);  // plain loads: kept in L2 for pass B
+#pragma unroll
+          for (int u = 0; u < 4; ++u) group(cv[u], j + 128 * u);
+        }
+        for (; j < N; j += 128) group(ld4(c + j), j);
+      } else {
+        for (int j = lane; j < N; j += 32) lse_push1(m, s, fmaf(c[j], sc, (g[j] + bias_of(a.mask, b, N, j)) * kLog2e));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        lse_merge(m, s, m2, s2);
+      }
+      if (lane == 0) {
+        const size_t i = prob * N + ri;
+        const float f = kap * (a.mu[i] - (m + __log2f(s)) * kLn2);
+        if (a.check) record_change(a.diff + prob, fabsf(f - a.lu[i]));
+        a.lu[i] = f;
+        tw[warp] = (f + bias_of(a.mask, b, N, ri)) * kLog2e;
+      }
+    } else if (lane == 0) {
+      tw[warp] = -INFINITY;  // no row: contributes nothing
+    }
+    __syncthreads();
+    // pass B: the group's rows into the column accumulators
+    const int nr = min(8, r1 - g0);
+    if constexpr (VEC) {
+      for (int j = 4 * threadIdx.x; j < N; j += 4 * kDenseThreads) {
+        float4 mm = *reinterpret_cast<float4*>(cm + j), ss = *reinterpret_cast<float4*>(cs + j);
+        for (int w0 = 0; w0 < 8; w0 += 4) {
+          float4 cv[4];
+          float t[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int w = w0 + u;
+            const int row = g0 + min(w, nr - 1);  // rows past the range re-read a valid row, weighted -inf
+            cv[u] = __ldcs(reinterpret_cast<const float4*>(cprob + static_cast<size_t>(row) * N + j));
+            t[u] = tw[w];
+          }
+          lse_push4(mm.x, ss.x, fmaf(cv[0].x, sc, t[0]), fmaf(cv[1].x, sc, t[1]), fmaf(cv[2].x, sc, t[2]),
+                    fmaf(cv[3].x, sc, t[3]));
+          lse_push4(mm.y, ss.y, fmaf(cv[0].y, sc, t[0]), fmaf(cv[1].y, sc, t[1]), fmaf(cv[2].y, sc, t[2]),
+                    fmaf(cv[3].y, sc, t[3]));
+          lse_push4(mm.z, ss.z, fmaf(cv[0].z, sc, t[0]), fmaf(cv[1].z, sc, t[1]), fmaf(cv[2].z, sc, t[2]),
+                    fmaf(cv[3].z, sc, t[3]));
+          lse_push4(mm.w, ss.w, fmaf(cv[0].w, sc, t[0]), fmaf(cv[1].w, sc, t[1]), fmaf(cv[2].w, sc, t[2]),
+                    fmaf(cv[3].w, sc, t[3]));
+        }
+        *reinterpret_cast<float4*>(cm + j) = mm;
+        *reinterpret_cast<float4*>(cs + j) = ss;
+      }
+    } else {
+      for (int j = threadIdx.x; j < N; j += kDenseThreads) {
+        float mm = cm[j], ss = cs[j];
+        for (int w = 0; w < nr; ++w)
+          lse_push1(mm, ss, fmaf(__ldcs(cprob + static_cast<size_t>(g0 + w) * N + j), sc, tw[w]));
+        cm[j] = mm;
+        cs[j] = ss;
+      }
+    }
+    __syncthreads();  // tw is rewritten by the next group
+  }
+  float* pm = part + static_cast<size_t>(blockIdx.x) * 2 * N;
+  for (int j = threadIdx.x; j < N; j += kDenseThreads) {
+    pm[j] = cm[j];
+    pm[N + j] = cs[j];
+  }
+}
+
+// v_j = kappa (log_nu_j - LSE), the LSE merged from the problem's CTA partials
+// in CTA order (deterministic)
+__global__ void dense_fused_merge(const DenseArgs a, FusePlan plan, const float* part, float* lv_out) {
+  const int N = a.N;
+  const size_t n = static_cast<size_t>(a.B) * a.H * N;
+  for (size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < n;
+       o += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t prob = o / N;
+    if (a.done != nullptr && a.done[prob]) continue;
+    const int j = static_cast<int>(o % N);
+    const float* p = part + prob * plan.S * 2 * static_cast<size_t>(N) + j;
+    float m = p[0], s = p[N];
+    for (int k = 1; k < plan.S; ++k)
+      lse_merge(m, s, p[2 * static_cast<size_t>(k) * N], p[(2 * static_cast<size_t>(k) + 1) * N]);
+    const float v = kappa_of(a.lam, a.eps[prob % a.H]) * (a.nu[o] - (m + __log2f(s)) * kLn2);
+    if (a.check) record_change(a.diff + static_cast<size_t>(a.B) * a.H + prob, fabsf(v - lv_out[o]));
+    lv_out[o] = v;
+  }
+}
+
 unsigned grid_for(size_t work_items, size_t per_cta) {
   const size_t g = (work_items + per_cta - 1) / per_cta;
   const size_t cap = 148u * 16u;  // 16 CTAs of 256 threads per SM at most: a few waves, grid-stride beyond
@@ -497,11 +666,55 @@ namespace {
 size_t r256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 }  // namespace
 
+// partials of the fused iteration: 2 x N floats per CTA, at most max(BH, 148 SMs x 8 CTAs) CTAs
+size_t dense_fuse_part_bytes(int B, int H, int N) {
+  if (N > kFuseMaxN) return 0;
+  return static_cast<size_t>(std::max(B * H, 148 * 8)) * 2 * N * sizeof(float);
+}
+
 size_t dense_fwd_workspace(int B, int H, int N) {
   // diff (2 x BH unsigned) and done (BH int); the transport's row statistics
-  // (2 x BH x N floats); each region 256-byte aligned
-  return r256(static_cast<size_t>(3) * B * H * 4) + r256(static_cast<size_t>(2) * B * H * N * 4);
+  // (2 x BH x N floats); the fused iteration's partials; each region 256-byte aligned
+  return r256(static_cast<size_t>(3) * B * H * 4) + r256(static_cast<size_t>(2) * B * H * N * 4) +
+         r256(dense_fuse_part_bytes(B, H, N));
 }
+
+namespace {
+// One iteration: u_i into a.lu from v_i-1 in a.lv, v_i into lv_out -- fused
+// (one read of C) when part is given and N <= kFuseMaxN, else the separate
+// row and column passes.
+cudaError_t dense_iteration(const DenseArgs& a, float* lv_out, float* part, size_t part_bytes, bool vec,
+                            cudaStream_t st) {
+  const int BH = a.B * a.H;
+  const size_t n = static_cast<size_t>(BH) * a.N;
+  if (part != nullptr && a.N <= kFuseMaxN) {
+    const size_t smem = fuse_smem(a.N);
+    auto kern = vec ? dense_fused_kernel<true> : dense_fused_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    int nb = 0, dev = 0, sms = 148;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kDenseThreads, smem);
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    FusePlan plan = fuse_plan(BH, a.N, std::max(1, nb) * sms);
+    while (static_cast<size_t>(BH) * plan.S * 2 * a.N * sizeof(float) > part_bytes && plan.S > 1)
+      plan = fuse_plan(BH, a.N, BH * (plan.S - 1));  // fewer CTAs per problem to fit the partials
+    kern<<<static_cast<unsigned>(BH) * plan.S, kDenseThreads, smem, st>>>(a, plan, part);
+    dense_fused_merge<<<grid_for(n, 256), 256, 0, st>>>(a, plan, part, lv_out);
+    return cudaGetLastError();
+  }
+  const unsigned grow = grid_for(n, kDenseThreads / 32);
+  const int cols = vec ? 128 : 32;
+  const unsigned gcol = static_cast<unsigned>(BH) * static_cast<unsigned>((a.N + cols - 1) / cols);
+  if (vec) dense_row_kernel<true, false><<<grow, kDenseThreads, 0, st>>>(a);
+  else dense_row_kernel<false, false><<<grow, kDenseThreads, 0, st>>>(a);
+  DenseArgs c = a;
+  c.lv = lv_out;
+  if (vec) dense_col_kernel<true><<<gcol, kDenseThreads, 0, st>>>(c);
+  else dense_col_kernel<false><<<gcol, kDenseThreads, 0, st>>>(c);
+  return cudaGetLastError();
+}
+}  // namespace
 
 cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
   const int BH = q.B * q.H;
@@ -510,6 +723,10 @@ cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
   int* done = reinterpret_cast<int*>(diff + 2 * static_cast<size_t>(BH));
   float* rmax = reinterpret_cast<float*>(static_cast<char*>(ws) + r256(static_cast<size_t>(3) * BH * 4));
   float* rsum = rmax + n;
+  const size_t part_bytes = dense_fuse_part_bytes(q.B, q.H, q.N);
+  float* part = part_bytes == 0 ? nullptr
+                                : reinterpret_cast<float*>(static_cast<char*>(ws) + r256(static_cast<size_t>(3) * BH * 4) +
+                                                           r256(2 * n * sizeof(float)));
   const bool vec = (q.N % 4) == 0 && (reinterpret_cast<uintptr_t>(q.C) & 15u) == 0;
   dense_init_kernel<<<grid_for(n, 256), 256, 0, st>>>(q.log_u_init, q.log_v_init, q.log_u, q.log_v, n, diff, done,
                                                        BH);
@@ -517,16 +734,11 @@ cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
   DenseArgs a{q.C, q.eps, q.log_mu, q.log_nu, q.mask, q.log_u, q.log_v, diff, q.threshold > 0.0f ? done : nullptr,
               rmax, rsum, q.B, q.H, q.N, q.lam, 0};
   const unsigned grow = grid_for(n, kDenseThreads / 32);
-  const int cols = vec ? 128 : 32;
-  const unsigned gcol = static_cast<unsigned>(BH) * static_cast<unsigned>((q.N + cols - 1) / cols);
   for (int it = 0; it < q.K_iter && e == cudaSuccess; ++it) {
     a.check = q.threshold > 0.0f && ((it + 1) % q.check_every) == 0;
-    if (vec) dense_row_kernel<true, false><<<grow, kDenseThreads, 0, st>>>(a);
-    else dense_row_kernel<false, false><<<grow, kDenseThreads, 0, st>>>(a);
-    if (vec) dense_col_kernel<true><<<gcol, kDenseThreads, 0, st>>>(a);
-    else dense_col_kernel<false><<<gcol, kDenseThreads, 0, st>>>(a);
+    e = dense_iteration(a, q.log_v, part, part_bytes, vec, st);
     if (a.check) dense_check_kernel<<<1, 256, 0, st>>>(diff, done, BH, q.threshold);
-    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
   }
   if (e != cudaSuccess) return e;
   if (q.O != nullptr || q.T_out != nullptr || q.x_centroid != nullptr) {
@@ -561,24 +773,15 @@ cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
 // forward that the dense gradients (dfs_dense_grad.cu) reverse.
 cudaError_t launch_dense_iterations(const float* C, const float* eps, const float* mu, const float* nu,
                                     const float* mask, int B, int H, int N, float lam, float* hist, int it_begin,
-                                    int it_end, cudaStream_t st) {
-  const int BH = B * H;
-  const size_t n = static_cast<size_t>(BH) * N;
+                                    int it_end, float* part, size_t part_bytes, cudaStream_t st) {
+  const size_t n = static_cast<size_t>(B) * H * N;
   const bool vec = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
   DenseArgs a{C, eps, mu, nu, mask, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, B, H, N, lam, 0};
-  const unsigned grow = grid_for(n, kDenseThreads / 32);
-  const int cols = vec ? 128 : 32;
-  const unsigned gcol = static_cast<unsigned>(BH) * static_cast<unsigned>((N + cols - 1) / cols);
   cudaError_t e = cudaSuccess;
   for (int it = it_begin + 1; it <= it_end && e == cudaSuccess; ++it) {
     a.lu = hist + static_cast<size_t>(2 * it) * n;      // u_it (written)
     a.lv = hist + static_cast<size_t>(2 * it - 1) * n;  // v_it-1 (read)
-    if (vec) dense_row_kernel<true, false><<<grow, kDenseThreads, 0, st>>>(a);
-    else dense_row_kernel<false, false><<<grow, kDenseThreads, 0, st>>>(a);
-    a.lv = hist + static_cast<size_t>(2 * it + 1) * n;  // v_it (written from u_it)
-    if (vec) dense_col_kernel<true><<<gcol, kDenseThreads, 0, st>>>(a);
-    else dense_col_kernel<false><<<gcol, kDenseThreads, 0, st>>>(a);
-    e = cudaGetLastError();
+    e = dense_iteration(a, hist + static_cast<size_t>(2 * it + 1) * n, part, part_bytes, vec, st);  // v_it
   }
   return e;
 }

@@ -885,13 +885,19 @@ bool dims_ok(int B, int H, int N) {
 int status_of(cudaError_t e) { return e == cudaSuccess ? DFS_OK : DFS_ERR_CUDA; }
 }  // namespace
 
+extern "C" size_t dfs_dense_work_bytes(int B, int H, int N) {
+  return dims_ok(B, H, N) ? dense_fuse_part_bytes(B, H, N) : 0;
+}
+
 extern "C" int dfs_dense_iterate(int B, int H, int N, float lam, const float* C, const float* eps,
                                  const float* log_mu, const float* log_nu, const float* log_u_init,
                                  const float* log_v_init, const float* mask, float* hist, int it_begin, int it_end,
-                                 float* log_u, float* log_v, float* change, int32_t* status, void* stream) {
+                                 float* log_u, float* log_v, float* change, void* work, int32_t* status,
+                                 void* stream) {
   if (!dims_ok(B, H, N) || C == nullptr || eps == nullptr || log_mu == nullptr || log_nu == nullptr ||
       hist == nullptr || log_u == nullptr || log_v == nullptr || it_begin < 0 || it_end < it_begin ||
-      !(lam > 0.0f))
+      !(lam > 0.0f) || (work == nullptr && dense_fuse_part_bytes(B, H, N) != 0) ||
+      (reinterpret_cast<uintptr_t>(work) & 15u) != 0)
     return DFS_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t n = static_cast<size_t>(B) * H * N;
@@ -899,7 +905,8 @@ extern "C" int dfs_dense_iterate(int B, int H, int N, float lam, const float* C,
   if (it_begin == 0) hist_init_kernel<<<ge, 256, 0, st>>>(log_u_init, log_v_init, hist, hist + n, n);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess)
-    e = launch_dense_iterations(C, eps, log_mu, log_nu, mask, B, H, N, lam, hist, it_begin, it_end, st);
+    e = launch_dense_iterations(C, eps, log_mu, log_nu, mask, B, H, N, lam, hist, it_begin, it_end,
+                                static_cast<float*>(work), dense_fuse_part_bytes(B, H, N), st);
   const float* uK = hist + static_cast<size_t>(2 * it_end) * n;
   if (e == cudaSuccess && change != nullptr) {
     if ((e = cudaMemsetAsync(change, 0, sizeof(float), st)) == cudaSuccess && it_end > 0)

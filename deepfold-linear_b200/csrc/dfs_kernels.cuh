@@ -160,9 +160,10 @@ cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
 // resident kernels' range): potentials, O / T_norm / x_centroid, early stop
 size_t dense_fwd_workspace(int B, int H, int N);
 cudaError_t launch_dense_fwd(const FwdParams& p, void* ws, cudaStream_t st);
+size_t dense_fuse_part_bytes(int B, int H, int N);
 cudaError_t launch_dense_iterations(const float* C, const float* eps, const float* mu, const float* nu,
                                     const float* mask, int B, int H, int N, float lam, float* hist, int it_begin,
-                                    int it_end, cudaStream_t st);
+                                    int it_end, float* part, size_t part_bytes, cudaStream_t st);
 // Peer exchange of a row-sharded forward: every GPU's workspace (same layout,
 // 256-byte aligned bases) and the cumulative arrival count the phase waits for.
 struct PeerInfo {

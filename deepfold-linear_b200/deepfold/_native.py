@@ -94,7 +94,7 @@ EXPORTED_SYMBOLS = ("dfs_abi_version", "dfs_status_string", "dfs_max_n", "dfs_wo
                     "dfs_fwd", "dfs_bwd", "dfs_selftest_mma", "dfs_fwd_static", "dfs_stream_op",
                     "dfs_peer_alloc", "dfs_peer_open", "dfs_peer_close", "dfs_peer_free", "dfs_stream_op_peer",
                     "dfs_compute_bins", "dfs_peer_gather_rows", "dfs_stream_cg_loop_peer",
-                    "dfs_dense_iterate", "dfs_dense_solve_bwd", "dfs_dense_solve_bwd_scratch",
+                    "dfs_dense_iterate", "dfs_dense_work_bytes", "dfs_dense_solve_bwd", "dfs_dense_solve_bwd_scratch",
                     "dfs_dense_transport_bwd")
 
 # phases of the streamed path for row-sharded runs (include/dfsink.h)
@@ -269,7 +269,9 @@ def lib() -> ctypes.CDLL:
                                                   ctypes.c_size_t, ctypes.POINTER(DfsPeerSet), ctypes.c_size_t, _P]
             _I, _F = ctypes.c_int, ctypes.c_float
             L.dfs_dense_iterate.restype = ctypes.c_int
-            L.dfs_dense_iterate.argtypes = [_I, _I, _I, _F] + [_P] * 8 + [_I, _I] + [_P] * 5
+            L.dfs_dense_iterate.argtypes = [_I, _I, _I, _F] + [_P] * 8 + [_I, _I] + [_P] * 6
+            L.dfs_dense_work_bytes.restype = ctypes.c_size_t
+            L.dfs_dense_work_bytes.argtypes = [_I, _I, _I]
             L.dfs_dense_solve_bwd_scratch.restype = ctypes.c_size_t
             L.dfs_dense_solve_bwd_scratch.argtypes = [_I, _I, _I, _I]
             L.dfs_dense_solve_bwd.restype = ctypes.c_int

@@ -132,12 +132,15 @@ class _DenseSolveFn(torch.autograd.Function):
         status = torch.zeros(1, device=dev, dtype=torch.int32)
         change = torch.zeros(1, device=dev, dtype=torch.float32) if threshold is not None else None
         L, st = nat.lib(), nat.stream_ptr(dev)
+        wbytes = L.dfs_dense_work_bytes(B, H, N)
+        work = torch.empty((wbytes + 3) // 4, device=dev, dtype=torch.float32) if wbytes else None
         ends = [K] if threshold is None else sorted(set(list(range(check_every, K + 1, check_every)) + [K]))
         done, it = False, 0
         for end in ends:
             nat.check(L.dfs_dense_iterate(B, H, N, float(lam), nat.ptr(Cc), nat.ptr(ep), nat.ptr(mu), nat.ptr(nu),
                                           nat.ptr(lui), nat.ptr(lvi), nat.ptr(mk), nat.ptr(hist), it, end,
-                                          nat.ptr(lu), nat.ptr(lv), nat.ptr(change), nat.ptr(status), st),
+                                          nat.ptr(lu), nat.ptr(lv), nat.ptr(change), nat.ptr(work),
+                                          nat.ptr(status), st),
                       "dfs_dense_iterate")
             it = end
             if threshold is not None and end % check_every == 0 and end > 0:

@@ -212,7 +212,12 @@ int dfs_bwd(const dfs_problem* p, const dfs_cg_params* cg, const dfs_bwd_args* a
 int dfs_dense_iterate(int B, int H, int N, float lam, const float* C, const float* eps, const float* log_mu,
                       const float* log_nu, const float* log_u_init, const float* log_v_init, const float* mask,
                       float* hist, int it_begin, int it_end, float* log_u, float* log_v, float* change,
-                      int32_t* status, void* stream);
+                      void* work, int32_t* status, void* stream);
+
+/* Bytes of the 16-byte aligned `work` buffer dfs_dense_iterate needs: the
+ * per-CTA column partials of its one-read iterations (N <= 8192); 0 beyond,
+ * where work may be NULL. */
+size_t dfs_dense_work_bytes(int B, int H, int N);
 
 /* dfs_dense_solve_bwd: the adjoint of `iters` iterations recorded in hist by
  * dfs_dense_iterate.  g_log_u / g_log_v: gradients of the returned log_u /

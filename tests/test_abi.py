@@ -77,8 +77,10 @@ def test_host_side_validation(lib):
     dense = nat.make_problem(2, 3, 1000, 128, __import__("torch").float32, 5, 1.0, 10.0,
                              cost_mode=nat.DFS_COST_DENSE)
     assert lib.dfs_workspace_size(dense, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
-    # per-problem early-stop state (256 bytes here), then the transport's two row statistics per point
-    assert fb.value == 256 + ((2 * 6 * 1000 * 4 + 255) // 256) * 256 and bb.value == 0
+    # per-problem early-stop state (256 bytes here), the transport's two row statistics per point, and
+    # the one-read iterations' column partials (2 x N floats for up to 148 x 8 CTAs)
+    r256 = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    assert fb.value == 256 + r256(2 * 6 * 1000 * 4) + r256(148 * 8 * 2 * 1000 * 4) and bb.value == 0
     fake_dense = nat.DfsFwdArgs(C=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16)
     assert lib.dfs_fwd(dense, fake_dense, None, 0, None) == nat.DFS_ERR_WORKSPACE
     wider = nat.make_problem(1, 1, 1000, 129, __import__("torch").float32, 5, 1.0, 10.0, cost_mode=nat.DFS_COST_DENSE)
@@ -151,14 +153,20 @@ def test_dense_gradient_entry_points_validate_on_the_host(lib):
     """The dense-gradient calls reject bad sizes and missing buffers before any
     device work (no GPU needed)."""
     E = nat.DFS_ERR_INVALID_ARGUMENT
-    p = 256  # any non-null address: nothing is dereferenced on these paths
-    assert lib.dfs_dense_iterate(0, 1, 8, 1.0, p, p, p, p, None, None, None, p, 0, 1, p, p, None, None, None) == E
-    assert lib.dfs_dense_iterate(1, 1, 8, 1.0, p, p, p, p, None, None, None, p, 2, 1, p, p, None, None, None) == E
-    assert lib.dfs_dense_iterate(1, 1, 1 << 17, 1.0, p, p, p, p, None, None, None, p, 0, 1, p, p, None, None,
-                                 None) == E
-    assert lib.dfs_dense_iterate(1, 1, 8, 0.0, p, p, p, p, None, None, None, p, 0, 1, p, p, None, None, None) == E
-    assert lib.dfs_dense_iterate(1, 1, 8, 1.0, p, p, p, p, None, None, None, None, 0, 1, p, p, None, None,
-                                 None) == E
+    p = 256  # any non-null, 16-byte aligned address: nothing is dereferenced on these paths
+
+    def it(B, H, N, lam, hist, i0, i1, work):
+        return lib.dfs_dense_iterate(B, H, N, lam, p, p, p, p, None, None, None, hist, i0, i1, p, p, None, work,
+                                     None, None)
+    assert it(0, 1, 8, 1.0, p, 0, 1, p) == E
+    assert it(1, 1, 8, 1.0, p, 2, 1, p) == E
+    assert it(1, 1, 1 << 17, 1.0, p, 0, 1, p) == E
+    assert it(1, 1, 8, 0.0, p, 0, 1, p) == E
+    assert it(1, 1, 8, 1.0, None, 0, 1, p) == E
+    assert it(1, 1, 8, 1.0, p, 0, 1, None) == E        # N <= 8192 needs the work buffer
+    assert it(1, 1, 8, 1.0, p, 0, 1, p + 4) == E       # ... 16-byte aligned
+    assert lib.dfs_dense_work_bytes(2, 3, 100) == 148 * 8 * 2 * 100 * 4
+    assert lib.dfs_dense_work_bytes(1, 1, 9000) == 0
     assert lib.dfs_dense_solve_bwd(1, 1, 8, -1, 1.0, p, p, p, p, None, p, None, None, None, None, None, None, None,
                                    p, None) == E
     assert lib.dfs_dense_solve_bwd(1, 1, 8, 3, 1.0, p, p, p, p, None, p, None, None, None, None, None, None, None,
