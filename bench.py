@@ -994,15 +994,18 @@ DENSE = dict(B=1, H=16, N=4096, d=64, eps=1.0, K_iter=20)
 def run_dense(args):
     """The dense-cost entry points beyond the resident range: sinkhorn_solve +
     compute_transport_output on a given fp32 cost C (B=1 H=16 N=4096: 1 GiB),
-    V head dim 64, K=20, uniform marginals, balanced.  Each half-update streams
-    C once (4 bytes per pair), the transport pass twice and writes T_norm; the
-    roofline is those bytes at the measured HBM bandwidth.  Forward only (the
-    dense entry points have no gradients)."""
+    V head dim 64, K=20, uniform marginals, balanced.  Each iteration streams C
+    once (4 bytes per pair: the row and column updates share one read), the
+    transport pass twice and writes T_norm; the roofline is those bytes at the
+    measured HBM bandwidth.  The line's value is the forward; "fwd_bwd" times
+    the same call with a loss on o backpropagated to C and V (the unrolled
+    K-step adjoint and the T_norm backward), as the reference's users run it
+    under autograd."""
     from deepfold.model.sinkhorn import compute_transport_output, sinkhorn_solve
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    c = DENSE
+    c = dict(DENSE, H=args.dense_heads or DENSE["H"])
     B, H, N, d = c["B"], c["H"], c["N"], c["d"]
     g = torch.Generator().manual_seed(0)
     C = torch.rand(B, H, N, N, generator=g).to(dev)
@@ -1030,10 +1033,31 @@ def run_dense(args):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    # forward + backward through the public autograd surface
+    Cg, Vg = C.clone().requires_grad_(True), V.clone().requires_grad_(True)
+    go = torch.randn(B, N, H * d, generator=g).to(dev)
+
+    def grad_step():
+        lu, lv = sinkhorn_solve(Cg, lm, lm, eps, lam=float("inf"), K=c["K_iter"])
+        o = compute_transport_output(Vg, G, lu, lv, Cg, eps)[0]
+        Cg.grad = Vg.grad = None
+        (o * go).sum().backward()
+
+    for _ in range(3):
+        grad_step()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    gsteps = max(1, min(args.steps, 10))
+    for _ in range(gsteps):
+        grad_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_fb = e0.elapsed_time(e1) / gsteps
     clocks = sampler.stop()
     pairs = B * H * N * N
-    # bytes per call: 2K half-updates reading C, the transport pass reading C twice and writing T_norm
-    nbytes = (2 * c["K_iter"] + 3) * 4 * pairs
+    # bytes per call: K iterations reading C once each (N <= 8192: row and column update in one read),
+    # the transport pass reading C twice and writing T_norm
+    nbytes = (c["K_iter"] + 3) * 4 * pairs
     _, peak, peak_src = load_peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
     line = {"metric": "dense-cost sinkhorn_solve + compute_transport_output calls/s", "value": round(1e3 / ms, 4),
@@ -1041,9 +1065,10 @@ def run_dense(args):
             "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32",
             "data": f"synthetic (uniform C in [0,1), N(0,1) V; B={B} H={H} N={N} d={d})",
             "config": {"workload": f"dense sinkhorn_solve K={c['K_iter']} + compute_transport_output, B={B} H={H} "
-                                   f"N={N} d={d}, balanced", "l2": "C (1 GiB) exceeds L2"},
+                                   f"N={N} d={d}, balanced", "l2": f"C ({pairs * 4 / 2**30:.2f} GiB) exceeds L2"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "peak_source": peak_src,
                          "unit": "GB/s", "frac": round(gbs / peak, 4), "bytes_per_call": nbytes},
+            "fwd_bwd": {"ms_per_step": round(ms_fb, 4), "steps": gsteps, "warmup": 3},
             "clocks": clocks}
     print(json.dumps(line), flush=True)
 
@@ -1057,6 +1082,8 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=None, help=argparse.SUPPRESS)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dense-heads", type=int, default=0,
+                    help="heads of the --config dense workload (default 16; fewer for small profiling captures)")
     ap.add_argument("--no-config4", action="store_true", help="skip the single-GPU long-sequence point")
     ap.add_argument("--config", choices=["2", "3", "4", "transport", "dense"], default=None,
                     help="default: 2 on one GPU, 4 (long-sequence row shards) on several; 'transport': the "
