@@ -323,9 +323,10 @@ namespace {
 // t: rows t / 16 + 16 m, columns 4 (t % 16) ...), written out when T_norm is
 // asked for, added into the rows' centroid partials and staged in shared memory
 // beside the chunk's 64 rows of V; then O = T_norm V as a register-blocked
-// product, thread t accumulating rows 4 (t / 8) .. + 3 and head dims DPT (t % 8)
-// .. + DPT - 1 with packed pair FMAs (16 pair FMAs per 6 shared-memory loads at
-// DPT = 8).
+// product, thread t accumulating rows t / 8 + 32 m (m < 4) and head dims
+// DPT (t % 8) .. + DPT - 1 with packed pair FMAs: per four columns, four 16-byte
+// reads of T and 4 DPT / 4 of V, each one shared-memory wavefront per warp, for
+// 8 DPT pair FMAs (64 at DPT = 8), so the product is bound by the FMA pipes.
 struct DenseOutArgs {
   const float* C;
   const float* V;     // (B,H,N,d) fp32 or null
@@ -378,7 +379,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
     inv[m] = ok ? rm / (a.rsum[r] + 1e-6f) : 0.0f;
     cx[m] = cy[m] = cz[m] = 0.0f;
   }
-  // product side: rows 4 rg .. + 3, dims DPT dg .. + DPT - 1
+  // product side: rows rg + 32 m (m < 4), dims DPT dg .. + DPT - 1
   const int rg = tid >> 3, dg = tid & 7;
   float2 acc[4][DPT / 2];
 #pragma unroll
@@ -435,23 +436,32 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
       Vs[e] = (c < rows && k < d) ? __ldg(vsrc + static_cast<size_t>(c) * d + k) : 0.0f;
     }
     __syncthreads();
-    const float* tb = Ts + 4 * rg * kOutTS;
+    // rows rg + 32 m: the four rows a warp reads start on banks 16 w + {0, 4, 8, 12}
+    // (row stride 68 floats), so each 16-byte read of four columns of T is one
+    // wavefront; V's 8 head-dim groups are one more per 16-byte read
+    const float* tb = Ts + rg * kOutTS;
     const float* vb = Vs + DPT * dg;
-#pragma unroll 4
-    for (int c = 0; c < kOutCols; ++c) {
-      float2 v[DPT / 2];
+#pragma unroll 2
+    for (int c = 0; c < kOutCols; c += 4) {
+      float4 tq[4];
 #pragma unroll
-      for (int q = 0; q < DPT / 4; ++q) {
-        const float4 v4 = *reinterpret_cast<const float4*>(vb + c * DP + 4 * q);
-        v[2 * q] = make_float2(v4.x, v4.y);
-        v[2 * q + 1] = make_float2(v4.z, v4.w);
-      }
+      for (int m = 0; m < 4; ++m) tq[m] = *reinterpret_cast<const float4*>(tb + 32 * m * kOutTS + c);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const float tv = tb[m * kOutTS + c];
-        const float2 t2 = make_float2(tv, tv);
+      for (int cc = 0; cc < 4; ++cc) {
+        float2 v[DPT / 2];
 #pragma unroll
-        for (int q = 0; q < DPT / 2; ++q) acc[m][q] = __ffma2_rn(t2, v[q], acc[m][q]);
+        for (int q = 0; q < DPT / 4; ++q) {
+          const float4 v4 = *reinterpret_cast<const float4*>(vb + (c + cc) * DP + 4 * q);
+          v[2 * q] = make_float2(v4.x, v4.y);
+          v[2 * q + 1] = make_float2(v4.z, v4.w);
+        }
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const float tv = cc == 0 ? tq[m].x : (cc == 1 ? tq[m].y : (cc == 2 ? tq[m].z : tq[m].w));
+          const float2 t2 = make_float2(tv, tv);
+#pragma unroll
+          for (int q = 0; q < DPT / 2; ++q) acc[m][q] = __ffma2_rn(t2, v[q], acc[m][q]);
+        }
       }
     }
   }
@@ -478,7 +488,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
   if (a.O != nullptr) {
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      const int i = i0 + 4 * rg + m;
+      const int i = i0 + rg + 32 * m;
       if (i >= N) continue;
       float* orow = a.O + (prob * N + i) * static_cast<size_t>(d);
 #pragma unroll
