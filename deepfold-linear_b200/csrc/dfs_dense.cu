@@ -344,6 +344,7 @@ struct DenseOutArgs {
 };
 
 constexpr int kOutRows = 128, kOutCols = 64, kOutTS = kOutCols + 4;  // T tile row stride (floats)
+constexpr int kOutTR = kOutRows / 16, kOutPR = kOutRows / 32;  // rows per thread: T side, product side
 
 template <int DPT>
 size_t dense_out_smem() {
@@ -365,11 +366,11 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
   const float sc = -kLog2e / a.eps[h];
   const float* g = a.lv + prob * N;
   const float* xb = a.x != nullptr ? a.x + static_cast<size_t>(b) * N * 3 : nullptr;
-  // T side: rows lrow0 + 16 m (m < 8), columns 4 c4 .. + 3 of each chunk
+  // T side: rows lrow0 + 16 m (m < kOutTR), columns 4 c4 .. + 3 of each chunk
   const int lrow0 = tid >> 4, c4 = tid & 15;
-  float ui[8], mt[8], inv[8], cx[8], cy[8], cz[8];
+  float ui[kOutTR], mt[kOutTR], inv[kOutTR], cx[kOutTR], cy[kOutTR], cz[kOutTR];
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
+  for (int m = 0; m < kOutTR; ++m) {
     const int i = i0 + lrow0 + 16 * m;
     const size_t r = prob * N + (i < N ? i : 0);
     const bool ok = i < N;
@@ -379,11 +380,11 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
     inv[m] = ok ? rm / (a.rsum[r] + 1e-6f) : 0.0f;
     cx[m] = cy[m] = cz[m] = 0.0f;
   }
-  // product side: rows rg + 32 m (m < 4), dims DPT dg .. + DPT - 1
+  // product side: rows rg + 32 m (m < kOutPR), dims DPT dg .. + DPT - 1
   const int rg = tid >> 3, dg = tid & 7;
-  float2 acc[4][DPT / 2];
+  float2 acc[kOutPR][DPT / 2];
 #pragma unroll
-  for (int m = 0; m < 4; ++m)
+  for (int m = 0; m < kOutPR; ++m)
 #pragma unroll
     for (int q = 0; q < DPT / 2; ++q) acc[m][q] = make_float2(0.0f, 0.0f);
   for (int j0 = 0; j0 < N; j0 += kOutCols) {
@@ -393,7 +394,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
     for (int e = 0; e < 4; ++e) gb[e] = (jc + e < N) ? (g[jc + e] + bias_of(a.mask, b, N, jc + e)) : 0.0f;
     __syncthreads();  // the previous chunk's product is done with Ts / Vs
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
+    for (int m = 0; m < kOutTR; ++m) {
       const int li = lrow0 + 16 * m, i = i0 + li;
       const float* crow = a.C + (prob * N + (i < N ? i : 0)) * static_cast<size_t>(N);
       float cv[4];
@@ -431,9 +432,20 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
     if (a.V == nullptr) continue;  // uniform: no O asked for
     const float* vsrc = a.V + (prob * N + j0) * static_cast<size_t>(d);
     const int rows = min(kOutCols, N - j0);
-    for (int e = tid; e < kOutCols * DP; e += kDenseThreads) {
-      const int c = e / DP, k = e - c * DP;
-      Vs[e] = (c < rows && k < d) ? __ldg(vsrc + static_cast<size_t>(c) * d + k) : 0.0f;
+    // every CTA of a problem reads all of V (from L2): 16-byte loads where the rows allow
+    if ((d & 3) == 0 && (reinterpret_cast<uintptr_t>(a.V) & 15u) == 0) {
+      const int d4 = d >> 2, DP4 = DP / 4;
+      for (int e = tid; e < kOutCols * DP4; e += kDenseThreads) {
+        const int c = e / DP4, k4 = e - c * DP4;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c < rows && k4 < d4) v = __ldg(reinterpret_cast<const float4*>(vsrc + static_cast<size_t>(c) * d) + k4);
+        reinterpret_cast<float4*>(Vs)[e] = v;
+      }
+    } else {
+      for (int e = tid; e < kOutCols * DP; e += kDenseThreads) {
+        const int c = e / DP, k = e - c * DP;
+        Vs[e] = (c < rows && k < d) ? __ldg(vsrc + static_cast<size_t>(c) * d + k) : 0.0f;
+      }
     }
     __syncthreads();
     // rows rg + 32 m: the four rows a warp reads start on banks 16 w + {0, 4, 8, 12}
@@ -443,9 +455,9 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
     const float* vb = Vs + DPT * dg;
 #pragma unroll 2
     for (int c = 0; c < kOutCols; c += 4) {
-      float4 tq[4];
+      float4 tq[kOutPR];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) tq[m] = *reinterpret_cast<const float4*>(tb + 32 * m * kOutTS + c);
+      for (int m = 0; m < kOutPR; ++m) tq[m] = *reinterpret_cast<const float4*>(tb + 32 * m * kOutTS + c);
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         float2 v[DPT / 2];
@@ -456,7 +468,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
           v[2 * q + 1] = make_float2(v4.z, v4.w);
         }
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < kOutPR; ++m) {
           const float tv = cc == 0 ? tq[m].x : (cc == 1 ? tq[m].y : (cc == 2 ? tq[m].z : tq[m].w));
           const float2 t2 = make_float2(tv, tv);
 #pragma unroll
@@ -468,7 +480,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
   if (a.xc != nullptr) {
     // the 16 threads of a row are consecutive lanes of one warp
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
+    for (int m = 0; m < kOutTR; ++m) {
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) {
         cx[m] += __shfl_xor_sync(0xffffffffu, cx[m], o);
@@ -487,7 +499,7 @@ __global__ void __launch_bounds__(kDenseThreads) dense_out_kernel(const DenseOut
   (void)lane;
   if (a.O != nullptr) {
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
+    for (int m = 0; m < kOutPR; ++m) {
       const int i = i0 + rg + 32 * m;
       if (i >= N) continue;
       float* orow = a.O + (prob * N + i) * static_cast<size_t>(d);
