@@ -89,7 +89,7 @@ def sinkhorn_solve(C, log_mu, log_nu, eps, lam=1.0, K=7, log_u_init=None, log_v_
         log_u = kappa[None, :, None] * (log_mu - torch.logsumexp(log_K + log_v[:, :, None, :] + col_bias, dim=-1))
         log_v = kappa[None, :, None] * (log_nu - torch.logsumexp(log_K + log_u[:, :, :, None] + row_bias, dim=-2))
         if threshold is not None and (i + 1) % check_every == 0:
-            ch = max(float((log_u - u_prev).abs().max()), float((log_v - v_prev).abs().max()))
+            ch = max(float((log_u - u_prev).detach().abs().max()), float((log_v - v_prev).detach().abs().max()))
             if ch < threshold:
                 break
     if mask is not None:

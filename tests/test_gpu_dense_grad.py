@@ -9,6 +9,7 @@ in fp32 with ex2.approx exponentials; the oracle in float64)."""
 
 import math
 
+import numpy as np
 import pytest
 import torch
 
@@ -210,3 +211,44 @@ def test_solve_then_transport_end_to_end():
         res.append((o, Cl.grad, Vl.grad))
     for what, a, b in zip(("o", "dC", "dV"), res[0], res[1]):
         close(a, b, what)
+
+
+@pytest.mark.parametrize("name", ["pure_balanced", "masked_varlen", "uot_full"])
+def test_dense_gradients_match_the_reference_autograd_goldens(name):
+    """The golden vectors hold the reference's own autograd through its cost,
+    sinkhorn_solve and compute_transport_output (tests/golden/make_golden.py):
+    the same loss through this library's dense entry points on the GPU (the
+    cost itself formed by torch ops, as the reference's user forms it) gives
+    the reference's outputs and the gradients of every input, including the
+    position table, the geometry weight and the coordinates (uot_full)."""
+    from test_oracle_torch import load
+
+    inp, out, meta = load(name)
+    f32 = lambda k: inp[k].to(DEV, torch.float32)  # noqa: E731
+    leaf = lambda k: f32(k).requires_grad_(True)  # noqa: E731
+    Q, K, V, G = leaf("Q"), leaf("K"), leaf("V"), leaf("G")
+    full = name == "uot_full"
+    x = leaf("x") if full else None
+    pos = leaf("pos_w") if full else None
+    w = leaf("w_dist") if full else None
+    bins = inp["bins"].to(DEV) if full else None
+    mask = f32("mask") if "mask" in inp else None
+    eps = f32("eps")
+    C = ort.cost(Q, K, x, pos, bins, w, float(meta["r_0"]))
+    lu, lv = sinkhorn_solve(C, f32("log_mu"), f32("log_nu"), eps, lam=float(meta["lam"]), K=int(meta["K_iter"]),
+                            mask=mask)
+    o, _, xc = compute_transport_output(V, G, lu, lv, C, eps, x_res=x, mask=mask)
+    loss = (o * f32("dO")).sum()
+    if full:
+        loss = loss + (xc * f32("dxc")).sum()
+    loss.backward()
+    rel = lambda a, b: float(np.max(np.abs(a.detach().cpu().double().numpy() - b)) / max(np.max(np.abs(b)), 1e-30))  # noqa: E731,E501
+    assert rel(o, out["o_dense" if full else "o"]) < 1e-3
+    if not full:  # uot_full's potentials are the flash path's (unconverged at K = 5)
+        assert float(np.max(np.abs(lu.detach().cpu().numpy() - out["log_u"]))) < 1e-3
+        assert float(np.max(np.abs(lv.detach().cpu().numpy() - out["log_v"]))) < 1e-3
+    grads = dict(dQ=Q.grad, dK=K.grad, dV=V.grad, dG=G.grad)
+    if full:
+        grads.update(dx=x.grad, dpos=pos.grad, dw=w.grad)
+    for k, g in grads.items():
+        assert rel(g, out[k]) < TOL, (k, rel(g, out[k]))
