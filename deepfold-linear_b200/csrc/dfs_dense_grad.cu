@@ -216,6 +216,151 @@ __global__ void __launch_bounds__(kRevThreads) rev_col_kernel(const RevArgs a) {
   }
 }
 
+// One reverse iteration in one read of C (N <= kRevFuseMaxN): the row pass and
+// the column pass above fused as dense_fused_kernel fuses the forward.  A CTA
+// takes rows [r0, r1) of one problem, eight at a time: each warp finishes its
+// row's gu_i,r (pass A, the row pass's reduction); then the CTA re-reads the
+// same rows (from L2) and adds gu_i,r Pr_rj into per-column sums kept in shared
+// memory (pass B), thread t owning columns 4t + 1024k.  Each CTA writes its
+// column sums; rev_fused_merge adds a problem's CTA sums in CTA order into
+// gv_i-1 (and its exponent pair, dlog_nu).
+constexpr int kRevFuseMaxN = 8192;
+
+struct RevPlan {
+  int S;    // CTAs per problem
+  int rpu;  // rows per CTA, a multiple of 8
+};
+
+RevPlan rev_plan(int BH, int N, int slots) {
+  RevPlan p;
+  p.S = std::max(1, std::min(slots / std::max(BH, 1), (N + 7) / 8));
+  p.rpu = ((N + p.S - 1) / p.S + 7) / 8 * 8;
+  p.S = (N + p.rpu - 1) / p.rpu;
+  return p;
+}
+
+size_t rev_fuse_smem(int N) { return static_cast<size_t>(2) * N * sizeof(float) + 16 * sizeof(float); }
+
+template <bool VEC>
+__global__ void __launch_bounds__(kRevThreads) rev_fused_kernel(const RevArgs a, RevPlan plan, float* part) {
+  extern __shared__ __align__(16) float rsm[];
+  const int N = a.N;
+  float* cacc = rsm;          // column sums of gu_r Pr_rj
+  float* cbv = rsm + N;       // (v_i-1,j + cb_j) log2e
+  float* gw = rsm + 2 * N;    // this group's gu_r
+  float* xw = gw + 8;         // this group's (u_i,r / kappa - a_r) log2e
+  const size_t prob = blockIdx.x / plan.S;
+  const int r0 = static_cast<int>(blockIdx.x % plan.S) * plan.rpu, r1 = min(N, r0 + plan.rpu);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = static_cast<int>(prob / a.H), h = static_cast<int>(prob % a.H);
+  const float eps = a.eps[h], kap = kappa_of(a.lam, eps), ikap = 1.0f / kap;
+  const float sc = -kLog2e / eps;
+  const float* cprob = a.C + prob * static_cast<size_t>(N) * N;
+  const float* yg = reinterpret_cast<const float*>(a.yg + prob * N);  // (y, g) pairs of v_i
+  for (int j = threadIdx.x; j < N; j += kRevThreads) {
+    cacc[j] = 0.0f;
+    cbv[j] = (a.v[prob * N + j] + bias_of(a.mask, b, N, j)) * kLog2e;
+  }
+  for (int g0 = r0; g0 < r1; g0 += 8) {
+    // pass A: gu of row g0 + warp
+    const int ri = g0 + warp;
+    if (ri < r1) {
+      const size_t r = prob * N + ri;
+      const float yr = (a.u[r] + bias_of(a.mask, b, N, ri)) * kLog2e;
+      const float* c = cprob + static_cast<size_t>(ri) * N;
+      float acc = 0.0f;
+      auto elem = [&](float cj, float yj, float gj) { acc = fmaf(gj, ex2c(fmaf(cj, sc, yj + yr)), acc); };
+      if constexpr (VEC) {
+        auto group = [&](const float4& cv, int j) {
+          const float4 p0 = ld4(yg + 2 * j), p1 = ld4(yg + 2 * j + 4);
+          elem(cv.x, p0.x, p0.y);
+          elem(cv.y, p0.z, p0.w);
+          elem(cv.z, p1.x, p1.y);
+          elem(cv.w, p1.z, p1.w);
+        };
+        int j = 4 * lane;
+        for (; j + 384 < N; j += 512) {
+          float4 cv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) cv[q] = ld4(c + j + 128 * q);  // plain loads: kept in L2 for pass B
+#pragma unroll
+          for (int q = 0; q < 4; ++q) group(cv[q], j + 128 * q);
+        }
+        for (; j < N; j += 128) group(ld4(c + j), j);
+      } else {
+        for (int j = lane; j < N; j += 32) elem(c[j], yg[2 * j], yg[2 * j + 1]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        const float gu = (a.gup != nullptr ? a.gup[r] : 0.0f) - kap * acc;
+        a.gout[r] = gu;
+        if (a.dsum != nullptr) a.dsum[r] = a.first ? kap * gu : a.dsum[r] + kap * gu;
+        gw[warp] = gu;
+        xw[warp] = (a.u[r] * ikap - a.mu[r]) * kLog2e;
+      }
+    } else if (lane == 0) {
+      gw[warp] = 0.0f;  // no row: weight 0 (its capped exponential stays finite)
+      xw[warp] = 0.0f;
+    }
+    __syncthreads();
+    // pass B: gu_r Pr_rj of the group's rows into the column sums
+    const int nr = min(8, r1 - g0);
+    if constexpr (VEC) {
+      for (int j = 4 * threadIdx.x; j < N; j += 4 * kRevThreads) {
+        float4 s4 = *reinterpret_cast<float4*>(cacc + j);
+        const float4 cb = *reinterpret_cast<const float4*>(cbv + j);
+        for (int w0 = 0; w0 < 8; w0 += 4) {
+          float4 cv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int row = g0 + min(w0 + q, nr - 1);  // rows past the range re-read a valid row, weight 0
+            cv[q] = __ldcs(reinterpret_cast<const float4*>(cprob + static_cast<size_t>(row) * N + j));
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float g = gw[w0 + q], x = xw[w0 + q];
+            s4.x = fmaf(g, ex2c(fmaf(cv[q].x, sc, cb.x) + x), s4.x);
+            s4.y = fmaf(g, ex2c(fmaf(cv[q].y, sc, cb.y) + x), s4.y);
+            s4.z = fmaf(g, ex2c(fmaf(cv[q].z, sc, cb.z) + x), s4.z);
+            s4.w = fmaf(g, ex2c(fmaf(cv[q].w, sc, cb.w) + x), s4.w);
+          }
+        }
+        *reinterpret_cast<float4*>(cacc + j) = s4;
+      }
+    } else {
+      for (int j = threadIdx.x; j < N; j += kRevThreads) {
+        float s1 = cacc[j];
+        for (int w = 0; w < nr; ++w)
+          s1 = fmaf(gw[w], ex2c(fmaf(__ldcs(cprob + static_cast<size_t>(g0 + w) * N + j), sc, cbv[j]) + xw[w]), s1);
+        cacc[j] = s1;
+      }
+    }
+    __syncthreads();  // gw / xw are rewritten by the next group
+  }
+  float* pp = part + static_cast<size_t>(blockIdx.x) * N;
+  for (int j = threadIdx.x; j < N; j += kRevThreads) pp[j] = cacc[j];
+}
+
+// gv_i-1,j = -kappa sum over the problem's CTAs (in CTA order) of their column sums
+__global__ void rev_fused_merge(const RevArgs a, RevPlan plan, const float* part) {
+  const int N = a.N;
+  const size_t n = static_cast<size_t>(a.B) * a.H * N;
+  for (size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < n;
+       o += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t prob = o / N;
+    const int j = static_cast<int>(o % N);
+    const float* p = part + prob * plan.S * static_cast<size_t>(N) + j;
+    float sum = p[0];
+    for (int k = 1; k < plan.S; ++k) sum += p[static_cast<size_t>(k) * N];
+    const float kap = kappa_of(a.lam, a.eps[prob % a.H]), ikap = 1.0f / kap;
+    const float gv = -kap * sum;
+    if (a.ygout != nullptr) a.ygout[o] = make_float2((a.v[o] * ikap - a.nu[o]) * kLog2e, gv);
+    if (a.gout != nullptr) a.gout[o] = gv;
+    if (a.dsum != nullptr) a.dsum[o] += kap * gv;
+  }
+}
+
 // The cost gradient from every iteration's adjoints at once (after the reverse
 // passes): dC_rj = sum_i w_i,j Pc_i,rj + w'_i,r Pr_i,rj over i = 1 .. K, with
 // the per-row and per-column parts of each exponent and weight staged in
@@ -750,11 +895,17 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Scratch of the reverse (floats), slots of ns = n rounded up to 64 floats
 // (every slot 256-byte aligned): gu_i (iters slots), (y, gv_i) pairs (2 iters),
 // the masked upstream adjoint of u_K (1), the factored pass's shifts (4) and
-// factors (4 iters), then 4 x BH per-problem ranges.
+// factors (4 iters), 4 x BH per-problem ranges (rounded up to 64), then the
+// one-read reverse iterations' column sums.
 size_t dense_bwd_slot(size_t n) { return (n + 63) / 64 * 64; }
+// column sums of the one-read reverse iterations: N floats per CTA, at most max(BH, 148 SMs x 8) CTAs
+size_t rev_part_floats(int B, int H, int N) {
+  return N > kRevFuseMaxN ? 0 : static_cast<size_t>(std::max(B * H, 148 * 8)) * N;
+}
 size_t dense_bwd_scratch_floats(int B, int H, int N, int iters) {
   const size_t n = static_cast<size_t>(B) * H * N;
-  return static_cast<size_t>(7 * iters + 5) * dense_bwd_slot(n) + 4 * static_cast<size_t>(B) * H;
+  return static_cast<size_t>(7 * iters + 5) * dense_bwd_slot(n) + dense_bwd_slot(4 * static_cast<size_t>(B) * H) +
+         rev_part_floats(B, H, N);
 }
 
 // ((v_K / kappa - b) log2e, gv_K) pairs from the masked upstream adjoint of v_K; dlog_nu = kappa gv_K
@@ -801,6 +952,24 @@ cudaError_t launch_dense_solve_bwd(int B, int H, int N, int iters, float lam, co
   const unsigned grow = grid_for(n, kRevThreads / 32);
   const int cols = vec ? 128 : 32;
   const unsigned gcol = static_cast<unsigned>(B) * H * static_cast<unsigned>((N + cols - 1) / cols);
+  // one read of C per reverse iteration for N <= kRevFuseMaxN
+  float* rpart = scratch + static_cast<size_t>(7 * iters + 5) * ns + dense_bwd_slot(4 * static_cast<size_t>(B) * H);
+  const size_t rpart_floats = rev_part_floats(B, H, N);
+  RevPlan plan{0, 0};
+  if (rpart_floats != 0) {
+    const size_t smem = rev_fuse_smem(N);
+    auto kern = vec ? rev_fused_kernel<true> : rev_fused_kernel<false>;
+    int nb = 0, dev = 0, sms = 148;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) ==
+            cudaSuccess &&
+        (e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, kRevThreads, smem)) == cudaSuccess &&
+        (e = cudaGetDevice(&dev)) == cudaSuccess)
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    plan = rev_plan(B * H, N, std::max(1, nb) * sms);
+    while (static_cast<size_t>(B) * H * plan.S * N > rpart_floats && plan.S > 1)
+      plan = rev_plan(B * H, N, B * H * (plan.S - 1));
+  }
   for (int i = iters; i >= 1 && e == cudaSuccess; --i) {
     RevArgs a{};
     a.C = C;
@@ -819,6 +988,23 @@ cudaError_t launch_dense_solve_bwd(int B, int H, int N, int iters, float lam, co
     a.gout = gu(i);
     a.dsum = dmu;
     a.first = i == iters;
+    const bool want_gv = i > 1 || dlvi != nullptr;  // gv_0 is wanted only as the warm start's gradient
+    if (plan.S > 0 && want_gv) {
+      // row and column pass in one read of C: gu_i, then gv_i-1 from the CTAs' column sums
+      a.v = slot(2 * i - 1);
+      a.gout = gu(i);
+      a.ygout = nullptr;
+      const size_t smem = rev_fuse_smem(N);
+      if (vec) rev_fused_kernel<true><<<static_cast<unsigned>(B * H * plan.S), kRevThreads, smem, st>>>(a, plan, rpart);
+      else rev_fused_kernel<false><<<static_cast<unsigned>(B * H * plan.S), kRevThreads, smem, st>>>(a, plan, rpart);
+      RevArgs m = a;
+      m.gout = i > 1 ? nullptr : dlvi;
+      m.ygout = i > 1 ? gvy(i - 1) : nullptr;
+      m.dsum = i > 1 ? dnu : nullptr;
+      rev_fused_merge<<<ge, 256, 0, st>>>(m, plan, rpart);
+      e = cudaGetLastError();
+      continue;
+    }
     if (vec) rev_row_kernel<true><<<grow, kRevThreads, 0, st>>>(a);
     else rev_row_kernel<false><<<grow, kRevThreads, 0, st>>>(a);
     // column pass: gv_i-1 from gu_i (the adjoint of the warm start at i = 1)
@@ -831,7 +1017,7 @@ cudaError_t launch_dense_solve_bwd(int B, int H, int N, int iters, float lam, co
     c.ygout = i > 1 ? gvy(i - 1) : nullptr;
     c.dsum = i > 1 ? dnu : nullptr;
     c.first = 0;
-    if (i > 1 || dlvi != nullptr) {  // gv_0 is wanted only as the warm start's gradient
+    if (want_gv) {
       if (vec) rev_col_kernel<true><<<gcol, kRevThreads, 0, st>>>(c);
       else rev_col_kernel<false><<<gcol, kRevThreads, 0, st>>>(c);
     }

@@ -176,9 +176,12 @@ def test_dense_gradient_entry_points_validate_on_the_host(lib):
 
 
 def test_dense_backward_scratch_size(lib):
-    """(7 iters + 5) slots of B*H*N floats rounded up to 64, plus 4 floats per
-    (batch, head); 0 for invalid sizes."""
-    assert lib.dfs_dense_solve_bwd_scratch(1, 1, 8, 3) == ((7 * 3 + 5) * 64 + 4) * 4
-    assert lib.dfs_dense_solve_bwd_scratch(2, 3, 100, 20) == ((7 * 20 + 5) * 640 + 24) * 4
+    """(7 iters + 5) slots of B*H*N floats rounded up to 64, 4 floats per
+    (batch, head) rounded up to 64, and for N <= 8192 the one-read reverse
+    iterations' column sums (N floats for up to max(B*H, 148 x 8) CTAs); 0 for
+    invalid sizes."""
+    assert lib.dfs_dense_solve_bwd_scratch(1, 1, 8, 3) == ((7 * 3 + 5) * 64 + 64 + 1184 * 8) * 4
+    assert lib.dfs_dense_solve_bwd_scratch(2, 3, 100, 20) == ((7 * 20 + 5) * 640 + 64 + 1184 * 100) * 4
+    assert lib.dfs_dense_solve_bwd_scratch(1, 1, 9000, 2) == ((7 * 2 + 5) * 9024 + 64) * 4
     assert lib.dfs_dense_solve_bwd_scratch(0, 1, 8, 3) == 0
     assert lib.dfs_dense_solve_bwd_scratch(1, 1, 8, -1) == 0
