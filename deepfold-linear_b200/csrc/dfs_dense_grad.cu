@@ -20,10 +20,11 @@
 //   dC_rj   += kappa / eps (gv_i,j Pc_rj + gu_i,r Pr_rj)
 //   dlog_mu  = kappa sum_i gu_i,   dlog_nu = kappa sum_i gv_i (i >= 1),
 //   dlog_v_init = gv_0,  dlog_u_init = 0 (u_0 is never read) unless K = 0.
-// The reverse runs as 2K passes over C that only form the adjoints -- a row
-// pass (one warp per row: gu_i from gv_i, a row reduction) and a column pass
-// (one CTA per 128 columns: gv_i-1 from gu_i), each reading C once, 4 bytes
-// per element -- and keeps every gu_i, gv_i; then one tiled pass forms
+// The reverse iterations only form the adjoints -- gu_i from gv_i (a row
+// reduction) and gv_i-1 from gu_i (a column reduction): one read of C per
+// iteration for N <= 8192 (rev_fused_kernel), else a row pass (one warp per
+// row) and a column pass (one CTA per 128 columns) of 4 bytes per element
+// each -- and keep every gu_i, gv_i; then one tiled pass forms
 //   dC_rj = kappa / eps sum_i (gv_i,j Pc_i,rj + gu_i,r Pr_i,rj)
 // from them, reading C and writing dC once: 2K exponentials per element, so
 // that pass is bound by the exponentials, not by HBM.

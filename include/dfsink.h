@@ -225,7 +225,9 @@ size_t dfs_dense_work_bytes(int B, int H, int N);
  * (each may be NULL when not wanted).  scratch: dfs_dense_solve_bwd_scratch bytes, 256-byte aligned.  eps and lam
  * get no gradient (eps is a fixed per-head constant in the reference). */
 /* Bytes of scratch dfs_dense_solve_bwd needs (0 for invalid sizes): about
- * (7 iters + 5) x 4 bytes per (batch, head, point). */
+ * (7 iters + 5) x 4 bytes per (batch, head, point), plus for N <= 8192 the
+ * one-read reverse iterations' column sums, 4 N bytes for each of up to
+ * max(B*H, 1184) CTAs. */
 size_t dfs_dense_solve_bwd_scratch(int B, int H, int N, int iters);
 
 int dfs_dense_solve_bwd(int B, int H, int N, int iters, float lam, const float* C, const float* eps,
