@@ -114,6 +114,20 @@ def _f32(t):
     return None if t is None else t.detach().float().contiguous()
 
 
+def _chunk_ends(K: int, threshold, check_every: int) -> list[int]:
+    """Iteration counts after which the differentiable forward returns to the
+    host: K alone without a threshold; else every multiple of check_every (where
+    the reference tests its stop condition, sinkhorn.py:98-103) and K."""
+    if threshold is None:
+        return [K]
+    return sorted(set(range(check_every, K + 1, check_every)) | {K})
+
+
+def _is_check(end: int, threshold, check_every: int) -> bool:
+    """Whether the reference tests for convergence after iteration `end`."""
+    return threshold is not None and end > 0 and end % check_every == 0
+
+
 class _DenseSolveFn(torch.autograd.Function):
     """sinkhorn_solve with its unrolled adjoint (sinkhorn.py:82-110 under autograd)."""
 
@@ -134,16 +148,15 @@ class _DenseSolveFn(torch.autograd.Function):
         L, st = nat.lib(), nat.stream_ptr(dev)
         wbytes = L.dfs_dense_work_bytes(B, H, N)
         work = torch.empty((wbytes + 3) // 4, device=dev, dtype=torch.float32) if wbytes else None
-        ends = [K] if threshold is None else sorted(set(list(range(check_every, K + 1, check_every)) + [K]))
         done, it = False, 0
-        for end in ends:
+        for end in _chunk_ends(K, threshold, check_every):
             nat.check(L.dfs_dense_iterate(B, H, N, float(lam), nat.ptr(Cc), nat.ptr(ep), nat.ptr(mu), nat.ptr(nu),
                                           nat.ptr(lui), nat.ptr(lvi), nat.ptr(mk), nat.ptr(hist), it, end,
                                           nat.ptr(lu), nat.ptr(lv), nat.ptr(change), nat.ptr(work),
                                           nat.ptr(status), st),
                       "dfs_dense_iterate")
             it = end
-            if threshold is not None and end % check_every == 0 and end > 0:
+            if _is_check(end, threshold, check_every):
                 done = float(change.item()) < threshold  # the reference's batch-wide test, one host sync
             if done:
                 break
