@@ -297,7 +297,7 @@ int dfs_fwd(const dfs_problem* p, const dfs_fwd_args* a, void* workspace, size_t
   if (dense_streamed(p)) {
     if (workspace == nullptr || workspace_bytes < dense_fwd_workspace(p->B, p->H, p->N) || !aligned16(workspace))
       return DFS_ERR_WORKSPACE;
-    return cuda_status(launch_dense_fwd(fwd_params(p, a), workspace, st));
+    return cuda_status(launch_dense_fwd(fwd_params(p, a), workspace, workspace_bytes, st));
   }
   // padded head dim: copies at the front of the workspace, the kernels' share after them
   const size_t pad = pad_fwd_bytes(p);

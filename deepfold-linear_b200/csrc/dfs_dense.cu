@@ -696,9 +696,9 @@ size_t dense_fuse_part_bytes(int B, int H, int N) {
 
 size_t dense_fwd_workspace(int B, int H, int N) {
   // diff (2 x BH unsigned) and done (BH int); the transport's row statistics
-  // (2 x BH x N floats); the fused iteration's partials; each region 256-byte aligned
-  return r256(static_cast<size_t>(3) * B * H * 4) + r256(static_cast<size_t>(2) * B * H * N * 4) +
-         r256(dense_fuse_part_bytes(B, H, N));
+  // (2 x BH x N floats); each region 256-byte aligned.  The one-read iteration's
+  // partials follow when the caller's workspace holds them too (dense_fuse_part_bytes).
+  return r256(static_cast<size_t>(3) * B * H * 4) + r256(static_cast<size_t>(2) * B * H * N * 4);
 }
 
 namespace {
@@ -738,17 +738,19 @@ cudaError_t dense_iteration(const DenseArgs& a, float* lv_out, float* part, size
 }
 }  // namespace
 
-cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, cudaStream_t st) {
+cudaError_t launch_dense_fwd(const FwdParams& q, void* ws, size_t ws_bytes, cudaStream_t st) {
   const int BH = q.B * q.H;
   const size_t n = static_cast<size_t>(BH) * q.N;
   unsigned* diff = static_cast<unsigned*>(ws);
   int* done = reinterpret_cast<int*>(diff + 2 * static_cast<size_t>(BH));
   float* rmax = reinterpret_cast<float*>(static_cast<char*>(ws) + r256(static_cast<size_t>(3) * BH * 4));
   float* rsum = rmax + n;
+  // the one-read iterations when the workspace also holds their partials, else two passes per iteration
+  const size_t base = dense_fwd_workspace(q.B, q.H, q.N);
   const size_t part_bytes = dense_fuse_part_bytes(q.B, q.H, q.N);
-  float* part = part_bytes == 0 ? nullptr
-                                : reinterpret_cast<float*>(static_cast<char*>(ws) + r256(static_cast<size_t>(3) * BH * 4) +
-                                                           r256(2 * n * sizeof(float)));
+  float* part = part_bytes != 0 && ws_bytes >= base + part_bytes
+                    ? reinterpret_cast<float*>(static_cast<char*>(ws) + base)
+                    : nullptr;
   const bool vec = (q.N % 4) == 0 && (reinterpret_cast<uintptr_t>(q.C) & 15u) == 0;
   dense_init_kernel<<<grid_for(n, 256), 256, 0, st>>>(q.log_u_init, q.log_v_init, q.log_u, q.log_v, n, diff, done,
                                                        BH);

@@ -159,7 +159,7 @@ cudaError_t launch_stream_fwd(const FwdParams& p, float* ws, cudaStream_t st);
 // dense-cost forward streamed from the caller's C (problems outside the
 // resident kernels' range): potentials, O / T_norm / x_centroid, early stop
 size_t dense_fwd_workspace(int B, int H, int N);
-cudaError_t launch_dense_fwd(const FwdParams& p, void* ws, cudaStream_t st);
+cudaError_t launch_dense_fwd(const FwdParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
 size_t dense_fuse_part_bytes(int B, int H, int N);
 cudaError_t launch_dense_iterations(const float* C, const float* eps, const float* mu, const float* nu,
                                     const float* mask, int B, int H, int N, float lam, float* hist, int it_begin,

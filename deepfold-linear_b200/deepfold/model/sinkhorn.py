@@ -96,6 +96,8 @@ def _dense_call(C, log_mu, log_nu, eps, lam, K, log_u_init, log_v_init, threshol
         x_centroid=nat.ptr(xc), log_u=nat.ptr(lu), log_v=nat.ptr(lv), status=nat.ptr(status),
         T_norm=nat.ptr(T))
     fwd_bytes, _ = nat.workspace_bytes(prob)  # copies of V when its head dim is transformed
+    if N > 384 or d > 32:  # the HBM passes: room for the one-read iterations' column partials too
+        fwd_bytes = (fwd_bytes + 255) // 256 * 256 + nat.lib().dfs_dense_work_bytes(B, H, N)
     ws = torch.empty((fwd_bytes + 3) // 4, device=dev, dtype=torch.float32) if fwd_bytes else None
     nat.check(nat.lib().dfs_fwd(prob, args, nat.ptr(ws), fwd_bytes, nat.stream_ptr(dev)), "dfs_fwd")
     return lu, lv, O, xc, T

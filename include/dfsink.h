@@ -216,7 +216,9 @@ int dfs_dense_iterate(int B, int H, int N, float lam, const float* C, const floa
 
 /* Bytes of the 16-byte aligned `work` buffer dfs_dense_iterate needs: the
  * per-CTA column partials of its one-read iterations (N <= 8192); 0 beyond,
- * where work may be NULL. */
+ * where work may be NULL.  For dfs_fwd with DFS_COST_DENSE, dfs_workspace_size
+ * reports the minimum (each iteration then reads C twice); a workspace of that
+ * size rounded up to 256 plus these bytes makes each iteration one read of C. */
 size_t dfs_dense_work_bytes(int B, int H, int N);
 
 /* dfs_dense_solve_bwd: the adjoint of `iters` iterations recorded in hist by

@@ -77,10 +77,11 @@ def test_host_side_validation(lib):
     dense = nat.make_problem(2, 3, 1000, 128, __import__("torch").float32, 5, 1.0, 10.0,
                              cost_mode=nat.DFS_COST_DENSE)
     assert lib.dfs_workspace_size(dense, ctypes.byref(fb), ctypes.byref(bb)) == nat.DFS_OK
-    # per-problem early-stop state (256 bytes here), the transport's two row statistics per point, and
-    # the one-read iterations' column partials (2 x N floats for up to 148 x 8 CTAs)
+    # the minimum: per-problem early-stop state (256 bytes here), then the transport's two row
+    # statistics per point; dfs_dense_work_bytes more enables the one-read iterations (N <= 8192)
     r256 = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    assert fb.value == 256 + r256(2 * 6 * 1000 * 4) + r256(148 * 8 * 2 * 1000 * 4) and bb.value == 0
+    assert fb.value == 256 + r256(2 * 6 * 1000 * 4) and bb.value == 0
+    assert lib.dfs_dense_work_bytes(2, 3, 1000) == 148 * 8 * 2 * 1000 * 4
     fake_dense = nat.DfsFwdArgs(C=16, eps=16, log_mu=16, log_nu=16, log_u=16, log_v=16)
     assert lib.dfs_fwd(dense, fake_dense, None, 0, None) == nat.DFS_ERR_WORKSPACE
     wider = nat.make_problem(1, 1, 1000, 129, __import__("torch").float32, 5, 1.0, 10.0, cost_mode=nat.DFS_COST_DENSE)
