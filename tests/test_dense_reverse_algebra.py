@@ -72,7 +72,8 @@ def reverse(C, mu, nu, eps, lam, K, lvi, mask, g_lu, g_lv):
     S2 = torch.einsum("kbhr,kbhj->bhrj", A1, B1)
     c2 = C * sc
     dC = (kap / eps[None, :, None])[..., None] * (
-        torch.exp2(c2 + s[..., :, None] + t[..., None, :]) * S1 + torch.exp2(c2 + s1[..., :, None] + t1[..., None, :]) * S2)
+        torch.exp2(c2 + s[..., :, None] + t[..., None, :]) * S1
+        + torch.exp2(c2 + s1[..., :, None] + t1[..., None, :]) * S2)
     if mask is not None:  # padded rows and columns exactly 0, as autograd gives them
         dC = dC * mask[:, None, :, None] * mask[:, None, None, :]
     return dict(dC=dC, dmu=dmu, dnu=dnu, dlvi=gv[0])

@@ -242,7 +242,9 @@ def test_dense_gradients_match_the_reference_autograd_goldens(name):
     if full:
         loss = loss + (xc * f32("dxc")).sum()
     loss.backward()
-    rel = lambda a, b: float(np.max(np.abs(a.detach().cpu().double().numpy() - b)) / max(np.max(np.abs(b)), 1e-30))  # noqa: E731,E501
+
+    def rel(a, b):
+        return float(np.max(np.abs(a.detach().cpu().double().numpy() - b)) / max(np.max(np.abs(b)), 1e-30))
     assert rel(o, out["o_dense" if full else "o"]) < 1e-3
     if not full:  # uot_full's potentials are the flash path's (unconverged at K = 5)
         assert float(np.max(np.abs(lu.detach().cpu().numpy() - out["log_u"]))) < 1e-3
